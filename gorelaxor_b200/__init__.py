@@ -1,0 +1,285 @@
+"""B200 token-loop library: Python host mirror of include/grx.h.
+
+The compute path is libgrx.so (CUDA kernels for sm_100a behind a C ABI);
+this module only binds it with ctypes and mirrors the reference's Go API
+for the token loop:
+
+* ``Weight`` / ``linear`` — kern.Weight and kern.Linear
+  (internal/kern/kern.go:41-201);
+* ``FlowLM`` — pockettts.Model's flow LM (pockettts/model.go:202-322),
+  ``FlowLM.load_voice`` — Model.LoadVoice (pockettts/voice.go:26-63);
+* ``Streams`` — speakChunk's per-frame loop (pockettts/speak.go:146-175)
+  for a batch of independent streams;
+* ``GGUF`` — the internal/gguf reader.
+
+There is no CPU fallback: importing works without a GPU, but every call
+that computes needs libgrx.so and a CUDA device and raises otherwise.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libgrx.so"
+
+GRX_ERRORS = {-1: "EINVAL", -2: "EFORMAT", -3: "ENOMEM", -4: "ECUDA", -5: "ERANGE", -6: "ENODEV"}
+
+_lib = None
+
+
+class GrxError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"grx {GRX_ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+def _sig(lib):
+    P, I, L, S, D, F = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_double, C.POINTER(C.c_float)
+    PP = C.POINTER(C.c_void_p)
+    sigs = {
+        "grx_last_error": (I, [C.c_char_p, S]),
+        "grx_device_count": (I, []),
+        "grx_gguf_open": (I, [P, S, PP]),
+        "grx_gguf_close": (None, [P]),
+        "grx_gguf_int": (L, [P, C.c_char_p, L]),
+        "grx_gguf_float": (D, [P, C.c_char_p, D]),
+        "grx_gguf_string": (I, [P, C.c_char_p, C.c_char_p, S]),
+        "grx_gguf_tensor": (I, [P, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_int64)]),
+        "grx_gguf_float32": (I, [P, C.c_char_p, P, S]),
+        "grx_weight_q8": (I, [I, P, I, I, PP]),
+        "grx_weight_f32": (I, [I, P, I, I, PP]),
+        "grx_weight_drop_rows": (I, [P]),
+        "grx_weight_free": (None, [P]),
+        "grx_linear": (I, [P, P, I, P, P]),
+        "grx_flowlm_load": (I, [P, S, I, PP]),
+        "grx_flowlm_free": (None, [P]),
+        "grx_flowlm_dims": (I, [P] + [C.POINTER(C.c_int)] * 8),
+        "grx_voice_load": (I, [P, P, S, PP]),
+        "grx_voice_raw": (I, [P, I, P, PP]),
+        "grx_voice_free": (None, [P]),
+        "grx_streams_create": (I, [P, I, P, I, PP]),
+        "grx_streams_free": (None, [P]),
+        "grx_streams_reset": (I, [P]),
+        "grx_streams_step": (I, [P, P, P, P, P, P]),
+        "grx_streams_run_device": (I, [P, I, P, P, P]),
+        "grx_streams_sync": (I, [P]),
+        "grx_streams_run_device_timed": (I, [P, I, P, P, P, P]),
+        "grx_streams_pos": (I, [P, I]),
+        "grx_streams_launches": (L, [P]),
+        "grx_streams_cuda_stream": (P, [P]),
+    }
+    for name, (res, args) in sigs.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+def lib():
+    """libgrx.so, loaded once. Raises if it was not built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m gorelaxor_b200.build`")
+        _lib = _sig(C.CDLL(str(LIB_PATH)))
+    return _lib
+
+
+def _check(rc: int):
+    if rc < 0:
+        buf = C.create_string_buffer(4096)
+        lib().grx_last_error(buf, 4096)
+        raise GrxError(rc, buf.value.decode(errors="replace"))
+    return rc
+
+
+def _ptr(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def device_count() -> int:
+    return lib().grx_device_count()
+
+
+class GGUF:
+    """internal/gguf's File: settings and tensors of a GGUF file."""
+
+    def __init__(self, data: bytes):
+        h = C.c_void_p()
+        self._buf = data
+        _check(lib().grx_gguf_open(data, len(data), C.byref(h)))
+        self._h = h
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().grx_gguf_close(self._h)
+            self._h = None
+
+    def int(self, key: str, default: int = -1) -> int:
+        return lib().grx_gguf_int(self._h, key.encode(), default)
+
+    def float(self, key: str, default: float = float("nan")) -> float:
+        return lib().grx_gguf_float(self._h, key.encode(), default)
+
+    def string(self, key: str) -> str:
+        n = _check(lib().grx_gguf_string(self._h, key.encode(), None, 0))
+        buf = C.create_string_buffer(n + 1)
+        lib().grx_gguf_string(self._h, key.encode(), buf, n + 1)
+        return buf.value.decode()
+
+    def tensor(self, name: str):
+        t = C.c_int()
+        dims = (C.c_int64 * 4)()
+        nd = _check(lib().grx_gguf_tensor(self._h, name.encode(), C.byref(t), dims))
+        return t.value, [dims[i] for i in range(nd)]
+
+    def float32(self, name: str) -> np.ndarray:
+        _, dims = self.tensor(name)
+        n = int(np.prod(dims))
+        out = np.empty(n, dtype=np.float32)
+        _check(lib().grx_gguf_float32(self._h, name.encode(), _ptr(out), n))
+        return out.reshape(list(reversed(dims)))
+
+
+class Weight:
+    """kern.Weight on a device (kern.go:41-103)."""
+
+    def __init__(self, h, rows, cols, kind):
+        self._h, self.rows, self.cols, self.kind = h, rows, cols, kind
+
+    @classmethod
+    def q8(cls, blocks: np.ndarray, rows: int, cols: int, device: int = 0) -> "Weight":
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        h = C.c_void_p()
+        _check(lib().grx_weight_q8(device, _ptr(b), rows, cols, C.byref(h)))
+        return cls(h, rows, cols, "q8_0")
+
+    @classmethod
+    def f32(cls, v: np.ndarray, device: int = 0) -> "Weight":
+        a = np.ascontiguousarray(v, dtype=np.float32)
+        h = C.c_void_p()
+        _check(lib().grx_weight_f32(device, _ptr(a), a.shape[0], a.shape[1], C.byref(h)))
+        return cls(h, a.shape[0], a.shape[1], "f32")
+
+    def drop_rows(self) -> "Weight":
+        _check(lib().grx_weight_drop_rows(self._h))
+        return self
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().grx_weight_free(self._h)
+            self._h = None
+
+
+def linear(w: Weight, x: np.ndarray, bias: np.ndarray | None = None) -> np.ndarray:
+    """kern.Linear (kern.go:199): x [m][cols] → [m][rows]."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, w.cols)
+    out = np.empty((x.shape[0], w.rows), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    _check(lib().grx_linear(w._h, _ptr(x), x.shape[0], _ptr(b), _ptr(out)))
+    return out
+
+
+class FlowLM:
+    """pockettts.Model's flow LM and flow head on one device."""
+
+    def __init__(self, gguf: bytes, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().grx_flowlm_load(gguf, len(gguf), device, C.byref(h)))
+        self._h = h
+        self.device = device
+        v = [C.c_int() for _ in range(8)]
+        _check(lib().grx_flowlm_dims(h, *[C.byref(x) for x in v]))
+        self.d, self.heads, self.ff, self.layers, self.ldim, self.fdim, self.depth, self.steps = [x.value for x in v]
+
+    def load_voice(self, gguf: bytes) -> "Voice":
+        h = C.c_void_p()
+        _check(lib().grx_voice_load(self._h, gguf, len(gguf), C.byref(h)))
+        return Voice(h)
+
+    def voice(self, kv: np.ndarray) -> "Voice":
+        """A voice from caches [layers][2][positions][d]."""
+        a = np.ascontiguousarray(kv, dtype=np.float32)
+        h = C.c_void_p()
+        _check(lib().grx_voice_raw(self._h, a.shape[2], _ptr(a), C.byref(h)))
+        return Voice(h)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().grx_flowlm_free(self._h)
+            self._h = None
+
+
+class Voice:
+    def __init__(self, h):
+        self._h = h
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().grx_voice_free(self._h)
+            self._h = None
+
+
+class Streams:
+    """n independent FlowLM streams, each starting from its voice."""
+
+    def __init__(self, model: FlowLM, voices: list[Voice], max_frames: int):
+        self.model, self.n = model, len(voices)
+        self._voices = voices
+        arr = (C.c_void_p * self.n)(*[v._h.value for v in voices])
+        h = C.c_void_p()
+        _check(lib().grx_streams_create(model._h, self.n, arr, max_frames, C.byref(h)))
+        self._h = h
+
+    def reset(self):
+        _check(lib().grx_streams_reset(self._h))
+
+    def step(self, noise: np.ndarray, want_lm_out: bool = False):
+        """One frame for every stream: returns (latent, eos, scaled, lm_out)."""
+        m = self.model
+        nz = np.ascontiguousarray(noise, dtype=np.float32).reshape(self.n, m.ldim)
+        lat = np.empty((self.n, m.ldim), np.float32)
+        sc = np.empty((self.n, m.ldim), np.float32)
+        eos = np.empty(self.n, np.float32)
+        lo = np.empty((self.n, m.d), np.float32) if want_lm_out else None
+        _check(lib().grx_streams_step(self._h, _ptr(nz), _ptr(lo), _ptr(eos), _ptr(lat), _ptr(sc)))
+        return lat, eos, sc, lo
+
+    def run_device(self, frames: int, d_noise: int, d_latent: int, d_eos: int | None):
+        """frames frames with device pointers (ints): noise [frames][n][ldim] in,
+        latent [frames][n][ldim] and eos [frames][n] out. Asynchronous."""
+        _check(lib().grx_streams_run_device(self._h, frames, C.c_void_p(d_noise), C.c_void_p(d_latent),
+                                            C.c_void_p(d_eos) if d_eos else None))
+
+    def run_device_timed(self, frames: int, d_noise: int, d_latent: int, d_eos: int | None, d_ts: int):
+        """run_device that also records each attention kernel's span into the
+        device array d_ts [frames][layers][2] (uint64 ns, preset to
+        {UINT64_MAX, 0})."""
+        _check(lib().grx_streams_run_device_timed(self._h, frames, C.c_void_p(d_noise), C.c_void_p(d_latent),
+                                                  C.c_void_p(d_eos) if d_eos else None, C.c_void_p(d_ts)))
+
+    def sync(self):
+        _check(lib().grx_streams_sync(self._h))
+
+    def pos(self, i: int) -> int:
+        return _check(lib().grx_streams_pos(self._h, i))
+
+    def cuda_stream(self) -> int:
+        """The cudaStream_t (as an int) the stream set's kernels run on."""
+        return lib().grx_streams_cuda_stream(self._h) or 0
+
+    def launches(self) -> int:
+        return lib().grx_streams_launches(self._h)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().grx_streams_free(self._h)
+            self._h = None

@@ -1,0 +1,1050 @@
+// The host side of libgrx: the C ABI of include/grx.h over the kernels.
+//
+// What it mirrors (paths in the gorelaxor tree):
+//  * kern.Weight / kern.Linear (internal/kern/kern.go:41-201) — grx_weight_*,
+//    grx_linear, with the reference's dispatch between the int8 and float
+//    paths (kern.go:189);
+//  * pockettts.Load / LoadVoice (pockettts/model.go:202-322,
+//    voice.go:26-63) — grx_flowlm_load, grx_voice_load: the same tensor
+//    names, shape checks and settings, the Q8_0 weights uploaded to HBM;
+//  * the per-frame loop of speakChunk (speak.go:146-175) for a batch of
+//    independent streams — grx_streams_*: the KV caches stay in HBM, one
+//    frame is one CUDA graph replay of the kernel sequence below, the raw
+//    latent is fed back on the device.
+// Errors are codes plus a per-thread message; nothing here aborts.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/grx.h"
+#include "gguf.h"
+#include "kernels.h"
+
+namespace grx {
+void q8_kernels_init();
+}
+
+using namespace grx;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define CK(call)                                                                                    \
+  do {                                                                                              \
+    cudaError_t e_ = (call);                                                                        \
+    if (e_ != cudaSuccess) return fail(GRX_ECUDA, std::string(#call ": ") + cudaGetErrorString(e_)); \
+  } while (0)
+
+// Device setup done once per device: kernel attributes.
+int device_init(int dev) {
+  static std::mutex mu;
+  static std::vector<bool> done(64, false);
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || dev < 0 || dev >= n || dev >= 64)
+    return fail(GRX_ENODEV, "no CUDA device " + std::to_string(dev));
+  CK(cudaSetDevice(dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (!done[size_t(dev)]) {
+    q8_kernels_init();
+    done[size_t(dev)] = true;
+  }
+  return GRX_OK;
+}
+
+// Device allocations of one owner, freed together on its device.
+struct Arena {
+  int dev = 0;
+  std::vector<void*> ptrs;
+  size_t bytes = 0;
+  template <class T>
+  T* alloc(size_t n, int* rc) {
+    void* p = nullptr;
+    if (*rc) return nullptr;
+    if (n == 0) n = 1;
+    cudaError_t e = cudaMalloc(&p, n * sizeof(T));
+    if (e != cudaSuccess) {
+      *rc = fail(GRX_ENOMEM, "cudaMalloc of " + std::to_string(n * sizeof(T)) + " bytes: " + cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs.push_back(p);
+    bytes += n * sizeof(T);
+    return (T*)p;
+  }
+  template <class T>
+  T* upload(const T* h, size_t n, int* rc) {
+    T* p = alloc<T>(n, rc);
+    if (p && cudaMemcpy(p, h, n * sizeof(T), cudaMemcpyHostToDevice) != cudaSuccess)
+      *rc = fail(GRX_ECUDA, "upload failed");
+    return p;
+  }
+  ~Arena() {
+    if (ptrs.empty()) return;
+    cudaSetDevice(dev);
+    for (void* p : ptrs) cudaFree(p);
+  }
+};
+
+// Splits rows×cols Q8_0 blocks (34 bytes: f16 scale, 32 int8) into the
+// device layout: int8 values [rows][cols] and f16 scales [rows][cols/32].
+DQ8 upload_q8(Arena& ar, const uint8_t* blocks, int rows, int cols, int* rc) {
+  DQ8 w;
+  w.rows = rows;
+  w.cols = cols;
+  size_t nb = size_t(cols) / 32;
+  std::vector<int8_t> q(size_t(rows) * cols);
+  std::vector<uint16_t> d(size_t(rows) * nb);
+  for (size_t b = 0; b < size_t(rows) * nb; b++) {
+    const uint8_t* blk = blocks + b * 34;
+    d[b] = uint16_t(blk[0] | blk[1] << 8);
+    std::memcpy(&q[b * 32], blk + 2, 32);
+  }
+  w.q = ar.upload(q.data(), q.size(), rc);
+  w.d = ar.upload(d.data(), d.size(), rc);
+  return w;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ handles ----
+
+struct grx_gguf {
+  GGUF f;
+};
+
+struct grx_weight {
+  Arena ar;
+  int type = 0;  // 0 F32, 2 Q8_0
+  int rows = 0, cols = 0;
+  bool dropped = false;
+  DQ8 q8;
+  float* f = nullptr;
+};
+
+struct Layer {
+  float *n1w, *n1b, *n2w, *n2b;
+  DQ8 qkv, out, ff1, ff2;
+};
+
+struct Res {
+  float *nw, *nb, *b1, *b2, *adab;
+  DQ8 fc1, fc2, ada;
+};
+
+struct grx_flowlm {
+  Arena ar;
+  int dev = 0;
+  int d = 0, heads = 0, ff = 0, L = 0, ldim = 0, fd = 0, depth = 0, steps = 1;
+  double period = 1e4;
+  std::string sha;
+  std::vector<Layer> layers;
+  std::vector<Res> res;
+  float *win = nullptr, *bos = nullptr, *outw = nullptr, *outb = nullptr, *eosw = nullptr;
+  float eosb = 0;
+  float *mean = nullptr, *stdv = nullptr;
+  DQ8 cond, fada;
+  float *condb = nullptr, *fin = nullptr, *finb = nullptr, *fadab = nullptr, *fout = nullptr, *foutb = nullptr;
+  float* tc = nullptr;  // [steps][fd] time conditions
+  std::vector<float> freqs;
+};
+
+struct grx_voice {
+  int positions = 0;
+  std::vector<float> kv;  // [L][2][positions][d]
+  std::string model;
+};
+
+struct grx_streams {
+  Arena ar;
+  grx_flowlm* m = nullptr;
+  int n = 0, cap = 0;
+  cudaStream_t st = nullptr;
+  float* kv = nullptr;
+  int *pos = nullptr, *pos0 = nullptr;
+  float *x = nullptr, *q = nullptr, *lm_out = nullptr, *eos = nullptr, *lat = nullptr, *rope = nullptr;
+  int8_t *xq = nullptr, *xqf = nullptr;
+  float *xs = nullptr, *xsf = nullptr;
+  float *y0 = nullptr, *sy = nullptr, *h = nullptr, *mod = nullptr, *mod2 = nullptr, *nrm = nullptr, *mm = nullptr,
+        *cur = nullptr;
+  float *noise1 = nullptr, *lat1 = nullptr, *scaled1 = nullptr, *eos1 = nullptr;
+  FrameIO* io = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  cudaGraph_t graph = nullptr;
+  int64_t launches = 0;
+  int per_frame = 0;
+  ~grx_streams() {
+    cudaSetDevice(ar.dev);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (st) cudaStreamDestroy(st);
+  }
+};
+
+namespace {
+
+// The kernel sequence of one frame for all streams (see grx.h): flowLM.step
+// (lm.go:185-195 → nn.go:142-182) then flowHead.sample (lm.go:108-160).
+// Returns the number of kernels launched.
+int enqueue_frame(grx_streams* s) {
+  grx_flowlm* m = s->m;
+  const int M = s->n, d = m->d, fd = m->fd;
+  cudaStream_t st = s->st;
+  int k = 0;
+  // x = lm.input · latent (F32 weight, dot4f32avx order; bos at frame 0).
+  {
+    FArgs a;
+    a.epi = FE_BIAS;
+    a.x = s->lat;
+    a.ldx = m->ldim;
+    a.wf = m->win;
+    a.N = d;
+    a.K = m->ldim;
+    a.y = s->x;
+    a.ldy = d;
+    launch_flin(a, M, st);
+    k++;
+  }
+  for (int l = 0; l < m->L; l++) {
+    const Layer& ly = m->layers[size_t(l)];
+    LnArgs ln;
+    ln.x = s->x;
+    ln.w = ly.n1w;
+    ln.b = ly.n1b;
+    ln.eps = 1e-5;
+    ln.mode = LN_Q8;
+    ln.q8 = s->xq;
+    ln.q8s = s->xs;
+    launch_ln(ln, M, d, st);
+    EpiArgs e;
+    e.epi = EPI_ROPE_KV;
+    e.kv.q = s->q;
+    e.kv.kv = s->kv;
+    e.kv.pos = s->pos;
+    e.kv.rope = s->rope;
+    e.kv.layer = l;
+    e.kv.layers = m->L;
+    e.kv.heads = m->heads;
+    e.kv.cap = s->cap;
+    e.kv.d = d;
+    launch_q8_product(s->xq, s->xs, M, ly.qkv, e, st);
+    AttnArgs at;
+    at.q = s->q;
+    at.kv = s->kv;
+    at.pos = s->pos;
+    at.q8 = s->xq;
+    at.q8s = s->xs;
+    at.layer = l;
+    at.layers = m->L;
+    at.heads = m->heads;
+    at.cap = s->cap;
+    at.d = d;
+    at.io = s->io;
+    launch_attn(at, M, st);
+    EpiArgs r;
+    r.epi = EPI_RESID;
+    r.y = s->x;
+    r.ldy = d;
+    launch_q8_product(s->xq, s->xs, M, ly.out, r, st);
+    ln.w = ly.n2w;
+    ln.b = ly.n2b;
+    launch_ln(ln, M, d, st);
+    EpiArgs g;
+    g.epi = EPI_GELU_Q8;
+    g.q8 = s->xqf;
+    g.q8s = s->xsf;
+    launch_q8_product(s->xq, s->xs, M, ly.ff1, g, st);
+    launch_q8_product(s->xqf, s->xsf, M, ly.ff2, r, st);
+    k += 7;
+  }
+  {  // out_norm → lm_out; eos; position += 1
+    LnArgs ln;
+    ln.x = s->x;
+    ln.w = m->outw;
+    ln.b = m->outb;
+    ln.eps = 1e-5;
+    ln.mode = LN_F32;
+    ln.y = s->lm_out;
+    launch_ln(ln, M, d, st);
+    launch_eos(s->lm_out, m->eosw, m->eosb, d, s->io, s->eos, s->pos, M, st);
+    k += 2;
+  }
+  // Flow head. y = cond·lm_out + b; per step: sy = silu(y + tc_i), net.
+  const bool one = m->steps == 1;
+  {
+    FArgs a;
+    a.epi = one ? FE_COND : FE_BIAS;
+    a.x = s->lm_out;
+    a.ldx = d;
+    a.wq = m->cond.q;
+    a.wd = m->cond.d;
+    a.N = fd;
+    a.K = d;
+    a.bias = m->condb;
+    a.y = one ? s->sy : s->y0;
+    a.ldy = fd;
+    a.aux = m->tc;
+    launch_flin(a, M, st);
+    k++;
+  }
+  for (int step = 0; step < m->steps; step++) {
+    if (!one) {
+      launch_cond_step(s->y0, m->tc + size_t(step) * fd, s->sy, M, fd, st);
+      k++;
+    }
+    {  // h = input·cur + b (cur = the noise at the first step)
+      FArgs a;
+      a.epi = FE_BIAS;
+      a.x = s->cur;
+      a.ldx = m->ldim;
+      a.io = s->io;
+      a.x_noise = step == 0;
+      a.wf = m->fin;
+      a.N = fd;
+      a.K = m->ldim;
+      a.bias = m->finb;
+      a.y = s->h;
+      a.ldy = fd;
+      launch_flin(a, M, st);
+      k++;
+    }
+    for (const Res& r : m->res) {
+      FArgs a;
+      a.epi = FE_BIAS;
+      a.x = s->sy;
+      a.ldx = fd;
+      a.wq = r.ada.q;
+      a.wd = r.ada.d;
+      a.N = 3 * fd;
+      a.K = fd;
+      a.bias = r.adab;
+      a.y = s->mod;
+      a.ldy = 3 * fd;
+      launch_flin(a, M, st);
+      LnArgs ln;
+      ln.x = s->h;
+      ln.w = r.nw;
+      ln.b = r.nb;
+      ln.eps = 1e-6;
+      ln.mode = LN_MOD;
+      ln.y = s->nrm;
+      ln.mod = s->mod;
+      ln.ldmod = 3 * fd;
+      ln.shift = 0;
+      ln.scale = fd;
+      launch_ln(ln, M, fd, st);
+      FArgs f1;
+      f1.epi = FE_SILU;
+      f1.x = s->nrm;
+      f1.ldx = fd;
+      f1.wq = r.fc1.q;
+      f1.wd = r.fc1.d;
+      f1.N = fd;
+      f1.K = fd;
+      f1.bias = r.b1;
+      f1.y = s->mm;
+      f1.ldy = fd;
+      launch_flin(f1, M, st);
+      FArgs f2 = f1;
+      f2.epi = FE_GATE;
+      f2.x = s->mm;
+      f2.wq = r.fc2.q;
+      f2.wd = r.fc2.d;
+      f2.bias = r.b2;
+      f2.y = s->h;
+      f2.aux = s->mod + 2 * fd;
+      f2.ldaux = 3 * fd;
+      launch_flin(f2, M, st);
+      k += 4;
+    }
+    {
+      FArgs a;
+      a.epi = FE_BIAS;
+      a.x = s->sy;
+      a.ldx = fd;
+      a.wq = m->fada.q;
+      a.wd = m->fada.d;
+      a.N = 2 * fd;
+      a.K = fd;
+      a.bias = m->fadab;
+      a.y = s->mod2;
+      a.ldy = 2 * fd;
+      launch_flin(a, M, st);
+      LnArgs ln;
+      ln.x = s->h;
+      ln.eps = 1e-6;
+      ln.mode = LN_MOD;
+      ln.y = s->nrm;
+      ln.mod = s->mod2;
+      ln.ldmod = 2 * fd;
+      ln.shift = 0;
+      ln.scale = fd;
+      launch_ln(ln, M, fd, st);
+      FArgs o;
+      const bool last = step + 1 == m->steps;
+      o.epi = FE_LATENT;
+      o.x = s->nrm;
+      o.ldx = fd;
+      o.wf = m->fout;
+      o.N = m->ldim;
+      o.K = fd;
+      o.bias = m->foutb;
+      o.y = last ? s->lat : s->cur;  // the last step's latent feeds the next frame
+      o.ldy = m->ldim;
+      o.aux = s->cur;  // cur before this step: the noise at the first step
+      o.ldaux = m->ldim;
+      o.aux_noise = step == 0;
+      o.io = s->io;
+      o.io_out = last;
+      o.steps = float(m->steps);
+      o.mean = m->mean;
+      o.stdv = m->stdv;
+      if (last) {
+        o.out2 = s->lat1;
+        o.out3 = s->scaled1;
+      }
+      launch_flin(o, M, st);
+      k += 3;
+    }
+  }
+  launch_tick(s->io, st);
+  k++;
+  return k;
+}
+
+int build_graph(grx_streams* s) {
+  CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+  int k = enqueue_frame(s);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s->st, &g);
+  if (e != cudaSuccess) return fail(GRX_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+  s->graph = g;
+  CK(cudaGraphInstantiate(&s->exec, g, 0));
+  s->per_frame = k;
+  return GRX_OK;
+}
+
+std::vector<float> rope_freqs(int hd, double period) {
+  float c = float(-std::log(period) * 2 / double(hd));
+  std::vector<float> f(size_t(hd / 2));
+  for (size_t i = 0; i < f.size(); i++) f[i] = float(std::exp(double(float(i) * c)));
+  return f;
+}
+
+}  // namespace
+
+// ================================================================ C ABI ==
+
+extern "C" {
+
+int grx_last_error(char* buf, size_t len) {
+  if (buf && len) {
+    size_t n = std::min(len - 1, g_err.size());
+    std::memcpy(buf, g_err.data(), n);
+    buf[n] = 0;
+  }
+  return int(g_err.size());
+}
+
+int grx_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+// ---- GGUF ----
+
+int grx_gguf_open(const void* bytes, size_t len, grx_gguf** out) {
+  if (!bytes || !out) return fail(GRX_EINVAL, "grx_gguf_open: null argument");
+  auto f = std::make_unique<grx_gguf>();
+  if (!f->f.parse(bytes, len)) return fail(GRX_EFORMAT, f->f.err);
+  *out = f.release();
+  return GRX_OK;
+}
+
+void grx_gguf_close(grx_gguf* f) { delete f; }
+
+int64_t grx_gguf_int(const grx_gguf* f, const char* key, int64_t def) { return f ? f->f.get_int(key, def) : def; }
+
+double grx_gguf_float(const grx_gguf* f, const char* key, double def) { return f ? f->f.get_float(key, def) : def; }
+
+int grx_gguf_string(const grx_gguf* f, const char* key, char* buf, size_t len) {
+  if (!f) return fail(GRX_EINVAL, "null file");
+  auto it = f->f.kv.find(key);
+  if (it == f->f.kv.end() || it->second.kind != GValue::STR) return fail(GRX_EINVAL, std::string("no string ") + key);
+  const std::string& s = it->second.s;
+  if (buf && len) {
+    size_t n = std::min(len - 1, s.size());
+    std::memcpy(buf, s.data(), n);
+    buf[n] = 0;
+  }
+  return int(s.size());
+}
+
+int grx_gguf_tensor(const grx_gguf* f, const char* name, int* type, int64_t dims[4]) {
+  if (!f) return fail(GRX_EINVAL, "null file");
+  auto it = f->f.tensors.find(name);
+  if (it == f->f.tensors.end()) return fail(GRX_EINVAL, std::string("no tensor ") + name);
+  if (type) *type = it->second.type;
+  for (size_t i = 0; i < 4; i++) dims[i] = i < it->second.dims.size() ? it->second.dims[i] : 1;
+  return int(it->second.dims.size());
+}
+
+int grx_gguf_float32(const grx_gguf* f, const char* name, float* dst, size_t n) {
+  if (!f || !dst) return fail(GRX_EINVAL, "null argument");
+  std::vector<float> v;
+  if (!f->f.float32(name, v)) return fail(GRX_EINVAL, std::string("no tensor ") + name);
+  if (v.size() != n) return fail(GRX_EINVAL, "wrong size for " + std::string(name));
+  std::memcpy(dst, v.data(), n * 4);
+  return GRX_OK;
+}
+
+// ---- operator ----
+
+int grx_weight_q8(int device, const void* blocks, int rows, int cols, grx_weight** out) {
+  if (!blocks || !out || rows <= 0 || cols <= 0 || cols % 32 != 0)
+    return fail(GRX_EINVAL, "kern: Q8_0 rows must be a multiple of 32 values");
+  int rc = device_init(device);
+  if (rc) return rc;
+  auto w = std::make_unique<grx_weight>();
+  w->ar.dev = device;
+  w->type = 2;
+  w->rows = rows;
+  w->cols = cols;
+  w->q8 = upload_q8(w->ar, (const uint8_t*)blocks, rows, cols, &rc);
+  if (rc) return rc;
+  *out = w.release();
+  return GRX_OK;
+}
+
+int grx_weight_f32(int device, const float* v, int rows, int cols, grx_weight** out) {
+  if (!v || !out || rows <= 0 || cols <= 0) return fail(GRX_EINVAL, "bad F32 weight");
+  int rc = device_init(device);
+  if (rc) return rc;
+  auto w = std::make_unique<grx_weight>();
+  w->ar.dev = device;
+  w->type = 0;
+  w->rows = rows;
+  w->cols = cols;
+  w->f = w->ar.upload(v, size_t(rows) * cols, &rc);
+  if (rc) return rc;
+  *out = w.release();
+  return GRX_OK;
+}
+
+int grx_weight_drop_rows(grx_weight* w) {
+  if (!w) return fail(GRX_EINVAL, "null weight");
+  if (w->type == 2) w->dropped = true;
+  return GRX_OK;
+}
+
+void grx_weight_free(grx_weight* w) { delete w; }
+
+int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, float* dst) {
+  if (!w || !x || !dst || m < 0) return fail(GRX_EINVAL, "grx_linear: bad argument");
+  if (m == 0) return GRX_OK;
+  CK(cudaSetDevice(w->ar.dev));
+  const int n = w->rows, k = w->cols;
+  const bool int8 = w->type == 2 && (w->dropped || m >= 2);
+  if (!int8 && m > 16) return fail(GRX_EINVAL, "grx_linear: float-path products take at most 16 rows");
+  if (int8 && m > 8 && k % 128 != 0) return fail(GRX_EINVAL, "grx_linear: int8 products of more than 8 rows need K % 128 == 0");
+  if (int8 && m <= 8 && n % 32 != 0) return fail(GRX_EINVAL, "grx_linear: int8 products of up to 8 rows need N % 32 == 0");
+  int rc = 0;
+  Arena ar;
+  ar.dev = w->ar.dev;
+  float* dx = ar.upload(x, size_t(m) * k, &rc);
+  float* db = bias ? ar.upload(bias, size_t(n), &rc) : nullptr;
+  float* dy = ar.alloc<float>(size_t(m) * n, &rc);
+  if (rc) return rc;
+  if (int8) {
+    int8_t* q = ar.alloc<int8_t>(size_t(m) * k, &rc);
+    float* s = ar.alloc<float>(size_t(m) * (k / 32), &rc);
+    if (rc) return rc;
+    launch_quant(dx, m, k, q, s, 0);
+    EpiArgs e;
+    e.epi = EPI_STORE;
+    e.y = dy;
+    e.ldy = n;
+    e.bias = db;
+    launch_q8_product(q, s, m, w->q8, e, 0);
+  } else {
+    if (w->type == 2 ? k % 32 : k % 16) return fail(GRX_EINVAL, "grx_linear: K must be whole blocks");
+    FArgs a;
+    a.epi = FE_BIAS;
+    a.x = dx;
+    a.ldx = k;
+    a.wq = w->type == 2 ? w->q8.q : nullptr;
+    a.wd = w->type == 2 ? w->q8.d : nullptr;
+    a.wf = w->type == 0 ? w->f : nullptr;
+    a.N = n;
+    a.K = k;
+    a.bias = db;
+    a.y = dy;
+    a.ldy = n;
+    launch_flin(a, m, 0);
+  }
+  CK(cudaGetLastError());
+  CK(cudaMemcpy(dst, dy, size_t(m) * n * 4, cudaMemcpyDeviceToHost));
+  return GRX_OK;
+}
+
+// ---- FlowLM ----
+
+int grx_flowlm_load(const void* bytes, size_t len, int device, grx_flowlm** out) {
+  if (!bytes || !out) return fail(GRX_EINVAL, "grx_flowlm_load: null argument");
+  int rc = device_init(device);
+  if (rc) return rc;
+  GGUF f;
+  if (!f.parse(bytes, len)) return fail(GRX_EFORMAT, f.err);
+  if (f.get_string("general.architecture", "") != "pockettts")
+    return fail(GRX_EFORMAT, "pockettts: the file isn't a Pocket TTS model");
+  auto m = std::make_unique<grx_flowlm>();
+  m->ar.dev = device;
+  m->dev = device;
+  m->sha = f.get_string("general.source.sha256", "");
+  if (m->sha.empty()) return fail(GRX_EFORMAT, "pockettts: the file doesn't name its source");
+  std::string err;
+  // loader.num, model.go:93-100.
+  auto num = [&](const char* key) -> int {
+    int64_t v = f.get_int(key, -1);
+    if (v < 1 || v > (1 << 16)) {
+      if (err.empty()) err = std::string("pockettts: the setting ") + key + " is " + std::to_string(v);
+      return 1;
+    }
+    return int(v);
+  };
+  // loader.mat / loader.vec with shape checks, model.go:61-91.
+  auto vec = [&](const std::string& name, int64_t n) -> float* {
+    if (!err.empty()) return nullptr;
+    std::vector<float> v;
+    auto it = f.tensors.find(name);
+    if (it == f.tensors.end() || it->second.elems() != n || !f.float32(name, v)) {
+      err = "pockettts: no " + std::to_string(n) + "-value " + name;
+      return nullptr;
+    }
+    return m->ar.upload(v.data(), v.size(), &rc);
+  };
+  auto shape_ok = [&](const std::string& name, int64_t rows, int64_t cols) -> const GTensor* {
+    if (!err.empty()) return nullptr;
+    int64_t r, c;
+    if (!f.matrix_shape(name, &r, &c)) {
+      err = "pockettts: no tensor " + name;
+      return nullptr;
+    }
+    if (r != rows || c != cols) {
+      err = "pockettts: " + name + " is " + std::to_string(r) + "x" + std::to_string(c) + ", want " +
+            std::to_string(rows) + "x" + std::to_string(cols);
+      return nullptr;
+    }
+    return &f.tensors.at(name);
+  };
+  auto q8 = [&](const std::string& name, int64_t rows, int64_t cols) -> DQ8 {
+    const GTensor* t = shape_ok(name, rows, cols);
+    if (!t) return DQ8{};
+    if (t->type != G_Q8_0) {
+      // A float tensor where Q8_0 is expected: round it the way ToQ8 does
+      // is not what the reference's loader does; refuse.
+      err = "pockettts: " + name + " is not Q8_0";
+      return DQ8{};
+    }
+    return upload_q8(m->ar, t->data, int(rows), int(cols), &rc);
+  };
+  auto f32m = [&](const std::string& name, int64_t rows, int64_t cols) -> float* {
+    const GTensor* t = shape_ok(name, rows, cols);
+    if (!t) return nullptr;
+    std::vector<float> v;
+    f.float32(name, v);
+    if (t->type == G_Q8_0) {
+      err = "pockettts: " + name + " is Q8_0 where float32 is expected";
+      return nullptr;
+    }
+    return m->ar.upload(v.data(), v.size(), &rc);
+  };
+  m->ldim = num("pockettts.latent_dim");
+  m->d = num("pockettts.lm.d_model");
+  m->heads = num("pockettts.lm.heads");
+  m->ff = num("pockettts.lm.ff");
+  m->L = num("pockettts.lm.layers");
+  m->fd = num("pockettts.flow.dim");
+  m->depth = num("pockettts.flow.depth");
+  m->steps = num("pockettts.decode_steps");
+  m->period = f.get_float("pockettts.lm.max_period", 1e4);
+  if (!err.empty()) return fail(GRX_EFORMAT, err);
+  const int d = m->d, ff = m->ff, fd = m->fd, ld = m->ldim;
+  if (d % m->heads != 0 || d / m->heads != 64)
+    return fail(GRX_EINVAL, "pockettts: heads of " + std::to_string(d / m->heads) + " values (this build runs 64)");
+  if (d % 128 || ff % 128 || fd % 128 || ld % 16 || d > 4096 || fd > 4096)
+    return fail(GRX_EINVAL, "pockettts: model dimensions outside what the kernels take");
+  for (int i = 0;; i++) {
+    std::string p = "lm.blk." + std::to_string(i) + ".";
+    if (!f.has(p + "norm1.weight")) break;
+    Layer ly;
+    ly.n1w = vec(p + "norm1.weight", d);
+    ly.n1b = vec(p + "norm1.bias", d);
+    ly.n2w = vec(p + "norm2.weight", d);
+    ly.n2b = vec(p + "norm2.bias", d);
+    ly.qkv = q8(p + "attn_qkv.weight", 3 * d, d);
+    ly.out = q8(p + "attn_out.weight", d, d);
+    ly.ff1 = q8(p + "ff1.weight", ff, d);
+    ly.ff2 = q8(p + "ff2.weight", d, ff);
+    m->layers.push_back(ly);
+  }
+  if (err.empty() && int(m->layers.size()) != m->L)
+    err = "pockettts: the flow LM has " + std::to_string(m->layers.size()) + " layers";
+  m->win = f32m("lm.input.weight", d, ld);
+  m->bos = vec("lm.bos", ld);
+  m->outw = vec("lm.out_norm.weight", d);
+  m->outb = vec("lm.out_norm.bias", d);
+  m->eosw = f32m("lm.eos.weight", 1, d);
+  {
+    std::vector<float> b;
+    if (err.empty() && (!f.float32("lm.eos.bias", b) || b.size() != 1)) err = "pockettts: no 1-value lm.eos.bias";
+    if (!b.empty()) m->eosb = b[0];
+  }
+  m->mean = vec("lm.emb_mean", ld);
+  m->stdv = vec("lm.emb_std", ld);
+  m->cond = q8("flow.cond.weight", fd, d);
+  m->condb = vec("flow.cond.bias", fd);
+  m->fin = f32m("flow.input.weight", fd, ld);
+  m->finb = vec("flow.input.bias", fd);
+  DQ8 tfc1[2], tfc2[2];
+  float *tb1[2], *tb2[2], *alpha[2];
+  std::vector<float> freqs[2];
+  for (int k = 0; k < 2; k++) {
+    std::string p = "flow.time." + std::to_string(k) + ".";
+    if (err.empty() && (!f.float32(p + "freqs", freqs[k]) || freqs[k].size() != 128))
+      err = "pockettts: no 128-value " + p + "freqs";
+    tfc1[k] = q8(p + "fc1.weight", fd, 256);
+    tb1[k] = vec(p + "fc1.bias", fd);
+    tfc2[k] = q8(p + "fc2.weight", fd, fd);
+    tb2[k] = vec(p + "fc2.bias", fd);
+    alpha[k] = vec(p + "norm.alpha", fd);
+  }
+  for (int i = 0; i < m->depth; i++) {
+    std::string p = "flow.res." + std::to_string(i) + ".";
+    Res r;
+    r.nw = vec(p + "norm.weight", fd);
+    r.nb = vec(p + "norm.bias", fd);
+    r.fc1 = q8(p + "fc1.weight", fd, fd);
+    r.b1 = vec(p + "fc1.bias", fd);
+    r.fc2 = q8(p + "fc2.weight", fd, fd);
+    r.b2 = vec(p + "fc2.bias", fd);
+    r.ada = q8(p + "ada.weight", 3 * fd, fd);
+    r.adab = vec(p + "ada.bias", 3 * fd);
+    m->res.push_back(r);
+  }
+  m->fada = q8("flow.final.ada.weight", 2 * fd, fd);
+  m->fadab = vec("flow.final.ada.bias", 2 * fd);
+  m->fout = f32m("flow.final.out.weight", ld, fd);
+  m->foutb = vec("flow.final.out.bias", ld);
+  if (!err.empty()) return fail(GRX_EFORMAT, err);
+  if (rc) return rc;
+  m->freqs = rope_freqs(64, m->period);
+
+  // The time conditions, once (Speak, speak.go:57 → lm.go:62-104): the
+  // embedders' [cos, sin] inputs in float64 on the host, the MLPs and the
+  // normalization on the device with the same kernels as the frame.
+  {
+    const int S = m->steps;
+    std::vector<float> in[2];
+    for (int k = 0; k < 2; k++) {
+      in[k].resize(size_t(S) * 256);
+      for (int s = 0; s < S; s++) {
+        float t = float(double(s + k) / double(S));
+        for (int i = 0; i < 128; i++) {
+          double a = double(t * freqs[k][size_t(i)]);
+          in[k][size_t(s) * 256 + i] = float(std::cos(a));
+          in[k][size_t(s) * 256 + 128 + i] = float(std::sin(a));
+        }
+      }
+    }
+    Arena tmp;
+    tmp.dev = device;
+    float* y[2];
+    for (int k = 0; k < 2; k++) {
+      float* din = tmp.upload(in[k].data(), in[k].size(), &rc);
+      float* hh = tmp.alloc<float>(size_t(S) * fd, &rc);
+      y[k] = tmp.alloc<float>(size_t(S) * fd, &rc);
+      if (rc) return rc;
+      FArgs a;
+      a.epi = FE_SILU;
+      a.x = din;
+      a.ldx = 256;
+      a.wq = tfc1[k].q;
+      a.wd = tfc1[k].d;
+      a.N = fd;
+      a.K = 256;
+      a.bias = tb1[k];
+      a.y = hh;
+      a.ldy = fd;
+      launch_flin(a, S, 0);
+      FArgs b = a;
+      b.epi = FE_BIAS;
+      b.x = hh;
+      b.ldx = fd;
+      b.wq = tfc2[k].q;
+      b.wd = tfc2[k].d;
+      b.K = fd;
+      b.bias = tb2[k];
+      b.y = y[k];
+      launch_flin(b, S, 0);
+    }
+    m->tc = m->ar.alloc<float>(size_t(S) * fd, &rc);
+    if (rc) return rc;
+    launch_time_norm(y[0], y[1], alpha[0], alpha[1], fd, S, m->tc, 0);
+    CK(cudaGetLastError());
+    CK(cudaDeviceSynchronize());
+  }
+  *out = m.release();
+  return GRX_OK;
+}
+
+void grx_flowlm_free(grx_flowlm* m) { delete m; }
+
+int grx_flowlm_dims(const grx_flowlm* m, int* d, int* heads, int* ff, int* layers, int* ldim, int* fdim, int* depth,
+                    int* steps) {
+  if (!m) return fail(GRX_EINVAL, "null model");
+  if (d) *d = m->d;
+  if (heads) *heads = m->heads;
+  if (ff) *ff = m->ff;
+  if (layers) *layers = m->L;
+  if (ldim) *ldim = m->ldim;
+  if (fdim) *fdim = m->fd;
+  if (depth) *depth = m->depth;
+  if (steps) *steps = m->steps;
+  return GRX_OK;
+}
+
+int grx_voice_raw(grx_flowlm* m, int positions, const float* kv, grx_voice** out) {
+  if (!m || !kv || !out) return fail(GRX_EINVAL, "grx_voice_raw: null argument");
+  if (positions < 1 || positions > 4096) return fail(GRX_EINVAL, "pockettts: a voice of " + std::to_string(positions) + " positions");
+  auto v = std::make_unique<grx_voice>();
+  v->positions = positions;
+  size_t n = size_t(m->L) * 2 * positions * m->d;
+  v->kv.assign(kv, kv + n);
+  for (float x : v->kv)
+    if (!std::isfinite(x)) return fail(GRX_EFORMAT, "pockettts: the voice has values that aren't numbers");
+  v->model = m->sha;
+  *out = v.release();
+  return GRX_OK;
+}
+
+int grx_voice_load(grx_flowlm* m, const void* bytes, size_t len, grx_voice** out) {
+  if (!m || !bytes || !out) return fail(GRX_EINVAL, "grx_voice_load: null argument");
+  GGUF f;
+  if (!f.parse(bytes, len)) return fail(GRX_EFORMAT, f.err);
+  if (f.get_string("general.architecture", "") != "pockettts-voice")
+    return fail(GRX_EFORMAT, "pockettts: the file isn't a Pocket TTS voice");
+  if (f.get_string("pockettts.voice.model.sha256", "") != m->sha)
+    return fail(GRX_EFORMAT, "pockettts: the voice was made for a different model file");
+  int64_t nl = f.get_int("pockettts.voice.layers", 0), n = f.get_int("pockettts.voice.positions", 0);
+  if (nl != m->L || n < 1 || n > 4096)
+    return fail(GRX_EFORMAT, "pockettts: the voice holds " + std::to_string(nl) + " layers of " + std::to_string(n) + " positions");
+  std::vector<float> kv(size_t(m->L) * 2 * size_t(n) * m->d);
+  for (int i = 0; i < m->L; i++)
+    for (int j = 0; j < 2; j++) {
+      std::string name = "voice." + std::to_string(i) + "." + "kv"[j];
+      auto it = f.tensors.find(name);
+      if (it == f.tensors.end() || it->second.dims.size() != 2 || it->second.dims[0] != m->d || it->second.dims[1] != n)
+        return fail(GRX_EFORMAT, "pockettts: the voice has no " + std::to_string(n) + "x" + std::to_string(m->d) + " " + name);
+      std::vector<float> v;
+      if (!f.float32(name, v)) return fail(GRX_EFORMAT, "pockettts: unreadable " + name);
+      std::memcpy(&kv[(size_t(i) * 2 + j) * size_t(n) * m->d], v.data(), v.size() * 4);
+    }
+  return grx_voice_raw(m, int(n), kv.data(), out);
+}
+
+void grx_voice_free(grx_voice* v) { delete v; }
+
+int grx_streams_reset(grx_streams* s) {
+  if (!s) return fail(GRX_EINVAL, "null streams");
+  grx_flowlm* m = s->m;
+  CK(cudaSetDevice(s->ar.dev));
+  CK(cudaMemcpyAsync(s->pos, s->pos0, sizeof(int) * size_t(s->n), cudaMemcpyDeviceToDevice, s->st));
+  for (int i = 0; i < s->n; i++)
+    CK(cudaMemcpyAsync(s->lat + size_t(i) * m->ldim, m->bos, sizeof(float) * size_t(m->ldim), cudaMemcpyDeviceToDevice,
+                       s->st));
+  CK(cudaStreamSynchronize(s->st));
+  return GRX_OK;
+}
+
+int grx_streams_create(grx_flowlm* m, int n, const grx_voice* const* voices, int max_frames, grx_streams** out) {
+  if (!m || !voices || !out || n < 1 || max_frames < 1) return fail(GRX_EINVAL, "grx_streams_create: bad argument");
+  int rc = device_init(m->dev);
+  if (rc) return rc;
+  int maxp = 0;
+  for (int i = 0; i < n; i++) {
+    if (!voices[i]) return fail(GRX_EINVAL, "null voice");
+    if (voices[i]->model != m->sha) return fail(GRX_EINVAL, "pockettts: the voice was made for a different model");
+    maxp = std::max(maxp, voices[i]->positions);
+  }
+  auto s = std::make_unique<grx_streams>();
+  s->ar.dev = m->dev;
+  s->m = m;
+  s->n = n;
+  s->cap = maxp + max_frames;
+  const int d = m->d, fd = m->fd, ld = m->ldim, H = m->heads, L = m->L, hd = 64;
+  const size_t per_stream = size_t(L) * 2 * H * s->cap * hd;
+  CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+  s->kv = s->ar.alloc<float>(per_stream * n, &rc);
+  s->pos = s->ar.alloc<int>(size_t(n), &rc);
+  s->pos0 = s->ar.alloc<int>(size_t(n), &rc);
+  s->x = s->ar.alloc<float>(size_t(n) * d, &rc);
+  s->q = s->ar.alloc<float>(size_t(n) * d, &rc);
+  s->lm_out = s->ar.alloc<float>(size_t(n) * d, &rc);
+  s->eos = s->ar.alloc<float>(size_t(n), &rc);
+  s->lat = s->ar.alloc<float>(size_t(n) * ld, &rc);
+  s->xq = s->ar.alloc<int8_t>(size_t(n) * d, &rc);
+  s->xs = s->ar.alloc<float>(size_t(n) * d / 32, &rc);
+  s->xqf = s->ar.alloc<int8_t>(size_t(n) * m->ff, &rc);
+  s->xsf = s->ar.alloc<float>(size_t(n) * m->ff / 32, &rc);
+  s->y0 = s->ar.alloc<float>(size_t(n) * fd, &rc);
+  s->sy = s->ar.alloc<float>(size_t(n) * fd, &rc);
+  s->h = s->ar.alloc<float>(size_t(n) * fd, &rc);
+  s->mod = s->ar.alloc<float>(size_t(n) * 3 * fd, &rc);
+  s->mod2 = s->ar.alloc<float>(size_t(n) * 2 * fd, &rc);
+  s->nrm = s->ar.alloc<float>(size_t(n) * fd, &rc);
+  s->mm = s->ar.alloc<float>(size_t(n) * fd, &rc);
+  s->cur = s->ar.alloc<float>(size_t(n) * ld, &rc);
+  s->noise1 = s->ar.alloc<float>(size_t(n) * ld, &rc);
+  s->lat1 = s->ar.alloc<float>(size_t(n) * ld, &rc);
+  s->scaled1 = s->ar.alloc<float>(size_t(n) * ld, &rc);
+  s->eos1 = s->ar.alloc<float>(size_t(n), &rc);
+  s->io = s->ar.alloc<FrameIO>(1, &rc);
+  if (rc) return rc;
+  // RoPE cos/sin for every position the streams can reach (nn.go:84-85).
+  {
+    std::vector<float> t(size_t(s->cap) * hd);
+    for (int p = 0; p < s->cap; p++)
+      for (int i = 0; i < hd / 2; i++) {
+        double a = double(m->freqs[size_t(i)] * float(p));
+        t[(size_t(p) * (hd / 2) + i) * 2] = float(std::cos(a));
+        t[(size_t(p) * (hd / 2) + i) * 2 + 1] = float(std::sin(a));
+      }
+    s->rope = s->ar.upload(t.data(), t.size(), &rc);
+  }
+  // The voices' caches, into the per-head layout; streams sharing a voice
+  // copy the first one's device rows.
+  std::vector<int> p0((size_t)n);
+  std::vector<float> lay;
+  for (int i = 0; i < n; i++) {
+    const grx_voice* v = voices[i];
+    p0[size_t(i)] = v->positions;
+    float* dst = s->kv + per_stream * size_t(i);
+    int first = -1;
+    for (int j = 0; j < i; j++)
+      if (voices[j] == v) {
+        first = j;
+        break;
+      }
+    if (first >= 0) {
+      CK(cudaMemcpy(dst, s->kv + per_stream * size_t(first), per_stream * 4, cudaMemcpyDeviceToDevice));
+      continue;
+    }
+    const int P = v->positions;
+    lay.assign(size_t(H) * P * hd, 0.f);
+    for (int l = 0; l < L; l++)
+      for (int kvi = 0; kvi < 2; kvi++) {
+        const float* src = &v->kv[(size_t(l) * 2 + kvi) * size_t(P) * d];
+        for (int p = 0; p < P; p++)
+          for (int h = 0; h < H; h++)
+            std::memcpy(&lay[(size_t(h) * P + p) * hd], src + size_t(p) * d + h * hd, hd * 4);
+        for (int h = 0; h < H; h++) {
+          float* hp = dst + ((size_t(l) * 2 + kvi) * H + h) * size_t(s->cap) * hd;
+          CK(cudaMemcpy(hp, &lay[size_t(h) * P * hd], size_t(P) * hd * 4, cudaMemcpyHostToDevice));
+        }
+      }
+  }
+  CK(cudaMemcpy(s->pos0, p0.data(), sizeof(int) * size_t(n), cudaMemcpyHostToDevice));
+  rc = grx_streams_reset(s.get());
+  if (rc) return rc;
+  rc = build_graph(s.get());
+  if (rc) return rc;
+  *out = s.release();
+  return GRX_OK;
+}
+
+void grx_streams_free(grx_streams* s) { delete s; }
+
+int grx_streams_pos(const grx_streams* s, int i) {
+  if (!s || i < 0 || i >= s->n) return fail(GRX_EINVAL, "bad stream index");
+  int p = 0;
+  cudaSetDevice(s->ar.dev);
+  if (cudaMemcpy(&p, s->pos + i, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return fail(GRX_ECUDA, "read pos");
+  return p;
+}
+
+int64_t grx_streams_launches(const grx_streams* s) { return s ? s->launches : 0; }
+
+void* grx_streams_cuda_stream(const grx_streams* s) { return s ? (void*)s->st : nullptr; }
+
+// Checks that `frames` more frames fit the caches (positions are equal for
+// streams that started from voices of equal length; the longest decides).
+static int check_room(grx_streams* s, int frames) {
+  int maxp = 0;
+  std::vector<int> p(size_t(s->n));
+  CK(cudaMemcpyAsync(p.data(), s->pos, sizeof(int) * size_t(s->n), cudaMemcpyDeviceToHost, s->st));
+  CK(cudaStreamSynchronize(s->st));
+  for (int v : p) maxp = std::max(maxp, v);
+  if (maxp + frames > s->cap)
+    return fail(GRX_ERANGE, "the streams hold " + std::to_string(maxp) + " positions; " + std::to_string(frames) +
+                                " more frames pass the " + std::to_string(s->cap) + " they were made for");
+  return GRX_OK;
+}
+
+int grx_streams_step(grx_streams* s, const float* noise, float* lm_out, float* eos, float* latent, float* scaled) {
+  if (!s || !noise) return fail(GRX_EINVAL, "grx_streams_step: null argument");
+  CK(cudaSetDevice(s->ar.dev));
+  int rc = check_room(s, 1);
+  if (rc) return rc;
+  const size_t nl = size_t(s->n) * s->m->ldim;
+  FrameIO io{s->noise1, nullptr, nullptr, s->eos1, 0, nullptr};
+  CK(cudaMemcpyAsync(s->noise1, noise, nl * 4, cudaMemcpyHostToDevice, s->st));
+  CK(cudaMemcpyAsync(s->io, &io, sizeof io, cudaMemcpyHostToDevice, s->st));
+  CK(cudaGraphLaunch(s->exec, s->st));
+  s->launches += s->per_frame;
+  if (lm_out) CK(cudaMemcpyAsync(lm_out, s->lm_out, size_t(s->n) * s->m->d * 4, cudaMemcpyDeviceToHost, s->st));
+  if (eos) CK(cudaMemcpyAsync(eos, s->eos1, size_t(s->n) * 4, cudaMemcpyDeviceToHost, s->st));
+  if (latent) CK(cudaMemcpyAsync(latent, s->lat1, nl * 4, cudaMemcpyDeviceToHost, s->st));
+  if (scaled) CK(cudaMemcpyAsync(scaled, s->scaled1, nl * 4, cudaMemcpyDeviceToHost, s->st));
+  CK(cudaStreamSynchronize(s->st));
+  return GRX_OK;
+}
+
+int grx_streams_run_device(grx_streams* s, int frames, const float* d_noise, float* d_latent, float* d_eos) {
+  return grx_streams_run_device_timed(s, frames, d_noise, d_latent, d_eos, nullptr);
+}
+
+int grx_streams_run_device_timed(grx_streams* s, int frames, const float* d_noise, float* d_latent, float* d_eos,
+                                 unsigned long long* d_attn_ts) {
+  if (!s || !d_noise || frames < 0) return fail(GRX_EINVAL, "grx_streams_run_device: bad argument");
+  CK(cudaSetDevice(s->ar.dev));
+  int rc = check_room(s, frames);
+  if (rc) return rc;
+  FrameIO io{d_noise, d_latent, nullptr, d_eos, 0, d_attn_ts};
+  CK(cudaMemcpyAsync(s->io, &io, sizeof io, cudaMemcpyHostToDevice, s->st));
+  for (int f = 0; f < frames; f++) CK(cudaGraphLaunch(s->exec, s->st));
+  s->launches += int64_t(frames) * s->per_frame;
+  return GRX_OK;
+}
+
+int grx_streams_sync(grx_streams* s) {
+  if (!s) return fail(GRX_EINVAL, "null streams");
+  CK(cudaSetDevice(s->ar.dev));
+  CK(cudaStreamSynchronize(s->st));
+  CK(cudaGetLastError());
+  return GRX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,150 @@
+// Host-side declarations of the token-loop kernels' launchers.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace grx {
+
+// A Q8_0 weight on the device: int8 values [rows][cols] and the blocks'
+// f16 scales [rows][cols/32], split from the 34-byte GGUF blocks so that
+// both are 16-byte aligned for vector and async loads.
+struct DQ8 {
+  const int8_t* q = nullptr;
+  const uint16_t* d = nullptr;
+  int rows = 0, cols = 0;
+};
+
+// What a Q8_0 product does with its outputs.
+enum Epi {
+  EPI_STORE = 0,    // y[m][n] = c (+ bias)
+  EPI_RESID = 1,    // x[m][n] += c  (kern.Add after the product, nn.go:173-174, 178-179)
+  EPI_ROPE_KV = 2,  // rotate q and k, append k and v to the cache (nn.go:153-171)
+  EPI_GELU_Q8 = 3,  // GELU, then round each 32-block to Q8_0 for the next product (nn.go:176-178)
+};
+
+// Where the qkv product's outputs go (EPI_ROPE_KV).
+struct KVArgs {
+  float* q = nullptr;        // [M][d] rotated queries
+  float* kv = nullptr;       // cache base: [M][L][2][H][cap][hd]
+  const int* pos = nullptr;  // [M] position being written
+  const float* rope = nullptr;  // [cap][hd/2][2] cos, sin
+  int layer = 0, layers = 0, heads = 0, cap = 0, d = 0;
+};
+
+struct EpiArgs {
+  int epi = EPI_STORE;
+  float* y = nullptr;  // STORE / RESID target, row stride ldy
+  int ldy = 0;
+  const float* bias = nullptr;
+  int8_t* q8 = nullptr;  // GELU_Q8 outputs: values [M][N], scales [M][N/32]
+  float* q8s = nullptr;
+  KVArgs kv;
+};
+
+// LayerNorm modes.
+enum LnOut { LN_Q8 = 0, LN_F32 = 1, LN_MOD = 2 };
+
+struct LnArgs {
+  const float* x = nullptr;
+  const float* w = nullptr;  // may be NULL (no affine)
+  const float* b = nullptr;
+  double eps = 1e-5;
+  int mode = LN_Q8;
+  int8_t* q8 = nullptr;
+  float* q8s = nullptr;
+  float* y = nullptr;
+  const float* mod = nullptr;  // LN_MOD: shift at mod[m*ldmod + shift], scale at +scale
+  int ldmod = 0, shift = 0, scale = 0;
+};
+
+void launch_ln(const LnArgs& a, int M, int D, cudaStream_t st);
+
+// C[M][N] = A·Wᵀ with the int8 path's arithmetic (q8int.go:148-223): a
+// (values [M][K], scales [M][K/32]) already rounded to Q8_0.
+void launch_q8_product(const int8_t* a, const float* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st);
+
+// The activations rounded to Q8_0 blocks (quantU8, q8int.go:88-105).
+void launch_quant(const float* x, int M, int K, int8_t* q, float* s, cudaStream_t st);
+
+// Per-frame inputs and outputs of a run, in device memory so that one
+// captured frame graph serves every frame: the frame's slice of each array
+// is base + frame·stride, and the last kernel of a frame moves `frame` on.
+struct FrameIO {
+  const float* noise;  // [frames][M][ldim]
+  float* latent;       // [frames][M][ldim] (may be NULL)
+  float* scaled;       // [frames][M][ldim] (may be NULL)
+  float* eos;          // [frames][M] (may be NULL)
+  int frame;
+  // Optional instrumentation: per frame and layer, the attention kernel's
+  // first CTA start and last CTA end (%globaltimer, ns) [frames][layers][2];
+  // slots must start at {UINT64_MAX, 0}.
+  unsigned long long* attn_ts;
+};
+
+struct AttnArgs {
+  const float* q = nullptr;   // [M][d]
+  const float* kv = nullptr;  // cache, as KVArgs
+  const int* pos = nullptr;   // [M]: keys 0..pos are attended
+  float* out = nullptr;       // [M][d] (may be NULL)
+  int8_t* q8 = nullptr;       // [M][d] output rounded to Q8_0 for attn_out
+  float* q8s = nullptr;       // [M][d/32]
+  int layer = 0, layers = 0, heads = 0, cap = 0, d = 0;
+  const FrameIO* io = nullptr;  // for io->attn_ts (may be NULL)
+};
+
+void launch_attn(const AttnArgs& a, int M, cudaStream_t st);
+
+// Float activations times a Q8_0 (rows kept) or F32 matrix with the
+// reference's float-path order (dot4q8avx / dot4f32avx, gemm.go:195-259).
+enum FEpi {
+  FE_BIAS = 0,    // y = dot + bias
+  FE_COND = 1,    // y = silu(dot + bias + tc)        (lm.go:110-115 and :131-132 with one step)
+  FE_SILU = 2,    // y = silu(dot + bias)             (lm.go:144-145)
+  FE_GATE = 3,    // h += gate · (dot + bias)         (lm.go:146-149)
+  FE_LATENT = 4,  // cur = noise + (dot + bias)/steps; latent, scaled  (lm.go:118-121; speak.go:165-168)
+};
+
+struct FArgs {
+  int epi = FE_BIAS;
+  const float* x = nullptr;  // [M][K], row stride ldx
+  int ldx = 0;
+  const int8_t* wq = nullptr;  // Q8_0 weight (values, scales), or
+  const uint16_t* wd = nullptr;
+  const float* wf = nullptr;  // F32 weight [N][K]
+  int N = 0, K = 0;
+  const float* bias = nullptr;
+  float* y = nullptr;  // [M][N], row stride ldy
+  int ldy = 0;
+  const float* aux = nullptr;  // tc [N] (COND); gate [M][ldaux] (GATE); noise (LATENT)
+  int ldaux = 0;
+  const float* mean = nullptr;  // LATENT: emb_mean, emb_std
+  const float* stdv = nullptr;
+  float* out2 = nullptr;  // LATENT: latent copy, scaled
+  float* out3 = nullptr;
+  float steps = 1.f;
+  // When set: x (FE_BIAS with x_noise) or aux (FE_LATENT with aux_noise)
+  // is this frame's noise, and FE_LATENT also writes the frame's latent and
+  // scaled rows to io.
+  const FrameIO* io = nullptr;
+  bool x_noise = false, aux_noise = false, io_out = false;
+};
+
+void launch_flin(const FArgs& a, int M, cudaStream_t st);
+
+// eos = dotF32Go(lm_out, w) + b (lm.go:193-194), then pos[m] += 1.
+void launch_eos(const float* x, const float* w, float b, int K, const FrameIO* io, float* eos, int* pos, int M,
+                cudaStream_t st);
+
+// io->frame += 1 (the end of a frame).
+void launch_tick(FrameIO* io, cudaStream_t st);
+
+// The flow head's time conditioning (pockettts/lm.go:62-104) from the two
+// embedders' MLP outputs: each row normalized (float64 mean, variance
+// with n−1, + 1e-5) times alpha, then the two averaged.
+void launch_time_norm(const float* y0, const float* y1, const float* a0, const float* a1, int N, int steps,
+                      float* tc, cudaStream_t st);
+
+// Elementwise: y = silu(y0 + tc) for decode steps beyond the first.
+void launch_cond_step(const float* y0, const float* tc, float* sy, int M, int N, cudaStream_t st);
+
+}  // namespace grx

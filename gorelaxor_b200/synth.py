@@ -1,0 +1,288 @@
+"""Synthetic model and voice files for the token-loop workloads.
+
+No weights ship with the reference (its model files are gitignored), so every
+workload runs on seeded synthetic files written in the reference's own
+formats:
+
+* Pocket TTS FlowLM: a GGUF v3 file with the tensor names and settings that
+  ``pockettts.Load`` reads (pockettts/model.go:202-278), and a voice GGUF with
+  the keys ``LoadVoice`` reads (pockettts/voice.go:26-63).
+* Parakeet TDT decoder: a GGUF v3 file with the decoder tensors
+  ``conformer.fromGGUF`` reads (conformer/model.go:305-313).
+* Whisper: a whisper.cpp ggml ``.bin`` file (whisper/model.go:117-226).
+
+Which tensors are Q8_0 follows the converter's placement rule: matrices of at
+least 64 by 64 whose rows are whole blocks (tools/convert_pocket_tts.py:150-156,
+the same rule in tools/convert_nemo.py:289-339). Q8_0 blocks are drawn
+directly from the benchmark's distributions (f16 scale = f16(|N(0, 0.002)|),
+int8 uniform on [-127, 127]); everything else is float32.
+
+The GGUF layout (header, key/value section, tensor table, 32-byte aligned
+data) is the one tools/convert_nemo.py:71-147 writes and
+internal/gguf/gguf.go:292-354 reads.
+"""
+
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass, field
+
+import numpy as np
+
+GGML_F32, GGML_F16, GGML_Q8_0 = 0, 1, 8
+T_U8, T_I8, T_U16, T_I16, T_U32, T_I32, T_F32, T_BOOL, T_STR, T_ARR, T_U64, T_I64, T_F64 = range(13)
+ALIGN = 32
+QK = 32
+Q8_BYTES = 34
+
+
+# --------------------------------------------------------------------- GGUF
+
+
+def _s(s: str) -> bytes:
+    b = s.encode("utf-8")
+    return struct.pack("<Q", len(b)) + b
+
+
+@dataclass
+class Q8:
+    """A Q8_0 matrix [rows][cols] held as raw 34-byte blocks."""
+
+    rows: int
+    cols: int
+    blocks: np.ndarray  # uint8 [rows * cols/32 * 34]
+
+    @property
+    def shape(self):
+        return (self.rows, self.cols)
+
+
+@dataclass
+class GGUFWriter:
+    arch: str
+    kv: list = field(default_factory=list)
+    tensors: list = field(default_factory=list)
+
+    def __post_init__(self):
+        self.add("general.architecture", T_STR, self.arch)
+
+    def add(self, key, vtype, value, etype=-1):
+        self.kv.append((key, vtype, value, etype))
+
+    def u32(self, k, v):
+        self.add(k, T_U32, int(v))
+
+    def i32(self, k, v):
+        self.add(k, T_I32, int(v))
+
+    def f32(self, k, v):
+        self.add(k, T_F32, float(v))
+
+    def str(self, k, v):
+        self.add(k, T_STR, str(v))
+
+    def bool(self, k, v):
+        self.add(k, T_BOOL, bool(v))
+
+    def i32s(self, k, v):
+        self.add(k, T_ARR, [int(x) for x in v], T_I32)
+
+    def tensor(self, name, arr):
+        self.tensors.append((name, arr))
+
+    @staticmethod
+    def _value(vtype, v, etype):
+        if vtype == T_STR:
+            return _s(v)
+        if vtype == T_ARR:
+            out = struct.pack("<IQ", etype, len(v))
+            if etype == T_STR:
+                return out + b"".join(_s(x) for x in v)
+            fmt = {T_I32: "<i", T_U32: "<I", T_F32: "<f", T_F64: "<d"}[etype]
+            return out + b"".join(struct.pack(fmt, x) for x in v)
+        fmt = {T_U32: "<I", T_I32: "<i", T_F32: "<f", T_BOOL: "<?", T_U64: "<Q", T_F64: "<d"}[vtype]
+        return struct.pack(fmt, v)
+
+    def to_bytes(self) -> bytes:
+        infos, datas = [], []
+        off = 0
+        for name, arr in self.tensors:
+            if isinstance(arr, Q8):
+                dims, gtype, data = [arr.cols, arr.rows], GGML_Q8_0, arr.blocks.tobytes()
+            else:
+                a = np.ascontiguousarray(arr, dtype="<f4")
+                dims, gtype, data = (list(reversed(a.shape)) or [1]), GGML_F32, a.tobytes()
+            info = _s(name) + struct.pack("<I", len(dims))
+            info += b"".join(struct.pack("<Q", d) for d in dims)
+            info += struct.pack("<IQ", gtype, off)
+            infos.append(info)
+            datas.append(data)
+            off += len(data)
+            off += (-off) % ALIGN
+        head = b"GGUF" + struct.pack("<IQQ", 3, len(self.tensors), len(self.kv))
+        for k, vtype, v, etype in self.kv:
+            head += _s(k) + struct.pack("<I", vtype) + self._value(vtype, v, etype)
+        head += b"".join(infos)
+        head += b"\0" * ((-len(head)) % ALIGN)
+        parts = [head]
+        for d in datas:
+            parts.append(d)
+            parts.append(b"\0" * ((-len(d)) % ALIGN))
+        return b"".join(parts)
+
+
+# ------------------------------------------------------- value distributions
+
+
+def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    """Round float32 to IEEE half, ties to even (numpy's astype does RNE)."""
+    return np.asarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def rand_q8(rng: np.random.Generator, rows: int, cols: int, scale_sd: float = 0.002) -> Q8:
+    """Q8_0 blocks with f16 scale f16(|N(0, scale_sd)|) and int8 uniform on
+    [-127, 127]: the benchmark configs' weight distribution."""
+    assert cols % QK == 0
+    nblk = rows * cols // QK
+    d = f32_to_f16_bits(np.abs(rng.normal(0.0, scale_sd, nblk)).astype(np.float32))
+    q = rng.integers(-127, 128, size=(nblk, QK), dtype=np.int16).astype(np.int8)
+    blk = np.empty((nblk, Q8_BYTES), dtype=np.uint8)
+    blk[:, 0:2] = d.view(np.uint8).reshape(nblk, 2)
+    blk[:, 2:] = q.view(np.uint8)
+    return Q8(rows, cols, blk.reshape(-1))
+
+
+def q8_dequant(w: Q8) -> np.ndarray:
+    """Q8_0 blocks widened to float32: f16 scale times int8 (exact)."""
+    b = w.blocks.reshape(-1, Q8_BYTES)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
+    q = b[:, 2:].view(np.int8).astype(np.float32)
+    return (q * d).reshape(w.rows, w.cols)
+
+
+def _n(rng, shape, sd):
+    return rng.normal(0.0, sd, shape).astype(np.float32)
+
+
+# ------------------------------------------------------------ Pocket TTS
+
+
+@dataclass
+class FlowLMConfig:
+    d: int = 1024
+    heads: int = 16
+    ff: int = 4096
+    layers: int = 6
+    ldim: int = 32
+    flow_dim: int = 512
+    flow_depth: int = 1
+    decode_steps: int = 1
+    temperature: float = 0.3
+    max_period: float = 10000.0
+    sha: str = "synthetic-flowlm-seed0"
+
+
+def flowlm_tensors(cfg: FlowLMConfig, seed: int = 0) -> dict:
+    """Every tensor of a synthetic FlowLM, in the converter's names."""
+    rng = np.random.default_rng(seed)
+    d, ff, ld, fd = cfg.d, cfg.ff, cfg.ldim, cfg.flow_dim
+    t: dict = {}
+    for i in range(cfg.layers):
+        p = f"lm.blk.{i}."
+        t[p + "norm1.weight"] = 1.0 + _n(rng, d, 0.1)
+        t[p + "norm1.bias"] = _n(rng, d, 0.1)
+        t[p + "norm2.weight"] = 1.0 + _n(rng, d, 0.1)
+        t[p + "norm2.bias"] = _n(rng, d, 0.1)
+        t[p + "attn_qkv.weight"] = rand_q8(rng, 3 * d, d)
+        t[p + "attn_out.weight"] = rand_q8(rng, d, d)
+        t[p + "ff1.weight"] = rand_q8(rng, ff, d)
+        t[p + "ff2.weight"] = rand_q8(rng, d, ff)
+    t["lm.input.weight"] = _n(rng, (d, ld), 1.0 / np.sqrt(ld))
+    t["lm.bos"] = _n(rng, ld, 1.0)
+    t["lm.bos_voice"] = _n(rng, d, 1.0)
+    t["lm.out_norm.weight"] = 1.0 + _n(rng, d, 0.1)
+    t["lm.out_norm.bias"] = _n(rng, d, 0.1)
+    t["lm.eos.weight"] = _n(rng, (1, d), 1.0 / np.sqrt(d))
+    t["lm.eos.bias"] = np.array([-2.0], dtype=np.float32)
+    t["lm.emb_mean"] = _n(rng, ld, 0.1)
+    t["lm.emb_std"] = (0.5 + np.abs(_n(rng, ld, 1.0))).astype(np.float32)
+    t["flow.cond.weight"] = rand_q8(rng, fd, d)
+    t["flow.cond.bias"] = _n(rng, fd, 0.02)
+    t["flow.input.weight"] = _n(rng, (fd, ld), 1.0 / np.sqrt(ld))
+    t["flow.input.bias"] = _n(rng, fd, 0.02)
+    half = 128
+    for k in range(2):
+        p = f"flow.time.{k}."
+        t[p + "freqs"] = np.exp(-np.log(10000.0) * np.arange(half) / half).astype(np.float32)
+        t[p + "fc1.weight"] = rand_q8(rng, fd, 2 * half)
+        t[p + "fc1.bias"] = _n(rng, fd, 0.02)
+        t[p + "fc2.weight"] = rand_q8(rng, fd, fd)
+        t[p + "fc2.bias"] = _n(rng, fd, 0.02)
+        t[p + "norm.alpha"] = 1.0 + _n(rng, fd, 0.1)
+    for i in range(cfg.flow_depth):
+        p = f"flow.res.{i}."
+        t[p + "norm.weight"] = 1.0 + _n(rng, fd, 0.1)
+        t[p + "norm.bias"] = _n(rng, fd, 0.1)
+        t[p + "fc1.weight"] = rand_q8(rng, fd, fd)
+        t[p + "fc1.bias"] = _n(rng, fd, 0.02)
+        t[p + "fc2.weight"] = rand_q8(rng, fd, fd)
+        t[p + "fc2.bias"] = _n(rng, fd, 0.02)
+        t[p + "ada.weight"] = rand_q8(rng, 3 * fd, fd)
+        t[p + "ada.bias"] = _n(rng, 3 * fd, 0.02)
+    t["flow.final.ada.weight"] = rand_q8(rng, 2 * fd, fd)
+    t["flow.final.ada.bias"] = _n(rng, 2 * fd, 0.02)
+    t["flow.final.out.weight"] = _n(rng, (ld, fd), 1.0 / np.sqrt(fd))
+    t["flow.final.out.bias"] = _n(rng, ld, 0.02)
+    return t
+
+
+def flowlm_gguf(cfg: FlowLMConfig, tensors: dict) -> bytes:
+    g = GGUFWriter("pockettts")
+    g.str("general.name", "Pocket TTS synthetic")
+    g.str("general.source.sha256", cfg.sha)
+    g.u32("pockettts.latent_dim", cfg.ldim)
+    g.u32("pockettts.lm.d_model", cfg.d)
+    g.u32("pockettts.lm.heads", cfg.heads)
+    g.f32("pockettts.lm.max_period", cfg.max_period)
+    g.u32("pockettts.lm.layers", cfg.layers)
+    g.u32("pockettts.lm.ff", cfg.ff)
+    g.u32("pockettts.flow.dim", cfg.flow_dim)
+    g.u32("pockettts.flow.depth", cfg.flow_depth)
+    g.f32("pockettts.temperature", cfg.temperature)
+    g.u32("pockettts.decode_steps", cfg.decode_steps)
+    g.f32("pockettts.eos_threshold", -4.0)
+    g.u32("pockettts.min_frames_before_eos", 6)
+    for name, arr in tensors.items():
+        g.tensor(name, arr)
+    return g.to_bytes()
+
+
+def voice_tensors(cfg: FlowLMConfig, positions: int = 64, seed: int = 1) -> dict:
+    """A voice prefill: per layer, keys and values [positions][d] of N(0,1)."""
+    rng = np.random.default_rng(seed)
+    t = {}
+    for i in range(cfg.layers):
+        t[f"voice.{i}.k"] = _n(rng, (positions, cfg.d), 1.0)
+        t[f"voice.{i}.v"] = _n(rng, (positions, cfg.d), 1.0)
+    return t
+
+
+def voice_gguf(cfg: FlowLMConfig, tensors: dict) -> bytes:
+    positions = next(iter(tensors.values())).shape[0]
+    g = GGUFWriter("pockettts-voice")
+    g.str("general.name", "synthetic voice")
+    g.str("pockettts.voice.model.sha256", cfg.sha)
+    g.u32("pockettts.voice.layers", cfg.layers)
+    g.u32("pockettts.voice.positions", positions)
+    for name, arr in tensors.items():
+        g.tensor(name, arr)
+    return g.to_bytes()
+
+
+def noise_frames(seed: int, frames: int, ldim: int, temperature: float) -> np.ndarray:
+    """Per-frame flow-head noise N(0,1)·√temperature (speak.go:148-154 draws
+    it from Go's PCG; the reference tests inject it, ref_test.go:168-172, and
+    so does this harness)."""
+    rng = np.random.default_rng(10_000 + seed)
+    std = np.float32(np.sqrt(np.float64(np.float32(temperature))))
+    return (rng.normal(0.0, 1.0, (frames, ldim)).astype(np.float32) * std).astype(np.float32)

@@ -1,0 +1,127 @@
+/*
+ * grx.h — the C ABI of the B200 token-loop library (libgrx.so).
+ *
+ * It replaces, for gorelaxor's autoregressive token loops, the Go calls
+ * listed beside each entry point (paths are inside the gorelaxor source
+ * tree). Plain pointers and sizes only; every call returns 0 or a negative
+ * GRX_E* code and never aborts; grx_last_error() gives the calling thread's
+ * message. Host buffers are the caller's; device memory is the library's.
+ * One handle lives on one device. Model handles may be shared by threads;
+ * a stream set is driven by one thread at a time (like the reference's
+ * tstate, pockettts/nn.go:120).
+ */
+#ifndef GRX_H
+#define GRX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GRX_OK 0
+#define GRX_EINVAL -1     /* bad argument or shape (the reference panics or returns an error) */
+#define GRX_EFORMAT -2    /* a model or voice file that does not parse or fit (internal/gguf) */
+#define GRX_ENOMEM -3     /* device allocation failed */
+#define GRX_ECUDA -4      /* a CUDA call failed */
+#define GRX_ERANGE -5     /* a stream ran past the positions its state was made for */
+#define GRX_ENODEV -6     /* no such device */
+
+/* The calling thread's last error message (empty if none); returns the
+ * message length. */
+int grx_last_error(char* buf, size_t len);
+/* Number of CUDA devices the library sees. */
+int grx_device_count(void);
+
+/* ------------------------------------------------------------- GGUF ----
+ * internal/gguf: the subset the token loops read (v2/v3; F32, F16, BF16,
+ * Q8_0 tensors), with the reference's hostile-input checks
+ * (internal/gguf/gguf.go:292-354). */
+typedef struct grx_gguf grx_gguf;
+/* gguf.Parse, internal/gguf/gguf.go:262-274 (copies the bytes). */
+int grx_gguf_open(const void* bytes, size_t len, grx_gguf** out);
+void grx_gguf_close(grx_gguf* f);
+/* File.Int / File.Float / File.String, gguf.go:416-460; def when absent. */
+int64_t grx_gguf_int(const grx_gguf* f, const char* key, int64_t def);
+double grx_gguf_float(const grx_gguf* f, const char* key, double def);
+int grx_gguf_string(const grx_gguf* f, const char* key, char* buf, size_t len);
+/* The tensor's type (0 F32, 1 F16, 8 Q8_0, 30 BF16) and GGUF dims
+ * (dims[0] fastest); returns the number of dims, or GRX_EINVAL if absent. */
+int grx_gguf_tensor(const grx_gguf* f, const char* name, int* type, int64_t dims[4]);
+/* File.Float32, gguf.go:498-523: the tensor widened to float32. */
+int grx_gguf_float32(const grx_gguf* f, const char* name, float* dst, size_t n);
+
+/* ------------------------------------------------ operator (kern) ------
+ * kern.Weight and kern.Linear (internal/kern/kern.go:41-201) on the GPU. */
+typedef struct grx_weight grx_weight;
+/* kern.NewQ8, kern.go:76-84: rows×cols as 34-byte Q8_0 blocks. */
+int grx_weight_q8(int device, const void* blocks, int rows, int cols, grx_weight** out);
+/* kern.NewF32, kern.go:53-58. */
+int grx_weight_f32(int device, const float* v, int rows, int cols, grx_weight** out);
+/* kern.Weight.Pack + DropRows, kern.go:89-103: after this every product
+ * with the weight takes the int8 path, a single row too. */
+int grx_weight_drop_rows(grx_weight* w);
+void grx_weight_free(grx_weight* w);
+/* kern.Linear, kern.go:199 (MatMul dispatch :185-196): dst[m][rows] =
+ * x[m][cols]·Wᵀ + bias (bias may be NULL). A Q8_0 weight with dropped rows,
+ * or any m ≥ 2, takes the int8 path (activations rounded to Q8_0 blocks,
+ * q8int.go:148-223); otherwise the float path (gemm.go:195-259). Host
+ * buffers; synchronous. */
+int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, float* dst);
+
+/* ------------------------------------------- Pocket TTS FlowLM ---------
+ * pockettts.Model (pockettts/model.go:14) restricted to the flow LM and
+ * its flow head; Mimi and the text path stay with the caller. */
+typedef struct grx_flowlm grx_flowlm;
+typedef struct grx_voice grx_voice;
+typedef struct grx_streams grx_streams;
+
+/* pockettts.Load, model.go:202-322 (the flow LM's tensors and settings),
+ * with the upload to `device`. */
+int grx_flowlm_load(const void* gguf, size_t len, int device, grx_flowlm** out);
+void grx_flowlm_free(grx_flowlm* m);
+/* Model dims: d, heads, ff, layers, latent dim, flow dim, flow depth,
+ * decode steps (any pointer may be NULL). */
+int grx_flowlm_dims(const grx_flowlm* m, int* d, int* heads, int* ff, int* layers, int* ldim, int* fdim, int* depth,
+                    int* steps);
+/* Model.LoadVoice, voice.go:26-63 (kept on the host until streams use it). */
+int grx_voice_load(grx_flowlm* m, const void* gguf, size_t len, grx_voice** out);
+/* A voice from raw caches: kv is [layers][2][positions][d] float32. */
+int grx_voice_raw(grx_flowlm* m, int positions, const float* kv, grx_voice** out);
+void grx_voice_free(grx_voice* v);
+
+/* n streams, stream i starting from voices[i] (speakChunk's
+ * v.st.clone(...), speak.go:117), each with room for max_frames frames. */
+int grx_streams_create(grx_flowlm* m, int n, const grx_voice* const* voices, int max_frames, grx_streams** out);
+void grx_streams_free(grx_streams* s);
+/* Puts every stream back at its voice prompt and the next frame at bos. */
+int grx_streams_reset(grx_streams* s);
+/* One frame for every stream: flowLM.step then flowHead.sample
+ * (pockettts/lm.go:185-195, 108-124; speak.go:146-174), the raw latent fed
+ * back on the device. noise is [n][ldim]. Outputs (host, any may be NULL):
+ * lm_out [n][d], eos [n], latent [n][ldim], scaled [n][ldim] (the latent
+ * times emb_std plus emb_mean, what speak.go:165-173 sends to Mimi). */
+int grx_streams_step(grx_streams* s, const float* noise, float* lm_out, float* eos, float* latent, float* scaled);
+/* `frames` frames with the same meaning, device-resident in and out:
+ * d_noise [frames][n][ldim], d_latent [frames][n][ldim], d_eos
+ * [frames][n] (device pointers on the stream set's device; d_eos may be
+ * NULL). Asynchronous on the library's stream; grx_streams_sync waits. */
+int grx_streams_run_device(grx_streams* s, int frames, const float* d_noise, float* d_latent, float* d_eos);
+int grx_streams_sync(grx_streams* s);
+/* grx_streams_run_device with instrumentation: d_attn_ts (device,
+ * [frames][layers][2] uint64, each pair preset to {UINT64_MAX, 0}) gets each
+ * attention kernel's first-CTA start and last-CTA end in %globaltimer ns. */
+int grx_streams_run_device_timed(grx_streams* s, int frames, const float* d_noise, float* d_latent, float* d_eos,
+                                 unsigned long long* d_attn_ts);
+/* The cudaStream_t the stream set's work runs on (for events). */
+void* grx_streams_cuda_stream(const grx_streams* s);
+/* Positions held by stream i (voice prompt plus frames so far). */
+int grx_streams_pos(const grx_streams* s, int i);
+/* Device kernel launches issued by this stream set since creation. */
+int64_t grx_streams_launches(const grx_streams* s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GRX_H */

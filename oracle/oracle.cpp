@@ -1,0 +1,284 @@
+// TEST INFRASTRUCTURE ONLY: C entry points of the CPU oracle, loaded by
+// tests/ (ctypes), __graft_entry__.smoke() and bench.py's CPU-baseline leg.
+// The product (gorelaxor_b200/csrc) never links or loads this library.
+//
+// Parity status: the kernel layer is pinned against the reference's own
+// known answers and converter fixtures (tests/golden, made by
+// tests/golden/make_golden.py from tools/convert_nemo.py); the model-level
+// restatement follows the reference line by line but no reference tensor
+// dumps exist to pin it end to end (the reference ships none).
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <thread>
+
+#include "flowlm.h"
+
+using namespace orc;
+
+namespace {
+
+struct OFlowLM {
+  FlowLM m;
+  std::map<std::string, Weight> w;
+  std::map<std::string, const float*> v;
+  std::vector<std::vector<float>> tc;
+  int decode_steps = 1;
+  std::string err;
+};
+
+Weight get_w(OFlowLM* o, const std::string& name) {
+  auto it = o->w.find(name);
+  if (it == o->w.end()) {
+    o->err = "missing " + name;
+    return Weight{};
+  }
+  return it->second;
+}
+
+const float* get_v(OFlowLM* o, const std::string& name) {
+  auto it = o->v.find(name);
+  if (it == o->v.end()) {
+    o->err = "missing " + name;
+    return nullptr;
+  }
+  return it->second;
+}
+
+}  // namespace
+
+extern "C" {
+
+// ---- kernel layer -------------------------------------------------------
+
+float orc_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
+uint16_t orc_f32_to_f16(float f) { return f32_to_f16(f); }
+float orc_expf_go(float x) { return expf_go(x); }
+float orc_exp_avx(float x) { return exp_avx(x); }
+float orc_gelu_go(float x) { return gelu_go(x); }
+float orc_gelu_avx(float x) { return gelu_avx(x); }
+float orc_silu_go(float x) { return silu_go(x); }
+float orc_silu_avx(float x) { return silu_avx(x); }
+float orc_expsub(float* x, int n, float mx) { return expsub_vec(x, n, mx); }
+void orc_gelu_vec(float* x, int n) { gelu_vec(x, n); }
+void orc_silu_vec(float* x, int n) { silu_vec(x, n); }
+
+void orc_quant_act(int8_t* q, float* sc, const float* x, int nb) { quant_q8_act(q, sc, x, nb); }
+
+// kern.Linear with the reference's dispatch. type: 0 F32, 1 F16, 2 Q8_0.
+void orc_linear(float* dst, const float* x, int m, int type, const void* w, int rows, int cols, int dropped,
+                const float* bias) {
+  Weight wt;
+  wt.rows = rows;
+  wt.cols = cols;
+  wt.type = WType(type);
+  wt.f = (const float*)w;
+  wt.h = (const uint16_t*)w;
+  wt.q = (const uint8_t*)w;
+  wt.dropped = dropped != 0;
+  linear(dst, x, m, wt, bias);
+}
+
+void orc_layer_norm_pt(float* dst, const float* src, int rows, int n, const float* w, const float* b, double eps) {
+  layer_norm_pt(dst, src, rows, n, w, b, eps);
+}
+
+void orc_rope_table(float* cs, int head_dim, double period, int positions) {
+  auto f = rope_freqs(head_dim, period);
+  int nf = int(f.size());
+  for (int p = 0; p < positions; p++)
+    for (int i = 0; i < nf; i++) rope_cs(f[size_t(i)], p, cs + (long(p) * nf + i) * 2, cs + (long(p) * nf + i) * 2 + 1);
+}
+
+void orc_attend_one(float* out, const float* q, const float* kc, const float* vc, int nk, int d, int heads) {
+  attend_one(out, q, kc, vc, nk, d, heads);
+}
+
+// ---- FlowLM -------------------------------------------------------------
+
+void* orc_flowlm_new(int d, int heads, int ff, int layers, int ldim, int fd, int depth, double period) {
+  auto* o = new OFlowLM();
+  o->m.d = d;
+  o->m.heads = heads;
+  o->m.ff = ff;
+  o->m.ldim = ldim;
+  o->m.fd = fd;
+  o->m.layers.resize(size_t(layers));
+  o->m.res.resize(size_t(depth));
+  o->m.freqs = rope_freqs(d / heads, period);
+  return o;
+}
+
+void orc_flowlm_free(void* h) { delete (OFlowLM*)h; }
+
+// Registers one tensor (the caller keeps the memory alive). Matrices are
+// [rows][cols]; Q8_0 rows are 34-byte blocks.
+void orc_flowlm_tensor(void* h, const char* name, int type, int rows, int cols, const void* p) {
+  auto* o = (OFlowLM*)h;
+  Weight w;
+  w.rows = rows;
+  w.cols = cols;
+  w.type = WType(type);
+  w.f = (const float*)p;
+  w.q = (const uint8_t*)p;
+  o->w[name] = w;
+  o->v[name] = (const float*)p;
+}
+
+// Binds the registered tensors (pockettts/model.go:240-278) and computes
+// the time conditions once (speak.go:57). Returns 0 or -1 (see orc_error).
+int orc_flowlm_ready(void* h, int decode_steps) {
+  auto* o = (OFlowLM*)h;
+  FlowLM& m = o->m;
+  char b[128];
+  for (size_t i = 0; i < m.layers.size(); i++) {
+    std::snprintf(b, sizeof b, "lm.blk.%zu.", i);
+    std::string p = b;
+    FlowLMLayer& l = m.layers[i];
+    l.norm1w = get_v(o, p + "norm1.weight");
+    l.norm1b = get_v(o, p + "norm1.bias");
+    l.norm2w = get_v(o, p + "norm2.weight");
+    l.norm2b = get_v(o, p + "norm2.bias");
+    l.qkv = get_w(o, p + "attn_qkv.weight");
+    l.out = get_w(o, p + "attn_out.weight");
+    l.ff1 = get_w(o, p + "ff1.weight");
+    l.ff2 = get_w(o, p + "ff2.weight");
+    // pack() drops the transformer's Q8_0 rows (model.go:331-366).
+    for (Weight* w : {&l.qkv, &l.out, &l.ff1, &l.ff2}) w->dropped = w->type == Q8_0;
+  }
+  m.input = get_w(o, "lm.input.weight");
+  m.bos = get_v(o, "lm.bos");
+  m.outw = get_v(o, "lm.out_norm.weight");
+  m.outb = get_v(o, "lm.out_norm.bias");
+  m.eosw = get_w(o, "lm.eos.weight");
+  const float* eb = get_v(o, "lm.eos.bias");
+  m.eosb = eb ? eb[0] : 0;
+  m.mean = get_v(o, "lm.emb_mean");
+  m.stdv = get_v(o, "lm.emb_std");
+  m.cond = get_w(o, "flow.cond.weight");
+  m.condb = get_v(o, "flow.cond.bias");
+  m.finput = get_w(o, "flow.input.weight");
+  m.finputb = get_v(o, "flow.input.bias");
+  for (int k = 0; k < 2; k++) {
+    std::snprintf(b, sizeof b, "flow.time.%d.", k);
+    std::string p = b;
+    TimeEmbed& t = m.time[k];
+    t.freqs = get_v(o, p + "freqs");
+    t.half = 128;
+    t.fc1 = get_w(o, p + "fc1.weight");
+    t.b1 = get_v(o, p + "fc1.bias");
+    t.fc2 = get_w(o, p + "fc2.weight");
+    t.b2 = get_v(o, p + "fc2.bias");
+    t.alpha = get_v(o, p + "norm.alpha");
+  }
+  for (size_t i = 0; i < m.res.size(); i++) {
+    std::snprintf(b, sizeof b, "flow.res.%zu.", i);
+    std::string p = b;
+    ResBlock& r = m.res[i];
+    r.normw = get_v(o, p + "norm.weight");
+    r.normb = get_v(o, p + "norm.bias");
+    r.fc1 = get_w(o, p + "fc1.weight");
+    r.b1 = get_v(o, p + "fc1.bias");
+    r.fc2 = get_w(o, p + "fc2.weight");
+    r.b2 = get_v(o, p + "fc2.bias");
+    r.ada = get_w(o, p + "ada.weight");
+    r.adab = get_v(o, p + "ada.bias");
+  }
+  m.final_ada = get_w(o, "flow.final.ada.weight");
+  m.final_adab = get_v(o, "flow.final.ada.bias");
+  m.fout = get_w(o, "flow.final.out.weight");
+  m.foutb = get_v(o, "flow.final.out.bias");
+  if (!o->err.empty()) return -1;
+  o->decode_steps = decode_steps;
+  o->tc = time_conds(m, decode_steps);
+  return 0;
+}
+
+const char* orc_error(void* h) { return ((OFlowLM*)h)->err.c_str(); }
+
+// The time conditions (fd values per decode step).
+void orc_flowlm_time_conds(void* h, float* out) {
+  auto* o = (OFlowLM*)h;
+  for (size_t i = 0; i < o->tc.size(); i++)
+    std::memcpy(out + i * size_t(o->m.fd), o->tc[i].data(), sizeof(float) * size_t(o->m.fd));
+}
+
+// A stream whose caches hold a voice prompt: kv is [layers][2][n][d]
+// (voice.go:40-62, keys already rotated).
+void* orc_stream_new(void* h, int n, const float* kv) {
+  auto* o = (OFlowLM*)h;
+  int L = int(o->m.layers.size()), d = o->m.d;
+  auto* s = new Stream();
+  s->k.resize(size_t(L));
+  s->v.resize(size_t(L));
+  for (int l = 0; l < L; l++) {
+    const float* kp = kv + (long(l) * 2 + 0) * n * d;
+    const float* vp = kv + (long(l) * 2 + 1) * n * d;
+    s->k[size_t(l)].assign(kp, kp + long(n) * d);
+    s->v[size_t(l)].assign(vp, vp + long(n) * d);
+  }
+  s->pos = n;
+  return s;
+}
+
+void orc_stream_free(void* s) { delete (Stream*)s; }
+int orc_stream_pos(void* s) { return ((Stream*)s)->pos; }
+
+// One frame of speakChunk's loop (speak.go:146-174) with the noise given:
+// step, flow head, scaled latent. latent_in == NULL is the first frame.
+// Outputs may be NULL, except latent_out. trace (may be NULL) gets, per
+// layer, the residual stream after the layer [L][d], then the input
+// projection [d].
+float orc_flowlm_frame(void* h, void* sp, const float* latent_in, const float* noise, float* lm_out, float* latent_out,
+                       float* scaled_out, float* trace) {
+  auto* o = (OFlowLM*)h;
+  const FlowLM& m = o->m;
+  auto* s = (Stream*)sp;
+  std::vector<float> out((size_t)(m.d));
+  Trace tr;
+  float eos = flowlm_step(m, latent_in, *s, out.data(), trace ? &tr : nullptr);
+  if (lm_out) std::memcpy(lm_out, out.data(), sizeof(float) * size_t(m.d));
+  flow_sample(m, out.data(), noise, o->tc, latent_out);
+  if (scaled_out)
+    for (int i = 0; i < m.ldim; i++) scaled_out[i] = latent_out[i] * m.stdv[i] + m.mean[i];
+  if (trace) {
+    size_t L = m.layers.size();
+    for (size_t l = 0; l < L; l++) std::memcpy(trace + l * size_t(m.d), tr.x_after[l].data(), sizeof(float) * size_t(m.d));
+    std::memcpy(trace + L * size_t(m.d), tr.x_in.data(), sizeof(float) * size_t(m.d));
+  }
+  return eos;
+}
+
+// `frames` frames for each of n streams, the first from bos, each next one
+// from the previous latent. noise is [frames][n][ldim]; latents_out
+// [frames][n][ldim], eos_out [frames][n], lm_out (may be NULL)
+// [frames][n][d]. Streams run on `threads` threads, one stream at a time
+// per thread (independent streams, as BASELINE's CPU plan has it).
+void orc_flowlm_run(void* h, int n, void** streams, int frames, const float* noise, float* latents_out, float* eos_out,
+                    float* lm_out, int threads) {
+  auto* o = (OFlowLM*)h;
+  int ld = o->m.ldim, d = o->m.d;
+  std::atomic<int> next{0};
+  auto work = [&]() {
+    for (;;) {
+      int i = next.fetch_add(1);
+      if (i >= n) return;
+      std::vector<float> lat((size_t)ld), prev((size_t)ld);
+      for (int f = 0; f < frames; f++) {
+        const float* nz = noise + (long(f) * n + i) * ld;
+        float* lmo = lm_out ? lm_out + (long(f) * n + i) * d : nullptr;
+        float e = orc_flowlm_frame(h, streams[i], f == 0 ? nullptr : prev.data(), nz, lmo, lat.data(), nullptr, nullptr);
+        std::memcpy(latents_out + (long(f) * n + i) * ld, lat.data(), sizeof(float) * size_t(ld));
+        eos_out[long(f) * n + i] = e;
+        prev = lat;
+      }
+    }
+  };
+  threads = std::max(1, std::min(threads, n));
+  std::vector<std::thread> ts;
+  for (int t = 1; t < threads; t++) ts.emplace_back(work);
+  work();
+  for (auto& t : ts) t.join();
+}
+
+}  // extern "C"

@@ -1,0 +1,190 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes access to the CPU oracle (liboracle.so,
+built from this folder by its Makefile). Imported by tests/, by
+__graft_entry__.smoke() as the checker, and by bench.py's CPU-baseline
+leg; never by the product (gorelaxor_b200/)."""
+
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "_build" / "liboracle.so"
+_lib = None
+
+
+def build() -> Path:
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            build()
+        L = C.CDLL(str(LIB))
+        P, I, F, D = C.c_void_p, C.c_int, C.c_float, C.c_double
+        sig = {
+            "orc_f16_to_f32": (F, [C.c_uint16]),
+            "orc_f32_to_f16": (C.c_uint16, [F]),
+            "orc_expf_go": (F, [F]),
+            "orc_exp_avx": (F, [F]),
+            "orc_gelu_go": (F, [F]),
+            "orc_gelu_avx": (F, [F]),
+            "orc_silu_go": (F, [F]),
+            "orc_silu_avx": (F, [F]),
+            "orc_expsub": (F, [P, I, F]),
+            "orc_gelu_vec": (None, [P, I]),
+            "orc_silu_vec": (None, [P, I]),
+            "orc_quant_act": (None, [P, P, P, I]),
+            "orc_linear": (None, [P, P, I, I, P, I, I, I, P]),
+            "orc_layer_norm_pt": (None, [P, P, I, I, P, P, D]),
+            "orc_rope_table": (None, [P, I, D, I]),
+            "orc_attend_one": (None, [P, P, P, P, I, I, I]),
+            "orc_flowlm_new": (P, [I, I, I, I, I, I, I, D]),
+            "orc_flowlm_free": (None, [P]),
+            "orc_flowlm_tensor": (None, [P, C.c_char_p, I, I, I, P]),
+            "orc_flowlm_ready": (I, [P, I]),
+            "orc_error": (C.c_char_p, [P]),
+            "orc_flowlm_time_conds": (None, [P, P]),
+            "orc_stream_new": (P, [P, I, P]),
+            "orc_stream_free": (None, [P]),
+            "orc_stream_pos": (I, [P]),
+            "orc_flowlm_frame": (F, [P, P, P, P, P, P, P, P]),
+            "orc_flowlm_run": (None, [P, I, P, I, P, P, P, P, I]),
+        }
+        for k, (r, a) in sig.items():
+            f = getattr(L, k)
+            f.restype, f.argtypes = r, a
+        _lib = L
+    return _lib
+
+
+def p(a):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(C.c_void_p)
+
+
+# ------------------------------------------------------------ kernels --
+
+
+def quant_act(x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    nb = x.size // 32
+    q = np.empty(x.size, np.int8)
+    s = np.empty(nb, np.float32)
+    lib().orc_quant_act(p(q), p(s), p(x), nb)
+    return q, s
+
+
+def linear(x: np.ndarray, kind: str, w: np.ndarray, rows: int, cols: int, bias=None, dropped=False):
+    """kern.Linear with the reference's dispatch; kind 'f32' | 'f16' | 'q8_0'."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, cols)
+    out = np.empty((x.shape[0], rows), np.float32)
+    t = {"f32": 0, "f16": 1, "q8_0": 2}[kind]
+    w = np.ascontiguousarray(w)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().orc_linear(p(out), p(x), x.shape[0], t, p(w), rows, cols, int(dropped), p(b))
+    return out
+
+
+def layer_norm_pt(x, w, b, eps):
+    x = np.ascontiguousarray(x, np.float32)
+    rows, n = x.reshape(-1, x.shape[-1]).shape
+    out = np.empty_like(x)
+    lib().orc_layer_norm_pt(p(out), p(x), rows, n, p(w), p(b), eps)
+    return out
+
+
+def attend_one(q, kc, vc, heads):
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(kc, np.float32)
+    vc = np.ascontiguousarray(vc, np.float32)
+    nk, d = kc.shape
+    out = np.empty(d, np.float32)
+    lib().orc_attend_one(p(out), p(q), p(kc), p(vc), nk, d, heads)
+    return out
+
+
+# -------------------------------------------------------------- FlowLM --
+
+
+class FlowLM:
+    """The oracle's FlowLM, from the synthetic generator's tensor dict."""
+
+    def __init__(self, cfg, tensors: dict):
+        from gorelaxor_b200.synth import Q8
+
+        self.cfg = cfg
+        self._keep = []
+        L = lib()
+        self.h = L.orc_flowlm_new(cfg.d, cfg.heads, cfg.ff, cfg.layers, cfg.ldim, cfg.flow_dim, cfg.flow_depth,
+                                  cfg.max_period)
+        for name, arr in tensors.items():
+            if isinstance(arr, Q8):
+                buf = np.ascontiguousarray(arr.blocks)
+                L.orc_flowlm_tensor(self.h, name.encode(), 2, arr.rows, arr.cols, p(buf))
+            else:
+                buf = np.ascontiguousarray(arr, np.float32)
+                rows, cols = (buf.shape if buf.ndim == 2 else (1, buf.size))
+                L.orc_flowlm_tensor(self.h, name.encode(), 0, rows, cols, p(buf))
+            self._keep.append(buf)
+        if L.orc_flowlm_ready(self.h, cfg.decode_steps) != 0:
+            raise RuntimeError(L.orc_error(self.h).decode())
+
+    def time_conds(self):
+        out = np.empty((self.cfg.decode_steps, self.cfg.flow_dim), np.float32)
+        lib().orc_flowlm_time_conds(self.h, p(out))
+        return out
+
+    def stream(self, kv: np.ndarray):
+        """kv: [layers][2][positions][d]."""
+        kv = np.ascontiguousarray(kv, np.float32)
+        return Stream(lib().orc_stream_new(self.h, kv.shape[2], p(kv)))
+
+    def frame(self, st: "Stream", latent, noise, trace=False):
+        c = self.cfg
+        lm_out = np.empty(c.d, np.float32)
+        lat = np.empty(c.ldim, np.float32)
+        sc = np.empty(c.ldim, np.float32)
+        tr = np.empty((c.layers + 1, c.d), np.float32) if trace else None
+        lat_in = None if latent is None else np.ascontiguousarray(latent, np.float32)
+        nz = np.ascontiguousarray(noise, np.float32)
+        eos = lib().orc_flowlm_frame(self.h, st.h, p(lat_in), p(nz), p(lm_out), p(lat), p(sc), p(tr))
+        return dict(lm_out=lm_out, eos=np.float32(eos), latent=lat, scaled=sc, trace=tr)
+
+    def run(self, streams: list, noise: np.ndarray, threads: int = 1, want_lm_out=False):
+        """noise [frames][n][ldim] → latents [frames][n][ldim], eos [frames][n]."""
+        frames, n, ld = noise.shape
+        arr = (C.c_void_p * n)(*[s.h for s in streams])
+        lat = np.empty((frames, n, ld), np.float32)
+        eos = np.empty((frames, n), np.float32)
+        lo = np.empty((frames, n, self.cfg.d), np.float32) if want_lm_out else None
+        nz = np.ascontiguousarray(noise, np.float32)
+        lib().orc_flowlm_run(self.h, n, arr, frames, p(nz), p(lat), p(eos), p(lo), threads)
+        return lat, eos, lo
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_flowlm_free(self.h)
+            self.h = None
+
+
+class Stream:
+    def __init__(self, h):
+        self.h = h
+
+    @property
+    def pos(self):
+        return lib().orc_stream_pos(self.h)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_stream_free(self.h)
+            self.h = None
