@@ -29,6 +29,44 @@ __device__ __forceinline__ float i2f_small(int32_t s) {
   return __fsub_rn(__int_as_float(s + 0x4B400000), 12582912.0f);
 }
 
+// Packed float32 pairs in one 64-bit register (sm_100 .f32x2 operations):
+// each half is the IEEE operation rounded once, so a pair operation gives
+// exactly two scalar results. Values stay packed between operations so no
+// moves are spent repacking them.
+typedef uint64_t f2;
+__device__ __forceinline__ f2 f2fma(f2 a, f2 b, f2 c) {
+  f2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f2 f2mul(f2 a, f2 b) {
+  f2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 f2add(f2 a, f2 b) {
+  f2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 f2dup(float x) {
+  f2 d;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(d) : "f"(x));
+  return d;
+}
+__device__ __forceinline__ f2 f2make(float lo, float hi) {
+  f2 d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ float f2lo(f2 v) { return __uint_as_float(uint32_t(v)); }
+__device__ __forceinline__ float f2hi(f2 v) { return __uint_as_float(uint32_t(v >> 32)); }
+
+// The float whose bits are 1.5·2^23: an int32 s with |s| < 2^22 added to its
+// bit pattern gives the float 1.5·2^23 + s exactly.
+constexpr int32_t MAGIC_BITS = 0x4B400000;
+constexpr float MAGIC = 12582912.0f;
+
 // EXP8, internal/kern/kernels_amd64.s:238-257 (constants :217-233): the
 // reference's vector e^x, lane by lane.
 __device__ __forceinline__ float exp_avx(float x) {

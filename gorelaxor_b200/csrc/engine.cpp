@@ -59,6 +59,9 @@ int device_init(int dev) {
   std::lock_guard<std::mutex> lk(mu);
   if (!done[size_t(dev)]) {
     q8_kernels_init();
+    flow_kernels_init();
+    cudaError_t e = cudaGetLastError();  // attribute calls report here; clear it
+    if (e != cudaSuccess) return fail(GRX_ECUDA, std::string("kernel attributes: ") + cudaGetErrorString(e));
     done[size_t(dev)] = true;
   }
   return GRX_OK;
@@ -111,8 +114,20 @@ DQ8 upload_q8(Arena& ar, const uint8_t* blocks, int rows, int cols, int* rc) {
     d[b] = uint16_t(blk[0] | blk[1] << 8);
     std::memcpy(&q[b * 32], blk + 2, 32);
   }
+  // dw and -1.5·2^23·dw, block-major: the product is exact in float32 for
+  // every finite half (at most 12 significant bits, far from over- or
+  // underflow).
+  std::vector<float> dwT(d.size()), nmT(d.size());
+  for (size_t r = 0; r < size_t(rows); r++)
+    for (size_t b = 0; b < nb; b++) {
+      float dw = f16_to_f32(d[r * nb + b]);
+      dwT[b * rows + r] = dw;
+      nmT[b * rows + r] = -12582912.0f * dw;
+    }
   w.q = ar.upload(q.data(), q.size(), rc);
   w.d = ar.upload(d.data(), d.size(), rc);
+  w.dwT = ar.upload(dwT.data(), dwT.size(), rc);
+  w.nmT = ar.upload(nmT.data(), nmT.size(), rc);
   return w;
 }
 
@@ -175,7 +190,7 @@ struct grx_streams {
   int *pos = nullptr, *pos0 = nullptr;
   float *x = nullptr, *q = nullptr, *lm_out = nullptr, *eos = nullptr, *lat = nullptr, *rope = nullptr;
   int8_t *xq = nullptr, *xqf = nullptr;
-  float *xs = nullptr, *xsf = nullptr;
+  float2 *xs = nullptr, *xsf = nullptr;
   float *y0 = nullptr, *sy = nullptr, *h = nullptr, *mod = nullptr, *mod2 = nullptr, *nrm = nullptr, *mm = nullptr,
         *cur = nullptr;
   float *noise1 = nullptr, *lat1 = nullptr, *scaled1 = nullptr, *eos1 = nullptr;
@@ -276,9 +291,13 @@ int enqueue_frame(grx_streams* s) {
     ln.eps = 1e-5;
     ln.mode = LN_F32;
     ln.y = s->lm_out;
+    ln.eosw = m->eosw;
+    ln.eosb = m->eosb;
+    ln.eos = s->eos;
+    ln.io = s->io;
+    ln.pos = s->pos;
     launch_ln(ln, M, d, st);
-    launch_eos(s->lm_out, m->eosw, m->eosb, d, s->io, s->eos, s->pos, M, st);
-    k += 2;
+    k += 1;
   }
   // Flow head. y = cond·lm_out + b; per step: sy = silu(y + tc_i), net.
   const bool one = m->steps == 1;
@@ -569,7 +588,7 @@ int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, fl
   if (rc) return rc;
   if (int8) {
     int8_t* q = ar.alloc<int8_t>(size_t(m) * k, &rc);
-    float* s = ar.alloc<float>(size_t(m) * (k / 32), &rc);
+    float2* s = ar.alloc<float2>(size_t(m) * (k / 32), &rc);
     if (rc) return rc;
     launch_quant(dx, m, k, q, s, 0);
     EpiArgs e;
@@ -580,6 +599,8 @@ int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, fl
     launch_q8_product(q, s, m, w->q8, e, 0);
   } else {
     if (w->type == 2 ? k % 32 : k % 16) return fail(GRX_EINVAL, "grx_linear: K must be whole blocks");
+    const int kmax = w->type == 2 ? flin_max_k_q8() : flin_max_k();
+    if (k > kmax) return fail(GRX_EINVAL, "grx_linear: float-path K above " + std::to_string(kmax));
     FArgs a;
     a.epi = FE_BIAS;
     a.x = dx;
@@ -906,9 +927,9 @@ int grx_streams_create(grx_flowlm* m, int n, const grx_voice* const* voices, int
   s->eos = s->ar.alloc<float>(size_t(n), &rc);
   s->lat = s->ar.alloc<float>(size_t(n) * ld, &rc);
   s->xq = s->ar.alloc<int8_t>(size_t(n) * d, &rc);
-  s->xs = s->ar.alloc<float>(size_t(n) * d / 32, &rc);
+  s->xs = s->ar.alloc<float2>(size_t(n) * d / 32, &rc);
   s->xqf = s->ar.alloc<int8_t>(size_t(n) * m->ff, &rc);
-  s->xsf = s->ar.alloc<float>(size_t(n) * m->ff / 32, &rc);
+  s->xsf = s->ar.alloc<float2>(size_t(n) * m->ff / 32, &rc);
   s->y0 = s->ar.alloc<float>(size_t(n) * fd, &rc);
   s->sy = s->ar.alloc<float>(size_t(n) * fd, &rc);
   s->h = s->ar.alloc<float>(size_t(n) * fd, &rc);

@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(64) k_attn(AttnArgs a) {
   float s;
   const int8_t qv = quant_lane(o, &s);
   a.q8[(size_t)m * a.d + h * HD + tid] = qv;
-  if (lane == 0) a.q8s[(size_t)m * (a.d / QK) + h * 2 + warp] = s;
+  if (lane == 0) a.q8s[(size_t)m * (a.d / QK) + h * 2 + warp] = make_float2(s, s);
   if (ts) {
     __syncthreads();
     if (tid == 0) {

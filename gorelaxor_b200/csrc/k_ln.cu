@@ -51,6 +51,28 @@ __global__ void k_ln(LnArgs a, int D) {
   }
   if (a.mode == LN_F32) {
     reinterpret_cast<float4*>(a.y + (size_t)m * D)[t] = make_float4(o[0], o[1], o[2], o[3]);
+    if (!a.eosw) return;
+    // eos = dotF32Go(y, w) + b: four strided unfused sums over the row
+    // (gemm.go:294-308), the row and the weight staged on chip.
+    __shared__ float srow[4096], sw[4096];
+    reinterpret_cast<float4*>(srow)[t] = make_float4(o[0], o[1], o[2], o[3]);
+    reinterpret_cast<float4*>(sw)[t] = reinterpret_cast<const float4*>(a.eosw)[t];
+    __syncthreads();
+    if (t < 32) {
+      const int D4 = D & ~3;
+      float s = 0.f;
+      if (t < 4)
+        for (int i = t; i < D4; i += 4) s = __fadd_rn(s, __fmul_rn(srow[i], sw[i]));
+      const float s1 = __shfl_sync(0xffffffffu, s, 1), s2 = __shfl_sync(0xffffffffu, s, 2),
+                  s3 = __shfl_sync(0xffffffffu, s, 3);
+      if (t == 0) {
+        for (int i = D4; i < D; i++) s = __fadd_rn(s, __fmul_rn(srow[i], sw[i]));
+        const float e = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3), a.eosb);
+        if (a.eos) a.eos[m] = e;
+        if (a.io && a.io->eos) a.io->eos[(size_t)a.io->frame * gridDim.x + m] = e;
+        if (a.pos) a.pos[m] += 1;
+      }
+    }
     return;
   }
   if (a.mode == LN_MOD) {
@@ -69,11 +91,14 @@ __global__ void k_ln(LnArgs a, int D) {
 #pragma unroll
   for (int i = 0; i < 4; i++) packed |= uint32_t(uint8_t(quant_val(o[i], amax))) << (8 * i);
   reinterpret_cast<uint32_t*>(a.q8 + (size_t)m * D)[t] = packed;
-  if ((t & 7) == 0) a.q8s[(size_t)m * (D / QK) + t / 8] = quant_scale(amax);
+  if ((t & 7) == 0) {
+    const float sc = quant_scale(amax);
+    a.q8s[(size_t)m * (D / QK) + t / 8] = make_float2(sc, sc);
+  }
 }
 
 // Plain Q8_0 rounding of float rows (the int8 path's quantU8 step alone).
-__global__ void k_quant(const float* x, int K, int8_t* q, float* s) {
+__global__ void k_quant(const float* x, int K, int8_t* q, float2* s) {
   int m = blockIdx.y;
   int i = blockIdx.x * blockDim.x + threadIdx.x;  // one value per thread
   if (i >= K) return;
@@ -81,14 +106,14 @@ __global__ void k_quant(const float* x, int K, int8_t* q, float* s) {
   float sc;
   int8_t qq = quant_lane(v, &sc);
   q[(size_t)m * K + i] = qq;
-  if ((threadIdx.x & 31) == 0) s[(size_t)m * (K / QK) + i / QK] = sc;
+  if ((threadIdx.x & 31) == 0) s[(size_t)m * (K / QK) + i / QK] = make_float2(sc, sc);
 }
 
 }  // namespace
 
 void launch_ln(const LnArgs& a, int M, int D, cudaStream_t st) { k_ln<<<M, D / 4, 0, st>>>(a, D); }
 
-void launch_quant(const float* x, int M, int K, int8_t* q, float* s, cudaStream_t st) {
+void launch_quant(const float* x, int M, int K, int8_t* q, float2* s, cudaStream_t st) {
   dim3 g((K + 255) / 256, M);
   k_quant<<<g, 256, 0, st>>>(x, K, q, s);
 }

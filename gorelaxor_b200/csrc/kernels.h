@@ -11,6 +11,10 @@ namespace grx {
 struct DQ8 {
   const int8_t* q = nullptr;
   const uint16_t* d = nullptr;
+  // For the tensor-core product: per block dw and −1.5·2^23·dw as float32
+  // (both exact; dw is a half), block-major: [cols/32][rows] each.
+  const float* dwT = nullptr;
+  const float* nmT = nullptr;
   int rows = 0, cols = 0;
 };
 
@@ -37,34 +41,9 @@ struct EpiArgs {
   int ldy = 0;
   const float* bias = nullptr;
   int8_t* q8 = nullptr;  // GELU_Q8 outputs: values [M][N], scales [M][N/32]
-  float* q8s = nullptr;
+  float2* q8s = nullptr;
   KVArgs kv;
 };
-
-// LayerNorm modes.
-enum LnOut { LN_Q8 = 0, LN_F32 = 1, LN_MOD = 2 };
-
-struct LnArgs {
-  const float* x = nullptr;
-  const float* w = nullptr;  // may be NULL (no affine)
-  const float* b = nullptr;
-  double eps = 1e-5;
-  int mode = LN_Q8;
-  int8_t* q8 = nullptr;
-  float* q8s = nullptr;
-  float* y = nullptr;
-  const float* mod = nullptr;  // LN_MOD: shift at mod[m*ldmod + shift], scale at +scale
-  int ldmod = 0, shift = 0, scale = 0;
-};
-
-void launch_ln(const LnArgs& a, int M, int D, cudaStream_t st);
-
-// C[M][N] = A·Wᵀ with the int8 path's arithmetic (q8int.go:148-223): a
-// (values [M][K], scales [M][K/32]) already rounded to Q8_0.
-void launch_q8_product(const int8_t* a, const float* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st);
-
-// The activations rounded to Q8_0 blocks (quantU8, q8int.go:88-105).
-void launch_quant(const float* x, int M, int K, int8_t* q, float* s, cudaStream_t st);
 
 // Per-frame inputs and outputs of a run, in device memory so that one
 // captured frame graph serves every frame: the frame's slice of each array
@@ -81,13 +60,49 @@ struct FrameIO {
   unsigned long long* attn_ts;
 };
 
+// LayerNorm modes.
+enum LnOut { LN_Q8 = 0, LN_F32 = 1, LN_MOD = 2 };
+
+struct LnArgs {
+  const float* x = nullptr;
+  const float* w = nullptr;  // may be NULL (no affine)
+  const float* b = nullptr;
+  double eps = 1e-5;
+  int mode = LN_Q8;
+  int8_t* q8 = nullptr;
+  float2* q8s = nullptr;
+  float* y = nullptr;
+  const float* mod = nullptr;  // LN_MOD: shift at mod[m*ldmod + shift], scale at +scale
+  int ldmod = 0, shift = 0, scale = 0;
+  // LN_F32 only, when eosw is set: the end-of-speech logit of each output
+  // row, dotF32Go(y, eosw) + eosb (lm.go:193-194), to eos[m] and the frame's
+  // io->eos slot; then pos[m] += 1 (the frame is done with the position).
+  const float* eosw = nullptr;
+  float eosb = 0.f;
+  float* eos = nullptr;
+  const FrameIO* io = nullptr;
+  int* pos = nullptr;
+};
+
+void launch_ln(const LnArgs& a, int M, int D, cudaStream_t st);
+
+// Activation blocks rounded to Q8_0 travel as int8 values [M][K] and block
+// scales [M][K/32], each scale stored twice as a float2 (s, s): the
+// tensor-core product consumes it as one packed operand.
+//
+// C[M][N] = A·Wᵀ with the int8 path's arithmetic (q8int.go:148-223).
+void launch_q8_product(const int8_t* a, const float2* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st);
+
+// The activations rounded to Q8_0 blocks (quantU8, q8int.go:88-105).
+void launch_quant(const float* x, int M, int K, int8_t* q, float2* s, cudaStream_t st);
+
 struct AttnArgs {
   const float* q = nullptr;   // [M][d]
   const float* kv = nullptr;  // cache, as KVArgs
   const int* pos = nullptr;   // [M]: keys 0..pos are attended
   float* out = nullptr;       // [M][d] (may be NULL)
   int8_t* q8 = nullptr;       // [M][d] output rounded to Q8_0 for attn_out
-  float* q8s = nullptr;       // [M][d/32]
+  float2* q8s = nullptr;      // [M][d/32]
   int layer = 0, layers = 0, heads = 0, cap = 0, d = 0;
   const FrameIO* io = nullptr;  // for io->attn_ts (may be NULL)
 };
@@ -122,6 +137,7 @@ struct FArgs {
   float* out2 = nullptr;  // LATENT: latent copy, scaled
   float* out3 = nullptr;
   float steps = 1.f;
+  int M = 0;  // rows (streams); set by launch_flin
   // When set: x (FE_BIAS with x_noise) or aux (FE_LATENT with aux_noise)
   // is this frame's noise, and FE_LATENT also writes the frame's latent and
   // scaled rows to io.
@@ -137,6 +153,12 @@ void launch_eos(const float* x, const float* w, float b, int K, const FrameIO* i
 
 // io->frame += 1 (the end of a frame).
 void launch_tick(FrameIO* io, cudaStream_t st);
+
+// Per-device kernel attributes (dynamic shared memory limits).
+void flow_kernels_init();
+// The largest K launch_flin takes with F32 and with Q8_0 weights.
+int flin_max_k();
+int flin_max_k_q8();
 
 // The flow head's time conditioning (pockettts/lm.go:62-104) from the two
 // embedders' MLP outputs: each row normalized (float64 mean, variance

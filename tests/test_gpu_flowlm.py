@@ -55,7 +55,7 @@ def test_q8_float_path_bit_exact(have_gpu, n, k):
     assert rel <= TOL
 
 
-@pytest.mark.parametrize("n,k", [(1024, 32), (32, 512), (512, 32), (1, 1024), (6, 48)])
+@pytest.mark.parametrize("n,k", [(1024, 32), (32, 512), (512, 32), (1, 1024), (6, 48), (100, 96)])
 def test_f32_float_path_bit_exact(have_gpu, n, k):
     rng = np.random.default_rng(n * k)
     w = rng.normal(0, 0.2, (n, k)).astype(np.float32)
