@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark: FlowLM frames/s on B200.
+"""Benchmark: FlowLM frames/s on B200 (the batched FlowLM configuration).
 
 Workload (one "step"): 256 independent Pocket-TTS-shaped FlowLM streams
 (6 layers, d 1024, 16 heads × 64, FFN 4096, Q8_0 weights; flow head
@@ -43,6 +43,7 @@ sys.path.insert(0, str(ROOT))
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 METRIC = "FlowLM frames/s (stream-frames per second, whole job)"
 UNIT = "frames/s"
+TRAFFIC_PER_ALGO = 143.51e6 / 139.79e6  # k_attn DRAM bytes / algorithmic bytes, measured (ncu)
 
 
 def peaks():
@@ -197,10 +198,13 @@ def main():
     cfg = synth.FlowLMConfig()
     tensors = synth.flowlm_tensors(cfg, 0)
     model = g.FlowLM(synth.flowlm_gguf(cfg, tensors), device=local)
-    _, kvs = make_workload(B, seed0=1 + rank * B)
+    from gorelaxor_b200.dist import max_over_ranks, partition
+
+    mine = partition(B * world, world, rank)  # this rank's streams of the job (no collective on the step)
+    _, kvs = make_workload(len(mine), seed0=1 + mine.start)
     st = g.Streams(model, [model.voice(kv) for kv in kvs], F)
     del kvs
-    noise = np.stack([synth.noise_frames(1 + rank * B + i, F, cfg.ldim, cfg.temperature) for i in range(B)], axis=1)
+    noise = np.stack([synth.noise_frames(1 + s, F, cfg.ldim, cfg.temperature) for s in mine], axis=1)
     d_noise = torch.from_numpy(noise).cuda()
     d_lat = torch.empty_like(d_noise)
     d_eos = torch.empty((F, B), device="cuda")
@@ -251,22 +255,22 @@ def main():
         dist.barrier()
     ck = clocks.stop()
     launches = st.launches() - launches0
-    total_ms = float(np.sum(step_ms))
-    if dist:
-        t = torch.tensor([total_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+    total_ms = max_over_ranks(float(np.sum(step_ms)), device="cuda")
     frames_total = args.steps * B * F * world
     value = frames_total / (total_ms / 1000)
 
     # attention roofline: algorithmic bytes per launch / its own span
     H, d = cfg.heads, cfg.d
     nk = 64 + np.arange(F) + 1
-    per_launch = B * (H * (nk * 64 * 4 * 2 + 64 * 4) + d * 1 + d // 32 * 4)  # K+V reads, q, q8 out
+    per_launch = B * (H * (nk * 64 * 4 * 2 + 64 * 4) + d * 1 + d // 32 * 8)  # K+V reads, q, Q8 out (s,s)
     per_launch = np.repeat(per_launch[:, None], cfg.layers, axis=1).astype(np.float64)
     durs = np.stack(attn_ns)  # [steps][F][L]
     achieved = float(per_launch.sum() * args.steps / durs.sum())  # B/ns = GB/s
     hbm, peak_kind = peaks()
+    # DRAM bytes per launch: one ncu capture at 66 keys (256 streams, frame 1,
+    # layers 0-1: read+write 143.51 MB against 139.79 MB algorithmic) scaled
+    # to every launch by its algorithmic bytes (the K/V rows dominate both).
+    traffic = float(per_launch.mean()) * TRAFFIC_PER_ALGO
 
     # ---- e2e: the public per-frame call with pinned host buffers ----
     e2e = None
@@ -285,11 +289,7 @@ def main():
                 lat, eos, sc, _ = st_step(st, pin_noise[f], outs[0], pe, outs[1])
             t1 = time.perf_counter()
             e2e_ms.append((t1 - t0) * 1000)
-        em = float(np.sum(e2e_ms))
-        if dist:
-            t = torch.tensor([em], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            em = float(t.item())
+        em = max_over_ranks(float(np.sum(e2e_ms)), device="cuda")
         e2e = {"value": args.e2e_steps * B * F * world / (em / 1000), "unit": UNIT,
                "h2d_bytes_per_step": F * B * cfg.ldim * 4,
                "d2h_bytes_per_step": F * B * (2 * cfg.ldim + 1) * 4,
@@ -319,7 +319,8 @@ def main():
                    "l2": "inputs larger than L2 (KV caches 7.3 GB per GPU)"},
         "e2e": e2e,
         "roofline": {"bound": "hbm", "kernel": "k_attn", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": None,
+                     "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": traffic,
+                     "traffic_unit": "bytes per launch (ncu dram read+write at 66 keys, scaled by key rows)",
                      "note": "algorithmic bytes per launch (K,V rows 0..pos of every head + q + Q8 output) over the "
                              "kernel's own first-CTA-start to last-CTA-end span, every launch of the timed steps"},
         "cpu_baseline": cpu,

@@ -80,6 +80,11 @@ def _sig(lib):
     return lib
 
 
+# Free functions bound when the library loads: destructors that run while
+# the interpreter shuts down must not look up module globals.
+_FREE: dict = {}
+
+
 def lib():
     """libgrx.so, loaded once. Raises if it was not built."""
     global _lib
@@ -87,6 +92,8 @@ def lib():
         if not LIB_PATH.exists():
             raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m gorelaxor_b200.build`")
         _lib = _sig(C.CDLL(str(LIB_PATH)))
+        for n in ("grx_gguf_close", "grx_weight_free", "grx_flowlm_free", "grx_voice_free", "grx_streams_free"):
+            _FREE[n] = getattr(_lib, n)
     return _lib
 
 
@@ -118,10 +125,10 @@ class GGUF:
         _check(lib().grx_gguf_open(data, len(data), C.byref(h)))
         self._h = h
 
-    def __del__(self):
-        if getattr(self, "_h", None):
-            lib().grx_gguf_close(self._h)
-            self._h = None
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_gguf_close"](h)
 
     def int(self, key: str, default: int = -1) -> int:
         return lib().grx_gguf_int(self._h, key.encode(), default)
@@ -173,10 +180,10 @@ class Weight:
         _check(lib().grx_weight_drop_rows(self._h))
         return self
 
-    def __del__(self):
-        if getattr(self, "_h", None):
-            lib().grx_weight_free(self._h)
-            self._h = None
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_weight_free"](h)
 
 
 def linear(w: Weight, x: np.ndarray, bias: np.ndarray | None = None) -> np.ndarray:
@@ -212,20 +219,20 @@ class FlowLM:
         _check(lib().grx_voice_raw(self._h, a.shape[2], _ptr(a), C.byref(h)))
         return Voice(h)
 
-    def __del__(self):
-        if getattr(self, "_h", None):
-            lib().grx_flowlm_free(self._h)
-            self._h = None
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_flowlm_free"](h)
 
 
 class Voice:
     def __init__(self, h):
         self._h = h
 
-    def __del__(self):
-        if getattr(self, "_h", None):
-            lib().grx_voice_free(self._h)
-            self._h = None
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_voice_free"](h)
 
 
 class Streams:
@@ -279,7 +286,7 @@ class Streams:
     def launches(self) -> int:
         return lib().grx_streams_launches(self._h)
 
-    def __del__(self):
-        if getattr(self, "_h", None):
-            lib().grx_streams_free(self._h)
-            self._h = None
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_streams_free"](h)

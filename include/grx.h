@@ -68,7 +68,7 @@ void grx_weight_free(grx_weight* w);
  * or any m ≥ 2, takes the int8 path (activations rounded to Q8_0 blocks,
  * q8int.go:148-223); otherwise the float path (gemm.go:195-259). Host
  * buffers; synchronous. Limits of this build: the float path takes at most
- * 16 rows and K ≤ 1536 (Q8_0) or K ≤ 640 (F32); the int8 path with more
+ * 16 rows and K ≤ 2048 (Q8_0) or K ≤ 1024 (F32); the int8 path with more
  * than 8 rows needs K % 128 == 0, with up to 8 rows N % 32 == 0. */
 int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, float* dst);
 

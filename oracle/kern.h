@@ -451,6 +451,27 @@ inline void matmul_q8_int(float* c, int ldc, const float* a, int lda, int m, con
   }
 }
 
+// Weight.ToQ8, internal/kern/kern.go:139-170: each block of 32 values
+// scaled by its largest magnitude over 127 (float32 division), rounded half
+// away from zero, the scale stored as f16 (the converter's rule,
+// tools/convert_nemo.py:154-167).
+inline void to_q8(uint8_t* out, const float* v, int rows, int cols) {
+  int nb = cols / QK;
+  for (int j = 0; j < rows; j++)
+    for (int b = 0; b < nb; b++) {
+      const float* xs = v + long(j) * cols + b * QK;
+      uint8_t* blk = out + (long(j) * nb + b) * Q8BYTES;
+      float amax = 0;
+      for (int i = 0; i < QK; i++) amax = std::max(amax, std::fabs(xs[i]));
+      float d = amax / 127.f;
+      float id = d != 0 ? 1.f / d : 0.f;
+      uint16_t h = f32_to_f16(d);
+      blk[0] = uint8_t(h & 0xff);
+      blk[1] = uint8_t(h >> 8);
+      for (int i = 0; i < QK; i++) blk[2 + i] = uint8_t(int8_t(std::round(double(xs[i] * id))));
+    }
+}
+
 // MatMul / Linear dispatch, internal/kern/kern.go:185-201 (the useInt
 // case, intMinM = 2, q8int.go:137; m ≤ smallM always on the token loop).
 inline void linear(float* dst, const float* x, int m, const Weight& w, const float* bias) {

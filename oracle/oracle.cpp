@@ -64,6 +64,7 @@ void orc_gelu_vec(float* x, int n) { gelu_vec(x, n); }
 void orc_silu_vec(float* x, int n) { silu_vec(x, n); }
 
 void orc_quant_act(int8_t* q, float* sc, const float* x, int nb) { quant_q8_act(q, sc, x, nb); }
+void orc_to_q8(uint8_t* out, const float* v, int rows, int cols) { to_q8(out, v, rows, cols); }
 
 // kern.Linear with the reference's dispatch. type: 0 F32, 1 F16, 2 Q8_0.
 void orc_linear(float* dst, const float* x, int m, int type, const void* w, int rows, int cols, int dropped,
@@ -253,7 +254,7 @@ float orc_flowlm_frame(void* h, void* sp, const float* latent_in, const float* n
 // from the previous latent. noise is [frames][n][ldim]; latents_out
 // [frames][n][ldim], eos_out [frames][n], lm_out (may be NULL)
 // [frames][n][d]. Streams run on `threads` threads, one stream at a time
-// per thread (independent streams, as BASELINE's CPU plan has it).
+// per thread (independent streams).
 void orc_flowlm_run(void* h, int n, void** streams, int frames, const float* noise, float* latents_out, float* eos_out,
                     float* lm_out, int threads) {
   auto* o = (OFlowLM*)h;

@@ -41,6 +41,7 @@ def lib():
             "orc_gelu_vec": (None, [P, I]),
             "orc_silu_vec": (None, [P, I]),
             "orc_quant_act": (None, [P, P, P, I]),
+            "orc_to_q8": (None, [P, P, I, I]),
             "orc_linear": (None, [P, P, I, I, P, I, I, I, P]),
             "orc_layer_norm_pt": (None, [P, P, I, I, P, P, D]),
             "orc_rope_table": (None, [P, I, D, I]),
@@ -81,6 +82,23 @@ def quant_act(x: np.ndarray):
     s = np.empty(nb, np.float32)
     lib().orc_quant_act(p(q), p(s), p(x), nb)
     return q, s
+
+
+def to_q8(v: np.ndarray) -> np.ndarray:
+    """Weight.ToQ8 (kern.go:139-170) of a [rows][cols] float32 matrix."""
+    v = np.ascontiguousarray(v, np.float32)
+    rows, cols = v.shape
+    out = np.empty(rows * cols // 32 * 34, np.uint8)
+    lib().orc_to_q8(p(out), p(v), rows, cols)
+    return out
+
+
+def f16_to_f32(h: int) -> float:
+    return lib().orc_f16_to_f32(h)
+
+
+def f32_to_f16(f: float) -> int:
+    return lib().orc_f32_to_f16(f)
 
 
 def linear(x: np.ndarray, kind: str, w: np.ndarray, rows: int, cols: int, bias=None, dropped=False):
