@@ -56,6 +56,7 @@ def _sig(lib):
         "grx_weight_drop_rows": (I, [P]),
         "grx_weight_free": (None, [P]),
         "grx_linear": (I, [P, P, I, P, P]),
+        "grx_linear_q8_static": (I, [P, P, I, P, P, P]),
         "grx_flowlm_load": (I, [P, S, I, PP]),
         "grx_flowlm_free": (None, [P]),
         "grx_flowlm_dims": (I, [P] + [C.POINTER(C.c_int)] * 8),
@@ -193,6 +194,18 @@ def linear(w: Weight, x: np.ndarray, bias: np.ndarray | None = None) -> np.ndarr
     b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
     _check(lib().grx_linear(w._h, _ptr(x), x.shape[0], _ptr(b), _ptr(out)))
     return out
+
+
+STATIC_MAX_ELEMS = 1 << 20  # GRX_STATIC_MAX_ELEMS: the largest m × cols of linear_q8_static
+
+
+def linear_q8_static(w: Weight, d_x: int, m: int, d_bias: int | None, d_dst: int, stream: int = 0) -> None:
+    """grx_linear_q8_static: the int8 path of `linear` on caller-owned device
+    buffers (addresses), queued on `stream`, allocating nothing — for hosts
+    whose device memory is all owned by their own allocator. The rounded
+    activations go to one fixed array shared by every call on the device:
+    calls that may overlap on the GPU must be ordered by the caller."""
+    _check(lib().grx_linear_q8_static(w._h, d_x, m, d_bias, d_dst, stream or None))
 
 
 class FlowLM:

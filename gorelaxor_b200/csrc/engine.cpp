@@ -1069,3 +1069,19 @@ int grx_streams_sync(grx_streams* s) {
 }
 
 }  // extern "C"
+
+// Accessors for entry points defined in other files.
+namespace grx {
+
+int set_error(int code, const char* msg) { return fail(code, msg); }
+
+int weight_device(const grx_weight* w) { return w->ar.dev; }
+
+bool weight_q8(const grx_weight* w, const DQ8** q8, bool* dropped) {
+  if (w->type != 2) return false;
+  *q8 = &w->q8;
+  *dropped = w->dropped;
+  return true;
+}
+
+}  // namespace grx

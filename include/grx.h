@@ -25,7 +25,7 @@ extern "C" {
 #define GRX_EFORMAT -2    /* a model or voice file that does not parse or fit (internal/gguf) */
 #define GRX_ENOMEM -3     /* device allocation failed */
 #define GRX_ECUDA -4      /* a CUDA call failed */
-#define GRX_ERANGE -5     /* a stream ran past the positions its state was made for */
+#define GRX_ERANGE -5     /* a stream ran past the positions its state was made for, or a size above a fixed limit */
 #define GRX_ENODEV -6     /* no such device */
 
 /* The calling thread's last error message (empty if none); returns the
@@ -71,6 +71,40 @@ void grx_weight_free(grx_weight* w);
  * 16 rows and K ≤ 2048 (Q8_0) or K ≤ 1024 (F32); the int8 path with more
  * than 8 rows needs K % 128 == 0, with up to 8 rows N % 32 == 0. */
 int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, float* dst);
+
+/* grx_linear_q8_static: the int8 path of grx_linear for callers that must
+ * not allocate GPU memory. No counterpart in the reference: its Go kernels
+ * run on the CPU and take scratch from the Go heap.
+ *
+ * Who needs it: a host that owns every byte of device memory itself — a
+ * serving process whose pool allocator has reserved the GPU's memory up
+ * front, or a real-time audio loop, where cudaMalloc/cudaFree would fail
+ * or stall the device mid-stream. grx_linear cannot serve them: it uploads
+ * its inputs and allocates the rounded activations on every call.
+ *
+ * Same product and dispatch rule as grx_linear's int8 path, bit for bit: w
+ * is a Q8_0 weight with dropped rows, or m >= 2 (otherwise GRX_EINVAL: the
+ * reference takes the float path there, which needs no scratch). d_x
+ * [m][cols], d_bias [rows] (may be NULL) and d_dst [m][rows] are DEVICE
+ * pointers on the weight's device, owned by the caller; work is queued on
+ * `stream` (a cudaStream_t, NULL for the default stream) and not waited
+ * for. The call allocates nothing: the activations rounded to Q8_0 go to one
+ * fixed array in the library's device memory, GRX_STATIC_MAX_ELEMS int8
+ * values plus their block scales (1.25 MiB), which every GPU that loads the
+ * library holds until the process exits. m*cols above GRX_STATIC_MAX_ELEMS
+ * is rejected with GRX_ERANGE before anything is queued.
+ *
+ * The first call on a device looks up that array's device address (with
+ * the device current) and keeps it; make that first call before any stream
+ * capture on the device. All calls share the one array, and each leaves its
+ * rounded activations there: calls that may overlap on the GPU (two
+ * streams, or two threads without ordering) race on it and must be ordered
+ * by the caller. Nothing needs clearing between calls: each call writes all
+ * of the array that it then reads. The same shape limits as grx_linear's
+ * int8 path apply (m > 8: cols % 128 == 0; m <= 8: rows % 32 == 0). */
+#define GRX_STATIC_MAX_ELEMS (1 << 20)
+int grx_linear_q8_static(const grx_weight* w, const float* d_x, int m, const float* d_bias, float* d_dst,
+                         void* stream);
 
 /* ------------------------------------------- Pocket TTS FlowLM ---------
  * pockettts.Model (pockettts/model.go:14) restricted to the flow LM and
