@@ -139,6 +139,29 @@ def run_reference(args, rank, world):
     from gorelaxor_b200 import synth
 
     cores = os.cpu_count() or 1
+    if args.workload == "tdt":
+        cfg = synth.TDTConfig()
+        tensors = synth.tdt_tensors(cfg, 0)
+        streams, frames = min(args.batch, cores), 100
+        tdt_cpu_sample(cfg, tensors, streams, 10, cores)
+        vals, times = [], []
+        for _ in range(args.steps):
+            v, dt = tdt_cpu_sample(cfg, tensors, streams, frames, cores)
+            vals.append(v)
+            times.append(dt)
+        value = float(np.mean(vals))
+        sample = f"{streams} streams x {frames} encoder frames per step, {cores} threads"
+        print(json.dumps({
+            "impl": "reference", "metric": TDT_METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
+            "data": "synthetic (seeded; the reference ships no weights)",
+            "config": {"workload": f"C3 TDT decode, {args.batch} streams x {args.frames} frames (sampled)",
+                       "global_batch": args.batch, "frames": args.frames, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "frames/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
     cfg = synth.FlowLMConfig()
     tensors = synth.flowlm_tensors(cfg, 0)
     streams, frames = min(args.batch, cores), 8
@@ -162,14 +185,132 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+TDT_METRIC = "TDT encoder frames/s (stream-frames decoded per second, whole job)"
+
+
+def tdt_cpu_sample(cfg, tensors, streams, frames, threads):
+    """The oracle's Decode on `threads` host threads: `streams` fresh streams
+    of `frames` encoder frames. Returns frames/s and the wall time."""
+    from gorelaxor_b200 import synth
+    from oracle import oracle as orc
+
+    om = orc.TDT(cfg, tensors)
+    enc = np.stack([synth.encoder_frames(1 + i, frames, cfg.D) for i in range(streams)])
+    t0 = time.perf_counter()
+    om.run(enc, 16 * frames + 1024, threads)
+    dt = time.perf_counter() - t0
+    return streams * frames / dt, dt
+
+
+def run_tdt(args, rank, world, local):
+    """--workload tdt: the Parakeet-TDT-shaped decode loop (C3): `batch`
+    streams per GPU of `frames` N(0,1) encoder frames (640 wide); one step =
+    Model.Decode of every stream (encoder projection + the greedy loop)."""
+    import torch
+
+    import gorelaxor_b200 as g
+    from gorelaxor_b200 import synth
+    from gorelaxor_b200.dist import max_over_ranks, partition
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    B, T = args.batch, args.frames
+    cfg = synth.TDTConfig()
+    tensors = synth.tdt_tensors(cfg, 0)
+    model = g.TDT(synth.tdt_gguf(cfg, tensors), device=local)
+    mine = partition(B * world, world, rank)
+    enc = np.stack([synth.encoder_frames(1 + s, T, cfg.D) for s in mine])
+    cap = 16 * T + 1024
+    b = g.TDTBatch(model, B, T, cap)
+    Ts = [T] * B
+    d_enc = torch.from_numpy(enc).cuda()
+    d_tok = torch.empty((B, cap, 4), dtype=torch.int32, device="cuda")
+    d_cnt = torch.empty(B, dtype=torch.int32, device="cuda")
+    ext = torch.cuda.ExternalStream(b.cuda_stream())
+
+    def one():
+        b.reset()
+        b.decode_device(d_enc.data_ptr(), Ts, d_tok.data_ptr(), d_cnt.data_ptr())
+
+    for _ in range(args.warmup):
+        one()
+    clocks = Clocks(local)
+    l0, i0 = b.launches(), b.iterations()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks.start()
+    ms = []
+    for _ in range(args.steps):
+        b.reset()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        b.decode_device(d_enc.data_ptr(), Ts, d_tok.data_ptr(), d_cnt.data_ptr())
+        e1.record(ext)
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    ck = clocks.stop()
+    launches, iters = b.launches() - l0, b.iterations() - i0
+    total_ms = max_over_ranks(float(np.sum(ms)), device="cuda")
+    value = args.steps * B * T * world / (total_ms / 1000)
+    tokens = int(d_cnt.sum().item())
+
+    e2e = None
+    if args.e2e_steps > 0:
+        pin = torch.from_numpy(enc).pin_memory().numpy()
+        em = []
+        for _ in range(args.e2e_steps):
+            b.reset()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            toks, counts = b.decode(pin, Ts)
+            em.append((time.perf_counter() - t0) * 1000)
+        emax = max_over_ranks(float(np.sum(em)), device="cuda")
+        e2e = {"value": args.e2e_steps * B * T * world / (emax / 1000), "unit": "frames/s",
+               "h2d_bytes_per_step": enc.nbytes, "d2h_bytes_per_step": B * cap * 16 + B * 4,
+               "note": "grx_tdt_decode: encoder output H2D from pinned memory, tokens and counts D2H"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        streams, frames = min(B, cores), 100
+        v, dt = tdt_cpu_sample(cfg, tensors, streams, frames, cores)
+        cpu = {"value": v, "unit": "frames/s", "cores": cores, "kind": "port",
+               "sample": f"{streams} streams x {frames} encoder frames ({dt:.1f} s wall)"}
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": TDT_METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8/f32",
+        "data": "synthetic (seeded Q8_0 decoder, N(0,1) encoder output; the reference ships no weights)",
+        "config": {"workload": f"C3 TDT decode: {B} streams x {T} encoder frames per GPU", "global_batch": B * world,
+                   "frames": T, "parallelism": f"streams partitioned, {world} GPU(s), no collective",
+                   "l2": "encoder output 245 MB per GPU, larger than L2"},
+        "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck,
+        "loop": {"iterations_per_step": iters / args.steps, "tokens_last_step": tokens},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="grx", choices=["grx", "reference"])
-    ap.add_argument("--batch", type=int, default=256, help="streams per GPU")
-    ap.add_argument("--frames", type=int, default=512)
+    ap.add_argument("--workload", default="flowlm", choices=["flowlm", "tdt"])
+    ap.add_argument("--batch", type=int, default=None, help="streams per GPU (flowlm 256, tdt 128)")
+    ap.add_argument("--frames", type=int, default=None, help="frames per stream (flowlm 512, tdt 750)")
     ap.add_argument("--e2e-steps", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -177,8 +318,13 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
+    tdt = args.workload == "tdt"
+    args.batch = args.batch or (128 if tdt else 256)
+    args.frames = args.frames or (750 if tdt else 512)
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if tdt:
+        return run_tdt(args, rank, world, local)
 
     import torch
 

@@ -73,6 +73,19 @@ def _sig(lib):
         "grx_streams_pos": (I, [P, I]),
         "grx_streams_launches": (L, [P]),
         "grx_streams_cuda_stream": (P, [P]),
+        "grx_tdt_load": (I, [P, S, I, PP]),
+        "grx_tdt_free": (None, [P]),
+        "grx_tdt_dims": (I, [P] + [C.POINTER(C.c_int)] * 8),
+        "grx_tdt_batch_create": (I, [P, I, I, I, PP]),
+        "grx_tdt_batch_free": (None, [P]),
+        "grx_tdt_batch_reset": (I, [P]),
+        "grx_tdt_state_get": (I, [P, I, P, P, C.POINTER(C.c_int)]),
+        "grx_tdt_state_set": (I, [P, I, P, P, I]),
+        "grx_tdt_decode": (I, [P, P, P, P, P, P]),
+        "grx_tdt_decode_device": (I, [P, P, P, P, P, P]),
+        "grx_tdt_batch_cuda_stream": (P, [P]),
+        "grx_tdt_batch_launches": (L, [P]),
+        "grx_tdt_batch_iterations": (L, [P]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -93,7 +106,8 @@ def lib():
         if not LIB_PATH.exists():
             raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m gorelaxor_b200.build`")
         _lib = _sig(C.CDLL(str(LIB_PATH)))
-        for n in ("grx_gguf_close", "grx_weight_free", "grx_flowlm_free", "grx_voice_free", "grx_streams_free"):
+        for n in ("grx_gguf_close", "grx_weight_free", "grx_flowlm_free", "grx_voice_free", "grx_streams_free",
+                  "grx_tdt_free", "grx_tdt_batch_free"):
             _FREE[n] = getattr(_lib, n)
     return _lib
 
@@ -303,3 +317,88 @@ class Streams:
         h, self._h = getattr(self, "_h", None), None
         if h:
             _free["grx_streams_free"](h)
+
+
+# ------------------------------------------------------------ TDT decoder
+
+TOKEN = np.dtype([("id", "<i4"), ("frame", "<i4"), ("duration", "<i4"), ("p", "<f4")])  # grx_tdt_token
+
+
+class TDT:
+    """The decoder of a conformer.Model (RNN-T or TDT head) on one device:
+    conformer.FromGGUF's pred.* and joint.* part (model.go:306-314)."""
+
+    def __init__(self, gguf: bytes, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().grx_tdt_load(gguf, len(gguf), device, C.byref(h)))
+        self._h = h
+        self.device = device
+        v = [C.c_int() for _ in range(8)]
+        _check(lib().grx_tdt_dims(h, *[C.byref(x) for x in v]))
+        (self.hidden, self.layers, self.vocab, self.joint, self.d_enc, self.n_durations, self.blank,
+         is_tdt) = [x.value for x in v]
+        self.is_tdt = bool(is_tdt)
+
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_tdt_free"](h)
+
+
+class TDTBatch:
+    """n DecoderStates decoded together: Model.Decode for each stream."""
+
+    def __init__(self, model: TDT, n: int, max_t: int, cap: int):
+        self.model, self.n, self.max_t, self.cap = model, n, max_t, cap
+        h = C.c_void_p()
+        _check(lib().grx_tdt_batch_create(model._h, n, max_t, cap, C.byref(h)))
+        self._h = h
+
+    def reset(self):
+        _check(lib().grx_tdt_batch_reset(self._h))
+
+    def state(self, i: int):
+        """Stream i's DecoderState: (h [layers][hidden], c, last)."""
+        m = self.model
+        hh = np.empty((m.layers, m.hidden), np.float32)
+        cc = np.empty_like(hh)
+        last = C.c_int()
+        _check(lib().grx_tdt_state_get(self._h, i, _ptr(hh), _ptr(cc), C.byref(last)))
+        return hh, cc, last.value
+
+    def set_state(self, i: int, h: np.ndarray, c: np.ndarray, last: int):
+        h = np.ascontiguousarray(h, np.float32)
+        c = np.ascontiguousarray(c, np.float32)
+        _check(lib().grx_tdt_state_set(self._h, i, _ptr(h), _ptr(c), last))
+
+    def decode(self, enc: np.ndarray, T, frame_offset=None):
+        """enc [n][max_t][d_enc]; T [n]. Returns each stream's tokens (TOKEN
+        records) and the full counts (which may exceed cap)."""
+        e = np.ascontiguousarray(enc, np.float32).reshape(self.n, self.max_t, self.model.d_enc)
+        t = np.ascontiguousarray(T, np.int32).reshape(self.n)
+        off = None if frame_offset is None else np.ascontiguousarray(frame_offset, np.int32).reshape(self.n)
+        toks = np.zeros((self.n, self.cap), TOKEN)
+        counts = np.zeros(self.n, np.int32)
+        _check(lib().grx_tdt_decode(self._h, _ptr(e), _ptr(t), _ptr(off), toks.ctypes.data, _ptr(counts)))
+        return [toks[i, :min(int(counts[i]), self.cap)] for i in range(self.n)], counts
+
+    def decode_device(self, d_enc: int, T, d_tokens: int, d_counts: int, frame_offset=None):
+        t = np.ascontiguousarray(T, np.int32).reshape(self.n)
+        off = None if frame_offset is None else np.ascontiguousarray(frame_offset, np.int32).reshape(self.n)
+        _check(lib().grx_tdt_decode_device(self._h, C.c_void_p(d_enc), _ptr(t), _ptr(off), C.c_void_p(d_tokens),
+                                           C.c_void_p(d_counts)))
+
+    def cuda_stream(self) -> int:
+        return lib().grx_tdt_batch_cuda_stream(self._h) or 0
+
+    def launches(self) -> int:
+        return lib().grx_tdt_batch_launches(self._h)
+
+    def iterations(self) -> int:
+        return lib().grx_tdt_batch_iterations(self._h)
+
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_tdt_batch_free"](h)
+

@@ -169,4 +169,37 @@ void launch_time_norm(const float* y0, const float* y1, const float* a0, const f
 // Elementwise: y = silu(y0 + tc) for decode steps beyond the first.
 void launch_cond_step(const float* y0, const float* tc, float* sy, int M, int N, cudaStream_t st);
 
+
+// ---- the greedy TDT / RNN-T decode loop (k_tdt.cu) ----
+constexpr int TDT_MAX_LAYERS = 8, TDT_MAX_DURATIONS = 8;
+
+// Device state of a batch of n decoder streams. Arrays indexed by stream s;
+// the LSTM state is [2 halves][layers][n][H] (half cur[s] is the stream's
+// DecoderState, the other one the prediction step's output).
+struct TdtArgs {
+  int n = 0, H = 0, layers = 0, V = 0, J = 0, nout = 0, ndur = 0, blank = 0, max_symbols = 0, tdt = 1, act = 0;
+  int max_t = 0, cap = 0;
+  int durations[TDT_MAX_DURATIONS] = {};
+  const float* embed = nullptr;  // [V][H]
+  DQ8 lstm_wx[TDT_MAX_LAYERS], lstm_wh[TDT_MAX_LAYERS];
+  const float* lstm_b[TDT_MAX_LAYERS] = {};
+  DQ8 jpred, jout;
+  const float *jpred_b = nullptr, *jout_b = nullptr;
+  const float* enc_proj = nullptr;  // [n][max_t][J]
+  float* pred_proj = nullptr;       // [n][J]
+  float* logits = nullptr;          // [n][nout]
+  float *h = nullptr, *c = nullptr;
+  int *cur = nullptr, *last = nullptr, *step = nullptr, *nsym = nullptr, *iter = nullptr, *ntok = nullptr;
+  const int *T = nullptr, *frame_offset = nullptr;
+  int* tokens = nullptr;  // [n][cap][4]: id, frame, duration, p (float bits)
+  int *active = nullptr, *dirty = nullptr;  // [2][n] stream lists by iteration parity
+  int* counts = nullptr;                    // [2][2]: active, dirty counts by parity
+};
+
+void tdt_kernels_init();
+size_t tdt_lin_smem(int K, bool lstm);
+void launch_tdt_begin(const TdtArgs& a, cudaStream_t st);
+// One loop iteration for every stream on the parity's lists.
+void launch_tdt_iteration(const TdtArgs& a, int parity, cudaStream_t st);
+
 }  // namespace grx

@@ -286,3 +286,92 @@ def noise_frames(seed: int, frames: int, ldim: int, temperature: float) -> np.nd
     rng = np.random.default_rng(10_000 + seed)
     std = np.float32(np.sqrt(np.float64(np.float32(temperature))))
     return (rng.normal(0.0, 1.0, (frames, ldim)).astype(np.float32) * std).astype(np.float32)
+
+
+# ---------------------------------------------------------- Parakeet TDT
+
+
+@dataclass
+class TDTConfig:
+    """The decoder of a Parakeet-TDT-shaped transducer (conformer/model.go
+    HParams): 2-layer LSTM prediction net, relu joint, 1025 tokens (blank
+    last) plus 5 durations."""
+
+    H: int = 640  # predictor.hidden
+    layers: int = 2  # predictor.n_layers
+    V: int = 1025  # predictor.vocab, tokens plus blank
+    J: int = 640  # joint.hidden
+    D: int = 640  # encoder output width
+    durations: tuple = (0, 1, 2, 3, 4)
+    max_symbols: int = 10
+    act: str = "relu"
+    head: str = "tdt"
+    # The blank logit is lifted by blank_lift × √(2 ln V) token-logit
+    # deviations (about the expected maximum of the others) so that, as in a
+    # trained model, many iterations emit nothing; random weights alone would
+    # emit a token nearly every time.
+    blank_lift: float = 0.8
+
+    @property
+    def blank(self) -> int:
+        return self.V - 1
+
+
+def tdt_tensors(cfg: TDTConfig, seed: int = 0) -> dict:
+    """The decoder tensors in the converter's names (convert_nemo.py:686-695):
+    matrices as Q8_0, the embedding and biases F32."""
+    rng = np.random.default_rng(seed)
+    H, J, D = cfg.H, cfg.J, cfg.D
+    t: dict = {"pred.embed.weight": _n(rng, (cfg.V, H), 1.0)}
+    for i in range(cfg.layers):
+        p = f"pred.lstm.{i}."
+        t[p + "Wx"] = rand_q8(rng, 4 * H, H)
+        t[p + "Wh"] = rand_q8(rng, 4 * H, H)
+        t[p + "bias"] = _n(rng, 4 * H, 0.1)
+    t["joint.enc.weight"] = rand_q8(rng, J, D)
+    t["joint.enc.bias"] = _n(rng, J, 0.1)
+    t["joint.pred.weight"] = rand_q8(rng, J, H)
+    t["joint.pred.bias"] = _n(rng, J, 0.1)
+    nout = cfg.V + (len(cfg.durations) if cfg.head == "tdt" else 0)
+    t["joint.out.weight"] = rand_q8(rng, nout, J)
+    # Centre each output on the relu hidden's mean, σ/√(2π) for the hidden's
+    # spread σ (encoder part N(0,1) inputs, prediction part |h| ≈ 0.55), so
+    # that no token wins on its row sum alone; then lift the blank: most
+    # iterations emit nothing, as with a trained model.
+    we = q8_dequant(t["joint.enc.weight"]).astype(np.float64)
+    wp = q8_dequant(t["joint.pred.weight"]).astype(np.float64)
+    sigma = np.sqrt((we ** 2).sum(axis=1).mean() + 0.3 * (wp ** 2).sum(axis=1).mean())
+    rowsum = q8_dequant(t["joint.out.weight"]).astype(np.float64).sum(axis=1)
+    b = (_n(rng, nout, 0.1) - sigma / np.sqrt(2 * np.pi) * rowsum).astype(np.float32)
+    wo = q8_dequant(t["joint.out.weight"]).astype(np.float64)
+    sd_logit = np.sqrt((wo ** 2).sum(axis=1).mean() * sigma ** 2 / 2)
+    b[cfg.blank] += np.float32(cfg.blank_lift * np.sqrt(2 * np.log(cfg.V)) * sd_logit)
+    t["joint.out.bias"] = b
+    return t
+
+
+def tdt_gguf(cfg: TDTConfig, tensors: dict) -> bytes:
+    """A parakeet GGUF with the decoder settings conformer/model.go:190-236
+    reads (the encoder's tensors are out of scope and not written)."""
+    g = GGUFWriter("parakeet")
+    p = "stt.parakeet."
+    g.str("general.name", "Parakeet TDT synthetic decoder")
+    g.str(p + "head_kind", cfg.head)
+    g.u32(p + "predictor.hidden", cfg.H)
+    g.u32(p + "predictor.n_layers", cfg.layers)
+    g.u32(p + "predictor.vocab", cfg.V)
+    g.u32(p + "joint.hidden", cfg.J)
+    g.str(p + "joint.activation", cfg.act)
+    g.u32(p + "encoder.d_model", cfg.D)
+    if cfg.head == "tdt":
+        g.i32s(p + "tdt.durations", cfg.durations)
+        g.u32(p + "tdt.max_symbols", cfg.max_symbols)
+    g.u32("tokenizer.ggml.blank_token_id", cfg.blank)
+    for name, arr in tensors.items():
+        g.tensor(name, arr)
+    return g.to_bytes()
+
+
+def encoder_frames(seed: int, T: int, D: int) -> np.ndarray:
+    """Encoder output [T][D] of N(0,1) values for stream `seed`."""
+    return np.random.default_rng(20_000 + seed).normal(0.0, 1.0, (T, D)).astype(np.float32)

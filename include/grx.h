@@ -157,6 +157,54 @@ int grx_streams_pos(const grx_streams* s, int i);
 /* Device kernel launches issued by this stream set since creation. */
 int64_t grx_streams_launches(const grx_streams* s);
 
+/* ------------------------------------------- TDT decoder (conformer) ------
+ * conformer.Model.Decode (conformer/rnnt.go:111-173), the greedy RNN-T /
+ * TDT loop over encoder output, for a batch of independent streams. */
+typedef struct grx_tdt grx_tdt;
+typedef struct grx_tdt_batch grx_tdt_batch;
+/* conformer.Token (rnnt.go:10-15). */
+typedef struct grx_tdt_token {
+  int id;       /* token id */
+  int frame;    /* encoder frame where it was emitted, plus the frame offset */
+  int duration; /* frames it covers (TDT); 1 for RNN-T */
+  float p;      /* softmax probability of the token */
+} grx_tdt_token;
+/* The decoder part of conformer.FromGGUF (model.go:190-236, 306-314): a
+ * parakeet GGUF's decoder settings and its pred.* and joint.* tensors (Q8_0
+ * matrices, as the converter writes them) on `device`. The encoder is not
+ * loaded (its output is Decode's input). */
+int grx_tdt_load(const void* bytes, size_t len, int device, grx_tdt** out);
+void grx_tdt_free(grx_tdt* m);
+/* Any pointer may be NULL. is_tdt: 1 TDT, 0 RNN-T. */
+int grx_tdt_dims(const grx_tdt* m, int* hidden, int* layers, int* vocab, int* joint, int* d_enc, int* n_durations,
+                 int* blank, int* is_tdt);
+/* n DecoderStates (rnnt.go:19-33), each at its start, and room for max_t
+ * encoder frames and cap tokens per stream and call. */
+int grx_tdt_batch_create(grx_tdt* m, int n, int max_t, int cap, grx_tdt_batch** out);
+void grx_tdt_batch_free(grx_tdt_batch* b);
+/* NewDecoderState (rnnt.go:27) for every stream. */
+int grx_tdt_batch_reset(grx_tdt_batch* b);
+/* Stream i's DecoderState: h and c [layers][hidden], the last token. */
+int grx_tdt_state_get(grx_tdt_batch* b, int i, float* h, float* c, int* last);
+int grx_tdt_state_set(grx_tdt_batch* b, int i, const float* h, const float* c, int last);
+/* Model.Decode for every stream i: enc [n][max_t][d_enc] (host), T[i] frames
+ * (0..max_t), frame_offset (may be NULL: 0). Continues from each stream's
+ * state and leaves it after the stream's last iteration, as Decode's st.
+ * tokens [n][cap] (host) gets each stream's tokens in order and counts[n]
+ * their number, which may exceed cap (only the first cap are kept). */
+int grx_tdt_decode(grx_tdt_batch* b, const float* enc, const int* T, const int* frame_offset, grx_tdt_token* tokens,
+                   int* counts);
+/* The same with device-resident buffers: d_enc [n][max_t][d_enc], d_tokens
+ * [n][cap], d_counts [n] on the batch's device (T and frame_offset on the
+ * host). Returns when every stream has finished its loop. */
+int grx_tdt_decode_device(grx_tdt_batch* b, const float* d_enc, const int* T, const int* frame_offset,
+                          grx_tdt_token* d_tokens, int* d_counts);
+/* The cudaStream_t the batch's work runs on. */
+void* grx_tdt_batch_cuda_stream(const grx_tdt_batch* b);
+/* Kernel launches and loop iterations (batch rounds) issued so far. */
+int64_t grx_tdt_batch_launches(const grx_tdt_batch* b);
+int64_t grx_tdt_batch_iterations(const grx_tdt_batch* b);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,7 @@
 #include <thread>
 
 #include "flowlm.h"
+#include "tdt.h"
 
 using namespace orc;
 
@@ -280,6 +281,138 @@ void orc_flowlm_run(void* h, int n, void** streams, int frames, const float* noi
   for (int t = 1; t < threads; t++) ts.emplace_back(work);
   work();
   for (auto& t : ts) t.join();
+}
+
+// ---------------------------------------------------------------- TDT ---
+// The greedy RNN-T / TDT decoder of conformer/rnnt.go (see tdt.h).
+
+struct OTDT {
+  TDT m;
+  std::map<std::string, Weight> w;
+  std::map<std::string, const float*> v;
+  std::string err;
+};
+
+void* orc_tdt_new(int H, int layers, int V, int J, int blank, int max_symbols, int tdt, int act, const int* durations,
+                  int nd) {
+  auto* o = new OTDT();
+  o->m.H = H;
+  o->m.V = V;
+  o->m.J = J;
+  o->m.blank = blank;
+  o->m.max_symbols = max_symbols;
+  o->m.tdt = tdt != 0;
+  o->m.act = act;
+  o->m.durations.assign(durations, durations + nd);
+  o->m.lstm.resize(size_t(layers));
+  return o;
+}
+
+void orc_tdt_free(void* h) { delete (OTDT*)h; }
+
+const char* orc_tdt_error(void* h) { return ((OTDT*)h)->err.c_str(); }
+
+void orc_tdt_tensor(void* h, const char* name, int type, int rows, int cols, const void* p) {
+  auto* o = (OTDT*)h;
+  Weight w;
+  w.rows = rows;
+  w.cols = cols;
+  w.type = WType(type);
+  w.f = (const float*)p;
+  w.q = (const uint8_t*)p;
+  o->w[name] = w;
+  o->v[name] = (const float*)p;
+}
+
+// Binds the decoder tensors (conformer/model.go:306-314).
+int orc_tdt_ready(void* h) {
+  auto* o = (OTDT*)h;
+  auto W = [&](const std::string& n) {
+    auto it = o->w.find(n);
+    if (it == o->w.end()) {
+      o->err = "missing " + n;
+      return Weight{};
+    }
+    return it->second;
+  };
+  auto Vv = [&](const std::string& n) -> const float* {
+    auto it = o->v.find(n);
+    if (it == o->v.end()) {
+      o->err = "missing " + n;
+      return nullptr;
+    }
+    return it->second;
+  };
+  TDT& m = o->m;
+  m.embed = Vv("pred.embed.weight");
+  for (size_t i = 0; i < m.lstm.size(); i++) {
+    const std::string p = "pred.lstm." + std::to_string(i) + ".";
+    m.lstm[i].wx = W(p + "Wx");
+    m.lstm[i].wh = W(p + "Wh");
+    m.lstm[i].b = Vv(p + "bias");
+  }
+  m.jenc = W("joint.enc.weight");
+  m.jencb = Vv("joint.enc.bias");
+  m.jpred = W("joint.pred.weight");
+  m.jpredb = Vv("joint.pred.bias");
+  m.jout = W("joint.out.weight");
+  m.joutb = Vv("joint.out.bias");
+  return o->err.empty() ? 0 : -1;
+}
+
+// Decode (rnnt.go:111) of one stream. h, c: [layers][H] and *last, the
+// DecoderState, read and updated. tokens: [cap][4] (id, frame, duration,
+// p as float bits). Returns the token count (all of them, even past cap).
+int orc_tdt_decode(void* hm, const float* enc, int T, int frame_offset, float* h, float* c, int* last, int* tokens,
+                   int cap, long* iters, long* preds) {
+  const TDT& m = ((OTDT*)hm)->m;
+  TDTState st;
+  st.init(m);
+  for (size_t l = 0; l < m.lstm.size(); l++) {
+    std::memcpy(st.h[l].data(), h + l * size_t(m.H), sizeof(float) * size_t(m.H));
+    std::memcpy(st.c[l].data(), c + l * size_t(m.H), sizeof(float) * size_t(m.H));
+  }
+  st.last = *last;
+  std::vector<TDTToken> out = tdt_decode(m, enc, T, st, frame_offset, iters, preds);
+  for (size_t l = 0; l < m.lstm.size(); l++) {
+    std::memcpy(h + l * size_t(m.H), st.h[l].data(), sizeof(float) * size_t(m.H));
+    std::memcpy(c + l * size_t(m.H), st.c[l].data(), sizeof(float) * size_t(m.H));
+  }
+  *last = st.last;
+  for (size_t i = 0; i < out.size() && int(i) < cap; i++) {
+    tokens[4 * i] = out[i].id;
+    tokens[4 * i + 1] = out[i].frame;
+    tokens[4 * i + 2] = out[i].duration;
+    std::memcpy(&tokens[4 * i + 3], &out[i].p, 4);
+  }
+  return int(out.size());
+}
+
+// n independent fresh decodes on `threads` host threads (the CPU baseline):
+// enc [n][T][D]; counts [n]; tokens [n][cap][4].
+void orc_tdt_run(void* hm, int n, const float* enc, int T, int D, int* tokens, int cap, int* counts, long* iters,
+                 int threads) {
+  const TDT& m = ((OTDT*)hm)->m;
+  std::atomic<int> next{0};
+  std::atomic<long> it_total{0};
+  auto work = [&]() {
+    for (;;) {
+      const int i = next.fetch_add(1);
+      if (i >= n) return;
+      std::vector<float> h(m.lstm.size() * size_t(m.H), 0.f), c(h.size(), 0.f);
+      int last = -1;
+      long it = 0;
+      counts[i] = orc_tdt_decode(hm, enc + size_t(i) * T * D, T, 0, h.data(), c.data(), &last,
+                                 tokens + size_t(i) * cap * 4, cap, &it, nullptr);
+      it_total += it;
+    }
+  };
+  threads = std::max(1, std::min(threads, n));
+  std::vector<std::thread> ts;
+  for (int t = 1; t < threads; t++) ts.emplace_back(work);
+  work();
+  for (auto& t : ts) t.join();
+  if (iters) *iters = it_total.load();
 }
 
 }  // extern "C"

@@ -57,6 +57,13 @@ def lib():
             "orc_stream_pos": (I, [P]),
             "orc_flowlm_frame": (F, [P, P, P, P, P, P, P, P]),
             "orc_flowlm_run": (None, [P, I, P, I, P, P, P, P, I]),
+            "orc_tdt_new": (P, [I, I, I, I, I, I, I, I, P, I]),
+            "orc_tdt_free": (None, [P]),
+            "orc_tdt_error": (C.c_char_p, [P]),
+            "orc_tdt_tensor": (None, [P, C.c_char_p, I, I, I, P]),
+            "orc_tdt_ready": (I, [P]),
+            "orc_tdt_decode": (I, [P, P, I, I, P, P, P, P, I, P, P]),
+            "orc_tdt_run": (None, [P, I, P, I, I, P, I, P, P, I]),
         }
         for k, (r, a) in sig.items():
             f = getattr(L, k)
@@ -206,3 +213,71 @@ class Stream:
         if getattr(self, "h", None):
             lib().orc_stream_free(self.h)
             self.h = None
+
+
+ACTS = {"relu": 0, "sigmoid": 1, "tanh": 2}
+
+
+class TDT:
+    """The oracle's greedy TDT / RNN-T decoder (conformer/rnnt.go), from the
+    synthetic generator's tensor dict."""
+
+    def __init__(self, cfg, tensors: dict):
+        from gorelaxor_b200.synth import Q8
+
+        self.cfg = cfg
+        self._keep = []
+        L = lib()
+        dur = np.ascontiguousarray(cfg.durations, np.int32)
+        self._keep.append(dur)
+        self.h = L.orc_tdt_new(cfg.H, cfg.layers, cfg.V, cfg.J, cfg.blank, cfg.max_symbols,
+                               int(cfg.head == "tdt"), ACTS[cfg.act], p(dur), len(dur))
+        for name, arr in tensors.items():
+            if isinstance(arr, Q8):
+                buf = np.ascontiguousarray(arr.blocks)
+                L.orc_tdt_tensor(self.h, name.encode(), 2, arr.rows, arr.cols, p(buf))
+            else:
+                buf = np.ascontiguousarray(arr, np.float32)
+                rows, cols = (buf.shape if buf.ndim == 2 else (1, buf.size))
+                L.orc_tdt_tensor(self.h, name.encode(), 0, rows, cols, p(buf))
+            self._keep.append(buf)
+        if L.orc_tdt_ready(self.h) != 0:
+            raise RuntimeError(L.orc_tdt_error(self.h).decode())
+
+    def state(self):
+        """A fresh DecoderState: (h [layers][H], c [layers][H], last)."""
+        z = np.zeros((self.cfg.layers, self.cfg.H), np.float32)
+        return [z.copy(), z.copy(), -1]
+
+    def decode(self, enc: np.ndarray, state=None, frame_offset: int = 0, cap: int | None = None):
+        """Model.Decode (rnnt.go:111): tokens as an int array [n][4] (id,
+        frame, duration, p as float32 bits), the state updated in place;
+        also returns (iterations, prediction steps)."""
+        enc = np.ascontiguousarray(enc, np.float32)
+        T = enc.shape[0]
+        st = state if state is not None else self.state()
+        cap = cap or 16 * T + 1024
+        toks = np.zeros((cap, 4), np.int32)
+        last = C.c_int(st[2])
+        it, npred = C.c_long(0), C.c_long(0)
+        n = lib().orc_tdt_decode(self.h, p(enc), T, frame_offset, p(st[0]), p(st[1]), C.byref(last), p(toks), cap,
+                                 C.byref(it), C.byref(npred))
+        st[2] = last.value
+        return toks[:min(n, cap)], it.value, npred.value
+
+    def run(self, enc: np.ndarray, cap: int, threads: int):
+        """n fresh decodes of enc [n][T][D] on host threads: (tokens [n][cap][4],
+        counts [n], total iterations)."""
+        enc = np.ascontiguousarray(enc, np.float32)
+        n, T, D = enc.shape
+        toks = np.zeros((n, cap, 4), np.int32)
+        counts = np.zeros(n, np.int32)
+        it = C.c_long(0)
+        lib().orc_tdt_run(self.h, n, p(enc), T, D, p(toks), cap, p(counts), C.byref(it), threads)
+        return toks, counts, it.value
+
+    def __del__(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.orc_tdt_free(self.h)
+            self.h = None
+
