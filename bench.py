@@ -162,6 +162,29 @@ def run_reference(args, rank, world):
             "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
             flush=True)
         return
+    if args.workload == "whisper":
+        cfg = synth.WhisperConfig()
+        tensors = synth.whisper_tensors(cfg, 0)
+        words = synth.whisper_words(cfg)
+        streams, steps = min(args.batch, cores), 8
+        vals, times = [], []
+        for _ in range(args.steps):
+            v, dt = whisper_cpu_sample(cfg, tensors, words, streams, steps, cores)
+            vals.append(v)
+            times.append(dt)
+        value = float(np.mean(vals))
+        sample = f"{streams} streams x {steps} tokens per step incl. cross K/V and prompt, {cores} threads"
+        print(json.dumps({
+            "impl": "reference", "metric": WHISPER_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0->f16/f32",
+            "data": "synthetic (seeded; the reference ships no weights)",
+            "config": {"workload": f"C2 Whisper, {args.batch} streams x {args.frames} tokens (sampled)",
+                       "global_batch": args.batch, "tokens": args.frames, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
     cfg = synth.FlowLMConfig()
     tensors = synth.flowlm_tensors(cfg, 0)
     streams, frames = min(args.batch, cores), 8
@@ -302,13 +325,135 @@ def run_tdt(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+WHISPER_METRIC = "Whisper tokens/s (greedy decode tokens per second, whole job)"
+
+
+def whisper_cpu_sample(cfg, tensors, words, streams, steps, threads):
+    """The oracle's window (cross K/V, 4-token prompt, greedy steps) for
+    `streams` streams on `threads` host threads: tokens/s and wall time."""
+    from gorelaxor_b200 import synth
+    from oracle import oracle as orc
+
+    om = orc.Whisper(cfg, tensors, words)
+    enc = np.stack([synth.whisper_encoder_out(1 + i, cfg) for i in range(streams)])
+    prompt = [50360, 100, 200, 50257]
+    t0 = time.perf_counter()
+    om.run(enc, prompt, 3, steps, threads)
+    dt = time.perf_counter() - t0
+    return streams * steps / dt, dt
+
+
+def run_whisper(args, rank, world, local):
+    """--workload whisper: the base.en-shaped decoder (C2): `batch` streams
+    per GPU, each with its own N(0,1) encoder output, a 4-token prompt and
+    `frames` greedy tokens. A step = the prompt and the token loop of every
+    stream; the window's cross K/V prep is timed apart."""
+    import torch
+
+    import gorelaxor_b200 as g
+    from gorelaxor_b200 import synth
+    from gorelaxor_b200.dist import max_over_ranks, partition
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    B, T = args.batch, args.frames
+    cfg = synth.WhisperConfig()
+    tensors = synth.whisper_tensors(cfg, 0)
+    words = synth.whisper_words(cfg)
+    model = g.Whisper(synth.whisper_ggml(cfg, tensors, words), device=local)
+    mine = partition(B * world, world, rank)
+    enc = np.stack([synth.whisper_encoder_out(1 + s, cfg) for s in mine])
+    b = g.WhisperBatch(model, B)
+    d_enc = torch.from_numpy(enc).cuda()
+    d_tok = torch.empty((T, B, 4), dtype=torch.int32, device="cuda")
+    ext = torch.cuda.ExternalStream(b.cuda_stream())
+    prompt = [model.prev, 100, 200, model.sot]
+
+    def one():
+        b.set_audio_device(d_enc.data_ptr())
+        b.prompt(prompt, 3)
+        b.run_device(T, d_tok.data_ptr())
+        b.sync()
+
+    for _ in range(args.warmup):
+        one()
+    clocks = Clocks(local)
+    l0 = b.launches()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks.start()
+    ms, kv_ms = [], []
+    for _ in range(args.steps):
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(ext)
+        b.set_audio_device(d_enc.data_ptr())
+        e1.record(ext)
+        b.prompt(prompt, 3)
+        b.run_device(T, d_tok.data_ptr())
+        e2.record(ext)
+        b.sync()
+        kv_ms.append(e0.elapsed_time(e1))
+        ms.append(e1.elapsed_time(e2))
+    ck = clocks.stop()
+    launches = b.launches() - l0
+    total_ms = max_over_ranks(float(np.sum(ms)), device="cuda")
+    value = args.steps * B * T * world / (total_ms / 1000)
+
+    e2e = None
+    if args.e2e_steps > 0:
+        pin = torch.from_numpy(enc).pin_memory().numpy()
+        em = []
+        for _ in range(args.e2e_steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            b.set_audio(pin)
+            b.prompt(prompt, 3)
+            b.run(T)
+            em.append((time.perf_counter() - t0) * 1000)
+        emax = max_over_ranks(float(np.sum(em)), device="cuda")
+        e2e = {"value": args.e2e_steps * B * T * world / (emax / 1000), "unit": "tokens/s",
+               "h2d_bytes_per_step": enc.nbytes + 4 * B * len(prompt), "d2h_bytes_per_step": T * B * 16 + 4 * B,
+               "note": "grx_whisper_set_audio (encoder output from pinned memory, cross K/V prep included), "
+                       "grx_whisper_prompt, grx_whisper_run with the tokens read back"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        streams, steps = min(B, cores), 8
+        v, dt = whisper_cpu_sample(cfg, tensors, words, streams, steps, cores)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{streams} streams x {steps} tokens incl. cross K/V and prompt ({dt:.1f} s wall)"}
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": WHISPER_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q8_0->f16/f32",
+        "data": "synthetic (seeded Q8_0 decoder, N(0,1) encoder output; the reference ships no weights)",
+        "config": {"workload": f"C2 Whisper base.en decoder: {B} streams x {T} greedy tokens from a 4-token prompt",
+                   "global_batch": B * world, "tokens": T,
+                   "parallelism": f"streams partitioned, {world} GPU(s), no collective",
+                   "l2": "cross K/V 36.9 MB per stream (1.2 GB at 32), larger than L2"},
+        "cross_kv_ms_per_step": float(np.mean(kv_ms)),
+        "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="grx", choices=["grx", "reference"])
-    ap.add_argument("--workload", default="flowlm", choices=["flowlm", "tdt"])
+    ap.add_argument("--workload", default="flowlm", choices=["flowlm", "tdt", "whisper"])
     ap.add_argument("--batch", type=int, default=None, help="streams per GPU (flowlm 256, tdt 128)")
     ap.add_argument("--frames", type=int, default=None, help="frames per stream (flowlm 512, tdt 750)")
     ap.add_argument("--e2e-steps", type=int, default=1)
@@ -318,13 +463,14 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
-    tdt = args.workload == "tdt"
-    args.batch = args.batch or (128 if tdt else 256)
-    args.frames = args.frames or (750 if tdt else 512)
+    args.batch = args.batch or {"flowlm": 256, "tdt": 128, "whisper": 32}[args.workload]
+    args.frames = args.frames or {"flowlm": 512, "tdt": 750, "whisper": 224}[args.workload]
     if args.impl == "reference":
         return run_reference(args, rank, world)
-    if tdt:
+    if args.workload == "tdt":
         return run_tdt(args, rank, world, local)
+    if args.workload == "whisper":
+        return run_whisper(args, rank, world, local)
 
     import torch
 
@@ -412,6 +558,7 @@ def main():
     per_launch = np.repeat(per_launch[:, None], cfg.layers, axis=1).astype(np.float64)
     durs = np.stack(attn_ns)  # [steps][F][L]
     achieved = float(per_launch.sum() * args.steps / durs.sum())  # B/ns = GB/s
+    attn_share = float(durs.sum() / 1e6 / np.sum(step_ms))  # of the timed steps, this rank
     hbm, peak_kind = peaks()
     # DRAM bytes per launch: one ncu capture at 66 keys (256 streams, frame 1,
     # layers 0-1: read+write 143.51 MB against 139.79 MB algorithmic) scaled
@@ -467,6 +614,7 @@ def main():
         "roofline": {"bound": "hbm", "kernel": "k_attn", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": traffic,
                      "traffic_unit": "bytes per launch (ncu dram read+write at 66 keys, scaled by key rows)",
+                     "share": attn_share,
                      "note": "algorithmic bytes per launch (K,V rows 0..pos of every head + q + Q8 output) over the "
                              "kernel's own first-CTA-start to last-CTA-end span, every launch of the timed steps"},
         "cpu_baseline": cpu,

@@ -86,6 +86,23 @@ def _sig(lib):
         "grx_tdt_batch_cuda_stream": (P, [P]),
         "grx_tdt_batch_launches": (L, [P]),
         "grx_tdt_batch_iterations": (L, [P]),
+        "grx_whisper_load": (I, [P, S, I, PP]),
+        "grx_whisper_free": (None, [P]),
+        "grx_whisper_dims": (I, [P] + [C.POINTER(C.c_int)] * 6),
+        "grx_whisper_tokens": (I, [P] + [C.POINTER(C.c_int)] * 6),
+        "grx_whisper_suppressed": (I, [P, P, I]),
+        "grx_whisper_batch_create": (I, [P, I, PP]),
+        "grx_whisper_batch_free": (None, [P]),
+        "grx_whisper_set_audio": (I, [P, P]),
+        "grx_whisper_set_audio_device": (I, [P, P]),
+        "grx_whisper_prompt": (I, [P, P, I, I, P]),
+        "grx_whisper_run": (I, [P, I, P]),
+        "grx_whisper_run_device": (I, [P, I, P]),
+        "grx_whisper_sync": (I, [P]),
+        "grx_whisper_cross": (I, [P, I, I, P, P]),
+        "grx_whisper_logits": (I, [P, P]),
+        "grx_whisper_batch_cuda_stream": (P, [P]),
+        "grx_whisper_batch_launches": (L, [P]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -107,7 +124,7 @@ def lib():
             raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m gorelaxor_b200.build`")
         _lib = _sig(C.CDLL(str(LIB_PATH)))
         for n in ("grx_gguf_close", "grx_weight_free", "grx_flowlm_free", "grx_voice_free", "grx_streams_free",
-                  "grx_tdt_free", "grx_tdt_batch_free"):
+                  "grx_tdt_free", "grx_tdt_batch_free", "grx_whisper_free", "grx_whisper_batch_free"):
             _FREE[n] = getattr(_lib, n)
     return _lib
 
@@ -401,4 +418,92 @@ class TDTBatch:
         h, self._h = getattr(self, "_h", None), None
         if h:
             _free["grx_tdt_batch_free"](h)
+
+
+# ---------------------------------------------------------------- Whisper
+
+
+class Whisper:
+    """whisper.Model's text decoder on one device, from a whisper.cpp ggml file."""
+
+    def __init__(self, data: bytes, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().grx_whisper_load(data, len(data), device, C.byref(h)))
+        self._h = h
+        self.device = device
+        v = [C.c_int() for _ in range(6)]
+        _check(lib().grx_whisper_dims(h, *[C.byref(x) for x in v]))
+        self.n_vocab, self.n_audio_ctx, self.n_state, self.n_head, self.n_text_layer, self.n_text_ctx = [x.value for x in v]
+        t = [C.c_int() for _ in range(6)]
+        _check(lib().grx_whisper_tokens(h, *[C.byref(x) for x in t]))
+        self.eot, self.sot, self.prev, self.nosp, self.beg, self.n_lang = [x.value for x in t]
+
+    def suppressed(self) -> list[int]:
+        out = np.zeros(512, np.int32)
+        n = _check(lib().grx_whisper_suppressed(self._h, _ptr(out), 512))
+        return out[:n].tolist()
+
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_whisper_free"](h)
+
+
+class WhisperBatch:
+    """n decoding sequences of a Whisper model."""
+
+    def __init__(self, model: Whisper, n: int):
+        self.model, self.n = model, n
+        h = C.c_void_p()
+        _check(lib().grx_whisper_batch_create(model._h, n, C.byref(h)))
+        self._h = h
+
+    def set_audio(self, enc: np.ndarray):
+        e = np.ascontiguousarray(enc, np.float32)
+        _check(lib().grx_whisper_set_audio(self._h, _ptr(e)))
+
+    def set_audio_device(self, d_enc: int):
+        _check(lib().grx_whisper_set_audio_device(self._h, C.c_void_p(d_enc)))
+
+    def prompt(self, prompt, sot_at: int) -> np.ndarray:
+        """prompt [n][np] (or one prompt for all); returns no_speech [n]."""
+        pr = np.ascontiguousarray(np.broadcast_to(np.asarray(prompt, np.int32), (self.n, np.shape(prompt)[-1])))
+        ns = np.zeros(self.n, np.float32)
+        _check(lib().grx_whisper_prompt(self._h, _ptr(pr), pr.shape[1], sot_at, _ptr(ns)))
+        return ns
+
+    def run(self, steps: int) -> np.ndarray:
+        """Tokens [steps][n][4] int32 (id, tid, p bits, plog bits)."""
+        out = np.zeros((steps, self.n, 4), np.int32)
+        _check(lib().grx_whisper_run(self._h, steps, _ptr(out)))
+        return out
+
+    def run_device(self, steps: int, d_tokens: int):
+        _check(lib().grx_whisper_run_device(self._h, steps, C.c_void_p(d_tokens)))
+
+    def sync(self):
+        _check(lib().grx_whisper_sync(self._h))
+
+    def cross(self, i: int, layer: int):
+        m = self.model
+        k = np.empty((m.n_head, m.n_audio_ctx, m.n_state // m.n_head), np.float32)
+        vt = np.empty((m.n_head, m.n_state // m.n_head, m.n_audio_ctx), np.float32)
+        _check(lib().grx_whisper_cross(self._h, i, layer, _ptr(k), _ptr(vt)))
+        return k, vt
+
+    def logits(self) -> np.ndarray:
+        out = np.empty((self.n, self.model.n_vocab), np.float32)
+        _check(lib().grx_whisper_logits(self._h, _ptr(out)))
+        return out
+
+    def cuda_stream(self) -> int:
+        return lib().grx_whisper_batch_cuda_stream(self._h) or 0
+
+    def launches(self) -> int:
+        return lib().grx_whisper_batch_launches(self._h)
+
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_whisper_batch_free"](h)
 

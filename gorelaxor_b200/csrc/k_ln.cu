@@ -99,8 +99,8 @@ __global__ void k_ln(LnArgs a, int D) {
 
 // Plain Q8_0 rounding of float rows (the int8 path's quantU8 step alone).
 __global__ void k_quant(const float* x, int K, int8_t* q, float2* s) {
-  int m = blockIdx.y;
-  int i = blockIdx.x * blockDim.x + threadIdx.x;  // one value per thread
+  int m = blockIdx.x;  // rows on x: up to 2^31 − 1 of them
+  int i = blockIdx.y * blockDim.x + threadIdx.x;  // one value per thread
   if (i >= K) return;
   float v = x[(size_t)m * K + i];
   float sc;
@@ -114,7 +114,7 @@ __global__ void k_quant(const float* x, int K, int8_t* q, float2* s) {
 void launch_ln(const LnArgs& a, int M, int D, cudaStream_t st) { k_ln<<<M, D / 4, 0, st>>>(a, D); }
 
 void launch_quant(const float* x, int M, int K, int8_t* q, float2* s, cudaStream_t st) {
-  dim3 g((K + 255) / 256, M);
+  dim3 g(M, (K + 255) / 256);
   k_quant<<<g, 256, 0, st>>>(x, K, q, s);
 }
 

@@ -1,0 +1,625 @@
+// The Whisper text decoder's token loop on the device (whisper/decoder.go,
+// encoder.go:120-140, transcribe.go:370-520): the embedding, the layer
+// norm, self- and cross-attention, the packed-order product used for the
+// cross K/V prep, and process + sample at temperature 0. The per-token
+// products are k_flin's F16 path (Q8_0 widened as f16(q·d)).
+//
+// Every reduction follows the reference's order: dotF32Go (four strided
+// unfused sums), dot4f32avx (16 lanes of fused chains, then HSUM), expSub
+// (EXP8 lanes over len&~7 with eight running lane sums, then Go expf for the
+// rest), softmax's ·(1/Σ), the unfused value sum of self-attention. The only
+// sums the GPU reorders are the three float32 sums over the vocabulary in
+// process/sample; they reach a token only through comparisons, which are
+// checked against a safe margin and, when closer, recomputed in the
+// reference's sequential order.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace grx {
+
+namespace {
+
+#define NINF (-__int_as_float(0x7f800000))
+
+__device__ __forceinline__ float q8h(int8_t q, float d) { return __half2float(__float2half_rn(__fmul_rn(float(q), d))); }
+
+__device__ __forceinline__ float wmat_at(const WMat& w, int row, int col) {
+  if (w.h) return __half2float(__ushort_as_half(w.h[(size_t)row * w.cols + col]));
+  return q8h(w.q[(size_t)row * w.cols + col], h2f(w.d[(size_t)row * (w.cols / QK) + col / QK]));
+}
+
+template <class T>
+__device__ __forceinline__ T warp_max(T v) {
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block max over blockDim.x threads (multiple of 32), result to all.
+__device__ float block_max(float v, float* sh) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[w] = v;
+  __syncthreads();
+  float r = sh[0];
+  for (int i = 1; i < nw; i++) r = fmaxf(r, sh[i]);
+  return r;
+}
+
+__device__ float block_sum(float v, float* sh) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[w] = v;
+  __syncthreads();
+  float r = 0.f;
+  for (int i = 0; i < nw; i++) r += sh[i];
+  return r;
+}
+
+__device__ double block_sum_d(double v, double* sh) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[w] = v;
+  __syncthreads();
+  double r = 0;
+  for (int i = 0; i < nw; i++) r += sh[i];
+  return r;
+}
+
+// ---------------------------------------------------------------- embed
+
+__global__ void k_wembed(WRows r, WMat emb, const float* pos, float* x) {
+  const int row = blockIdx.x, tok = r.row_tok[row], p = r.row_pos[row];
+  for (int j = threadIdx.x; j < r.st; j += blockDim.x)
+    x[(size_t)row * r.st + j] = __fadd_rn(wmat_at(emb, tok, j), pos[(size_t)p * r.st + j]);
+}
+
+// ------------------------------------------------------------ layerNorm
+// whisper/mathx.go:55-75: float64 sums (their order does not reach the
+// float32 results but in a last-ulp tie), mean and 1/sd as float32, then
+// ((v − mean)·inv)·w + b.
+__global__ void k_wln(const float* x, float* y, const float* w, const float* b, int n) {
+  __shared__ double sh[32];
+  const float* xr = x + (size_t)blockIdx.x * n;
+  float* yr = y + (size_t)blockIdx.x * n;
+  double s = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += double(xr[i]);
+  s = block_sum_d(s, sh);
+  const float mean = float(s / double(n));
+  double vs = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const double d = double(__fsub_rn(xr[i], mean));
+    vs += d * d;
+  }
+  vs = block_sum_d(vs, sh);
+  const float inv = float(1.0 / sqrt(vs / double(n) + 1e-5));
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    yr[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[i], mean), inv), w[i]), b[i]);
+}
+
+// expSub of e[0, n) in place (kernels_amd64.go expSub + expSubAVX): EXP8 for
+// the first n&~7 with eight lane sums in order, HSUM, then Go expf for the
+// rest summed in order. Threads 0..7 of the block do the sums. Returns Σ to
+// every thread.
+__device__ float exp_sub(float* e, int n, float mx, float* sh) {
+  const int n8 = n & ~7;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float d = __fsub_rn(e[j], mx);
+    e[j] = j < n8 ? exp_avx(d) : expf_go(d);
+  }
+  __syncthreads();
+  if (threadIdx.x < 8) {
+    float a = 0.f;
+    for (int c = threadIdx.x; c < n8; c += 8) a = __fadd_rn(a, e[c]);
+    sh[threadIdx.x] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    if (n8 > 0)
+      s = __fadd_rn(__fadd_rn(__fadd_rn(sh[0], sh[4]), __fadd_rn(sh[1], sh[5])),
+                    __fadd_rn(__fadd_rn(sh[2], sh[6]), __fadd_rn(sh[3], sh[7])));
+    float t = 0.f;
+    for (int j = n8; j < n; j++) t = __fadd_rn(t, e[j]);
+    sh[8] = __fadd_rn(s, t);
+  }
+  __syncthreads();
+  return sh[8];
+}
+
+// -------------------------------------------------------- self-attention
+// decoder.go:70-87 for (row, head): s_j = dotF32Go(q, k_j)·(1/√hd) over the
+// stream's cache rows 0..pos, softmax, o[d] = Σ_j p_j·v_j[d] (unfused, in j
+// order). 128 threads; hd = 64.
+__global__ void __launch_bounds__(128) k_wself(WRows r, const float* q, const float* sk, const float* sv, float* att) {
+  extern __shared__ float wsm[];  // [text_ctx] scores, [64] q
+  __shared__ float sh[40];
+  const int row = blockIdx.x, h = blockIdx.y, hd = 64, st = r.st;
+  const int s = r.row_stream[row], n = r.row_pos[row] + 1;
+  float* sc = wsm;
+  float* qh = wsm + r.text_ctx;
+  if (threadIdx.x < hd) qh[threadIdx.x] = q[(size_t)row * st + h * hd + threadIdx.x];
+  __syncthreads();
+  const float scale = float(1.0 / sqrt(double(hd)));
+  const float* kb = sk + (size_t)s * r.text_ctx * st + h * hd;
+  float mx = NINF;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float* kj = kb + (size_t)j * st;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; i += 4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kj + i);
+      s0 = __fadd_rn(s0, __fmul_rn(qh[i], k4.x));
+      s1 = __fadd_rn(s1, __fmul_rn(qh[i + 1], k4.y));
+      s2 = __fadd_rn(s2, __fmul_rn(qh[i + 2], k4.z));
+      s3 = __fadd_rn(s3, __fmul_rn(qh[i + 3], k4.w));
+    }
+    const float v = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3), scale);
+    sc[j] = v;
+    mx = fmaxf(mx, v);
+  }
+  mx = block_max(mx, sh);
+  const float sum = exp_sub(sc, n, mx, sh);
+  const float inv = __fdiv_rn(1.f, sum);
+  for (int j = threadIdx.x; j < n; j += blockDim.x) sc[j] = __fmul_rn(sc[j], inv);
+  __syncthreads();
+  if (threadIdx.x < hd) {
+    const float* vb = sv + (size_t)s * r.text_ctx * st + h * hd + threadIdx.x;
+    float o = 0.f;
+    for (int j = 0; j < n; j++) o = __fadd_rn(o, __fmul_rn(sc[j], vb[(size_t)j * st]));
+    att[(size_t)row * st + h * hd + threadIdx.x] = o;
+  }
+}
+
+// ------------------------------------------------------- cross-attention
+// decoder.go:93-119 for (row, head): scores by dot4f32avx over the stream's
+// pre-scaled keys (16 lanes per key: lane l16 chains element 16c + l16,
+// then lanes l and l+8 add, HSUM), softmax, and o[d] = dot4f32avx(p, Vᵀ[d])
+// over ctx&~15 plus dotF32Go of the rest. 256 threads; hd = 64.
+__global__ void __launch_bounds__(256) k_wcross(WRows r, const float* q, const float* ck, const float* cvt, float* att) {
+  extern __shared__ float wsm[];  // [audio_ctx] scores, [64] q
+  __shared__ float sh[40];
+  const int row = blockIdx.x, h = blockIdx.y, hd = 64, st = r.st, ctx = r.audio_ctx;
+  const int s = r.row_stream[row];
+  float* sc = wsm;
+  float* qh = wsm + ctx;
+  if (threadIdx.x < hd) qh[threadIdx.x] = q[(size_t)row * st + h * hd + threadIdx.x];
+  __syncthreads();
+  const float* kb = ck + ((size_t)s * r.nh + h) * ctx * hd;
+  const float* vb = cvt + ((size_t)s * r.nh + h) * hd * ctx;
+  const int lane = threadIdx.x & 31, l16 = threadIdx.x & 15, grp = threadIdx.x >> 4;
+  const int ctx4 = ctx & ~3;
+  float mx = NINF;
+  for (int j0 = 0; j0 < ctx4; j0 += 16) {
+    const int j = j0 + grp;
+    float a = 0.f;
+    if (j < ctx4) {
+      const float* kj = kb + (size_t)j * hd;
+#pragma unroll
+      for (int c = 0; c < 4; c++) a = __fmaf_rn(qh[16 * c + l16], kj[16 * c + l16], a);
+    }
+    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));  // lanes l < 8: acc0_l + acc1_l
+    float x = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
+    float y = __fadd_rn(x, __shfl_down_sync(0xffffffffu, x, 1));
+    const float z = __fadd_rn(y, __shfl_down_sync(0xffffffffu, y, 2));
+    if (l16 == 0 && j < ctx4) {
+      sc[j] = z;
+      mx = fmaxf(mx, z);
+    }
+    (void)lane;
+  }
+  for (int j = ctx4 + threadIdx.x; j < ctx; j += blockDim.x) {  // keys past the last group of four: dotF32Go
+    const float* kj = kb + (size_t)j * hd;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    for (int i = 0; i < hd; i += 4) {
+      s0 = __fadd_rn(s0, __fmul_rn(qh[i], kj[i]));
+      s1 = __fadd_rn(s1, __fmul_rn(qh[i + 1], kj[i + 1]));
+      s2 = __fadd_rn(s2, __fmul_rn(qh[i + 2], kj[i + 2]));
+      s3 = __fadd_rn(s3, __fmul_rn(qh[i + 3], kj[i + 3]));
+    }
+    sc[j] = __fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3);
+    mx = fmaxf(mx, sc[j]);
+  }
+  mx = block_max(mx, sh);
+  const float sum = exp_sub(sc, ctx, mx, sh);
+  const float inv = __fdiv_rn(1.f, sum);
+  for (int j = threadIdx.x; j < ctx; j += blockDim.x) sc[j] = __fmul_rn(sc[j], inv);
+  __syncthreads();
+  // o[d] for d = grp + 16i: the 16 lanes chain over ctx&~15 in steps of 16
+  const int cf = ctx & ~15;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int c = 0; c < cf; c += 16) {
+    const float p = sc[c + l16];
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[i] = __fmaf_rn(p, vb[(size_t)(grp + 16 * i) * ctx + c + l16], acc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float a = __fadd_rn(acc[i], __shfl_down_sync(0xffffffffu, acc[i], 8));
+    float x = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
+    float y = __fadd_rn(x, __shfl_down_sync(0xffffffffu, x, 1));
+    float z = __fadd_rn(y, __shfl_down_sync(0xffffffffu, y, 2));
+    if (l16 == 0) {
+      const int d = grp + 16 * i;
+      if (cf < ctx) {  // + dotF32Go of the tail (kernels_amd64.go dotF32x4)
+        const float* vd = vb + (size_t)d * ctx;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        int t = cf;
+        for (; t + 4 <= ctx; t += 4) {
+          s0 = __fadd_rn(s0, __fmul_rn(sc[t], vd[t]));
+          s1 = __fadd_rn(s1, __fmul_rn(sc[t + 1], vd[t + 1]));
+          s2 = __fadd_rn(s2, __fmul_rn(sc[t + 2], vd[t + 2]));
+          s3 = __fadd_rn(s3, __fmul_rn(sc[t + 3], vd[t + 3]));
+        }
+        for (; t < ctx; t++) s0 = __fadd_rn(s0, __fmul_rn(sc[t], vd[t]));
+        z = __fadd_rn(z, __fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3));
+      }
+      att[(size_t)row * st + h * hd + d] = z;
+    }
+  }
+}
+
+// --------------------------------------------------- packed-order product
+// whisper/gemm.go:150-186 + k6x16avx: every output starts at its bias (or
+// 0) and gets += the fused chain of each 256-deep pass. Tile 64 × 64, 256
+// threads of 4 × 4 outputs, 32-deep slices staged in shared memory.
+constexpr int MM_T = 64, MM_S = 32, MM_LD = MM_T + 4;
+
+__global__ void __launch_bounds__(256) k_wmm(const float* a, int lda, size_t a_stride, int m, WMat w,
+                                             const float* bias, int mode, float* c, int ldc, int nh, float tsc) {
+  __shared__ __align__(16) float As[MM_S][MM_LD];
+  __shared__ __align__(16) float Bs[MM_S][MM_LD];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int i0 = blockIdx.y * MM_T, j0 = blockIdx.x * MM_T, str = blockIdx.z;
+  const int n = w.rows, k = w.cols;
+  const float* A = a + str * a_stride;
+  float cv[4][4], ch[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; u++)
+#pragma unroll
+    for (int v = 0; v < 4; v++) {
+      const int j = j0 + tx * 4 + v;
+      cv[u][v] = bias && j < n ? bias[j] : 0.f;
+    }
+  const int sr = tid >> 2, sk8 = (tid & 3) * 8;  // staging: row/col sr, 8 values from sk8
+  for (int p0 = 0; p0 < k; p0 += 256) {
+    const int pn = min(256, k - p0);
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int v = 0; v < 4; v++) ch[u][v] = 0.f;
+    for (int s0 = 0; s0 < pn; s0 += MM_S) {
+      const int kk0 = p0 + s0;
+      {
+        const int i = i0 + sr;
+        float va[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const int kk = kk0 + sk8 + e;
+          va[e] = i < m && kk < p0 + pn ? A[(size_t)i * lda + kk] : 0.f;
+        }
+        const int j = j0 + sr;
+        float vbv[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const int kk = kk0 + sk8 + e;
+          vbv[e] = j < n && kk < p0 + pn ? wmat_at(w, j, kk) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          As[sk8 + e][sr] = va[e];
+          Bs[sk8 + e][sr] = vbv[e];
+        }
+        __syncthreads();
+      }
+      const int sn = min(MM_S, pn - s0);
+      for (int kk = 0; kk < sn; kk++) {
+        const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+        const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+          for (int v = 0; v < 4; v++) ch[u][v] = __fmaf_rn(av[u], bv[v], ch[u][v]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int v = 0; v < 4; v++) cv[u][v] = __fadd_rn(cv[u][v], ch[u][v]);
+  }
+  const int hd = n / max(nh, 1);
+#pragma unroll
+  for (int u = 0; u < 4; u++)
+#pragma unroll
+    for (int v = 0; v < 4; v++) {
+      const int i = i0 + ty * 4 + u, j = j0 + tx * 4 + v;
+      if (i >= m || j >= n) continue;
+      if (mode == 0) {
+        c[(size_t)str * m * ldc + (size_t)i * ldc + j] = cv[u][v];
+      } else {
+        const int hh = j / hd, d = j % hd;
+        const size_t base = ((size_t)str * nh + hh) * (size_t)m * hd;
+        if (mode == 1)
+          c[base + (size_t)i * hd + d] = __fmul_rn(cv[u][v], tsc);
+        else
+          c[base + (size_t)d * m + i] = cv[u][v];
+      }
+    }
+}
+
+// ------------------------------------------------------ process + sample
+
+__device__ float expf_go_d(float x) { return expf_go(x); }
+
+// The reference's sequential process + sample (transcribe.go:409-494) from
+// logits already masked by the rules; one thread. The slow path for rows
+// whose parallel decisions fall within the margin.
+__device__ void proc_exact(const float* lg, int n, int beg, int* out) {
+  float mx = NINF;
+  for (int i = 0; i < n; i++) mx = fmaxf(mx, lg[i]);
+  float s = 0.f;
+  for (int i = 0; i < n; i++)
+    if (lg[i] > NINF) s = __fadd_rn(s, expf_go_d(__fsub_rn(lg[i], mx)));
+  const float ls = __fadd_rn(float(log(double(s))), mx);
+  auto lp = [&](int i) { return lg[i] > NINF ? __fsub_rn(lg[i], ls) : NINF; };
+  float ts_max = NINF;
+  for (int i = beg; i < n; i++) ts_max = fmaxf(ts_max, lp(i));
+  bool mask_text = false;
+  if (ts_max > NINF) {
+    float sum = 0.f;
+    for (int i = beg; i < n; i++)
+      if (lp(i) > NINF) sum = __fadd_rn(sum, expf_go_d(__fsub_rn(lp(i), ts_max)));
+    const float ts_lp = __fadd_rn(float(log(double(sum))), ts_max);
+    float text_max = NINF;
+    for (int i = 0; i < beg; i++) text_max = fmaxf(text_max, lp(i));
+    mask_text = ts_lp > text_max;
+  }
+  auto eff = [&](int i) { return mask_text && i < beg ? NINF : lg[i]; };
+  float mx2 = NINF;
+  for (int i = 0; i < n; i++) mx2 = fmaxf(mx2, eff(i));
+  float s2 = 0.f;
+  for (int i = 0; i < n; i++)
+    if (eff(i) > NINF) s2 = __fadd_rn(s2, expf_go_d(__fsub_rn(eff(i), mx2)));
+  auto prob = [&](int i) { return eff(i) > NINF ? __fdiv_rn(expf_go_d(__fsub_rn(eff(i), mx2)), s2) : 0.f; };
+  int id = 0;
+  float pid = prob(0);
+  for (int i = 1; i < n; i++) {
+    const float p = prob(i);
+    if (p > pid) id = i, pid = p;
+  }
+  int tid = beg;
+  float pt = prob(beg);
+  for (int i = beg + 1; i < n; i++) {
+    const float p = prob(i);
+    if (p > pt) tid = i, pt = p;
+  }
+  if (id >= beg) tid = id;
+  const float plog = mask_text && id < beg ? NINF : lp(id);
+  out[0] = id;
+  out[1] = tid;
+  out[2] = __float_as_int(pid);
+  out[3] = __float_as_int(plog);
+}
+
+// (value, index) with the larger value, the smaller index on a tie.
+struct VI {
+  float v;
+  int i;
+};
+__device__ __forceinline__ VI vi_max(VI a, VI b) { return (b.v > a.v || (b.v == a.v && b.i < a.i)) ? b : a; }
+
+__device__ VI block_vi_max(VI x, VI* sh) {
+  for (int o = 16; o > 0; o >>= 1) {
+    VI y{__shfl_xor_sync(0xffffffffu, x.v, o), __shfl_xor_sync(0xffffffffu, x.i, o)};
+    x = vi_max(x, y);
+  }
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[w] = x;
+  __syncthreads();
+  VI r = sh[0];
+  for (int i = 1; i < nw; i++) r = vi_max(r, sh[i]);
+  return r;
+}
+
+// One CTA per row. The rules mask in place (transcribe.go:378-408); the
+// three float32 sums of logSoftmax, the timestamp rule and softmaxInf are
+// taken in parallel, and every decision they feed is checked: the
+// timestamp rule must clear a relative margin of 2e-4, and the winning
+// probability must beat every earlier index's by a factor 1 − 2^-20 (the
+// division by the sum can then not tie them). A row that misses a margin is
+// recomputed by one thread in the reference's order.
+__global__ void __launch_bounds__(512) k_wproc(WRows r, float* logits, WVocabDev v, WSample* state, int* out,
+                                               const int* step, int* next_tok) {
+  __shared__ float shf[40];
+  __shared__ VI shv[32];
+  __shared__ int amb;
+  const int row = blockIdx.x, s = r.row_stream[row], n = v.n, beg = v.beg;
+  float* lg = logits + (size_t)row * n;
+  const WSample q = state[s];
+  const bool initial = q.nt == 0;
+  // ---- the rules
+  if (threadIdx.x == 0) {
+    amb = 0;
+    if (initial) {
+      lg[v.eot] = NINF;
+      if (v.space >= 0) lg[v.space] = NINF;
+    }
+    lg[v.not_] = NINF;
+    lg[v.sot] = lg[v.nosp] = lg[v.solm] = NINF;
+    lg[v.translate] = lg[v.transcribe] = lg[v.prev] = NINF;
+  }
+  for (int i = threadIdx.x; i < v.n_lang; i += blockDim.x) lg[v.sot + 1 + i] = NINF;
+  for (int i = threadIdx.x; i < v.n_suppress; i += blockDim.x) lg[v.suppress[i]] = NINF;
+  __syncthreads();
+  const bool last = q.nt > 0 && q.last >= beg, penult = q.nt < 2 || q.penult >= beg;
+  const int tid0 = int(round(1.0 / (30.0 / double(v.audio_ctx))));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    bool m = false;
+    if (last) m = penult ? i >= beg : i < v.eot;
+    if (initial && i >= beg + tid0 + 1) m = true;
+    if (q.has_ts && i >= beg && i < beg + q.seek_delta / 2) m = true;
+    if (m) lg[i] = NINF;
+  }
+  __syncthreads();
+  // ---- logSoftmax and the timestamp rule
+  float mx = NINF, mts = NINF, mtx = NINF;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float x = lg[i];
+    mx = fmaxf(mx, x);
+    if (i >= beg) mts = fmaxf(mts, x);
+    else mtx = fmaxf(mtx, x);
+  }
+  mx = block_max(mx, shf);
+  mts = block_max(mts, shf);
+  mtx = block_max(mtx, shf);
+  float s1 = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    if (lg[i] > NINF) s1 = __fadd_rn(s1, expf_go(__fsub_rn(lg[i], mx)));
+  s1 = block_sum(s1, shf);
+  const float ls = __fadd_rn(float(log(double(s1))), mx);
+  const float ts_max = mts > NINF ? __fsub_rn(mts, ls) : NINF;  // max of logprobs[beg:]
+  bool mask_text = false;
+  if (ts_max > NINF) {
+    float sum = 0.f;
+    for (int i = beg + threadIdx.x; i < n; i += blockDim.x)
+      if (lg[i] > NINF) sum = __fadd_rn(sum, expf_go(__fsub_rn(__fsub_rn(lg[i], ls), ts_max)));
+    sum = block_sum(sum, shf);
+    const float ts_lp = __fadd_rn(float(log(double(sum))), ts_max);
+    const float text_max = mtx > NINF ? __fsub_rn(mtx, ls) : NINF;
+    mask_text = ts_lp > text_max;
+    if (text_max > NINF && fabsf(ts_lp - text_max) <= 2e-4f * (1.f + fabsf(text_max))) amb = 1;
+  }
+  // ---- softmaxInf and the argmaxes, on e_i = expf(lg'_i − max) (exact);
+  // only the division by their sum is left out
+  const float mx2 = mask_text ? mts : mx;
+  VI best{-1.f, n}, bts{-1.f, n};
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float x = (mask_text && i < beg) ? NINF : lg[i];
+    const float e = x > NINF ? expf_go(__fsub_rn(x, mx2)) : 0.f;
+    best = vi_max(best, VI{e, i});
+    if (i >= beg) bts = vi_max(bts, VI{e, i});
+  }
+  best = block_vi_max(best, shv);
+  bts = block_vi_max(bts, shv);
+  // the largest e before each winner that is smaller than it
+  float near = 0.f, near_t = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float x = (mask_text && i < beg) ? NINF : lg[i];
+    const float e = x > NINF ? expf_go(__fsub_rn(x, mx2)) : 0.f;
+    if (i < best.i && e < best.v) near = fmaxf(near, e);
+    if (i >= beg && i < bts.i && e < bts.v) near_t = fmaxf(near_t, e);
+  }
+  near = block_max(near, shf);
+  near_t = block_max(near_t, shf);
+  const float margin = 1.f - 9.5367431640625e-07f;  // 1 − 2^-20
+  if ((best.v > 0.f && near >= best.v * margin) || (bts.v > 0.f && near_t >= bts.v * margin)) amb = 1;
+  float s2 = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float x = (mask_text && i < beg) ? NINF : lg[i];
+    if (x > NINF) s2 = __fadd_rn(s2, expf_go(__fsub_rn(x, mx2)));
+  }
+  s2 = block_sum(s2, shf);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int o[4];
+    if (amb) {
+      proc_exact(lg, n, beg, o);
+    } else {
+      const int id = best.i;
+      const int tid = id >= beg ? id : bts.i;
+      o[0] = id;
+      o[1] = tid;
+      o[2] = __float_as_int(__fdiv_rn(best.v, s2));
+      o[3] = __float_as_int(mask_text && id < beg ? NINF : __fsub_rn(lg[id], ls));
+    }
+    int* orow = out + ((size_t)(step ? *step : 0) * r.rows + row) * 4;
+    for (int i = 0; i < 4; i++) orow[i] = o[i];
+    // the window loop's bookkeeping that process depends on (transcribe.go:218-224)
+    WSample ns = q;
+    ns.penult = q.last;
+    ns.last = o[0];
+    ns.nt = q.nt + 1;
+    if (o[0] > beg) {
+      ns.seek_delta = 2 * (o[0] - beg);
+      ns.has_ts = 1;
+    }
+    state[s] = ns;
+    if (next_tok) next_tok[row] = o[0];
+  }
+}
+
+// softmax(row)[nosp] (mathx.go:78-90): EXP8 lanes over n&~7 summed in order
+// per lane, HSUM, Go expf over the rest; one CTA per row.
+__global__ void k_wnospeech(const float* logits, int n, int nosp, float* scratch, float* out) {
+  __shared__ float sh[40];
+  const float* lg = logits + (size_t)blockIdx.x * n;
+  float* e = scratch + (size_t)blockIdx.x * n;
+  float mx = NINF;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    e[i] = lg[i];
+    mx = fmaxf(mx, lg[i]);
+  }
+  mx = block_max(mx, sh);
+  const float s = exp_sub(e, n, mx, sh);
+  if (threadIdx.x == 0) out[blockIdx.x] = __fmul_rn(e[nosp], __fdiv_rn(1.f, s));
+}
+
+// Every row's position moves on by `advance` and its cache row for the next
+// decode is set; the run's step counter, when given, moves on by one.
+__global__ void k_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int advance, int* step) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r == 0 && step) *step += 1;
+  if (r >= rows) return;
+  const int p = row_pos[r] + advance;
+  row_pos[r] = p;
+  dst_row[r] = r * text_ctx + p;
+}
+
+}  // namespace
+
+void launch_wembed(const WRows& r, const WMat& emb, const float* pos, float* x, cudaStream_t st) {
+  k_wembed<<<r.rows, 128, 0, st>>>(r, emb, pos, x);
+}
+
+void launch_wln(const float* x, float* y, const float* w, const float* b, int rows, int n, cudaStream_t st) {
+  k_wln<<<rows, 128, 0, st>>>(x, y, w, b, n);
+}
+
+void launch_wself(const WRows& r, const float* q, const float* sk, const float* sv, float* att, cudaStream_t st) {
+  k_wself<<<dim3(r.rows, r.nh), 128, (r.text_ctx + 64) * 4, st>>>(r, q, sk, sv, att);
+}
+
+void launch_wcross(const WRows& r, const float* q, const float* ck, const float* cvt, float* att, cudaStream_t st) {
+  k_wcross<<<dim3(r.rows, r.nh), 256, (r.audio_ctx + 64) * 4, st>>>(r, q, ck, cvt, att);
+}
+
+void launch_wmm(const float* a, int lda, size_t a_stream_stride, int m, const WMat& w, const float* bias, int mode,
+                float* c, int ldc, int nh, float tsc, int streams, cudaStream_t st) {
+  dim3 grid((w.rows + MM_T - 1) / MM_T, (m + MM_T - 1) / MM_T, streams);
+  k_wmm<<<grid, 256, 0, st>>>(a, lda, a_stream_stride, m, w, bias, mode, c, ldc, nh, tsc);
+}
+
+void launch_wproc(const WRows& r, float* logits, const WVocabDev& v, WSample* state, int* out, const int* step,
+                  int* next_tok, cudaStream_t st) {
+  k_wproc<<<r.rows, 512, 0, st>>>(r, logits, v, state, out, step, next_tok);
+}
+
+void launch_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int advance, int* step, cudaStream_t st) {
+  k_wtick<<<(rows + 127) / 128, 128, 0, st>>>(rows, row_pos, dst_row, text_ctx, advance, step);
+}
+
+void launch_wnospeech(const float* logits, int vocab, int nosp, float* scratch, float* out, int rows, cudaStream_t st) {
+  k_wnospeech<<<rows, 1024, 0, st>>>(logits, vocab, nosp, scratch, out);
+}
+
+void whisper_kernels_init() {}
+
+}  // namespace grx

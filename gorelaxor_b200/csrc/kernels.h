@@ -109,14 +109,18 @@ struct AttnArgs {
 
 void launch_attn(const AttnArgs& a, int M, cudaStream_t st);
 
-// Float activations times a Q8_0 (rows kept) or F32 matrix with the
-// reference's float-path order (dot4q8avx / dot4f32avx, gemm.go:195-259).
+// Float activations times a Q8_0 (rows kept), F32 or F16 matrix with the
+// reference's float-path order (dot4q8avx / dot4f32avx / dot4f16avx,
+// gemm.go:195-259; whisper/gemm.go:212-256).
 enum FEpi {
   FE_BIAS = 0,    // y = dot + bias
   FE_COND = 1,    // y = silu(dot + bias + tc)        (lm.go:110-115 and :131-132 with one step)
   FE_SILU = 2,    // y = silu(dot + bias)             (lm.go:144-145)
   FE_GATE = 3,    // h += gate · (dot + bias)         (lm.go:146-149)
   FE_LATENT = 4,  // cur = noise + (dot + bias)/steps; latent, scaled  (lm.go:118-121; speak.go:165-168)
+  FE_RESID = 5,   // y += dot + bias                  (whisper/decoder.go:89,121,129: matmul then addTo)
+  FE_GELU = 6,    // y = geluAVX(dot + bias)          (whisper/decoder.go:127)
+  FE_ROWPOS = 7,  // y[dst_row[m]·ldy + n] = dot + bias  (a cache row per input row)
 };
 
 struct FArgs {
@@ -125,7 +129,12 @@ struct FArgs {
   int ldx = 0;
   const int8_t* wq = nullptr;  // Q8_0 weight (values, scales), or
   const uint16_t* wd = nullptr;
-  const float* wf = nullptr;  // F32 weight [N][K]
+  const float* wf = nullptr;  // F32 weight [N][K], or
+  const uint16_t* wh = nullptr;  // F16 weight [N][K]
+  // With wq: widen each value as the Whisper loader does, f16(q·d)
+  // (whisper/model.go:486-490), and take the F16 product order.
+  bool q8_as_f16 = false;
+  const int* dst_row = nullptr;  // FE_ROWPOS: the destination row of each input row
   int N = 0, K = 0;
   const float* bias = nullptr;
   float* y = nullptr;  // [M][N], row stride ldy
@@ -147,15 +156,12 @@ struct FArgs {
 
 void launch_flin(const FArgs& a, int M, cudaStream_t st);
 
-// eos = dotF32Go(lm_out, w) + b (lm.go:193-194), then pos[m] += 1.
-void launch_eos(const float* x, const float* w, float b, int K, const FrameIO* io, float* eos, int* pos, int M,
-                cudaStream_t st);
-
 // io->frame += 1 (the end of a frame).
 void launch_tick(FrameIO* io, cudaStream_t st);
 
 // Per-device kernel attributes (dynamic shared memory limits).
 void flow_kernels_init();
+void flin_kernels_init();
 // The largest K launch_flin takes with F32 and with Q8_0 weights.
 int flin_max_k();
 int flin_max_k_q8();
@@ -201,5 +207,62 @@ size_t tdt_lin_smem(int K, bool lstm);
 void launch_tdt_begin(const TdtArgs& a, cudaStream_t st);
 // One loop iteration for every stream on the parity's lists.
 void launch_tdt_iteration(const TdtArgs& a, int parity, cudaStream_t st);
+
+
+// ---- the Whisper text decoder's token loop (k_whisper.cu) ----
+// A decoder weight matrix: Q8_0 values widened through f16(q·d) as the
+// reference loads them, or float16.
+struct WMat {
+  const int8_t* q = nullptr;
+  const uint16_t* d = nullptr;  // Q8_0 scales [rows][cols/32]
+  const uint16_t* h = nullptr;  // or float16 values [rows][cols]
+  int rows = 0, cols = 0;
+};
+
+// The rows of one call: row r is token row_tok[r] at position row_pos[r] of
+// stream row_stream[r].
+struct WRows {
+  int rows = 0, st = 0, nh = 0, text_ctx = 0, audio_ctx = 0, vocab = 0;
+  const int *row_stream = nullptr, *row_pos = nullptr, *row_tok = nullptr;
+};
+
+// Sampling state of a stream (transcribe.go:56-64): sampled so far, the last
+// two tokens, timestamps seen, the window's seek delta.
+struct WSample {
+  int nt, last, penult, has_ts, seek_delta;
+};
+
+// The vocabulary's special tokens and the suppressed ones (vocab.go).
+struct WVocabDev {
+  int n = 0, n_lang = 0, eot = 0, sot = 0, translate = 0, transcribe = 0, solm = 0, prev = 0, nosp = 0, not_ = 0, beg = 0,
+      space = -1, n_suppress = 0;
+  const int* suppress = nullptr;
+  int audio_ctx = 1500;
+};
+
+void launch_wembed(const WRows& r, const WMat& tok_emb, const float* dec_pos, float* x, cudaStream_t st);
+void launch_wln(const float* x, float* y, const float* w, const float* b, int rows, int n, cudaStream_t st);
+// Self-attention of every row over its stream's cache rows 0..pos.
+void launch_wself(const WRows& r, const float* q, const float* sk, const float* sv, float* att, cudaStream_t st);
+// Cross-attention over the stream's pre-scaled keys [nh][ctx][hd] and
+// transposed values [nh][hd][ctx].
+void launch_wcross(const WRows& r, const float* q, const float* ck, const float* cvt, float* att, cudaStream_t st);
+// The packed-order product (whisper/gemm.go:124-209, rows < m/6·6):
+// C = A·Wᵀ + bias. mode 0 stores C [m][ldc]; 1 writes keys ·tsc into
+// [stream][nh][ctx][hd]; 2 writes values into [stream][nh][hd][ctx] (cross
+// K/V prep, A = encoder output of stream blockIdx.z, rows = ctx).
+void launch_wmm(const float* a, int lda, size_t a_stream_stride, int m, const WMat& w, const float* bias, int mode,
+                float* c, int ldc, int nh, float tsc, int streams, cudaStream_t st);
+// process + sample at temperature 0 for every row (transcribe.go:370-494):
+// logits [rows][vocab] are masked in place; writes out[*step][rows][4] (id,
+// tid, p, plog), the next token and the stream's sampling state.
+void launch_wproc(const WRows& r, float* logits, const WVocabDev& v, WSample* state, int* out, const int* step,
+                  int* next_tok, cudaStream_t st);
+// row_pos += advance; dst_row = r·text_ctx + row_pos; *step += 1 when step is given.
+void launch_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int advance, int* step, cudaStream_t st);
+void whisper_kernels_init();
+// softmax(logits row)[nosp] (the no-speech probability, transcribe.go:176-180);
+// scratch [rows][vocab].
+void launch_wnospeech(const float* logits, int vocab, int nosp, float* scratch, float* out, int rows, cudaStream_t st);
 
 }  // namespace grx

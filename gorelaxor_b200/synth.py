@@ -375,3 +375,99 @@ def tdt_gguf(cfg: TDTConfig, tensors: dict) -> bytes:
 def encoder_frames(seed: int, T: int, D: int) -> np.ndarray:
     """Encoder output [T][D] of N(0,1) values for stream `seed`."""
     return np.random.default_rng(20_000 + seed).normal(0.0, 1.0, (T, D)).astype(np.float32)
+
+
+# --------------------------------------------------------------- Whisper
+
+
+@dataclass
+class WhisperConfig:
+    """A whisper.cpp ggml model's hparams (whisper/model.go:16-21, 117-135);
+    the defaults are base.en's."""
+
+    n_vocab: int = 51864
+    n_audio_ctx: int = 1500
+    n_state: int = 512
+    n_head: int = 8
+    n_audio_layer: int = 6
+    n_text_ctx: int = 448
+    n_text_layer: int = 6
+    n_mels: int = 80
+    ftype: int = 8  # matrices as Q8_0
+    n_words: int = 50256  # vocabulary entries written to the file (text tokens)
+
+
+GGML_MAGIC = 0x67676D6C
+
+# Words placed in the synthetic vocabulary at fixed ids so that the
+# reference's suppression rules (vocab.go:96-118) and the initial " " rule
+# (transcribe.go:383-385) have tokens to act on.
+WHISPER_MARKED = {220: " ", 12: "(", 13: " (", 60: "♪", 61: " ♪", 1000: " -", 1001: " '", 1002: "<<", 5000: "[["}
+
+
+def whisper_words(cfg: WhisperConfig) -> list[bytes]:
+    words = [f"w{i}".encode() for i in range(cfg.n_words)]
+    for i, w in WHISPER_MARKED.items():
+        if i < cfg.n_words:
+            words[i] = w.encode()
+    return words
+
+
+def whisper_tensors(cfg: WhisperConfig, seed: int = 0) -> dict:
+    """The text decoder's tensors in whisper.cpp's names (model.go:464-484):
+    matrices as Q8_0 (ftype 8), vectors and positions float32. The encoder's
+    tensors are not made (the decoder consumes its output)."""
+    rng = np.random.default_rng(seed)
+    st = cfg.n_state
+    t: dict = {"decoder.positional_embedding": _n(rng, (cfg.n_text_ctx, st), 0.1),
+               "decoder.token_embedding.weight": rand_q8(rng, cfg.n_vocab, st),
+               "decoder.ln.weight": 1.0 + _n(rng, st, 0.1), "decoder.ln.bias": _n(rng, st, 0.1)}
+    for i in range(cfg.n_text_layer):
+        p = f"decoder.blocks.{i}."
+        for ln in ("attn_ln", "cross_attn_ln", "mlp_ln"):
+            t[p + ln + ".weight"] = 1.0 + _n(rng, st, 0.1)
+            t[p + ln + ".bias"] = _n(rng, st, 0.1)
+        for a in ("attn", "cross_attn"):
+            for w in ("query", "key", "value", "out"):
+                t[f"{p}{a}.{w}.weight"] = rand_q8(rng, st, st)
+                if w != "key":
+                    t[f"{p}{a}.{w}.bias"] = _n(rng, st, 0.1)
+        t[p + "mlp.0.weight"] = rand_q8(rng, 4 * st, st)
+        t[p + "mlp.0.bias"] = _n(rng, 4 * st, 0.1)
+        t[p + "mlp.2.weight"] = rand_q8(rng, st, 4 * st)
+        t[p + "mlp.2.bias"] = _n(rng, st, 0.1)
+    return t
+
+
+def whisper_ggml(cfg: WhisperConfig, tensors: dict, words: list[bytes] | None = None, seed: int = 0,
+                 f16_bits: dict | None = None) -> bytes:
+    """A whisper.cpp model file (model.go:115-223): magic, hparams, mel
+    filters, vocabulary, then the tensors (dims fastest first). f16_bits
+    maps names to float16 bit arrays written as F16 tensors instead."""
+    rng = np.random.default_rng(seed + 77)
+    words = whisper_words(cfg) if words is None else words
+    out = [struct.pack("<I", GGML_MAGIC)]
+    out.append(struct.pack("<11i", cfg.n_vocab, cfg.n_audio_ctx, cfg.n_state, cfg.n_head, cfg.n_audio_layer,
+                           cfg.n_text_ctx, cfg.n_state, cfg.n_head, cfg.n_text_layer, cfg.n_mels, cfg.ftype))
+    out.append(struct.pack("<ii", cfg.n_mels, 201))
+    out.append(np.abs(rng.normal(0, 0.01, (cfg.n_mels, 201))).astype("<f4").tobytes())
+    out.append(struct.pack("<i", len(words)))
+    for w in words:
+        out.append(struct.pack("<i", len(w)) + w)
+    for name, arr in tensors.items():
+        nb = name.encode()
+        if f16_bits and name in f16_bits:
+            h = np.ascontiguousarray(f16_bits[name], dtype="<u2")
+            dims, typ, data = list(reversed(h.shape)), 1, h.tobytes()
+        elif isinstance(arr, Q8):
+            dims, typ, data = [arr.cols, arr.rows], 8, arr.blocks.tobytes()
+        else:
+            a = np.ascontiguousarray(arr, dtype="<f4")
+            dims, typ, data = list(reversed(a.shape)), 0, a.tobytes()
+        out.append(struct.pack("<iii", len(dims), len(nb), typ) + struct.pack(f"<{len(dims)}i", *dims) + nb + data)
+    return b"".join(out)
+
+
+def whisper_encoder_out(seed: int, cfg: WhisperConfig) -> np.ndarray:
+    """Encoder output [n_audio_ctx][n_state] of N(0,1) values for stream `seed`."""
+    return np.random.default_rng(30_000 + seed).normal(0.0, 1.0, (cfg.n_audio_ctx, cfg.n_state)).astype(np.float32)

@@ -68,7 +68,7 @@ void grx_weight_free(grx_weight* w);
  * or any m ≥ 2, takes the int8 path (activations rounded to Q8_0 blocks,
  * q8int.go:148-223); otherwise the float path (gemm.go:195-259). Host
  * buffers; synchronous. Limits of this build: the float path takes at most
- * 16 rows and K ≤ 2048 (Q8_0) or K ≤ 1024 (F32); the int8 path with more
+ * 16 rows and K ≤ 1536 (Q8_0) or K ≤ 1024 (F32); the int8 path with more
  * than 8 rows needs K % 128 == 0, with up to 8 rows N % 32 == 0. */
 int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, float* dst);
 
@@ -204,6 +204,52 @@ void* grx_tdt_batch_cuda_stream(const grx_tdt_batch* b);
 /* Kernel launches and loop iterations (batch rounds) issued so far. */
 int64_t grx_tdt_batch_launches(const grx_tdt_batch* b);
 int64_t grx_tdt_batch_iterations(const grx_tdt_batch* b);
+
+/* ------------------------------------------- Whisper text decoder ---------
+ * The token loop of whisper.Model (whisper/decoder.go:33-140,
+ * transcribe.go:150-269 and 370-520) for a batch of independent streams. */
+typedef struct grx_whisper grx_whisper;
+typedef struct grx_whisper_batch grx_whisper_batch;
+/* whisper.Load's decoder part (model.go:94-223, 320-448): a whisper.cpp
+ * ggml file; the encoder's tensors are read and left (the decoder is given
+ * the encoder's output). Matrices keep Q8_0 in HBM, widened as f16(q·d) on
+ * the fly exactly as the reference widens them at load; other types are
+ * widened to float16 at load as the reference does. Heads of 64 values. */
+int grx_whisper_load(const void* bytes, size_t len, int device, grx_whisper** out);
+void grx_whisper_free(grx_whisper* m);
+int grx_whisper_dims(const grx_whisper* m, int* n_vocab, int* n_audio_ctx, int* n_state, int* n_head,
+                     int* n_text_layer, int* n_text_ctx);
+/* The vocabulary's special tokens (vocab.go:19-43). */
+int grx_whisper_tokens(const grx_whisper* m, int* eot, int* sot, int* prev, int* nosp, int* beg, int* n_lang);
+/* vocab.suppressed() (vocab.go:103-118) into out (up to cap); returns the count. */
+int grx_whisper_suppressed(const grx_whisper* m, int* out, int cap);
+/* n streams, each a decoding sequence (its self-attention cache, this
+ * window's cross K/V, its sampling state). */
+int grx_whisper_batch_create(grx_whisper* m, int n, grx_whisper_batch** out);
+void grx_whisper_batch_free(grx_whisper_batch* b);
+/* A window for every stream: enc [n][n_audio_ctx][n_state] (host, or device
+ * for _device) → each layer's cross keys (·1/√64) and values
+ * (encoder.go:120-140, the packed product order of gemm.go:124-209); the
+ * caches and sampling states start over. */
+int grx_whisper_set_audio(grx_whisper_batch* b, const float* enc);
+int grx_whisper_set_audio_device(grx_whisper_batch* b, const float* d_enc);
+/* The prompt decode (transcribe.go:166-181): prompt [n][np] tokens, np ≤ 5
+ * (a prompt of 6 or more takes the reference's packed product, not in this
+ * build); no_speech [n] (may be NULL) gets softmax(logits at sot_at)[nosp]. */
+int grx_whisper_prompt(grx_whisper_batch* b, const int* prompt, int np, int sot_at, float* no_speech);
+/* `steps` rounds of the greedy loop at temperature 0 (transcribe.go:196-269:
+ * process, sample, decode of the sampled token), for every stream, without
+ * the window's stop rules. tokens [steps][n][4]: id, tid, p and plog (float
+ * bits), host or device (_device, asynchronous; grx_whisper_sync waits). */
+int grx_whisper_run(grx_whisper_batch* b, int steps, int* tokens);
+int grx_whisper_run_device(grx_whisper_batch* b, int steps, int* d_tokens);
+int grx_whisper_sync(grx_whisper_batch* b);
+/* Stream i's cross K [heads][ctx][64] and Vᵀ [heads][64][ctx] of a layer. */
+int grx_whisper_cross(grx_whisper_batch* b, int i, int layer, float* k, float* vt);
+/* The logits of the last decode, [n][n_vocab]. */
+int grx_whisper_logits(grx_whisper_batch* b, float* out);
+void* grx_whisper_batch_cuda_stream(const grx_whisper_batch* b);
+int64_t grx_whisper_batch_launches(const grx_whisper_batch* b);
 
 #ifdef __cplusplus
 }

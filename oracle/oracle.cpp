@@ -14,6 +14,7 @@
 
 #include "flowlm.h"
 #include "tdt.h"
+#include "whisper.h"
 
 using namespace orc;
 
@@ -413,6 +414,222 @@ void orc_tdt_run(void* hm, int n, const float* enc, int T, int D, int* tokens, i
   work();
   for (auto& t : ts) t.join();
   if (iters) *iters = it_total.load();
+}
+
+// ------------------------------------------------------------ Whisper ---
+// The text decoder's token loop (whisper/decoder.go, transcribe.go; see
+// whisper.h). Matrices are registered as float16 (the reference's memory
+// form); orc_q8_to_f16 widens Q8_0 blocks the way the reference loads them.
+
+struct OWhisper {
+  Whisper m;
+  std::map<std::string, Weight> w;
+  std::map<std::string, const float*> v;
+  std::string err;
+};
+
+void orc_q8_to_f16(const uint8_t* blocks, long n, uint16_t* out) { q8_to_f16(blocks, n, out); }
+
+void* orc_whisper_new(int n_vocab, int n_text_ctx, int n_state, int n_head, int n_layer) {
+  auto* o = new OWhisper();
+  o->m.n_vocab = n_vocab;
+  o->m.n_text_ctx = n_text_ctx;
+  o->m.n_state = n_state;
+  o->m.n_head = n_head;
+  o->m.layers.resize(size_t(n_layer));
+  o->m.voc.init(n_vocab);
+  return o;
+}
+
+void orc_whisper_free(void* h) { delete (OWhisper*)h; }
+
+const char* orc_whisper_error(void* h) { return ((OWhisper*)h)->err.c_str(); }
+
+// type 0: float32 (vectors or matrices), 1: float16 matrix [rows][cols].
+void orc_whisper_tensor(void* h, const char* name, int type, int rows, int cols, const void* p) {
+  auto* o = (OWhisper*)h;
+  Weight w;
+  w.rows = rows;
+  w.cols = cols;
+  w.type = WType(type);
+  w.f = (const float*)p;
+  w.h = (const uint16_t*)p;
+  o->w[name] = w;
+  o->v[name] = (const float*)p;
+}
+
+// The vocabulary's words (lengths[i] bytes each, concatenated): the " "
+// token and vocab.suppressed() (vocab.go:96-118): the non-speech marks and
+// their " "-prefixed forms below eot, then " -" and " '".
+void orc_whisper_vocab(void* h, const char* bytes, const int* lengths, int nwords) {
+  auto* o = (OWhisper*)h;
+  std::map<std::string, int> to_id;
+  long off = 0;
+  for (int i = 0; i < nwords; i++) {
+    std::string w(bytes + off, size_t(lengths[i]));
+    off += lengths[i];
+    to_id.emplace(w, i);
+  }
+  WVocab& v = o->m.voc;
+  auto it = to_id.find(" ");
+  v.space = it == to_id.end() ? -1 : it->second;
+  static const char* marks[] = {"\"", "#", "(", ")", "*", "+", "/", ":", ";", "<", "=", ">", "@", "[", "\\", "]", "^",
+                                "_", "`", "{", "|", "}", "~", "「", "」", "『", "』", "<<", ">>", "<<<", ">>>", "--",
+                                "---", "-(", "-[", "('", "(\"", "((", "))", "(((", ")))", "[[", "]]", "{{", "}}",
+                                "♪♪", "♪♪♪", "♩", "♪", "♫", "♬", "♭", "♮", "♯"};
+  v.suppress.clear();
+  for (const char* t : marks)
+    for (const std::string& s : {std::string(t), " " + std::string(t)}) {
+      auto f = to_id.find(s);
+      if (f != to_id.end() && f->second < v.eot) v.suppress.push_back(f->second);
+    }
+  for (const char* s : {" -", " '"}) {
+    auto f = to_id.find(s);
+    if (f != to_id.end()) v.suppress.push_back(f->second);
+  }
+}
+
+int orc_whisper_suppress(void* h, int* out, int cap) {
+  const auto& s = ((OWhisper*)h)->m.voc.suppress;
+  for (size_t i = 0; i < s.size() && int(i) < cap; i++) out[i] = s[i];
+  return int(s.size());
+}
+
+// Binds the decoder tensors (whisper/model.go:464-484).
+int orc_whisper_ready(void* h) {
+  auto* o = (OWhisper*)h;
+  auto W = [&](const std::string& n) {
+    auto it = o->w.find(n);
+    if (it == o->w.end()) {
+      o->err = "missing " + n;
+      return Weight{};
+    }
+    return it->second;
+  };
+  auto V = [&](const std::string& n) -> const float* {
+    auto it = o->v.find(n);
+    if (it == o->v.end()) {
+      o->err = "missing " + n;
+      return nullptr;
+    }
+    return it->second;
+  };
+  Whisper& m = o->m;
+  m.dec_pos = V("decoder.positional_embedding");
+  m.tok_emb = W("decoder.token_embedding.weight");
+  m.ln_w = V("decoder.ln.weight");
+  m.ln_b = V("decoder.ln.bias");
+  for (size_t i = 0; i < m.layers.size(); i++) {
+    const std::string p = "decoder.blocks." + std::to_string(i) + ".";
+    WLayer& L = m.layers[i];
+    L.attn_ln_w = V(p + "attn_ln.weight");
+    L.attn_ln_b = V(p + "attn_ln.bias");
+    L.q = W(p + "attn.query.weight");
+    L.qb = V(p + "attn.query.bias");
+    L.k = W(p + "attn.key.weight");
+    L.v = W(p + "attn.value.weight");
+    L.vb = V(p + "attn.value.bias");
+    L.o = W(p + "attn.out.weight");
+    L.ob = V(p + "attn.out.bias");
+    L.x_ln_w = V(p + "cross_attn_ln.weight");
+    L.x_ln_b = V(p + "cross_attn_ln.bias");
+    L.xq = W(p + "cross_attn.query.weight");
+    L.xqb = V(p + "cross_attn.query.bias");
+    L.xk = W(p + "cross_attn.key.weight");
+    L.xv = W(p + "cross_attn.value.weight");
+    L.xvb = V(p + "cross_attn.value.bias");
+    L.xo = W(p + "cross_attn.out.weight");
+    L.xob = V(p + "cross_attn.out.bias");
+    L.mlp_ln_w = V(p + "mlp_ln.weight");
+    L.mlp_ln_b = V(p + "mlp_ln.bias");
+    L.fc1 = W(p + "mlp.0.weight");
+    L.fc1b = V(p + "mlp.0.bias");
+    L.fc2 = W(p + "mlp.2.weight");
+    L.fc2b = V(p + "mlp.2.bias");
+  }
+  return o->err.empty() ? 0 : -1;
+}
+
+void* orc_wseq_new(void* h) {
+  auto* s = new WSeq();
+  s->init(((OWhisper*)h)->m);
+  return s;
+}
+
+void orc_wseq_free(void* s) { delete (WSeq*)s; }
+
+void orc_whisper_cross_kv(void* h, void* s, const float* enc) { whisper_cross_kv(((OWhisper*)h)->m, *(WSeq*)s, enc); }
+
+// The sequence's cross K ([heads][ctx][hd], pre-scaled) and V ([heads][hd][ctx]) of a layer.
+void orc_wseq_cross(void* s, int layer, float* k, float* v) {
+  auto* q = (WSeq*)s;
+  std::copy(q->ck[size_t(layer)].begin(), q->ck[size_t(layer)].end(), k);
+  std::copy(q->cv[size_t(layer)].begin(), q->cv[size_t(layer)].end(), v);
+}
+
+int orc_whisper_decode(void* h, void* s, const int* tokens, int nt, const int* want, int nwant, float* logits) {
+  return whisper_decode(((OWhisper*)h)->m, *(WSeq*)s, tokens, nt, want, nwant, logits) ? 0 : -1;
+}
+
+// The packed or per-row matmul of whisper/gemm.go (tests of its order).
+void orc_whisper_matmul(float* c, const float* a, int m, int n, int k, int type, const void* b, const float* bias) {
+  Weight w;
+  w.rows = n;
+  w.cols = k;
+  w.type = WType(type);
+  w.f = (const float*)b;
+  w.h = (const uint16_t*)b;
+  matmul_whisper(c, n, a, k, m, n, k, w, bias);
+}
+
+// process + sample at temperature 0 for a sequence in state st = {nt,
+// last, penult, has_ts, seek_delta}; lg is modified as process does.
+// out = {id, tid, p bits, plog bits}.
+void orc_whisper_process_sample(void* h, const int* st, float* lg, int* out) {
+  WSampleState q;
+  q.nt = st[0], q.last = st[1], q.penult = st[2], q.has_ts = st[3] != 0, q.seek_delta = st[4];
+  const WToken t = whisper_process_sample(((OWhisper*)h)->m, q, lg);
+  out[0] = t.id;
+  out[1] = t.tid;
+  std::memcpy(&out[2], &t.p, 4);
+  std::memcpy(&out[3], &t.plog, 4);
+}
+
+// whisper_greedy (see whisper.h). tokens [steps][4]; returns the count.
+int orc_whisper_greedy(void* h, void* s, const int* prompt, int np, int sot_at, int steps, int* tokens,
+                       float* no_speech) {
+  const std::vector<WToken> out = whisper_greedy(((OWhisper*)h)->m, *(WSeq*)s, prompt, np, sot_at, steps, no_speech);
+  for (size_t i = 0; i < out.size(); i++) {
+    tokens[4 * i] = out[i].id;
+    tokens[4 * i + 1] = out[i].tid;
+    std::memcpy(&tokens[4 * i + 2], &out[i].p, 4);
+    std::memcpy(&tokens[4 * i + 3], &out[i].plog, 4);
+  }
+  return int(out.size());
+}
+
+// n independent streams on host threads (the CPU baseline): each takes its
+// encoder output enc + i·ctx·state, the cross K/V, then the greedy run.
+void orc_whisper_run(void* h, int n, const float* enc, const int* prompt, int np, int sot_at, int steps, int* tokens,
+                     int threads) {
+  const Whisper& m = ((OWhisper*)h)->m;
+  std::atomic<int> next{0};
+  auto work = [&]() {
+    for (;;) {
+      const int i = next.fetch_add(1);
+      if (i >= n) return;
+      WSeq s;
+      s.init(m);
+      whisper_cross_kv(m, s, enc + size_t(i) * m.n_audio_ctx * m.n_state);
+      const std::vector<WToken> out = whisper_greedy(m, s, prompt, np, sot_at, steps, nullptr);
+      for (size_t k = 0; k < out.size(); k++) tokens[(size_t(i) * steps + k)] = out[k].id;
+    }
+  };
+  threads = std::max(1, std::min(threads, n));
+  std::vector<std::thread> ts;
+  for (int t = 1; t < threads; t++) ts.emplace_back(work);
+  work();
+  for (auto& t : ts) t.join();
 }
 
 }  // extern "C"

@@ -64,6 +64,23 @@ def lib():
             "orc_tdt_ready": (I, [P]),
             "orc_tdt_decode": (I, [P, P, I, I, P, P, P, P, I, P, P]),
             "orc_tdt_run": (None, [P, I, P, I, I, P, I, P, P, I]),
+            "orc_q8_to_f16": (None, [P, C.c_long, P]),
+            "orc_whisper_new": (P, [I, I, I, I, I]),
+            "orc_whisper_free": (None, [P]),
+            "orc_whisper_error": (C.c_char_p, [P]),
+            "orc_whisper_tensor": (None, [P, C.c_char_p, I, I, I, P]),
+            "orc_whisper_vocab": (None, [P, P, P, I]),
+            "orc_whisper_suppress": (I, [P, P, I]),
+            "orc_whisper_ready": (I, [P]),
+            "orc_wseq_new": (P, [P]),
+            "orc_wseq_free": (None, [P]),
+            "orc_whisper_cross_kv": (None, [P, P, P]),
+            "orc_wseq_cross": (None, [P, I, P, P]),
+            "orc_whisper_decode": (I, [P, P, P, I, P, I, P]),
+            "orc_whisper_matmul": (None, [P, P, I, I, I, I, P, P]),
+            "orc_whisper_process_sample": (None, [P, P, P, P]),
+            "orc_whisper_greedy": (I, [P, P, P, I, I, I, P, P]),
+            "orc_whisper_run": (None, [P, I, P, P, I, I, I, P, I]),
         }
         for k, (r, a) in sig.items():
             f = getattr(L, k)
@@ -279,5 +296,107 @@ class TDT:
     def __del__(self):
         if getattr(self, "h", None) and _lib is not None:
             _lib.orc_tdt_free(self.h)
+            self.h = None
+
+
+def q8_to_f16(q8) -> np.ndarray:
+    """Q8_0 blocks widened as the Whisper loader does (model.go:486-490):
+    float16 bits [rows][cols]."""
+    out = np.empty((q8.rows, q8.cols), np.uint16)
+    lib().orc_q8_to_f16(p(np.ascontiguousarray(q8.blocks)), q8.rows * q8.cols, p(out))
+    return out
+
+
+class Whisper:
+    """The oracle's Whisper text decoder (whisper/decoder.go, transcribe.go)
+    from the synthetic generator's tensors and words."""
+
+    def __init__(self, cfg, tensors: dict, words: list[bytes]):
+        from gorelaxor_b200.synth import Q8
+
+        self.cfg = cfg
+        self._keep = []
+        L = lib()
+        self.h = L.orc_whisper_new(cfg.n_vocab, cfg.n_text_ctx, cfg.n_state, cfg.n_head, cfg.n_text_layer)
+        for name, arr in tensors.items():
+            if isinstance(arr, Q8):
+                buf = q8_to_f16(arr)
+                L.orc_whisper_tensor(self.h, name.encode(), 1, arr.rows, arr.cols, p(buf))
+            else:
+                buf = np.ascontiguousarray(arr, np.float32)
+                rows, cols = (buf.shape if buf.ndim == 2 else (1, buf.size))
+                L.orc_whisper_tensor(self.h, name.encode(), 0, rows, cols, p(buf))
+            self._keep.append(buf)
+        blob = np.frombuffer(b"".join(words), np.uint8) if words else np.zeros(1, np.uint8)
+        lens = np.array([len(w) for w in words], np.int32)
+        self._keep += [blob, lens]
+        L.orc_whisper_vocab(self.h, p(blob), p(lens), len(words))
+        if L.orc_whisper_ready(self.h) != 0:
+            raise RuntimeError(L.orc_whisper_error(self.h).decode())
+
+    def suppress(self) -> list[int]:
+        out = np.zeros(256, np.int32)
+        n = lib().orc_whisper_suppress(self.h, p(out), 256)
+        return out[:n].tolist()
+
+    def seq(self, enc: np.ndarray | None = None):
+        s = WSeq(lib().orc_wseq_new(self.h))
+        if enc is not None:
+            lib().orc_whisper_cross_kv(self.h, s.h, p(np.ascontiguousarray(enc, np.float32)))
+        return s
+
+    def cross(self, s, layer: int):
+        c = self.cfg
+        hd = c.n_state // c.n_head
+        k = np.empty((c.n_head, c.n_audio_ctx, hd), np.float32)
+        v = np.empty((c.n_head, hd, c.n_audio_ctx), np.float32)
+        lib().orc_wseq_cross(s.h, layer, p(k), p(v))
+        return k, v
+
+    def decode(self, s, tokens, want):
+        t = np.ascontiguousarray(tokens, np.int32)
+        w = np.ascontiguousarray(want, np.int32)
+        out = np.empty((len(w), self.cfg.n_vocab), np.float32)
+        if lib().orc_whisper_decode(self.h, s.h, p(t), len(t), p(w), len(w), p(out)) != 0:
+            return None
+        return out
+
+    def process_sample(self, state, lg):
+        """state = (nt, last, penult, has_ts, seek_delta); lg is modified in
+        place. Returns (id, tid, p, plog)."""
+        st = np.ascontiguousarray(state, np.int32)
+        out = np.zeros(4, np.int32)
+        lib().orc_whisper_process_sample(self.h, p(st), p(lg), p(out))
+        return int(out[0]), int(out[1]), float(out[2:3].view(np.float32)[0]), float(out[3:4].view(np.float32)[0])
+
+    def greedy(self, s, prompt, sot_at: int, steps: int):
+        """Tokens [n][4] (id, tid, p bits, plog bits) and the no-speech probability."""
+        pr = np.ascontiguousarray(prompt, np.int32)
+        toks = np.zeros((steps, 4), np.int32)
+        ns = C.c_float(0)
+        n = lib().orc_whisper_greedy(self.h, s.h, p(pr), len(pr), sot_at, steps, p(toks), C.byref(ns))
+        return toks[:n], ns.value
+
+    def run(self, enc: np.ndarray, prompt, sot_at: int, steps: int, threads: int) -> np.ndarray:
+        """n streams (enc [n][ctx][state]) decoded on host threads: token ids [n][steps]."""
+        enc = np.ascontiguousarray(enc, np.float32)
+        pr = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros((enc.shape[0], steps), np.int32)
+        lib().orc_whisper_run(self.h, enc.shape[0], p(enc), p(pr), len(pr), sot_at, steps, p(out), threads)
+        return out
+
+    def __del__(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.orc_whisper_free(self.h)
+            self.h = None
+
+
+class WSeq:
+    def __init__(self, h):
+        self.h = h
+
+    def __del__(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.orc_wseq_free(self.h)
             self.h = None
 

@@ -55,11 +55,14 @@ def test_q8_float_path_bit_exact(have_gpu, n, k):
     assert rel <= TOL
 
 
-@pytest.mark.parametrize("n,k", [(1024, 32), (32, 512), (512, 32), (1, 1024), (6, 48), (100, 96)])
-def test_f32_float_path_bit_exact(have_gpu, n, k):
+@pytest.mark.parametrize("n,k,m", [(1024, 32, 1), (32, 512, 1), (512, 32, 13), (1, 1024, 1), (6, 48, 16),
+                                   (100, 96, 3)])
+def test_f32_float_path_bit_exact(have_gpu, n, k, m):
+    """F32 weights take the float path for any number of rows (dot4f32avx
+    per four rows, dotF32Go for the rest)."""
     rng = np.random.default_rng(n * k)
     w = rng.normal(0, 0.2, (n, k)).astype(np.float32)
-    x = rng.normal(0, 1, (1, k)).astype(np.float32)
+    x = rng.normal(0, 1, (m, k)).astype(np.float32)
     got = g.linear(g.Weight.f32(w), x)
     want = orc.linear(x, "f32", w, n, k)
     assert bits_equal(got, want)
