@@ -500,7 +500,8 @@ def main():
     d_noise = torch.from_numpy(noise).cuda()
     d_lat = torch.empty_like(d_noise)
     d_eos = torch.empty((F, B), device="cuda")
-    d_ts = torch.empty((F, cfg.layers, 2), dtype=torch.int64, device="cuda")
+    P = st.parts()
+    d_ts = torch.empty((F, cfg.layers, P, 2), dtype=torch.int64, device="cuda")
     ext = torch.cuda.ExternalStream(st.cuda_stream())  # the library's stream: events go there
 
     def one_step(timed_ts=False):
@@ -556,9 +557,9 @@ def main():
     nk = 64 + np.arange(F) + 1
     per_launch = B * (H * (nk * 64 * 4 * 2 + 64 * 4) + d * 1 + d // 32 * 8)  # K+V reads, q, Q8 out (s,s)
     per_launch = np.repeat(per_launch[:, None], cfg.layers, axis=1).astype(np.float64)
-    durs = np.stack(attn_ns)  # [steps][F][L]
+    durs = np.stack(attn_ns)  # [steps][F][L][parts]
     achieved = float(per_launch.sum() * args.steps / durs.sum())  # B/ns = GB/s
-    attn_share = float(durs.sum() / 1e6 / np.sum(step_ms))  # of the timed steps, this rank
+    attn_share = float(durs.sum() / 1e6 / np.sum(step_ms) / P)  # of each part's timeline, this rank
     hbm, peak_kind = peaks()
     # DRAM bytes per launch: one ncu capture at 66 keys (256 streams, frame 1,
     # layers 0-1: read+write 143.51 MB against 139.79 MB algorithmic) scaled

@@ -73,6 +73,7 @@ def _sig(lib):
         "grx_streams_pos": (I, [P, I]),
         "grx_streams_launches": (L, [P]),
         "grx_streams_cuda_stream": (P, [P]),
+        "grx_streams_parts": (I, [P]),
         "grx_tdt_load": (I, [P, S, I, PP]),
         "grx_tdt_free": (None, [P]),
         "grx_tdt_dims": (I, [P] + [C.POINTER(C.c_int)] * 8),
@@ -312,7 +313,7 @@ class Streams:
 
     def run_device_timed(self, frames: int, d_noise: int, d_latent: int, d_eos: int | None, d_ts: int):
         """run_device that also records each attention kernel's span into the
-        device array d_ts [frames][layers][2] (uint64 ns, preset to
+        device array d_ts [frames][layers][parts][2] (uint64 ns, preset to
         {UINT64_MAX, 0})."""
         _check(lib().grx_streams_run_device_timed(self._h, frames, C.c_void_p(d_noise), C.c_void_p(d_latent),
                                                   C.c_void_p(d_eos) if d_eos else None, C.c_void_p(d_ts)))
@@ -329,6 +330,10 @@ class Streams:
 
     def launches(self) -> int:
         return lib().grx_streams_launches(self._h)
+
+    def parts(self) -> int:
+        """1, or 2 when the set runs as two concurrent parts."""
+        return _check(lib().grx_streams_parts(self._h))
 
     def __del__(self, _free=_FREE):
         h, self._h = getattr(self, "_h", None), None

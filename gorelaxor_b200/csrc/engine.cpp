@@ -96,15 +96,26 @@ struct grx_streams {
   cudaGraph_t graph = nullptr;
   int64_t launches = 0;
   int per_frame = 0;
+  // A large set runs as parts, each with its own CUDA stream and frame graph,
+  // so that one part's memory-bound attention overlaps the other's
+  // latency-bound products; the parent's stream forks to and joins them.
+  std::vector<std::unique_ptr<grx_streams>> parts;
+  int row0 = 0;  // a part's first stream within its parent
+  cudaEvent_t ev = nullptr;
   ~grx_streams() {
+    parts.clear();
     cudaSetDevice(ar.dev);
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
+    if (ev) cudaEventDestroy(ev);
     if (st) cudaStreamDestroy(st);
   }
 };
 
 namespace {
+
+// A stream set of at least twice this many streams runs as two parts.
+constexpr int kMinPart = 64;
 
 // The kernel sequence of one frame for all streams (see grx.h): flowLM.step
 // (lm.go:185-195 → nn.go:142-182) then flowHead.sample (lm.go:108-160).
@@ -788,6 +799,11 @@ void grx_voice_free(grx_voice* v) { delete v; }
 
 int grx_streams_reset(grx_streams* s) {
   if (!s) return fail(GRX_EINVAL, "null streams");
+  for (auto& p : s->parts) {
+    int rc = grx_streams_reset(p.get());
+    if (rc) return rc;
+  }
+  if (!s->parts.empty()) return GRX_OK;
   grx_flowlm* m = s->m;
   CK(cudaSetDevice(s->ar.dev));
   CK(cudaMemcpyAsync(s->pos, s->pos0, sizeof(int) * size_t(s->n), cudaMemcpyDeviceToDevice, s->st));
@@ -798,10 +814,46 @@ int grx_streams_reset(grx_streams* s) {
   return GRX_OK;
 }
 
+static int streams_create_one(grx_flowlm* m, int n, const grx_voice* const* voices, int max_frames,
+                              std::unique_ptr<grx_streams>* out);
+
 int grx_streams_create(grx_flowlm* m, int n, const grx_voice* const* voices, int max_frames, grx_streams** out) {
   if (!m || !voices || !out || n < 1 || max_frames < 1) return fail(GRX_EINVAL, "grx_streams_create: bad argument");
   int rc = device_init(m->dev);
   if (rc) return rc;
+  const int nparts = n >= 2 * kMinPart ? 2 : 1;
+  if (nparts == 1) {
+    std::unique_ptr<grx_streams> s;
+    rc = streams_create_one(m, n, voices, max_frames, &s);
+    if (rc) return rc;
+    *out = s.release();
+    return GRX_OK;
+  }
+  auto s = std::make_unique<grx_streams>();
+  s->ar.dev = m->dev;
+  s->m = m;
+  s->n = n;
+  CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+  CK(cudaEventCreateWithFlags(&s->ev, cudaEventDisableTiming));
+  for (int i = 0, r0 = 0; i < nparts; i++) {
+    const int ni = n / nparts + (i < n % nparts ? 1 : 0);
+    std::unique_ptr<grx_streams> p;
+    rc = streams_create_one(m, ni, voices + r0, max_frames, &p);
+    if (rc) return rc;
+    p->row0 = r0;
+    CK(cudaEventCreateWithFlags(&p->ev, cudaEventDisableTiming));
+    s->cap = p->cap;
+    s->per_frame += p->per_frame;
+    s->parts.push_back(std::move(p));
+    r0 += ni;
+  }
+  *out = s.release();
+  return GRX_OK;
+}
+
+static int streams_create_one(grx_flowlm* m, int n, const grx_voice* const* voices, int max_frames,
+                              std::unique_ptr<grx_streams>* out) {
+  int rc = 0;
   int maxp = 0;
   for (int i = 0; i < n; i++) {
     if (!voices[i]) return fail(GRX_EINVAL, "null voice");
@@ -890,7 +942,7 @@ int grx_streams_create(grx_flowlm* m, int n, const grx_voice* const* voices, int
   if (rc) return rc;
   rc = build_graph(s.get());
   if (rc) return rc;
-  *out = s.release();
+  *out = std::move(s);
   return GRX_OK;
 }
 
@@ -898,19 +950,36 @@ void grx_streams_free(grx_streams* s) { delete s; }
 
 int grx_streams_pos(const grx_streams* s, int i) {
   if (!s || i < 0 || i >= s->n) return fail(GRX_EINVAL, "bad stream index");
+  for (const auto& p : s->parts)
+    if (i < p->row0 + p->n) return grx_streams_pos(p.get(), i - p->row0);
   int p = 0;
   cudaSetDevice(s->ar.dev);
   if (cudaMemcpy(&p, s->pos + i, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return fail(GRX_ECUDA, "read pos");
   return p;
 }
 
-int64_t grx_streams_launches(const grx_streams* s) { return s ? s->launches : 0; }
+int64_t grx_streams_launches(const grx_streams* s) {
+  if (!s) return 0;
+  int64_t l = s->launches;
+  for (const auto& p : s->parts) l += p->launches;
+  return l;
+}
 
 void* grx_streams_cuda_stream(const grx_streams* s) { return s ? (void*)s->st : nullptr; }
+
+int grx_streams_parts(const grx_streams* s) {
+  if (!s) return fail(GRX_EINVAL, "null streams");
+  return s->parts.empty() ? 1 : int(s->parts.size());
+}
 
 // Checks that `frames` more frames fit the caches (positions are equal for
 // streams that started from voices of equal length; the longest decides).
 static int check_room(grx_streams* s, int frames) {
+  for (auto& p : s->parts) {
+    int rc = check_room(p.get(), frames);
+    if (rc) return rc;
+  }
+  if (!s->parts.empty()) return GRX_OK;
   int maxp = 0;
   std::vector<int> p(size_t(s->n));
   CK(cudaMemcpyAsync(p.data(), s->pos, sizeof(int) * size_t(s->n), cudaMemcpyDeviceToHost, s->st));
@@ -927,17 +996,24 @@ int grx_streams_step(grx_streams* s, const float* noise, float* lm_out, float* e
   CK(cudaSetDevice(s->ar.dev));
   int rc = check_room(s, 1);
   if (rc) return rc;
-  const size_t nl = size_t(s->n) * s->m->ldim;
-  FrameIO io{s->noise1, nullptr, nullptr, s->eos1, 0, nullptr};
-  CK(cudaMemcpyAsync(s->noise1, noise, nl * 4, cudaMemcpyHostToDevice, s->st));
-  CK(cudaMemcpyAsync(s->io, &io, sizeof io, cudaMemcpyHostToDevice, s->st));
-  CK(cudaGraphLaunch(s->exec, s->st));
-  s->launches += s->per_frame;
-  if (lm_out) CK(cudaMemcpyAsync(lm_out, s->lm_out, size_t(s->n) * s->m->d * 4, cudaMemcpyDeviceToHost, s->st));
-  if (eos) CK(cudaMemcpyAsync(eos, s->eos1, size_t(s->n) * 4, cudaMemcpyDeviceToHost, s->st));
-  if (latent) CK(cudaMemcpyAsync(latent, s->lat1, nl * 4, cudaMemcpyDeviceToHost, s->st));
-  if (scaled) CK(cudaMemcpyAsync(scaled, s->scaled1, nl * 4, cudaMemcpyDeviceToHost, s->st));
-  CK(cudaStreamSynchronize(s->st));
+  // each part (or the set itself) queues its frame on its own stream
+  std::vector<grx_streams*> sets;
+  if (s->parts.empty()) sets.push_back(s);
+  for (auto& p : s->parts) sets.push_back(p.get());
+  const int ld = s->m->ldim, d = s->m->d;
+  for (grx_streams* q : sets) {
+    const size_t r0 = size_t(q->row0), nl = size_t(q->n) * ld;
+    FrameIO io{q->noise1, nullptr, nullptr, q->eos1, 0, nullptr, q->n, 0, 0, 1};
+    CK(cudaMemcpyAsync(q->noise1, noise + r0 * ld, nl * 4, cudaMemcpyHostToDevice, q->st));
+    CK(cudaMemcpyAsync(q->io, &io, sizeof io, cudaMemcpyHostToDevice, q->st));
+    CK(cudaGraphLaunch(q->exec, q->st));
+    q->launches += q->per_frame;
+    if (lm_out) CK(cudaMemcpyAsync(lm_out + r0 * d, q->lm_out, size_t(q->n) * d * 4, cudaMemcpyDeviceToHost, q->st));
+    if (eos) CK(cudaMemcpyAsync(eos + r0, q->eos1, size_t(q->n) * 4, cudaMemcpyDeviceToHost, q->st));
+    if (latent) CK(cudaMemcpyAsync(latent + r0 * ld, q->lat1, nl * 4, cudaMemcpyDeviceToHost, q->st));
+    if (scaled) CK(cudaMemcpyAsync(scaled + r0 * ld, q->scaled1, nl * 4, cudaMemcpyDeviceToHost, q->st));
+  }
+  for (grx_streams* q : sets) CK(cudaStreamSynchronize(q->st));
   return GRX_OK;
 }
 
@@ -951,10 +1027,29 @@ int grx_streams_run_device_timed(grx_streams* s, int frames, const float* d_nois
   CK(cudaSetDevice(s->ar.dev));
   int rc = check_room(s, frames);
   if (rc) return rc;
-  FrameIO io{d_noise, d_latent, nullptr, d_eos, 0, d_attn_ts};
-  CK(cudaMemcpyAsync(s->io, &io, sizeof io, cudaMemcpyHostToDevice, s->st));
-  for (int f = 0; f < frames; f++) CK(cudaGraphLaunch(s->exec, s->st));
-  s->launches += int64_t(frames) * s->per_frame;
+  if (s->parts.empty()) {
+    FrameIO io{d_noise, d_latent, nullptr, d_eos, 0, d_attn_ts, s->n, 0, 0, 1};
+    CK(cudaMemcpyAsync(s->io, &io, sizeof io, cudaMemcpyHostToDevice, s->st));
+    for (int f = 0; f < frames; f++) CK(cudaGraphLaunch(s->exec, s->st));
+    s->launches += int64_t(frames) * s->per_frame;
+    return GRX_OK;
+  }
+  // fork: the parts wait for what was queued on the parent's stream
+  CK(cudaEventRecord(s->ev, s->st));
+  for (size_t i = 0; i < s->parts.size(); i++) {
+    auto& p = s->parts[i];
+    CK(cudaStreamWaitEvent(p->st, s->ev, 0));
+    FrameIO io{d_noise, d_latent, nullptr, d_eos, 0, d_attn_ts, s->n, p->row0, int(i), int(s->parts.size())};
+    CK(cudaMemcpyAsync(p->io, &io, sizeof io, cudaMemcpyHostToDevice, p->st));
+  }
+  for (int f = 0; f < frames; f++)
+    for (auto& p : s->parts) CK(cudaGraphLaunch(p->exec, p->st));
+  // join: the parent's stream waits for every part
+  for (auto& p : s->parts) {
+    p->launches += int64_t(frames) * p->per_frame;
+    CK(cudaEventRecord(p->ev, p->st));
+    CK(cudaStreamWaitEvent(s->st, p->ev, 0));
+  }
   return GRX_OK;
 }
 

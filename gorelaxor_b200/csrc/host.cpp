@@ -67,8 +67,15 @@ DQ8 upload_q8(Arena& ar, const uint8_t* blocks, int rows, int cols, int* rc) {
     }
   w.q = ar.upload(q.data(), q.size(), rc);
   w.d = ar.upload(d.data(), d.size(), rc);
-  w.dwT = ar.upload(dwT.data(), dwT.size(), rc);
-  w.nmT = ar.upload(nmT.data(), nmT.size(), rc);
+  const size_t np = (size_t(rows) + 1) / 2;
+  std::vector<float> quads(nb * np * 4, 0.f);
+  for (size_t b = 0; b < nb; b++)
+    for (size_t r = 0; r < size_t(rows); r++) {
+      float* q4 = &quads[(b * np + r / 2) * 4];
+      q4[r & 1] = dwT[b * rows + r];
+      q4[2 + (r & 1)] = nmT[b * rows + r];
+    }
+  w.dwnm = reinterpret_cast<const float4*>(ar.upload(quads.data(), quads.size(), rc));
   return w;
 }
 

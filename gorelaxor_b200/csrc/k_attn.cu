@@ -42,7 +42,8 @@ __global__ void __launch_bounds__(64) k_attn(AttnArgs a) {
   const float* V = a.kv + vbase;
   const float* q = a.q + (size_t)m * a.d + h * HD;
   unsigned long long* ts = nullptr;
-  if (a.io && a.io->attn_ts) ts = a.io->attn_ts + ((size_t)a.io->frame * a.layers + a.layer) * 2;
+  if (a.io && a.io->attn_ts)
+    ts = a.io->attn_ts + (((size_t)a.io->frame * a.layers + a.layer) * a.io->parts + a.io->part) * 2;
   if (ts && tid == 0) {
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));

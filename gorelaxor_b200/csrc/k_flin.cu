@@ -117,15 +117,15 @@ __device__ __forceinline__ void fl_out(const FArgs& a, int m, int n, float r) {
       *yp = __fadd_rn(*yp, __fmul_rn(a.aux[(size_t)m * a.ldaux + n], v));
       break;
     case FE_LATENT: {
-      const int Mr = a.M;
-      const float* aux = a.aux_noise ? a.io->noise + (size_t)a.io->frame * Mr * a.ldaux : a.aux;
+      const float* aux =
+          a.aux_noise ? a.io->noise + ((size_t)a.io->frame * a.io->rows + a.io->row0) * a.ldaux : a.aux;
       const float cur = __fadd_rn(aux[(size_t)m * a.ldaux + n], __fdiv_rn(v, a.steps));
       *yp = cur;
       const float sc = __fadd_rn(__fmul_rn(cur, a.stdv[n]), a.mean[n]);
       if (a.out2) a.out2[(size_t)m * a.ldy + n] = cur;
       if (a.out3) a.out3[(size_t)m * a.ldy + n] = sc;
       if (a.io_out) {
-        const size_t o = ((size_t)a.io->frame * Mr + m) * a.ldy + n;
+        const size_t o = ((size_t)a.io->frame * a.io->rows + a.io->row0 + m) * a.ldy + n;
         if (a.io->latent) a.io->latent[o] = cur;
         if (a.io->scaled) a.io->scaled[o] = sc;
       }
@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(256) k_flin(FArgs a) {
   uint8_t* ws = fsm + size_t(KC) * XS * 4;
   constexpr int wst = T::wbytes, dst = T::dstride;
   float* ds = reinterpret_cast<float*>(ws + size_t(TN) * wst);
-  const float* xsrc = a.x_noise ? a.io->noise + (size_t)a.io->frame * a.M * a.ldx : a.x;
+  const float* xsrc = a.x_noise ? a.io->noise + ((size_t)a.io->frame * a.io->rows + a.io->row0) * a.ldx : a.x;
   const int kfull = WM == W_Q8 ? K : (K & ~15);  // the vector part of the dot
 
   f2 acc[R][M / 2], acc1[R][M / 2];
@@ -387,17 +387,17 @@ void fl_dispatch(const FArgs& a, cudaStream_t st) {
   else if (a.M <= 8)
     fl_launch<WM, 1, 8, 16>(a, st);  // 16 rows × 16 streams
   else if (WM == W_Q8)
-    fl_launch<WM, 1, 16, 16>(a, st);  // 16 rows × 32 streams
+    fl_launch<WM, 2, 16, 16>(a, st);  // 32 rows × 32 streams
   else
-    fl_launch<WM, 1, 8, 8>(a, st);  // 8 rows × 32 streams
+    fl_launch<WM, 4, 8, 8>(a, st);  // 32 rows × 32 streams
 }
 
 template <int WM>
 void fl_init_all() {
   fl_init<WM, 2, 4, 32>();
   fl_init<WM, 1, 8, 16>();
-  fl_init<WM, 1, 16, 16>();
-  fl_init<WM, 1, 8, 8>();
+  fl_init<WM, 2, 16, 16>();
+  fl_init<WM, 4, 8, 8>();
 }
 
 }  // namespace

@@ -69,7 +69,7 @@ __global__ void k_ln(LnArgs a, int D) {
         for (int i = D4; i < D; i++) s = __fadd_rn(s, __fmul_rn(srow[i], sw[i]));
         const float e = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3), a.eosb);
         if (a.eos) a.eos[m] = e;
-        if (a.io && a.io->eos) a.io->eos[(size_t)a.io->frame * gridDim.x + m] = e;
+        if (a.io && a.io->eos) a.io->eos[(size_t)a.io->frame * a.io->rows + a.io->row0 + m] = e;
         if (a.pos) a.pos[m] += 1;
       }
     }

@@ -9,7 +9,7 @@
 //  * k_q8_gemv for M ≤ 8 (one stream, or a few): HBM-bound, one warp per
 //    weight row, lanes split K into blocks, dp4a block dots, then the
 //    block chain in order through warp shuffles.
-//  * k_q8_gemm for more rows (batched streams): mma.sync m16n8k32 s8 — one
+//  * k_q8_gemm2 for more rows (batched streams): mma.sync m16n8k32 s8 — one
 //    MMA k-step is exactly one Q8_0 block, so each block's int32 tile comes
 //    out of the tensor core whole and is folded into float32 accumulators
 //    with the per-block scales before the next block.
@@ -166,9 +166,7 @@ __global__ void __launch_bounds__(256) k_q8_gemv(const int8_t* __restrict__ a, c
 // The chain over K blocks cannot be split, so the parallelism of a product
 // is its M×N outputs (at M = 256 streams and N = 1024 only 256K). A warp
 // owns TM×TN m16n8 tiles (TM·TN MMAs per block, the A fragment shared by the
-// TN column tiles), eight warps a CTA tile; a stage carries KB blocks of K.
-// Every shared-memory address is a 32-bit offset computed once, and the
-// scale operands are read as ready-made pairs. The tile shape is chosen per
+// TN column tiles), WGM×WGN warps a CTA tile. The tile shape is chosen per
 // product shape (launch_q8_product).
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
@@ -196,30 +194,6 @@ __device__ __forceinline__ f2 lds64(uint32_t a) {
   return v;
 }
 
-// One Q8_0 block of a 16×8 tile, in one piece of PTX so every value stays
-// in its register pair: D = A·B + MAGIC_BITS (the tensor core's int32 sum
-// lands on the bits of the float 1.5·2^23 + s, |s| ≤ 32·128·128 = 2^19), then
-// t = fma(1.5·2^23 + s, dw, −1.5·2^23·dw) = fl(float(s)·dw) — one rounding
-// of the exact product, as the reference's VMULPS (vnni_amd64.s:63-64) —
-// and acc = fma(t, da, acc) (its VFMADD213PS, :66-67), both as f32x2 pairs.
-__device__ __forceinline__ void q8_block(f2& acc01, f2& acc23, const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
-                                         f2 dw, f2 nm, f2 da0, f2 da1) {
-  asm("{\n"
-      " .reg .b32 d0, d1, d2, d3;\n"
-      " .reg .b64 p01, p23;\n"
-      " mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {d0,d1,d2,d3}, {%2,%3,%4,%5}, {%6,%7}, {%12,%12,%12,%12};\n"
-      " mov.b64 p01, {d0, d1};\n"
-      " mov.b64 p23, {d2, d3};\n"
-      " fma.rn.f32x2 p01, p01, %8, %9;\n"
-      " fma.rn.f32x2 p23, p23, %8, %9;\n"
-      " fma.rn.f32x2 %0, p01, %10, %0;\n"
-      " fma.rn.f32x2 %1, p23, %11, %1;\n"
-      "}\n"
-      : "+l"(acc01), "+l"(acc23)
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "l"(dw), "l"(nm), "l"(da0), "l"(da1),
-        "r"(MAGIC_BITS));
-}
-
 // The same block split in two, so the MMAs of a whole stage can be issued
 // before the first of their results is folded into the chains: the MMA
 // (into the magic-initialized pairs) ...
@@ -239,160 +213,12 @@ __device__ __forceinline__ void q8_fold(f2& acc01, f2& acc23, f2 p01, f2 p23, f2
   acc23 = f2fma(f2fma(p23, dw, nm), da1, acc23);
 }
 
-template <int TM, int TN, int WGM, int WGN, int KB>
-struct GemmCfg {
-  static constexpr int BM = 16 * TM * WGM, BN = 8 * TN * WGN, BKB = KB * QK;
-  static constexpr int OFF_A = 0, OFF_W = OFF_A + BM * BKB, OFF_SA = OFF_W + BN * BKB,
-                       OFF_DW = OFF_SA + BM * KB * 8, OFF_NM = OFF_DW + KB * BN * 4,
-                       SST = (OFF_NM + KB * BN * 4 + 1023) / 1024 * 1024;  // stages 1 KB aligned: the swizzle
-                                                                          // XORs address bits 4-6
-  static constexpr int CPR = BKB / 16;  // 16-byte chunks per tile row
-};
-
-template <int TM, int TN, int WGM, int WGN, int KB, int STAGES, bool PIPE>
-__global__ void __launch_bounds__(256) k_q8_gemm(const int8_t* __restrict__ a, const float2* __restrict__ as, int M,
-                                                 const int8_t* __restrict__ wq, const float* __restrict__ dwT,
-                                                 const float* __restrict__ nmT, int N, int K, EpiArgs e) {
-  using C = GemmCfg<TM, TN, WGM, WGN, KB>;
-  constexpr int BM = C::BM, BN = C::BN, BKB = C::BKB, CPR = C::CPR;
-  static_assert(WGM * WGN == 8, "eight warps");
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
-  const int wm = warp / WGN, wn = warp % WGN;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int nb = K / QK, nkt = (nb + KB - 1) / KB;
-  const int arow = wm * 16 * TM, brow = wn * 8 * TN;
-  const uint32_t sbase = smem_u32(smem_raw);
-
-  // ---- the copies of one stage: A and W tiles (rows × CPR chunks), the
-  // (da, da) pairs (BM rows × KB/2 chunks) and dw, nm (KB × BN/4 chunks each).
-  constexpr int NA = BM * CPR, NW = BN * CPR, NS = BM * KB / 2, ND = KB * BN / 4;
-  auto load = [&](int kt, uint32_t st) {
-    const int kb0 = kt * KB;
-    for (int i = tid; i < NA + NW; i += 256) {
-      const bool isw = i >= NA;
-      const int j = isw ? i - NA : i, r = j / CPR, c = j % CPR;
-      const int swz = ((c & ~7) | ((c & 7) ^ (r & 7))) << 4;
-      const int gr = (isw ? n0 : m0) + r, kc = kb0 * QK + c * 16;
-      const bool v = gr < (isw ? N : M) && kc < K;
-      const int8_t* src = (isw ? wq : a) + (size_t)(v ? gr : 0) * K + (v ? kc : 0);
-      cp_async16(st + (isw ? C::OFF_W : C::OFF_A) + r * BKB + swz, src, v);
-    }
-    for (int i = tid; i < NS + 2 * ND; i += 256) {
-      if (i < NS) {
-        const int r = i / (KB / 2), q = i % (KB / 2), gr = m0 + r;
-        const bool v = gr < M && kb0 + 2 * q < nb;
-        cp_async16(st + C::OFF_SA + (r * KB + 2 * q) * 8, as + (size_t)(v ? gr : 0) * nb + (v ? kb0 + 2 * q : 0), v);
-      } else {
-        const int j = i - NS, which = j / ND, jj = j % ND, kb = jj / (BN / 4), c4 = (jj % (BN / 4)) * 4;
-        const bool v = kb0 + kb < nb && n0 + c4 < N;
-        const float* src = (which ? nmT : dwT) + (v ? (size_t)(kb0 + kb) * N + n0 + c4 : 0);
-        cp_async16(st + (which ? C::OFF_NM : C::OFF_DW) + (kb * BN + c4) * 4, src, v);
-      }
-    }
-  };
-
-  // ---- the warp's fragment and operand offsets within a stage.
-  const int mat = lane >> 3;
-  uint32_t aoff[TM], boff[TN];
-#pragma unroll
-  for (int i = 0; i < TM; i++) {
-    const int ra = arow + i * 16 + (lane & 7) + (mat & 1) * 8;
-    aoff[i] = C::OFF_A + ra * BKB + (((mat >> 1) ^ (ra & 7)) << 4);
-  }
-#pragma unroll
-  for (int j = 0; j < TN; j++) {
-    const int rb = brow + j * 8 + (lane & 7);
-    boff[j] = C::OFF_W + rb * BKB + ((((lane >> 3) & 1) ^ (rb & 7)) << 4);
-  }
-
-  // Each output's chain starts at its bias, or 0 (q8int.go:175-182).
-  // acc[i][j][0]: rows g of m-tile i, columns (c, c+1) of n-tile j; [1]: row g+8.
-  f2 acc[TM][TN][2];
-#pragma unroll
-  for (int j = 0; j < TN; j++) {
-    const int c0 = n0 + brow + j * 8 + 2 * t4;
-    const f2 b = f2make(e.bias && c0 < N ? e.bias[c0] : 0.f, e.bias && c0 + 1 < N ? e.bias[c0 + 1] : 0.f);
-#pragma unroll
-    for (int i = 0; i < TM; i++) acc[i][j][0] = acc[i][j][1] = b;
-  }
-
-#pragma unroll
-  for (int s = 0; s < STAGES - 1; s++) {
-    if (s < nkt) load(s, sbase + s * C::SST);
-    cp_commit();
-  }
-  int rs = 0, ws = STAGES - 1;  // read and write stage
-  for (int kt = 0; kt < nkt; kt++) {
-    cp_wait<STAGES - 2>();
-    __syncthreads();
-    if (kt + STAGES - 1 < nkt) load(kt + STAGES - 1, sbase + ws * C::SST);
-    cp_commit();
-    ws = ws + 1 == STAGES ? 0 : ws + 1;
-    const uint32_t cur = sbase + rs * C::SST;
-    rs = rs + 1 == STAGES ? 0 : rs + 1;
-    const int nblk = min(KB, nb - kt * KB);
-    if (PIPE && nblk == KB) {
-      // all MMAs of the stage first, then the chains: the tensor-core latency
-      // is paid once per stage, not once per block.
-      f2 p[KB][TM][TN][2];
-#pragma unroll
-      for (int kk = 0; kk < KB; kk++) {
-        const uint32_t kx = (uint32_t)((2 * kk) & ~7) << 4, kl = (uint32_t)((2 * kk) & 7) << 4;
-        uint32_t af[TM][4];
-#pragma unroll
-        for (int i = 0; i < TM; i++) ldsm_x4(af[i][0], af[i][1], af[i][2], af[i][3], (cur + aoff[i] + kx) ^ kl);
-#pragma unroll
-        for (int j = 0; j < TN; j++) {
-          uint32_t b0, b1;
-          ldsm_x2(b0, b1, (cur + boff[j] + kx) ^ kl);
-#pragma unroll
-          for (int i = 0; i < TM; i++) q8_mma(p[kk][i][j][0], p[kk][i][j][1], af[i], b0, b1);
-        }
-      }
-#pragma unroll
-      for (int kk = 0; kk < KB; kk++)
-#pragma unroll
-        for (int j = 0; j < TN; j++) {
-          const uint32_t so = cur + kk * BN * 4 + (brow + j * 8 + 2 * t4) * 4;
-          const f2 dw = lds64(so + C::OFF_DW), nm = lds64(so + C::OFF_NM);
-#pragma unroll
-          for (int i = 0; i < TM; i++) {
-            const uint32_t sa = cur + C::OFF_SA + ((arow + i * 16 + g) * KB + kk) * 8;
-            q8_fold(acc[i][j][0], acc[i][j][1], p[kk][i][j][0], p[kk][i][j][1], dw, nm, lds64(sa),
-                    lds64(sa + 8 * KB * 8));
-          }
-        }
-      continue;
-    }
-#pragma unroll
-    for (int kk = 0; kk < KB; kk++) {
-      if (kk < nblk) {
-        // chunk 2kk (k 0..15 of the block) and 2kk+1: the swizzle keeps the
-        // chunk's high bits, so the block's offset is added before it.
-        const uint32_t kx = (uint32_t)((2 * kk) & ~7) << 4;
-        const uint32_t kl = (uint32_t)((2 * kk) & 7) << 4;
-        uint32_t af[TM][4];
-#pragma unroll
-        for (int i = 0; i < TM; i++) ldsm_x4(af[i][0], af[i][1], af[i][2], af[i][3], (cur + aoff[i] + kx) ^ kl);
-#pragma unroll
-        for (int j = 0; j < TN; j++) {
-          uint32_t b0, b1;
-          ldsm_x2(b0, b1, (cur + boff[j] + kx) ^ kl);
-          const uint32_t so = cur + kk * BN * 4 + (brow + j * 8 + 2 * t4) * 4;
-          const f2 dw = lds64(so + C::OFF_DW), nm = lds64(so + C::OFF_NM);
-#pragma unroll
-          for (int i = 0; i < TM; i++) {
-            const uint32_t sa = cur + C::OFF_SA + ((arow + i * 16 + g) * KB + kk) * 8;
-            const f2 da0 = lds64(sa), da1 = lds64(sa + 8 * KB * 8);
-            q8_block(acc[i][j][0], acc[i][j][1], af[i], b0, b1, dw, nm, da0, da1);
-          }
-        }
-      }
-    }
-  }
-  cp_wait<0>();
-
+// The epilogue of both GEMM kernels: each thread's accumulators (rows g and
+// g+8 of its m-tiles, column pairs of its n-tiles) go where e says.
+template <int TM, int TN, int NWARPS>
+__device__ __forceinline__ void gemm_epilogue(f2 (&acc)[TM][TN][2], const EpiArgs& e, uint8_t* smem_raw, int m0,
+                                              int n0, int arow, int brow, int g, int t4, int warp, int lane, int M,
+                                              int N, int BM, int BN) {
   if (e.epi == EPI_GELU_Q8) {
     // A row's 32-column blocks span several warps: gather the tile in shared
     // memory, then one warp per (row, block) rounds its block to Q8_0.
@@ -409,7 +235,7 @@ __global__ void __launch_bounds__(256) k_q8_gemm(const int8_t* __restrict__ a, c
           tile[r * (BN + 1) + c + 1] = gelu_avx(f2hi(acc[i][j][h]));
         }
     __syncthreads();
-    for (int rb = warp; rb < BM * (BN / 32); rb += 8) {
+    for (int rb = warp; rb < BM * (BN / 32); rb += NWARPS) {
       const int r = rb / (BN / 32), cb = rb % (BN / 32), row = m0 + r;
       float sc;
       const int8_t qv = quant_lane(tile[r * (BN + 1) + cb * 32 + lane], &sc);
@@ -443,29 +269,193 @@ __global__ void __launch_bounds__(256) k_q8_gemm(const int8_t* __restrict__ a, c
       }
 }
 
-template <int TM, int TN, int WGM, int WGN, int KB, int STAGES, bool PIPE = true>
-struct Gemm {
-  using C = GemmCfg<TM, TN, WGM, WGN, KB>;
+// ------------------------------------------------ GEMM, lean inner loop --
+//
+// k_q8_gemm2: a stage is four Q8_0 blocks (128 bytes of K). Every thread's async-copy
+// sources and destinations are computed once and only advance per stage;
+// the weight scales come as {dw[n], dw[n+1], nm[n], nm[n+1]} quads (one
+// 16-byte read per column pair, DQ8::dwnm); B fragments come two column
+// tiles per ldmatrix.x4. Per block a warp issues its TM·TN MMAs, then folds
+// them (four packed FMAs each).
+template <int TM, int TN, int WGM, int WGN>
+struct Cfg2 {
+  static constexpr int BM = 16 * TM * WGM, BN = 8 * TN * WGN, NT = 32 * WGM * WGN, KB = 4;
+  static constexpr int OFF_A = 0, OFF_W = BM * 128, OFF_SA = OFF_W + BN * 128, OFF_DN = OFF_SA + BM * KB * 8,
+                       SST = (OFF_DN + KB * BN * 8 + 1023) / 1024 * 1024;
+  static constexpr int CA = BM * 8, CW = BN * 8, CS = BM * 2, CD = KB * BN / 2;  // 16-byte chunks per stage
+  static constexpr int PA = (CA + NT - 1) / NT, PW = (CW + NT - 1) / NT, PS = (CS + NT - 1) / NT,
+                       PD = (CD + NT - 1) / NT;
+};
+
+template <int TM, int TN, int WGM, int WGN, int STAGES>
+__global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __restrict__ a,
+                                                            const float2* __restrict__ as, int M,
+                                                            const int8_t* __restrict__ wq,
+                                                            const float4* __restrict__ dwnm, int N, int K, EpiArgs e) {
+  using C = Cfg2<TM, TN, WGM, WGN>;
+  constexpr int BM = C::BM, BN = C::BN, NT = C::NT;
+  static_assert(TN % 2 == 0, "B fragments two column tiles at a time");
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const int wm = warp / WGN, wn = warp % WGN;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int nb = K / QK, nkt = nb / 4, np2 = (N + 1) / 2;
+  const int arow = wm * 16 * TM, brow = wn * 8 * TN;
+  const uint32_t sbase = smem_u32(smem_raw);
+
+  // ---- this thread's copies of a stage: sources (advance per stage) and
+  // destinations within a stage
+  const int8_t* srcA[C::PA];
+  uint32_t dstA[C::PA];
+  bool okA[C::PA];
+#pragma unroll
+  for (int u = 0; u < C::PA; u++) {
+    const int i = tid + u * NT, r = i >> 3, c = i & 7;
+    okA[u] = i < C::CA && m0 + r < M;
+    srcA[u] = a + (size_t)(okA[u] ? m0 + r : 0) * K + c * 16;
+    dstA[u] = C::OFF_A + r * 128 + ((c ^ (r & 7)) << 4);
+  }
+  const int8_t* srcW[C::PW];
+  uint32_t dstW[C::PW];
+  bool okW[C::PW];
+#pragma unroll
+  for (int u = 0; u < C::PW; u++) {
+    const int i = tid + u * NT, r = i >> 3, c = i & 7;
+    okW[u] = i < C::CW && n0 + r < N;
+    srcW[u] = wq + (size_t)(okW[u] ? n0 + r : 0) * K + c * 16;
+    dstW[u] = C::OFF_W + r * 128 + ((c ^ (r & 7)) << 4);
+  }
+  const float2* srcS[C::PS];
+  uint32_t dstS[C::PS];
+  bool okS[C::PS];
+#pragma unroll
+  for (int u = 0; u < C::PS; u++) {
+    const int i = tid + u * NT, r = i >> 1, h = i & 1;
+    okS[u] = i < C::CS && m0 + r < M;
+    srcS[u] = as + (size_t)(okS[u] ? m0 + r : 0) * nb + 2 * h;
+    dstS[u] = C::OFF_SA + r * 32 + h * 16;
+  }
+  const float4* srcD[C::PD];
+  uint32_t dstD[C::PD];
+  bool okD[C::PD];
+#pragma unroll
+  for (int u = 0; u < C::PD; u++) {
+    const int i = tid + u * NT, kb = i / (BN / 2), p = i % (BN / 2);
+    okD[u] = i < C::CD && n0 + 2 * p < N;
+    srcD[u] = dwnm + (size_t)kb * np2 + (okD[u] ? n0 / 2 + p : 0);
+    dstD[u] = C::OFF_DN + (kb * (BN / 2) + p) * 16;
+  }
+  auto load = [&](int kt, uint32_t st) {
+#pragma unroll
+    for (int u = 0; u < C::PA; u++)
+      if (tid + u * NT < C::CA) cp_async16(st + dstA[u], srcA[u] + kt * 128, okA[u]);
+#pragma unroll
+    for (int u = 0; u < C::PW; u++)
+      if (tid + u * NT < C::CW) cp_async16(st + dstW[u], srcW[u] + kt * 128, okW[u]);
+#pragma unroll
+    for (int u = 0; u < C::PS; u++)
+      if (tid + u * NT < C::CS) cp_async16(st + dstS[u], srcS[u] + kt * 4, okS[u]);
+#pragma unroll
+    for (int u = 0; u < C::PD; u++)
+      if (tid + u * NT < C::CD) cp_async16(st + dstD[u], srcD[u] + (size_t)kt * 4 * np2, okD[u]);
+  };
+
+  // ---- fragment offsets within a stage
+  const int mat = lane >> 3;
+  uint32_t aoff[TM], boff[TN / 2];
+#pragma unroll
+  for (int i = 0; i < TM; i++) {
+    const int ra = arow + i * 16 + (lane & 7) + (mat & 1) * 8;
+    aoff[i] = C::OFF_A + ra * 128 + (((mat >> 1) ^ (ra & 7)) << 4);
+  }
+#pragma unroll
+  for (int j = 0; j < TN / 2; j++) {
+    const int rb = brow + j * 16 + (lane & 7) + (mat >> 1) * 8;
+    boff[j] = C::OFF_W + rb * 128 + (((mat & 1) ^ (rb & 7)) << 4);
+  }
+  uint32_t soff[TM], doff[TN];
+#pragma unroll
+  for (int i = 0; i < TM; i++) soff[i] = C::OFF_SA + (arow + i * 16 + g) * 32;
+#pragma unroll
+  for (int j = 0; j < TN; j++) doff[j] = C::OFF_DN + ((brow + j * 8) / 2 + t4) * 16;
+
+  // Each output's chain starts at its bias, or 0 (q8int.go:175-182).
+  f2 acc[TM][TN][2];
+#pragma unroll
+  for (int j = 0; j < TN; j++) {
+    const int c0 = n0 + brow + j * 8 + 2 * t4;
+    const f2 b = f2make(e.bias && c0 < N ? e.bias[c0] : 0.f, e.bias && c0 + 1 < N ? e.bias[c0 + 1] : 0.f);
+#pragma unroll
+    for (int i = 0; i < TM; i++) acc[i][j][0] = acc[i][j][1] = b;
+  }
+
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; s++) {
+    if (s < nkt) load(s, sbase + s * C::SST);
+    cp_commit();
+  }
+  int rs = 0, ws = STAGES - 1;
+  for (int kt = 0; kt < nkt; kt++) {
+    cp_wait<STAGES - 2>();
+    __syncthreads();
+    if (kt + STAGES - 1 < nkt) load(kt + STAGES - 1, sbase + ws * C::SST);
+    cp_commit();
+    ws = ws + 1 == STAGES ? 0 : ws + 1;
+    const uint32_t cur = sbase + rs * C::SST;
+    rs = rs + 1 == STAGES ? 0 : rs + 1;
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      const uint32_t kl = uint32_t(2 * kk) << 4;  // the block's first chunk (the swizzle keeps bit 0)
+      uint32_t af[TM][4], bf[TN][2];
+#pragma unroll
+      for (int i = 0; i < TM; i++) ldsm_x4(af[i][0], af[i][1], af[i][2], af[i][3], (cur + aoff[i]) ^ kl);
+#pragma unroll
+      for (int j = 0; j < TN / 2; j++)
+        ldsm_x4(bf[2 * j][0], bf[2 * j][1], bf[2 * j + 1][0], bf[2 * j + 1][1], (cur + boff[j]) ^ kl);
+      f2 p[TM][TN][2];
+#pragma unroll
+      for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) q8_mma(p[i][j][0], p[i][j][1], af[i], bf[j][0], bf[j][1]);
+#pragma unroll
+      for (int j = 0; j < TN; j++) {
+        f2 dw, nm;
+        asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];\n" : "=l"(dw), "=l"(nm) : "r"(cur + doff[j] + kk * (BN / 2) * 16));
+#pragma unroll
+        for (int i = 0; i < TM; i++) {
+          const uint32_t sa = cur + soff[i] + kk * 8;
+          q8_fold(acc[i][j][0], acc[i][j][1], p[i][j][0], p[i][j][1], dw, nm, lds64(sa), lds64(sa + 8 * 32));
+        }
+      }
+    }
+  }
+  cp_wait<0>();
+  gemm_epilogue<TM, TN, WGM * WGN>(acc, e, smem_raw, m0, n0, arow, brow, g, t4, warp, lane, M, N, BM, BN);
+}
+
+template <int TM, int TN, int WGM, int WGN, int STAGES>
+struct Gemm2 {
+  using C = Cfg2<TM, TN, WGM, WGN>;
   static constexpr size_t smem() {
     const size_t s = size_t(C::SST) * STAGES, t = size_t(C::BM) * (C::BN + 1) * 4;
     return s > t ? s : t;
   }
   static void init() {
-    cudaFuncSetAttribute(k_q8_gemm<TM, TN, WGM, WGN, KB, STAGES, PIPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_q8_gemm2<TM, TN, WGM, WGN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          int(smem()));
   }
   static void launch(const int8_t* a, const float2* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st) {
     dim3 grid((w.rows + C::BN - 1) / C::BN, (M + C::BM - 1) / C::BM);
-    k_q8_gemm<TM, TN, WGM, WGN, KB, STAGES, PIPE><<<grid, 256, smem(), st>>>(a, as, M, w.q, w.dwT, w.nmT, w.rows,
-                                                                             w.cols, e);
+    k_q8_gemm2<TM, TN, WGM, WGN, STAGES><<<grid, C::NT, smem(), st>>>(a, as, M, w.q, w.dwnm, w.rows, w.cols, e);
   }
 };
 
 // Tile shapes per product shape, the fastest of those timed at M = 256 on
-// B200 (qkv 16.6 µs, attn_out 10.4, ff1 21.4, ff2 26.8 per product).
-using GemmNarrow = Gemm<1, 1, 2, 4, 4, 4>;  // N ≤ 2048, K ≤ 2048
-using GemmWide = Gemm<2, 2, 2, 4, 4, 4>;    // N > 2048
-using GemmDeep = Gemm<1, 2, 2, 4, 8, 4>;    // K > 2048
+// B200, every one bit-identical to the others: 64×32 CTA tiles of four 32×16
+// warps for most (qkv 11.3 µs, attn_out 7.6, ff2 18.5 per product), 64×64
+// of four 32×32 warps for the widest (ff1 12.4).
+using GemmMid = Gemm2<2, 2, 2, 2, 4>;
+using GemmWide = Gemm2<2, 4, 2, 2, 4>;  // N > 3072
 
 }  // namespace
 
@@ -485,19 +475,16 @@ void launch_q8_product(const int8_t* a, const float2* as, int M, const DQ8& w, c
       k_q8_gemv<8><<<grid, 256, sm, st>>>(a, as, M, w.q, w.d, N, K, e);
     return;
   }
-  if (K > 2048)
-    GemmDeep::launch(a, as, M, w, e, st);
-  else if (N > 2048)
+  if (N > 3072)
     GemmWide::launch(a, as, M, w, e, st);
   else
-    GemmNarrow::launch(a, as, M, w, e, st);
+    GemmMid::launch(a, as, M, w, e, st);
 }
 
 // Raises the kernels' dynamic shared memory limits once per device.
 void q8_kernels_init() {
-  GemmNarrow::init();
+  GemmMid::init();
   GemmWide::init();
-  GemmDeep::init();
   const int gv = 8 * 4096 + 8 * 128 * 4 + 8 * 32 * 4;
   cudaFuncSetAttribute(k_q8_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gv);
   cudaFuncSetAttribute(k_q8_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, gv);

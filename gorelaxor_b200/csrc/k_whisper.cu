@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(256) k_wcross(WRows r, const float* q, const f
   const int lane = threadIdx.x & 31, l16 = threadIdx.x & 15, grp = threadIdx.x >> 4;
   const int ctx4 = ctx & ~3;
   float mx = NINF;
+#pragma unroll 4
   for (int j0 = 0; j0 < ctx4; j0 += 16) {
     const int j = j0 + grp;
     float a = 0.f;
@@ -233,6 +234,7 @@ __global__ void __launch_bounds__(256) k_wcross(WRows r, const float* q, const f
   // o[d] for d = grp + 16i: the 16 lanes chain over ctx&~15 in steps of 16
   const int cf = ctx & ~15;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
   for (int c = 0; c < cf; c += 16) {
     const float p = sc[c + l16];
 #pragma unroll
@@ -270,21 +272,21 @@ __global__ void __launch_bounds__(256) k_wcross(WRows r, const float* q, const f
 // threads of 4 × 4 outputs, 32-deep slices staged in shared memory.
 constexpr int MM_T = 64, MM_S = 32, MM_LD = MM_T + 4;
 
-__global__ void __launch_bounds__(256) k_wmm(const float* a, int lda, size_t a_stride, int m, WMat w,
-                                             const float* bias, int mode, float* c, int ldc, int nh, float tsc) {
+__global__ void __launch_bounds__(256) k_wmm(WmmArgs p) {
   __shared__ __align__(16) float As[MM_S][MM_LD];
   __shared__ __align__(16) float Bs[MM_S][MM_LD];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int i0 = blockIdx.y * MM_T, j0 = blockIdx.x * MM_T, str = blockIdx.z;
-  const int n = w.rows, k = w.cols;
-  const float* A = a + str * a_stride;
+  const WMat& w = p.w;
+  const int n = w.rows, k = w.cols, m = p.m, lda = p.lda;
+  const float* A = p.a + str * p.a_zs;
   float cv[4][4], ch[4][4];
 #pragma unroll
   for (int u = 0; u < 4; u++)
 #pragma unroll
     for (int v = 0; v < 4; v++) {
       const int j = j0 + tx * 4 + v;
-      cv[u][v] = bias && j < n ? bias[j] : 0.f;
+      cv[u][v] = p.bias && j < n ? p.bias[j] : 0.f;
     }
   const int sr = tid >> 2, sk8 = (tid & 3) * 8;  // staging: row/col sr, 8 values from sk8
   for (int p0 = 0; p0 < k; p0 += 256) {
@@ -334,22 +336,37 @@ __global__ void __launch_bounds__(256) k_wmm(const float* a, int lda, size_t a_s
 #pragma unroll
       for (int v = 0; v < 4; v++) cv[u][v] = __fadd_rn(cv[u][v], ch[u][v]);
   }
-  const int hd = n / max(nh, 1);
+  const int hd = n / max(p.nh, 1);
 #pragma unroll
   for (int u = 0; u < 4; u++)
 #pragma unroll
     for (int v = 0; v < 4; v++) {
       const int i = i0 + ty * 4 + u, j = j0 + tx * 4 + v;
       if (i >= m || j >= n) continue;
-      if (mode == 0) {
-        c[(size_t)str * m * ldc + (size_t)i * ldc + j] = cv[u][v];
-      } else {
-        const int hh = j / hd, d = j % hd;
-        const size_t base = ((size_t)str * nh + hh) * (size_t)m * hd;
-        if (mode == 1)
-          c[base + (size_t)i * hd + d] = __fmul_rn(cv[u][v], tsc);
-        else
-          c[base + (size_t)d * m + i] = cv[u][v];
+      const float val = cv[u][v];
+      float* cz = p.c + str * p.c_zs;
+      switch (p.mode) {
+        case WM_CROSSK: {
+          const int hh = j / hd, d = j % hd;
+          p.c[((size_t)str * p.nh + hh) * (size_t)m * hd + (size_t)i * hd + d] = __fmul_rn(val, p.tsc);
+          break;
+        }
+        case WM_CROSSV: {
+          const int hh = j / hd, d = j % hd;
+          p.c[((size_t)str * p.nh + hh) * (size_t)m * hd + (size_t)d * m + i] = val;
+          break;
+        }
+        case WM_RESID:
+          cz[(size_t)i * p.ldc + j] = __fadd_rn(cz[(size_t)i * p.ldc + j], val);
+          break;
+        case WM_GELU:
+          cz[(size_t)i * p.ldc + j] = gelu_avx(val);
+          break;
+        case WM_ROWPOS:
+          p.c[(size_t)p.dst_row[i * p.rs_i + str] * p.ldc + j] = val;
+          break;
+        default:
+          cz[(size_t)i * p.ldc + j] = val;
       }
     }
 }
@@ -436,13 +453,18 @@ __device__ VI block_vi_max(VI x, VI* sh) {
 // probability must beat every earlier index's by a factor 1 − 2^-20 (the
 // division by the sum can then not tie them). A row that misses a margin is
 // recomputed by one thread in the reference's order.
-__global__ void __launch_bounds__(512) k_wproc(WRows r, float* logits, WVocabDev v, WSample* state, int* out,
-                                               const int* step, int* next_tok) {
+//
+// One pass takes e_i = expf(lg_i − max) for the whole row into scratch;
+// without the timestamp rule's masking softmaxInf's terms are those same
+// e_i (and so is its sum), so only the timestamps are taken again.
+__global__ void __launch_bounds__(1024) k_wproc(WRows r, float* logits, float* scratch, WVocabDev v, WSample* state,
+                                                int* out, const int* step, int* next_tok) {
   __shared__ float shf[40];
   __shared__ VI shv[32];
   __shared__ int amb;
   const int row = blockIdx.x, s = r.row_stream[row], n = v.n, beg = v.beg;
   float* lg = logits + (size_t)row * n;
+  float* e = scratch + (size_t)row * n;
   const WSample q = state[s];
   const bool initial = q.nt == 0;
   // ---- the rules
@@ -461,18 +483,14 @@ __global__ void __launch_bounds__(512) k_wproc(WRows r, float* logits, WVocabDev
   __syncthreads();
   const bool last = q.nt > 0 && q.last >= beg, penult = q.nt < 2 || q.penult >= beg;
   const int tid0 = int(round(1.0 / (30.0 / double(v.audio_ctx))));
+  float mx = NINF, mts = NINF, mtx = NINF;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     bool m = false;
     if (last) m = penult ? i >= beg : i < v.eot;
     if (initial && i >= beg + tid0 + 1) m = true;
     if (q.has_ts && i >= beg && i < beg + q.seek_delta / 2) m = true;
-    if (m) lg[i] = NINF;
-  }
-  __syncthreads();
-  // ---- logSoftmax and the timestamp rule
-  float mx = NINF, mts = NINF, mtx = NINF;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float x = lg[i];
+    float x = lg[i];
+    if (m) lg[i] = x = NINF;
     mx = fmaxf(mx, x);
     if (i >= beg) mts = fmaxf(mts, x);
     else mtx = fmaxf(mtx, x);
@@ -480,12 +498,18 @@ __global__ void __launch_bounds__(512) k_wproc(WRows r, float* logits, WVocabDev
   mx = block_max(mx, shf);
   mts = block_max(mts, shf);
   mtx = block_max(mtx, shf);
+  // ---- logSoftmax's sum, with e_i kept
   float s1 = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
-    if (lg[i] > NINF) s1 = __fadd_rn(s1, expf_go(__fsub_rn(lg[i], mx)));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float x = lg[i];
+    const float ei = x > NINF ? expf_go(__fsub_rn(x, mx)) : 0.f;
+    e[i] = ei;
+    s1 = __fadd_rn(s1, ei);
+  }
   s1 = block_sum(s1, shf);
   const float ls = __fadd_rn(float(log(double(s1))), mx);
-  const float ts_max = mts > NINF ? __fsub_rn(mts, ls) : NINF;  // max of logprobs[beg:]
+  // ---- the timestamp rule
+  const float ts_max = mts > NINF ? __fsub_rn(mts, ls) : NINF;  // the largest of logprobs[beg:]
   bool mask_text = false;
   if (ts_max > NINF) {
     float sum = 0.f;
@@ -497,36 +521,43 @@ __global__ void __launch_bounds__(512) k_wproc(WRows r, float* logits, WVocabDev
     mask_text = ts_lp > text_max;
     if (text_max > NINF && fabsf(ts_lp - text_max) <= 2e-4f * (1.f + fabsf(text_max))) amb = 1;
   }
-  // ---- softmaxInf and the argmaxes, on e_i = expf(lg'_i − max) (exact);
-  // only the division by their sum is left out
-  const float mx2 = mask_text ? mts : mx;
-  VI best{-1.f, n}, bts{-1.f, n};
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float x = (mask_text && i < beg) ? NINF : lg[i];
-    const float e = x > NINF ? expf_go(__fsub_rn(x, mx2)) : 0.f;
-    best = vi_max(best, VI{e, i});
-    if (i >= beg) bts = vi_max(bts, VI{e, i});
+  // ---- softmaxInf's terms: the same e_i, or, with text masked, the
+  // timestamps' again against their own maximum
+  const int lo = mask_text ? beg : 0;
+  float s2 = s1;
+  if (mask_text) {
+    s2 = 0.f;
+    for (int i = beg + threadIdx.x; i < n; i += blockDim.x) {
+      const float x = lg[i];
+      const float ei = x > NINF ? expf_go(__fsub_rn(x, mts)) : 0.f;
+      e[i] = ei;
+      s2 = __fadd_rn(s2, ei);
+    }
+    s2 = block_sum(s2, shf);
   }
+  __syncthreads();
+  VI best{-1.f, n}, bts{-1.f, n};
+  for (int i = lo + threadIdx.x; i < n; i += blockDim.x) {
+    const float ei = e[i];
+    best = vi_max(best, VI{ei, i});
+    if (i >= beg) bts = vi_max(bts, VI{ei, i});
+  }
+  if (mask_text && lo > 0 && best.v < 0.f) best = VI{-1.f, n};
   best = block_vi_max(best, shv);
   bts = block_vi_max(bts, shv);
+  // masked text has probability 0: it only wins if nothing else is positive
+  if (mask_text && !(best.v > 0.f)) best = VI{0.f, 0};
   // the largest e before each winner that is smaller than it
   float near = 0.f, near_t = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float x = (mask_text && i < beg) ? NINF : lg[i];
-    const float e = x > NINF ? expf_go(__fsub_rn(x, mx2)) : 0.f;
-    if (i < best.i && e < best.v) near = fmaxf(near, e);
-    if (i >= beg && i < bts.i && e < bts.v) near_t = fmaxf(near_t, e);
+  for (int i = lo + threadIdx.x; i < n; i += blockDim.x) {
+    const float ei = e[i];
+    if (i < best.i && ei < best.v) near = fmaxf(near, ei);
+    if (i >= beg && i < bts.i && ei < bts.v) near_t = fmaxf(near_t, ei);
   }
   near = block_max(near, shf);
   near_t = block_max(near_t, shf);
   const float margin = 1.f - 9.5367431640625e-07f;  // 1 − 2^-20
   if ((best.v > 0.f && near >= best.v * margin) || (bts.v > 0.f && near_t >= bts.v * margin)) amb = 1;
-  float s2 = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float x = (mask_text && i < beg) ? NINF : lg[i];
-    if (x > NINF) s2 = __fadd_rn(s2, expf_go(__fsub_rn(x, mx2)));
-  }
-  s2 = block_sum(s2, shf);
   __syncthreads();
   if (threadIdx.x == 0) {
     int o[4];
@@ -601,15 +632,14 @@ void launch_wcross(const WRows& r, const float* q, const float* ck, const float*
   k_wcross<<<dim3(r.rows, r.nh), 256, (r.audio_ctx + 64) * 4, st>>>(r, q, ck, cvt, att);
 }
 
-void launch_wmm(const float* a, int lda, size_t a_stream_stride, int m, const WMat& w, const float* bias, int mode,
-                float* c, int ldc, int nh, float tsc, int streams, cudaStream_t st) {
-  dim3 grid((w.rows + MM_T - 1) / MM_T, (m + MM_T - 1) / MM_T, streams);
-  k_wmm<<<grid, 256, 0, st>>>(a, lda, a_stream_stride, m, w, bias, mode, c, ldc, nh, tsc);
+void launch_wmm(const WmmArgs& a, int groups, cudaStream_t st) {
+  dim3 grid((a.w.rows + MM_T - 1) / MM_T, (a.m + MM_T - 1) / MM_T, groups);
+  k_wmm<<<grid, 256, 0, st>>>(a);
 }
 
-void launch_wproc(const WRows& r, float* logits, const WVocabDev& v, WSample* state, int* out, const int* step,
-                  int* next_tok, cudaStream_t st) {
-  k_wproc<<<r.rows, 512, 0, st>>>(r, logits, v, state, out, step, next_tok);
+void launch_wproc(const WRows& r, float* logits, float* scratch, const WVocabDev& v, WSample* state, int* out,
+                  const int* step, int* next_tok, cudaStream_t st) {
+  k_wproc<<<r.rows, 1024, 0, st>>>(r, logits, scratch, v, state, out, step, next_tok);
 }
 
 void launch_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int advance, int* step, cudaStream_t st) {

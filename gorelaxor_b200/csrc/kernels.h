@@ -11,10 +11,11 @@ namespace grx {
 struct DQ8 {
   const int8_t* q = nullptr;
   const uint16_t* d = nullptr;
-  // For the tensor-core product: per block dw and −1.5·2^23·dw as float32
-  // (both exact; dw is a half), block-major: [cols/32][rows] each.
-  const float* dwT = nullptr;
-  const float* nmT = nullptr;
+  // For the tensor-core product: per block dw and nm = −1.5·2^23·dw as
+  // float32 (both exact; dw is a half), as quads per block and column pair
+  // {dw[n], dw[n+1], nm[n], nm[n+1]} for n = 2p, [cols/32][(rows+1)/2] (the
+  // second of an odd last row is 0).
+  const float4* dwnm = nullptr;
   int rows = 0, cols = 0;
 };
 
@@ -49,15 +50,18 @@ struct EpiArgs {
 // captured frame graph serves every frame: the frame's slice of each array
 // is base + frame·stride, and the last kernel of a frame moves `frame` on.
 struct FrameIO {
-  const float* noise;  // [frames][M][ldim]
-  float* latent;       // [frames][M][ldim] (may be NULL)
-  float* scaled;       // [frames][M][ldim] (may be NULL)
-  float* eos;          // [frames][M] (may be NULL)
+  const float* noise;  // [frames][rows][ldim]
+  float* latent;       // [frames][rows][ldim] (may be NULL)
+  float* scaled;       // [frames][rows][ldim] (may be NULL)
+  float* eos;          // [frames][rows] (may be NULL)
   int frame;
   // Optional instrumentation: per frame and layer, the attention kernel's
   // first CTA start and last CTA end (%globaltimer, ns) [frames][layers][2];
   // slots must start at {UINT64_MAX, 0}.
   unsigned long long* attn_ts;
+  int rows;  // rows per frame in the arrays above (every stream of the job)
+  int row0;  // this stream set's first row
+  int part, parts;  // attn_ts is [frames][layers][parts][2]
 };
 
 // LayerNorm modes.
@@ -247,17 +251,36 @@ void launch_wself(const WRows& r, const float* q, const float* sk, const float* 
 // Cross-attention over the stream's pre-scaled keys [nh][ctx][hd] and
 // transposed values [nh][hd][ctx].
 void launch_wcross(const WRows& r, const float* q, const float* ck, const float* cvt, float* att, cudaStream_t st);
-// The packed-order product (whisper/gemm.go:124-209, rows < m/6·6):
-// C = A·Wᵀ + bias. mode 0 stores C [m][ldc]; 1 writes keys ·tsc into
-// [stream][nh][ctx][hd]; 2 writes values into [stream][nh][hd][ctx] (cross
-// K/V prep, A = encoder output of stream blockIdx.z, rows = ctx).
-void launch_wmm(const float* a, int lda, size_t a_stream_stride, int m, const WMat& w, const float* bias, int mode,
-                float* c, int ldc, int nh, float tsc, int streams, cudaStream_t st);
+// The packed-order product (whisper/gemm.go:124-209, rows < m/6·6) for
+// `groups` independent matrices (grid z): C = A·Wᵀ + bias, row i of group z
+// at a + z·a_zs + i·lda. Epilogues (mode): WM_STORE / WM_RESID (+=) /
+// WM_GELU (geluAVX) at c + z·c_zs + i·ldc; WM_ROWPOS at c + dst_row[i·rs_i +
+// z]·ldc; WM_CROSSK keys ·tsc into [z][nh][m][hd] and WM_CROSSV values into
+// [z][nh][hd][m] (the cross K/V prep, A = encoder output of stream z).
+enum WmmMode { WM_STORE = 0, WM_CROSSK = 1, WM_CROSSV = 2, WM_RESID = 3, WM_GELU = 4, WM_ROWPOS = 5 };
+struct WmmArgs {
+  const float* a = nullptr;
+  int lda = 0;
+  size_t a_zs = 0;
+  int m = 0;
+  WMat w;
+  const float* bias = nullptr;
+  int mode = WM_STORE;
+  float* c = nullptr;
+  int ldc = 0;
+  size_t c_zs = 0;
+  int nh = 1;
+  float tsc = 1.f;
+  const int* dst_row = nullptr;
+  int rs_i = 0;
+};
+void launch_wmm(const WmmArgs& a, int groups, cudaStream_t st);
 // process + sample at temperature 0 for every row (transcribe.go:370-494):
-// logits [rows][vocab] are masked in place; writes out[*step][rows][4] (id,
-// tid, p, plog), the next token and the stream's sampling state.
-void launch_wproc(const WRows& r, float* logits, const WVocabDev& v, WSample* state, int* out, const int* step,
-                  int* next_tok, cudaStream_t st);
+// logits [rows][vocab] are masked in place (scratch [rows][vocab]); writes
+// out[*step][rows][4] (id, tid, p, plog), the next token and the stream's
+// sampling state.
+void launch_wproc(const WRows& r, float* logits, float* scratch, const WVocabDev& v, WSample* state, int* out,
+                  const int* step, int* next_tok, cudaStream_t st);
 // row_pos += advance; dst_row = r·text_ctx + row_pos; *step += 1 when step is given.
 void launch_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int advance, int* step, cudaStream_t st);
 void whisper_kernels_init();

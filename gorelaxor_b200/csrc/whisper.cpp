@@ -168,6 +168,10 @@ struct grx_whisper_batch {
   int* run_out = nullptr;  // [steps][n][4] of the current run (device)
   int run_cap = 0;
   int pos = 0;  // positions every stream holds (they all move together)
+  // prompt rows [token][stream]: capacity in rows and the buffers
+  int p_cap = 0;
+  float *px = nullptr, *pcur = nullptr, *pq = nullptr, *patt = nullptr, *pff = nullptr;
+  int *p_stream = nullptr, *p_pos = nullptr, *p_tok = nullptr, *p_dst = nullptr;
   cudaGraphExec_t g_decode = nullptr, g_step = nullptr;
   int per_decode = 0;
   int64_t launches = 0;
@@ -242,7 +246,7 @@ int capture(grx_whisper_batch* b, bool with_sample, cudaGraphExec_t* out) {
   CK(cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal));
   int k = 0;
   if (with_sample) {
-    launch_wproc(b->rows, b->logits, b->m->voc, b->state, b->run_out, b->step, b->row_tok, b->st), k++;
+    launch_wproc(b->rows, b->logits, b->scratch, b->m->voc, b->state, b->run_out, b->step, b->row_tok, b->st), k++;
     launch_wtick(b->n, b->row_pos, b->dst_row, b->m->n_text_ctx, 0, b->step, b->st), k++;  // step += 1 only
   }
   k += enqueue_decode(b);
@@ -569,10 +573,22 @@ int set_audio(grx_whisper_batch* b, const float* d_enc) {
   const float tsc = float(1 / std::sqrt(double(st / m->n_head)));
   for (size_t l = 0; l < m->layers.size(); l++) {
     const WLayerDev& L = m->layers[l];
-    launch_wmm(d_enc, st, size_t(ctx) * st, ctx, L.xk, nullptr, 1, b->ck + l * layer_stride_cross(m, n), 0,
-               m->n_head, tsc, n, b->st);
-    launch_wmm(d_enc, st, size_t(ctx) * st, ctx, L.xv, L.xvb, 2, b->cvt + l * layer_stride_cross(m, n), 0,
-               m->n_head, 0.f, n, b->st);
+    WmmArgs a;
+    a.a = d_enc;
+    a.lda = st;
+    a.a_zs = size_t(ctx) * st;
+    a.m = ctx;
+    a.w = L.xk;
+    a.mode = WM_CROSSK;
+    a.c = b->ck + l * layer_stride_cross(m, n);
+    a.nh = m->n_head;
+    a.tsc = tsc;
+    launch_wmm(a, n, b->st);
+    a.w = L.xv;
+    a.bias = L.xvb;
+    a.mode = WM_CROSSV;
+    a.c = b->cvt + l * layer_stride_cross(m, n);
+    launch_wmm(a, n, b->st);
     b->launches += 2;
   }
   CK(cudaMemsetAsync(b->row_pos, 0, sizeof(int) * size_t(n), b->st));
@@ -600,6 +616,113 @@ int ensure_run_out(grx_whisper_batch* b, int steps) {
   return GRX_OK;
 }
 
+// One product of the prompt rows ([token][stream] order, np tokens per
+// stream): whisper/gemm.go's matmul takes the packed kernel for each
+// stream's first np/6·6 rows when np ≥ 6 and gemv for the rest.
+void prompt_product(grx_whisper_batch* b, int np, const WMat& w, const float* a, int lda, const float* bias, int epi,
+                    float* c, int ldc) {
+  const int n = b->n, mfull = np >= 6 ? np / 6 * 6 : 0;
+  if (mfull > 0) {
+    WmmArgs p;
+    p.a = a;
+    p.lda = n * lda;  // consecutive tokens of one stream are n rows apart
+    p.a_zs = size_t(lda);
+    p.m = mfull;
+    p.w = w;
+    p.bias = bias;
+    p.mode = epi == FE_RESID ? WM_RESID : epi == FE_GELU ? WM_GELU : epi == FE_ROWPOS ? WM_ROWPOS : WM_STORE;
+    p.c = c;
+    p.ldc = epi == FE_ROWPOS ? ldc : n * ldc;
+    p.c_zs = size_t(ldc);
+    p.dst_row = b->p_dst;
+    p.rs_i = n;
+    launch_wmm(p, n, b->st);
+    b->launches++;
+  }
+  if (mfull < np) {
+    const size_t r0 = size_t(mfull) * n;
+    flin_w(w, a + r0 * lda, lda, (np - mfull) * n, bias, epi, epi == FE_ROWPOS ? c : c + r0 * ldc, ldc,
+           epi == FE_ROWPOS ? b->p_dst + r0 : nullptr, b->st);
+    b->launches++;
+  }
+}
+
+// decode (decoder.go:33-140) of np prompt tokens per stream: all rows at
+// once, causal self-attention per row; the no-speech probability from the
+// logits of row sot_at, the next sample's logits from the last row.
+int prefill(grx_whisper_batch* b, const int* prompt, int np, int sot_at) {
+  const grx_whisper* m = b->m;
+  const int n = b->n, st = m->n_state, R = np * n;
+  int rc = 0;
+  if (R > b->p_cap) {
+    b->px = b->ar.alloc<float>(size_t(R) * st, &rc);
+    b->pcur = b->ar.alloc<float>(size_t(R) * st, &rc);
+    b->pq = b->ar.alloc<float>(size_t(R) * st, &rc);
+    b->patt = b->ar.alloc<float>(size_t(R) * st, &rc);
+    b->pff = b->ar.alloc<float>(size_t(R) * 4 * st, &rc);
+    b->p_stream = b->ar.alloc<int>(R, &rc);
+    b->p_pos = b->ar.alloc<int>(R, &rc);
+    b->p_tok = b->ar.alloc<int>(R, &rc);
+    b->p_dst = b->ar.alloc<int>(R, &rc);
+    if (rc) return rc;
+    b->p_cap = R;
+  }
+  std::vector<int> hs((size_t)R), hp((size_t)R), ht((size_t)R), hd((size_t)R);
+  for (int i = 0; i < np; i++)
+    for (int s = 0; s < n; s++) {
+      const size_t r = size_t(i) * n + s;
+      hs[r] = s;
+      hp[r] = b->pos + i;
+      ht[r] = prompt[size_t(s) * np + i];
+      hd[r] = s * m->n_text_ctx + b->pos + i;
+    }
+  CK(cudaMemcpyAsync(b->p_stream, hs.data(), sizeof(int) * R, cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(b->p_pos, hp.data(), sizeof(int) * R, cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(b->p_tok, ht.data(), sizeof(int) * R, cudaMemcpyHostToDevice, b->st));
+  CK(cudaMemcpyAsync(b->p_dst, hd.data(), sizeof(int) * R, cudaMemcpyHostToDevice, b->st));
+  WRows pr = b->rows;
+  pr.rows = R;
+  pr.row_stream = b->p_stream;
+  pr.row_pos = b->p_pos;
+  pr.row_tok = b->p_tok;
+  cudaStream_t s = b->st;
+  launch_wembed(pr, m->tok_emb, m->dec_pos, b->px, s);
+  for (size_t l = 0; l < m->layers.size(); l++) {
+    const WLayerDev& L = m->layers[l];
+    float* skl = b->sk + l * layer_stride_self(m, n);
+    float* svl = b->sv + l * layer_stride_self(m, n);
+    launch_wln(b->px, b->pcur, L.attn_ln_w, L.attn_ln_b, R, st, s);
+    prompt_product(b, np, L.q, b->pcur, st, L.qb, FE_BIAS, b->pq, st);
+    prompt_product(b, np, L.k, b->pcur, st, nullptr, FE_ROWPOS, skl, st);
+    prompt_product(b, np, L.v, b->pcur, st, L.vb, FE_ROWPOS, svl, st);
+    launch_wself(pr, b->pq, skl, svl, b->patt, s);
+    prompt_product(b, np, L.o, b->patt, st, L.ob, FE_RESID, b->px, st);
+    launch_wln(b->px, b->pcur, L.x_ln_w, L.x_ln_b, R, st, s);
+    prompt_product(b, np, L.xq, b->pcur, st, L.xqb, FE_BIAS, b->pq, st);
+    launch_wcross(pr, b->pq, b->ck + l * layer_stride_cross(m, n), b->cvt + l * layer_stride_cross(m, n), b->patt, s);
+    prompt_product(b, np, L.xo, b->patt, st, L.xob, FE_RESID, b->px, st);
+    launch_wln(b->px, b->pcur, L.mlp_ln_w, L.mlp_ln_b, R, st, s);
+    prompt_product(b, np, L.fc1, b->pcur, st, L.fc1b, FE_GELU, b->pff, 4 * st);
+    prompt_product(b, np, L.fc2, b->pff, 4 * st, L.fc2b, FE_RESID, b->px, st);
+    b->launches += 6;
+  }
+  // the no-speech probability from row sot_at, then the logits of the last row
+  launch_wln(b->px + size_t(sot_at) * n * st, b->pcur, m->ln_w, m->ln_b, n, st, s);
+  flin_w(m->tok_emb, b->pcur, st, n, nullptr, FE_BIAS, b->logits, m->n_vocab, nullptr, s);
+  launch_wnospeech(b->logits, m->n_vocab, m->voc.nosp, b->scratch, b->no_speech, n, s);
+  launch_wln(b->px + size_t(np - 1) * n * st, b->pcur, m->ln_w, m->ln_b, n, st, s);
+  flin_w(m->tok_emb, b->pcur, st, n, nullptr, FE_BIAS, b->logits, m->n_vocab, nullptr, s);
+  b->launches += 6;
+  // the token loop's rows continue after the prompt
+  b->pos += np;
+  std::vector<int> pos((size_t)n, b->pos);
+  CK(cudaMemcpyAsync(b->row_pos, pos.data(), sizeof(int) * size_t(n), cudaMemcpyHostToDevice, s));
+  launch_wtick(n, b->row_pos, b->dst_row, m->n_text_ctx, 0, nullptr, s);
+  CK(cudaGetLastError());
+  CK(cudaStreamSynchronize(s));  // the host arrays above are local
+  return GRX_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -619,30 +742,13 @@ int grx_whisper_set_audio_device(grx_whisper_batch* b, const float* d_enc) {
 
 int grx_whisper_prompt(grx_whisper_batch* b, const int* prompt, int np, int sot_at, float* no_speech) {
   if (!b || !prompt || np <= 0 || sot_at < 0 || sot_at >= np) return fail(GRX_EINVAL, "grx_whisper_prompt: bad argument");
-  if (np >= 6)
-    return fail(GRX_EINVAL, "grx_whisper_prompt: prompts of 6 or more tokens take the packed product (not in this build)");
   const grx_whisper* m = b->m;
   if (b->pos + np > m->n_text_ctx) return fail(GRX_ERANGE, "whisper: prompt too long");
   for (int i = 0; i < b->n * np; i++)
     if (prompt[i] < 0 || prompt[i] >= m->n_vocab) return fail(GRX_EINVAL, "grx_whisper_prompt: token out of range");
   CK(cudaSetDevice(b->ar.dev));
-  if (!b->g_decode) {
-    int rc = capture(b, false, &b->g_decode);
-    if (rc) return rc;
-  }
-  std::vector<int> col((size_t)b->n);
-  for (int i = 0; i < np; i++) {
-    for (int s = 0; s < b->n; s++) col[size_t(s)] = prompt[size_t(s) * np + i];
-    CK(cudaMemcpyAsync(b->row_tok, col.data(), sizeof(int) * size_t(b->n), cudaMemcpyHostToDevice, b->st));
-    CK(cudaGraphLaunch(b->g_decode, b->st));
-    b->launches += b->per_decode;
-    if (i == sot_at) {
-      launch_wnospeech(b->logits, m->n_vocab, m->voc.nosp, b->scratch, b->no_speech, b->n, b->st);
-      b->launches++;
-    }
-    CK(cudaStreamSynchronize(b->st));  // col is reused
-  }
-  b->pos += np;
+  int rc = prefill(b, prompt, np, sot_at);
+  if (rc) return rc;
   if (no_speech) CK(cudaMemcpy(no_speech, b->no_speech, sizeof(float) * size_t(b->n), cudaMemcpyDeviceToHost));
   CK(cudaGetLastError());
   return GRX_OK;

@@ -146,12 +146,19 @@ int grx_streams_step(grx_streams* s, const float* noise, float* lm_out, float* e
 int grx_streams_run_device(grx_streams* s, int frames, const float* d_noise, float* d_latent, float* d_eos);
 int grx_streams_sync(grx_streams* s);
 /* grx_streams_run_device with instrumentation: d_attn_ts (device,
- * [frames][layers][2] uint64, each pair preset to {UINT64_MAX, 0}) gets each
- * attention kernel's first-CTA start and last-CTA end in %globaltimer ns. */
+ * [frames][layers][parts][2] uint64, each pair preset to {UINT64_MAX, 0})
+ * gets each attention kernel's first-CTA start and last-CTA end in
+ * %globaltimer ns. */
 int grx_streams_run_device_timed(grx_streams* s, int frames, const float* d_noise, float* d_latent, float* d_eos,
                                  unsigned long long* d_attn_ts);
-/* The cudaStream_t the stream set's work runs on (for events). */
+/* The cudaStream_t the stream set's work runs on (for events); work is
+ * queued behind what this stream holds and finishes before what is queued
+ * on it later. */
 void* grx_streams_cuda_stream(const grx_streams* s);
+/* A set of 128 or more streams runs as two parts, each on its own CUDA
+ * stream, so one part's memory-bound attention can overlap the other's
+ * products; returns the number of parts (1 or 2). */
+int grx_streams_parts(const grx_streams* s);
 /* Positions held by stream i (voice prompt plus frames so far). */
 int grx_streams_pos(const grx_streams* s, int i);
 /* Device kernel launches issued by this stream set since creation. */
@@ -233,9 +240,10 @@ void grx_whisper_batch_free(grx_whisper_batch* b);
  * caches and sampling states start over. */
 int grx_whisper_set_audio(grx_whisper_batch* b, const float* enc);
 int grx_whisper_set_audio_device(grx_whisper_batch* b, const float* d_enc);
-/* The prompt decode (transcribe.go:166-181): prompt [n][np] tokens, np ≤ 5
- * (a prompt of 6 or more takes the reference's packed product, not in this
- * build); no_speech [n] (may be NULL) gets softmax(logits at sot_at)[nosp]. */
+/* The prompt decode (transcribe.go:166-181): prompt [n][np] tokens, all
+ * rows at once as decoder.go does (the packed product for each stream's
+ * first np/6·6 rows when np ≥ 6); no_speech [n] (may be NULL) gets
+ * softmax(logits at sot_at)[nosp]. */
 int grx_whisper_prompt(grx_whisper_batch* b, const int* prompt, int np, int sot_at, float* no_speech);
 /* `steps` rounds of the greedy loop at temperature 0 (transcribe.go:196-269:
  * process, sample, decode of the sampled token), for every stream, without

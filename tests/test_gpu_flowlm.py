@@ -136,3 +136,32 @@ def test_flowlm_batched_run_device_bit_exact(have_gpu):
     ne, rel = mismatch(dl.cpu().numpy(), lat_o)
     assert ne == 0, f"{ne} latents differ, max rel {rel:.2e}"
     assert bits_equal(de.cpu().numpy(), eos_o)
+
+
+@pytest.mark.parametrize("n", [128, 131])
+def test_flowlm_parts_run_device_and_step(have_gpu, n):
+    """A set of 128 or more streams runs as two parts on their own CUDA
+    streams (an odd count splits unevenly): device-resident frames and the
+    per-frame host call both match the oracle bit for bit."""
+    import torch
+
+    cfg = synth.FlowLMConfig(**SMALL)
+    gm, om = _models(cfg, seed=4)
+    frames = 3
+    kvs = [voice_kv(cfg, 8 + i % 5, 1 + i) for i in range(n)]  # ragged prefills
+    noise = np.stack([synth.noise_frames(1 + i, frames, cfg.ldim, cfg.temperature) for i in range(n)], axis=1)
+    lat_o, eos_o, _ = om.run([om.stream(kv) for kv in kvs], noise, threads=8)
+    st = g.Streams(gm, [gm.voice(kv) for kv in kvs], frames)
+    dn = torch.from_numpy(noise).cuda()
+    dl = torch.empty_like(dn)
+    de = torch.empty((frames, n), device="cuda")
+    st.run_device(frames, dn.data_ptr(), dl.data_ptr(), de.data_ptr())
+    st.sync()
+    ne, rel = mismatch(dl.cpu().numpy(), lat_o)
+    assert ne == 0, f"{ne} latents differ, max rel {rel:.2e}"
+    assert bits_equal(de.cpu().numpy(), eos_o)
+    assert [st.pos(i) for i in (0, n - 1)] == [8 + frames, 8 + (n - 1) % 5 + frames]
+    st.reset()
+    for f in range(frames):
+        lat, eos, _, _ = st.step(noise[f])
+        assert bits_equal(lat, lat_o[f]) and bits_equal(eos, eos_o[f]), f"frame {f}"

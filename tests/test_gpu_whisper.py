@@ -127,3 +127,30 @@ def test_whisper_loader_rejects_bad_files(have_gpu):
     assert "doesn't know" in str(e.value)
     with pytest.raises(g.GrxError):
         g.Whisper(good[: len(good) - 7])
+
+
+@pytest.mark.parametrize("np_", [6, 9])
+def test_whisper_long_prompt_packed_rows(have_gpu, np_):
+    """A prompt of 6 or more tokens takes the packed product for each
+    stream's first np/6·6 rows (whisper/gemm.go:150-186) and gemv for the
+    rest; logits, no-speech probability and the following tokens match."""
+    cfg = synth.WhisperConfig(**SMALL_W)
+    gm, om = _models(cfg, seed=2)
+    n = 2
+    enc = _enc(cfg, n, seed0=11)
+    prompt = [gm.prev] + list(range(300, 300 + np_ - 2)) + [gm.sot]
+    sot_at = np_ - 1
+    b = g.WhisperBatch(gm, n)
+    b.set_audio(enc)
+    ns = b.prompt(prompt, sot_at)
+    lg = b.logits()
+    for i in range(n):
+        want = om.decode(om.seq(enc[i]), prompt, [sot_at, np_ - 1])
+        ne, rel = mismatch(lg[i], want[1])
+        assert ne == 0, f"{ne} logits differ (max rel {rel:.2e})"
+    toks = b.run(5)
+    for i in range(n):
+        want, wns = om.greedy(om.seq(enc[i]), prompt, sot_at, 5)
+        _check_tokens(toks[:, i], want)
+        assert abs(ns[i] - wns) <= TOL * abs(wns)
+
