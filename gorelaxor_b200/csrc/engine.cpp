@@ -486,7 +486,7 @@ int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, fl
   const int n = w->rows, k = w->cols;
   const bool int8 = w->type == 2 && (w->dropped || m >= 2);
   if (!int8 && m > 16) return fail(GRX_EINVAL, "grx_linear: float-path products take at most 16 rows");
-  if (int8 && m > 8 && k % 128 != 0) return fail(GRX_EINVAL, "grx_linear: int8 products of more than 8 rows need K % 128 == 0");
+  if (int8 && m > 8 && k % 64 != 0) return fail(GRX_EINVAL, "grx_linear: int8 products of more than 8 rows need K % 64 == 0");
   if (int8 && m <= 8 && n % 32 != 0) return fail(GRX_EINVAL, "grx_linear: int8 products of up to 8 rows need N % 32 == 0");
   int rc = 0;
   Arena ar;

@@ -14,9 +14,13 @@
 //    out of the tensor core whole and is folded into float32 accumulators
 //    with the per-block scales before the next block.
 // Both fuse what follows the product in the transformer (see Epi).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
+#include <cstdlib>
+#include <cstdint>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -174,6 +178,9 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0));
 }
+__device__ __forceinline__ void cp_async_n(uint32_t dst, const void* src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(bytes));
+}
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_wait() {
@@ -184,9 +191,6 @@ __device__ __forceinline__ void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(a));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, uint32_t a) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(r0), "=r"(r1) : "r"(a));
 }
 __device__ __forceinline__ f2 lds64(uint32_t a) {
   f2 v;
@@ -299,7 +303,7 @@ __global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __res
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
   const int wm = warp / WGN, wn = warp % WGN;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int nb = K / QK, nkt = nb / 4, np2 = (N + 1) / 2;
+  const int nb = K / QK, nkt = (nb + 3) / 4, np2 = (N + 1) / 2;  // a last stage may hold fewer blocks
   const int arow = wm * 16 * TM, brow = wn * 8 * TN;
   const uint32_t sbase = smem_u32(smem_raw);
 
@@ -308,9 +312,11 @@ __global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __res
   const int8_t* srcA[C::PA];
   uint32_t dstA[C::PA];
   bool okA[C::PA];
+  int blA[C::PA], blW[C::PW], blS[C::PS], blD[C::PD];  // the first block of the chunk within a stage
 #pragma unroll
   for (int u = 0; u < C::PA; u++) {
     const int i = tid + u * NT, r = i >> 3, c = i & 7;
+    blA[u] = c >> 1;
     okA[u] = i < C::CA && m0 + r < M;
     srcA[u] = a + (size_t)(okA[u] ? m0 + r : 0) * K + c * 16;
     dstA[u] = C::OFF_A + r * 128 + ((c ^ (r & 7)) << 4);
@@ -321,6 +327,7 @@ __global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __res
 #pragma unroll
   for (int u = 0; u < C::PW; u++) {
     const int i = tid + u * NT, r = i >> 3, c = i & 7;
+    blW[u] = c >> 1;
     okW[u] = i < C::CW && n0 + r < N;
     srcW[u] = wq + (size_t)(okW[u] ? n0 + r : 0) * K + c * 16;
     dstW[u] = C::OFF_W + r * 128 + ((c ^ (r & 7)) << 4);
@@ -331,6 +338,7 @@ __global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __res
 #pragma unroll
   for (int u = 0; u < C::PS; u++) {
     const int i = tid + u * NT, r = i >> 1, h = i & 1;
+    blS[u] = 2 * h;
     okS[u] = i < C::CS && m0 + r < M;
     srcS[u] = as + (size_t)(okS[u] ? m0 + r : 0) * nb + 2 * h;
     dstS[u] = C::OFF_SA + r * 32 + h * 16;
@@ -341,23 +349,28 @@ __global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __res
 #pragma unroll
   for (int u = 0; u < C::PD; u++) {
     const int i = tid + u * NT, kb = i / (BN / 2), p = i % (BN / 2);
+    blD[u] = kb;
     okD[u] = i < C::CD && n0 + 2 * p < N;
     srcD[u] = dwnm + (size_t)kb * np2 + (okD[u] ? n0 / 2 + p : 0);
     dstD[u] = C::OFF_DN + (kb * (BN / 2) + p) * 16;
   }
+  // Chunks past the last block are zero-filled without a read (an odd
+  // block count ends with a half scale chunk).
   auto load = [&](int kt, uint32_t st) {
+    const int left = nb - kt * 4;
 #pragma unroll
     for (int u = 0; u < C::PA; u++)
-      if (tid + u * NT < C::CA) cp_async16(st + dstA[u], srcA[u] + kt * 128, okA[u]);
+      if (tid + u * NT < C::CA) cp_async16(st + dstA[u], srcA[u] + kt * 128, okA[u] && blA[u] < left);
 #pragma unroll
     for (int u = 0; u < C::PW; u++)
-      if (tid + u * NT < C::CW) cp_async16(st + dstW[u], srcW[u] + kt * 128, okW[u]);
+      if (tid + u * NT < C::CW) cp_async16(st + dstW[u], srcW[u] + kt * 128, okW[u] && blW[u] < left);
 #pragma unroll
     for (int u = 0; u < C::PS; u++)
-      if (tid + u * NT < C::CS) cp_async16(st + dstS[u], srcS[u] + kt * 4, okS[u]);
+      if (tid + u * NT < C::CS)
+        cp_async_n(st + dstS[u], srcS[u] + kt * 4, okS[u] ? (blS[u] + 1 < left ? 16 : blS[u] < left ? 8 : 0) : 0);
 #pragma unroll
     for (int u = 0; u < C::PD; u++)
-      if (tid + u * NT < C::CD) cp_async16(st + dstD[u], srcD[u] + (size_t)kt * 4 * np2, okD[u]);
+      if (tid + u * NT < C::CD) cp_async16(st + dstD[u], srcD[u] + (size_t)kt * 4 * np2, okD[u] && blD[u] < left);
   };
 
   // ---- fragment offsets within a stage
@@ -405,6 +418,7 @@ __global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __res
     rs = rs + 1 == STAGES ? 0 : rs + 1;
 #pragma unroll
     for (int kk = 0; kk < 4; kk++) {
+      if (kt * 4 + kk >= nb) break;
       const uint32_t kl = uint32_t(2 * kk) << 4;  // the block's first chunk (the swizzle keeps bit 0)
       uint32_t af[TM][4], bf[TN][2];
 #pragma unroll
@@ -450,6 +464,415 @@ struct Gemm2 {
   }
 };
 
+// ------------------------------------------ GEMM on the 5th-gen tensor core --
+//
+// k_q8_tc: the same per-block chain with the int8 block products from
+// tcgen05.mma (kind::i8, M = 128 activation rows, N = BN weight rows, K = 32 =
+// one Q8_0 block per instruction) into Tensor Memory. A stage is four blocks
+// of K (one 128-byte swizzle row of both operands). Warp roles:
+//  * warp 0, one thread: the TMA loads of a stage (activation and weight
+//    tiles in the 128-byte swizzled K-major layout the MMA reads, the
+//    activation scales and the {dw, dw', nm, nm'} quads);
+//  * warp 1: allocates TMEM; one thread issues a stage's four MMAs into one
+//    of two groups of four int32 tiles and commits the group once;
+//  * the epilogue warps: thread r of lane quarter q owns activation row
+//    32q + r and a slice of CW columns. Per block it loads its row of the
+//    int32 tile (tcgen05.ld), adds the magic bits (1.5·2^23 + s as float, as
+//    the mma.sync path gets from its accumulator initialisation) and folds
+//    it into the chain with two packed FMAs per column pair; per stage it
+//    frees the group and the stage's shared memory.
+// Synchronisation is per stage, not per block: the barrier operations of the
+// single issuing thread cost more than an MMA. Every wait is bounded (about a
+// second of clocks); one that runs out sets the kernel's fault word, every
+// role then leaves its loop, and the block still reaches the TMEM release.
+constexpr int TC_BM = 128, TC_KB = 4, TC_STAGES = 4, TC_GROUPS = 2;
+
+template <int BN, int EPW>
+struct TcCfg {
+  static constexpr int NT = 64 + 32 * EPW;  // producer warp, MMA warp, epilogue warps
+  static constexpr int CW = BN / (EPW / 4);  // columns per epilogue thread
+  static_assert(EPW % 4 == 0 && CW % 16 == 0, "epilogue warps cover the lane quarters evenly");
+  static constexpr int TMEM_COLS = TC_GROUPS * TC_KB * BN;  // power of two for BN = 16, 32, 64
+  static constexpr int A_BYTES = TC_BM * 128, B_BYTES = BN * 128, S_BYTES = TC_BM * TC_KB * 8,
+                       D_BYTES = TC_KB * BN * 8;
+  static constexpr int OFF_B = A_BYTES, OFF_S = OFF_B + B_BYTES, OFF_D = OFF_S + S_BYTES;
+  static constexpr int STAGE = (OFF_D + D_BYTES + 1023) / 1024 * 1024;
+  static constexpr int TX = A_BYTES + B_BYTES + S_BYTES + D_BYTES;
+  static constexpr int OFF_BAR = STAGE * TC_STAGES;
+  static constexpr int NBAR = 2 * TC_STAGES + 2 * TC_GROUPS + 1;
+  static constexpr int SMEM = 1024 + OFF_BAR + NBAR * 8 + 16;  // + alignment slack
+  // Shared memory bounds how many blocks share an SM (228 KB), so their TMEM
+  // allocations together never exceed the 512 columns and never wait.
+  static_assert((228 * 1024 / SMEM) * TMEM_COLS <= 512, "co-resident blocks must fit in TMEM");
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "allocation size");
+};
+
+__device__ int g_q8_tc_fault = 0;
+
+__device__ __forceinline__ bool mb_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false once about 2^31 clocks passed or another role gave up.
+__device__ __forceinline__ bool mb_wait(uint32_t bar, uint32_t parity, volatile int* dead) {
+  if (mb_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mb_try(bar, parity)) {
+    if (*dead || clock64() - t0 > (1LL << 31)) {
+      if (!*dead) {
+        *dead = 1;
+        atomicExch(&g_q8_tc_fault, 1);
+      }
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void mb_init(uint32_t bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mb_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+// The single-thread instructions below are executed by a whole warp in
+// step and issued by the one lane elect.sync picks, so the warp's control
+// flow and operands stay uniform.
+__device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n"
+      "@p cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n}\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mb_expect_one(uint32_t bar, uint32_t bytes) {
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n@p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n}\n" ::"r"(bar),
+      "r"(bytes)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n"
+      "@p tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(bar)
+      : "memory");
+}
+// K-major operand in the 128-byte swizzle: rows of 128 bytes, groups of 8
+// rows 1024 bytes apart; the start moves 32 bytes per block within a row.
+__device__ __forceinline__ uint64_t tc_desc(uint32_t addr) {
+  return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(2) << 61);
+}
+// D += A·Bᵀ (the tile holds the magic bits, so D ends as 1.5·2^23 + s).
+__device__ __forceinline__ void tc_mma_i8(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t idesc) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, 1, 0;\n elect.sync _|e, 0xffffffff;\n"
+      "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(ad), "l"(bd), "r"(idesc)
+      : "memory");
+}
+// 16 consecutive int32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t* d) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7]), "=r"(d[8]),
+        "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15])
+      : "r"(taddr)
+      : "memory");
+}
+// 16 consecutive columns of this thread's TMEM lane set to v.
+__device__ __forceinline__ void tc_st16(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};\n" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+template <int BN, int EPW>
+__global__ void __launch_bounds__(TcCfg<BN, EPW>::NT, 1)
+    k_q8_tc(const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mw,
+            const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap md, int M, int N, int nb,
+            EpiArgs e) {
+  using C = TcCfg<BN, EPW>;
+  constexpr int S = TC_STAGES, G = TC_GROUPS, CW = C::CW;
+  extern __shared__ uint8_t tc_raw[];
+  const uint32_t raw = smem_u32(tc_raw), base = (raw + 1023) & ~1023u;
+  uint8_t* gbase = tc_raw + (base - raw);
+  const uint32_t bars = base + C::OFF_BAR;
+  auto full = [&](int s) { return bars + 8 * s; };
+  auto empty = [&](int s) { return bars + 8 * (S + s); };
+  auto tfull = [&](int g) { return bars + 8 * (2 * S + g); };
+  auto tempty = [&](int g) { return bars + 8 * (2 * S + G + g); };
+  const uint32_t done = bars + 8 * (2 * S + 2 * G);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::OFF_BAR + C::NBAR * 8);
+  __shared__ int dead_s;
+  volatile int* dead = &dead_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * TC_BM;
+  if (threadIdx.x == 0) {
+    dead_s = 0;
+    for (int s = 0; s < S; s++) {
+      mb_init(full(s), 1);
+      mb_init(empty(s), EPW);
+    }
+    for (int g = 0; g < G; g++) {
+      mb_init(tfull(g), 1);
+      mb_init(tempty(g), EPW);
+    }
+    mb_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile(
+        "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n"
+        "tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::"r"(smem_u32(tmem_slot)),
+        "r"(C::TMEM_COLS)
+        : "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nst = (nb + TC_KB - 1) / TC_KB;
+  if (warp >= 2) {  // every tile starts as the magic bits; the epilogue restores them after each read
+    const uint32_t t0 = tmem + (uint32_t((warp & 3) * 32) << 16) + uint32_t(((warp - 2) >> 2) * CW);
+    for (int b = 0; b < TC_GROUPS * TC_KB; b++)
+#pragma unroll
+      for (int c = 0; c < CW / 16; c++) tc_st16(t0 + uint32_t(b * BN + 16 * c), uint32_t(MAGIC_BITS));
+    tc_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (warp == 0) {
+    {
+      int issued = 0;
+      for (int st = 0; st < nst; st++) {
+        const int s = st % S;
+        if (!__all_sync(FULL, mb_wait(empty(s), ((st / S) & 1) ^ 1, dead))) break;
+        const uint32_t sb = base + s * C::STAGE;
+        mb_expect_one(full(s), C::TX);
+        tma2d(sb, &ma, st * 128, m0, full(s));
+        tma2d(sb + C::OFF_B, &mw, st * 128, n0, full(s));
+        tma2d(sb + C::OFF_S, &ms, st * 8, m0, full(s));
+        tma2d(sb + C::OFF_D, &md, n0 * 2, st * TC_KB, full(s));
+        issued = st + 1;
+      }
+      // After a failure, let this block's copies land before it exits.
+      if (*dead)
+        for (int st = issued > S ? issued - S : 0; st < issued; st++) {
+          const long long t0 = clock64();
+          while (!mb_try(full(st % S), (st / S) & 1) && clock64() - t0 < (1LL << 30)) {
+          }
+        }
+    }
+  } else if (warp == 1) {
+    {
+      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(TC_BM >> 4) << 24);
+      for (int st = 0; st < nst; st++) {
+        const int s = st % S, g = st % G, nbl = min(TC_KB, nb - st * TC_KB);
+        if (!__all_sync(FULL, mb_wait(full(s), (st / S) & 1, dead))) break;
+        if (!__all_sync(FULL, mb_wait(tempty(g), ((st / G) & 1) ^ 1, dead))) break;
+        tc_fence_after();
+        const uint32_t sb = base + s * C::STAGE;
+        for (int kk = 0; kk < nbl; kk++)
+          tc_mma_i8(tmem + uint32_t((g * TC_KB + kk) * BN), tc_desc(sb + kk * 32), tc_desc(sb + C::OFF_B + kk * 32),
+                    idesc);
+        tc_commit(tfull(g));
+      }
+      // Every MMA issued has completed before the TMEM is released.
+      tc_commit(done);
+      const long long t0 = clock64();
+      while (!mb_try(done, 0) && clock64() - t0 < (1LL << 31)) {
+      }
+    }
+  } else {
+    // lane quarter q (TMEM lanes 32q..32q+31 are this warp's), column slice h
+    const int q = warp & 3, h = (warp - 2) >> 2, r = q * 32 + lane, m = m0 + r, c0 = h * CW;
+    const uint32_t trow = tmem + (uint32_t(q * 32) << 16) + uint32_t(c0);
+    f2 acc[CW / 2];
+#pragma unroll
+    for (int j = 0; j < CW / 2; j++) {
+      const int c = n0 + c0 + 2 * j;
+      acc[j] = f2make(e.bias && c < N ? e.bias[c] : 0.f, e.bias && c + 1 < N ? e.bias[c + 1] : 0.f);
+    }
+    for (int st = 0; st < nst; st++) {
+      const int s = st % S, g = st % G, nbl = min(TC_KB, nb - st * TC_KB);
+      // (warp-uniform outcomes: the TMEM loads below are warp-collective)
+      if (!__all_sync(FULL, mb_wait(full(s), (st / S) & 1, dead))) break;
+      if (!__all_sync(FULL, mb_wait(tfull(g), (st / G) & 1, dead))) break;
+      tc_fence_after();
+      const uint32_t sb = base + s * C::STAGE;
+      const uint8_t* sg = gbase + (sb - base);
+      const float4 da4 = *reinterpret_cast<const float4*>(sg + C::OFF_S + r * 32);
+      const float4 da4b = *reinterpret_cast<const float4*>(sg + C::OFF_S + r * 32 + 16);
+#pragma unroll
+      for (int kk = 0; kk < TC_KB; kk++) {
+        if (kk >= nbl) break;
+        const uint32_t tb = trow + uint32_t((g * TC_KB + kk) * BN);
+        uint32_t d[CW];
+#pragma unroll
+        for (int c = 0; c < CW / 16; c++) tc_ld16(tb + 16 * c, d + 16 * c);
+        tc_wait_ld();
+#pragma unroll
+        for (int c = 0; c < CW / 16; c++) tc_st16(tb + 16 * c, uint32_t(MAGIC_BITS));
+        const float dsc = kk == 0 ? da4.x : kk == 1 ? da4.z : kk == 2 ? da4b.x : da4b.z;
+        const f2 da = f2dup(dsc);
+        const float4* dq = reinterpret_cast<const float4*>(sg + C::OFF_D) + kk * (BN / 2) + c0 / 2;
+        // in three independent passes, so the packed FMAs issue back to back
+        float4 qd[CW / 2];  // {dw[n], dw[n+1], nm[n], nm[n+1]}
+#pragma unroll
+        for (int j = 0; j < CW / 2; j++) qd[j] = dq[j];
+        f2 t[CW / 2];
+#pragma unroll
+        for (int j = 0; j < CW / 2; j++)
+          t[j] = f2fma(f2make(__uint_as_float(d[2 * j]), __uint_as_float(d[2 * j + 1])), f2make(qd[j].x, qd[j].y),
+                       f2make(qd[j].z, qd[j].w));
+#pragma unroll
+        for (int j = 0; j < CW / 2; j++) acc[j] = f2fma(t[j], da, acc[j]);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mb_arrive(tempty(g));
+        mb_arrive(empty(s));
+      }
+    }
+    if (!*dead && m < M) {
+      if (e.epi == EPI_GELU_Q8) {
+#pragma unroll
+        for (int cb = 0; cb < CW / 32; cb++) {
+          float g[32], amax = 0.f;
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            g[2 * j] = gelu_avx(f2lo(acc[cb * 16 + j]));
+            g[2 * j + 1] = gelu_avx(f2hi(acc[cb * 16 + j]));
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(g[j]));
+          const int col = n0 + c0 + cb * 32;
+          if (col < N) {
+            uint32_t w[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              uint32_t v = 0;
+#pragma unroll
+              for (int b = 0; b < 4; b++) v |= uint32_t(uint8_t(quant_val(g[4 * j + b], amax))) << (8 * b);
+              w[j] = v;
+            }
+            uint4* dst = reinterpret_cast<uint4*>(e.q8 + (size_t)m * N + col);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            const float sc = quant_scale(amax);
+            e.q8s[(size_t)m * (N / QK) + col / QK] = make_float2(sc, sc);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < CW / 2; j++) {
+          const int col = n0 + c0 + 2 * j;
+          if (col >= N) continue;
+          const float c0v = f2lo(acc[j]), c1v = f2hi(acc[j]);
+          if (e.epi == EPI_ROPE_KV) {
+            store_qkv_pair(e.kv, m, col, c0v, c1v);
+            continue;
+          }
+          float2* yp = reinterpret_cast<float2*>(e.y + (size_t)m * e.ldy + col);
+          if (e.epi == EPI_RESID) {
+            const float2 o = *yp;
+            *yp = make_float2(__fadd_rn(o.x, c0v), __fadd_rn(o.y, c1v));
+          } else {
+            *yp = make_float2(c0v, c1v);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+bool tmap2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner, uint64_t outer,
+            uint64_t stride_bytes, uint32_t box_in, uint32_t box_out, CUtensorMapSwizzle sw) {
+  const cuuint64_t dims[2] = {inner, outer}, strides[1] = {stride_bytes};
+  const cuuint32_t box[2] = {box_in, box_out}, es[2] = {1, 1};
+  return g_encode(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// A product's four tensor maps and launch shape, encoded once (a captured
+// graph replays the launch with them).
+struct TcLaunch {
+  CUtensorMap ma, mw, ms, md;
+  int M = 0, N = 0, nb = 0;
+};
+
+bool tc_prepare(TcLaunch& L, const int8_t* a, const float2* as, int M, const DQ8& w, int bn) {
+  const int N = w.rows, K = w.cols, nb = K / QK, np2 = (N + 1) / 2;
+  if (!g_encode || nb % 2 || ((uintptr_t(a) | uintptr_t(as) | uintptr_t(w.q) | uintptr_t(w.dwnm)) & 15)) return false;
+  L.M = M, L.N = N, L.nb = nb;
+  return tmap2d(&L.ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, K, M, K, 128, TC_BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         tmap2d(&L.mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q, K, N, K, 128, bn, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         tmap2d(&L.ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, as, 2 * nb, M, 8 * nb, 2 * TC_KB, TC_BM,
+                CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         tmap2d(&L.md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.dwnm, 4 * np2, nb, 16 * np2, 2 * bn, TC_KB,
+                CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+template <int BN, int EPW>
+struct GemmTc {
+  using C = TcCfg<BN, EPW>;
+  static void init() {
+    cudaFuncSetAttribute(k_q8_tc<BN, EPW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  }
+  static bool suits(const DQ8& w, const EpiArgs& e) { return !(e.epi == EPI_GELU_Q8 && (w.rows % 32 || C::CW % 32)); }
+  static void run(const TcLaunch& L, const EpiArgs& e, cudaStream_t st) {
+    dim3 grid((L.N + BN - 1) / BN, (L.M + TC_BM - 1) / TC_BM);
+    k_q8_tc<BN, EPW><<<grid, C::NT, C::SMEM, st>>>(L.ma, L.mw, L.ms, L.md, L.M, L.N, L.nb, e);
+  }
+  // False when the shape or the buffers do not suit the tensor maps (the
+  // caller then takes the mma.sync kernel, which gives identical results).
+  static bool launch(const int8_t* a, const float2* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st) {
+    TcLaunch L;
+    if (!suits(w, e) || !tc_prepare(L, a, as, M, w, BN)) return false;
+    run(L, e, st);
+    return true;
+  }
+};
+
+void tc_init_encode() {
+  if (g_encode) return;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+}
+
+// The tensor-core kernel gives the same bits as the mma.sync one but was
+// slower at every product shape timed on B200 (one tcgen05.mma per 32-deep
+// Q8_0 block costs about 100 clocks to issue, and the exact per-block chain
+// rules out split-K), so it runs only when GRX_Q8_TC=1 is set at
+// initialisation.
+bool g_q8_tc = false;
+
 // Tile shapes per product shape, the fastest of those timed at M = 256 on
 // B200, every one bit-identical to the others: 64×32 CTA tiles of four 32×16
 // warps for most (qkv 11.3 µs, attn_out 7.6, ff2 18.5 per product), 64×64
@@ -458,6 +881,12 @@ using GemmMid = Gemm2<2, 2, 2, 2, 4>;
 using GemmWide = Gemm2<2, 4, 2, 2, 4>;  // N > 3072
 
 }  // namespace
+
+int q8_tc_fault() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_q8_tc_fault, sizeof v);
+  return v;
+}
 
 void launch_q8_product(const int8_t* a, const float2* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st) {
   const int N = w.rows, K = w.cols;
@@ -475,6 +904,7 @@ void launch_q8_product(const int8_t* a, const float2* as, int M, const DQ8& w, c
       k_q8_gemv<8><<<grid, 256, sm, st>>>(a, as, M, w.q, w.d, N, K, e);
     return;
   }
+  if (g_q8_tc && GemmTc<32, 4>::launch(a, as, M, w, e, st)) return;
   if (N > 3072)
     GemmWide::launch(a, as, M, w, e, st);
   else
@@ -483,6 +913,10 @@ void launch_q8_product(const int8_t* a, const float2* as, int M, const DQ8& w, c
 
 // Raises the kernels' dynamic shared memory limits once per device.
 void q8_kernels_init() {
+  tc_init_encode();
+  const char* tc = getenv("GRX_Q8_TC");
+  g_q8_tc = tc && tc[0] == '1';
+  GemmTc<32, 4>::init();
   GemmMid::init();
   GemmWide::init();
   const int gv = 8 * 4096 + 8 * 128 * 4 + 8 * 32 * 4;

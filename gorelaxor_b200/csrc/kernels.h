@@ -97,6 +97,10 @@ void launch_ln(const LnArgs& a, int M, int D, cudaStream_t st);
 // C[M][N] = A·Wᵀ with the int8 path's arithmetic (q8int.go:148-223).
 void launch_q8_product(const int8_t* a, const float2* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st);
 
+// Nonzero once a tensor-core product gave up on a wait (its outputs are then
+// not written); read after the stream is synchronised.
+int q8_tc_fault();
+
 // The activations rounded to Q8_0 blocks (quantU8, q8int.go:88-105).
 void launch_quant(const float* x, int M, int K, int8_t* q, float2* s, cudaStream_t st);
 

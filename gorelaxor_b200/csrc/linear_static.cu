@@ -63,8 +63,8 @@ extern "C" int grx_linear_q8_static(const grx_weight* w, const float* d_x, int m
                                  "use grx_linear");
   if (m == 0) return GRX_OK;
   const int n = q8->rows, k = q8->cols;
-  if (m > 8 && k % 128 != 0)
-    return set_error(GRX_EINVAL, "grx_linear_q8_static: int8 products of more than 8 rows need K % 128 == 0");
+  if (m > 8 && k % 64 != 0)
+    return set_error(GRX_EINVAL, "grx_linear_q8_static: int8 products of more than 8 rows need K % 64 == 0");
   if (m <= 8 && n % 32 != 0)
     return set_error(GRX_EINVAL, "grx_linear_q8_static: int8 products of up to 8 rows need N % 32 == 0");
   const size_t elems = size_t(m) * size_t(k);

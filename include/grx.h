@@ -68,8 +68,9 @@ void grx_weight_free(grx_weight* w);
  * or any m ≥ 2, takes the int8 path (activations rounded to Q8_0 blocks,
  * q8int.go:148-223); otherwise the float path (gemm.go:195-259). Host
  * buffers; synchronous. Limits of this build: the float path takes at most
- * 16 rows and K ≤ 1536 (Q8_0) or K ≤ 1024 (F32); the int8 path with more
- * than 8 rows needs K % 128 == 0, with up to 8 rows N % 32 == 0. */
+ * 16 rows and K ≤ 65536; the int8 path with more
+ * than 8 rows needs K % 64 == 0 (an even number of blocks: the activation
+ * scales are copied two blocks at a time), with up to 8 rows N % 32 == 0. */
 int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, float* dst);
 
 /* grx_linear_q8_static: the int8 path of grx_linear for callers that must
@@ -101,7 +102,7 @@ int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, fl
  * streams, or two threads without ordering) race on it and must be ordered
  * by the caller. Nothing needs clearing between calls: each call writes all
  * of the array that it then reads. The same shape limits as grx_linear's
- * int8 path apply (m > 8: cols % 128 == 0; m <= 8: rows % 32 == 0). */
+ * int8 path apply (m > 8: cols % 64 == 0; m <= 8: rows % 32 == 0). */
 #define GRX_STATIC_MAX_ELEMS (1 << 20)
 int grx_linear_q8_static(const grx_weight* w, const float* d_x, int m, const float* d_bias, float* d_dst,
                          void* stream);
