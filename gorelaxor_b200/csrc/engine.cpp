@@ -17,6 +17,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -114,8 +115,16 @@ struct grx_streams {
 
 namespace {
 
-// A stream set of at least twice this many streams runs as two parts.
+// A stream set runs as up to stream_parts_max() parts of at least this many
+// streams each.
 constexpr int kMinPart = 64;
+
+// Two parts unless GRX_STREAM_PARTS (1 to 8) says otherwise.
+int stream_parts_max() {
+  const char* v = getenv("GRX_STREAM_PARTS");
+  const int p = v ? atoi(v) : 2;
+  return p < 1 ? 1 : p > 8 ? 8 : p;
+}
 
 // The kernel sequence of one frame for all streams (see grx.h): flowLM.step
 // (lm.go:185-195 → nn.go:142-182) then flowHead.sample (lm.go:108-160).
@@ -821,7 +830,7 @@ int grx_streams_create(grx_flowlm* m, int n, const grx_voice* const* voices, int
   if (!m || !voices || !out || n < 1 || max_frames < 1) return fail(GRX_EINVAL, "grx_streams_create: bad argument");
   int rc = device_init(m->dev);
   if (rc) return rc;
-  const int nparts = n >= 2 * kMinPart ? 2 : 1;
+  const int nparts = std::max(1, std::min(stream_parts_max(), n / kMinPart));
   if (nparts == 1) {
     std::unique_ptr<grx_streams> s;
     rc = streams_create_one(m, n, voices, max_frames, &s);

@@ -44,9 +44,10 @@ __host__ __device__ constexpr int fl_wstride(int bytes) { return bytes + ((160 -
 
 constexpr int KC = 256;  // K per shared-memory chunk (small enough for several CTAs per SM)
 
-template <int WM, int R, int M, int GR>
+template <int WM, int R, int M, int GR, int NTH>
 struct FlinTile {
-  static constexpr int GM = 32 / GR;  // stream groups
+  static constexpr int GM = NTH / 8 / GR;  // stream groups
+  static_assert(GM * GR * 8 == NTH, "groups of 8 lanes tile the block");
   static constexpr int TN = GR * R;   // weight rows per CTA
   static constexpr int TS = GM * M;   // streams per CTA
   static constexpr int XS = TS + (TS % 8 == 0 ? 4 : 8);
@@ -158,9 +159,9 @@ __device__ __forceinline__ uint32_t lane_word(const uint32_t (&w)[8], int l) {
   return __byte_perm(lo, hi, 0x5410);
 }
 
-template <int WM, int R, int M, int GR>
-__global__ void __launch_bounds__(256) k_flin(FArgs a) {
-  using T = FlinTile<WM, R, M, GR>;
+template <int WM, int R, int M, int GR, int NTH>
+__global__ void __launch_bounds__(NTH) k_flin(FArgs a) {
+  using T = FlinTile<WM, R, M, GR, NTH>;
   constexpr int TS = T::TS, TN = T::TN, XS = T::XS, NC = M / 4, RM = R * M;
   extern __shared__ __align__(16) uint8_t fsm[];
   const int K = a.K;
@@ -185,7 +186,7 @@ __global__ void __launch_bounds__(256) k_flin(FArgs a) {
     if (kc0 > 0) __syncthreads();  // the previous chunk's readers are done
     // ---- the chunk's weights
     if (WM == W_Q8) {
-      for (int i = tid; i < nrows * nb; i += 256) {
+      for (int i = tid; i < nrows * nb; i += NTH) {
         const int r = i / nb, b = i - r * nb;
         const uint4* src = reinterpret_cast<const uint4*>(a.wq + (size_t)(n0 + r) * K + kc0 + b * QK);
         const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(256) k_flin(FArgs a) {
       }
     } else if (WM == W_Q8H) {
       // 8 values per thread: f16(q·d), stored as halves
-      for (int i = tid; i < nrows * (kn / 8); i += 256) {
+      for (int i = tid; i < nrows * (kn / 8); i += NTH) {
         const int r = i / (kn / 8), c8 = i - r * (kn / 8), k = kc0 + c8 * 8;
         const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.wq + (size_t)(n0 + r) * K + k));
         const float d = h2f(a.wd[(size_t)(n0 + r) * (K / QK) + k / QK]);
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(256) k_flin(FArgs a) {
       constexpr int esz = WM == W_F32 ? 4 : 2;
       const int cpr = kn * esz / 16;
       const uint8_t* wsrc = WM == W_F32 ? reinterpret_cast<const uint8_t*>(a.wf) : reinterpret_cast<const uint8_t*>(a.wh);
-      for (int i = tid; i < nrows * cpr; i += 256) {
+      for (int i = tid; i < nrows * cpr; i += NTH) {
         const int r = i / cpr, c = i - r * cpr;
         cp16f(ws + size_t(r) * wst + c * 16, wsrc + ((size_t)(n0 + r) * K + kc0) * esz + c * 16);
       }
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(256) k_flin(FArgs a) {
     }
     // ---- the chunk's activations: a thread reads 8 consecutive values of
     // one stream (one 32-byte sector) and stores them stream-minor
-    for (int i = tid; i < TS * (kn / 8); i += 256) {
+    for (int i = tid; i < TS * (kn / 8); i += NTH) {
       const int m = i % TS, k8 = i / TS;
       float v[8];
       if (m < mt) {
@@ -365,39 +366,58 @@ __global__ void __launch_bounds__(256) k_flin(FArgs a) {
   }
 }
 
-template <int WM, int R, int M, int GR>
+template <int WM, int R, int M, int GR, int NTH>
 void fl_init() {
-  cudaFuncSetAttribute(k_flin<WM, R, M, GR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       int(FlinTile<WM, R, M, GR>::smem));
+  cudaFuncSetAttribute(k_flin<WM, R, M, GR, NTH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       int(FlinTile<WM, R, M, GR, NTH>::smem));
 }
 
-template <int WM, int R, int M, int GR>
+template <int WM, int R, int M, int GR, int NTH>
 void fl_launch(const FArgs& a, cudaStream_t st) {
-  using T = FlinTile<WM, R, M, GR>;
+  using T = FlinTile<WM, R, M, GR, NTH>;
   dim3 grid((a.N + T::TN - 1) / T::TN, (a.M + T::TS - 1) / T::TS);
-  k_flin<WM, R, M, GR><<<grid, 256, T::smem, st>>>(a);
+  k_flin<WM, R, M, GR, NTH><<<grid, NTH, T::smem, st>>>(a);
 }
 
-// Per weight kind: streams per CTA follow the number of streams, so a
-// single stream does not pay for 32.
+template <int WM, int R, int M, int GR, int NTH>
+int fl_ctas(const FArgs& a) {
+  using T = FlinTile<WM, R, M, GR, NTH>;
+  return ((a.N + T::TN - 1) / T::TN) * ((a.M + T::TS - 1) / T::TS);
+}
+
+// Per weight kind and shape. Every configuration gives the same bits (the
+// lanes' order over k is fixed); the largest tile that still makes about an
+// SM's worth of blocks wins, since a product too small to fill the GPU is
+// bound by one block's latency through K.
+constexpr int kFillCtas = 148;
 template <int WM>
 void fl_dispatch(const FArgs& a, cudaStream_t st) {
-  if (a.M <= 4)
-    fl_launch<WM, 2, 4, 32>(a, st);  // 64 rows × 4 streams
-  else if (a.M <= 8)
-    fl_launch<WM, 1, 8, 16>(a, st);  // 16 rows × 16 streams
-  else if (WM == W_Q8)
-    fl_launch<WM, 2, 16, 16>(a, st);  // 32 rows × 32 streams
-  else
-    fl_launch<WM, 4, 8, 8>(a, st);  // 32 rows × 32 streams
+  if (a.M <= 4) {
+    fl_launch<WM, 2, 4, 32, 256>(a, st);  // 64 rows × 4 streams
+  } else if (a.M <= 8) {
+    if (fl_ctas<WM, 1, 8, 16, 256>(a) >= kFillCtas)
+      fl_launch<WM, 1, 8, 16, 256>(a, st);  // 16 rows × 16 streams
+    else
+      fl_launch<WM, 1, 8, 8, 64>(a, st);  // 8 rows × 8 streams
+  } else if (WM == W_Q8 && fl_ctas<WM, 2, 16, 16, 256>(a) >= kFillCtas) {
+    fl_launch<WM, 2, 16, 16, 256>(a, st);  // 32 rows × 32 streams
+  } else if (WM != W_Q8 && fl_ctas<WM, 4, 8, 8, 256>(a) >= kFillCtas) {
+    fl_launch<WM, 4, 8, 8, 256>(a, st);  // 32 rows × 32 streams
+  } else if (fl_ctas<WM, 2, 8, 8, 128>(a) >= kFillCtas) {
+    fl_launch<WM, 2, 8, 8, 128>(a, st);  // 16 rows × 16 streams
+  } else {
+    fl_launch<WM, 1, 8, 8, 64>(a, st);  // 8 rows × 8 streams
+  }
 }
 
 template <int WM>
 void fl_init_all() {
-  fl_init<WM, 2, 4, 32>();
-  fl_init<WM, 1, 8, 16>();
-  fl_init<WM, 2, 16, 16>();
-  fl_init<WM, 4, 8, 8>();
+  fl_init<WM, 2, 4, 32, 256>();
+  fl_init<WM, 1, 8, 16, 256>();
+  fl_init<WM, 2, 16, 16, 256>();
+  fl_init<WM, 4, 8, 8, 256>();
+  fl_init<WM, 2, 8, 8, 128>();
+  fl_init<WM, 1, 8, 8, 64>();
 }
 
 }  // namespace

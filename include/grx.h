@@ -156,9 +156,11 @@ int grx_streams_run_device_timed(grx_streams* s, int frames, const float* d_nois
  * queued behind what this stream holds and finishes before what is queued
  * on it later. */
 void* grx_streams_cuda_stream(const grx_streams* s);
-/* A set of 128 or more streams runs as two parts, each on its own CUDA
- * stream, so one part's memory-bound attention can overlap the other's
- * products; returns the number of parts (1 or 2). */
+/* A set of 128 or more streams runs as parts of at least 64 streams, each
+ * on its own CUDA stream, so one part's memory-bound attention can overlap
+ * another's products: two parts at most unless the environment variable
+ * GRX_STREAM_PARTS (1 to 8, read when the set is created) allows more.
+ * Returns the number of parts. */
 int grx_streams_parts(const grx_streams* s);
 /* Positions held by stream i (voice prompt plus frames so far). */
 int grx_streams_pos(const grx_streams* s, int i);
