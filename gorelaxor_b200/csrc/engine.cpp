@@ -93,8 +93,10 @@ struct grx_streams {
         *cur = nullptr;
   float *noise1 = nullptr, *lat1 = nullptr, *scaled1 = nullptr, *eos1 = nullptr;
   FrameIO* io = nullptr;
-  cudaGraphExec_t exec = nullptr;
+  cudaGraphExec_t exec = nullptr;  // one frame
   cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec_n = nullptr;  // kGraphFrames frames, for device-resident runs
+  cudaGraph_t graph_n = nullptr;
   int64_t launches = 0;
   int per_frame = 0;
   // A large set runs as parts, each with its own CUDA stream and frame graph,
@@ -108,6 +110,8 @@ struct grx_streams {
     cudaSetDevice(ar.dev);
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
+    if (exec_n) cudaGraphExecDestroy(exec_n);
+    if (graph_n) cudaGraphDestroy(graph_n);
     if (ev) cudaEventDestroy(ev);
     if (st) cudaStreamDestroy(st);
   }
@@ -359,15 +363,36 @@ int enqueue_frame(grx_streams* s) {
   return k;
 }
 
+// A device-resident run replays kGraphFrames frames per graph launch (the
+// frame counter in FrameIO moves on inside the graph), which spares most of
+// the gaps between graph launches; the step-by-step path replays one frame.
+constexpr int kGraphFrames = 8;
+
 int build_graph(grx_streams* s) {
-  CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
-  int k = enqueue_frame(s);
-  cudaGraph_t g = nullptr;
-  cudaError_t e = cudaStreamEndCapture(s->st, &g);
-  if (e != cudaSuccess) return fail(GRX_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
-  s->graph = g;
-  CK(cudaGraphInstantiate(&s->exec, g, 0));
-  s->per_frame = k;
+  for (int n : {1, kGraphFrames}) {
+    CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+    int k = 0;
+    for (int f = 0; f < n; f++) k = enqueue_frame(s);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s->st, &g);
+    if (e != cudaSuccess) return fail(GRX_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    if (n == 1) {
+      s->graph = g;
+      CK(cudaGraphInstantiate(&s->exec, g, 0));
+      s->per_frame = k;
+    } else {
+      s->graph_n = g;
+      CK(cudaGraphInstantiate(&s->exec_n, g, 0));
+    }
+  }
+  return GRX_OK;
+}
+
+// Queues `frames` frames of one set (or part) on its stream.
+int replay_frames(grx_streams* s, int frames) {
+  int f = 0;
+  for (; f + kGraphFrames <= frames; f += kGraphFrames) CK(cudaGraphLaunch(s->exec_n, s->st));
+  for (; f < frames; f++) CK(cudaGraphLaunch(s->exec, s->st));
   return GRX_OK;
 }
 
@@ -1039,7 +1064,8 @@ int grx_streams_run_device_timed(grx_streams* s, int frames, const float* d_nois
   if (s->parts.empty()) {
     FrameIO io{d_noise, d_latent, nullptr, d_eos, 0, d_attn_ts, s->n, 0, 0, 1};
     CK(cudaMemcpyAsync(s->io, &io, sizeof io, cudaMemcpyHostToDevice, s->st));
-    for (int f = 0; f < frames; f++) CK(cudaGraphLaunch(s->exec, s->st));
+    int rc2 = replay_frames(s, frames);
+    if (rc2) return rc2;
     s->launches += int64_t(frames) * s->per_frame;
     return GRX_OK;
   }
@@ -1051,8 +1077,11 @@ int grx_streams_run_device_timed(grx_streams* s, int frames, const float* d_nois
     FrameIO io{d_noise, d_latent, nullptr, d_eos, 0, d_attn_ts, s->n, p->row0, int(i), int(s->parts.size())};
     CK(cudaMemcpyAsync(p->io, &io, sizeof io, cudaMemcpyHostToDevice, p->st));
   }
-  for (int f = 0; f < frames; f++)
-    for (auto& p : s->parts) CK(cudaGraphLaunch(p->exec, p->st));
+  for (int f = 0; f < frames; f += kGraphFrames)
+    for (auto& p : s->parts) {
+      int rc2 = replay_frames(p.get(), std::min(kGraphFrames, frames - f));
+      if (rc2) return rc2;
+    }
   // join: the parent's stream waits for every part
   for (auto& p : s->parts) {
     p->launches += int64_t(frames) * p->per_frame;
