@@ -54,7 +54,9 @@ struct FlinTile {
   static_assert(M % 4 == 0 && R * M >= 8, "streams in fours; at least one output per lane after the HSUM");
   static constexpr int wbytes = fl_wstride(WM == W_Q8 ? KC : WM == W_F32 ? 4 * KC : 2 * KC);
   static constexpr int dstride = (KC / QK) | 1;
-  static constexpr size_t smem = size_t(KC) * XS * 4 + size_t(TN) * wbytes + (WM == W_Q8 ? size_t(TN) * dstride * 4 : 0);
+  static constexpr int wbufs = (WM == W_F32 || WM == W_H16) ? 2 : 1;  // async-copied weights double-buffer
+  static constexpr size_t smem =
+      size_t(KC) * XS * 4 + size_t(TN) * wbytes * wbufs + (WM == W_Q8 ? size_t(TN) * dstride * 4 : 0);
 };
 
 __device__ __forceinline__ float q8h(int8_t q, float d) { return __half2float(__float2half_rn(__fmul_rn(float(q), d))); }
@@ -181,66 +183,133 @@ __global__ void __launch_bounds__(NTH) k_flin(FArgs a) {
 #pragma unroll
     for (int p = 0; p < M / 2; p++) acc[r][p] = acc1[r][p] = 0;
 
-  for (int kc0 = 0; kc0 < kfull; kc0 += KC) {
-    const int kn = min(KC, kfull - kc0), nb = kn / QK;
-    if (kc0 > 0) __syncthreads();  // the previous chunk's readers are done
-    // ---- the chunk's weights
+  // Chunk c+1's operands come from global memory into registers (the F32 and
+  // F16 weights by async copy into the other of two buffers) while chunk c is
+  // multiplied, so a product waits on memory once rather than once per chunk
+  // and per load.
+  constexpr bool WASYNC = WM == W_F32 || WM == W_H16;
+  constexpr int XI = (TS * (KC / 8) + NTH - 1) / NTH;   // activation items: (stream, 8 values)
+  constexpr int WQI = (TN * (KC / QK) + NTH - 1) / NTH;  // Q8_0 items: (row, block)
+  constexpr int WHI = (TN * (KC / 8) + NTH - 1) / NTH;   // widened Q8_0 items: (row, 8 values)
+  constexpr int WDI = WQI > WHI ? WQI : WHI;
+  float4 xr0[XI], xr1[XI];
+  uint4 qr0[WQI], qr1[WQI];
+  uint2 hr[WHI];
+  uint16_t qd[WDI];
+  const size_t wrow_bytes = WM == W_F32 ? 4 : 2;
+  auto fetch = [&](int kc0) {
+    const int kn = min(KC, kfull - kc0);
+#pragma unroll
+    for (int u = 0; u < XI; u++) {
+      const int i = tid + u * NTH, m = i % TS, k8 = i / TS;
+      if (k8 < kn / 8 && m < mt) {
+        const float4* p = reinterpret_cast<const float4*>(xsrc + (size_t)(m0 + m) * a.ldx + kc0 + k8 * 8);
+        xr0[u] = p[0];
+        xr1[u] = p[1];
+      }
+    }
     if (WM == W_Q8) {
-      for (int i = tid; i < nrows * nb; i += NTH) {
-        const int r = i / nb, b = i - r * nb;
-        const uint4* src = reinterpret_cast<const uint4*>(a.wq + (size_t)(n0 + r) * K + kc0 + b * QK);
-        const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
-        const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        uint4* dstp = reinterpret_cast<uint4*>(ws + size_t(r) * wst + b * 32);
-        dstp[0] = make_uint4(lane_word(w, 0), lane_word(w, 1), lane_word(w, 2), lane_word(w, 3));
-        dstp[1] = make_uint4(lane_word(w, 4), lane_word(w, 5), lane_word(w, 6), lane_word(w, 7));
-        ds[r * dst + b] = h2f(a.wd[(size_t)(n0 + r) * (K / QK) + kc0 / QK + b]);
+#pragma unroll
+      for (int u = 0; u < WQI; u++) {
+        const int i = tid + u * NTH, r = i / (KC / QK), b = i % (KC / QK);
+        if (r < nrows && b < kn / QK) {
+          const uint4* src = reinterpret_cast<const uint4*>(a.wq + (size_t)(n0 + r) * K + kc0 + b * QK);
+          qr0[u] = __ldg(src);
+          qr1[u] = __ldg(src + 1);
+          qd[u] = a.wd[(size_t)(n0 + r) * (K / QK) + kc0 / QK + b];
+        }
       }
     } else if (WM == W_Q8H) {
-      // 8 values per thread: f16(q·d), stored as halves
-      for (int i = tid; i < nrows * (kn / 8); i += NTH) {
-        const int r = i / (kn / 8), c8 = i - r * (kn / 8), k = kc0 + c8 * 8;
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.wq + (size_t)(n0 + r) * K + k));
-        const float d = h2f(a.wd[(size_t)(n0 + r) * (K / QK) + k / QK]);
-        const int8_t* qb = reinterpret_cast<const int8_t*>(&u);
-        __half h[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) h[j] = __float2half_rn(__fmul_rn(float(qb[j]), d));
-        *reinterpret_cast<uint4*>(ws + size_t(r) * wst + c8 * 16) = *reinterpret_cast<const uint4*>(h);
+      for (int u = 0; u < WHI; u++) {
+        const int i = tid + u * NTH, r = i / (KC / 8), c8 = i % (KC / 8);
+        if (r < nrows && c8 < kn / 8) {
+          const int k = kc0 + c8 * 8;
+          hr[u] = __ldg(reinterpret_cast<const uint2*>(a.wq + (size_t)(n0 + r) * K + k));
+          qd[u] = a.wd[(size_t)(n0 + r) * (K / QK) + k / QK];
+        }
       }
-    } else {
-      constexpr int esz = WM == W_F32 ? 4 : 2;
-      const int cpr = kn * esz / 16;
-      const uint8_t* wsrc = WM == W_F32 ? reinterpret_cast<const uint8_t*>(a.wf) : reinterpret_cast<const uint8_t*>(a.wh);
-      for (int i = tid; i < nrows * cpr; i += NTH) {
-        const int r = i / cpr, c = i - r * cpr;
-        cp16f(ws + size_t(r) * wst + c * 16, wsrc + ((size_t)(n0 + r) * K + kc0) * esz + c * 16);
-      }
-      asm volatile("cp.async.commit_group;\n" ::);
     }
-    // ---- the chunk's activations: a thread reads 8 consecutive values of
-    // one stream (one 32-byte sector) and stores them stream-minor
-    for (int i = tid; i < TS * (kn / 8); i += NTH) {
-      const int m = i % TS, k8 = i / TS;
-      float v[8];
-      if (m < mt) {
-        const float4* p = reinterpret_cast<const float4*>(xsrc + (size_t)(m0 + m) * a.ldx + kc0 + k8 * 8);
-        const float4 p0 = p[0], p1 = p[1];
-        v[0] = p0.x, v[1] = p0.y, v[2] = p0.z, v[3] = p0.w, v[4] = p1.x, v[5] = p1.y, v[6] = p1.z, v[7] = p1.w;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = 0.f;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; j++) xs[(k8 * 8 + j) * XS + m] = v[j];
+  };
+  auto fetch_async = [&](int kc0, int buf) {
+    const int kn = min(KC, kfull - kc0), cpr = kn * int(wrow_bytes) / 16;
+    const uint8_t* wsrc = WM == W_F32 ? reinterpret_cast<const uint8_t*>(a.wf) : reinterpret_cast<const uint8_t*>(a.wh);
+    uint8_t* wb = ws + size_t(buf) * TN * wst;
+    for (int i = tid; i < nrows * cpr; i += NTH) {
+      const int r = i / cpr, c = i - r * cpr;
+      cp16f(wb + size_t(r) * wst + c * 16, wsrc + ((size_t)(n0 + r) * K + kc0) * wrow_bytes + c * 16);
     }
-    if (WM == W_F32 || WM == W_H16) asm volatile("cp.async.wait_all;\n" ::);
+    asm volatile("cp.async.commit_group;\n" ::);
+  };
+  // The fetched registers to shared memory: activations stream-minor, Q8_0
+  // blocks re-laid into lane words, widened values as halves.
+  auto stage = [&](int kc0) {
+    const int kn = min(KC, kfull - kc0);
+#pragma unroll
+    for (int u = 0; u < XI; u++) {
+      const int i = tid + u * NTH, m = i % TS, k8 = i / TS;
+      if (k8 < kn / 8) {
+        const bool ok = m < mt;
+        const float v[8] = {ok ? xr0[u].x : 0.f, ok ? xr0[u].y : 0.f, ok ? xr0[u].z : 0.f, ok ? xr0[u].w : 0.f,
+                            ok ? xr1[u].x : 0.f, ok ? xr1[u].y : 0.f, ok ? xr1[u].z : 0.f, ok ? xr1[u].w : 0.f};
+#pragma unroll
+        for (int j = 0; j < 8; j++) xs[(k8 * 8 + j) * XS + m] = v[j];
+      }
+    }
+    if (WM == W_Q8) {
+#pragma unroll
+      for (int u = 0; u < WQI; u++) {
+        const int i = tid + u * NTH, r = i / (KC / QK), b = i % (KC / QK);
+        if (r < nrows && b < kn / QK) {
+          const uint32_t w[8] = {qr0[u].x, qr0[u].y, qr0[u].z, qr0[u].w, qr1[u].x, qr1[u].y, qr1[u].z, qr1[u].w};
+          uint4* dstp = reinterpret_cast<uint4*>(ws + size_t(r) * wst + b * 32);
+          dstp[0] = make_uint4(lane_word(w, 0), lane_word(w, 1), lane_word(w, 2), lane_word(w, 3));
+          dstp[1] = make_uint4(lane_word(w, 4), lane_word(w, 5), lane_word(w, 6), lane_word(w, 7));
+          ds[r * dst + b] = h2f(qd[u]);
+        }
+      }
+    } else if (WM == W_Q8H) {
+#pragma unroll
+      for (int u = 0; u < WHI; u++) {
+        const int i = tid + u * NTH, r = i / (KC / 8), c8 = i % (KC / 8);
+        if (r < nrows && c8 < kn / 8) {
+          const float d = h2f(qd[u]);
+          const int8_t* qb = reinterpret_cast<const int8_t*>(&hr[u]);
+          __half h[8];
+#pragma unroll
+          for (int j = 0; j < 8; j++) h[j] = __float2half_rn(__fmul_rn(float(qb[j]), d));
+          *reinterpret_cast<uint4*>(ws + size_t(r) * wst + c8 * 16) = *reinterpret_cast<const uint4*>(h);
+        }
+      }
+    }
+  };
+
+  const int nch = (kfull + KC - 1) / KC;
+  if (nch > 0) {
+    fetch(0);
+    if (WASYNC) fetch_async(0, 0);
+  }
+  for (int ch = 0; ch < nch; ch++) {
+    const int kc0 = ch * KC, kn = min(KC, kfull - kc0), nb = kn / QK;
+    if (ch > 0) __syncthreads();  // the previous chunk's readers are done
+    stage(kc0);
+    if (ch + 1 < nch) {
+      fetch(kc0 + KC);
+      if (WASYNC) fetch_async(kc0 + KC, (ch + 1) & 1);
+    }
+    if (WASYNC) {
+      if (ch + 1 < nch)
+        asm volatile("cp.async.wait_group 1;\n" ::);
+      else
+        asm volatile("cp.async.wait_group 0;\n" ::);
+    }
     __syncthreads();
+    const uint8_t* wsb = ws + (WASYNC ? size_t(ch & 1) * TN * wst : 0);
 
     // ---- the dots over this chunk: rows rg·R + r, streams sg·M + 4c + e
     const float* xg = xs + sg * M;
     if (WM == W_Q8) {
-      const uint8_t* wr = ws + size_t(rg * R) * wst + 4 * l;
+      const uint8_t* wr = wsb + size_t(rg * R) * wst + 4 * l;
       const float* dr = ds + rg * R * dst;
       for (int b = 0; b < nb; b++) {
         uint32_t qw[R];
@@ -291,7 +360,7 @@ __global__ void __launch_bounds__(NTH) k_flin(FArgs a) {
         }
 #pragma unroll
         for (int r = 0; r < R; r++) {
-          const uint8_t* wrow = ws + size_t(rg * R + r) * wst;
+          const uint8_t* wrow = wsb + size_t(rg * R + r) * wst;
           float w0, w1;
           if (WM == W_F32) {
             w0 = reinterpret_cast<const float*>(wrow)[c16 + l];
@@ -386,25 +455,22 @@ int fl_ctas(const FArgs& a) {
 }
 
 // Per weight kind and shape. Every configuration gives the same bits (the
-// lanes' order over k is fixed); the largest tile that still makes about an
-// SM's worth of blocks wins, since a product too small to fill the GPU is
-// bound by one block's latency through K.
+// lanes' order over k is fixed), so the choice is by speed, from timings of
+// the path's product shapes on B200: a product too small to fill the GPU is
+// bound by one block's latency through K, so the tile shrinks until the
+// blocks cover the SMs; K of one chunk or less wants square tiles (a tall
+// weight tile is re-read once per stream tile).
 constexpr int kFillCtas = 148;
 template <int WM>
 void fl_dispatch(const FArgs& a, cudaStream_t st) {
-  if (a.M <= 4) {
-    fl_launch<WM, 2, 4, 32, 256>(a, st);  // 64 rows × 4 streams
-  } else if (a.M <= 8) {
-    if (fl_ctas<WM, 1, 8, 16, 256>(a) >= kFillCtas)
-      fl_launch<WM, 1, 8, 16, 256>(a, st);  // 16 rows × 16 streams
-    else
-      fl_launch<WM, 1, 8, 8, 64>(a, st);  // 8 rows × 8 streams
-  } else if (WM == W_Q8 && fl_ctas<WM, 2, 16, 16, 256>(a) >= kFillCtas) {
+  if (a.M <= 8) {
+    fl_launch<WM, 1, 8, 8, 64>(a, st);  // 8 rows × 8 streams
+  } else if (fl_ctas<WM, 2, 16, 16, 256>(a) >= 2 * kFillCtas) {
     fl_launch<WM, 2, 16, 16, 256>(a, st);  // 32 rows × 32 streams
-  } else if (WM != W_Q8 && fl_ctas<WM, 4, 8, 8, 256>(a) >= kFillCtas) {
-    fl_launch<WM, 4, 8, 8, 256>(a, st);  // 32 rows × 32 streams
-  } else if (fl_ctas<WM, 2, 8, 8, 128>(a) >= kFillCtas) {
+  } else if (a.K <= 64) {
     fl_launch<WM, 2, 8, 8, 128>(a, st);  // 16 rows × 16 streams
+  } else if (fl_ctas<WM, 2, 4, 32, 256>(a) >= kFillCtas) {
+    fl_launch<WM, 2, 4, 32, 256>(a, st);  // 64 rows × 4 streams
   } else {
     fl_launch<WM, 1, 8, 8, 64>(a, st);  // 8 rows × 8 streams
   }
@@ -413,9 +479,7 @@ void fl_dispatch(const FArgs& a, cudaStream_t st) {
 template <int WM>
 void fl_init_all() {
   fl_init<WM, 2, 4, 32, 256>();
-  fl_init<WM, 1, 8, 16, 256>();
   fl_init<WM, 2, 16, 16, 256>();
-  fl_init<WM, 4, 8, 8, 256>();
   fl_init<WM, 2, 8, 8, 128>();
   fl_init<WM, 1, 8, 8, 64>();
 }
