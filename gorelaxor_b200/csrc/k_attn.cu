@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(64) k_attn(AttnArgs a) {
   const int half = lane >> 4, l = lane & 15;
   const float q0 = q[l], q1 = q[16 + l], q2 = q[32 + l], q3 = q[48 + l];
   const int nk4 = nk & ~3;
-  constexpr int U = 4;  // key pairs in flight per warp
+  constexpr int U = 8;  // key pairs in flight per warp
   for (int p0 = warp * U; 2 * p0 < nk4; p0 += 2 * U) {
     float k[U][4];
 #pragma unroll
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(64) k_attn(AttnArgs a) {
   // --- values: thread tid owns output value tid, chain over j in order ---
   float o = 0.f;
   const float* vp = V + tid;
-  constexpr int UV = 8;
+  constexpr int UV = 16;
   int j = 0;
   for (; j + UV <= nk; j += UV) {
     float v[UV];
