@@ -161,52 +161,82 @@ __global__ void __launch_bounds__(256) k_tdt_lin(TdtArgs a, TLin t, int parity) 
         const int tr = i / cpr, c = i - tr * cpr;
         cp16t(sw + (size_t(in) * TROWS + tr) * ws + c * 16, W.q + size_t(grow(tr)) * K + c * 16);
       }
-      for (int i = threadIdx.x; i < nrows * nb; i += blockDim.x) {
-        const int tr = i / nb, b = i - tr * nb;
-        sd[(size_t(in) * TROWS + tr) * nb + b] = W.d[size_t(grow(tr)) * nb + b];
+      // scales: every load of the tile issued before the first store
+      constexpr int SI = (TROWS * (1024 / QK) + 255) / 256;
+      uint16_t dv[SI];
+#pragma unroll
+      for (int u = 0; u < SI; u++) {
+        const int i = threadIdx.x + u * 256, tr = i / nb, b = i - tr * nb;
+        if (i < nrows * nb) dv[u] = W.d[size_t(grow(tr)) * nb + b];
+      }
+#pragma unroll
+      for (int u = 0; u < SI; u++) {
+        const int i = threadIdx.x + u * 256, tr = i / nb, b = i - tr * nb;
+        if (i < nrows * nb) sd[(size_t(in) * TROWS + tr) * nb + b] = dv[u];
       }
     }
     asm volatile("cp.async.commit_group;\n" ::);
   }
   __syncthreads();  // s_stream
 
-  // ---- the streams' inputs, stream-minor (four streams per 16-byte store)
+  // ---- the streams' inputs, stream-minor: an item is four consecutive k of
+  // one stream (16-byte loads along the stream's row); BATCH items' loads
+  // are in flight before the first is stored.
+  constexpr int BATCH = 8;
+  const int k4n = K / 4, items = TM * k4n;
   for (int in = 0; in < NIN; in++) {
     float* dst = sx + size_t(in) * TM * K;
-    for (int i = threadIdx.x; i < K * (TM / 4); i += blockDim.x) {
-      const int k = i % K, q4 = i / K;
-      float v[4];
+    for (int i0 = 0; i0 < items; i0 += BATCH * 256) {
+      float4 v[BATCH], e[BATCH];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int m = 4 * q4 + j, s = s_stream[m];
-        float x = 0.f;
-        if (s >= 0) {
-          const int cur = a.cur[s];
-          if (MODE == T_LSTM) {
-            if (in == 0) {
-              if (layer == 0) {
-                const int last = a.last[s];
-                x = last >= 0 && last != a.blank ? a.embed[size_t(last) * a.H + k] : 0.f;
-              } else {
-                x = a.h[((size_t(cur ^ 1) * a.layers + layer - 1) * a.n + s) * a.H + k];
-              }
+      for (int u = 0; u < BATCH; u++) {
+        const int i = i0 + threadIdx.x + u * 256;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        e[u] = v[u];
+        if (i >= items) continue;
+        const int m = i / k4n, k = 4 * (i - m * k4n), s = s_stream[m];
+        if (s < 0) continue;
+        const int cur = a.cur[s];
+        const float* src = nullptr;
+        if (MODE == T_LSTM) {
+          if (in == 0) {
+            if (layer == 0) {
+              const int last = a.last[s];
+              if (last >= 0 && last != a.blank) src = a.embed + size_t(last) * a.H;
             } else {
-              x = a.h[((size_t(cur) * a.layers + layer) * a.n + s) * a.H + k];
+              src = a.h + ((size_t(cur ^ 1) * a.layers + layer - 1) * a.n + s) * a.H;
             }
-          } else if (MODE == T_PROJ) {
-            x = a.h[((size_t(cur ^ 1) * a.layers + a.layers - 1) * a.n + s) * a.H + k];
           } else {
-            const float e = a.enc_proj[(size_t(s) * a.max_t + a.step[s]) * a.J + k];
-            float v = __fadd_rn(e, a.pred_proj[size_t(s) * a.J + k]);
-            if (a.act == 1) v = sigmoid_go(v);
-            else if (a.act == 2) v = tanh32(v);
-            else v = relu_go(v);
-            x = v;
+            src = a.h + ((size_t(cur) * a.layers + layer) * a.n + s) * a.H;
+          }
+        } else if (MODE == T_PROJ) {
+          src = a.h + ((size_t(cur ^ 1) * a.layers + a.layers - 1) * a.n + s) * a.H;
+        } else {
+          src = a.enc_proj + (size_t(s) * a.max_t + a.step[s]) * a.J;
+          e[u] = *reinterpret_cast<const float4*>(a.pred_proj + size_t(s) * a.J + k);
+        }
+        if (src) v[u] = *reinterpret_cast<const float4*>(src + k);
+      }
+#pragma unroll
+      for (int u = 0; u < BATCH; u++) {
+        const int i = i0 + threadIdx.x + u * 256;
+        if (i >= items) continue;
+        const int m = i / k4n, k = 4 * (i - m * k4n);
+        float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        if (MODE == T_JOINT) {
+          const float p[4] = {e[u].x, e[u].y, e[u].z, e[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            float w = __fadd_rn(x[j], p[j]);
+            if (a.act == 1) w = sigmoid_go(w);
+            else if (a.act == 2) w = tanh32(w);
+            else w = relu_go(w);
+            x[j] = s_stream[m] >= 0 ? w : 0.f;
           }
         }
-        v[j] = x;
+#pragma unroll
+        for (int j = 0; j < 4; j++) dst[tx_at(k + j, m)] = x[j];
       }
-      *reinterpret_cast<float4*>(&dst[tx_at(k, 4 * q4)]) = make_float4(v[0], v[1], v[2], v[3]);
     }
   }
   asm volatile("cp.async.wait_all;\n" ::);
