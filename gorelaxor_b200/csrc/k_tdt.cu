@@ -29,8 +29,10 @@ namespace {
 constexpr int TM = 16;       // streams per CTA
 constexpr int TROWS = 32;    // weight rows per CTA (8 warps × 4 groups of 8 lanes)
 
-// x[m][k] at k·TM + 4·((m/4) ^ (k mod 4)) + m mod 4 (as k_flow.cu's sx_at).
-__device__ __forceinline__ int tx_at(int k, int m) { return k * TM + 4 * ((m >> 2) ^ (k & 3)) + (m & 3); }
+// x[m][k] at k·TM + 4·((m/4) ^ ((k/2) mod 4)) + m mod 4: the 16-byte group of
+// streams 4g..4g+3 at the 8 consecutive k of a lane group falls on 8
+// different bank quads, so a group's 16-byte loads are conflict-free.
+__device__ __forceinline__ int tx_at(int k, int m) { return k * TM + 4 * ((m >> 2) ^ ((k >> 1) & 3)) + (m & 3); }
 
 __host__ __device__ constexpr int t_wstride(int K) { return K + 16; }
 
@@ -57,9 +59,9 @@ __device__ __forceinline__ void row_lanes(const int8_t* wr, const uint16_t* sd, 
       f2 X[4][2];
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        const f2* xp = reinterpret_cast<const f2*>(&sx[tx_at(k + 8 * i, 4 * g4)]);
-        X[i][0] = xp[0];
-        X[i][1] = xp[1];
+        const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(&sx[tx_at(k + 8 * i, 4 * g4)]);
+        X[i][0] = v.x;
+        X[i][1] = v.y;
       }
 #pragma unroll
       for (int h = 0; h < 2; h++) {
