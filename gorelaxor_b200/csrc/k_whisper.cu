@@ -195,22 +195,36 @@ __global__ void __launch_bounds__(256) k_wcross(WRows r, const float* q, const f
   const int lane = threadIdx.x & 31, l16 = threadIdx.x & 15, grp = threadIdx.x >> 4;
   const int ctx4 = ctx & ~3;
   float mx = NINF;
-#pragma unroll 4
-  for (int j0 = 0; j0 < ctx4; j0 += 16) {
-    const int j = j0 + grp;
-    float a = 0.f;
-    if (j < ctx4) {
-      const float* kj = kb + (size_t)j * hd;
+  // UK keys' rows are loaded before the first of them is used (bytes in
+  // flight for the HBM stream); each key's dot is unchanged.
+  constexpr int UK = 8;
+  for (int j0 = 0; j0 < ctx4; j0 += 16 * UK) {
+    float kv[UK][4];
 #pragma unroll
-      for (int c = 0; c < 4; c++) a = __fmaf_rn(qh[16 * c + l16], kj[16 * c + l16], a);
+    for (int u = 0; u < UK; u++) {
+      const int j = j0 + 16 * u + grp;
+      if (j < ctx4) {
+        const float* kj = kb + (size_t)j * hd;
+#pragma unroll
+        for (int c = 0; c < 4; c++) kv[u][c] = kj[16 * c + l16];
+      }
     }
-    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));  // lanes l < 8: acc0_l + acc1_l
-    float x = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
-    float y = __fadd_rn(x, __shfl_down_sync(0xffffffffu, x, 1));
-    const float z = __fadd_rn(y, __shfl_down_sync(0xffffffffu, y, 2));
-    if (l16 == 0 && j < ctx4) {
-      sc[j] = z;
-      mx = fmaxf(mx, z);
+#pragma unroll
+    for (int u = 0; u < UK; u++) {
+      const int j = j0 + 16 * u + grp;
+      float a = 0.f;
+      if (j < ctx4) {
+#pragma unroll
+        for (int c = 0; c < 4; c++) a = __fmaf_rn(qh[16 * c + l16], kv[u][c], a);
+      }
+      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));  // lanes l < 8: acc0_l + acc1_l
+      float x = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
+      float y = __fadd_rn(x, __shfl_down_sync(0xffffffffu, x, 1));
+      const float z = __fadd_rn(y, __shfl_down_sync(0xffffffffu, y, 2));
+      if (l16 == 0 && j < ctx4) {
+        sc[j] = z;
+        mx = fmaxf(mx, z);
+      }
     }
     (void)lane;
   }
@@ -234,11 +248,25 @@ __global__ void __launch_bounds__(256) k_wcross(WRows r, const float* q, const f
   // o[d] for d = grp + 16i: the 16 lanes chain over ctx&~15 in steps of 16
   const int cf = ctx & ~15;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-  for (int c = 0; c < cf; c += 16) {
-    const float p = sc[c + l16];
+  constexpr int UV = 8;
+  for (int c0 = 0; c0 < cf; c0 += 16 * UV) {
+    float vv[UV][4];
 #pragma unroll
-    for (int i = 0; i < 4; i++) acc[i] = __fmaf_rn(p, vb[(size_t)(grp + 16 * i) * ctx + c + l16], acc[i]);
+    for (int u = 0; u < UV; u++) {
+      const int c = c0 + 16 * u;
+      if (c < cf)
+#pragma unroll
+        for (int i = 0; i < 4; i++) vv[u][i] = vb[(size_t)(grp + 16 * i) * ctx + c + l16];
+    }
+#pragma unroll
+    for (int u = 0; u < UV; u++) {
+      const int c = c0 + 16 * u;
+      if (c < cf) {
+        const float p = sc[c + l16];
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[i] = __fmaf_rn(p, vv[u][i], acc[i]);
+      }
+    }
   }
 #pragma unroll
   for (int i = 0; i < 4; i++) {
