@@ -177,6 +177,7 @@ class FlowLMConfig:
     flow_dim: int = 512
     flow_depth: int = 1
     decode_steps: int = 1
+    text_vocab: int = 4000  # text tokens; lm.embed has one row more (model.go:246)
     temperature: float = 0.3
     max_period: float = 10000.0
     sha: str = "synthetic-flowlm-seed0"
@@ -233,6 +234,9 @@ def flowlm_tensors(cfg: FlowLMConfig, seed: int = 0) -> dict:
     t["flow.final.ada.bias"] = _n(rng, 2 * fd, 0.02)
     t["flow.final.out.weight"] = _n(rng, (ld, fd), 1.0 / np.sqrt(fd))
     t["flow.final.out.bias"] = _n(rng, ld, 0.02)
+    # the text embedding, drawn from its own generator so that the tensors
+    # above do not depend on it
+    t["lm.embed"] = rand_q8(np.random.default_rng(seed + 7919), cfg.text_vocab + 1, d)
     return t
 
 

@@ -83,6 +83,7 @@ struct FlowLM {
   std::vector<FlowLMLayer> layers;
   std::vector<float> freqs;
   Weight input, eosw, cond, finput, final_ada, fout;
+  Weight embed;  // lm.embed [tokens + 1][d] (rows 0 when the model has none)
   const float *bos, *outw, *outb, *mean, *stdv, *condb, *finputb, *final_adab, *foutb;
   float eosb;
   TimeEmbed time[2];
@@ -208,6 +209,144 @@ inline void transformer_step(const FlowLM& m, float* x, Stream& st, float* lm_ou
   }
   st.pos += 1;
   layer_norm_pt(lm_out, x, 1, d, m.outw, m.outb, 1e-5);
+}
+
+// kern.MatMulF32 (kern.go:205-211 → gemm.go:116-185) with a float32 B of
+// row stride ldb, no bias: up to 16 rows of A take gemvRows (dotF32x4 per
+// group of four B rows, dotF32Go for the rest); more rows take the packed
+// kernel for the first m/6·6 (C starts at 0 and each 256-deep pass adds
+// its fused chain, k6x16avx) and gemvRows for the others.
+inline void matmul_kern_f32(float* c, int ldc, const float* a, int lda, const float* b, int ldb, int m, int n, int k) {
+  auto gemv_row = [&](float* y, const float* x) {
+    for (int j = 0; j < n; j += 4) {
+      if (j + 4 <= n) {
+        float o4[4];
+        dot_f32x4(x, b + long(j) * ldb, ldb, k, o4);
+        for (int r = 0; r < 4; r++) y[j + r] = o4[r];
+      } else {
+        for (int jj = j; jj < n; jj++) y[jj] = dot_f32_go(x, b + long(jj) * ldb, k);
+      }
+    }
+  };
+  if (m <= 16) {
+    for (int i = 0; i < m; i++) gemv_row(c + long(i) * ldc, a + long(i) * lda);
+    return;
+  }
+  const int mfull = m / 6 * 6;
+  for (int i = 0; i < mfull; i++)
+    for (int j = 0; j < n; j++) c[long(i) * ldc + j] = 0.f;
+  for (int k0 = 0; k0 < k; k0 += 256) {
+    const int kn = std::min(256, k - k0);
+    for (int i = 0; i < mfull; i++)
+      for (int j = 0; j < n; j++) {
+        float acc = 0.f;
+        for (int kk = 0; kk < kn; kk++) acc = std::fma(a[long(i) * lda + k0 + kk], b[long(j) * ldb + k0 + kk], acc);
+        c[long(i) * ldc + j] = c[long(i) * ldc + j] + acc;
+      }
+  }
+  for (int i = mfull; i < m; i++) gemv_row(c + long(i) * ldc, a + long(i) * lda);
+}
+
+// transformer.attend for T queries at positions pos0.. (nn.go:200-243, no
+// context window): per head the scores of all T queries against the nk =
+// pos0 + T keys are one MatMulF32; each query's visible scores are scaled,
+// softmaxed (expSub, × 1/Σ) and the rest cleared; the values are added key
+// by key (AddScaled) for T < 4, else one MatMulF32 against the head's
+// transposed values.
+inline void attend_rows(float* out, const float* qkv, int T, const float* kc, const float* vc, int pos0, int d,
+                        int heads) {
+  const int hd = d / heads, nk = pos0 + T;
+  const float scale = float(1 / std::sqrt(double(hd)));
+  std::vector<float> sc(size_t(T) * nk), vt(size_t(hd) * nk);
+  for (int h = 0; h < heads; h++) {
+    matmul_kern_f32(sc.data(), nk, qkv + h * hd, 3 * d, kc + h * hd, d, T, nk, hd);
+    for (int r = 0; r < T; r++) {
+      const int p = pos0 + r;
+      float* row = sc.data() + size_t(r) * nk;
+      float mx = -INFINITY;
+      for (int j = 0; j <= p; j++) {
+        row[j] *= scale;
+        mx = std::max(mx, row[j]);
+      }
+      const float inv = 1.f / expsub_vec(row, p + 1, mx);
+      for (int j = 0; j <= p; j++) row[j] *= inv;
+      for (int j = p + 1; j < nk; j++) row[j] = 0.f;
+    }
+    if (T < 4) {
+      for (int r = 0; r < T; r++) {
+        float* o = out + long(r) * d + h * hd;
+        for (int i = 0; i < hd; i++) o[i] = 0.f;
+        for (int j = 0; j < nk; j++) {
+          const float w = sc[size_t(r) * nk + j];
+          if (w != 0) {
+            const float* vj = vc + long(j) * d + h * hd;
+            for (int i = 0; i < hd; i++) o[i] = std::fma(w, vj[i], o[i]);
+          }
+        }
+      }
+      continue;
+    }
+    for (int j = 0; j < nk; j++)
+      for (int i = 0; i < hd; i++) vt[size_t(i) * nk + j] = vc[long(j) * d + h * hd + i];
+    matmul_kern_f32(out + h * hd, d, sc.data(), nk, vt.data(), nk, T, hd, nk);
+  }
+}
+
+// transformer.forward for T rows (nn.go:142-182, no layer scale, context
+// 0): every layer's products take all T rows at once (int8 path for T ≥ 2),
+// RoPE at positions pos.., the T keys and values appended before
+// attending. Then out_norm of the last row (lm.go:164-170) into lm_out.
+inline void transformer_rows(const FlowLM& m, float* x, int T, Stream& st, float* lm_out) {
+  const int d = m.d;
+  std::vector<float> h(size_t(T) * d), qkv(size_t(T) * 3 * d), att(size_t(T) * d), ff(size_t(T) * m.ff);
+  for (size_t li = 0; li < m.layers.size(); li++) {
+    const FlowLMLayer& l = m.layers[li];
+    layer_norm_pt(h.data(), x, T, d, l.norm1w, l.norm1b, 1e-5);
+    linear(qkv.data(), h.data(), T, l.qkv, nullptr);
+    for (int r = 0; r < T; r++) {
+      float* row = qkv.data() + size_t(r) * 3 * d;
+      apply_rope(row, m.heads, m.freqs, st.pos + r);
+      apply_rope(row + d, m.heads, m.freqs, st.pos + r);
+    }
+    for (int r = 0; r < T; r++) {
+      const float* row = qkv.data() + size_t(r) * 3 * d;
+      st.k[li].insert(st.k[li].end(), row + d, row + 2 * d);
+      st.v[li].insert(st.v[li].end(), row + 2 * d, row + 3 * d);
+    }
+    attend_rows(att.data(), qkv.data(), T, st.k[li].data(), st.v[li].data(), st.pos, d, m.heads);
+    linear(h.data(), att.data(), T, l.out, nullptr);
+    add_to(x, h.data(), T * d);
+    layer_norm_pt(h.data(), x, T, d, l.norm2w, l.norm2b, 1e-5);
+    linear(ff.data(), h.data(), T, l.ff1, nullptr);
+    gelu_vec(ff.data(), T * m.ff);
+    linear(h.data(), ff.data(), T, l.ff2, nullptr);
+    add_to(x, h.data(), T * d);
+  }
+  st.pos += T;
+  if (lm_out) layer_norm_pt(lm_out, x + size_t(T - 1) * d, 1, d, m.outw, m.outb, 1e-5);
+}
+
+// Weight.Row for the embedding (kern.go:116-122): float32 rows are copied,
+// Q8_0 rows dequantised (dequantQ8: float(q)·d, exact).
+inline void weight_row(const Weight& w, int j, float* dst) {
+  if (w.type == Q8_0) {
+    const int nb = w.cols / QK;
+    const uint8_t* blk = w.q + long(j) * nb * Q8BYTES;
+    for (int b = 0; b < nb; b++, blk += Q8BYTES) {
+      const float dd = f16_to_f32(uint16_t(blk[0] | blk[1] << 8));
+      for (int i = 0; i < QK; i++) dst[b * QK + i] = float(int8_t(blk[2 + i])) * dd;
+    }
+    return;
+  }
+  for (int i = 0; i < w.cols; i++) dst[i] = w.f[long(j) * w.cols + i];
+}
+
+// flowLM.text, pockettts/lm.go:172-181: the tokens' embedding rows through
+// the transformer; lm_out gets the output at the last token.
+inline void flowlm_text(const FlowLM& m, const int* ids, int T, Stream& st, float* lm_out) {
+  std::vector<float> x(size_t(T) * m.d);
+  for (int i = 0; i < T; i++) weight_row(m.embed, ids[i], x.data() + size_t(i) * m.d);
+  transformer_rows(m, x.data(), T, st, lm_out);
 }
 
 // flowLM.step, pockettts/lm.go:185-195. latent == nullptr is the first

@@ -191,6 +191,7 @@ int orc_flowlm_ready(void* h, int decode_steps) {
   m.final_adab = get_v(o, "flow.final.ada.bias");
   m.fout = get_w(o, "flow.final.out.weight");
   m.foutb = get_v(o, "flow.final.out.bias");
+  if (o->w.count("lm.embed")) m.embed = get_w(o, "lm.embed");  // optional: text prefill only
   if (!o->err.empty()) return -1;
   o->decode_steps = decode_steps;
   o->tc = time_conds(m, decode_steps);
@@ -225,6 +226,18 @@ void* orc_stream_new(void* h, int n, const float* kv) {
 }
 
 void orc_stream_free(void* s) { delete (Stream*)s; }
+
+// flowLM.text (lm.go:172-181) on one stream: T token ids appended to its
+// caches; lm_out (may be NULL) gets the output at the last token. Returns
+// -1 if the model has no lm.embed or an id is out of range.
+int orc_flowlm_text(void* h, void* sp, const int* ids, int T, float* lm_out) {
+  auto* o = (OFlowLM*)h;
+  if (o->m.embed.rows == 0 || T < 1) return -1;
+  for (int i = 0; i < T; i++)
+    if (ids[i] < 0 || ids[i] >= o->m.embed.rows) return -1;
+  flowlm_text(o->m, ids, T, *(Stream*)sp, lm_out);
+  return 0;
+}
 int orc_stream_pos(void* s) { return ((Stream*)s)->pos; }
 
 // One frame of speakChunk's loop (speak.go:146-174) with the noise given:

@@ -55,6 +55,7 @@ def lib():
             "orc_stream_new": (P, [P, I, P]),
             "orc_stream_free": (None, [P]),
             "orc_stream_pos": (I, [P]),
+            "orc_flowlm_text": (I, [P, P, P, I, P]),
             "orc_flowlm_frame": (F, [P, P, P, P, P, P, P, P]),
             "orc_flowlm_run": (None, [P, I, P, I, P, P, P, P, I]),
             "orc_tdt_new": (P, [I, I, I, I, I, I, I, I, P, I]),
@@ -189,6 +190,15 @@ class FlowLM:
         """kv: [layers][2][positions][d]."""
         kv = np.ascontiguousarray(kv, np.float32)
         return Stream(lib().orc_stream_new(self.h, kv.shape[2], p(kv)))
+
+    def text(self, st: "Stream", ids):
+        """flowLM.text (lm.go:172-181): the token ids through the
+        transformer on st; returns the output at the last token."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty(self.cfg.d, np.float32)
+        if lib().orc_flowlm_text(self.h, st.h, p(ids), len(ids), p(out)) != 0:
+            raise ValueError("orc_flowlm_text: no lm.embed or a token id out of range")
+        return out
 
     def frame(self, st: "Stream", latent, noise, trace=False):
         c = self.cfg

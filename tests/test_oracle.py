@@ -235,3 +235,74 @@ def test_flowlm_frame_against_numpy_model():
         assert rel(r["latent"], lat) < 0.02
         assert abs(r["eos"] - eos) < 0.02 * max(1, abs(eos))
         latent = r["latent"]
+
+
+def _np_text(cfg, t, kvs, ids, pos0):
+    """flowLM.text in float64 numpy: the token rows through the transformer
+    with causal attention over the voice prefill and the earlier tokens, the
+    int8 path's activation rounding per row; the output at the last token."""
+    D = lambda a: np.asarray(a, np.float64)
+    W = lambda name: D(synth.q8_dequant(t[name])) if isinstance(t[name], synth.Q8) else D(t[name])
+
+    def q8round(x):
+        out = np.empty_like(x)
+        for b in range(0, x.size, 32):
+            blk = x[b:b + 32]
+            amax = np.abs(blk).max()
+            out[b:b + 32] = np.rint(blk * 127 / amax) * amax / 127 if amax else 0
+        return out
+
+    def ln(x, w, b, eps):
+        return (x - x.mean()) / np.sqrt(x.var() + eps) * w + b
+
+    hd = cfg.d // cfg.heads
+
+    def rope(v, pos):
+        f = np.exp(-np.log(cfg.max_period) * 2 / hd * np.arange(hd // 2))
+        a = f * pos
+        v = v.reshape(cfg.heads, hd // 2, 2).copy()
+        r, i = v[..., 0].copy(), v[..., 1].copy()
+        v[..., 0], v[..., 1] = r * np.cos(a) - i * np.sin(a), r * np.sin(a) + i * np.cos(a)
+        return v.reshape(-1)
+
+    gelu = lambda v: 0.5 * v * (1 + np.tanh(np.sqrt(2 / np.pi) * v * (1 + 0.044715 * v * v)))
+    E = W("lm.embed")
+    xs = [E[i].copy() for i in ids]
+    T = len(ids)
+    for l in range(cfg.layers):
+        p = f"lm.blk.{l}."
+        qs, K, V = [], D(kvs[l][0]), D(kvs[l][1])
+        for r in range(T):
+            qkv = W(p + "attn_qkv.weight") @ q8round(ln(xs[r], D(t[p + "norm1.weight"]), D(t[p + "norm1.bias"]), 1e-5))
+            qs.append(rope(qkv[:cfg.d], pos0 + r))
+            K = np.vstack([K, rope(qkv[cfg.d:2 * cfg.d], pos0 + r)])
+            V = np.vstack([V, qkv[2 * cfg.d:]])
+        for r in range(T):
+            nk = pos0 + r + 1
+            att = np.zeros(cfg.d)
+            for hh in range(cfg.heads):
+                sl = slice(hh * hd, (hh + 1) * hd)
+                s = K[:nk, sl] @ qs[r][sl] / np.sqrt(hd)
+                e = np.exp(s - s.max())
+                att[sl] = (e / e.sum()) @ V[:nk, sl]
+            xs[r] = xs[r] + W(p + "attn_out.weight") @ q8round(att)
+            h = ln(xs[r], D(t[p + "norm2.weight"]), D(t[p + "norm2.bias"]), 1e-5)
+            xs[r] = xs[r] + W(p + "ff2.weight") @ q8round(gelu(W(p + "ff1.weight") @ q8round(h)))
+    return ln(xs[-1], D(t["lm.out_norm.weight"]), D(t["lm.out_norm.bias"]), 1e-5)
+
+
+@pytest.mark.parametrize("T", [1, 3, 5, 17])
+def test_flowlm_text_against_numpy_model(T):
+    """flowLM.text restated (T rows through the transformer, attend's T > 1
+    products) follows the model: the output at the last token against an
+    independent float64 numpy model within 2% RMS."""
+    cfg = synth.FlowLMConfig(**SMALL)
+    t = synth.flowlm_tensors(cfg, 0)
+    om = orc.FlowLM(cfg, t)
+    kv = voice_kv(cfg, 6, 1)
+    st = om.stream(kv)
+    ids = [(7 * i + 3) % cfg.text_vocab for i in range(T)]
+    got = om.text(st, ids)
+    assert st.pos == 6 + T
+    want = _np_text(cfg, t, [(kv[l, 0], kv[l, 1]) for l in range(cfg.layers)], ids, 6)
+    assert np.sqrt(((got - want) ** 2).sum() / (want ** 2).sum()) < 0.02
