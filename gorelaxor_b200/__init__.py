@@ -66,6 +66,7 @@ def _sig(lib):
         "grx_streams_create": (I, [P, I, P, I, PP]),
         "grx_streams_free": (None, [P]),
         "grx_streams_reset": (I, [P]),
+        "grx_streams_text": (I, [P, P, P, P]),
         "grx_streams_step": (I, [P, P, P, P, P, P]),
         "grx_streams_run_device": (I, [P, I, P, P, P]),
         "grx_streams_sync": (I, [P]),
@@ -293,6 +294,20 @@ class Streams:
 
     def reset(self):
         _check(lib().grx_streams_reset(self._h))
+
+    def text(self, ids: list) -> np.ndarray:
+        """flowLM.text for every stream (lm.go:172-181): ids[i] is stream i's
+        list of token ids (may be empty). Returns [n][d], out_norm at each
+        stream's last token (zeros for streams without tokens)."""
+        if len(ids) != self.n:
+            raise ValueError(f"text: {len(ids)} token lists for {self.n} streams")
+        off = np.zeros(self.n + 1, np.int32)
+        off[1:] = np.cumsum([len(t) for t in ids])
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(t, np.int32) for t in ids]) if off[-1] else
+                                    np.zeros(1, np.int32), np.int32)
+        out = np.zeros((self.n, self.model.d), np.float32)
+        _check(lib().grx_streams_text(self._h, _ptr(flat), _ptr(off), _ptr(out)))
+        return out
 
     def step(self, noise: np.ndarray, want_lm_out: bool = False):
         """One frame for every stream: returns (latent, eos, scaled, lm_out)."""

@@ -71,6 +71,8 @@ struct grx_flowlm {
   float *condb = nullptr, *fin = nullptr, *finb = nullptr, *fadab = nullptr, *fout = nullptr, *foutb = nullptr;
   float* tc = nullptr;  // [steps][fd] time conditions
   std::vector<float> freqs;
+  float* embed = nullptr;  // lm.embed widened to float32 [embed_rows][d], if the file has it
+  int embed_rows = 0;
 };
 
 struct grx_voice {
@@ -682,6 +684,16 @@ int grx_flowlm_load(const void* bytes, size_t len, int device, grx_flowlm** out)
   m->condb = vec("flow.cond.bias", fd);
   m->fin = f32m("flow.input.weight", fd, ld);
   m->finb = vec("flow.input.bias", fd);
+  if (err.empty() && f.has("lm.embed")) {  // the text embedding (model.go:246): text prefill only
+    int64_t r = 0, c = 0;
+    std::vector<float> v;
+    if (!f.matrix_shape("lm.embed", &r, &c) || c != d || r < 1 || r > (1 << 24) || !f.float32("lm.embed", v)) {
+      err = "pockettts: lm.embed is not a [tokens + 1][" + std::to_string(d) + "] matrix";
+    } else {
+      m->embed = m->ar.upload(v.data(), v.size(), &rc);
+      m->embed_rows = int(r);
+    }
+  }
   DQ8 tfc1[2], tfc2[2];
   float *tb1[2], *tb2[2], *alpha[2];
   std::vector<float> freqs[2];
@@ -845,6 +857,158 @@ int grx_streams_reset(grx_streams* s) {
     CK(cudaMemcpyAsync(s->lat + size_t(i) * m->ldim, m->bos, sizeof(float) * size_t(m->ldim), cudaMemcpyDeviceToDevice,
                        s->st));
   CK(cudaStreamSynchronize(s->st));
+  return GRX_OK;
+}
+
+// flowLM.text (lm.go:172-181) for the streams of one set or part: stream i's
+// tokens are ids[off[i] .. off[i+1]) (off relative to the caller's array).
+// All streams' token rows go through each layer together; rows r of stream
+// i sit at positions pos[i] + r and write its cache.
+static int streams_text_one(grx_streams* q, const int* ids, const int* off, float* out) {
+  grx_flowlm* m = q->m;
+  const int n = q->n, d = m->d, ff = m->ff;
+  std::vector<int> pos((size_t(n)));
+  CK(cudaMemcpyAsync(pos.data(), q->pos, sizeof(int) * size_t(n), cudaMemcpyDeviceToHost, q->st));
+  CK(cudaStreamSynchronize(q->st));
+  std::vector<int> row_id, row_slot, row_pos, c_row0, c_T, c_pos0, c_slot, last_row;
+  int tmax = 0;
+  for (int i = 0; i < n; i++) {
+    const int T = off[i + 1] - off[i];
+    if (T == 0) continue;
+    if (pos[size_t(i)] + T > q->cap)
+      return fail(GRX_ERANGE, "grx_streams_text: stream " + std::to_string(q->row0 + i) + " holds " +
+                                  std::to_string(pos[size_t(i)]) + " positions; " + std::to_string(T) +
+                                  " tokens pass the " + std::to_string(q->cap) + " it was made for");
+    c_row0.push_back(int(row_id.size()));
+    c_T.push_back(T);
+    c_pos0.push_back(pos[size_t(i)]);
+    c_slot.push_back(i);
+    for (int r = 0; r < T; r++) {
+      row_id.push_back(ids[off[i] - off[0] + r]);
+      row_slot.push_back(i);
+      row_pos.push_back(pos[size_t(i)] + r);
+    }
+    last_row.push_back(int(row_id.size()) - 1);
+    tmax = std::max(tmax, T);
+  }
+  const int R = int(row_id.size()), ns = int(c_T.size());
+  if (R == 0) return GRX_OK;
+  int rc = 0;
+  Arena ar;
+  ar.dev = q->ar.dev;
+  float* x = ar.alloc<float>(size_t(R) * d, &rc);
+  float* qb = ar.alloc<float>(size_t(R) * d, &rc);
+  int8_t* xq = ar.alloc<int8_t>(size_t(R) * d, &rc);
+  float2* xs = ar.alloc<float2>(size_t(R) * (d / 32), &rc);  // a scale per 32-value block
+  int8_t* fq = ar.alloc<int8_t>(size_t(R) * ff, &rc);
+  float2* fs = ar.alloc<float2>(size_t(R) * (ff / 32), &rc);
+  int* dint = ar.alloc<int>(size_t(3) * R + size_t(5) * ns, &rc);
+  float* lo = out ? ar.alloc<float>(size_t(ns) * d, &rc) : nullptr;
+  float* lrow = out ? ar.alloc<float>(size_t(ns) * d, &rc) : nullptr;
+  if (rc) return rc;
+  std::vector<int> hint;
+  for (const auto* v : {&row_id, &row_slot, &row_pos, &c_row0, &c_T, &c_pos0, &c_slot, &last_row})
+    hint.insert(hint.end(), v->begin(), v->end());
+  CK(cudaMemcpyAsync(dint, hint.data(), sizeof(int) * hint.size(), cudaMemcpyHostToDevice, q->st));
+  const int *d_id = dint, *d_slot = dint + R, *d_pos = dint + 2 * R, *d_row0 = dint + 3 * R, *d_T = d_row0 + ns,
+            *d_pos0 = d_T + ns, *d_cslot = d_pos0 + ns, *d_last = d_cslot + ns;
+  cudaStream_t st = q->st;
+  launch_embed_rows(x, m->embed, d_id, R, d, st);
+  for (int l = 0; l < m->L; l++) {
+    const Layer& ly = m->layers[size_t(l)];
+    LnArgs ln;
+    ln.x = x;
+    ln.w = ly.n1w;
+    ln.b = ly.n1b;
+    ln.eps = 1e-5;
+    ln.mode = LN_Q8;
+    ln.q8 = xq;
+    ln.q8s = xs;
+    launch_ln(ln, R, d, st);
+    EpiArgs e;
+    e.epi = EPI_ROPE_KV;
+    e.kv.q = qb;
+    e.kv.kv = q->kv;
+    e.kv.pos = d_pos;
+    e.kv.row_stream = d_slot;
+    e.kv.rope = q->rope;
+    e.kv.layer = l;
+    e.kv.layers = m->L;
+    e.kv.heads = m->heads;
+    e.kv.cap = q->cap;
+    e.kv.d = d;
+    launch_q8_product(xq, xs, R, ly.qkv, e, st);
+    AttnRowsArgs at;
+    at.q = qb;
+    at.kv = q->kv;
+    at.row0 = d_row0;
+    at.T = d_T;
+    at.pos0 = d_pos0;
+    at.slot = d_cslot;
+    at.q8 = xq;
+    at.q8s = xs;
+    at.layer = l;
+    at.layers = m->L;
+    at.heads = m->heads;
+    at.cap = q->cap;
+    at.d = d;
+    launch_attn_rows(at, ns, tmax, st);
+    EpiArgs r;
+    r.epi = EPI_RESID;
+    r.y = x;
+    r.ldy = d;
+    launch_q8_product(xq, xs, R, ly.out, r, st);
+    ln.w = ly.n2w;
+    ln.b = ly.n2b;
+    launch_ln(ln, R, d, st);
+    EpiArgs g;
+    g.epi = EPI_GELU_Q8;
+    g.q8 = fq;
+    g.q8s = fs;
+    launch_q8_product(xq, xs, R, ly.ff1, g, st);
+    launch_q8_product(fq, fs, R, ly.ff2, r, st);
+  }
+  for (size_t i = 0; i < c_T.size(); i++) pos[size_t(c_slot[i])] += c_T[i];
+  CK(cudaMemcpyAsync(q->pos, pos.data(), sizeof(int) * size_t(n), cudaMemcpyHostToDevice, st));
+  if (out) {
+    // out_norm of each stream's last token row (lm.go:164-170)
+    launch_embed_rows(lrow, x, d_last, ns, d, st);
+    LnArgs on;
+    on.x = lrow;
+    on.w = m->outw;
+    on.b = m->outb;
+    on.eps = 1e-5;
+    on.mode = LN_F32;
+    on.y = lo;
+    launch_ln(on, ns, d, st);
+    std::vector<float> h((size_t(ns) * d));
+    CK(cudaMemcpyAsync(h.data(), lo, sizeof(float) * h.size(), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    for (int i = 0; i < ns; i++)
+      std::memcpy(out + size_t(c_slot[size_t(i)]) * d, h.data() + size_t(i) * d, sizeof(float) * size_t(d));
+  }
+  CK(cudaStreamSynchronize(st));
+  CK(cudaGetLastError());
+  return GRX_OK;
+}
+
+int grx_streams_text(grx_streams* s, const int* ids, const int* offsets, float* out) {
+  if (!s || !offsets || (!ids && offsets[s->n] > 0)) return fail(GRX_EINVAL, "grx_streams_text: null argument");
+  grx_flowlm* m = s->m;
+  if (!m->embed) return fail(GRX_EINVAL, "grx_streams_text: the model has no lm.embed");
+  if (offsets[0] != 0) return fail(GRX_EINVAL, "grx_streams_text: offsets[0] must be 0");
+  for (int i = 0; i < s->n; i++)
+    if (offsets[i + 1] < offsets[i]) return fail(GRX_EINVAL, "grx_streams_text: offsets must not decrease");
+  for (int j = 0; j < offsets[s->n]; j++)
+    if (ids[j] < 0 || ids[j] >= m->embed_rows)
+      return fail(GRX_EINVAL, "grx_streams_text: token id " + std::to_string(ids[j]) + " outside the " +
+                                  std::to_string(m->embed_rows) + "-row embedding");
+  CK(cudaSetDevice(s->ar.dev));
+  if (s->parts.empty()) return streams_text_one(s, ids, offsets, out);
+  for (auto& p : s->parts) {
+    int rc = streams_text_one(p.get(), ids + offsets[p->row0], offsets + p->row0, out ? out + size_t(p->row0) * m->d : nullptr);
+    if (rc) return rc;
+  }
   return GRX_OK;
 }
 

@@ -157,7 +157,183 @@ __global__ void __launch_bounds__(64) k_attn(AttnArgs a) {
   }
 }
 
+// dot4f32avx of two 64-value rows (kernels_amd64.s:157-204): lane l's two
+// fused chains over elements 16c+l and 16c+8+l, added, then HSUM.
+__device__ __forceinline__ float dot4_64(const float* x, const float* y) {
+  float a[8], b[8];
+#pragma unroll
+  for (int l = 0; l < 8; l++) a[l] = b[l] = 0.f;
+#pragma unroll
+  for (int c = 0; c < 64; c += 16)
+#pragma unroll
+    for (int l = 0; l < 8; l++) {
+      a[l] = __fmaf_rn(x[c + l], y[c + l], a[l]);
+      b[l] = __fmaf_rn(x[c + 8 + l], y[c + 8 + l], b[l]);
+    }
+#pragma unroll
+  for (int l = 0; l < 8; l++) a[l] = __fadd_rn(a[l], b[l]);
+  return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[1], a[5])), __fadd_rn(__fadd_rn(a[2], a[6]), __fadd_rn(a[3], a[7])));
+}
+
+// dotF32Go (gemm.go:294-308) of n values: four strided unfused sums.
+template <class X, class Y>
+__device__ __forceinline__ float dot_go(X x, Y y, int n) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int i = 0;
+  for (; i + 4 <= n; i += 4) {
+    s0 = __fadd_rn(s0, __fmul_rn(x(i), y(i)));
+    s1 = __fadd_rn(s1, __fmul_rn(x(i + 1), y(i + 1)));
+    s2 = __fadd_rn(s2, __fmul_rn(x(i + 2), y(i + 2)));
+    s3 = __fadd_rn(s3, __fmul_rn(x(i + 3), y(i + 3)));
+  }
+  for (; i < n; i++) s0 = __fadd_rn(s0, __fmul_rn(x(i), y(i)));
+  return __fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3);
+}
+
+// transformer.attend for T queries of one stream (nn.go:200-243, T > 1),
+// one block per (head, stream, query t). The reference makes each head's
+// T × nk scores one kern.MatMulF32 (nk = pos0 + T, the call's keys) and, for
+// T ≥ 4, the values another (kern.go:205 → gemm.go:116-185), and those
+// choose the arithmetic: up to 16 rows of A, gemvRows (dot4f32avx per group
+// of four B rows of the product, dotF32Go past the last group, and a
+// dotF32Go of any K tail added); with more, the packed kernel for rows below
+// T/6·6 (each output starts at 0 and adds the fused chain of every 256-deep
+// pass). Here one thread computes one output in that order. Scores past the
+// query's own position are cleared by the reference before the values;
+// they are never computed here and enter the value products as zeros. For
+// T < 4 the values are added key by key (AddScaled), skipping zero weights.
+__global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
+  extern __shared__ float rsc[];  // [nk] scores, then weights
+  __shared__ float qh[HD];
+  __shared__ float red[8];
+  const int h = blockIdx.x, si = blockIdx.y, t = blockIdx.z;
+  const int T = a.T[si];
+  if (t >= T) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int s = a.slot[si], pos0 = a.pos0[si], row = a.row0[si] + t;
+  const int nk = pos0 + T, nvis = pos0 + t + 1;
+  const size_t kbase = ((((size_t)s * a.layers + a.layer) * 2 + 0) * a.heads + h) * (size_t)a.cap * HD;
+  const size_t vbase = ((((size_t)s * a.layers + a.layer) * 2 + 1) * a.heads + h) * (size_t)a.cap * HD;
+  const float* K = a.kv + kbase;
+  const float* V = a.kv + vbase;
+  if (tid < HD) qh[tid] = a.q[(size_t)row * a.d + h * HD + tid];
+  __syncthreads();
+  const bool packed = T > 16 && t < T / 6 * 6;  // this query row goes through the packed kernel
+  const int nk4 = nk & ~3;
+
+  // --- scores of the visible keys, ·1/√64 ---
+  float mx = -__int_as_float(0x7f800000);
+  for (int j = tid; j < nvis; j += 128) {
+    const float* kj = K + (size_t)j * HD;
+    float sj;
+    if (packed) {
+      float acc = 0.f;
+      for (int k = 0; k < HD; k++) acc = __fmaf_rn(qh[k], kj[k], acc);
+      sj = __fadd_rn(0.f, acc);
+    } else if (j < nk4) {
+      sj = dot4_64(qh, kj);
+    } else {
+      sj = dot_go([&](int i) { return qh[i]; }, [&](int i) { return kj[i]; }, HD);
+    }
+    sj = __fmul_rn(sj, 0.125f);
+    rsc[j] = sj;
+    mx = fmaxf(mx, sj);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  // --- softmax over the visible keys (expSub: EXP8 lanes + HSUM + Go tail) ---
+  const int n8 = nvis & ~7;
+  for (int j = tid; j < nvis; j += 128) {
+    const float x = __fsub_rn(rsc[j], mx);
+    rsc[j] = j < n8 ? exp_avx(x) : expf_go(x);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float part = 0.f;
+    if (lane < 8)
+      for (int c = lane; c < n8; c += 8) part = __fadd_rn(part, rsc[c]);
+    const float savx = hsum8_lanes(part);
+    if (lane == 0) {
+      float tail = 0.f;
+      for (int j = n8; j < nvis; j++) tail = __fadd_rn(tail, rsc[j]);
+      red[4] = __fdiv_rn(1.f, __fadd_rn(savx, tail));
+    }
+  }
+  __syncthreads();
+  const float inv = red[4];
+  for (int j = tid; j < nk; j += 128) rsc[j] = j < nvis ? __fmul_rn(rsc[j], inv) : 0.f;
+  __syncthreads();
+
+  // --- values: thread d owns output d ---
+  if (tid < HD) {
+    const int d = tid;
+    const float* vd = V + d;  // element j of the transposed row d is vd[j·64]
+    float o;
+    if (T < 4) {
+      o = 0.f;
+      for (int j = 0; j < nk; j++) {
+        const float w = rsc[j];
+        if (w != 0.f) o = __fmaf_rn(w, vd[(size_t)j * HD], o);
+      }
+    } else if (packed) {
+      o = 0.f;
+      for (int k0 = 0; k0 < nk; k0 += 256) {
+        const int k1 = min(nk, k0 + 256);
+        float acc = 0.f;
+        for (int j = k0; j < k1; j++) acc = __fmaf_rn(rsc[j], vd[(size_t)j * HD], acc);
+        o = __fadd_rn(o, acc);
+      }
+    } else {
+      const int kk = nk & ~15;
+      float av[8], bv[8];
+#pragma unroll
+      for (int l = 0; l < 8; l++) av[l] = bv[l] = 0.f;
+      for (int c = 0; c < kk; c += 16)
+#pragma unroll
+        for (int l = 0; l < 8; l++) {
+          av[l] = __fmaf_rn(rsc[c + l], vd[(size_t)(c + l) * HD], av[l]);
+          bv[l] = __fmaf_rn(rsc[c + 8 + l], vd[(size_t)(c + 8 + l) * HD], bv[l]);
+        }
+      if (kk > 0) {
+#pragma unroll
+        for (int l = 0; l < 8; l++) av[l] = __fadd_rn(av[l], bv[l]);
+        o = __fadd_rn(__fadd_rn(__fadd_rn(av[0], av[4]), __fadd_rn(av[1], av[5])),
+                      __fadd_rn(__fadd_rn(av[2], av[6]), __fadd_rn(av[3], av[7])));
+      } else {
+        o = 0.f;
+      }
+      if (kk < nk)
+        o = __fadd_rn(o, dot_go([&](int i) { return rsc[kk + i]; }, [&](int i) { return vd[(size_t)(kk + i) * HD]; },
+                                nk - kk));
+    }
+    if (a.out) a.out[(size_t)row * a.d + h * HD + d] = o;
+    float sc;
+    const int8_t qv = quant_lane(o, &sc);
+    a.q8[(size_t)row * a.d + h * HD + d] = qv;
+    if (lane == 0) a.q8s[(size_t)row * (a.d / QK) + h * 2 + warp] = make_float2(sc, sc);
+  }
+}
+
+__global__ void k_embed_rows(float* x, const float* embed, const int* ids, int rows, int d) {
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const float* src = embed + (size_t)ids[r] * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) x[(size_t)r * d + i] = src[i];
+}
+
 }  // namespace
+
+void launch_attn_rows(const AttnRowsArgs& a, int nstreams, int tmax, cudaStream_t st) {
+  if (nstreams < 1 || tmax < 1) return;
+  k_attn_rows<<<dim3(a.heads, nstreams, tmax), 128, size_t(a.cap) * sizeof(float), st>>>(a);
+}
+
+void launch_embed_rows(float* x, const float* embed, const int* ids, int rows, int d, cudaStream_t st) {
+  if (rows > 0) k_embed_rows<<<rows, 256, 0, st>>>(x, embed, ids, rows, d);
+}
 
 void launch_attn(const AttnArgs& a, int M, cudaStream_t st) {
   dim3 grid(a.heads, M);

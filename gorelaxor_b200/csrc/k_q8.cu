@@ -43,11 +43,13 @@ __device__ __forceinline__ void rope_pair(float& x0, float& x1, float2 cs) {
 }
 
 // Stores the qkv product's pair (n, n+1) of row m: q rotated to the query
-// buffer, k rotated and v as they are to the cache row at pos[m].
+// buffer, k rotated and v as they are to the cache row at pos[m] of the
+// row's stream.
 __device__ __forceinline__ void store_qkv_pair(const KVArgs& kv, int m, int n, float c0, float c1) {
   int d = kv.d, hd = d / kv.heads;
   int region = n / d, w = n - region * d, h = w / hd, i = w - h * hd;
   int p = kv.pos[m];
+  const int slot = kv.row_stream ? kv.row_stream[m] : m;
   if (region < 2) {
     float2 cs = reinterpret_cast<const float2*>(kv.rope)[(size_t)p * (hd / 2) + i / 2];
     rope_pair(c0, c1, cs);
@@ -56,7 +58,7 @@ __device__ __forceinline__ void store_qkv_pair(const KVArgs& kv, int m, int n, f
     *reinterpret_cast<float2*>(kv.q + (size_t)m * d + w) = make_float2(c0, c1);
     return;
   }
-  size_t base = ((((size_t)m * kv.layers + kv.layer) * 2 + (region - 1)) * kv.heads + h) * (size_t)kv.cap;
+  size_t base = ((((size_t)slot * kv.layers + kv.layer) * 2 + (region - 1)) * kv.heads + h) * (size_t)kv.cap;
   *reinterpret_cast<float2*>(kv.kv + (base + p) * hd + i) = make_float2(c0, c1);
 }
 

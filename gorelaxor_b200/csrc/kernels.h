@@ -34,6 +34,9 @@ struct KVArgs {
   const int* pos = nullptr;  // [M] position being written
   const float* rope = nullptr;  // [cap][hd/2][2] cos, sin
   int layer = 0, layers = 0, heads = 0, cap = 0, d = 0;
+  // Rows of several positions per stream (text prefill): the cache slot of
+  // row m is row_stream[m] (NULL: row m is stream m).
+  const int* row_stream = nullptr;
 };
 
 struct EpiArgs {
@@ -116,6 +119,25 @@ struct AttnArgs {
 };
 
 void launch_attn(const AttnArgs& a, int M, cudaStream_t st);
+
+// transformer.attend for T queries per stream (text prefill, nn.go:200-243
+// with T > 1): call-stream i owns rows row0[i] .. row0[i] + T[i] − 1 of q
+// and the output, at positions pos0[i] ..; its keys are the cache slot
+// slot[i]'s rows 0 .. pos0[i] + T[i] − 1 (already appended).
+struct AttnRowsArgs {
+  const float* q = nullptr;  // [R][d] rotated queries
+  const float* kv = nullptr;
+  const int *row0 = nullptr, *T = nullptr, *pos0 = nullptr, *slot = nullptr;
+  float* out = nullptr;  // [R][d] (may be NULL)
+  int8_t* q8 = nullptr;  // [R][d] output rounded to Q8_0
+  float2* q8s = nullptr;
+  int layer = 0, layers = 0, heads = 0, cap = 0, d = 0;
+};
+
+void launch_attn_rows(const AttnRowsArgs& a, int nstreams, int tmax, cudaStream_t st);
+
+// x[r] = embedding row ids[r] (float32 rows of width d).
+void launch_embed_rows(float* x, const float* embed, const int* ids, int rows, int d, cudaStream_t st);
 
 // Float activations times a Q8_0 (rows kept), F32 or F16 matrix with the
 // reference's float-path order (dot4q8avx / dot4f32avx / dot4f16avx,

@@ -134,6 +134,17 @@ int grx_streams_create(grx_flowlm* m, int n, const grx_voice* const* voices, int
 void grx_streams_free(grx_streams* s);
 /* Puts every stream back at its voice prompt and the next frame at bos. */
 int grx_streams_reset(grx_streams* s);
+/* flowLM.text (pockettts/lm.go:172-181), what speakChunk runs before its
+ * frames (speak.go:119): stream i's text tokens ids[offsets[i] ..
+ * offsets[i+1]) go through the transformer after the positions it holds,
+ * with attend's arithmetic for several queries (nn.go:200-243), and stay in
+ * its caches; the next frame still starts at bos. offsets has n + 1
+ * non-decreasing entries from 0 (a stream may have no tokens). The tokens
+ * count against the room the set was made with (max_frames). out (host,
+ * may be NULL) gets [n][d]: out_norm of each stream's last token row, which
+ * the reference returns (streams without tokens keep their row). Needs a
+ * model with lm.embed; ids must be rows of it. Synchronous. */
+int grx_streams_text(grx_streams* s, const int* ids, const int* offsets, float* out);
 /* One frame for every stream: flowLM.step then flowHead.sample
  * (pockettts/lm.go:185-195, 108-124; speak.go:146-174), the raw latent fed
  * back on the device. noise is [n][ldim]. Outputs (host, any may be NULL):

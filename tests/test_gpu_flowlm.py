@@ -166,3 +166,75 @@ def test_flowlm_parts_run_device_and_step(have_gpu, n):
     for f in range(frames):
         lat, eos, _, _ = st.step(noise[f])
         assert bits_equal(lat, lat_o[f]) and bits_equal(eos, eos_o[f]), f"frame {f}"
+
+
+def _text_ids(cfg, lens, seed):
+    return [[(11 * i + 5 * j + seed) % cfg.text_vocab for j in range(T)] for i, T in enumerate(lens)]
+
+
+@pytest.mark.parametrize("lens", [[1, 3, 5, 16], [17, 30, 0, 4], [2, 40, 6, 23]])
+def test_flowlm_text_prefill_bit_exact(have_gpu, lens):
+    """flowLM.text (lm.go:172-181) for ragged token counts — attend's T < 4
+    (values key by key), 4 ≤ T ≤ 16 (gemvRows products) and T > 16 (packed
+    rows below T/6·6) — then frames from bos: the output at each stream's
+    last token, the positions and every frame bit-identical to the oracle."""
+    cfg = synth.FlowLMConfig(**SMALL)
+    gm, om = _models(cfg, seed=5)
+    n, frames = len(lens), 3
+    kvs = [voice_kv(cfg, 6 + i, 1 + i) for i in range(n)]
+    ids = _text_ids(cfg, lens, 3)
+    st = g.Streams(gm, [gm.voice(kv) for kv in kvs], max(lens) + frames)
+    out = st.text(ids)
+    os_ = [om.stream(kv) for kv in kvs]
+    for i in range(n):
+        if ids[i]:
+            ne, rel = mismatch(out[i], om.text(os_[i], ids[i]))
+            assert ne == 0, f"stream {i} (T={lens[i]}): {ne} of the output differ, max rel {rel:.2e}"
+        assert st.pos(i) == os_[i].pos == 6 + i + lens[i]
+    noise = np.stack([synth.noise_frames(1 + i, frames, cfg.ldim, cfg.temperature) for i in range(n)], axis=1)
+    lat_o, eos_o, _ = om.run(os_, noise, threads=4)
+    for f in range(frames):
+        lat, eos, _, _ = st.step(noise[f])
+        assert bits_equal(lat, lat_o[f]) and bits_equal(eos, eos_o[f]), f"frame {f}"
+
+
+def test_flowlm_text_prefill_parts(have_gpu):
+    """A set of 130 streams (two parts on their own CUDA streams) prefilled
+    with ragged texts of 0-20 tokens, then two device-resident frames."""
+    import torch
+
+    cfg = synth.FlowLMConfig(**SMALL)
+    gm, om = _models(cfg, seed=6)
+    n, frames = 130, 2
+    rng = np.random.default_rng(7)
+    lens = [int(v) for v in rng.integers(0, 21, n)]
+    kvs = [voice_kv(cfg, 4 + i % 5, 1 + i) for i in range(n)]
+    ids = _text_ids(cfg, lens, 9)
+    st = g.Streams(gm, [gm.voice(kv) for kv in kvs], 20 + frames)
+    assert st.parts() == 2
+    out = st.text(ids)
+    os_ = [om.stream(kv) for kv in kvs]
+    for i in range(n):
+        if ids[i]:
+            assert bits_equal(out[i], om.text(os_[i], ids[i])), f"stream {i}"
+    noise = np.stack([synth.noise_frames(1 + i, frames, cfg.ldim, cfg.temperature) for i in range(n)], axis=1)
+    lat_o, eos_o, _ = om.run(os_, noise, threads=8)
+    dn = torch.from_numpy(noise).cuda()
+    dl = torch.empty_like(dn)
+    de = torch.empty((frames, n), device="cuda")
+    st.run_device(frames, dn.data_ptr(), dl.data_ptr(), de.data_ptr())
+    st.sync()
+    assert bits_equal(dl.cpu().numpy(), lat_o) and bits_equal(de.cpu().numpy(), eos_o)
+
+
+def test_flowlm_text_errors(have_gpu):
+    """Token ids outside lm.embed and texts longer than the set's room are
+    refused before anything runs."""
+    cfg = synth.FlowLMConfig(**SMALL)
+    gm, _ = _models(cfg)
+    st = g.Streams(gm, [gm.voice(voice_kv(cfg, 4, 1))], 5)
+    with pytest.raises(g.GrxError):
+        st.text([[cfg.text_vocab + 1]])
+    with pytest.raises(g.GrxError):
+        st.text([list(range(6))])
+    assert st.pos(0) == 4
