@@ -63,6 +63,8 @@ def _sig(lib):
         "grx_voice_load": (I, [P, P, S, PP]),
         "grx_voice_raw": (I, [P, I, P, PP]),
         "grx_voice_free": (None, [P]),
+        "grx_voice_from_latents": (I, [P, P, I, PP]),
+        "grx_voice_kv": (I, [P, P, P]),
         "grx_streams_create": (I, [P, I, P, I, PP]),
         "grx_streams_free": (None, [P]),
         "grx_streams_reset": (I, [P]),
@@ -265,6 +267,16 @@ class FlowLM:
         _check(lib().grx_voice_raw(self._h, a.shape[2], _ptr(a), C.byref(h)))
         return Voice(h)
 
+    def voice_from_latents(self, latents: np.ndarray) -> "Voice":
+        """The voice a clip's Mimi latents [n][ldim] make (the flow-LM half
+        of CloneVoice, voice.go:94-106)."""
+        a = np.ascontiguousarray(latents, dtype=np.float32)
+        h = C.c_void_p()
+        _check(lib().grx_voice_from_latents(self._h, _ptr(a), a.shape[0], C.byref(h)))
+        v = Voice(h)
+        v._model = self
+        return v
+
     def __del__(self, _free=_FREE):
         h, self._h = getattr(self, "_h", None), None
         if h:
@@ -274,6 +286,14 @@ class FlowLM:
 class Voice:
     def __init__(self, h):
         self._h = h
+
+    def kv(self, layers: int, d: int) -> np.ndarray:
+        """The caches [layers][2][positions][d]."""
+        n = C.c_int()
+        _check(lib().grx_voice_kv(self._h, C.byref(n), None))
+        out = np.empty((layers, 2, n.value, d), np.float32)
+        _check(lib().grx_voice_kv(self._h, None, _ptr(out)))
+        return out
 
     def __del__(self, _free=_FREE):
         h, self._h = getattr(self, "_h", None), None

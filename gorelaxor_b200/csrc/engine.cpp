@@ -73,6 +73,8 @@ struct grx_flowlm {
   std::vector<float> freqs;
   float* embed = nullptr;  // lm.embed widened to float32 [embed_rows][d], if the file has it
   int embed_rows = 0;
+  float* speaker = nullptr;  // lm.speaker_proj [d][ldim] float32, and lm.bos_voice [d], if the file has them
+  float* bosv = nullptr;
 };
 
 struct grx_voice {
@@ -694,6 +696,10 @@ int grx_flowlm_load(const void* bytes, size_t len, int device, grx_flowlm** out)
       m->embed_rows = int(r);
     }
   }
+  if (err.empty() && f.has("lm.speaker_proj") && f.has("lm.bos_voice")) {  // voice cloning (model.go:309-316)
+    m->speaker = f32m("lm.speaker_proj", d, ld);
+    m->bosv = vec("lm.bos_voice", d);
+  }
   DQ8 tfc1[2], tfc2[2];
   float *tb1[2], *tb2[2], *alpha[2];
   std::vector<float> freqs[2];
@@ -802,6 +808,13 @@ int grx_flowlm_dims(const grx_flowlm* m, int* d, int* heads, int* ff, int* layer
   return GRX_OK;
 }
 
+int grx_voice_kv(const grx_voice* v, int* positions, float* kv) {
+  if (!v) return fail(GRX_EINVAL, "grx_voice_kv: null voice");
+  if (positions) *positions = v->positions;
+  if (kv) std::memcpy(kv, v->kv.data(), sizeof(float) * v->kv.size());
+  return GRX_OK;
+}
+
 int grx_voice_raw(grx_flowlm* m, int positions, const float* kv, grx_voice** out) {
   if (!m || !kv || !out) return fail(GRX_EINVAL, "grx_voice_raw: null argument");
   if (positions < 1 || positions > 4096) return fail(GRX_EINVAL, "pockettts: a voice of " + std::to_string(positions) + " positions");
@@ -864,7 +877,7 @@ int grx_streams_reset(grx_streams* s) {
 // tokens are ids[off[i] .. off[i+1]) (off relative to the caller's array).
 // All streams' token rows go through each layer together; rows r of stream
 // i sit at positions pos[i] + r and write its cache.
-static int streams_text_one(grx_streams* q, const int* ids, const int* off, float* out) {
+static int streams_text_one(grx_streams* q, const int* ids, const int* off, float* out, const float* d_xin = nullptr) {
   grx_flowlm* m = q->m;
   const int n = q->n, d = m->d, ff = m->ff;
   std::vector<int> pos((size_t(n)));
@@ -884,7 +897,7 @@ static int streams_text_one(grx_streams* q, const int* ids, const int* off, floa
     c_pos0.push_back(pos[size_t(i)]);
     c_slot.push_back(i);
     for (int r = 0; r < T; r++) {
-      row_id.push_back(ids[off[i] - off[0] + r]);
+      row_id.push_back(ids ? ids[off[i] - off[0] + r] : 0);
       row_slot.push_back(i);
       row_pos.push_back(pos[size_t(i)] + r);
     }
@@ -913,7 +926,10 @@ static int streams_text_one(grx_streams* q, const int* ids, const int* off, floa
   const int *d_id = dint, *d_slot = dint + R, *d_pos = dint + 2 * R, *d_row0 = dint + 3 * R, *d_T = d_row0 + ns,
             *d_pos0 = d_T + ns, *d_cslot = d_pos0 + ns, *d_last = d_cslot + ns;
   cudaStream_t st = q->st;
-  launch_embed_rows(x, m->embed, d_id, R, d, st);
+  if (d_xin)  // the rows themselves (voice conditioning), in row order
+    CK(cudaMemcpyAsync(x, d_xin, sizeof(float) * size_t(R) * d, cudaMemcpyDeviceToDevice, st));
+  else
+    launch_embed_rows(x, m->embed, d_id, R, d, st);
   for (int l = 0; l < m->L; l++) {
     const Layer& ly = m->layers[size_t(l)];
     LnArgs ln;
@@ -1009,6 +1025,81 @@ int grx_streams_text(grx_streams* s, const int* ids, const int* offsets, float* 
     int rc = streams_text_one(p.get(), ids + offsets[p->row0], offsets + p->row0, out ? out + size_t(p->row0) * m->d : nullptr);
     if (rc) return rc;
   }
+  return GRX_OK;
+}
+
+// The flow-LM half of Model.CloneVoice (voice.go:94-106; cloneCond :113-127
+// after Mimi's encoder): cond = kern.Linear(latents, lm.speaker_proj), a
+// float32 weight, so MatMul's float path — gemvRows up to 16 rows, else the
+// packed kernel for the first n/6·6 rows and gemvRows for the rest — then
+// [bos_voice; cond] through the transformer from an empty state (lm.run with
+// n + 1 rows); the caches are the voice.
+static int streams_create_one(grx_flowlm* m, int n, const grx_voice* const* voices, int max_frames,
+                              std::unique_ptr<grx_streams>* out);
+
+int grx_voice_from_latents(grx_flowlm* m, const float* latents, int n, grx_voice** out) {
+  if (!m || !latents || !out) return fail(GRX_EINVAL, "grx_voice_from_latents: null argument");
+  if (!m->speaker || !m->bosv) return fail(GRX_EINVAL, "pockettts: this model file has no voice cloning");
+  if (n < 1 || n > 4095) return fail(GRX_EINVAL, "pockettts: " + std::to_string(n) + " latent frames");
+  int rc = device_init(m->dev);
+  if (rc) return rc;
+  const int d = m->d, ld = m->ldim, L = m->L, H = m->heads, hd = 64;
+  grx_voice empty;
+  empty.model = m->sha;
+  const grx_voice* vp = &empty;
+  std::unique_ptr<grx_streams> s;
+  rc = streams_create_one(m, 1, &vp, n + 1, &s);
+  if (rc) return rc;
+  Arena ar;
+  ar.dev = m->dev;
+  float* dl = ar.upload(latents, size_t(n) * ld, &rc);
+  float* rows = ar.alloc<float>(size_t(n + 1) * d, &rc);
+  if (rc) return rc;
+  cudaStream_t st = s->st;
+  CK(cudaMemcpyAsync(rows, m->bosv, sizeof(float) * d, cudaMemcpyDeviceToDevice, st));
+  const int packed = n > 16 ? n / 6 * 6 : 0;  // rows through the packed kernel
+  if (packed > 0) {
+    WmmArgs w;
+    w.a = dl;
+    w.lda = ld;
+    w.m = packed;
+    w.w.f = m->speaker;
+    w.w.rows = d;
+    w.w.cols = ld;
+    w.mode = WM_STORE;
+    w.c = rows + d;
+    w.ldc = d;
+    launch_wmm(w, 1, st);
+  }
+  if (packed < n) {
+    FArgs a;
+    a.epi = FE_BIAS;
+    a.x = dl + size_t(packed) * ld;
+    a.ldx = ld;
+    a.wf = m->speaker;
+    a.N = d;
+    a.K = ld;
+    a.y = rows + size_t(1 + packed) * d;
+    a.ldy = d;
+    launch_flin(a, n - packed, st);
+  }
+  std::vector<int> off = {0, n + 1};
+  rc = streams_text_one(s.get(), nullptr, off.data(), nullptr, rows);
+  if (rc) return rc;
+  // the cache [layer][k|v][head][position][64] → the voice's [layer][k|v][position][d]
+  std::vector<float> c(size_t(L) * 2 * H * s->cap * hd);
+  CK(cudaMemcpy(c.data(), s->kv, sizeof(float) * c.size(), cudaMemcpyDeviceToHost));
+  auto v = std::make_unique<grx_voice>();
+  v->positions = n + 1;
+  v->model = m->sha;
+  v->kv.resize(size_t(L) * 2 * (n + 1) * d);
+  for (int l = 0; l < L; l++)
+    for (int k = 0; k < 2; k++)
+      for (int h = 0; h < H; h++)
+        for (int p = 0; p <= n; p++)
+          std::memcpy(&v->kv[((size_t(l) * 2 + k) * (n + 1) + p) * d + size_t(h) * hd],
+                      &c[(((size_t(l) * 2 + k) * H + h) * s->cap + p) * hd], sizeof(float) * hd);
+  *out = v.release();
   return GRX_OK;
 }
 

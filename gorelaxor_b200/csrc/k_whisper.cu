@@ -27,6 +27,7 @@ namespace {
 __device__ __forceinline__ float q8h(int8_t q, float d) { return __half2float(__float2half_rn(__fmul_rn(float(q), d))); }
 
 __device__ __forceinline__ float wmat_at(const WMat& w, int row, int col) {
+  if (w.f) return w.f[(size_t)row * w.cols + col];
   if (w.h) return __half2float(__ushort_as_half(w.h[(size_t)row * w.cols + col]));
   return q8h(w.q[(size_t)row * w.cols + col], h2f(w.d[(size_t)row * (w.cols / QK) + col / QK]));
 }

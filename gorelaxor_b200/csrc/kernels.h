@@ -246,6 +246,7 @@ struct WMat {
   const int8_t* q = nullptr;
   const uint16_t* d = nullptr;  // Q8_0 scales [rows][cols/32]
   const uint16_t* h = nullptr;  // or float16 values [rows][cols]
+  const float* f = nullptr;     // or float32 values [rows][cols]
   int rows = 0, cols = 0;
 };
 

@@ -237,6 +237,9 @@ def flowlm_tensors(cfg: FlowLMConfig, seed: int = 0) -> dict:
     # the text embedding, drawn from its own generator so that the tensors
     # above do not depend on it
     t["lm.embed"] = rand_q8(np.random.default_rng(seed + 7919), cfg.text_vocab + 1, d)
+    # voice cloning's projection of Mimi latents (float32: too narrow for
+    # the converter's Q8_0 rule, convert_pocket_tts.py:150-156)
+    t["lm.speaker_proj"] = _n(np.random.default_rng(seed + 104729), (d, ld), 1.0 / np.sqrt(ld))
     return t
 
 

@@ -127,6 +127,16 @@ int grx_voice_load(grx_flowlm* m, const void* gguf, size_t len, grx_voice** out)
 /* A voice from raw caches: kv is [layers][2][positions][d] float32. */
 int grx_voice_raw(grx_flowlm* m, int positions, const float* kv, grx_voice** out);
 void grx_voice_free(grx_voice* v);
+/* The flow-LM half of Model.CloneVoice (pockettts/voice.go:94-106 and
+ * cloneCond :113-127 after Mimi's encoder): latents are the clip's Mimi
+ * latents [n][ldim] (1 ≤ n ≤ 4095); cond = kern.Linear(latents,
+ * lm.speaker_proj), then [lm.bos_voice; cond] runs through the transformer
+ * from an empty state and its caches become the voice (n + 1 positions).
+ * Needs a model file with lm.speaker_proj (float32) and lm.bos_voice. */
+int grx_voice_from_latents(grx_flowlm* m, const float* latents, int n, grx_voice** out);
+/* A voice's positions and (kv may be NULL) its caches [layers][2][positions][d]
+ * — the tstate a Voice holds (voice.go:14-17). */
+int grx_voice_kv(const grx_voice* v, int* positions, float* kv);
 
 /* n streams, stream i starting from voices[i] (speakChunk's
  * v.st.clone(...), speak.go:117), each with room for max_frames frames. */

@@ -84,6 +84,8 @@ struct FlowLM {
   std::vector<float> freqs;
   Weight input, eosw, cond, finput, final_ada, fout;
   Weight embed;  // lm.embed [tokens + 1][d] (rows 0 when the model has none)
+  Weight speaker;  // lm.speaker_proj [d][ldim] float32 (rows 0 when the model has none)
+  const float* bosv = nullptr;  // lm.bos_voice [d]
   const float *bos, *outw, *outb, *mean, *stdv, *condb, *finputb, *final_adab, *foutb;
   float eosb;
   TimeEmbed time[2];
@@ -347,6 +349,22 @@ inline void flowlm_text(const FlowLM& m, const int* ids, int T, Stream& st, floa
   std::vector<float> x(size_t(T) * m.d);
   for (int i = 0; i < T; i++) weight_row(m.embed, ids[i], x.data() + size_t(i) * m.d);
   transformer_rows(m, x.data(), T, st, lm_out);
+}
+
+// The flow-LM half of Model.CloneVoice (voice.go:94-106, cloneCond :113-127
+// after Mimi's encoder): cond = kern.Linear(latents, lm.speaker_proj)
+// (float32 weight: MatMul's gemvRows up to 16 rows, the packed kernel
+// beyond), then [bos_voice; cond] through the transformer from an empty
+// state, whose caches are the voice.
+inline void flowlm_voice_latents(const FlowLM& m, const float* lat, int n, Stream& st) {
+  const int d = m.d;
+  std::vector<float> x(size_t(n + 1) * d);
+  std::copy(m.bosv, m.bosv + d, x.begin());
+  matmul_kern_f32(x.data() + d, d, lat, m.speaker.cols, m.speaker.f, m.speaker.cols, n, d, m.speaker.cols);
+  st.k.assign(m.layers.size(), {});
+  st.v.assign(m.layers.size(), {});
+  st.pos = 0;
+  transformer_rows(m, x.data(), n + 1, st, nullptr);
 }
 
 // flowLM.step, pockettts/lm.go:185-195. latent == nullptr is the first

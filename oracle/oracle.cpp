@@ -192,6 +192,10 @@ int orc_flowlm_ready(void* h, int decode_steps) {
   m.fout = get_w(o, "flow.final.out.weight");
   m.foutb = get_v(o, "flow.final.out.bias");
   if (o->w.count("lm.embed")) m.embed = get_w(o, "lm.embed");  // optional: text prefill only
+  if (o->w.count("lm.speaker_proj") && o->v.count("lm.bos_voice")) {  // optional: voice conditioning only
+    m.speaker = get_w(o, "lm.speaker_proj");
+    m.bosv = get_v(o, "lm.bos_voice");
+  }
   if (!o->err.empty()) return -1;
   o->decode_steps = decode_steps;
   o->tc = time_conds(m, decode_steps);
@@ -226,6 +230,23 @@ void* orc_stream_new(void* h, int n, const float* kv) {
 }
 
 void orc_stream_free(void* s) { delete (Stream*)s; }
+
+// The voice a clip's Mimi latents [n][ldim] make (voice.go:94-106 after
+// the encoder): kv_out gets [layers][2][n + 1][d]. -1 without
+// lm.speaker_proj (float32) and lm.bos_voice.
+int orc_flowlm_voice_latents(void* h, const float* lat, int n, float* kv_out) {
+  auto* o = (OFlowLM*)h;
+  const FlowLM& m = o->m;
+  if (m.speaker.rows != m.d || m.speaker.type != F32 || !m.bosv || n < 1) return -1;
+  Stream st;
+  flowlm_voice_latents(m, lat, n, st);
+  const size_t rows = size_t(n + 1) * m.d;
+  for (size_t l = 0; l < m.layers.size(); l++) {
+    std::copy(st.k[l].begin(), st.k[l].end(), kv_out + (l * 2 + 0) * rows);
+    std::copy(st.v[l].begin(), st.v[l].end(), kv_out + (l * 2 + 1) * rows);
+  }
+  return 0;
+}
 
 // flowLM.text (lm.go:172-181) on one stream: T token ids appended to its
 // caches; lm_out (may be NULL) gets the output at the last token. Returns

@@ -56,6 +56,7 @@ def lib():
             "orc_stream_free": (None, [P]),
             "orc_stream_pos": (I, [P]),
             "orc_flowlm_text": (I, [P, P, P, I, P]),
+            "orc_flowlm_voice_latents": (I, [P, P, I, P]),
             "orc_flowlm_frame": (F, [P, P, P, P, P, P, P, P]),
             "orc_flowlm_run": (None, [P, I, P, I, P, P, P, P, I]),
             "orc_tdt_new": (P, [I, I, I, I, I, I, I, I, P, I]),
@@ -199,6 +200,16 @@ class FlowLM:
         if lib().orc_flowlm_text(self.h, st.h, p(ids), len(ids), p(out)) != 0:
             raise ValueError("orc_flowlm_text: no lm.embed or a token id out of range")
         return out
+
+    def voice_from_latents(self, lat):
+        """The voice caches [layers][2][n + 1][d] a clip's Mimi latents
+        [n][ldim] make (voice.go:94-106 after the encoder)."""
+        lat = np.ascontiguousarray(lat, np.float32)
+        n = lat.shape[0]
+        kv = np.empty((self.cfg.layers, 2, n + 1, self.cfg.d), np.float32)
+        if lib().orc_flowlm_voice_latents(self.h, p(lat), n, p(kv)) != 0:
+            raise ValueError("orc_flowlm_voice_latents: no float32 lm.speaker_proj / lm.bos_voice")
+        return kv
 
     def frame(self, st: "Stream", latent, noise, trace=False):
         c = self.cfg

@@ -238,3 +238,27 @@ def test_flowlm_text_errors(have_gpu):
     with pytest.raises(g.GrxError):
         st.text([list(range(6))])
     assert st.pos(0) == 4
+
+
+@pytest.mark.parametrize("n", [3, 16, 17, 40])
+def test_flowlm_voice_from_latents_bit_exact(have_gpu, n):
+    """The flow-LM half of CloneVoice (voice.go:94-106): the speaker
+    projection (gemvRows up to 16 rows, packed rows beyond) and [bos_voice;
+    cond] through the transformer from an empty state give caches
+    bit-identical to the oracle's; frames from that voice match too."""
+    cfg = synth.FlowLMConfig(**SMALL)
+    gm, om = _models(cfg, seed=8)
+    lat = np.random.default_rng(n).normal(0, 1, (n, cfg.ldim)).astype(np.float32)
+    v = gm.voice_from_latents(lat)
+    kv_o = om.voice_from_latents(lat)
+    kv = v.kv(cfg.layers, cfg.d)
+    ne, rel = mismatch(kv, kv_o)
+    assert ne == 0, f"{ne} of {kv.size} cache values differ, max rel {rel:.2e}"
+    frames = 2
+    st = g.Streams(gm, [v], frames)
+    os_ = om.stream(kv_o)
+    noise = synth.noise_frames(3, frames, cfg.ldim, cfg.temperature)[:, None, :]
+    lat_o, eos_o, _ = om.run([os_], noise)
+    for f in range(frames):
+        l_, e_, _, _ = st.step(noise[f])
+        assert bits_equal(l_, lat_o[f]) and bits_equal(e_, eos_o[f]), f"frame {f}"

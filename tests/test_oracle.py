@@ -306,3 +306,61 @@ def test_flowlm_text_against_numpy_model(T):
     assert st.pos == 6 + T
     want = _np_text(cfg, t, [(kv[l, 0], kv[l, 1]) for l in range(cfg.layers)], ids, 6)
     assert np.sqrt(((got - want) ** 2).sum() / (want ** 2).sum()) < 0.02
+
+
+@pytest.mark.parametrize("n", [3, 20])
+def test_flowlm_voice_latents_against_numpy_model(n):
+    """The flow-LM half of CloneVoice (voice.go:94-106): [bos_voice;
+    latents·speaker_projᵀ] through the transformer from an empty state. The
+    last layer's cached values against an independent float64 model within
+    2% RMS."""
+    cfg = synth.FlowLMConfig(**SMALL)
+    t = synth.flowlm_tensors(cfg, 0)
+    om = orc.FlowLM(cfg, t)
+    lat = np.random.default_rng(n).normal(0, 1, (n, cfg.ldim)).astype(np.float32)
+    kv = om.voice_from_latents(lat)
+    D = lambda a: np.asarray(a, np.float64)
+    W = lambda name: D(synth.q8_dequant(t[name])) if isinstance(t[name], synth.Q8) else D(t[name])
+
+    def q8round(x):
+        out = np.empty_like(x)
+        for b in range(0, x.size, 32):
+            blk = x[b:b + 32]
+            amax = np.abs(blk).max()
+            out[b:b + 32] = np.rint(blk * 127 / amax) * amax / 127 if amax else 0
+        return out
+
+    ln = lambda x, w, b: (x - x.mean()) / np.sqrt(x.var() + 1e-5) * w + b
+    hd = cfg.d // cfg.heads
+
+    def rope(v, pos):
+        f = np.exp(-np.log(cfg.max_period) * 2 / hd * np.arange(hd // 2))
+        v = v.reshape(cfg.heads, hd // 2, 2).copy()
+        r, i = v[..., 0].copy(), v[..., 1].copy()
+        v[..., 0], v[..., 1] = r * np.cos(f * pos) - i * np.sin(f * pos), r * np.sin(f * pos) + i * np.cos(f * pos)
+        return v.reshape(-1)
+
+    gelu = lambda v: 0.5 * v * (1 + np.tanh(np.sqrt(2 / np.pi) * v * (1 + 0.044715 * v * v)))
+    xs = [D(t["lm.bos_voice"])] + list(D(lat) @ W("lm.speaker_proj").T)
+    for l in range(cfg.layers):
+        p = f"lm.blk.{l}."
+        qs, K, V = [], [], []
+        for r, x in enumerate(xs):
+            qkv = W(p + "attn_qkv.weight") @ q8round(ln(x, D(t[p + "norm1.weight"]), D(t[p + "norm1.bias"])))
+            qs.append(rope(qkv[:cfg.d], r))
+            K.append(rope(qkv[cfg.d:2 * cfg.d], r))
+            V.append(qkv[2 * cfg.d:])
+        K, V = np.array(K), np.array(V)
+        if l == cfg.layers - 1:
+            got = kv[l, 1].astype(np.float64)
+            assert np.sqrt(((got - V) ** 2).sum() / (V ** 2).sum()) < 0.02
+        for r in range(len(xs)):
+            att = np.zeros(cfg.d)
+            for hh in range(cfg.heads):
+                sl = slice(hh * hd, (hh + 1) * hd)
+                s = K[:r + 1, sl] @ qs[r][sl] / np.sqrt(hd)
+                e = np.exp(s - s.max())
+                att[sl] = (e / e.sum()) @ V[:r + 1, sl]
+            xs[r] = xs[r] + W(p + "attn_out.weight") @ q8round(att)
+            h = ln(xs[r], D(t[p + "norm2.weight"]), D(t[p + "norm2.bias"]))
+            xs[r] = xs[r] + W(p + "ff2.weight") @ q8round(gelu(W(p + "ff1.weight") @ q8round(h)))
