@@ -243,8 +243,119 @@ def flowlm_tensors(cfg: FlowLMConfig, seed: int = 0) -> dict:
     return t
 
 
-def flowlm_gguf(cfg: FlowLMConfig, tensors: dict) -> bytes:
+@dataclass
+class MimiConfig:
+    """Mimi's decoder as a Pocket TTS file configures it (model.go:280-300);
+    the defaults are a small one that still takes every product path: Q8_0
+    for the first convolution, the first transposed one and the transformer
+    (the converter's rule: both dimensions at least 64, columns whole
+    blocks, convert_pocket_tts.py:150-156), float32 for the narrow last
+    stages, and rows past 16 so that those take the packed kernel."""
+
+    d: int = 128
+    heads: int = 2
+    ff: int = 256
+    layers: int = 2
+    context: int = 8
+    max_period: float = 10000.0
+    upsample: int = 4
+    ratios: tuple = (5, 2)
+    nf: int = 16
+    k: int = 7
+    resk: int = 3
+    lastk: int = 3
+    dil: int = 2
+    comp: int = 2
+    nres: int = 1
+    frame_rate: float = 12.5
+
+    @property
+    def frame(self) -> int:
+        return int(np.prod(self.ratios)) * self.upsample
+
+    @property
+    def sample_rate(self) -> int:
+        return int(round(self.frame * self.frame_rate))
+
+
+def _mat(rng, rows, cols):
+    """A matrix the way the converter stores it: Q8_0 when both dimensions
+    are at least 64 and the columns whole blocks, else float32; values of
+    standard deviation 1/√cols."""
+    sd = 1.0 / np.sqrt(cols)
+    if rows >= 64 and cols >= 64 and cols % QK == 0:
+        return rand_q8(rng, rows, cols, scale_sd=sd / 73.0)
+    return _n(rng, (rows, cols), sd)
+
+
+def mimi_tensors(mc: MimiConfig, ldim: int, seed: int = 0) -> dict:
+    """Mimi decoder tensors in the converter's names (model.go:102-200)."""
+    rng = np.random.default_rng(seed + 31337)
+    d = mc.d
+    t: dict = {"mimi.quant": _n(rng, (d, ldim), 1.0 / np.sqrt(ldim)),
+               "mimi.up": _n(rng, d * 2 * mc.upsample, 0.5)}
+    for i in range(mc.layers):
+        p = f"mimi.dec_tf.{i}."
+        t[p + "norm1.weight"] = 1.0 + _n(rng, d, 0.1)
+        t[p + "norm1.bias"] = _n(rng, d, 0.1)
+        t[p + "norm2.weight"] = 1.0 + _n(rng, d, 0.1)
+        t[p + "norm2.bias"] = _n(rng, d, 0.1)
+        t[p + "attn_qkv.weight"] = _mat(rng, 3 * d, d)
+        t[p + "attn_out.weight"] = _mat(rng, d, d)
+        t[p + "ff1.weight"] = _mat(rng, mc.ff, d)
+        t[p + "ff2.weight"] = _mat(rng, d, mc.ff)
+        t[p + "ls1"] = np.abs(_n(rng, d, 0.2))
+        t[p + "ls2"] = np.abs(_n(rng, d, 0.2))
+
+    def conv(name, cin, cout, k):
+        t[name + ".weight"] = _mat(rng, cout, k * cin)
+        t[name + ".bias"] = _n(rng, cout, 0.05)
+
+    mult = 1 << len(mc.ratios)
+    conv("mimi.dec.0", d, mult * mc.nf, mc.k)
+    idx = 1
+    for r in mc.ratios:
+        idx += 1
+        cin, cout = mult * mc.nf, mult * mc.nf // 2
+        t[f"mimi.dec.{idx}.weight"] = _mat(rng, 2 * r * cout, cin)
+        t[f"mimi.dec.{idx}.bias"] = _n(rng, cout, 0.05)
+        idx += 1
+        for _ in range(mc.nres):
+            conv(f"mimi.dec.{idx}.1", cout, cout // mc.comp, mc.resk)
+            conv(f"mimi.dec.{idx}.3", cout // mc.comp, cout, 1)
+            idx += 1
+        mult //= 2
+    idx += 1
+    conv(f"mimi.dec.{idx}", mc.nf, 1, mc.lastk)
+    return t
+
+
+def mimi_keys(g: "GGUFWriter", mc: MimiConfig) -> None:
+    g.u32("pockettts.sample_rate", mc.sample_rate)
+    g.f32("pockettts.frame_rate", mc.frame_rate)
+    g.u32("pockettts.mimi.d_model", mc.d)
+    g.u32("pockettts.mimi.heads", mc.heads)
+    g.u32("pockettts.mimi.ff", mc.ff)
+    g.u32("pockettts.mimi.context", mc.context)
+    g.f32("pockettts.mimi.max_period", mc.max_period)
+    g.u32("pockettts.mimi.upsample", mc.upsample)
+    g.i32s("pockettts.seanet.ratios", list(mc.ratios))
+    g.u32("pockettts.seanet.n_filters", mc.nf)
+    g.u32("pockettts.seanet.dimension", mc.d)
+    g.u32("pockettts.seanet.kernel_size", mc.k)
+    g.u32("pockettts.seanet.residual_kernel_size", mc.resk)
+    g.u32("pockettts.seanet.last_kernel_size", mc.lastk)
+    g.u32("pockettts.seanet.dilation_base", mc.dil)
+    g.u32("pockettts.seanet.compress", mc.comp)
+    g.u32("pockettts.seanet.n_residual_layers", mc.nres)
+
+
+def flowlm_gguf(cfg: FlowLMConfig, tensors: dict, mimi: "MimiConfig | None" = None) -> bytes:
+    """A Pocket TTS file with the FlowLM's tensors (and, given mimi, the
+    decoder's tensors in `tensors` and its keys)."""
     g = GGUFWriter("pockettts")
+    if mimi is not None:
+        mimi_keys(g, mimi)
     g.str("general.name", "Pocket TTS synthetic")
     g.str("general.source.sha256", cfg.sha)
     g.u32("pockettts.latent_dim", cfg.ldim)

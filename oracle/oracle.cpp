@@ -13,6 +13,7 @@
 #include <thread>
 
 #include "flowlm.h"
+#include "mimi.h"
 #include "tdt.h"
 #include "whisper.h"
 
@@ -666,4 +667,142 @@ void orc_whisper_run(void* h, int n, const float* enc, const int* prompt, int np
   for (auto& t : ts) t.join();
 }
 
+
+// ---- Mimi decoder ---------------------------------------------------------
+
+struct OMimi {
+  MimiDecoder m;
+  std::map<std::string, Weight> w;
+  std::map<std::string, const float*> v;
+  std::string err;
+  std::vector<int> ratios;
+  int nf = 0, kk = 0, resk = 0, lastk = 0, dil = 0, comp = 0, nres = 0;
+};
+
+// Config as the loader reads it (model.go:280-300): d, heads, ff, context,
+// max period, upsample; SEANet ratios, n_filters, kernel sizes, dilation
+// base, compress, residual layers; latent dim and sample rate.
+void* orc_mimi_new(int d, int heads, int ff, int context, double period, int up, const int* ratios, int nratios,
+                   int nf, int k, int resk, int lastk, int dil, int comp, int nres, int ldim, int sample_rate) {
+  auto* o = new OMimi();
+  o->m.tf.d = d;
+  o->m.tf.heads = heads;
+  o->m.tf.ff = ff;
+  o->m.tf.context = context;
+  o->m.tf.freqs = rope_freqs(d / heads, period);
+  o->m.upS = up;
+  o->m.ldim = ldim;
+  o->m.sample_rate = sample_rate;
+  o->ratios.assign(ratios, ratios + nratios);
+  o->nf = nf, o->kk = k, o->resk = resk, o->lastk = lastk, o->dil = dil, o->comp = comp, o->nres = nres;
+  int hop = 1;
+  for (int r : o->ratios) hop *= r;
+  o->m.frame = hop * up;
+  return o;
+}
+void orc_mimi_free(void* h) { delete (OMimi*)h; }
+void orc_mimi_tensor(void* h, const char* name, int type, int rows, int cols, const void* p) {
+  auto* o = (OMimi*)h;
+  Weight w;
+  w.rows = rows;
+  w.cols = cols;
+  w.type = WType(type);
+  w.f = (const float*)p;
+  w.q = (const uint8_t*)p;
+  o->w[name] = w;
+  o->v[name] = (const float*)p;
+}
+const char* orc_mimi_error(void* h) { return ((OMimi*)h)->err.c_str(); }
+
+// Binds the tensors the way model.go:102-200 names them.
+int orc_mimi_ready(void* h) {
+  auto* o = (OMimi*)h;
+  MimiDecoder& m = o->m;
+  auto W = [&](const std::string& n) {
+    auto it = o->w.find(n);
+    if (it == o->w.end()) {
+      if (o->err.empty()) o->err = "missing " + n;
+      return Weight{};
+    }
+    return it->second;
+  };
+  auto V = [&](const std::string& n) -> const float* {
+    auto it = o->v.find(n);
+    if (it == o->v.end()) {
+      if (o->err.empty()) o->err = "missing " + n;
+      return nullptr;
+    }
+    return it->second;
+  };
+  m.quant = W("mimi.quant");
+  m.up = V("mimi.up");
+  for (int i = 0;; i++) {
+    const std::string p = "mimi.dec_tf." + std::to_string(i) + ".";
+    if (!o->w.count(p + "attn_qkv.weight")) break;
+    MLayer l;
+    l.norm1w = V(p + "norm1.weight");
+    l.norm1b = V(p + "norm1.bias");
+    l.norm2w = V(p + "norm2.weight");
+    l.norm2b = V(p + "norm2.bias");
+    l.ls1 = V(p + "ls1");
+    l.ls2 = V(p + "ls2");
+    l.qkv = W(p + "attn_qkv.weight");
+    l.out = W(p + "attn_out.weight");
+    l.ff1 = W(p + "ff1.weight");
+    l.ff2 = W(p + "ff2.weight");
+    m.tf.layers.push_back(l);
+  }
+  auto conv = [&](const std::string& n, int cin, int cout, int k, int stride, int dl) {
+    MConv c;
+    c.w = W(n + ".weight");
+    c.b = V(n + ".bias");
+    c.cin = cin, c.cout = cout, c.k = k, c.stride = stride, c.dil = dl;
+    return c;
+  };
+  int mult = 1 << o->ratios.size();
+  MStep first;
+  first.kind = 0;
+  first.c = conv("mimi.dec.0", m.tf.d, mult * o->nf, o->kk, 1, 1);
+  m.steps.push_back(first);
+  int idx = 1;
+  for (int r : o->ratios) {
+    idx++;
+    MStep t;
+    t.kind = 1;
+    t.elu = true;
+    const std::string n = "mimi.dec." + std::to_string(idx);
+    t.t.w = W(n + ".weight");
+    t.t.b = V(n + ".bias");
+    t.t.cin = mult * o->nf, t.t.cout = mult * o->nf / 2, t.t.k = 2 * r, t.t.stride = r;
+    m.steps.push_back(t);
+    idx++;
+    const int dim = mult * o->nf / 2;
+    for (int j = 0, dl = 1; j < o->nres; j++, dl *= o->dil) {
+      const std::string p = "mimi.dec." + std::to_string(idx) + ".";
+      MStep rb;
+      rb.kind = 2;
+      rb.ra = conv(p + "1", dim, dim / o->comp, o->resk, 1, dl);
+      rb.rb = conv(p + "3", dim / o->comp, dim, 1, 1, 1);
+      m.steps.push_back(rb);
+      idx++;
+    }
+    mult /= 2;
+  }
+  idx++;
+  MStep last;
+  last.kind = 0;
+  last.elu = true;
+  last.c = conv("mimi.dec." + std::to_string(idx), o->nf, 1, o->lastk, 1, 1);
+  m.steps.push_back(last);
+  return o->err.empty() ? 0 : -1;
+}
+
+void* orc_mimi_state(void* h) { return new MimiState(mimi_state(((OMimi*)h)->m)); }
+void orc_mimi_state_free(void* s) { delete (MimiState*)s; }
+// One latent [ldim] → one frame of samples.
+void orc_mimi_decode(void* h, void* s, const float* lat, float* pcm) {
+  mimi_decode(((OMimi*)h)->m, *(MimiState*)s, lat, pcm);
+}
+int orc_mimi_frame(void* h) { return ((OMimi*)h)->m.frame; }
+void orc_elu(float* x, long n) { elu_vec(x, n); }
 }  // extern "C"

@@ -57,6 +57,16 @@ def lib():
             "orc_stream_pos": (I, [P]),
             "orc_flowlm_text": (I, [P, P, P, I, P]),
             "orc_flowlm_voice_latents": (I, [P, P, I, P]),
+            "orc_mimi_new": (P, [I, I, I, I, D, I, P, I, I, I, I, I, I, I, I, I, I]),
+            "orc_mimi_free": (None, [P]),
+            "orc_mimi_tensor": (None, [P, C.c_char_p, I, I, I, P]),
+            "orc_mimi_error": (C.c_char_p, [P]),
+            "orc_mimi_ready": (I, [P]),
+            "orc_mimi_state": (P, [P]),
+            "orc_mimi_state_free": (None, [P]),
+            "orc_mimi_decode": (None, [P, P, P, P]),
+            "orc_mimi_frame": (I, [P]),
+            "orc_elu": (None, [P, C.c_long]),
             "orc_flowlm_frame": (F, [P, P, P, P, P, P, P, P]),
             "orc_flowlm_run": (None, [P, I, P, I, P, P, P, P, I]),
             "orc_tdt_new": (P, [I, I, I, I, I, I, I, I, P, I]),
@@ -421,3 +431,62 @@ class WSeq:
             _lib.orc_wseq_free(self.h)
             self.h = None
 
+
+
+# --------------------------------------------------------------- Mimi --
+
+
+class Mimi:
+    """The oracle's Mimi decoder (oracle/mimi.h), from a MimiConfig and the
+    generator's tensor dict."""
+
+    def __init__(self, mc, tensors: dict, ldim: int):
+        from gorelaxor_b200.synth import Q8
+
+        L = lib()
+        self._keep = []
+        r = np.ascontiguousarray(mc.ratios, np.int32)
+        self._keep.append(r)
+        self.h = L.orc_mimi_new(mc.d, mc.heads, mc.ff, mc.context, mc.max_period, mc.upsample, p(r), len(r), mc.nf,
+                                mc.k, mc.resk, mc.lastk, mc.dil, mc.comp, mc.nres, ldim, mc.sample_rate)
+        for name, arr in tensors.items():
+            if not name.startswith("mimi."):
+                continue
+            if isinstance(arr, Q8):
+                buf = np.ascontiguousarray(arr.blocks)
+                L.orc_mimi_tensor(self.h, name.encode(), 2, arr.rows, arr.cols, p(buf))
+            else:
+                buf = np.ascontiguousarray(arr, np.float32)
+                rows, cols = (buf.shape if buf.ndim == 2 else (1, buf.size))
+                L.orc_mimi_tensor(self.h, name.encode(), 0, rows, cols, p(buf))
+            self._keep.append(buf)
+        if L.orc_mimi_ready(self.h) != 0:
+            raise RuntimeError(L.orc_mimi_error(self.h).decode())
+        self.frame = L.orc_mimi_frame(self.h)
+        self.ldim = ldim
+
+    def state(self):
+        return MimiState(lib().orc_mimi_state(self.h))
+
+    def decode(self, st: "MimiState", latent) -> np.ndarray:
+        """One latent (already scaled) → one frame of samples, with
+        speakChunk's fade-in on the state's first frame."""
+        lat = np.ascontiguousarray(latent, np.float32)
+        pcm = np.empty(self.frame, np.float32)
+        lib().orc_mimi_decode(self.h, st.h, p(lat), p(pcm))
+        return pcm
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_mimi_free(self.h)
+            self.h = None
+
+
+class MimiState:
+    def __init__(self, h):
+        self.h = h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_mimi_state_free(self.h)
+            self.h = None
