@@ -185,6 +185,29 @@ def run_reference(args, rank, world):
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
             flush=True)
         return
+    if args.workload == "mimi":
+        mc = mimi_config()
+        tensors = synth.mimi_tensors(mc, 32, 0)
+        streams, frames = min(args.batch, cores), 8
+        vals, times = [], []
+        for _ in range(args.steps):
+            v, dt = mimi_cpu_sample(mc, tensors, streams, frames, cores)
+            vals.append(v)
+            times.append(dt)
+        value = float(np.mean(vals))
+        sample = f"{streams} streams x {frames} latents from a fresh state per step, {min(cores, streams)} threads"
+        print(json.dumps({
+            "impl": "reference", "metric": MIMI_METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
+            "data": "synthetic (seeded; the reference ships no weights)",
+            "config": {"workload": f"Mimi decode, {args.batch} streams x {args.frames} latents (sampled)",
+                       "global_batch": args.batch, "frames": args.frames, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "frames/s", "cores": min(cores, streams), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
     cfg = synth.FlowLMConfig()
     tensors = synth.flowlm_tensors(cfg, 0)
     streams, frames = min(args.batch, cores), 8
@@ -325,6 +348,143 @@ def run_tdt(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+MIMI_METRIC = "Mimi frames/s (latent frames decoded to 1920-sample audio frames per second, whole job)"
+
+
+def mimi_config():
+    """Pocket TTS's Mimi decoder shape: d 512, 8 heads × 64, FFN 2048, 2
+    layers, a 250-position window, 2 rows per latent, SEANet ratios
+    (8, 6, 5, 4) with 64 filters: 1920 samples per latent at 24 kHz."""
+    from gorelaxor_b200 import synth
+
+    return synth.MimiConfig(d=512, heads=8, ff=2048, layers=2, context=250, upsample=2, ratios=(8, 6, 5, 4), nf=64)
+
+
+def mimi_latents(streams, frames, ldim=32, seed0=1):
+    """[frames][streams][ldim] scaled latents, N(0,1), stream i seeded seed0 + i."""
+    return np.stack([np.random.default_rng(seed0 + i).normal(0, 1, (frames, ldim)).astype(np.float32)
+                     for i in range(streams)], axis=1)
+
+
+def mimi_cpu_sample(mc, tensors, streams, frames, threads):
+    """The oracle's decoder on host threads: `streams` fresh states ×
+    `frames` latents, one thread per stream (ctypes drops the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+
+    om = orc.Mimi(mc, tensors, 32)
+    lat = mimi_latents(streams, frames)
+    sts = [om.state() for _ in range(streams)]
+
+    def one(i):
+        for f in range(frames):
+            om.decode(sts[i], lat[f, i])
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=min(threads, streams)) as ex:
+        list(ex.map(one, range(streams)))
+    dt = time.perf_counter() - t0
+    return streams * frames / dt, dt
+
+
+def run_mimi(args, rank, world, local):
+    """--workload mimi: Pocket TTS's Mimi decoder (the next stage of the
+    FlowLM loop): `batch` streams per GPU, each decoding `frames` latents in
+    order with its streaming state; one step = every stream's frames from a
+    fresh state."""
+    import torch
+
+    import gorelaxor_b200 as g
+    from gorelaxor_b200 import synth
+    from gorelaxor_b200.dist import max_over_ranks, partition
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    B, F = args.batch, args.frames
+    mc = mimi_config()
+    tensors = synth.mimi_tensors(mc, 32, 0)
+    gm = g.Mimi(synth.flowlm_gguf(synth.FlowLMConfig(), tensors, mimi=mc), device=local)
+    mine = partition(B * world, world, rank)
+    lat = mimi_latents(len(mine), F, seed0=1 + mine.start)
+    s = g.MimiStreams(gm, B, F)
+    d_lat = torch.from_numpy(lat).cuda()
+    d_pcm = torch.empty((F, B, gm.frame), dtype=torch.float32, device="cuda")
+    ext = torch.cuda.ExternalStream(s.cuda_stream())
+
+    def one():
+        s.reset()
+        s.decode_device(F, d_lat.data_ptr(), d_pcm.data_ptr())
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    l0 = s.launches()
+    if dist:
+        dist.barrier()
+    clocks.start()
+    ms = []
+    for _ in range(args.steps):
+        s.reset()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        s.decode_device(F, d_lat.data_ptr(), d_pcm.data_ptr())
+        e1.record(ext)
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    ck = clocks.stop()
+    launches = s.launches() - l0
+    total_ms = max_over_ranks(float(np.sum(ms)), device="cuda")
+    value = args.steps * B * F * world / (total_ms / 1000)
+
+    e2e = None
+    if args.e2e_steps > 0:
+        pin = torch.from_numpy(lat).pin_memory().numpy()
+        em = []
+        for _ in range(args.e2e_steps):
+            s.reset()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for f in range(F):
+                s.decode(pin[f])
+            em.append((time.perf_counter() - t0) * 1000)
+        emax = max_over_ranks(float(np.sum(em)), device="cuda")
+        e2e = {"value": args.e2e_steps * B * F * world / (emax / 1000), "unit": "frames/s",
+               "h2d_bytes_per_step": int(lat.nbytes), "d2h_bytes_per_step": int(F * B * gm.frame * 4),
+               "note": "grx_mimi_decode per frame: latents H2D from pinned memory, samples D2H"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        streams, frames = min(B, cores), 8
+        v, dt = mimi_cpu_sample(mc, tensors, streams, frames, cores)
+        cpu = {"value": v, "unit": "frames/s", "cores": min(cores, streams), "kind": "port",
+               "sample": f"{streams} streams x {frames} latents from a fresh state ({dt:.1f} s wall)"}
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": MIMI_METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8/f32",
+        "data": "synthetic (seeded Q8_0/f32 decoder in the converter's types, N(0,1) latents)",
+        "config": {"workload": f"Mimi decode: {B} streams x {F} latents per GPU", "global_batch": B * world,
+                   "frames": F, "parallelism": f"streams partitioned, {world} GPU(s), no collective",
+                   "l2": f"activations {B * 5} MB per GPU per frame, larger than L2"},
+        "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck,
+    }
+    print(json.dumps(line), flush=True)
+
+
 WHISPER_METRIC = "Whisper tokens/s (greedy decode tokens per second, whole job)"
 
 
@@ -453,7 +613,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="grx", choices=["grx", "reference"])
-    ap.add_argument("--workload", default="flowlm", choices=["flowlm", "tdt", "whisper"])
+    ap.add_argument("--workload", default="flowlm", choices=["flowlm", "tdt", "whisper", "mimi"])
     ap.add_argument("--batch", type=int, default=None, help="streams per GPU (flowlm 256, tdt 128)")
     ap.add_argument("--frames", type=int, default=None, help="frames per stream (flowlm 512, tdt 750)")
     ap.add_argument("--e2e-steps", type=int, default=1)
@@ -463,14 +623,16 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
-    args.batch = args.batch or {"flowlm": 256, "tdt": 128, "whisper": 32}[args.workload]
-    args.frames = args.frames or {"flowlm": 512, "tdt": 750, "whisper": 224}[args.workload]
+    args.batch = args.batch or {"flowlm": 256, "tdt": 128, "whisper": 32, "mimi": 64}[args.workload]
+    args.frames = args.frames or {"flowlm": 512, "tdt": 750, "whisper": 224, "mimi": 32}[args.workload]
     if args.impl == "reference":
         return run_reference(args, rank, world)
     if args.workload == "tdt":
         return run_tdt(args, rank, world, local)
     if args.workload == "whisper":
         return run_whisper(args, rank, world, local)
+    if args.workload == "mimi":
+        return run_mimi(args, rank, world, local)
 
     import torch
 

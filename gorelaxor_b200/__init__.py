@@ -77,6 +77,18 @@ def _sig(lib):
         "grx_streams_launches": (L, [P]),
         "grx_streams_cuda_stream": (P, [P]),
         "grx_streams_parts": (I, [P]),
+        "grx_mimi_load": (I, [P, S, I, PP]),
+        "grx_mimi_free": (None, [P]),
+        "grx_mimi_dims": (I, [P] + [C.POINTER(C.c_int)] * 8),
+        "grx_mimi_streams_create": (I, [P, I, I, PP]),
+        "grx_mimi_streams_free": (None, [P]),
+        "grx_mimi_streams_reset": (I, [P]),
+        "grx_mimi_decode": (I, [P, P, P]),
+        "grx_mimi_decode_device": (I, [P, I, P, P]),
+        "grx_mimi_sync": (I, [P]),
+        "grx_mimi_cuda_stream": (P, [P]),
+        "grx_mimi_launches": (L, [P]),
+        "grx_mimi_frames": (I, [P]),
         "grx_tdt_load": (I, [P, S, I, PP]),
         "grx_tdt_free": (None, [P]),
         "grx_tdt_dims": (I, [P] + [C.POINTER(C.c_int)] * 8),
@@ -128,7 +140,8 @@ def lib():
             raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m gorelaxor_b200.build`")
         _lib = _sig(C.CDLL(str(LIB_PATH)))
         for n in ("grx_gguf_close", "grx_weight_free", "grx_flowlm_free", "grx_voice_free", "grx_streams_free",
-                  "grx_tdt_free", "grx_tdt_batch_free", "grx_whisper_free", "grx_whisper_batch_free"):
+                  "grx_mimi_free", "grx_mimi_streams_free", "grx_tdt_free", "grx_tdt_batch_free", "grx_whisper_free",
+                  "grx_whisper_batch_free"):
             _FREE[n] = getattr(_lib, n)
     return _lib
 
@@ -374,6 +387,74 @@ class Streams:
         h, self._h = getattr(self, "_h", None), None
         if h:
             _free["grx_streams_free"](h)
+
+
+# ------------------------------------------------------- Mimi decoder
+
+
+class Mimi:
+    """Pocket TTS's Mimi decoder (pockettts/mimi.go:24-150) on one device,
+    from a Pocket TTS file."""
+
+    def __init__(self, gguf: bytes, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().grx_mimi_load(gguf, len(gguf), device, C.byref(h)))
+        self._h = h
+        self.device = device
+        v = [C.c_int() for _ in range(8)]
+        _check(lib().grx_mimi_dims(h, *[C.byref(x) for x in v]))
+        (self.d, self.heads, self.layers, self.context, self.upsample, self.ldim, self.frame,
+         self.sample_rate) = [x.value for x in v]
+
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_mimi_free"](h)
+
+
+class MimiStreams:
+    """n independent decoder states (decState, mimi.go:108-124); each call
+    turns one latent per stream into one frame per stream."""
+
+    def __init__(self, model: Mimi, n: int, max_frames: int):
+        self.model, self.n = model, n
+        h = C.c_void_p()
+        _check(lib().grx_mimi_streams_create(model._h, n, max_frames, C.byref(h)))
+        self._h = h
+
+    def reset(self):
+        _check(lib().grx_mimi_streams_reset(self._h))
+
+    def decode(self, latents: np.ndarray) -> np.ndarray:
+        """latents [n][ldim] → samples [n][frame] (the first frame of each
+        stream faded in, speak.go:185-190)."""
+        m = self.model
+        lat = np.ascontiguousarray(latents, dtype=np.float32).reshape(self.n, m.ldim)
+        out = np.empty((self.n, m.frame), np.float32)
+        _check(lib().grx_mimi_decode(self._h, _ptr(lat), _ptr(out)))
+        return out
+
+    def decode_device(self, frames: int, d_latents: int, d_pcm: int):
+        """frames calls with device pointers (ints): latents [frames][n][ldim]
+        in, samples [frames][n][frame] out. Asynchronous."""
+        _check(lib().grx_mimi_decode_device(self._h, frames, C.c_void_p(d_latents), C.c_void_p(d_pcm)))
+
+    def sync(self):
+        _check(lib().grx_mimi_sync(self._h))
+
+    def frames(self) -> int:
+        return _check(lib().grx_mimi_frames(self._h))
+
+    def cuda_stream(self) -> int:
+        return lib().grx_mimi_cuda_stream(self._h) or 0
+
+    def launches(self) -> int:
+        return lib().grx_mimi_launches(self._h)
+
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_mimi_streams_free"](h)
 
 
 # ------------------------------------------------------------ TDT decoder

@@ -20,6 +20,8 @@
 // from HBM once: the kernel is bound by those bytes.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -211,7 +213,15 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   if (t >= T) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int s = a.slot[si], pos0 = a.pos0[si], row = a.row0[si] + t;
-  const int nk = pos0 + T, nvis = pos0 + t + 1;
+  // keys lo0 .. pos0 + T − 1 are the call's (indices j below are relative
+  // to lo0); this query sees lo .. p
+  const int p = pos0 + t, lo0 = a.context > 0 ? max(0, pos0 - a.context + 1) : 0;
+  const int lo = a.context > 0 ? max(lo0, p - a.context + 1) : lo0;
+  const int nk = pos0 + T - lo0, v0 = lo - lo0, nvis = p + 1 - lo0;  // visible: v0 .. nvis − 1
+  auto krow = [&](int j) {  // cache row of relative key j
+    const int ab = lo0 + j;
+    return a.ring ? ab % a.ring : ab;
+  };
   const size_t kbase = ((((size_t)s * a.layers + a.layer) * 2 + 0) * a.heads + h) * (size_t)a.cap * HD;
   const size_t vbase = ((((size_t)s * a.layers + a.layer) * 2 + 1) * a.heads + h) * (size_t)a.cap * HD;
   const float* K = a.kv + kbase;
@@ -223,8 +233,8 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
 
   // --- scores of the visible keys, ·1/√64 ---
   float mx = -__int_as_float(0x7f800000);
-  for (int j = tid; j < nvis; j += 128) {
-    const float* kj = K + (size_t)j * HD;
+  for (int j = v0 + tid; j < nvis; j += 128) {
+    const float* kj = K + (size_t)krow(j) * HD;
     float sj;
     if (packed) {
       float acc = 0.f;
@@ -244,9 +254,10 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   if (lane == 0) red[warp] = mx;
   __syncthreads();
   mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  // --- softmax over the visible keys (expSub: EXP8 lanes + HSUM + Go tail) ---
-  const int n8 = nvis & ~7;
-  for (int j = tid; j < nvis; j += 128) {
+  // --- softmax over the visible keys (expSub over the slice v0 .. nvis − 1:
+  // EXP8 lanes for its first count&~7, HSUM, Go tail) ---
+  const int cnt = nvis - v0, n8 = v0 + (cnt & ~7);
+  for (int j = v0 + tid; j < nvis; j += 128) {
     const float x = __fsub_rn(rsc[j], mx);
     rsc[j] = j < n8 ? exp_avx(x) : expf_go(x);
   }
@@ -254,7 +265,7 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   if (warp == 0) {
     float part = 0.f;
     if (lane < 8)
-      for (int c = lane; c < n8; c += 8) part = __fadd_rn(part, rsc[c]);
+      for (int c = v0 + lane; c < n8; c += 8) part = __fadd_rn(part, rsc[c]);
     const float savx = hsum8_lanes(part);
     if (lane == 0) {
       float tail = 0.f;
@@ -264,26 +275,26 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   }
   __syncthreads();
   const float inv = red[4];
-  for (int j = tid; j < nk; j += 128) rsc[j] = j < nvis ? __fmul_rn(rsc[j], inv) : 0.f;
+  for (int j = tid; j < nk; j += 128) rsc[j] = j >= v0 && j < nvis ? __fmul_rn(rsc[j], inv) : 0.f;
   __syncthreads();
 
   // --- values: thread d owns output d ---
   if (tid < HD) {
     const int d = tid;
-    const float* vd = V + d;  // element j of the transposed row d is vd[j·64]
+    const float* vd = V + d;  // element j of the transposed row d is vd[krow(j)·64]
     float o;
     if (T < 4) {
       o = 0.f;
       for (int j = 0; j < nk; j++) {
         const float w = rsc[j];
-        if (w != 0.f) o = __fmaf_rn(w, vd[(size_t)j * HD], o);
+        if (w != 0.f) o = __fmaf_rn(w, vd[(size_t)krow(j) * HD], o);
       }
     } else if (packed) {
       o = 0.f;
       for (int k0 = 0; k0 < nk; k0 += 256) {
         const int k1 = min(nk, k0 + 256);
         float acc = 0.f;
-        for (int j = k0; j < k1; j++) acc = __fmaf_rn(rsc[j], vd[(size_t)j * HD], acc);
+        for (int j = k0; j < k1; j++) acc = __fmaf_rn(rsc[j], vd[(size_t)krow(j) * HD], acc);
         o = __fadd_rn(o, acc);
       }
     } else {
@@ -294,8 +305,8 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
       for (int c = 0; c < kk; c += 16)
 #pragma unroll
         for (int l = 0; l < 8; l++) {
-          av[l] = __fmaf_rn(rsc[c + l], vd[(size_t)(c + l) * HD], av[l]);
-          bv[l] = __fmaf_rn(rsc[c + 8 + l], vd[(size_t)(c + 8 + l) * HD], bv[l]);
+          av[l] = __fmaf_rn(rsc[c + l], vd[(size_t)krow(c + l) * HD], av[l]);
+          bv[l] = __fmaf_rn(rsc[c + 8 + l], vd[(size_t)krow(c + 8 + l) * HD], bv[l]);
         }
       if (kk > 0) {
 #pragma unroll
@@ -306,7 +317,7 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
         o = 0.f;
       }
       if (kk < nk)
-        o = __fadd_rn(o, dot_go([&](int i) { return rsc[kk + i]; }, [&](int i) { return vd[(size_t)(kk + i) * HD]; },
+        o = __fadd_rn(o, dot_go([&](int i) { return rsc[kk + i]; }, [&](int i) { return vd[(size_t)krow(kk + i) * HD]; },
                                 nk - kk));
     }
     if (a.out) a.out[(size_t)row * a.d + h * HD + d] = o;
@@ -328,7 +339,9 @@ __global__ void k_embed_rows(float* x, const float* embed, const int* ids, int r
 
 void launch_attn_rows(const AttnRowsArgs& a, int nstreams, int tmax, cudaStream_t st) {
   if (nstreams < 1 || tmax < 1) return;
-  k_attn_rows<<<dim3(a.heads, nstreams, tmax), 128, size_t(a.cap) * sizeof(float), st>>>(a);
+  // the scores of one query: at most the call's keys
+  const int nk = a.context > 0 ? std::min(a.cap, a.context - 1 + tmax) : a.cap;
+  k_attn_rows<<<dim3(a.heads, nstreams, tmax), 128, size_t(nk) * sizeof(float), st>>>(a);
 }
 
 void launch_embed_rows(float* x, const float* embed, const int* ids, int rows, int d, cudaStream_t st) {

@@ -105,10 +105,15 @@ __device__ float q8_go(const FArgs& a, int n, X x) {
   return s;
 }
 
+// The physical row of logical row m (FArgs row groups).
+__device__ __forceinline__ int fl_row(const FArgs& a, int m) {
+  return a.rg_len ? (m / a.rg_len) * a.rg_stride + a.rg_off + m % a.rg_len : m;
+}
+
 // Output (m, n) of the dot r: bias, then the epilogue.
 __device__ __forceinline__ void fl_out(const FArgs& a, int m, int n, float r) {
   const float v = a.bias ? __fadd_rn(r, a.bias[n]) : r;
-  float* yp = a.y + (size_t)m * a.ldy + n;
+  float* yp = a.y + (size_t)fl_row(a, m) * a.ldy + n;
   switch (a.epi) {
     case FE_COND:
       *yp = silu_avx(__fadd_rn(v, a.aux[n]));
@@ -203,7 +208,7 @@ __global__ void __launch_bounds__(NTH) k_flin(FArgs a) {
     for (int u = 0; u < XI; u++) {
       const int i = tid + u * NTH, m = i % TS, k8 = i / TS;
       if (k8 < kn / 8 && m < mt) {
-        const float4* p = reinterpret_cast<const float4*>(xsrc + (size_t)(m0 + m) * a.ldx + kc0 + k8 * 8);
+        const float4* p = reinterpret_cast<const float4*>(xsrc + (size_t)fl_row(a, m0 + m) * a.ldx + kc0 + k8 * 8);
         xr0[u] = p[0];
         xr1[u] = p[1];
       }
@@ -422,7 +427,7 @@ __global__ void __launch_bounds__(NTH) k_flin(FArgs a) {
     const int nl = rg * R + r, ml = sg * M + mm;
     if (nl >= nrows || ml >= mt) continue;
     const int n = n0 + nl, m = m0 + ml;
-    const float* xrow = xsrc + (size_t)m * a.ldx;
+    const float* xrow = xsrc + (size_t)fl_row(a, m) * a.ldx;
     auto xg = [&](int k) { return xrow[k]; };
     float r_;
     if (n >= ntail)  // a row past the last group of four: the scalar Go dot

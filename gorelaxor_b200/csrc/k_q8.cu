@@ -50,6 +50,7 @@ __device__ __forceinline__ void store_qkv_pair(const KVArgs& kv, int m, int n, f
   int region = n / d, w = n - region * d, h = w / hd, i = w - h * hd;
   int p = kv.pos[m];
   const int slot = kv.row_stream ? kv.row_stream[m] : m;
+  const int pc = kv.ring ? p % kv.ring : p;  // the cache row
   if (region < 2) {
     float2 cs = reinterpret_cast<const float2*>(kv.rope)[(size_t)p * (hd / 2) + i / 2];
     rope_pair(c0, c1, cs);
@@ -59,7 +60,7 @@ __device__ __forceinline__ void store_qkv_pair(const KVArgs& kv, int m, int n, f
     return;
   }
   size_t base = ((((size_t)slot * kv.layers + kv.layer) * 2 + (region - 1)) * kv.heads + h) * (size_t)kv.cap;
-  *reinterpret_cast<float2*>(kv.kv + (base + p) * hd + i) = make_float2(c0, c1);
+  *reinterpret_cast<float2*>(kv.kv + (base + pc) * hd + i) = make_float2(c0, c1);
 }
 
 // ------------------------------------------------------------- GEMV ------
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(256) k_q8_gemv(const int8_t* __restrict__ a, c
         float* yp = e.y + (size_t)m * e.ldy + nrow0 + r;
         const float v = c[r][m];
         if (e.epi == EPI_RESID)
-          *yp = __fadd_rn(*yp, v);
+          *yp = __fadd_rn(*yp, e.ls ? __fmul_rn(e.ls[nrow0 + r], v) : v);
         else
           *yp = v;
       }
@@ -268,7 +269,8 @@ __device__ __forceinline__ void gemm_epilogue(f2 (&acc)[TM][TN][2], const EpiArg
         float2* yp = reinterpret_cast<float2*>(e.y + (size_t)row * e.ldy + col);
         if (e.epi == EPI_RESID) {
           const float2 o = *yp;
-          *yp = make_float2(__fadd_rn(o.x, c0v), __fadd_rn(o.y, c1v));
+          const float a0 = e.ls ? __fmul_rn(e.ls[col], c0v) : c0v, a1 = e.ls ? __fmul_rn(e.ls[col + 1], c1v) : c1v;
+          *yp = make_float2(__fadd_rn(o.x, a0), __fadd_rn(o.y, a1));
         } else {
           *yp = make_float2(c0v, c1v);
         }
@@ -793,7 +795,8 @@ __global__ void __launch_bounds__(TcCfg<BN, EPW>::NT, 1)
           float2* yp = reinterpret_cast<float2*>(e.y + (size_t)m * e.ldy + col);
           if (e.epi == EPI_RESID) {
             const float2 o = *yp;
-            *yp = make_float2(__fadd_rn(o.x, c0v), __fadd_rn(o.y, c1v));
+            const float a0 = e.ls ? __fmul_rn(e.ls[col], c0v) : c0v, a1 = e.ls ? __fmul_rn(e.ls[col + 1], c1v) : c1v;
+            *yp = make_float2(__fadd_rn(o.x, a0), __fadd_rn(o.y, a1));
           } else {
             *yp = make_float2(c0v, c1v);
           }

@@ -37,6 +37,9 @@ struct KVArgs {
   // Rows of several positions per stream (text prefill): the cache slot of
   // row m is row_stream[m] (NULL: row m is stream m).
   const int* row_stream = nullptr;
+  // A ring of this many positions (0: position p at row p); RoPE still
+  // takes the position itself.
+  int ring = 0;
 };
 
 struct EpiArgs {
@@ -46,6 +49,7 @@ struct EpiArgs {
   const float* bias = nullptr;
   int8_t* q8 = nullptr;  // GELU_Q8 outputs: values [M][N], scales [M][N/32]
   float2* q8s = nullptr;
+  const float* ls = nullptr;  // RESID: y += ls[col]·c (addScaled, unfused) when set
   KVArgs kv;
 };
 
@@ -132,9 +136,28 @@ struct AttnRowsArgs {
   int8_t* q8 = nullptr;  // [R][d] output rounded to Q8_0
   float2* q8s = nullptr;
   int layer = 0, layers = 0, heads = 0, cap = 0, d = 0;
+  // A context window (0: none): keys from max(0, pos0 − context + 1), query
+  // p sees [max(that, p − context + 1), p]; and the cache as a ring of
+  // `ring` positions (0: none).
+  int context = 0, ring = 0;
 };
 
 void launch_attn_rows(const AttnRowsArgs& a, int nstreams, int tmax, cudaStream_t st);
+
+// Mimi's decoder steps between products (k_mimi.cu); rows [stream][time][channel].
+void launch_mimi_up(const float* z, const float* up, const float* part_in, float* x, float* part_out, int n, int S,
+                    int C, cudaStream_t st);
+void launch_mimi_elu(const float* in, float* out, int n, int len, cudaStream_t st);
+void launch_mimi_im2col(const float* x, const float* prev_in, float* prev_out, float* col, int n, int T, int cin, int k,
+                        int stride, int dil, int P, cudaStream_t st);
+void launch_mimi_convtr(const float* z, const float* bias, const float* part_in, float* y, float* part_out, int n, int T,
+                        int co, int k, int S, cudaStream_t st);
+void launch_mimi_add(const float* a, const float* b, float* y, size_t n, cudaStream_t st);
+// rowpos[r] = pos[r / S] + r % S for the R rows of a call; pos[i] += S after it.
+void launch_mimi_rows(const int* pos, int S, int R, int* rowpos, cudaStream_t st);
+void launch_mimi_advance(int* pos, int S, int n, cudaStream_t st);
+// The fade-in of each not yet started stream's frame (pcm [n][frame]); marks it started.
+void launch_mimi_fade(float* pcm, int* started, int n, int frame, int fade, cudaStream_t st);
 
 // x[r] = embedding row ids[r] (float32 rows of width d).
 void launch_embed_rows(float* x, const float* embed, const int* ids, int rows, int d, cudaStream_t st);
@@ -182,6 +205,10 @@ struct FArgs {
   // scaled rows to io.
   const FrameIO* io = nullptr;
   bool x_noise = false, aux_noise = false, io_out = false;
+  // Row groups (FE_BIAS and plain stores only): logical row m is physical
+  // row (m / rg_len)·rg_stride + rg_off + m % rg_len of x and y (rg_len 0:
+  // row m).
+  int rg_len = 0, rg_stride = 0, rg_off = 0;
 };
 
 void launch_flin(const FArgs& a, int M, cudaStream_t st);

@@ -188,6 +188,51 @@ int grx_streams_pos(const grx_streams* s, int i);
 /* Device kernel launches issued by this stream set since creation. */
 int64_t grx_streams_launches(const grx_streams* s);
 
+/* ------------------------------------------- Pocket TTS Mimi decoder ----
+ * mimiDecoder (pockettts/mimi.go:24-150): the latent projection, the
+ * depthwise upsampling, the windowed transformer with layer scales and the
+ * SEANet decoder, streaming, for n independent streams that each turn one
+ * latent into one frame of samples per call. */
+typedef struct grx_mimi grx_mimi;
+typedef struct grx_mimi_streams grx_mimi_streams;
+/* The decoder half of pockettts.Load (model.go:102-178, 220-227, 280-307):
+ * the pockettts.mimi.* and pockettts.seanet.* settings and the mimi.quant,
+ * mimi.up, mimi.dec_tf.* and mimi.dec.* tensors of a Pocket TTS file, with
+ * the same shape checks. Q8_0 matrices take the int8 path (the reference
+ * packs them and drops their rows), float32 ones MatMul's float path. This
+ * build takes 64-value heads, Q8_0 transformer matrices, Q8_0 matrices
+ * with rows % 32 == 0 and cols <= 4096 and float32 ones with cols % 4 == 0;
+ * other files give GRX_EINVAL or GRX_EFORMAT. */
+int grx_mimi_load(const void* gguf, size_t len, int device, grx_mimi** out);
+void grx_mimi_free(grx_mimi* m);
+/* d, heads, transformer layers, context, upsampling stride, latent dim,
+ * samples per frame, sample rate (any pointer may be NULL). */
+int grx_mimi_dims(const grx_mimi* m, int* d, int* heads, int* layers, int* context, int* upsample, int* ldim,
+                  int* frame, int* sample_rate);
+/* n streams (1 ≤ n ≤ 65535), each a fresh decState (mimi.go:108-124) with
+ * room for max_frames frames. */
+int grx_mimi_streams_create(grx_mimi* m, int n, int max_frames, grx_mimi_streams** out);
+void grx_mimi_streams_free(grx_mimi_streams* s);
+/* Every stream back to a fresh decState; the next frame fades in again. */
+int grx_mimi_streams_reset(grx_mimi_streams* s);
+/* mimiDecoder.decode of one latent per stream (latents [n][ldim], host, the
+ * flow LM's scaled latents), then speakChunk's fade-in on each stream's
+ * first frame (speak.go:185-190): pcm (host, may be NULL) gets [n][frame]
+ * samples. Synchronous. */
+int grx_mimi_decode(grx_mimi_streams* s, const float* latents, float* pcm);
+/* `frames` calls of grx_mimi_decode, device-resident: d_latents
+ * [frames][n][ldim] in, d_pcm [frames][n][frame] out (device pointers on
+ * the set's device). Asynchronous on the library's stream; grx_mimi_sync
+ * waits. */
+int grx_mimi_decode_device(grx_mimi_streams* s, int frames, const float* d_latents, float* d_pcm);
+int grx_mimi_sync(grx_mimi_streams* s);
+/* The cudaStream_t the set's kernels run on. */
+void* grx_mimi_cuda_stream(const grx_mimi_streams* s);
+/* Device kernel launches issued by this set since creation. */
+int64_t grx_mimi_launches(const grx_mimi_streams* s);
+/* Frames decoded since creation or the last reset. */
+int grx_mimi_frames(const grx_mimi_streams* s);
+
 /* ------------------------------------------- TDT decoder (conformer) ------
  * conformer.Model.Decode (conformer/rnnt.go:111-173), the greedy RNN-T /
  * TDT loop over encoder output, for a batch of independent streams. */
