@@ -159,24 +159,6 @@ __global__ void __launch_bounds__(64) k_attn(AttnArgs a) {
   }
 }
 
-// dot4f32avx of two 64-value rows (kernels_amd64.s:157-204): lane l's two
-// fused chains over elements 16c+l and 16c+8+l, added, then HSUM.
-__device__ __forceinline__ float dot4_64(const float* x, const float* y) {
-  float a[8], b[8];
-#pragma unroll
-  for (int l = 0; l < 8; l++) a[l] = b[l] = 0.f;
-#pragma unroll
-  for (int c = 0; c < 64; c += 16)
-#pragma unroll
-    for (int l = 0; l < 8; l++) {
-      a[l] = __fmaf_rn(x[c + l], y[c + l], a[l]);
-      b[l] = __fmaf_rn(x[c + 8 + l], y[c + 8 + l], b[l]);
-    }
-#pragma unroll
-  for (int l = 0; l < 8; l++) a[l] = __fadd_rn(a[l], b[l]);
-  return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[1], a[5])), __fadd_rn(__fadd_rn(a[2], a[6]), __fadd_rn(a[3], a[7])));
-}
-
 // dotF32Go (gemm.go:294-308) of n values: four strided unfused sums.
 template <class X, class Y>
 __device__ __forceinline__ float dot_go(X x, Y y, int n) {
@@ -233,21 +215,59 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
 
   // --- scores of the visible keys, ·1/√64 ---
   float mx = -__int_as_float(0x7f800000);
-  for (int j = v0 + tid; j < nvis; j += 128) {
-    const float* kj = K + (size_t)krow(j) * HD;
-    float sj;
-    if (packed) {
+  if (packed) {
+    for (int j = v0 + tid; j < nvis; j += 128) {
+      const float* kj = K + (size_t)krow(j) * HD;
       float acc = 0.f;
       for (int k = 0; k < HD; k++) acc = __fmaf_rn(qh[k], kj[k], acc);
-      sj = __fadd_rn(0.f, acc);
-    } else if (j < nk4) {
-      sj = dot4_64(qh, kj);
-    } else {
-      sj = dot_go([&](int i) { return qh[i]; }, [&](int i) { return kj[i]; }, HD);
+      const float sj = __fmul_rn(__fadd_rn(0.f, acc), 0.125f);
+      rsc[j] = sj;
+      mx = fmaxf(mx, sj);
     }
-    sj = __fmul_rn(sj, 0.125f);
-    rsc[j] = sj;
-    mx = fmaxf(mx, sj);
+  } else {
+    // dot4f32avx for keys below nk&~3: 16 lanes per key, lane l the AVX
+    // accumulator of elements 16c + l (lanes 8-15 the second register),
+    // two keys per warp pass and U pairs in flight
+    const int half = lane >> 4, l = lane & 15, jend = min(nvis, nk4);
+    const float q0 = qh[l], q1 = qh[16 + l], q2 = qh[32 + l], q3 = qh[48 + l];
+    constexpr int U = 4;
+    for (int j0 = v0 + warp * 2 * U; j0 < jend; j0 += 4 * 2 * U) {
+      float k[U][4];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int j = j0 + 2 * u + half;
+        if (j < jend) {
+          const float* kr = K + (size_t)krow(j) * HD + l;
+          k[u][0] = kr[0];
+          k[u][1] = kr[16];
+          k[u][2] = kr[32];
+          k[u][3] = kr[48];
+        } else {
+          k[u][0] = k[u][1] = k[u][2] = k[u][3] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int j = j0 + 2 * u + half;
+        float acc = __fmaf_rn(q0, k[u][0], 0.f);
+        acc = __fmaf_rn(q1, k[u][1], acc);
+        acc = __fmaf_rn(q2, k[u][2], acc);
+        acc = __fmaf_rn(q3, k[u][3], acc);
+        const float sum = hsum8_lanes(__fadd_rn(acc, __shfl_down_sync(FULL, acc, 8)));
+        if (l == 0 && j < jend) {
+          const float sj = __fmul_rn(sum, 0.125f);
+          rsc[j] = sj;
+          mx = fmaxf(mx, sj);
+        }
+      }
+    }
+    // keys from nk&~3 on: dotF32Go
+    for (int j = max(v0, nk4) + tid; j < nvis; j += 128) {
+      const float* kj = K + (size_t)krow(j) * HD;
+      const float sj = __fmul_rn(dot_go([&](int i) { return qh[i]; }, [&](int i) { return kj[i]; }, HD), 0.125f);
+      rsc[j] = sj;
+      mx = fmaxf(mx, sj);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
@@ -284,17 +304,32 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
     const float* vd = V + d;  // element j of the transposed row d is vd[krow(j)·64]
     float o;
     if (T < 4) {
+      // AddScaled skips zero weights, and every key outside v0 .. nvis − 1
+      // has one; the values come eight at a time ahead of their products
       o = 0.f;
-      for (int j = 0; j < nk; j++) {
-        const float w = rsc[j];
-        if (w != 0.f) o = __fmaf_rn(w, vd[(size_t)krow(j) * HD], o);
+      for (int j0 = v0; j0 < nvis; j0 += 8) {
+        float vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) vv[u] = j0 + u < nvis ? vd[(size_t)krow(j0 + u) * HD] : 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const float w = j0 + u < nvis ? rsc[j0 + u] : 0.f;
+          if (w != 0.f) o = __fmaf_rn(w, vv[u], o);
+        }
       }
     } else if (packed) {
       o = 0.f;
       for (int k0 = 0; k0 < nk; k0 += 256) {
         const int k1 = min(nk, k0 + 256);
         float acc = 0.f;
-        for (int j = k0; j < k1; j++) acc = __fmaf_rn(rsc[j], vd[(size_t)krow(j) * HD], acc);
+        for (int j0 = k0; j0 < k1; j0 += 8) {
+          float vv[8];
+#pragma unroll
+          for (int u = 0; u < 8; u++) vv[u] = j0 + u < k1 ? vd[(size_t)krow(j0 + u) * HD] : 0.f;
+#pragma unroll
+          for (int u = 0; u < 8; u++)
+            if (j0 + u < k1) acc = __fmaf_rn(rsc[j0 + u], vv[u], acc);
+        }
         o = __fadd_rn(o, acc);
       }
     } else {

@@ -105,15 +105,18 @@ __device__ float q8_go(const FArgs& a, int n, X x) {
   return s;
 }
 
-// The physical row of logical row m (FArgs row groups).
+// The physical rows of logical row m in x and y (FArgs row groups).
 __device__ __forceinline__ int fl_row(const FArgs& a, int m) {
   return a.rg_len ? (m / a.rg_len) * a.rg_stride + a.rg_off + m % a.rg_len : m;
+}
+__device__ __forceinline__ int fl_yrow(const FArgs& a, int m) {
+  return a.rg_len ? (m / a.rg_len) * a.ry_stride + a.ry_off + m % a.rg_len : m;
 }
 
 // Output (m, n) of the dot r: bias, then the epilogue.
 __device__ __forceinline__ void fl_out(const FArgs& a, int m, int n, float r) {
   const float v = a.bias ? __fadd_rn(r, a.bias[n]) : r;
-  float* yp = a.y + (size_t)fl_row(a, m) * a.ldy + n;
+  float* yp = a.y + (size_t)fl_yrow(a, m) * a.ldy + n;
   switch (a.epi) {
     case FE_COND:
       *yp = silu_avx(__fadd_rn(v, a.aux[n]));

@@ -1,10 +1,15 @@
 // Mimi's decoder (pockettts/mimi.go:24-150, nn.go:52-64 and 258-327) on
-// the device: the elementwise steps between its products, for n streams
+// the device: the steps between and inside its products, for n streams
 // decoding one latent each per call, rows laid out [stream][time][channel].
-// Each keeps the reference's float32 operations element by element; the
-// products themselves are the int8 path (Q8_0 weights) and the float path
-// (float32 weights) of k_q8.cu, k_flin.cu and k_whisper.cu's packed-order
-// kernel.
+// Each keeps the reference's float32 operations element by element.
+//
+// Grids are (per-stream work, stream), so index arithmetic stays in 32 bits;
+// rows move as float4 (every channel count here is a multiple of 4).
+//
+// A causal convolution of stride 1 and dilation 1 never materialises its
+// im2col matrix: k_mimi_stage writes [carried rows; ELU(x)] contiguously per
+// stream, and output row t's window is then the k·cin values from staged
+// row t on — a row of stride cin that the products read in place.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -14,83 +19,252 @@ namespace grx {
 
 namespace {
 
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+// elu (nn.go:52-64) of the value at index e of its stream's len-value
+// array: per 512-value chunk t = min(v, 0) through ExpSub(t, 0) — EXP8 for
+// the chunk's first len&~7 values, Go's expf for the rest — then
+// max(v, 0) + (t − 1).
+__device__ __forceinline__ float elu_at(float v, int e, int len) {
+  const int c0 = e & ~511, clen = min(512, len - c0);
+  const float t = __fsub_rn(v < 0.f ? v : 0.f, 0.f);
+  const float ex = e - c0 < (clen & ~7) ? exp_avx(t) : expf_go(t);
+  return __fadd_rn(v > 0.f ? v : 0.f, __fsub_rn(ex, 1.f));
+}
+
+__device__ __forceinline__ float4 elu4(float4 v, int e, int len) {
+  return make_float4(elu_at(v.x, e, len), elu_at(v.y, e + 1, len), elu_at(v.z, e + 2, len), elu_at(v.w, e + 3, len));
+}
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
 // decode's depthwise ConvTranspose1d for one latent (mimi.go:130-145): with
 // z the projected latent, row j < 2S of the full output is 0 + z[c]·up[c][j]
-// (cleared, then +=), rows j < S get the partial carried from the last call
+// (cleared, then +=); rows j < S get the partial carried from the last call
 // added and are the transformer's input, rows S.. are the next partial.
-__global__ void k_mimi_up(const float* z, const float* up, const float* part_in, float* x, float* part_out, int n,
-                          int S, int C) {
-  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const size_t total = size_t(n) * 2 * S * C;
-  if (i >= total) return;
-  const int c = int(i % C), j = int((i / C) % (2 * S)), s = int(i / (size_t(C) * 2 * S));
+__global__ void k_mimi_up(const float* z, const float* up, const float* part_in, float* x, float* part_out, int S,
+                          int C) {
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 2 * S * C) return;
+  const int j = i / C, c = i - j * C;
   const float v = __fadd_rn(0.f, __fmul_rn(z[size_t(s) * C + c], up[size_t(c) * 2 * S + j]));
+  const size_t o = size_t(s) * S * C;
   if (j < S)
-    x[(size_t(s) * S + j) * C + c] = __fadd_rn(v, part_in[(size_t(s) * S + j) * C + c]);
+    x[o + i] = __fadd_rn(v, part_in[o + i]);
   else
-    part_out[(size_t(s) * S + j - S) * C + c] = v;
+    part_out[o + i - S * C] = v;
 }
 
-// elu (nn.go:52-64) of every stream's len values: per 512-value chunk of
-// the stream's array, t = min(v, 0) through ExpSub(t, 0) — EXP8 for the
-// chunk's first len&~7 values, Go's expf for the rest — then
-// max(v, 0) + (t − 1).
-__global__ void k_mimi_elu(const float* in, float* out, int n, int len) {
-  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= size_t(n) * len) return;
-  const int e = int(i % len), c0 = e / 512 * 512, clen = min(512, len - c0);
-  const float v = in[i];
-  const float t = v < 0.f ? v : 0.f;
-  const float x = __fsub_rn(t, 0.f);
-  const float ex = e - c0 < (clen & ~7) ? exp_avx(x) : expf_go(x);
-  out[i] = __fadd_rn(v > 0.f ? v : 0.f, __fsub_rn(ex, 1.f));
+// The ELU of every stream's len values (len % 4 == 0).
+__global__ void k_mimi_elu(const float* in, float* out, int len) {
+  const int s = blockIdx.y, i = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i >= len) return;
+  const size_t o = size_t(s) * len + i;
+  st4(out + o, elu4(ld4(in + o), i, len));
 }
 
-// conv.run's window (nn.go:275-300): rows [prev (P); x (T)] of cin values;
-// output row t takes rows t·stride + j·dil for j < k. The last P rows
-// become the next call's prev (a separate buffer: the old one is read here).
-__global__ void k_mimi_im2col(const float* x, const float* prev_in, float* prev_out, float* col, int n, int T, int cin,
+// Rows [carry (P); x (T), through the ELU when elu] of C values into
+// stage [P + T]; carry_out gets the last P of those rows (the next call's).
+__global__ void k_mimi_stage(const float* x, const float* carry_in, float* carry_out, float* stage, int T, int C,
+                             int P, int elu) {
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int C4 = C >> 2, nst = (P + T) * C4;
+  if (i >= nst + P * C4) return;
+  const int q = i < nst ? i : i - nst;
+  const int rq = q / C4, c = (q - rq * C4) * 4, r = rq + (i < nst ? 0 : T);
+  float4 v;
+  if (r < P) {
+    v = ld4(carry_in + (size_t(s) * P + r) * C + c);
+  } else {
+    v = ld4(x + (size_t(s) * T + r - P) * C + c);
+    if (elu) v = elu4(v, (r - P) * C + c, T * C);
+  }
+  if (i < nst)
+    st4(stage + (size_t(s) * (P + T) + r) * C + c, v);
+  else
+    st4(carry_out + (size_t(s) * P + r - T) * C + c, v);
+}
+
+// conv.run's window (nn.go:275-300) for any stride and dilation: rows
+// [prev (P); x (T)] of cin values; output row t takes rows t·stride + j·dil
+// for j < k. The last P rows become the next call's prev.
+__global__ void k_mimi_im2col(const float* x, const float* prev_in, float* prev_out, float* col, int T, int cin,
                               int k, int stride, int dil, int P) {
-  const int To = T / stride;
-  const size_t cols = size_t(k) * cin;
-  const size_t ncol = size_t(n) * To * cols, nprev = size_t(n) * P * cin;
-  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  auto row = [&](int s, int r, int c) {
-    return r < P ? prev_in[(size_t(s) * P + r) * cin + c] : x[(size_t(s) * T + r - P) * cin + c];
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int C4 = cin >> 2, To = T / stride, ncol = To * k * C4;
+  if (i >= ncol + P * C4) return;
+  auto row = [&](int r, int c) {
+    return r < P ? ld4(prev_in + (size_t(s) * P + r) * cin + c) : ld4(x + (size_t(s) * T + r - P) * cin + c);
   };
   if (i < ncol) {
-    const int c = int(i % cin), j = int((i / cin) % k), t = int((i / cols) % To), s = int(i / (cols * To));
-    col[i] = row(s, t * stride + j * dil, c);
-  } else if (i < ncol + nprev) {
-    const size_t q = i - ncol;
-    const int c = int(q % cin), r = int((q / cin) % P), s = int(q / (size_t(P) * cin));
-    prev_out[q] = row(s, T + r, c);
+    const int c4 = i % C4, tj = i / C4, j = tj % k, t = tj / k;
+    st4(col + size_t(s) * To * k * cin + size_t(i) * 4, row(t * stride + j * dil, c4 * 4));
+  } else {
+    const int q = i - ncol, r = q / C4, c = (q % C4) * 4;
+    st4(prev_out + (size_t(s) * P + r) * cin + c, row(T + r, c));
+  }
+}
+
+// The int8 path's activation rounding (quantU8, q8int.go:88-105) of rows of
+// K values: row t of stream s at x + (s·sstride + t)·ldx (rows may overlap:
+// a staged convolution window), through the ELU first when elu_len (x then
+// dense, the element's index in its stream's array is t·K + k). Eight values
+// per thread, a 32-value block over four lanes; outputs dense [n·T][K].
+__global__ void k_mimi_quant(const float* x, int ldx, int sstride, int T, int K, int elu_len, int8_t* q, float2* qs) {
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int K8 = K >> 3;
+  const bool live = i < T * K8;
+  const int t = live ? i / K8 : 0, k = live ? (i - t * K8) * 8 : 0;
+  float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (live) {
+    const float* src = x + (size_t(s) * sstride + t) * ldx + k;
+    float4 a = ld4(src), b = ld4(src + 4);
+    if (elu_len) {
+      a = elu4(a, t * K + k, elu_len);
+      b = elu4(b, t * K + k + 4, elu_len);
+    }
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int u = 0; u < 8; u++) amax = fmaxf(amax, fabsf(v[u]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  if (!live) return;
+  uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+  for (int u = 0; u < 4; u++) {
+    w0 |= uint32_t(uint8_t(quant_val(v[u], amax))) << (8 * u);
+    w1 |= uint32_t(uint8_t(quant_val(v[4 + u], amax))) << (8 * u);
+  }
+  const size_t row = size_t(s) * T + t;
+  *reinterpret_cast<uint2*>(q + row * K + k) = make_uint2(w0, w1);
+  if ((k & 31) == 0) {
+    const float sc = quant_scale(amax);
+    qs[row * (K >> 5) + (k >> 5)] = make_float2(sc, sc);
+  }
+}
+
+// MatMul's packed kernel for a float32 weight (gemm.go k6x16, the rows
+// below m/6·6 of a call): every output starts at its bias (or 0) and gets
+// += the fused chain of each 256-deep pass. Here for a convolution over
+// staged rows: output row t of stream s reads the K = k·cin values from
+// x + (s·sstride + t)·cin on. Rows t < mf; y dense [n·T][N], stored or added
+// to (resid: y = y + c, the residual block's x + o).
+//
+// A CTA holds TM output rows of one stream and all N ≤ 64 columns: the
+// TM + k − 1 input rows (padded by 4 floats) and the weight (as float4s
+// [k/4][4][column group]) sit in shared memory. Thread (cg, rg) — column
+// group fastest, so a warp's lanes span consecutive columns — keeps RM rows
+// rg + i·TMG × the four columns 4cg.. in registers and walks k in order,
+// four values per step: weight reads are consecutive float4s, row reads
+// broadcasts or rows apart, and the outputs leave as whole float4 rows.
+template <int RM>
+__global__ void __launch_bounds__(256) k_mimi_fconv(const float* x, int sstride, int cin, int K, int T, int mf,
+                                                    const float* w, const float* bias, int N, float* y, int resid,
+                                                    int ngp) {
+  extern __shared__ __align__(16) float fsm[];
+  const int tmg = 256 / ngp, TM = tmg * RM, k = K / cin;
+  const int s = blockIdx.y, t0 = blockIdx.x * TM;
+  const int rows = TM + k - 1, cinp = cin + 4, C4 = cin >> 2, K4 = K >> 2;
+  float* xs = fsm;
+  float4* ws = reinterpret_cast<float4*>(fsm + rows * cinp);
+  const int tid = threadIdx.x;
+  const int avail = sstride - t0;  // staged rows from t0 on
+  for (int i = tid; i < rows * C4; i += 256) {
+    const int r = i / C4, c = (i - r * C4) * 4;
+    st4(xs + r * cinp + c, r < avail ? ld4(x + (size_t(s) * sstride + t0 + r) * cin + c) : make_float4(0, 0, 0, 0));
+  }
+  for (int i = tid; i < K4 * 4 * ngp; i += 256) {
+    const int kq = i / (4 * ngp), rem = i - kq * 4 * ngp, u = rem / ngp, g = rem - u * ngp, n = g * 4 + u;
+    ws[i] = n < N ? ld4(w + size_t(n) * K + kq * 4) : make_float4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const int cg = tid % ngp, rg = tid / ngp;
+  if (cg * 4 >= N) return;
+  float cv[RM][4];
+#pragma unroll
+  for (int u = 0; u < 4; u++) {
+    const int n = cg * 4 + u;
+    const float b = bias && n < N ? bias[n] : 0.f;
+#pragma unroll
+    for (int i = 0; i < RM; i++) cv[i][u] = b;
+  }
+  for (int k0 = 0; k0 < K; k0 += 256) {
+    const int k1 = min(K, k0 + 256);
+    float acc[RM][4];
+#pragma unroll
+    for (int i = 0; i < RM; i++)
+#pragma unroll
+      for (int u = 0; u < 4; u++) acc[i][u] = 0.f;
+    int j = k0 / cin, c = k0 - j * cin;
+    for (int kk = k0; kk < k1; kk += 4) {
+      float4 wv[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) wv[u] = ws[((kk >> 2) * 4 + u) * ngp + cg];
+#pragma unroll
+      for (int i = 0; i < RM; i++) {
+        const float4 a = ld4(xs + (rg + i * tmg + j) * cinp + c);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          float r = acc[i][u];
+          r = __fmaf_rn(a.x, wv[u].x, r);
+          r = __fmaf_rn(a.y, wv[u].y, r);
+          r = __fmaf_rn(a.z, wv[u].z, r);
+          r = __fmaf_rn(a.w, wv[u].w, r);
+          acc[i][u] = r;
+        }
+      }
+      c += 4;
+      if (c == cin) c = 0, j++;
+    }
+#pragma unroll
+    for (int i = 0; i < RM; i++)
+#pragma unroll
+      for (int u = 0; u < 4; u++) cv[i][u] = __fadd_rn(cv[i][u], acc[i][u]);
+  }
+  const bool vec = (N & 3) == 0;
+#pragma unroll
+  for (int i = 0; i < RM; i++) {
+    const int t = t0 + rg + i * tmg;
+    if (t >= mf) continue;
+    float* yp = y + (size_t(s) * T + t) * N + cg * 4;
+    if (vec) {
+      float4 v = make_float4(cv[i][0], cv[i][1], cv[i][2], cv[i][3]);
+      if (resid) v = add4(ld4(yp), v);
+      st4(yp, v);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (cg * 4 + u < N) yp[u] = resid ? __fadd_rn(yp[u], cv[i][u]) : cv[i][u];
+    }
   }
 }
 
 // convtr.run (nn.go:305-327): output row q of cout values starts at the bias
 // and adds tap q − t·S of every input row t in order; rows below k − S then
 // add the carried partial. Rows below T·S are the output, the rest (less the
-// bias) the next partial.
-__global__ void k_mimi_convtr(const float* z, const float* bias, const float* part_in, float* y, float* part_out, int n,
+// bias) the next partial. Four channels per thread.
+__global__ void k_mimi_convtr(const float* z, const float* bias, const float* part_in, float* y, float* part_out,
                               int T, int co, int k, int S) {
-  const int L = (T - 1) * S + k, PT = k - S;
-  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= size_t(n) * L * co) return;
-  const int c = int(i % co), q = int((i / co) % L), s = int(i / (size_t(co) * L));
-  float v = bias[c];
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int L = (T - 1) * S + k, PT = k - S, C4 = co >> 2;
+  if (i >= L * C4) return;
+  const int q = i / C4, c = (i - q * C4) * 4;
+  const float4 b = ld4(bias + c);
+  float4 v = b;
   const int t0 = q >= k ? (q - k) / S + 1 : 0, t1 = min(T - 1, q / S);
-  for (int t = t0; t <= t1; t++) v = __fadd_rn(v, z[((size_t(s) * T + t) * k + (q - t * S)) * co + c]);
-  if (q < PT) v = __fadd_rn(v, part_in[(size_t(s) * PT + q) * co + c]);
+  const float* zs = z + size_t(s) * T * k * co;
+  for (int t = t0; t <= t1; t++) v = add4(v, ld4(zs + (size_t(t) * k + (q - t * S)) * co + c));
+  if (q < PT) v = add4(v, ld4(part_in + (size_t(s) * PT + q) * co + c));
   if (q < T * S)
-    y[(size_t(s) * T * S + q) * co + c] = v;
+    st4(y + (size_t(s) * T * S + q) * co + c, v);
   else
-    part_out[(size_t(s) * PT + q - T * S) * co + c] = __fsub_rn(v, bias[c]);
-}
-
-__global__ void k_mimi_add(const float* a, const float* b, float* y, size_t n) {
-  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i < n) y[i] = __fadd_rn(a[i], b[i]);
+    st4(part_out + (size_t(s) * PT + q - T * S) * co + c,
+        make_float4(__fsub_rn(v.x, b.x), __fsub_rn(v.y, b.y), __fsub_rn(v.z, b.z), __fsub_rn(v.w, b.w)));
 }
 
 // Row r of a call is stream r / S at position pos[r / S] + r % S.
@@ -119,45 +293,98 @@ __global__ void k_mimi_fade(float* pcm, int* started, int frame, int fade) {
   if (threadIdx.x == 0) started[s] = 1;
 }
 
-unsigned blocks_for(size_t n) { return unsigned((n + 255) / 256); }
+dim3 grid2(int per_stream, int n) { return dim3(unsigned((per_stream + 255) / 256), unsigned(n)); }
+
+// k_mimi_fconv's tiling: column groups of four, rounded up to a power of two
+// (ngp lanes per row), and rows per thread: a CTA holds 256 output rows for
+// N ≤ 8, 128 for N ≤ 32 and 64 beyond.
+int fconv_ngp(int N) {
+  const int ncg = (N + 3) / 4;
+  int p = 1;
+  while (p < ncg) p *= 2;
+  return p;
+}
+
+int fconv_rm(int ngp) { return ngp <= 2 ? ngp : ngp <= 8 ? 128 * ngp / 256 : 4; }
+
+size_t fconv_smem(int cin, int K, int N) {
+  const int ngp = fconv_ngp(N), TM = 256 / ngp * fconv_rm(ngp);
+  return (size_t(TM + K / cin - 1) * (cin + 4) + size_t(K) * 4 * ngp) * sizeof(float);
+}
+
+constexpr size_t kFconvSmemMax = 200 * 1024;
 
 }  // namespace
 
 void launch_mimi_up(const float* z, const float* up, const float* part_in, float* x, float* part_out, int n, int S,
                     int C, cudaStream_t st) {
-  k_mimi_up<<<blocks_for(size_t(n) * 2 * S * C), 256, 0, st>>>(z, up, part_in, x, part_out, n, S, C);
+  k_mimi_up<<<grid2(2 * S * C, n), 256, 0, st>>>(z, up, part_in, x, part_out, S, C);
 }
 
 void launch_mimi_elu(const float* in, float* out, int n, int len, cudaStream_t st) {
-  k_mimi_elu<<<blocks_for(size_t(n) * len), 256, 0, st>>>(in, out, n, len);
+  k_mimi_elu<<<grid2(len / 4, n), 256, 0, st>>>(in, out, len);
+}
+
+void launch_mimi_stage(const float* x, const float* carry_in, float* carry_out, float* stage, int n, int T, int C,
+                       int P, bool elu, cudaStream_t st) {
+  k_mimi_stage<<<grid2((2 * P + T) * (C / 4), n), 256, 0, st>>>(x, carry_in, carry_out, stage, T, C, P, elu ? 1 : 0);
 }
 
 void launch_mimi_im2col(const float* x, const float* prev_in, float* prev_out, float* col, int n, int T, int cin, int k,
                         int stride, int dil, int P, cudaStream_t st) {
-  const size_t total = size_t(n) * (T / stride) * k * cin + size_t(n) * P * cin;
-  k_mimi_im2col<<<blocks_for(total), 256, 0, st>>>(x, prev_in, prev_out, col, n, T, cin, k, stride, dil, P);
+  k_mimi_im2col<<<grid2((T / stride * k + P) * (cin / 4), n), 256, 0, st>>>(x, prev_in, prev_out, col, T, cin, k,
+                                                                              stride, dil, P);
+}
+
+void launch_mimi_quant(const float* x, int ldx, int sstride, int n, int T, int K, int elu_len, int8_t* q, float2* qs,
+                       cudaStream_t st) {
+  k_mimi_quant<<<grid2(T * (K / 8), n), 256, 0, st>>>(x, ldx, sstride, T, K, elu_len, q, qs);
+}
+
+bool mimi_fconv_fits(int cin, int K, int N) {
+  return N >= 1 && N <= 64 && cin % 4 == 0 && K % cin == 0 && fconv_smem(cin, K, N) <= kFconvSmemMax;
+}
+
+void launch_mimi_fconv(const float* x, int sstride, int cin, int K, int n, int T, int mf, const float* w,
+                       const float* bias, int N, float* y, bool resid, cudaStream_t st) {
+  const int ngp = fconv_ngp(N), rm = fconv_rm(ngp), TM = 256 / ngp * rm;
+  const size_t sm = fconv_smem(cin, K, N);
+  const dim3 grid(unsigned((mf + TM - 1) / TM), unsigned(n));
+  const int r = resid ? 1 : 0;
+  switch (rm) {
+    case 1:
+      k_mimi_fconv<1><<<grid, 256, sm, st>>>(x, sstride, cin, K, T, mf, w, bias, N, y, r, ngp);
+      break;
+    case 2:
+      k_mimi_fconv<2><<<grid, 256, sm, st>>>(x, sstride, cin, K, T, mf, w, bias, N, y, r, ngp);
+      break;
+    default:
+      k_mimi_fconv<4><<<grid, 256, sm, st>>>(x, sstride, cin, K, T, mf, w, bias, N, y, r, ngp);
+  }
 }
 
 void launch_mimi_convtr(const float* z, const float* bias, const float* part_in, float* y, float* part_out, int n, int T,
                         int co, int k, int S, cudaStream_t st) {
-  k_mimi_convtr<<<blocks_for(size_t(n) * ((T - 1) * S + k) * co), 256, 0, st>>>(z, bias, part_in, y, part_out, n, T,
-                                                                                 co, k, S);
+  k_mimi_convtr<<<grid2(((T - 1) * S + k) * (co / 4), n), 256, 0, st>>>(z, bias, part_in, y, part_out, T, co, k, S);
 }
 
 void launch_mimi_rows(const int* pos, int S, int R, int* rowpos, cudaStream_t st) {
-  k_mimi_rows<<<blocks_for(size_t(R)), 256, 0, st>>>(pos, S, R, rowpos);
+  k_mimi_rows<<<(R + 255) / 256, 256, 0, st>>>(pos, S, R, rowpos);
 }
 
 void launch_mimi_advance(int* pos, int S, int n, cudaStream_t st) {
-  k_mimi_advance<<<blocks_for(size_t(n)), 256, 0, st>>>(pos, S, n);
+  k_mimi_advance<<<(n + 255) / 256, 256, 0, st>>>(pos, S, n);
 }
 
 void launch_mimi_fade(float* pcm, int* started, int n, int frame, int fade, cudaStream_t st) {
   k_mimi_fade<<<n, 128, 0, st>>>(pcm, started, frame, fade);
 }
 
-void launch_mimi_add(const float* a, const float* b, float* y, size_t n, cudaStream_t st) {
-  k_mimi_add<<<blocks_for(n), 256, 0, st>>>(a, b, y, n);
+void mimi_kernels_init() {
+  const int sm = int(kFconvSmemMax);
+  cudaFuncSetAttribute(k_mimi_fconv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  cudaFuncSetAttribute(k_mimi_fconv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  cudaFuncSetAttribute(k_mimi_fconv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
 }
 
 }  // namespace grx

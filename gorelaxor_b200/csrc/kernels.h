@@ -144,20 +144,34 @@ struct AttnRowsArgs {
 
 void launch_attn_rows(const AttnRowsArgs& a, int nstreams, int tmax, cudaStream_t st);
 
-// Mimi's decoder steps between products (k_mimi.cu); rows [stream][time][channel].
+// ---- Mimi's decoder (k_mimi.cu); rows [stream][time][channel], n streams ----
 void launch_mimi_up(const float* z, const float* up, const float* part_in, float* x, float* part_out, int n, int S,
                     int C, cudaStream_t st);
+// The ELU of each stream's len values (len % 4 == 0), in place when in == out.
 void launch_mimi_elu(const float* in, float* out, int n, int len, cudaStream_t st);
+// stage [n][P + T][C] = [carry_in; x or ELU(x)]; carry_out = its last P rows.
+void launch_mimi_stage(const float* x, const float* carry_in, float* carry_out, float* stage, int n, int T, int C,
+                       int P, bool elu, cudaStream_t st);
 void launch_mimi_im2col(const float* x, const float* prev_in, float* prev_out, float* col, int n, int T, int cin, int k,
                         int stride, int dil, int P, cudaStream_t st);
+// Q8_0 rounding of rows t < T of K values at x + (s·sstride + t)·ldx, ELU
+// first when elu_len (> 0: the per-stream array length, x dense), into
+// dense q [n·T][K], qs [n·T][K/32].
+void launch_mimi_quant(const float* x, int ldx, int sstride, int n, int T, int K, int elu_len, int8_t* q, float2* qs,
+                       cudaStream_t st);
+// The packed-order float32 product over staged rows (rows t < mf of each
+// stream, y dense [n·T][N]); mimi_fconv_fits says whether a shape fits.
+bool mimi_fconv_fits(int cin, int K, int N);
+void launch_mimi_fconv(const float* x, int sstride, int cin, int K, int n, int T, int mf, const float* w,
+                       const float* bias, int N, float* y, bool resid, cudaStream_t st);
 void launch_mimi_convtr(const float* z, const float* bias, const float* part_in, float* y, float* part_out, int n, int T,
                         int co, int k, int S, cudaStream_t st);
-void launch_mimi_add(const float* a, const float* b, float* y, size_t n, cudaStream_t st);
 // rowpos[r] = pos[r / S] + r % S for the R rows of a call; pos[i] += S after it.
 void launch_mimi_rows(const int* pos, int S, int R, int* rowpos, cudaStream_t st);
 void launch_mimi_advance(int* pos, int S, int n, cudaStream_t st);
 // The fade-in of each not yet started stream's frame (pcm [n][frame]); marks it started.
 void launch_mimi_fade(float* pcm, int* started, int n, int frame, int fade, cudaStream_t st);
+void mimi_kernels_init();
 
 // x[r] = embedding row ids[r] (float32 rows of width d).
 void launch_embed_rows(float* x, const float* embed, const int* ids, int rows, int d, cudaStream_t st);
@@ -205,10 +219,10 @@ struct FArgs {
   // scaled rows to io.
   const FrameIO* io = nullptr;
   bool x_noise = false, aux_noise = false, io_out = false;
-  // Row groups (FE_BIAS and plain stores only): logical row m is physical
-  // row (m / rg_len)·rg_stride + rg_off + m % rg_len of x and y (rg_len 0:
-  // row m).
-  int rg_len = 0, rg_stride = 0, rg_off = 0;
+  // Row groups (FE_BIAS and FE_RESID only): logical row m is row
+  // (m / rg_len)·rg_stride + rg_off + m % rg_len of x and row
+  // (m / rg_len)·ry_stride + ry_off + m % rg_len of y (rg_len 0: row m).
+  int rg_len = 0, rg_stride = 0, rg_off = 0, ry_stride = 0, ry_off = 0;
 };
 
 void launch_flin(const FArgs& a, int M, cudaStream_t st);

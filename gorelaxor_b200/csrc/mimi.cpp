@@ -94,7 +94,7 @@ struct grx_mimi_streams {
   // per carried-rows slot (steps in order; a residual block has two), two buffers
   std::vector<float*> carry[2];
   std::vector<size_t> carry_n;  // values per stream
-  float *sa = nullptr, *sb = nullptr, *se = nullptr, *col = nullptr, *zt = nullptr, *sh = nullptr;
+  float *sa = nullptr, *sb = nullptr, *se = nullptr, *stage = nullptr, *col = nullptr, *zt = nullptr, *sh = nullptr;
   int par = 0;
   int64_t launches = 0;
   ~grx_mimi_streams() {
@@ -105,10 +105,14 @@ struct grx_mimi_streams {
 
 namespace {
 
-// The largest per-stream sizes one call needs, from the step plan.
+// The largest per-stream sizes one call needs, from the step plan (floats,
+// except qk: the int8 path's rounded activations, values).
 struct MimiSizes {
-  size_t act = 0, col = 0, zt = 0, h = 0, qk = 0;
+  size_t act = 0, stage = 0, col = 0, zt = 0, h = 0, qk = 0;
 };
+
+// A convolution of stride 1 and dilation 1 reads its window from staged rows.
+bool staged(const MConv& c) { return c.k > 1 && c.stride == 1 && c.dil == 1; }
 
 MimiSizes mimi_sizes(const grx_mimi* m) {
   MimiSizes s;
@@ -119,14 +123,17 @@ MimiSizes mimi_sizes(const grx_mimi* m) {
   prod(m->quant, 1);
   auto conv = [&](const MConv& c, int t) {
     const int To = t / c.stride;
-    if (!(c.k == 1 && c.stride == 1)) s.col = std::max(s.col, size_t(To) * c.k * c.cin);
+    if (staged(c))
+      s.stage = std::max(s.stage, size_t(c.past() + t) * c.cin);
+    else if (!(c.k == 1 && c.stride == 1))
+      s.col = std::max(s.col, size_t(To) * c.k * c.cin);
     prod(c.w, To);
     return To;
   };
   for (const MStep& st : m->steps) {
+    s.act = std::max(s.act, size_t(T) * C);
     if (st.kind == 0) {
-      const int To = conv(st.c, T);
-      T = To;
+      T = conv(st.c, T);
       C = st.c.cout;
     } else if (st.kind == 1) {
       s.zt = std::max(s.zt, size_t(T) * st.c.k * st.c.cout);
@@ -143,16 +150,27 @@ MimiSizes mimi_sizes(const grx_mimi* m) {
   return s;
 }
 
-// y[n·T][N] = x[n·T][K]·Wᵀ (+ bias) with the reference's order for a call of
-// T rows per stream (linear of mimi.go's steps, kern.go:185-201).
-void mimi_product(grx_mimi_streams* s, const MW& w, const float* x, int T, const float* bias, float* y) {
+// A product's input: T rows per stream, row t of stream s the K values at
+// x + (s·sstride + t)·ldx (ldx < K: a staged convolution window), through the
+// ELU first when elu_len (the per-stream array length; x dense, Q8_0 only).
+struct MIn {
+  const float* x;
+  int ldx, sstride, K, elu_len;
+};
+
+// y[n·T][N] = (or, resid, +=) the input times Wᵀ (+ bias), with the
+// reference's order for a call of T rows per stream (kern.Linear,
+// kern.go:185-201): the int8 path for a Q8_0 weight; for a float32 one
+// gemvRows up to 16 rows, else the packed kernel for each stream's first
+// T/6·6 rows and gemvRows for the rest.
+void mimi_product(grx_mimi_streams* s, const MW& w, const MIn& in, int T, const float* bias, float* y, bool resid) {
   const int n = s->n, N = w.rows, K = w.cols, M = n * T;
   cudaStream_t st = s->st;
   if (w.q8) {
-    launch_quant(x, M, K, s->aq, s->as, st);
+    launch_mimi_quant(in.x, in.ldx, in.sstride, n, T, K, in.elu_len, s->aq, s->as, st);
     s->launches++;
     EpiArgs e;
-    e.epi = EPI_STORE;
+    e.epi = resid ? EPI_RESID : EPI_STORE;
     e.bias = bias;
     e.ldy = N;
     if (M <= 8 || K % 64 == 0) {
@@ -169,58 +187,82 @@ void mimi_product(grx_mimi_streams* s, const MW& w, const float* x, int T, const
     }
     return;
   }
-  FArgs a;
-  a.epi = FE_BIAS;
-  a.x = x;
-  a.ldx = K;
-  a.wf = w.f;
-  a.N = N;
-  a.K = K;
-  a.bias = bias;
-  a.y = y;
-  a.ldy = N;
-  if (T <= 16) {  // gemvRows for every row
-    launch_flin(a, M, st);
+  const int mf = T > 16 ? T / 6 * 6 : 0;  // rows per stream through the packed kernel
+  if (mf > 0) {
+    if (mimi_fconv_fits(in.ldx, K, N)) {
+      launch_mimi_fconv(in.x, in.sstride, in.ldx, K, n, T, mf, w.f, bias, N, y, resid, st);
+    } else {
+      WmmArgs p;
+      p.a = in.x;
+      p.lda = in.ldx;
+      p.a_zs = size_t(in.sstride) * in.ldx;
+      p.m = mf;
+      p.w.f = w.f;
+      p.w.rows = N;
+      p.w.cols = K;
+      p.bias = bias;
+      p.mode = resid ? WM_RESID : WM_STORE;
+      p.c = y;
+      p.ldc = N;
+      p.c_zs = size_t(T) * N;
+      launch_wmm(p, n, st);
+    }
     s->launches++;
-    return;
   }
-  // the packed kernel for each stream's first T/6·6 rows, gemvRows for the rest
-  const int mf = T / 6 * 6;
-  WmmArgs p;
-  p.a = x;
-  p.lda = K;
-  p.a_zs = size_t(T) * K;
-  p.m = mf;
-  p.w.f = w.f;
-  p.w.rows = N;
-  p.w.cols = K;
-  p.bias = bias;
-  p.mode = WM_STORE;
-  p.c = y;
-  p.ldc = N;
-  p.c_zs = size_t(T) * N;
-  launch_wmm(p, n, st);
-  s->launches++;
   if (mf < T) {
+    FArgs a;
+    a.epi = resid ? FE_RESID : FE_BIAS;
+    a.x = in.x;
+    a.ldx = in.ldx;
+    a.wf = w.f;
+    a.N = N;
+    a.K = K;
+    a.bias = bias;
+    a.y = y;
+    a.ldy = N;
     a.rg_len = T - mf;
-    a.rg_stride = T;
+    a.rg_stride = in.sstride;
     a.rg_off = mf;
+    a.ry_stride = T;
+    a.ry_off = mf;
     launch_flin(a, n * (T - mf), st);
     s->launches++;
   }
 }
 
-// conv.run (nn.go:275-300) for T rows per stream; carried rows in slot ci.
-void mimi_conv(grx_mimi_streams* s, const MConv& c, int ci, const float* x, int T, float* y) {
+// conv.run (nn.go:275-300) for the T rows per stream of x (dense
+// [n][T][cin]), through the ELU first when elu; carried rows in slot ci.
+void mimi_conv(grx_mimi_streams* s, const MConv& c, int ci, const float* x, int T, bool elu, float* y, bool resid) {
+  const int n = s->n, cin = c.cin;
+  cudaStream_t st = s->st;
   if (c.k == 1 && c.stride == 1) {
-    mimi_product(s, c.w, x, T, c.b, y);
+    if (elu && !c.w.q8) {
+      launch_mimi_elu(x, s->se, n, T * cin, st);
+      s->launches++;
+      x = s->se;
+      elu = false;
+    }
+    mimi_product(s, c.w, MIn{x, cin, T, cin, elu ? T * cin : 0}, T, c.b, y, resid);
     return;
   }
   const int P = c.past();
-  launch_mimi_im2col(x, s->carry[s->par][size_t(ci)], s->carry[s->par ^ 1][size_t(ci)], s->col, s->n, T, c.cin, c.k,
-                     c.stride, c.dil, P, s->st);
+  float* cin_ = s->carry[s->par][size_t(ci)];
+  float* cout_ = s->carry[s->par ^ 1][size_t(ci)];
+  if (staged(c)) {
+    launch_mimi_stage(x, cin_, cout_, s->stage, n, T, cin, P, elu, st);
+    s->launches++;
+    mimi_product(s, c.w, MIn{s->stage, cin, P + T, c.k * cin, 0}, T, c.b, y, resid);
+    return;
+  }
+  if (elu) {
+    launch_mimi_elu(x, s->se, n, T * cin, st);
+    s->launches++;
+    x = s->se;
+  }
+  launch_mimi_im2col(x, cin_, cout_, s->col, n, T, cin, c.k, c.stride, c.dil, P, st);
   s->launches++;
-  mimi_product(s, c.w, s->col, T / c.stride, c.b, y);
+  const int To = T / c.stride;
+  mimi_product(s, c.w, MIn{s->col, c.k * cin, To, c.k * cin, 0}, To, c.b, y, resid);
 }
 
 // transformer.forward (nn.go:142-182) with the window and layer scales for
@@ -301,7 +343,7 @@ void mimi_enqueue(grx_mimi_streams* s, const float* d_lat, float* d_pcm) {
   grx_mimi* m = s->m;
   const int n = s->n, C = m->d, S = m->S;
   cudaStream_t st = s->st;
-  mimi_product(s, m->quant, d_lat, 1, nullptr, s->z);
+  mimi_product(s, m->quant, MIn{d_lat, m->ldim, 1, m->ldim, 0}, 1, nullptr, s->z, false);
   launch_mimi_up(s->z, m->up, s->up_part[s->par], s->x, s->up_part[s->par ^ 1], n, S, C, st);
   s->launches++;
   mimi_transformer(s);
@@ -310,21 +352,24 @@ void mimi_enqueue(grx_mimi_streams* s, const float* d_lat, float* d_pcm) {
   size_t ci = 0;
   auto other = [&](const float* p) { return p == s->sa ? s->sb : s->sa; };
   for (const MStep& stp : m->steps) {
-    const float* in = x;
-    if (stp.elu) {
-      launch_mimi_elu(x, s->se, n, T * Cc, st);
-      s->launches++;
-      in = s->se;
-    }
     if (stp.kind == 0) {
-      float* y = stp.c.cout == 1 && &stp == &m->steps.back() ? d_pcm : other(x);
-      mimi_conv(s, stp.c, int(ci++), in, T, y);
+      float* y = &stp == &m->steps.back() && stp.c.cout == 1 && stp.c.stride == 1 ? d_pcm : other(x);
+      mimi_conv(s, stp.c, int(ci++), x, T, stp.elu, y, false);
       T /= stp.c.stride;
       Cc = stp.c.cout;
       x = y;
     } else if (stp.kind == 1) {
       const MConv& c = stp.c;
-      mimi_product(s, c.w, in, T, nullptr, s->zt);
+      const float* in = x;
+      int elu_len = 0;
+      if (stp.elu && c.w.q8) {
+        elu_len = T * Cc;
+      } else if (stp.elu) {
+        launch_mimi_elu(x, s->se, n, T * Cc, st);
+        s->launches++;
+        in = s->se;
+      }
+      mimi_product(s, c.w, MIn{in, Cc, T, Cc, elu_len}, T, nullptr, s->zt, false);
       float* y = other(x);
       launch_mimi_convtr(s->zt, c.b, s->carry[s->par][ci], y, s->carry[s->par ^ 1][ci], n, T, c.cout, c.k, c.stride,
                          st);
@@ -334,20 +379,14 @@ void mimi_enqueue(grx_mimi_streams* s, const float* d_lat, float* d_pcm) {
       Cc = c.cout;
       x = y;
     } else {
-      launch_mimi_elu(x, s->se, n, T * Cc, st);
-      mimi_conv(s, stp.ra, int(ci), s->se, T, s->sh);
-      launch_mimi_elu(s->sh, s->sh, n, T * stp.ra.cout, st);
-      float* o = other(x);
-      mimi_conv(s, stp.rb, int(ci + 1), s->sh, T, o);
-      launch_mimi_add(x, o, o, size_t(n) * T * Cc, st);
-      s->launches += 3;
+      // x + conv1x1(ELU(conv(ELU(x)))), the sum added into x in place
+      mimi_conv(s, stp.ra, int(ci), x, T, true, s->sh, false);
+      mimi_conv(s, stp.rb, int(ci + 1), s->sh, T, true, x, true);
       ci += 2;
-      x = o;
     }
   }
-  if (x != d_pcm) {  // a decoder that does not end in the one-channel conv
+  if (x != d_pcm)  // a decoder that does not end in the one-channel conv
     cudaMemcpyAsync(d_pcm, x, sizeof(float) * size_t(n) * T * Cc, cudaMemcpyDeviceToDevice, st);
-  }
   launch_mimi_fade(d_pcm, s->started, n, m->frame, m->sample_rate / 200, st);
   s->launches++;
   s->par ^= 1;
@@ -606,6 +645,7 @@ int grx_mimi_streams_create(grx_mimi* m, int n, int max_frames, grx_mimi_streams
   s->sa = s->ar.alloc<float>(N * z.act, &rc);
   s->sb = s->ar.alloc<float>(N * z.act, &rc);
   s->se = s->ar.alloc<float>(N * z.act, &rc);
+  s->stage = s->ar.alloc<float>(N * z.stage, &rc);
   s->col = s->ar.alloc<float>(N * z.col, &rc);
   s->zt = s->ar.alloc<float>(N * z.zt, &rc);
   s->sh = s->ar.alloc<float>(N * z.h, &rc);

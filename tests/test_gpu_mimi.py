@@ -31,6 +31,9 @@ CONFIGS = {
     # Mimi's own 2 rows per latent (attend's AddScaled for the values), a
     # 5-position window over a 6-row ring
     "upsample2": dataclasses.replace(_BASE, upsample=2, ratios=(5, 4), context=5),
+    # two residual blocks per ratio, the second dilated (its window through
+    # an explicit im2col)
+    "dilated": dataclasses.replace(_BASE, nres=2),
 }
 
 
