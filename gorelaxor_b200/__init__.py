@@ -111,6 +111,9 @@ def _sig(lib):
         "grx_whisper_batch_free": (None, [P]),
         "grx_whisper_set_audio": (I, [P, P]),
         "grx_whisper_set_audio_device": (I, [P, P]),
+        "grx_whisper_encode": (I, [P, P]),
+        "grx_whisper_encode_device": (I, [P, P]),
+        "grx_whisper_encoder_out": (I, [P, P]),
         "grx_whisper_prompt": (I, [P, P, I, I, P]),
         "grx_whisper_run": (I, [P, I, P]),
         "grx_whisper_run_device": (I, [P, I, P]),
@@ -585,6 +588,22 @@ class WhisperBatch:
 
     def set_audio_device(self, d_enc: int):
         _check(lib().grx_whisper_set_audio_device(self._h, C.c_void_p(d_enc)))
+
+    def encode(self, mel: np.ndarray):
+        """Model.encode (encoder.go:10-118) of each stream's window, mel
+        [n][n_mels][3000], then the window's cross K/V (as set_audio)."""
+        a = np.ascontiguousarray(mel, np.float32)
+        _check(lib().grx_whisper_encode(self._h, _ptr(a)))
+
+    def encode_device(self, d_mel: int):
+        _check(lib().grx_whisper_encode_device(self._h, C.c_void_p(d_mel)))
+
+    def encoder_out(self) -> np.ndarray:
+        """The window's encoder output [n][1500][n_state]."""
+        m = self.model
+        out = np.empty((self.n, m.n_audio_ctx, m.n_state), np.float32)
+        _check(lib().grx_whisper_encoder_out(self._h, _ptr(out)))
+        return out
 
     def prompt(self, prompt, sot_at: int) -> np.ndarray:
         """prompt [n][np] (or one prompt for all); returns no_speech [n]."""

@@ -35,6 +35,7 @@ int device_init(int dev) {
     tdt_kernels_init();
     whisper_kernels_init();
     mimi_kernels_init();
+    attn_kernels_init();
     cudaError_t e = cudaGetLastError();  // attribute calls report here; clear it
     if (e != cudaSuccess) return fail(GRX_ECUDA, std::string("kernel attributes: ") + cudaGetErrorString(e));
     done[size_t(dev)] = true;

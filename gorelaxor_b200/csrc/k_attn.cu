@@ -174,6 +174,11 @@ __device__ __forceinline__ float dot_go(X x, Y y, int n) {
   return __fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3);
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(uint32_t(__cvta_generic_to_shared(dst))),
+               "l"(src));
+}
+
 // transformer.attend for T queries of one stream (nn.go:200-243, T > 1),
 // one block per (head, stream, query t). The reference makes each head's
 // T × nk scores one kern.MatMulF32 (nk = pos0 + T, the call's keys) and, for
@@ -187,7 +192,7 @@ __device__ __forceinline__ float dot_go(X x, Y y, int n) {
 // they are never computed here and enter the value products as zeros. For
 // T < 4 the values are added key by key (AddScaled), skipping zero weights.
 __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
-  extern __shared__ float rsc[];  // [nk] scores, then weights
+  extern __shared__ __align__(16) float rsc[];  // [nk] scores, then weights; then (vstage) V rows
   __shared__ float qh[HD];
   __shared__ float red[8];
   const int h = blockIdx.x, si = blockIdx.y, t = blockIdx.z;
@@ -209,6 +214,16 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   const float* K = a.kv + kbase;
   const float* V = a.kv + vbase;
   if (tid < HD) qh[tid] = a.q[(size_t)row * a.d + h * HD + tid];
+  // With vstage, the call's value rows come into shared memory while the
+  // scores are computed (rows [nk][64] after vstage score slots).
+  float* vsm = rsc + a.vstage;
+  if (a.vstage) {
+    for (int i = tid; i < nk * (HD / 4); i += 128) {
+      const int j = i / (HD / 4), c = (i % (HD / 4)) * 4;
+      cp_async16(vsm + j * HD + c, V + (size_t)krow(j) * HD + c);
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+  }
   __syncthreads();
   const bool packed = T > 16 && t < T / 6 * 6;  // this query row goes through the packed kernel
   const int nk4 = nk & ~3;
@@ -299,9 +314,15 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   __syncthreads();
 
   // --- values: thread d owns output d ---
+  if (a.vstage) {
+    asm volatile("cp.async.wait_all;\n" ::);
+    __syncthreads();
+  }
   if (tid < HD) {
     const int d = tid;
     const float* vd = V + d;  // element j of the transposed row d is vd[krow(j)·64]
+    const float* vsd = vsm + d;
+    auto vat = [&](int j) { return a.vstage ? vsd[j * HD] : vd[(size_t)krow(j) * HD]; };
     float o;
     if (T < 4) {
       // AddScaled skips zero weights, and every key outside v0 .. nvis − 1
@@ -310,7 +331,7 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
       for (int j0 = v0; j0 < nvis; j0 += 8) {
         float vv[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++) vv[u] = j0 + u < nvis ? vd[(size_t)krow(j0 + u) * HD] : 0.f;
+        for (int u = 0; u < 8; u++) vv[u] = j0 + u < nvis ? vat(j0 + u) : 0.f;
 #pragma unroll
         for (int u = 0; u < 8; u++) {
           const float w = j0 + u < nvis ? rsc[j0 + u] : 0.f;
@@ -325,7 +346,7 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
         for (int j0 = k0; j0 < k1; j0 += 8) {
           float vv[8];
 #pragma unroll
-          for (int u = 0; u < 8; u++) vv[u] = j0 + u < k1 ? vd[(size_t)krow(j0 + u) * HD] : 0.f;
+          for (int u = 0; u < 8; u++) vv[u] = j0 + u < k1 ? vat(j0 + u) : 0.f;
 #pragma unroll
           for (int u = 0; u < 8; u++)
             if (j0 + u < k1) acc = __fmaf_rn(rsc[j0 + u], vv[u], acc);
@@ -340,8 +361,8 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
       for (int c = 0; c < kk; c += 16)
 #pragma unroll
         for (int l = 0; l < 8; l++) {
-          av[l] = __fmaf_rn(rsc[c + l], vd[(size_t)krow(c + l) * HD], av[l]);
-          bv[l] = __fmaf_rn(rsc[c + 8 + l], vd[(size_t)krow(c + 8 + l) * HD], bv[l]);
+          av[l] = __fmaf_rn(rsc[c + l], vat(c + l), av[l]);
+          bv[l] = __fmaf_rn(rsc[c + 8 + l], vat(c + 8 + l), bv[l]);
         }
       if (kk > 0) {
 #pragma unroll
@@ -352,8 +373,7 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
         o = 0.f;
       }
       if (kk < nk)
-        o = __fadd_rn(o, dot_go([&](int i) { return rsc[kk + i]; }, [&](int i) { return vd[(size_t)krow(kk + i) * HD]; },
-                                nk - kk));
+        o = __fadd_rn(o, dot_go([&](int i) { return rsc[kk + i]; }, [&](int i) { return vat(kk + i); }, nk - kk));
     }
     if (a.out) a.out[(size_t)row * a.d + h * HD + d] = o;
     float sc;
@@ -370,13 +390,27 @@ __global__ void k_embed_rows(float* x, const float* embed, const int* ids, int r
   for (int i = threadIdx.x; i < d; i += blockDim.x) x[(size_t)r * d + i] = src[i];
 }
 
+// The most keys whose value rows k_attn_rows stages in shared memory.
+constexpr int kVStageRows = 384;
+
 }  // namespace
 
-void launch_attn_rows(const AttnRowsArgs& a, int nstreams, int tmax, cudaStream_t st) {
+void launch_attn_rows(const AttnRowsArgs& a0, int nstreams, int tmax, cudaStream_t st) {
   if (nstreams < 1 || tmax < 1) return;
-  // the scores of one query: at most the call's keys
+  // the scores of one query: at most the call's keys; up to kVStageRows of
+  // them, the value rows too
+  AttnRowsArgs a = a0;
   const int nk = a.context > 0 ? std::min(a.cap, a.context - 1 + tmax) : a.cap;
-  k_attn_rows<<<dim3(a.heads, nstreams, tmax), 128, size_t(nk) * sizeof(float), st>>>(a);
+  a.vstage = nk <= kVStageRows ? (nk + 3) & ~3 : 0;
+  const size_t sm = (a.vstage ? size_t(a.vstage) * (1 + HD) : size_t(nk)) * sizeof(float);
+  k_attn_rows<<<dim3(a.heads, nstreams, tmax), 128, sm, st>>>(a);
+}
+
+// Dynamic shared memory up to 200 KB (the per-block limit less the kernels'
+// static arrays, with room to spare).
+void attn_kernels_init() {
+  cudaFuncSetAttribute(k_attn_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
 }
 
 void launch_embed_rows(float* x, const float* embed, const int* ids, int rows, int d, cudaStream_t st) {

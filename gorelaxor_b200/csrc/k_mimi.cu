@@ -162,22 +162,39 @@ __global__ void k_mimi_quant(const float* x, int ldx, int sstride, int T, int K,
 // rg + i·TMG × the four columns 4cg.. in registers and walks k in order,
 // four values per step: weight reads are consecutive float4s, row reads
 // broadcasts or rows apart, and the outputs leave as whole float4 rows.
+//
+// Fused (a.virt): the rows are not staged beforehand; x is dense [n][T][cin]
+// and row r of the window is carry row r (r < P) or ELU?(x row r − P), as
+// k_mimi_stage would write them; the stream's first CTA writes the next
+// call's carried rows.
 template <int RM>
-__global__ void __launch_bounds__(256) k_mimi_fconv(const float* x, int sstride, int cin, int K, int T, int mf,
-                                                    const float* w, const float* bias, int N, float* y, int resid,
-                                                    int ngp) {
+__global__ void __launch_bounds__(256) k_mimi_fconv(FconvArgs a) {
   extern __shared__ __align__(16) float fsm[];
+  const int cin = a.cin, K = a.K, T = a.T, N = a.N, ngp = a.ngp, P = a.P;
   const int tmg = 256 / ngp, TM = tmg * RM, k = K / cin;
   const int s = blockIdx.y, t0 = blockIdx.x * TM;
   const int rows = TM + k - 1, cinp = cin + 4, C4 = cin >> 2, K4 = K >> 2;
   float* xs = fsm;
   float4* ws = reinterpret_cast<float4*>(fsm + rows * cinp);
   const int tid = threadIdx.x;
-  const int avail = sstride - t0;  // staged rows from t0 on
+  const int total = a.virt ? P + T : a.sstride;  // window rows of the stream
+  auto window_row = [&](int vr, int c) {
+    if (!a.virt) return ld4(a.x + (size_t(s) * a.sstride + vr) * cin + c);
+    if (vr < P) return ld4(a.carry_in + (size_t(s) * P + vr) * cin + c);
+    const float4 v = ld4(a.x + (size_t(s) * T + vr - P) * cin + c);
+    return a.elu ? elu4(v, (vr - P) * cin + c, T * cin) : v;
+  };
   for (int i = tid; i < rows * C4; i += 256) {
     const int r = i / C4, c = (i - r * C4) * 4;
-    st4(xs + r * cinp + c, r < avail ? ld4(x + (size_t(s) * sstride + t0 + r) * cin + c) : make_float4(0, 0, 0, 0));
+    st4(xs + r * cinp + c, t0 + r < total ? window_row(t0 + r, c) : make_float4(0, 0, 0, 0));
   }
+  if (a.virt && P > 0 && blockIdx.x == 0)
+    for (int i = tid; i < P * C4; i += 256) {
+      const int r = i / C4, c = (i - r * C4) * 4;
+      st4(a.carry_out + (size_t(s) * P + r) * cin + c, window_row(T + r, c));
+    }
+  const float* w = a.w;
+  const float* bias = a.bias;
   for (int i = tid; i < K4 * 4 * ngp; i += 256) {
     const int kq = i / (4 * ngp), rem = i - kq * 4 * ngp, u = rem / ngp, g = rem - u * ngp, n = g * 4 + u;
     ws[i] = n < N ? ld4(w + size_t(n) * K + kq * 4) : make_float4(0, 0, 0, 0);
@@ -230,16 +247,16 @@ __global__ void __launch_bounds__(256) k_mimi_fconv(const float* x, int sstride,
 #pragma unroll
   for (int i = 0; i < RM; i++) {
     const int t = t0 + rg + i * tmg;
-    if (t >= mf) continue;
-    float* yp = y + (size_t(s) * T + t) * N + cg * 4;
+    if (t >= a.mf) continue;
+    float* yp = a.y + (size_t(s) * T + t) * N + cg * 4;
     if (vec) {
       float4 v = make_float4(cv[i][0], cv[i][1], cv[i][2], cv[i][3]);
-      if (resid) v = add4(ld4(yp), v);
+      if (a.resid) v = add4(ld4(yp), v);
       st4(yp, v);
     } else {
 #pragma unroll
       for (int u = 0; u < 4; u++)
-        if (cg * 4 + u < N) yp[u] = resid ? __fadd_rn(yp[u], cv[i][u]) : cv[i][u];
+        if (cg * 4 + u < N) yp[u] = a.resid ? __fadd_rn(yp[u], cv[i][u]) : cv[i][u];
     }
   }
 }
@@ -345,21 +362,21 @@ bool mimi_fconv_fits(int cin, int K, int N) {
   return N >= 1 && N <= 64 && cin % 4 == 0 && K % cin == 0 && fconv_smem(cin, K, N) <= kFconvSmemMax;
 }
 
-void launch_mimi_fconv(const float* x, int sstride, int cin, int K, int n, int T, int mf, const float* w,
-                       const float* bias, int N, float* y, bool resid, cudaStream_t st) {
-  const int ngp = fconv_ngp(N), rm = fconv_rm(ngp), TM = 256 / ngp * rm;
-  const size_t sm = fconv_smem(cin, K, N);
-  const dim3 grid(unsigned((mf + TM - 1) / TM), unsigned(n));
-  const int r = resid ? 1 : 0;
+void launch_mimi_fconv(const FconvArgs& a0, int n, cudaStream_t st) {
+  FconvArgs a = a0;
+  a.ngp = fconv_ngp(a.N);
+  const int rm = fconv_rm(a.ngp), TM = 256 / a.ngp * rm;
+  const size_t sm = fconv_smem(a.cin, a.K, a.N);
+  const dim3 grid(unsigned((a.mf + TM - 1) / TM), unsigned(n));
   switch (rm) {
     case 1:
-      k_mimi_fconv<1><<<grid, 256, sm, st>>>(x, sstride, cin, K, T, mf, w, bias, N, y, r, ngp);
+      k_mimi_fconv<1><<<grid, 256, sm, st>>>(a);
       break;
     case 2:
-      k_mimi_fconv<2><<<grid, 256, sm, st>>>(x, sstride, cin, K, T, mf, w, bias, N, y, r, ngp);
+      k_mimi_fconv<2><<<grid, 256, sm, st>>>(a);
       break;
     default:
-      k_mimi_fconv<4><<<grid, 256, sm, st>>>(x, sstride, cin, K, T, mf, w, bias, N, y, r, ngp);
+      k_mimi_fconv<4><<<grid, 256, sm, st>>>(a);
   }
 }
 

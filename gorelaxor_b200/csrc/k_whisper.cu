@@ -306,7 +306,8 @@ __global__ void __launch_bounds__(256) k_wmm(WmmArgs p) {
   __shared__ __align__(16) float Bs[MM_S][MM_LD];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int i0 = blockIdx.y * MM_T, j0 = blockIdx.x * MM_T, str = blockIdx.z;
-  const WMat& w = p.w;
+  WMat w = p.w;
+  if (w.f) w.f += str * p.w_zs;  // a float32 weight per group (attention's keys and values)
   const int n = w.rows, k = w.cols, m = p.m, lda = p.lda;
   const float* A = p.a + str * p.a_zs;
   float cv[4][4], ch[4][4];
@@ -391,6 +392,9 @@ __global__ void __launch_bounds__(256) k_wmm(WmmArgs p) {
         case WM_GELU:
           cz[(size_t)i * p.ldc + j] = gelu_avx(val);
           break;
+        case WM_GELU_ADD:
+          cz[(size_t)i * p.ldc + j] = __fadd_rn(gelu_avx(val), p.aux[(size_t)i * p.ldc + j]);
+          break;
         case WM_ROWPOS:
           p.c[(size_t)p.dst_row[i * p.rs_i + str] * p.ldc + j] = val;
           break;
@@ -398,6 +402,73 @@ __global__ void __launch_bounds__(256) k_wmm(WmmArgs p) {
           cz[(size_t)i * p.ldc + j] = val;
       }
     }
+}
+
+// ------------------------------------------------------- audio encoder
+// encode (encoder.go:10-118), per stream (grid y): the convolutions' window
+// rows, the per-head split of q/k/v and the rows' softmax; the products are
+// k_wmm's packed order.
+
+// conv1's rows from a channel-major log-mel: x1[t][c·3 + k] = mel[c][t + k − 1]
+// (0 outside the 3000 frames).
+__global__ void k_wenc_conv1(const float* mel, float* x1, int nmel) {
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x, cols = nmel * 3;
+  if (i >= 3000 * cols) return;
+  const int t = i / cols, r = i - t * cols, c = r / 3, src = t + r - c * 3 - 1;
+  x1[(size_t)s * 3000 * cols + i] = src >= 0 && src < 3000 ? mel[((size_t)s * nmel + c) * 3000 + src] : 0.f;
+}
+
+// conv2's (stride 2): x2[t][c·3 + k] = h1[2t + k − 1][c] (0 outside).
+__global__ void k_wenc_conv2(const float* h1, float* x2, int st, int ctx) {
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x, cols = st * 3;
+  if (i >= ctx * cols) return;
+  const int t = i / cols, r = i - t * cols, c = r / 3, src = 2 * t + r - c * 3 - 1;
+  x2[(size_t)s * ctx * cols + i] = src >= 0 && src < 3000 ? h1[((size_t)s * 3000 + src) * st + c] : 0.f;
+}
+
+// Per (stream, head) z: qh[z][t][d] = q·sc (copy, then scale), kh[z][t][d],
+// vt[z][d][t].
+__global__ void k_wenc_heads(const float* q, const float* k, const float* v, float* qh, float* kh, float* vt, int ctx,
+                             int st, int nh, float sc) {
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= ctx * st) return;
+  const int hd = st / nh, t = i / st, j = i - t * st, h = j / hd, d = j - h * hd;
+  const size_t src = (size_t)s * ctx * st + i, z = (size_t)s * nh + h;
+  qh[(z * ctx + t) * hd + d] = __fmul_rn(q[src], sc);
+  kh[(z * ctx + t) * hd + d] = k[src];
+  vt[(z * hd + d) * ctx + t] = v[src];
+}
+
+// softmax (mathx.go:78-90) of rows of len values, a warp per row: the max,
+// expSub (EXP8 lanes for the first len&~7 with eight running sums and HSUM,
+// Go's expf and a sequential sum for the rest, added after), then × 1/Σ.
+__global__ void k_wenc_softmax(float* x, int len, long rows) {
+  const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float* r = x + row * len;
+  float mx = NINF;
+  for (int j = lane; j < len; j += 32) mx = fmaxf(mx, r[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int n8 = len & ~7;
+  for (int j = lane; j < len; j += 32) {
+    const float e = __fsub_rn(r[j], mx);
+    r[j] = j < n8 ? exp_avx(e) : expf_go(e);
+  }
+  __syncwarp();
+  float part = 0.f;
+  if (lane < 8)
+    for (int c = lane; c < n8; c += 8) part = __fadd_rn(part, r[c]);
+  float sum = hsum8_lanes(part);
+  if (lane == 0) {
+    float tail = 0.f;
+    for (int j = n8; j < len; j++) tail = __fadd_rn(tail, r[j]);
+    sum = __fdiv_rn(1.f, __fadd_rn(sum, tail));
+  }
+  const float inv = __shfl_sync(0xffffffffu, sum, 0);
+  __syncwarp();
+  for (int j = lane; j < len; j += 32) r[j] = __fmul_rn(r[j], inv);
 }
 
 // ------------------------------------------------------ process + sample
@@ -677,6 +748,23 @@ void launch_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int advanc
 
 void launch_wnospeech(const float* logits, int vocab, int nosp, float* scratch, float* out, int rows, cudaStream_t st) {
   k_wnospeech<<<rows, 1024, 0, st>>>(logits, vocab, nosp, scratch, out);
+}
+
+void launch_wenc_conv1(const float* mel, float* x1, int nmel, int n, cudaStream_t st) {
+  k_wenc_conv1<<<dim3((3000 * nmel * 3 + 255) / 256, n), 256, 0, st>>>(mel, x1, nmel);
+}
+
+void launch_wenc_conv2(const float* h1, float* x2, int state, int ctx, int n, cudaStream_t st) {
+  k_wenc_conv2<<<dim3((ctx * state * 3 + 255) / 256, n), 256, 0, st>>>(h1, x2, state, ctx);
+}
+
+void launch_wenc_heads(const float* q, const float* k, const float* v, float* qh, float* kh, float* vt, int ctx,
+                       int state, int nh, float sc, int n, cudaStream_t st) {
+  k_wenc_heads<<<dim3((ctx * state + 255) / 256, n), 256, 0, st>>>(q, k, v, qh, kh, vt, ctx, state, nh, sc);
+}
+
+void launch_wenc_softmax(float* x, int len, long rows, cudaStream_t st) {
+  k_wenc_softmax<<<unsigned((rows + 7) / 8), 256, 0, st>>>(x, len, rows);
 }
 
 void whisper_kernels_init() {}

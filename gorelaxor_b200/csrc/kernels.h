@@ -140,9 +140,12 @@ struct AttnRowsArgs {
   // p sees [max(that, p − context + 1), p]; and the cache as a ring of
   // `ring` positions (0: none).
   int context = 0, ring = 0;
+  // Set by launch_attn_rows: score slots before the staged value rows (0: values read from the cache).
+  int vstage = 0;
 };
 
 void launch_attn_rows(const AttnRowsArgs& a, int nstreams, int tmax, cudaStream_t st);
+void attn_kernels_init();
 
 // ---- Mimi's decoder (k_mimi.cu); rows [stream][time][channel], n streams ----
 void launch_mimi_up(const float* z, const float* up, const float* part_in, float* x, float* part_out, int n, int S,
@@ -159,11 +162,27 @@ void launch_mimi_im2col(const float* x, const float* prev_in, float* prev_out, f
 // dense q [n·T][K], qs [n·T][K/32].
 void launch_mimi_quant(const float* x, int ldx, int sstride, int n, int T, int K, int elu_len, int8_t* q, float2* qs,
                        cudaStream_t st);
-// The packed-order float32 product over staged rows (rows t < mf of each
-// stream, y dense [n·T][N]); mimi_fconv_fits says whether a shape fits.
+// The packed-order float32 product over convolution windows (rows t < mf
+// of each stream, y dense [n·T][N], stored or added to); row t's window is
+// the K = k·cin values from window row t on: staged rows x + (s·sstride +
+// t)·cin, or (virt) [carry_in (P); x or ELU(x)] read in place from dense x
+// [n][T][cin], the next carry_out written on the way. mimi_fconv_fits says
+// whether a shape fits.
+struct FconvArgs {
+  const float* x = nullptr;
+  int sstride = 0, cin = 0, K = 0, T = 0, mf = 0;
+  const float* w = nullptr;
+  const float* bias = nullptr;
+  int N = 0;
+  float* y = nullptr;
+  int resid = 0;
+  int virt = 0, P = 0, elu = 0;
+  const float* carry_in = nullptr;
+  float* carry_out = nullptr;
+  int ngp = 0;  // set by the launcher
+};
 bool mimi_fconv_fits(int cin, int K, int N);
-void launch_mimi_fconv(const float* x, int sstride, int cin, int K, int n, int T, int mf, const float* w,
-                       const float* bias, int N, float* y, bool resid, cudaStream_t st);
+void launch_mimi_fconv(const FconvArgs& a, int n, cudaStream_t st);
 void launch_mimi_convtr(const float* z, const float* bias, const float* part_in, float* y, float* part_out, int n, int T,
                         int co, int k, int S, cudaStream_t st);
 // rowpos[r] = pos[r / S] + r % S for the R rows of a call; pos[i] += S after it.
@@ -325,7 +344,10 @@ void launch_wcross(const WRows& r, const float* q, const float* ck, const float*
 // WM_GELU (geluAVX) at c + z·c_zs + i·ldc; WM_ROWPOS at c + dst_row[i·rs_i +
 // z]·ldc; WM_CROSSK keys ·tsc into [z][nh][m][hd] and WM_CROSSV values into
 // [z][nh][hd][m] (the cross K/V prep, A = encoder output of stream z).
-enum WmmMode { WM_STORE = 0, WM_CROSSK = 1, WM_CROSSV = 2, WM_RESID = 3, WM_GELU = 4, WM_ROWPOS = 5 };
+// WM_GELU_ADD: geluAVX, then + aux at the same place (the encoder's
+// positional embedding after conv2). A float32 weight may differ per group:
+// w.f + z·w_zs.
+enum WmmMode { WM_STORE = 0, WM_CROSSK = 1, WM_CROSSV = 2, WM_RESID = 3, WM_GELU = 4, WM_ROWPOS = 5, WM_GELU_ADD = 6 };
 struct WmmArgs {
   const float* a = nullptr;
   int lda = 0;
@@ -341,8 +363,21 @@ struct WmmArgs {
   float tsc = 1.f;
   const int* dst_row = nullptr;
   int rs_i = 0;
+  size_t w_zs = 0;
+  const float* aux = nullptr;
 };
 void launch_wmm(const WmmArgs& a, int groups, cudaStream_t st);
+// The audio encoder's steps between products (encode, encoder.go:10-118),
+// n streams: conv1's window rows from a log-mel [n][nmel][3000] into x1
+// [n][3000][nmel·3]; conv2's (stride 2) from h1 [n][3000][state] into x2
+// [n][ctx][state·3]; q/k/v [n][ctx][state] split per (stream, head) into qh
+// (·sc) and kh [n·nh][ctx][hd] and vt [n·nh][hd][ctx]; the softmax of rows of
+// len values.
+void launch_wenc_conv1(const float* mel, float* x1, int nmel, int n, cudaStream_t st);
+void launch_wenc_conv2(const float* h1, float* x2, int state, int ctx, int n, cudaStream_t st);
+void launch_wenc_heads(const float* q, const float* k, const float* v, float* qh, float* kh, float* vt, int ctx,
+                       int state, int nh, float sc, int n, cudaStream_t st);
+void launch_wenc_softmax(float* x, int len, long rows, cudaStream_t st);
 // process + sample at temperature 0 for every row (transcribe.go:370-494):
 // logits [rows][vocab] are masked in place (scratch [rows][vocab]); writes
 // out[*step][rows][4] (id, tid, p, plog), the next token and the stream's

@@ -190,7 +190,19 @@ void mimi_product(grx_mimi_streams* s, const MW& w, const MIn& in, int T, const 
   const int mf = T > 16 ? T / 6 * 6 : 0;  // rows per stream through the packed kernel
   if (mf > 0) {
     if (mimi_fconv_fits(in.ldx, K, N)) {
-      launch_mimi_fconv(in.x, in.sstride, in.ldx, K, n, T, mf, w.f, bias, N, y, resid, st);
+      FconvArgs f;
+      f.x = in.x;
+      f.sstride = in.sstride;
+      f.cin = in.ldx;
+      f.K = K;
+      f.T = T;
+      f.mf = mf;
+      f.w = w.f;
+      f.bias = bias;
+      f.N = N;
+      f.y = y;
+      f.resid = resid;
+      launch_mimi_fconv(f, n, st);
     } else {
       WmmArgs p;
       p.a = in.x;
@@ -235,6 +247,30 @@ void mimi_product(grx_mimi_streams* s, const MW& w, const MIn& in, int T, const 
 void mimi_conv(grx_mimi_streams* s, const MConv& c, int ci, const float* x, int T, bool elu, float* y, bool resid) {
   const int n = s->n, cin = c.cin;
   cudaStream_t st = s->st;
+  const bool window = staged(c) || (c.k == 1 && c.stride == 1);
+  if (window && !c.w.q8 && T > 16 && T % 6 == 0 && mimi_fconv_fits(cin, c.k * cin, c.cout)) {
+    // every row through the packed kernel: the window read in place from x
+    // (carried rows, ELU) by the product itself
+    FconvArgs f;
+    f.x = x;
+    f.cin = cin;
+    f.K = c.k * cin;
+    f.T = T;
+    f.mf = T;
+    f.w = c.w.f;
+    f.bias = c.b;
+    f.N = c.cout;
+    f.y = y;
+    f.resid = resid;
+    f.virt = 1;
+    f.P = c.k == 1 ? 0 : c.past();
+    f.elu = elu;
+    f.carry_in = s->carry[s->par][size_t(ci)];
+    f.carry_out = s->carry[s->par ^ 1][size_t(ci)];
+    launch_mimi_fconv(f, n, st);
+    s->launches++;
+    return;
+  }
   if (c.k == 1 && c.stride == 1) {
     if (elu && !c.w.q8) {
       launch_mimi_elu(x, s->se, n, T * cin, st);

@@ -142,10 +142,23 @@ const char* const kNonSpeech[] = {"\"", "#", "(", ")", "*", "+", "/", ":", ";", 
 
 }  // namespace
 
+// An audio encoder block (model.go:360-372).
+struct WEncDev {
+  float *attn_ln_w, *attn_ln_b, *mlp_ln_w, *mlp_ln_b;
+  WMat q, k, v, o, fc1, fc2;
+  float *qb, *vb, *ob, *fc1b, *fc2b;
+};
+
 struct grx_whisper {
   Arena ar;
   int dev = 0;
   int n_vocab = 0, n_audio_ctx = 0, n_state = 0, n_head = 0, n_text_layer = 0, n_text_ctx = 0, n_mels = 0;
+  int n_audio_head = 0;
+  // the audio encoder, when the file has its tensors (model.go:352-372)
+  bool has_enc = false;
+  WMat conv1, conv2;
+  float *conv1b = nullptr, *conv2b = nullptr, *enc_pos = nullptr, *enc_ln_w = nullptr, *enc_ln_b = nullptr;
+  std::vector<WEncDev> enc;
   std::vector<WLayerDev> layers;
   WMat tok_emb;
   float *dec_pos = nullptr, *ln_w = nullptr, *ln_b = nullptr;
@@ -162,6 +175,12 @@ struct grx_whisper_batch {
   float *sk = nullptr, *sv = nullptr, *ck = nullptr, *cvt = nullptr;
   float *x = nullptr, *cur = nullptr, *q = nullptr, *att = nullptr, *ff = nullptr, *logits = nullptr, *scratch = nullptr;
   float *enc = nullptr, *no_speech = nullptr;
+  // the audio encoder's work buffers, made at the first encode; its
+  // attention runs enc_chunk streams at a time
+  float *e_mel = nullptr, *e_x1 = nullptr, *e_h1 = nullptr, *e_x2 = nullptr, *e_x = nullptr, *e_cur = nullptr;
+  float *e_q = nullptr, *e_k = nullptr, *e_v = nullptr, *e_att = nullptr, *e_ff = nullptr;
+  float *e_qh = nullptr, *e_kh = nullptr, *e_vt = nullptr, *e_sc = nullptr;
+  int enc_chunk = 0;
   int *row_stream = nullptr, *row_pos = nullptr, *row_tok = nullptr, *dst_row = nullptr, *out_step = nullptr;
   int* step = nullptr;
   WSample* state = nullptr;
@@ -286,6 +305,7 @@ int grx_whisper_load(const void* bytes, size_t len, int device, grx_whisper** ou
   m->n_vocab = hv[0];
   m->n_audio_ctx = hv[1];
   const int n_audio_state = hv[2], n_audio_head = hv[3], n_audio_layer = hv[4];
+  m->n_audio_head = n_audio_head;
   m->n_text_ctx = hv[5];
   m->n_state = hv[6];
   m->n_head = hv[7];
@@ -444,6 +464,37 @@ int grx_whisper_load(const void* bytes, size_t len, int device, grx_whisper** ou
     L.fc2 = mat(lp + "mlp.2.weight", st, 4 * st);
     L.fc2b = vec(lp + "mlp.2.bias", st);
     m->layers.push_back(L);
+  }
+  // the audio encoder (model.go:352-372), bound when the file has it
+  if (err.empty() && ts.count("encoder.conv1.weight")) {
+    m->has_enc = true;
+    m->enc_pos = vec2("encoder.positional_embedding", m->n_audio_ctx, st);
+    m->conv1 = mat("encoder.conv1.weight", st, m->n_mels * 3);
+    m->conv1b = vec("encoder.conv1.bias", st);
+    m->conv2 = mat("encoder.conv2.weight", st, st * 3);
+    m->conv2b = vec("encoder.conv2.bias", st);
+    m->enc_ln_w = vec("encoder.ln_post.weight", st);
+    m->enc_ln_b = vec("encoder.ln_post.bias", st);
+    for (int i = 0; i < n_audio_layer; i++) {
+      const std::string lp = "encoder.blocks." + std::to_string(i) + ".";
+      WEncDev L;
+      L.attn_ln_w = vec(lp + "attn_ln.weight", st);
+      L.attn_ln_b = vec(lp + "attn_ln.bias", st);
+      L.q = mat(lp + "attn.query.weight", st, st);
+      L.qb = vec(lp + "attn.query.bias", st);
+      L.k = mat(lp + "attn.key.weight", st, st);
+      L.v = mat(lp + "attn.value.weight", st, st);
+      L.vb = vec(lp + "attn.value.bias", st);
+      L.o = mat(lp + "attn.out.weight", st, st);
+      L.ob = vec(lp + "attn.out.bias", st);
+      L.mlp_ln_w = vec(lp + "mlp_ln.weight", st);
+      L.mlp_ln_b = vec(lp + "mlp_ln.bias", st);
+      L.fc1 = mat(lp + "mlp.0.weight", 4 * st, st);
+      L.fc1b = vec(lp + "mlp.0.bias", 4 * st);
+      L.fc2 = mat(lp + "mlp.2.weight", st, 4 * st);
+      L.fc2b = vec(lp + "mlp.2.bias", st);
+      m->enc.push_back(L);
+    }
   }
   if (!err.empty()) return fail(GRX_EFORMAT, err);
   for (const auto& kv : ts)
@@ -723,9 +774,154 @@ int prefill(grx_whisper_batch* b, const int* prompt, int np, int sot_at) {
   return GRX_OK;
 }
 
+// One product of the encoder over `groups` streams of m rows each (all
+// rows ≥ 6: whisper/gemm.go's packed kernel throughout).
+void enc_product(grx_whisper_batch* b, const float* a, int lda, int m, const WMat& w, const float* bias, int mode,
+                 float* c, int ldc, int groups, const float* aux = nullptr) {
+  WmmArgs p;
+  p.a = a;
+  p.lda = lda;
+  p.a_zs = size_t(m) * lda;
+  p.m = m;
+  p.w = w;
+  p.bias = bias;
+  p.mode = mode;
+  p.c = c;
+  p.ldc = ldc;
+  p.c_zs = size_t(m) * ldc;
+  p.aux = aux;
+  launch_wmm(p, groups, b->st);
+  b->launches++;
+}
+
+// encode (encoder.go:10-118) of every stream's window d_mel [n][n_mels][3000]
+// into b->enc [n][ctx][state].
+int encode(grx_whisper_batch* b, const float* d_mel) {
+  const grx_whisper* m = b->m;
+  const int n = b->n, st = m->n_state, ctx = m->n_audio_ctx, nmel = m->n_mels, W = 3000;
+  const int nh = m->n_audio_head, hd = st / nh;
+  int rc = 0;
+  if (!b->e_x) {
+    // attention's scores take nh·ctx² floats per stream: at most ~2 GB at once
+    b->enc_chunk = int(std::max<size_t>(1, std::min<size_t>(n, (size_t(2) << 30) / (size_t(nh) * ctx * ctx * 4))));
+    const size_t N = size_t(n);
+    b->e_x1 = b->ar.alloc<float>(N * W * nmel * 3, &rc);
+    b->e_h1 = b->ar.alloc<float>(N * W * st, &rc);
+    b->e_x2 = b->ar.alloc<float>(N * ctx * st * 3, &rc);
+    b->e_x = b->ar.alloc<float>(N * ctx * st, &rc);
+    b->e_cur = b->ar.alloc<float>(N * ctx * st, &rc);
+    b->e_q = b->ar.alloc<float>(N * ctx * st, &rc);
+    b->e_k = b->ar.alloc<float>(N * ctx * st, &rc);
+    b->e_v = b->ar.alloc<float>(N * ctx * st, &rc);
+    b->e_att = b->ar.alloc<float>(N * ctx * st, &rc);
+    b->e_ff = b->ar.alloc<float>(N * ctx * 4 * st, &rc);
+    b->e_qh = b->ar.alloc<float>(N * ctx * st, &rc);
+    b->e_kh = b->ar.alloc<float>(N * ctx * st, &rc);
+    b->e_vt = b->ar.alloc<float>(N * ctx * st, &rc);
+    b->e_sc = b->ar.alloc<float>(size_t(b->enc_chunk) * nh * ctx * ctx, &rc);
+    if (rc) {
+      b->e_x = nullptr;
+      return rc;
+    }
+  }
+  cudaStream_t s = b->st;
+  // conv1 + GELU, conv2 + GELU + positions
+  launch_wenc_conv1(d_mel, b->e_x1, nmel, n, s);
+  enc_product(b, b->e_x1, nmel * 3, W, m->conv1, m->conv1b, WM_GELU, b->e_h1, st, n);
+  launch_wenc_conv2(b->e_h1, b->e_x2, st, ctx, n, s);
+  enc_product(b, b->e_x2, st * 3, ctx, m->conv2, m->conv2b, WM_GELU_ADD, b->e_x, st, n, m->enc_pos);
+  b->launches += 2;
+  const float sc = float(1 / std::sqrt(double(hd)));
+  for (const WEncDev& L : m->enc) {
+    launch_wln(b->e_x, b->e_cur, L.attn_ln_w, L.attn_ln_b, n * ctx, st, s);
+    enc_product(b, b->e_cur, st, ctx, L.q, L.qb, WM_STORE, b->e_q, st, n);
+    enc_product(b, b->e_cur, st, ctx, L.k, nullptr, WM_STORE, b->e_k, st, n);
+    enc_product(b, b->e_cur, st, ctx, L.v, L.vb, WM_STORE, b->e_v, st, n);
+    launch_wenc_heads(b->e_q, b->e_k, b->e_v, b->e_qh, b->e_kh, b->e_vt, ctx, st, nh, sc, n, s);
+    b->launches += 2;
+    for (int c0 = 0; c0 < n; c0 += b->enc_chunk) {
+      const int cn = std::min(b->enc_chunk, n - c0), z0 = c0 * nh;
+      // scores = qh·khᵀ per (stream, head), then the rows' softmax
+      WmmArgs p;
+      p.a = b->e_qh + size_t(z0) * ctx * hd;
+      p.lda = hd;
+      p.a_zs = size_t(ctx) * hd;
+      p.m = ctx;
+      p.w.f = b->e_kh + size_t(z0) * ctx * hd;
+      p.w.rows = ctx;
+      p.w.cols = hd;
+      p.w_zs = size_t(ctx) * hd;
+      p.c = b->e_sc;
+      p.ldc = ctx;
+      p.c_zs = size_t(ctx) * ctx;
+      launch_wmm(p, cn * nh, s);
+      launch_wenc_softmax(b->e_sc, ctx, long(cn) * nh * ctx, s);
+      // oh = scores·vtᵀ, into the heads' columns of att
+      for (int i = 0; i < cn; i++) {
+        WmmArgs o;
+        o.a = b->e_sc + size_t(i) * nh * ctx * ctx;
+        o.lda = ctx;
+        o.a_zs = size_t(ctx) * ctx;
+        o.m = ctx;
+        o.w.f = b->e_vt + size_t(c0 + i) * nh * hd * ctx;
+        o.w.rows = hd;
+        o.w.cols = ctx;
+        o.w_zs = size_t(hd) * ctx;
+        o.c = b->e_att + size_t(c0 + i) * ctx * st;
+        o.ldc = st;
+        o.c_zs = size_t(hd);
+        launch_wmm(o, nh, s);
+        b->launches++;
+      }
+      b->launches += 2;
+    }
+    enc_product(b, b->e_att, st, ctx, L.o, L.ob, WM_RESID, b->e_x, st, n);
+    launch_wln(b->e_x, b->e_cur, L.mlp_ln_w, L.mlp_ln_b, n * ctx, st, s);
+    enc_product(b, b->e_cur, st, ctx, L.fc1, L.fc1b, WM_GELU, b->e_ff, 4 * st, n);
+    enc_product(b, b->e_ff, 4 * st, ctx, L.fc2, L.fc2b, WM_RESID, b->e_x, st, n);
+    b->launches += 2;
+  }
+  launch_wln(b->e_x, b->enc, m->enc_ln_w, m->enc_ln_b, n * ctx, st, s);
+  b->launches++;
+  CK(cudaGetLastError());
+  return GRX_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int grx_whisper_encode(grx_whisper_batch* b, const float* mel) {
+  if (!b || !mel) return fail(GRX_EINVAL, "grx_whisper_encode: null argument");
+  const grx_whisper* m = b->m;
+  if (!m->has_enc) return fail(GRX_EINVAL, "grx_whisper_encode: the model file has no encoder");
+  CK(cudaSetDevice(b->ar.dev));
+  const size_t nm = size_t(b->n) * m->n_mels * 3000;
+  int rc = 0;
+  if (!b->e_mel) b->e_mel = b->ar.alloc<float>(nm, &rc);
+  if (rc) return rc;
+  CK(cudaMemcpyAsync(b->e_mel, mel, sizeof(float) * nm, cudaMemcpyHostToDevice, b->st));
+  rc = encode(b, b->e_mel);
+  if (rc) return rc;
+  return set_audio(b, b->enc);
+}
+
+int grx_whisper_encode_device(grx_whisper_batch* b, const float* d_mel) {
+  if (!b || !d_mel) return fail(GRX_EINVAL, "grx_whisper_encode_device: null argument");
+  if (!b->m->has_enc) return fail(GRX_EINVAL, "grx_whisper_encode_device: the model file has no encoder");
+  CK(cudaSetDevice(b->ar.dev));
+  int rc = encode(b, d_mel);
+  if (rc) return rc;
+  return set_audio(b, b->enc);
+}
+
+int grx_whisper_encoder_out(grx_whisper_batch* b, float* out) {
+  if (!b || !out) return fail(GRX_EINVAL, "grx_whisper_encoder_out: null argument");
+  CK(cudaSetDevice(b->ar.dev));
+  CK(cudaMemcpyAsync(out, b->enc, sizeof(float) * layer_stride_cross(b->m, b->n), cudaMemcpyDeviceToHost, b->st));
+  CK(cudaStreamSynchronize(b->st));
+  return GRX_OK;
+}
 
 int grx_whisper_set_audio(grx_whisper_batch* b, const float* enc) {
   if (!b || !enc) return fail(GRX_EINVAL, "grx_whisper_set_audio: null argument");

@@ -557,6 +557,49 @@ def whisper_tensors(cfg: WhisperConfig, seed: int = 0) -> dict:
     return t
 
 
+def whisper_encoder_tensors(cfg: WhisperConfig, seed: int = 0) -> dict:
+    """The audio encoder's tensors in whisper.cpp's names (model.go:352-372):
+    the convolutions float16 (as whisper.cpp's quantized files keep them;
+    [state][in·3], a row's values (channel, tap) → channel·3 + tap), the
+    blocks' matrices Q8_0, vectors and positions float32. Weights of
+    standard deviation about 1/√cols keep activations O(1) through the
+    layers."""
+    rng = np.random.default_rng(seed + 4242)
+    st = cfg.n_state
+
+    def f16(rows, cols):
+        return (rng.normal(0, 1 / np.sqrt(cols), (rows, cols))).astype(np.float16)
+
+    def q8(rows, cols):
+        return rand_q8(rng, rows, cols, scale_sd=1 / np.sqrt(cols) / 73.0)
+
+    t: dict = {"encoder.positional_embedding": _n(rng, (cfg.n_audio_ctx, st), 0.1),
+               "encoder.conv1.weight": f16(st, cfg.n_mels * 3), "encoder.conv1.bias": _n(rng, st, 0.1),
+               "encoder.conv2.weight": f16(st, st * 3), "encoder.conv2.bias": _n(rng, st, 0.1),
+               "encoder.ln_post.weight": 1.0 + _n(rng, st, 0.1), "encoder.ln_post.bias": _n(rng, st, 0.1)}
+    for i in range(cfg.n_audio_layer):
+        p = f"encoder.blocks.{i}."
+        for ln in ("attn_ln", "mlp_ln"):
+            t[p + ln + ".weight"] = 1.0 + _n(rng, st, 0.1)
+            t[p + ln + ".bias"] = _n(rng, st, 0.1)
+        for w in ("query", "key", "value", "out"):
+            t[f"{p}attn.{w}.weight"] = q8(st, st)
+            if w != "key":
+                t[f"{p}attn.{w}.bias"] = _n(rng, st, 0.1)
+        t[p + "mlp.0.weight"] = q8(4 * st, st)
+        t[p + "mlp.0.bias"] = _n(rng, 4 * st, 0.1)
+        t[p + "mlp.2.weight"] = q8(st, 4 * st)
+        t[p + "mlp.2.bias"] = _n(rng, st, 0.1)
+    return t
+
+
+def whisper_mel(seed: int, cfg: WhisperConfig) -> np.ndarray:
+    """A window's log-mel [n_mels][3000] for stream `seed`: values in the
+    range logMel gives (its floor max − 8 and the (v + 4)/4 scaling, mel.go:
+    80-95), here N(0, 0.5) around −0.3."""
+    return np.random.default_rng(40_000 + seed).normal(-0.3, 0.5, (cfg.n_mels, 3000)).astype(np.float32)
+
+
 def whisper_ggml(cfg: WhisperConfig, tensors: dict, words: list[bytes] | None = None, seed: int = 0,
                  f16_bits: dict | None = None) -> bytes:
     """A whisper.cpp model file (model.go:115-223): magic, hparams, mel
@@ -579,6 +622,9 @@ def whisper_ggml(cfg: WhisperConfig, tensors: dict, words: list[bytes] | None = 
             dims, typ, data = list(reversed(h.shape)), 1, h.tobytes()
         elif isinstance(arr, Q8):
             dims, typ, data = [arr.cols, arr.rows], 8, arr.blocks.tobytes()
+        elif arr.dtype == np.float16:
+            h = np.ascontiguousarray(arr, dtype="<f2")
+            dims, typ, data = list(reversed(h.shape)), 1, h.tobytes()
         else:
             a = np.ascontiguousarray(arr, dtype="<f4")
             dims, typ, data = list(reversed(a.shape)), 0, a.tobytes()

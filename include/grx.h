@@ -309,6 +309,18 @@ void grx_whisper_batch_free(grx_whisper_batch* b);
  * caches and sampling states start over. */
 int grx_whisper_set_audio(grx_whisper_batch* b, const float* enc);
 int grx_whisper_set_audio_device(grx_whisper_batch* b, const float* d_enc);
+/* Model.encode (whisper/encoder.go:10-118) of every stream's window, then
+ * what grx_whisper_set_audio does with its output: mel is [n][n_mels][3000]
+ * (the log-mel as logMel lays it out, channel-major). conv1 and conv2 with
+ * GELU, the positions, the encoder blocks and the final LayerNorm, every
+ * product in whisper/gemm.go's packed order. Needs a model file with the
+ * encoder's tensors. Synchronous. */
+int grx_whisper_encode(grx_whisper_batch* b, const float* mel);
+/* The same from device memory (d_mel on the batch's device). */
+int grx_whisper_encode_device(grx_whisper_batch* b, const float* d_mel);
+/* The last window's encoder output [n][1500][n_state] (from
+ * grx_whisper_encode, or what grx_whisper_set_audio was given). */
+int grx_whisper_encoder_out(grx_whisper_batch* b, float* out);
 /* The prompt decode (transcribe.go:166-181): prompt [n][np] tokens, all
  * rows at once as decoder.go does (the packed product for each stream's
  * first np/6·6 rows when np ≥ 6); no_speech [n] (may be NULL) gets

@@ -582,8 +582,48 @@ int orc_whisper_ready(void* h) {
     L.fc2 = W(p + "mlp.2.weight");
     L.fc2b = V(p + "mlp.2.bias");
   }
+  if (m.n_mels > 0) {  // the audio encoder (model.go:352-372)
+    m.enc_pos = V("encoder.positional_embedding");
+    m.conv1 = W("encoder.conv1.weight");
+    m.conv1b = V("encoder.conv1.bias");
+    m.conv2 = W("encoder.conv2.weight");
+    m.conv2b = V("encoder.conv2.bias");
+    m.enc_ln_w = V("encoder.ln_post.weight");
+    m.enc_ln_b = V("encoder.ln_post.bias");
+    for (size_t i = 0; i < m.enc.size(); i++) {
+      const std::string p = "encoder.blocks." + std::to_string(i) + ".";
+      WEncLayer& L = m.enc[i];
+      L.attn_ln_w = V(p + "attn_ln.weight");
+      L.attn_ln_b = V(p + "attn_ln.bias");
+      L.q = W(p + "attn.query.weight");
+      L.qb = V(p + "attn.query.bias");
+      L.k = W(p + "attn.key.weight");
+      L.v = W(p + "attn.value.weight");
+      L.vb = V(p + "attn.value.bias");
+      L.o = W(p + "attn.out.weight");
+      L.ob = V(p + "attn.out.bias");
+      L.mlp_ln_w = V(p + "mlp_ln.weight");
+      L.mlp_ln_b = V(p + "mlp_ln.bias");
+      L.fc1 = W(p + "mlp.0.weight");
+      L.fc1b = V(p + "mlp.0.bias");
+      L.fc2 = W(p + "mlp.2.weight");
+      L.fc2b = V(p + "mlp.2.bias");
+    }
+  }
   return o->err.empty() ? 0 : -1;
 }
+
+// Declares the audio encoder's shape; its tensors are then bound by
+// orc_whisper_ready.
+void orc_whisper_encoder(void* h, int n_mels, int n_audio_head, int n_audio_layer) {
+  Whisper& m = ((OWhisper*)h)->m;
+  m.n_mels = n_mels;
+  m.n_audio_head = n_audio_head;
+  m.enc.resize(size_t(n_audio_layer));
+}
+
+// encode of one window: mel [n_mels][3000] → out [1500][state].
+void orc_whisper_encode(void* h, const float* mel, float* out) { whisper_encode(((OWhisper*)h)->m, mel, out); }
 
 void* orc_wseq_new(void* h) {
   auto* s = new WSeq();

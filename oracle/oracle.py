@@ -84,6 +84,8 @@ def lib():
             "orc_whisper_vocab": (None, [P, P, P, I]),
             "orc_whisper_suppress": (I, [P, P, I]),
             "orc_whisper_ready": (I, [P]),
+            "orc_whisper_encoder": (None, [P, I, I, I]),
+            "orc_whisper_encode": (None, [P, P, P]),
             "orc_wseq_new": (P, [P]),
             "orc_wseq_free": (None, [P]),
             "orc_whisper_cross_kv": (None, [P, P, P]),
@@ -353,6 +355,9 @@ class Whisper:
             if isinstance(arr, Q8):
                 buf = q8_to_f16(arr)
                 L.orc_whisper_tensor(self.h, name.encode(), 1, arr.rows, arr.cols, p(buf))
+            elif arr.dtype == np.float16:  # a float16 matrix (the convolutions)
+                buf = np.ascontiguousarray(arr).view(np.uint16)
+                L.orc_whisper_tensor(self.h, name.encode(), 1, arr.shape[0], arr.shape[1], p(buf))
             else:
                 buf = np.ascontiguousarray(arr, np.float32)
                 rows, cols = (buf.shape if buf.ndim == 2 else (1, buf.size))
@@ -362,8 +367,17 @@ class Whisper:
         lens = np.array([len(w) for w in words], np.int32)
         self._keep += [blob, lens]
         L.orc_whisper_vocab(self.h, p(blob), p(lens), len(words))
+        self.has_encoder = "encoder.conv1.weight" in tensors
+        if self.has_encoder:
+            L.orc_whisper_encoder(self.h, cfg.n_mels, cfg.n_head, cfg.n_audio_layer)
         if L.orc_whisper_ready(self.h) != 0:
             raise RuntimeError(L.orc_whisper_error(self.h).decode())
+
+    def encode(self, mel: np.ndarray) -> np.ndarray:
+        """encode (encoder.go:10-118): mel [n_mels][3000] → [1500][state]."""
+        out = np.empty((self.cfg.n_audio_ctx, self.cfg.n_state), np.float32)
+        lib().orc_whisper_encode(self.h, p(np.ascontiguousarray(mel, np.float32)), p(out))
+        return out
 
     def suppress(self) -> list[int]:
         out = np.zeros(256, np.int32)

@@ -1,5 +1,6 @@
 // TEST INFRASTRUCTURE — the CPU oracle of the Whisper text decoder's token
-// loop (whisper/decoder.go, encoder.go:120-140, transcribe.go:370-494).
+// loop (whisper/decoder.go, encoder.go:120-140, transcribe.go:370-494) and
+// of the audio encoder (encoder.go:10-118).
 // Only tests, the smoke check and the benchmark's CPU baseline use it.
 //
 // Restated from the reference operation by operation on the kernels of
@@ -118,8 +119,23 @@ struct WVocab {
   }
 };
 
+// An encoder block (model.go:360-372).
+struct WEncLayer {
+  const float *attn_ln_w = nullptr, *attn_ln_b = nullptr;
+  Weight q, k, v, o;
+  const float *qb = nullptr, *vb = nullptr, *ob = nullptr;
+  const float *mlp_ln_w = nullptr, *mlp_ln_b = nullptr;
+  Weight fc1, fc2;
+  const float *fc1b = nullptr, *fc2b = nullptr;
+};
+
 struct Whisper {
   int n_vocab = 0, n_audio_ctx = 1500, n_text_ctx = 0, n_state = 0, n_head = 0;
+  // the audio encoder (model.go:352-372), when bound
+  int n_mels = 0, n_audio_head = 0;
+  Weight conv1, conv2;  // [state][n_mels·3], [state][state·3] F16
+  const float *conv1b = nullptr, *conv2b = nullptr, *enc_pos = nullptr, *enc_ln_w = nullptr, *enc_ln_b = nullptr;
+  std::vector<WEncLayer> enc;
   const float* dec_pos = nullptr;  // [n_text_ctx][n_state]
   Weight tok_emb;                  // [n_vocab][n_state] F16
   const float *ln_w = nullptr, *ln_b = nullptr;
@@ -140,6 +156,78 @@ struct WSeq {
     n = 0;
   }
 };
+
+// parGelu, encoder.go:147-151: geluVec over chunks of 2^14 values.
+inline void par_gelu(float* x, long n) {
+  const long chunk = 1 << 14;
+  for (long o = 0; o < n; o += chunk) gelu_vec(x + o, int(std::min(chunk, n - o)));
+}
+
+// encode, whisper/encoder.go:10-118: a window's log-mel [n_mels][3000]
+// (channel-major) → the encoder output [n_audio_ctx][state].
+inline void whisper_encode(const Whisper& m, const float* mel, float* out) {
+  const int st = m.n_state, nmel = m.n_mels, W = 3000, ctx = m.n_audio_ctx;
+  // conv1: 3 taps, stride 1, padding 1; a row is (channel, tap) → c·3 + k
+  const int cols1 = nmel * 3;
+  std::vector<float> x1(size_t(W) * cols1, 0.f), h1(size_t(W) * st);
+  for (int t = 0; t < W; t++)
+    for (int c = 0; c < nmel; c++)
+      for (int k = 0; k < 3; k++)
+        if (t + k - 1 >= 0 && t + k - 1 < W) x1[size_t(t) * cols1 + c * 3 + k] = mel[size_t(c) * W + t + k - 1];
+  matmul_whisper(h1.data(), st, x1.data(), cols1, W, st, cols1, m.conv1, m.conv1b);
+  par_gelu(h1.data(), long(h1.size()));
+  // conv2: 3 taps, stride 2, padding 1, down to ctx positions
+  const int cols2 = st * 3;
+  std::vector<float> x2(size_t(ctx) * cols2, 0.f), x(size_t(ctx) * st);
+  for (int t = 0; t < ctx; t++)
+    for (int k = 0; k < 3; k++) {
+      const int i = 2 * t + k - 1;
+      if (i < 0 || i >= W) continue;
+      for (int c = 0; c < st; c++) x2[size_t(t) * cols2 + c * 3 + k] = h1[size_t(i) * st + c];
+    }
+  matmul_whisper(x.data(), st, x2.data(), cols2, ctx, st, cols2, m.conv2, m.conv2b);
+  par_gelu(x.data(), long(x.size()));
+  for (size_t i = 0; i < x.size(); i++) x[i] += m.enc_pos[i];
+  const int nh = m.n_audio_head, hd = st / nh;
+  const float sc = float(1 / std::sqrt(double(hd)));
+  std::vector<float> cur(x.size()), q(x.size()), k(x.size()), v(x.size()), att(x.size()), ff(size_t(ctx) * 4 * st);
+  std::vector<float> qh(size_t(ctx) * hd), kh(size_t(ctx) * hd), vt(size_t(hd) * ctx), oh(size_t(ctx) * hd);
+  std::vector<float> scores(size_t(ctx) * ctx);
+  Weight wk, wv;
+  wk.type = wv.type = F32;
+  wk.rows = ctx, wk.cols = hd, wk.f = kh.data();
+  wv.rows = hd, wv.cols = ctx, wv.f = vt.data();
+  auto ln_rows = [&](float* y, const float* src, const float* w, const float* b) {
+    for (int t = 0; t < ctx; t++) ln_whisper(y + size_t(t) * st, src + size_t(t) * st, st, w, b);
+  };
+  for (const WEncLayer& L : m.enc) {
+    ln_rows(cur.data(), x.data(), L.attn_ln_w, L.attn_ln_b);
+    matmul_whisper(q.data(), st, cur.data(), st, ctx, st, st, L.q, L.qb);
+    matmul_whisper(k.data(), st, cur.data(), st, ctx, st, st, L.k, nullptr);
+    matmul_whisper(v.data(), st, cur.data(), st, ctx, st, st, L.v, L.vb);
+    for (int h = 0; h < nh; h++) {
+      for (int t = 0; t < ctx; t++)
+        for (int d = 0; d < hd; d++) {
+          qh[size_t(t) * hd + d] = q[size_t(t) * st + h * hd + d] * sc;  // copy, then scale(qh, sc)
+          kh[size_t(t) * hd + d] = k[size_t(t) * st + h * hd + d];
+          vt[size_t(d) * ctx + t] = v[size_t(t) * st + h * hd + d];
+        }
+      matmul_whisper(scores.data(), ctx, qh.data(), hd, ctx, ctx, hd, wk, nullptr);
+      for (int t = 0; t < ctx; t++) softmax_whisper(scores.data() + size_t(t) * ctx, ctx);
+      matmul_whisper(oh.data(), hd, scores.data(), ctx, ctx, hd, ctx, wv, nullptr);
+      for (int t = 0; t < ctx; t++)
+        for (int d = 0; d < hd; d++) att[size_t(t) * st + h * hd + d] = oh[size_t(t) * hd + d];
+    }
+    matmul_whisper(cur.data(), st, att.data(), st, ctx, st, st, L.o, L.ob);
+    for (size_t i = 0; i < x.size(); i++) x[i] += cur[i];
+    ln_rows(cur.data(), x.data(), L.mlp_ln_w, L.mlp_ln_b);
+    matmul_whisper(ff.data(), 4 * st, cur.data(), st, ctx, 4 * st, st, L.fc1, L.fc1b);
+    par_gelu(ff.data(), long(ff.size()));
+    matmul_whisper(cur.data(), st, ff.data(), 4 * st, ctx, st, 4 * st, L.fc2, L.fc2b);
+    for (size_t i = 0; i < x.size(); i++) x[i] += cur[i];
+  }
+  ln_rows(out, x.data(), m.enc_ln_w, m.enc_ln_b);
+}
 
 // encoder.go:120-140: cross keys (scaled by 1/√hd) and values from the
 // encoder output enc [ctx][state].

@@ -34,6 +34,9 @@ CONFIGS = {
     # two residual blocks per ratio, the second dilated (its window through
     # an explicit im2col)
     "dilated": dataclasses.replace(_BASE, nres=2),
+    # a last stage of 48 rows per latent: every row of its float32 convs
+    # takes the packed kernel (the window read in place, ELU fused)
+    "whole_packed": dataclasses.replace(_BASE, upsample=2, ratios=(6, 4)),
 }
 
 
