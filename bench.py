@@ -185,6 +185,31 @@ def run_reference(args, rank, world):
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
             flush=True)
         return
+    if args.workload == "whisper_encoder":
+        cfg = synth.WhisperConfig()
+        tensors = synth.whisper_tensors(cfg, 0)
+        tensors.update(synth.whisper_encoder_tensors(cfg, 0))
+        words = synth.whisper_words(cfg)
+        windows = min(args.batch, cores)
+        vals, times = [], []
+        for _ in range(args.steps):
+            v, dt = wenc_cpu_sample(cfg, tensors, words, windows, cores)
+            vals.append(v)
+            times.append(dt)
+        value = float(np.mean(vals))
+        sample = (f"{windows} windows, one per thread: conv front end alone and with 1 of the {cfg.n_audio_layer} "
+                  f"blocks, scaled to a whole window; cross K/V prep not included")
+        print(json.dumps({
+            "impl": "reference", "metric": WENC_METRIC, "value": value, "unit": "windows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f16/Q8_0 weights widened)",
+            "data": "synthetic (seeded; the reference ships no weights)",
+            "config": {"workload": f"Whisper base.en encoder + cross K/V, {args.batch} windows (sampled)",
+                       "global_batch": args.batch, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "windows/s", "cores": windows, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "windows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
     if args.workload == "mimi":
         mc = mimi_config()
         tensors = synth.mimi_tensors(mc, 32, 0)
@@ -485,6 +510,124 @@ def run_mimi(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+WENC_METRIC = "Whisper encoder windows/s (30 s log-mel windows encoded, cross K/V included, whole job)"
+
+
+def wenc_cpu_sample(cfg, tensors, words, windows, threads):
+    """The oracle's encoder on host threads, one window per thread: the
+    conv front end alone and with one block, scaled to conv + all blocks.
+    Returns (windows/s, wall seconds of the sample)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from gorelaxor_b200 import synth
+    from oracle import oracle as orc
+
+    om = orc.Whisper(cfg, tensors, words)
+    mels = [synth.whisper_mel(1 + i, cfg) for i in range(windows)]
+
+    def timed(blocks):
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=min(threads, windows)) as ex:
+            list(ex.map(lambda m: om.encode(m, blocks), mels))
+        return time.perf_counter() - t0
+
+    t_front, t_one = timed(0), timed(1)
+    per_window = t_front + cfg.n_audio_layer * (t_one - t_front)
+    return windows / per_window, t_front + t_one
+
+
+def run_whisper_encoder(args, rank, world, local):
+    """--workload whisper_encoder: base.en's audio encoder (conv front end,
+    6 blocks of 512 × 8 heads over 1500 positions, final LayerNorm) and the
+    decoder layers' cross K/V, for `batch` windows per GPU; one step =
+    grx_whisper_encode_device of every window."""
+    import torch
+
+    import gorelaxor_b200 as g
+    from gorelaxor_b200 import synth
+    from gorelaxor_b200.dist import max_over_ranks, partition
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    B = args.batch
+    cfg = synth.WhisperConfig()
+    tensors = synth.whisper_tensors(cfg, 0)
+    tensors.update(synth.whisper_encoder_tensors(cfg, 0))
+    words = synth.whisper_words(cfg)
+    model = g.Whisper(synth.whisper_ggml(cfg, tensors, words), device=local)
+    mine = partition(B * world, world, rank)
+    mel = np.stack([synth.whisper_mel(1 + s, cfg) for s in mine])
+    b = g.WhisperBatch(model, B)
+    d_mel = torch.from_numpy(mel).cuda()
+    ext = torch.cuda.ExternalStream(b.cuda_stream())
+    for _ in range(args.warmup):
+        b.encode_device(d_mel.data_ptr())
+    clocks = Clocks(local)
+    l0 = b.launches()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks.start()
+    ms = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        b.encode_device(d_mel.data_ptr())
+        e1.record(ext)
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    ck = clocks.stop()
+    launches = b.launches() - l0
+    total_ms = max_over_ranks(float(np.sum(ms)), device="cuda")
+    value = args.steps * B * world / (total_ms / 1000)
+    e2e = None
+    if args.e2e_steps > 0:
+        pin = torch.from_numpy(mel).pin_memory().numpy()
+        em = []
+        for _ in range(args.e2e_steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            b.encode(pin)
+            out = b.encoder_out()
+            em.append((time.perf_counter() - t0) * 1000)
+        emax = max_over_ranks(float(np.sum(em)), device="cuda")
+        e2e = {"value": args.e2e_steps * B * world / (emax / 1000), "unit": "windows/s",
+               "h2d_bytes_per_step": int(mel.nbytes), "d2h_bytes_per_step": int(out.nbytes),
+               "note": "grx_whisper_encode (log-mel from pinned memory, cross K/V prep included), then the "
+                       "encoder output read back with grx_whisper_encoder_out"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        windows = min(B, cores)
+        v, dt = wenc_cpu_sample(cfg, tensors, words, windows, cores)
+        cpu = {"value": v, "unit": "windows/s", "cores": windows, "kind": "port",
+               "sample": f"{windows} windows, one per thread: conv front end alone and with 1 of the "
+                         f"{cfg.n_audio_layer} blocks, scaled to a whole window; cross K/V prep not included ({dt:.1f} s wall)"}
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    flop = 2 * (3000 * 240 * 512 + 1500 * 1536 * 512 + cfg.n_audio_layer * (
+        4 * 1500 * 512 * 512 + 2 * 1500 * 512 * 2048 + 2 * 8 * 1500 * 1500 * 64) + cfg.n_text_layer * 2 * 1500 * 512 * 512)
+    print(json.dumps({
+        "metric": WENC_METRIC, "value": value, "unit": "windows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (f16/Q8_0 weights widened)",
+        "data": "synthetic (seeded weights in whisper.cpp's types, N(-0.3, 0.5) log-mel windows)",
+        "config": {"workload": f"Whisper base.en encoder + cross K/V: {B} windows per GPU", "global_batch": B * world,
+                   "parallelism": f"windows partitioned, {world} GPU(s), no collective",
+                   "l2": "activations and scores well above L2 per window"},
+        "fp32_tflops": flop * value / world / 1e12,
+        "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck}), flush=True)
+
+
 WHISPER_METRIC = "Whisper tokens/s (greedy decode tokens per second, whole job)"
 
 
@@ -613,7 +756,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="grx", choices=["grx", "reference"])
-    ap.add_argument("--workload", default="flowlm", choices=["flowlm", "tdt", "whisper", "mimi"])
+    ap.add_argument("--workload", default="flowlm", choices=["flowlm", "tdt", "whisper", "mimi", "whisper_encoder"])
     ap.add_argument("--batch", type=int, default=None, help="streams per GPU (flowlm 256, tdt 128)")
     ap.add_argument("--frames", type=int, default=None, help="frames per stream (flowlm 512, tdt 750)")
     ap.add_argument("--e2e-steps", type=int, default=1)
@@ -623,8 +766,10 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
-    args.batch = args.batch or {"flowlm": 256, "tdt": 128, "whisper": 32, "mimi": 64}[args.workload]
-    args.frames = args.frames or {"flowlm": 512, "tdt": 750, "whisper": 224, "mimi": 32}[args.workload]
+    args.batch = args.batch or {"flowlm": 256, "tdt": 128, "whisper": 32, "mimi": 256,
+                                "whisper_encoder": 8}[args.workload]
+    args.frames = args.frames or {"flowlm": 512, "tdt": 750, "whisper": 224, "mimi": 32,
+                                  "whisper_encoder": 1}[args.workload]
     if args.impl == "reference":
         return run_reference(args, rank, world)
     if args.workload == "tdt":
@@ -633,6 +778,8 @@ def main():
         return run_whisper(args, rank, world, local)
     if args.workload == "mimi":
         return run_mimi(args, rank, world, local)
+    if args.workload == "whisper_encoder":
+        return run_whisper_encoder(args, rank, world, local)
 
     import torch
 

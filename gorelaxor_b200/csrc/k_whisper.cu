@@ -299,6 +299,38 @@ __global__ void __launch_bounds__(256) k_wcross(WRows r, const float* q, const f
 // whisper/gemm.go:150-186 + k6x16avx: every output starts at its bias (or
 // 0) and gets += the fused chain of each 256-deep pass. Tile 64 × 64, 256
 // threads of 4 × 4 outputs, 32-deep slices staged in shared memory.
+// Output (i, j) of group str of a packed-order product: the epilogue.
+__device__ __forceinline__ void wmm_out(const WmmArgs& p, int str, int m, int n, int i, int j, float val) {
+  float* cz = p.c + str * p.c_zs;
+  const int hd = n / max(p.nh, 1);
+  switch (p.mode) {
+    case WM_CROSSK: {
+      const int hh = j / hd, d = j % hd;
+      p.c[((size_t)str * p.nh + hh) * (size_t)m * hd + (size_t)i * hd + d] = __fmul_rn(val, p.tsc);
+      break;
+    }
+    case WM_CROSSV: {
+      const int hh = j / hd, d = j % hd;
+      p.c[((size_t)str * p.nh + hh) * (size_t)m * hd + (size_t)d * m + i] = val;
+      break;
+    }
+    case WM_RESID:
+      cz[(size_t)i * p.ldc + j] = __fadd_rn(cz[(size_t)i * p.ldc + j], val);
+      break;
+    case WM_GELU:
+      cz[(size_t)i * p.ldc + j] = gelu_avx(val);
+      break;
+    case WM_GELU_ADD:
+      cz[(size_t)i * p.ldc + j] = __fadd_rn(gelu_avx(val), p.aux[(size_t)i * p.ldc + j]);
+      break;
+    case WM_ROWPOS:
+      p.c[(size_t)p.dst_row[i * p.rs_i + str] * p.ldc + j] = val;
+      break;
+    default:
+      cz[(size_t)i * p.ldc + j] = val;
+  }
+}
+
 constexpr int MM_T = 64, MM_S = 32, MM_LD = MM_T + 4;
 
 __global__ void __launch_bounds__(256) k_wmm(WmmArgs p) {
@@ -366,42 +398,147 @@ __global__ void __launch_bounds__(256) k_wmm(WmmArgs p) {
 #pragma unroll
       for (int v = 0; v < 4; v++) cv[u][v] = __fadd_rn(cv[u][v], ch[u][v]);
   }
-  const int hd = n / max(p.nh, 1);
 #pragma unroll
   for (int u = 0; u < 4; u++)
 #pragma unroll
     for (int v = 0; v < 4; v++) {
       const int i = i0 + ty * 4 + u, j = j0 + tx * 4 + v;
-      if (i >= m || j >= n) continue;
-      const float val = cv[u][v];
-      float* cz = p.c + str * p.c_zs;
-      switch (p.mode) {
-        case WM_CROSSK: {
-          const int hh = j / hd, d = j % hd;
-          p.c[((size_t)str * p.nh + hh) * (size_t)m * hd + (size_t)i * hd + d] = __fmul_rn(val, p.tsc);
-          break;
+      if (i < m && j < n) wmm_out(p, str, m, n, i, j, cv[u][v]);
+    }
+}
+
+// The packed order again, for the larger products: a 128 × 128 tile per CTA,
+// 256 threads of 8 × 8 outputs (rows ty·4 + {0..3, 64..67}, columns likewise,
+// so that each thread's float4 reads of the staged slices are
+// conflict-free), 16-deep slices double-buffered through registers into
+// shared memory (k-major). Each output still runs its own fused chain over
+// k in order, folded into C at every 256-deep boundary; slices past K are
+// zeros, and fma(0, 0, acc) leaves acc as it is (acc never becomes −0 from
+// +0 by round-to-nearest sums). Needs K % 4 == 0, lda % 4 == 0 and 16-byte
+// aligned A rows; WT selects the weight: 0 float32, 1 float16, 2 Q8_0
+// widened to f16(q·d).
+constexpr int G_BM = 128, G_BK = 16, G_LD = G_BM + 4;
+
+template <int WT>
+__device__ __forceinline__ float4 wmm2_wload(const WMat& w, int row, int k) {
+  const size_t o = (size_t)row * w.cols + k;
+  if (WT == 0) return *reinterpret_cast<const float4*>(w.f + o);
+  if (WT == 1) {
+    const uint2 h = *reinterpret_cast<const uint2*>(w.h + o);
+    const __half2 lo = *reinterpret_cast<const __half2*>(&h.x), hi = *reinterpret_cast<const __half2*>(&h.y);
+    return make_float4(__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi));
+  }
+  const int q4 = *reinterpret_cast<const int*>(w.q + o);
+  const float d = h2f(w.d[(size_t)row * (w.cols / QK) + k / QK]);
+  return make_float4(q8h(int8_t(q4), d), q8h(int8_t(q4 >> 8), d), q8h(int8_t(q4 >> 16), d), q8h(int8_t(q4 >> 24), d));
+}
+
+template <int WT>
+__global__ void __launch_bounds__(256) k_wmm2(WmmArgs p) {
+  __shared__ __align__(16) float As[2][G_BK][G_LD];
+  __shared__ __align__(16) float Bs[2][G_BK][G_LD];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int i0 = blockIdx.y * G_BM, j0 = blockIdx.x * G_BM, str = blockIdx.z;
+  WMat w = p.w;
+  if (w.f) w.f += str * p.w_zs;
+  const int n = w.rows, K = w.cols, m = p.m, lda = p.lda;
+  const float* A = p.a + str * p.a_zs;
+  // loads: rows lr and lr + 64 of A and of W, four k from lk
+  const int lr = tid >> 2, lk = (tid & 3) * 4;
+  float4 ra[2], rb[2];
+  auto gload = [&](int k0) {
+    const int k = k0 + lk;
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int r = i0 + lr + 64 * u, c = j0 + lr + 64 * u;
+      ra[u] = r < m && k < K ? *reinterpret_cast<const float4*>(A + (size_t)r * lda + k) : make_float4(0, 0, 0, 0);
+      rb[u] = c < n && k < K ? wmm2_wload<WT>(w, c, k) : make_float4(0, 0, 0, 0);
+    }
+  };
+  auto sstore = [&](int b) {
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int r = lr + 64 * u;
+      As[b][lk][r] = ra[u].x, As[b][lk + 1][r] = ra[u].y, As[b][lk + 2][r] = ra[u].z, As[b][lk + 3][r] = ra[u].w;
+      Bs[b][lk][r] = rb[u].x, Bs[b][lk + 1][r] = rb[u].y, Bs[b][lk + 2][r] = rb[u].z, Bs[b][lk + 3][r] = rb[u].w;
+    }
+  };
+  float cv[8][8], acc[8][8];
+#pragma unroll
+  for (int v = 0; v < 8; v++) {
+    const int j = j0 + tx * 4 + (v & 3) + (v >> 2) * 64;
+    const float b = p.bias && j < n ? p.bias[j] : 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; u++) cv[u][v] = b;
+  }
+  const int ns = (K + G_BK - 1) / G_BK;
+  gload(0);
+  sstore(0);
+  __syncthreads();
+  for (int s = 0; s < ns; s++) {
+    const int k0 = s * G_BK, b = s & 1;
+    if ((k0 & 255) == 0) {
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+#pragma unroll
+        for (int v = 0; v < 8; v++) acc[u][v] = 0.f;
+    }
+    if (s + 1 < ns) gload(k0 + G_BK);
+#pragma unroll
+    for (int kk = 0; kk < G_BK; kk++) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[b][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[b][kk][ty * 4 + 64]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[b][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[b][kk][tx * 4 + 64]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+#pragma unroll
+        for (int v = 0; v < 8; v++) acc[u][v] = __fmaf_rn(av[u], bv[v], acc[u][v]);
+    }
+    if (((k0 + G_BK) & 255) == 0 || s + 1 == ns) {
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+#pragma unroll
+        for (int v = 0; v < 8; v++) cv[u][v] = __fadd_rn(cv[u][v], acc[u][v]);
+    }
+    if (s + 1 < ns) {
+      sstore(b ^ 1);
+      __syncthreads();
+    }
+  }
+  // plain row-major outputs leave as float4s (four columns of one row)
+  const bool vec = (p.mode == WM_STORE || p.mode == WM_RESID || p.mode == WM_GELU || p.mode == WM_GELU_ADD) &&
+                   p.ldc % 4 == 0 && p.c_zs % 4 == 0 && (reinterpret_cast<uintptr_t>(p.c) & 15) == 0;
+#pragma unroll
+  for (int u = 0; u < 8; u++) {
+    const int i = i0 + ty * 4 + (u & 3) + (u >> 2) * 64;
+    if (i >= m) continue;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int jb = j0 + tx * 4 + h * 64;
+      if (vec && jb + 3 < n) {
+        float* cp = p.c + str * p.c_zs + (size_t)i * p.ldc + jb;
+        float4 o = make_float4(cv[u][4 * h], cv[u][4 * h + 1], cv[u][4 * h + 2], cv[u][4 * h + 3]);
+        if (p.mode == WM_RESID) {
+          const float4 y = *reinterpret_cast<const float4*>(cp);
+          o = make_float4(__fadd_rn(y.x, o.x), __fadd_rn(y.y, o.y), __fadd_rn(y.z, o.z), __fadd_rn(y.w, o.w));
+        } else if (p.mode == WM_GELU || p.mode == WM_GELU_ADD) {
+          o = make_float4(gelu_avx(o.x), gelu_avx(o.y), gelu_avx(o.z), gelu_avx(o.w));
+          if (p.mode == WM_GELU_ADD) {
+            const float4 a = *reinterpret_cast<const float4*>(p.aux + (size_t)i * p.ldc + jb);
+            o = make_float4(__fadd_rn(o.x, a.x), __fadd_rn(o.y, a.y), __fadd_rn(o.z, a.z), __fadd_rn(o.w, a.w));
+          }
         }
-        case WM_CROSSV: {
-          const int hh = j / hd, d = j % hd;
-          p.c[((size_t)str * p.nh + hh) * (size_t)m * hd + (size_t)d * m + i] = val;
-          break;
-        }
-        case WM_RESID:
-          cz[(size_t)i * p.ldc + j] = __fadd_rn(cz[(size_t)i * p.ldc + j], val);
-          break;
-        case WM_GELU:
-          cz[(size_t)i * p.ldc + j] = gelu_avx(val);
-          break;
-        case WM_GELU_ADD:
-          cz[(size_t)i * p.ldc + j] = __fadd_rn(gelu_avx(val), p.aux[(size_t)i * p.ldc + j]);
-          break;
-        case WM_ROWPOS:
-          p.c[(size_t)p.dst_row[i * p.rs_i + str] * p.ldc + j] = val;
-          break;
-        default:
-          cz[(size_t)i * p.ldc + j] = val;
+        *reinterpret_cast<float4*>(cp) = o;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (jb + e < n) wmm_out(p, str, m, n, i, jb + e, cv[u][4 * h + e]);
       }
     }
+  }
 }
 
 // ------------------------------------------------------- audio encoder
@@ -469,6 +606,55 @@ __global__ void k_wenc_softmax(float* x, int len, long rows) {
   const float inv = __shfl_sync(0xffffffffu, sum, 0);
   __syncwarp();
   for (int j = lane; j < len; j += 32) r[j] = __fmul_rn(r[j], inv);
+}
+
+// The same softmax for rows of up to kSmRow values in one pass: a warp per
+// row holds it in registers (lane l: values l + 32c), the exponentials go
+// through shared memory for the eight lane sums.
+constexpr int kSmRow = 1536, kSmPer = kSmRow / 32;
+
+__global__ void __launch_bounds__(256) k_wenc_softmax_reg(float* x, int len, long rows) {
+  __shared__ float es[8][kSmRow];
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * 8 + wid;
+  if (row >= rows) return;
+  float* r = x + row * len;
+  float v[kSmPer];
+  float mx = NINF;
+#pragma unroll
+  for (int c = 0; c < kSmPer; c++) {
+    const int j = lane + 32 * c;
+    v[c] = j < len ? r[j] : NINF;
+    mx = fmaxf(mx, v[c]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int n8 = len & ~7;
+#pragma unroll
+  for (int c = 0; c < kSmPer; c++) {
+    const int j = lane + 32 * c;
+    if (j < len) {
+      const float e = __fsub_rn(v[c], mx);
+      v[c] = j < n8 ? exp_avx(e) : expf_go(e);
+      es[wid][j] = v[c];
+    }
+  }
+  __syncwarp();
+  float part = 0.f;
+  if (lane < 8)
+    for (int c = lane; c < n8; c += 8) part = __fadd_rn(part, es[wid][c]);
+  float sum = hsum8_lanes(part);
+  if (lane == 0) {
+    float tail = 0.f;
+    for (int j = n8; j < len; j++) tail = __fadd_rn(tail, es[wid][j]);
+    sum = __fdiv_rn(1.f, __fadd_rn(sum, tail));
+  }
+  const float inv = __shfl_sync(0xffffffffu, sum, 0);
+#pragma unroll
+  for (int c = 0; c < kSmPer; c++) {
+    const int j = lane + 32 * c;
+    if (j < len) r[j] = __fmul_rn(v[c], inv);
+  }
 }
 
 // ------------------------------------------------------ process + sample
@@ -733,6 +919,23 @@ void launch_wcross(const WRows& r, const float* q, const float* ck, const float*
 }
 
 void launch_wmm(const WmmArgs& a, int groups, cudaStream_t st) {
+  // the 128-wide kernel when the product fills its tiles, is at least one
+  // 256-deep pass deep and its rows are float4-aligned; the 64-wide one
+  // otherwise (both give the same bits)
+  const int K = a.w.cols;
+  const bool aligned = K % 4 == 0 && a.lda % 4 == 0 && a.a_zs % 4 == 0 && (reinterpret_cast<uintptr_t>(a.a) & 15) == 0 &&
+                       (a.w.f ? (reinterpret_cast<uintptr_t>(a.w.f) & 15) == 0 && a.w_zs % 4 == 0
+                              : a.w.h ? (reinterpret_cast<uintptr_t>(a.w.h) & 7) == 0 : K % QK == 0);
+  if (aligned && a.m >= 96 && a.w.rows >= 96 && K >= 256) {
+    dim3 grid((a.w.rows + G_BM - 1) / G_BM, (a.m + G_BM - 1) / G_BM, groups);
+    if (a.w.f)
+      k_wmm2<0><<<grid, 256, 0, st>>>(a);
+    else if (a.w.h)
+      k_wmm2<1><<<grid, 256, 0, st>>>(a);
+    else
+      k_wmm2<2><<<grid, 256, 0, st>>>(a);
+    return;
+  }
   dim3 grid((a.w.rows + MM_T - 1) / MM_T, (a.m + MM_T - 1) / MM_T, groups);
   k_wmm<<<grid, 256, 0, st>>>(a);
 }
@@ -764,7 +967,10 @@ void launch_wenc_heads(const float* q, const float* k, const float* v, float* qh
 }
 
 void launch_wenc_softmax(float* x, int len, long rows, cudaStream_t st) {
-  k_wenc_softmax<<<unsigned((rows + 7) / 8), 256, 0, st>>>(x, len, rows);
+  if (len <= kSmRow)
+    k_wenc_softmax_reg<<<unsigned((rows + 7) / 8), 256, 0, st>>>(x, len, rows);
+  else
+    k_wenc_softmax<<<unsigned((rows + 7) / 8), 256, 0, st>>>(x, len, rows);
 }
 
 void whisper_kernels_init() {}

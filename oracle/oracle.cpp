@@ -624,6 +624,10 @@ void orc_whisper_encoder(void* h, int n_mels, int n_audio_head, int n_audio_laye
 
 // encode of one window: mel [n_mels][3000] → out [1500][state].
 void orc_whisper_encode(void* h, const float* mel, float* out) { whisper_encode(((OWhisper*)h)->m, mel, out); }
+// The front end and the first `blocks` blocks only (a timing sample).
+void orc_whisper_encode_blocks(void* h, const float* mel, float* out, int blocks) {
+  whisper_encode(((OWhisper*)h)->m, mel, out, blocks);
+}
 
 void* orc_wseq_new(void* h) {
   auto* s = new WSeq();

@@ -86,6 +86,7 @@ def lib():
             "orc_whisper_ready": (I, [P]),
             "orc_whisper_encoder": (None, [P, I, I, I]),
             "orc_whisper_encode": (None, [P, P, P]),
+            "orc_whisper_encode_blocks": (None, [P, P, P, I]),
             "orc_wseq_new": (P, [P]),
             "orc_wseq_free": (None, [P]),
             "orc_whisper_cross_kv": (None, [P, P, P]),
@@ -373,10 +374,15 @@ class Whisper:
         if L.orc_whisper_ready(self.h) != 0:
             raise RuntimeError(L.orc_whisper_error(self.h).decode())
 
-    def encode(self, mel: np.ndarray) -> np.ndarray:
-        """encode (encoder.go:10-118): mel [n_mels][3000] → [1500][state]."""
+    def encode(self, mel: np.ndarray, blocks: int | None = None) -> np.ndarray:
+        """encode (encoder.go:10-118): mel [n_mels][3000] → [1500][state];
+        with `blocks`, the front end and that many blocks only (timing)."""
         out = np.empty((self.cfg.n_audio_ctx, self.cfg.n_state), np.float32)
-        lib().orc_whisper_encode(self.h, p(np.ascontiguousarray(mel, np.float32)), p(out))
+        m = p(np.ascontiguousarray(mel, np.float32))
+        if blocks is None:
+            lib().orc_whisper_encode(self.h, m, p(out))
+        else:
+            lib().orc_whisper_encode_blocks(self.h, m, p(out), blocks)
         return out
 
     def suppress(self) -> list[int]:

@@ -164,8 +164,9 @@ inline void par_gelu(float* x, long n) {
 }
 
 // encode, whisper/encoder.go:10-118: a window's log-mel [n_mels][3000]
-// (channel-major) → the encoder output [n_audio_ctx][state].
-inline void whisper_encode(const Whisper& m, const float* mel, float* out) {
+// (channel-major) → the encoder output [n_audio_ctx][state]. max_blocks ≥ 0
+// runs only that many blocks (for timing a bounded sample).
+inline void whisper_encode(const Whisper& m, const float* mel, float* out, int max_blocks = -1) {
   const int st = m.n_state, nmel = m.n_mels, W = 3000, ctx = m.n_audio_ctx;
   // conv1: 3 taps, stride 1, padding 1; a row is (channel, tap) → c·3 + k
   const int cols1 = nmel * 3;
@@ -200,7 +201,9 @@ inline void whisper_encode(const Whisper& m, const float* mel, float* out) {
   auto ln_rows = [&](float* y, const float* src, const float* w, const float* b) {
     for (int t = 0; t < ctx; t++) ln_whisper(y + size_t(t) * st, src + size_t(t) * st, st, w, b);
   };
+  int nb = 0;
   for (const WEncLayer& L : m.enc) {
+    if (max_blocks >= 0 && nb++ >= max_blocks) break;  // a timing sample only
     ln_rows(cur.data(), x.data(), L.attn_ln_w, L.attn_ln_b);
     matmul_whisper(q.data(), st, cur.data(), st, ctx, st, st, L.q, L.qb);
     matmul_whisper(k.data(), st, cur.data(), st, ctx, st, st, L.k, nullptr);
