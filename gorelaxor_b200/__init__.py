@@ -89,6 +89,15 @@ def _sig(lib):
         "grx_mimi_cuda_stream": (P, [P]),
         "grx_mimi_launches": (L, [P]),
         "grx_mimi_frames": (I, [P]),
+        "grx_fconf_load": (I, [P, S, I, PP]),
+        "grx_fconf_free": (None, [P]),
+        "grx_fconf_dims": (I, [P] + [C.POINTER(C.c_int)] * 5),
+        "grx_fconf_out_rows": (I, [I]),
+        "grx_fconf_encode": (I, [P, P, I, I, P, C.POINTER(C.c_int)]),
+        "grx_fconf_encode_device": (I, [P, P, I, I, P, C.POINTER(C.c_int)]),
+        "grx_fconf_sync": (I, [P]),
+        "grx_fconf_cuda_stream": (P, [P]),
+        "grx_fconf_launches": (L, [P]),
         "grx_tdt_load": (I, [P, S, I, PP]),
         "grx_tdt_free": (None, [P]),
         "grx_tdt_dims": (I, [P] + [C.POINTER(C.c_int)] * 8),
@@ -143,7 +152,7 @@ def lib():
             raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m gorelaxor_b200.build`")
         _lib = _sig(C.CDLL(str(LIB_PATH)))
         for n in ("grx_gguf_close", "grx_weight_free", "grx_flowlm_free", "grx_voice_free", "grx_streams_free",
-                  "grx_mimi_free", "grx_mimi_streams_free", "grx_tdt_free", "grx_tdt_batch_free", "grx_whisper_free",
+                  "grx_mimi_free", "grx_mimi_streams_free", "grx_fconf_free", "grx_tdt_free", "grx_tdt_batch_free", "grx_whisper_free",
                   "grx_whisper_batch_free"):
             _FREE[n] = getattr(_lib, n)
     return _lib
@@ -458,6 +467,54 @@ class MimiStreams:
         h, self._h = getattr(self, "_h", None), None
         if h:
             _free["grx_mimi_streams_free"](h)
+
+
+# -------------------------------------------------- FastConformer encoder
+
+
+class FConf:
+    """conformer.Model's FastConformer encoder (encoder.go:123-489) on one
+    device, from a parakeet GGUF; offline attention over all frames."""
+
+    def __init__(self, gguf: bytes, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().grx_fconf_load(gguf, len(gguf), device, C.byref(h)))
+        self._h = h
+        self.device = device
+        v = [C.c_int() for _ in range(5)]
+        _check(lib().grx_fconf_dims(h, *[C.byref(x) for x in v]))
+        self.d, self.heads, self.layers, self.n_mels, self.sub_c = [x.value for x in v]
+
+    def encode(self, mel: np.ndarray, valid: int | None = None) -> np.ndarray:
+        """mel [n_mels][frames] (the first `valid` real) → [L][d]."""
+        a = np.ascontiguousarray(mel, np.float32)
+        frames = a.shape[1]
+        out = np.empty((lib().grx_fconf_out_rows(frames), self.d), np.float32)
+        rows = C.c_int()
+        _check(lib().grx_fconf_encode(self._h, _ptr(a), frames, frames if valid is None else valid, _ptr(out),
+                                      C.byref(rows)))
+        return out[:rows.value]
+
+    def encode_device(self, d_mel: int, frames: int, valid: int, d_out: int) -> int:
+        """Device pointers (ints); asynchronous. Returns the valid rows."""
+        rows = C.c_int()
+        _check(lib().grx_fconf_encode_device(self._h, C.c_void_p(d_mel), frames, valid, C.c_void_p(d_out),
+                                             C.byref(rows)))
+        return rows.value
+
+    def sync(self):
+        _check(lib().grx_fconf_sync(self._h))
+
+    def cuda_stream(self) -> int:
+        return lib().grx_fconf_cuda_stream(self._h) or 0
+
+    def launches(self) -> int:
+        return lib().grx_fconf_launches(self._h)
+
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_fconf_free"](h)
 
 
 # ------------------------------------------------------------ TDT decoder

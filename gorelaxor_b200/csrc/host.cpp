@@ -36,6 +36,7 @@ int device_init(int dev) {
     whisper_kernels_init();
     mimi_kernels_init();
     attn_kernels_init();
+    fconf_kernels_init();
     cudaError_t e = cudaGetLastError();  // attribute calls report here; clear it
     if (e != cudaSuccess) return fail(GRX_ECUDA, std::string("kernel attributes: ") + cudaGetErrorString(e));
     done[size_t(dev)] = true;

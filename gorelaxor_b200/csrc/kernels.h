@@ -266,6 +266,26 @@ void launch_time_norm(const float* y0, const float* y1, const float* a0, const f
 void launch_cond_step(const float* y0, const float* tc, float* sy, int M, int N, cudaStream_t st);
 
 
+// ---- the FastConformer encoder (k_fconf.cu), one utterance, rows [time][channels] ----
+void launch_fc_mel_in(const float* mel, float* in, int frames, int nm, int valid, cudaStream_t st);
+void launch_fc_conv0(const float* in, int T, int F, const float* w, const float* b, int c, float* out, int T1, int F1,
+                     int L, cudaStream_t st);
+void launch_fc_dwconv2(const float* in, int T, int F, int c, const float* w, const float* b, float* out, int T1, int F1,
+                       int L, cudaStream_t st);
+void launch_fc_mask_relu(float* x, long n, long width, int L, cudaStream_t st);
+void launch_fc_flatten(const float* y, float* flat, int T, int F, int c, cudaStream_t st);
+void launch_fc_scale(float* x, long n, float s, cudaStream_t st);
+void launch_fc_silu(float* x, long n, cudaStream_t st);
+void launch_fc_axpy_half(float* x, const float* y, long n, cudaStream_t st);
+void launch_fc_qpos(const float* q, const float* pu, const float* pv, float* qu, float* qv, long n, int D,
+                    cudaStream_t st);
+void launch_fc_glu(const float* a, float* g, int T, int D, int L, cudaStream_t st);
+void launch_fc_dwconv(const float* g, const float* w, const float* dwb, const float* cnw, const float* cnb, float* out,
+                      int T, int D, int K, int padL, bool bn_silu, cudaStream_t st);
+void launch_fc_attn(const float* qu, const float* qv, const float* k, const float* v, const float* pp, float* out,
+                    int T, int D, int H, int L, float scale, cudaStream_t st);
+void fconf_kernels_init();
+
 // ---- the greedy TDT / RNN-T decode loop (k_tdt.cu) ----
 constexpr int TDT_MAX_LAYERS = 8, TDT_MAX_DURATIONS = 8;
 

@@ -109,6 +109,9 @@ class GGUFWriter:
         for name, arr in self.tensors:
             if isinstance(arr, Q8):
                 dims, gtype, data = [arr.cols, arr.rows], GGML_Q8_0, arr.blocks.tobytes()
+            elif arr.dtype == np.float16:
+                a = np.ascontiguousarray(arr, dtype="<f2")
+                dims, gtype, data = (list(reversed(a.shape)) or [1]), GGML_F16, a.tobytes()
             else:
                 a = np.ascontiguousarray(arr, dtype="<f4")
                 dims, gtype, data = (list(reversed(a.shape)) or [1]), GGML_F32, a.tobytes()
@@ -488,6 +491,108 @@ def tdt_gguf(cfg: TDTConfig, tensors: dict) -> bytes:
     for name, arr in tensors.items():
         g.tensor(name, arr)
     return g.to_bytes()
+
+
+@dataclass
+class FConfConfig:
+    """A FastConformer encoder (conformer/model.go:160-189, 350-410); the
+    defaults are a small one of Parakeet's shape rules (8× depthwise-striding
+    subsampling, relative-position attention over all frames, centred
+    depthwise convolution, batch norm). Parakeet TDT 0.6B is d 1024, 8 heads,
+    24 layers, d_ff 4096, 256 subsampling channels, 128 mels."""
+
+    d: int = 128
+    heads: int = 2
+    layers: int = 2
+    dff: int = 512
+    kernel: int = 9
+    sub_c: int = 64
+    n_mels: int = 32
+    xscaling: bool = True
+    conv_norm: str = "batch_norm"
+
+    @property
+    def sub_f(self) -> int:
+        f = self.n_mels
+        for _ in range(3):
+            f = (f - 1) // 2 + 1
+        return f
+
+
+def fconf_tensors(fc: FConfConfig, seed: int = 0) -> dict:
+    """The encoder's tensors in the converter's names (model.go:350-410):
+    the blocks' linear layers and the subsampling's pointwise convolutions
+    Q8_0, the 1×1 convolutions of the conv module float16 (as the converter
+    keeps them), taps, norms, biases and batch-norm statistics float32.
+    Weights of standard deviation about 1/√fan-in."""
+    rng = np.random.default_rng(seed + 777)
+    d, c, K = fc.d, fc.sub_c, fc.kernel
+
+    def q8(rows, cols):
+        return rand_q8(rng, rows, cols, scale_sd=1 / np.sqrt(cols) / 73.0)
+
+    pe = "enc.pre_encode."
+    t: dict = {pe + "conv.0.weight": _n(rng, (c, 1, 3, 3), 1 / 3.0), pe + "conv.0.bias": _n(rng, c, 0.1),
+               pe + "conv.2.weight": _n(rng, (c, 1, 3, 3), 1 / 3.0), pe + "conv.2.bias": _n(rng, c, 0.1),
+               pe + "conv.3.weight": q8(c, c), pe + "conv.3.bias": _n(rng, c, 0.1),
+               pe + "conv.5.weight": _n(rng, (c, 1, 3, 3), 1 / 3.0), pe + "conv.5.bias": _n(rng, c, 0.1),
+               pe + "conv.6.weight": q8(c, c), pe + "conv.6.bias": _n(rng, c, 0.1),
+               pe + "out.weight": q8(d, c * fc.sub_f), pe + "out.bias": _n(rng, d, 0.1)}
+    for i in range(fc.layers):
+        p = f"enc.blocks.{i}."
+        for n in ("norm_ff1", "norm_attn", "norm_conv", "norm_ff2", "norm_out"):
+            t[p + n + ".weight"] = 1.0 + _n(rng, d, 0.1)
+            t[p + n + ".bias"] = _n(rng, d, 0.1)
+        for ff in ("ff1", "ff2"):
+            t[f"{p}{ff}.linear1.weight"] = q8(fc.dff, d)
+            t[f"{p}{ff}.linear1.bias"] = _n(rng, fc.dff, 0.1)
+            t[f"{p}{ff}.linear2.weight"] = q8(d, fc.dff)
+            t[f"{p}{ff}.linear2.bias"] = _n(rng, d, 0.1)
+        for w in ("q", "k", "v", "out"):
+            t[f"{p}attn.linear_{w}.weight"] = q8(d, d)
+            t[f"{p}attn.linear_{w}.bias"] = _n(rng, d, 0.1)
+        t[p + "attn.linear_pos.weight"] = q8(d, d)
+        t[p + "attn.pos_bias_u"] = _n(rng, (fc.heads, d // fc.heads), 0.1)
+        t[p + "attn.pos_bias_v"] = _n(rng, (fc.heads, d // fc.heads), 0.1)
+        t[p + "conv.pointwise1.weight"] = (rng.normal(0, 1 / np.sqrt(d), (2 * d, d))).astype(np.float16)
+        t[p + "conv.pointwise1.bias"] = _n(rng, 2 * d, 0.1)
+        t[p + "conv.depthwise.weight"] = _n(rng, (d, 1, K), 1 / np.sqrt(K))
+        t[p + "conv.depthwise.bias"] = _n(rng, d, 0.1)
+        t[p + "conv.bn.weight"] = 1.0 + _n(rng, d, 0.1)
+        t[p + "conv.bn.bias"] = _n(rng, d, 0.1)
+        t[p + "conv.bn.running_mean"] = _n(rng, d, 0.1)
+        t[p + "conv.bn.running_var"] = (1.0 + np.abs(_n(rng, d, 0.3))).astype(np.float32)
+        t[p + "conv.pointwise2.weight"] = (rng.normal(0, 1 / np.sqrt(d), (d, d))).astype(np.float16)
+        t[p + "conv.pointwise2.bias"] = _n(rng, d, 0.1)
+    return t
+
+
+def fconf_gguf(fc: FConfConfig, tensors: dict, style: str = "regular") -> bytes:
+    """A parakeet GGUF with the encoder's settings (model.go:160-189) and
+    tensors (style: the attention's att_context_style)."""
+    g = GGUFWriter("parakeet")
+    p = "stt.parakeet.encoder."
+    g.str("general.name", "Parakeet FastConformer synthetic encoder")
+    g.u32(p + "d_model", fc.d)
+    g.u32(p + "n_heads", fc.heads)
+    g.u32(p + "n_layers", fc.layers)
+    g.u32(p + "d_ff", fc.dff)
+    g.u32(p + "conv_kernel", fc.kernel)
+    g.u32(p + "subsampling_channels", fc.sub_c)
+    g.u32(p + "subsampling_factor", 8)
+    g.bool(p + "xscaling", fc.xscaling)
+    g.str(p + "att_context_style", style)
+    g.str(p + "conv_norm_type", fc.conv_norm)
+    g.u32("stt.frontend.num_mels", fc.n_mels)
+    for name, arr in tensors.items():
+        g.tensor(name, arr)
+    return g.to_bytes()
+
+
+def fconf_mel(seed: int, n_mels: int, frames: int) -> np.ndarray:
+    """Log-mel features [mels][frames] as NeMo's per-feature normalisation
+    leaves them (about N(0, 1))."""
+    return np.random.default_rng(50_000 + seed).normal(0.0, 1.0, (n_mels, frames)).astype(np.float32)
 
 
 def encoder_frames(seed: int, T: int, D: int) -> np.ndarray:

@@ -233,6 +233,36 @@ int64_t grx_mimi_launches(const grx_mimi_streams* s);
 /* Frames decoded since creation or the last reset. */
 int grx_mimi_frames(const grx_mimi_streams* s);
 
+/* ----------------------------------------- FastConformer encoder --------
+ * conformer.Model.encode (conformer/encoder.go:123-489): the 8x
+ * depthwise-striding subsampling and the Conformer blocks (macaron
+ * feed-forwards, relative-position attention, the convolution module), for
+ * the offline case — "regular" attention over every frame of the utterance,
+ * non-causal subsampling — one utterance per call. */
+typedef struct grx_fconf grx_fconf;
+/* The encoder half of conformer.FromGGUF (model.go:160-189, 350-410) from a
+ * parakeet GGUF: the stt.parakeet.encoder.* settings, stt.frontend.num_mels
+ * and the enc.* tensors, with the same names and shape checks; taps
+ * transposed, batch norm folded, float16 1x1 convolutions rounded by ToQ8.
+ * This build takes files whose matrices are Q8_0 (the int8 path) and the
+ * offline attention; others give GRX_EINVAL. */
+int grx_fconf_load(const void* gguf, size_t len, int device, grx_fconf** out);
+void grx_fconf_free(grx_fconf* m);
+int grx_fconf_dims(const grx_fconf* m, int* d_model, int* heads, int* layers, int* n_mels, int* sub_channels);
+/* Rows the subsampling makes from `frames` (three stride-2 steps). */
+int grx_fconf_out_rows(int frames);
+/* Encode of log-mel features mel [n_mels][frames] (host), the first valid
+ * frames real: out (host, room for grx_fconf_out_rows(frames) rows of
+ * d_model) gets the valid rows, *rows their count. Synchronous; calls on
+ * one handle must not overlap. */
+int grx_fconf_encode(grx_fconf* m, const float* mel, int frames, int valid, float* out, int* rows);
+/* The same with device buffers, asynchronous on the handle's stream
+ * (grx_fconf_sync waits). */
+int grx_fconf_encode_device(grx_fconf* m, const float* d_mel, int frames, int valid, float* d_out, int* rows);
+int grx_fconf_sync(grx_fconf* m);
+void* grx_fconf_cuda_stream(const grx_fconf* m);
+int64_t grx_fconf_launches(const grx_fconf* m);
+
 /* ------------------------------------------- TDT decoder (conformer) ------
  * conformer.Model.Decode (conformer/rnnt.go:111-173), the greedy RNN-T /
  * TDT loop over encoder output, for a batch of independent streams. */

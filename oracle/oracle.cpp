@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <thread>
 
+#include "conformer.h"
 #include "flowlm.h"
 #include "mimi.h"
 #include "tdt.h"
@@ -849,4 +850,164 @@ void orc_mimi_decode(void* h, void* s, const float* lat, float* pcm) {
 }
 int orc_mimi_frame(void* h) { return ((OMimi*)h)->m.frame; }
 void orc_elu(float* x, long n) { elu_vec(x, n); }
+
+// ---- the FastConformer encoder (conformer.h) ----
+
+struct OConf {
+  Conformer m;
+  std::map<std::string, Weight> w;
+  std::map<std::string, const float*> v;
+  std::map<std::string, std::pair<int, int>> shape;
+  std::vector<std::vector<uint8_t>> own;  // Q8_0 blocks made by ToQ8
+  std::string err;
+};
+
+void* orc_fconf_new(int d, int heads, int layers, int dff, int kernel, int sub_c, int n_mels, int xscaling,
+                    int ln_conv) {
+  auto* o = new OConf();
+  Conformer& m = o->m;
+  m.d = d, m.heads = heads, m.dff = dff, m.kernel = kernel, m.sub_c = sub_c, m.n_mels = n_mels;
+  m.xscaling = xscaling != 0, m.ln_conv = ln_conv != 0;
+  m.blocks.resize(size_t(layers));
+  return o;
+}
+void orc_fconf_free(void* h) { delete (OConf*)h; }
+const char* orc_fconf_error(void* h) { return ((OConf*)h)->err.c_str(); }
+
+// type 0: float32 values, 1: float16 bits (a matrix), 2: Q8_0 blocks.
+void orc_fconf_tensor(void* h, const char* name, int type, int rows, int cols, const void* p) {
+  auto* o = (OConf*)h;
+  Weight w;
+  w.rows = rows, w.cols = cols;
+  w.type = type == 2 ? Q8_0 : type == 1 ? F16 : F32;
+  w.f = (const float*)p;
+  w.h = (const uint16_t*)p;
+  w.q = (const uint8_t*)p;
+  o->w[name] = w;
+  o->v[name] = (const float*)p;
+  o->shape[name] = {rows, cols};
+}
+
+// loadEncoder, model.go:357-410.
+int orc_fconf_ready(void* h) {
+  auto* o = (OConf*)h;
+  Conformer& m = o->m;
+  auto V = [&](const std::string& n) -> const float* {
+    auto it = o->v.find(n);
+    if (it == o->v.end()) {
+      if (o->err.empty()) o->err = "missing " + n;
+      return nullptr;
+    }
+    return it->second;
+  };
+  auto Vopt = [&](const std::string& n) -> const float* {
+    auto it = o->v.find(n);
+    return it == o->v.end() ? nullptr : it->second;
+  };
+  auto W = [&](const std::string& n) -> Weight {
+    auto it = o->w.find(n);
+    if (it == o->w.end()) {
+      if (o->err.empty()) o->err = "missing " + n;
+      return Weight{};
+    }
+    Weight w = it->second;
+    if (w.type == F16 && w.cols % QK == 0) {  // ToQ8 (kern.go:139-170) from the widened values
+      std::vector<float> f(size_t(w.rows) * w.cols);
+      for (size_t i = 0; i < f.size(); i++) f[i] = f16_to_f32(w.h[i]);
+      o->own.emplace_back(size_t(w.rows) * (w.cols / QK) * Q8BYTES);
+      to_q8(o->own.back().data(), f.data(), w.rows, w.cols);
+      w.type = Q8_0;
+      w.q = o->own.back().data();
+    }
+    return w;
+  };
+  auto taps = [&](const std::string& n, int c, int ntaps) {  // transposeTaps: [c][taps] → [taps][c]
+    std::vector<float> out(size_t(c) * ntaps);
+    const float* src = V(n);
+    if (src)
+      for (int i = 0; i < c; i++)
+        for (int j = 0; j < ntaps; j++) out[size_t(j) * c + i] = src[size_t(i) * ntaps + j];
+    return out;
+  };
+  const std::string pe = "enc.pre_encode.";
+  const int c = m.sub_c, d = m.d;
+  m.w0 = taps(pe + "conv.0.weight", c, 9);
+  m.b0 = V(pe + "conv.0.bias");
+  m.w2 = taps(pe + "conv.2.weight", c, 9);
+  m.b2 = V(pe + "conv.2.bias");
+  m.w3 = W(pe + "conv.3.weight");
+  m.b3 = V(pe + "conv.3.bias");
+  m.w5 = taps(pe + "conv.5.weight", c, 9);
+  m.b5 = V(pe + "conv.5.bias");
+  m.w6 = W(pe + "conv.6.weight");
+  m.b6 = V(pe + "conv.6.bias");
+  m.out = W(pe + "out.weight");
+  m.outb = V(pe + "out.bias");
+  for (size_t i = 0; i < m.blocks.size(); i++) {
+    const std::string p = "enc.blocks." + std::to_string(i) + ".";
+    CBlock& b = m.blocks[i];
+    auto ff = [&](const std::string& n) {
+      CFF f;
+      f.norm_w = V(p + "norm_" + n + ".weight");
+      f.norm_b = V(p + "norm_" + n + ".bias");
+      f.w1 = W(p + n + ".linear1.weight");
+      f.b1 = Vopt(p + n + ".linear1.bias");
+      f.w2 = W(p + n + ".linear2.weight");
+      f.b2 = Vopt(p + n + ".linear2.bias");
+      return f;
+    };
+    b.ff1 = ff("ff1");
+    b.ff2 = ff("ff2");
+    b.norm_att_w = V(p + "norm_attn.weight");
+    b.norm_att_b = V(p + "norm_attn.bias");
+    b.q = W(p + "attn.linear_q.weight");
+    b.qb = Vopt(p + "attn.linear_q.bias");
+    b.k = W(p + "attn.linear_k.weight");
+    b.kb = Vopt(p + "attn.linear_k.bias");
+    b.v = W(p + "attn.linear_v.weight");
+    b.vb = Vopt(p + "attn.linear_v.bias");
+    b.out = W(p + "attn.linear_out.weight");
+    b.outb = Vopt(p + "attn.linear_out.bias");
+    b.pos = W(p + "attn.linear_pos.weight");
+    b.pos_u = V(p + "attn.pos_bias_u");
+    b.pos_v = V(p + "attn.pos_bias_v");
+    b.norm_conv_w = V(p + "norm_conv.weight");
+    b.norm_conv_b = V(p + "norm_conv.bias");
+    b.pw1 = W(p + "conv.pointwise1.weight");
+    b.pw1b = Vopt(p + "conv.pointwise1.bias");
+    b.pw2 = W(p + "conv.pointwise2.weight");
+    b.pw2b = Vopt(p + "conv.pointwise2.bias");
+    b.dw = taps(p + "conv.depthwise.weight", d, m.kernel);
+    b.dwb = Vopt(p + "conv.depthwise.bias");
+    b.norm_out_w = V(p + "norm_out.weight");
+    b.norm_out_b = V(p + "norm_out.bias");
+    const float *gw = V(p + "conv.bn.weight"), *gb = V(p + "conv.bn.bias");
+    if (m.ln_conv) {
+      if (gw && gb) b.cn_w.assign(gw, gw + d), b.cn_b.assign(gb, gb + d);
+    } else {
+      const float *mean = V(p + "conv.bn.running_mean"), *vr = V(p + "conv.bn.running_var");
+      if (gw && gb && mean && vr) {
+        b.cn_w.resize(size_t(d));
+        b.cn_b.resize(size_t(d));
+        for (int j = 0; j < d; j++) {
+          const float sc = float(double(gw[j]) / std::sqrt(double(vr[j]) + 1e-5));
+          b.cn_w[size_t(j)] = sc;
+          b.cn_b[size_t(j)] = gb[j] - mean[j] * sc;
+        }
+      }
+    }
+  }
+  return o->err.empty() ? 0 : -1;
+}
+
+// Model.encode of one utterance: mel [n_mels][frames], the first valid real;
+// out gets [L][d] (room for sub_out³(frames) rows); returns L. max_blocks ≥ 0
+// runs that many blocks only (a timing sample).
+int orc_fconf_encode(void* h, const float* mel, int frames, int valid, float* out, int max_blocks) {
+  int L = 0;
+  std::vector<float> x = conformer_encode(((OConf*)h)->m, mel, frames, valid, &L, max_blocks);
+  std::copy(x.begin(), x.end(), out);
+  return L;
+}
+
 }  // extern "C"

@@ -85,6 +85,12 @@ def lib():
             "orc_whisper_suppress": (I, [P, P, I]),
             "orc_whisper_ready": (I, [P]),
             "orc_whisper_encoder": (None, [P, I, I, I]),
+            "orc_fconf_new": (P, [I, I, I, I, I, I, I, I, I]),
+            "orc_fconf_free": (None, [P]),
+            "orc_fconf_error": (C.c_char_p, [P]),
+            "orc_fconf_tensor": (None, [P, C.c_char_p, I, I, I, P]),
+            "orc_fconf_ready": (I, [P]),
+            "orc_fconf_encode": (I, [P, P, I, I, P, I]),
             "orc_whisper_encode": (None, [P, P, P]),
             "orc_whisper_encode_blocks": (None, [P, P, P, I]),
             "orc_wseq_new": (P, [P]),
@@ -510,3 +516,50 @@ class MimiState:
         if getattr(self, "h", None):
             lib().orc_mimi_state_free(self.h)
             self.h = None
+
+
+# ------------------------------------------------------- FastConformer --
+
+
+class FConf:
+    """The oracle's FastConformer encoder (oracle/conformer.h) from an
+    FConfConfig and the generator's tensor dict."""
+
+    def __init__(self, fc, tensors: dict):
+        from gorelaxor_b200.synth import Q8
+
+        L = lib()
+        self.fc = fc
+        self._keep = []
+        self.h = L.orc_fconf_new(fc.d, fc.heads, fc.layers, fc.dff, fc.kernel, fc.sub_c, fc.n_mels,
+                                 int(fc.xscaling), int(fc.conv_norm == "layer_norm"))
+        for name, arr in tensors.items():
+            if isinstance(arr, Q8):
+                buf = np.ascontiguousarray(arr.blocks)
+                L.orc_fconf_tensor(self.h, name.encode(), 2, arr.rows, arr.cols, p(buf))
+            elif arr.dtype == np.float16:
+                buf = np.ascontiguousarray(arr).view(np.uint16)
+                L.orc_fconf_tensor(self.h, name.encode(), 1, arr.shape[0], arr.shape[-1], p(buf))
+            else:
+                buf = np.ascontiguousarray(arr, np.float32)
+                L.orc_fconf_tensor(self.h, name.encode(), 0, 1, buf.size, p(buf))
+            self._keep.append(buf)
+        if L.orc_fconf_ready(self.h) != 0:
+            raise RuntimeError(L.orc_fconf_error(self.h).decode())
+
+    def encode(self, mel: np.ndarray, valid: int | None = None, blocks: int = -1) -> np.ndarray:
+        """Model.encode (encoder.go:436-489): mel [n_mels][frames] → [L][d]."""
+        mel = np.ascontiguousarray(mel, np.float32)
+        frames = mel.shape[1]
+        t = frames
+        for _ in range(3):
+            t = (t - 1) // 2 + 1
+        out = np.empty((t, self.fc.d), np.float32)
+        n = lib().orc_fconf_encode(self.h, p(mel), frames, frames if valid is None else valid, p(out), blocks)
+        return out[:n]
+
+    def __del__(self):
+        if getattr(self, "h", None) and _lib is not None:
+            lib().orc_fconf_free(self.h)
+            self.h = None
+
