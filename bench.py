@@ -185,6 +185,30 @@ def run_reference(args, rank, world):
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
             flush=True)
         return
+    if args.workload == "fconf":
+        fc = fconf_config()
+        tensors = synth.fconf_tensors(fc, 0)
+        utts = min(args.batch, cores)
+        vals, times = [], []
+        for _ in range(args.steps):
+            v, dt = fconf_cpu_sample(fc, tensors, utts, args.frames, cores)
+            vals.append(v)
+            times.append(dt)
+        value = float(np.mean(vals))
+        print(json.dumps({
+            "impl": "reference", "metric": FCONF_METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
+            "data": "synthetic (seeded; the reference ships no weights)",
+            "config": {"workload": f"Parakeet TDT 0.6B encoder, {args.batch} utterances x {args.frames} frames "
+                                   f"(sampled)", "global_batch": args.batch, "frames": args.frames,
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "frames/s", "cores": utts, "kind": "port",
+                             "sample": f"{utts} utterances, one per thread: the subsampling alone and with 1 of "
+                                       f"the {fc.layers} blocks, scaled to all blocks"},
+            "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
     if args.workload == "whisper_encoder":
         cfg = synth.WhisperConfig()
         tensors = synth.whisper_tensors(cfg, 0)
@@ -628,6 +652,138 @@ def run_whisper_encoder(args, rank, world, local):
         "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck}), flush=True)
 
 
+FCONF_METRIC = "FastConformer encoder frames/s (80 ms encoder frames per second, whole job)"
+
+
+def fconf_config():
+    """Parakeet TDT 0.6B's encoder shape: d 1024, 8 heads × 128, 24 layers,
+    d_ff 4096, 256 subsampling channels, 128 mels, kernel 9."""
+    from gorelaxor_b200 import synth
+
+    return synth.FConfConfig(d=1024, heads=8, layers=24, dff=4096, sub_c=256, n_mels=128)
+
+
+def fconf_cpu_sample(fc, tensors, utts, frames, threads):
+    """The oracle's encoder on host threads, one utterance per thread: the
+    subsampling alone and with one block, scaled to all blocks. Returns
+    (encoder frames/s, wall seconds)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from gorelaxor_b200 import synth
+    from oracle import oracle as orc
+
+    oc = orc.FConf(fc, tensors)
+    mels = [synth.fconf_mel(1 + i, fc.n_mels, frames) for i in range(utts)]
+
+    def timed(blocks):
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=min(threads, utts)) as ex:
+            rows = list(ex.map(lambda m: oc.encode(m, None, blocks).shape[0], mels))
+        return time.perf_counter() - t0, rows[0]
+
+    (t0, T), (t1, _) = timed(0), timed(1)
+    per_utt = t0 + fc.layers * (t1 - t0)
+    return utts * T / per_utt, t0 + t1
+
+
+def run_fconf(args, rank, world, local):
+    """--workload fconf: Parakeet TDT 0.6B's FastConformer encoder on
+    `batch` utterances of `frames` 10 ms log-mel frames per GPU (one
+    grx_fconf_encode_device call each); one step = every utterance."""
+    import torch
+
+    import gorelaxor_b200 as g
+    from gorelaxor_b200 import synth
+    from gorelaxor_b200.dist import max_over_ranks, partition
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    B, Fr = args.batch, args.frames
+    fc = fconf_config()
+    tensors = synth.fconf_tensors(fc, 0)
+    gm = g.FConf(synth.fconf_gguf(fc, tensors), device=local)
+    mine = partition(B * world, world, rank)
+    mel = np.stack([synth.fconf_mel(1 + s, fc.n_mels, Fr) for s in mine])
+    d_mel = torch.from_numpy(mel).cuda()
+    t = Fr
+    for _ in range(3):
+        t = (t - 1) // 2 + 1
+    T = t
+    d_out = torch.empty((B, T, fc.d), dtype=torch.float32, device="cuda")
+    ext = torch.cuda.ExternalStream(gm.cuda_stream())
+
+    def one():
+        for i in range(B):
+            gm.encode_device(d_mel[i].data_ptr(), Fr, Fr, d_out[i].data_ptr())
+
+    for _ in range(args.warmup):
+        one()
+    gm.sync()
+    clocks = Clocks(local)
+    l0 = gm.launches()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks.start()
+    ms = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        one()
+        e1.record(ext)
+        gm.sync()
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    ck = clocks.stop()
+    launches = gm.launches() - l0
+    total_ms = max_over_ranks(float(np.sum(ms)), device="cuda")
+    value = args.steps * B * T * world / (total_ms / 1000)
+    e2e = None
+    if args.e2e_steps > 0:
+        pin = torch.from_numpy(mel).pin_memory().numpy()
+        em = []
+        for _ in range(args.e2e_steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for i in range(B):
+                out = gm.encode(pin[i])
+            em.append((time.perf_counter() - t0) * 1000)
+        emax = max_over_ranks(float(np.sum(em)), device="cuda")
+        e2e = {"value": args.e2e_steps * B * T * world / (emax / 1000), "unit": "frames/s",
+               "h2d_bytes_per_step": int(mel.nbytes), "d2h_bytes_per_step": int(B * out.nbytes),
+               "note": "grx_fconf_encode per utterance: log-mel in from pinned memory, the encoder rows read back"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        utts = min(B, cores)
+        v, dt = fconf_cpu_sample(fc, tensors, utts, Fr, cores)
+        cpu = {"value": v, "unit": "frames/s", "cores": utts, "kind": "port",
+               "sample": f"{utts} utterances of {Fr} frames, one per thread: the subsampling alone and with 1 of "
+                         f"the {fc.layers} blocks, scaled to all blocks ({dt:.1f} s wall)"}
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": FCONF_METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8/f32",
+        "data": "synthetic (seeded Q8_0 matrices, float16 1x1 convolutions as the converter keeps them, N(0,1) "
+                "log-mel)",
+        "config": {"workload": f"Parakeet TDT 0.6B encoder: {B} utterances x {Fr} frames ({T} encoder frames) per GPU",
+                   "global_batch": B * world, "frames": Fr,
+                   "parallelism": f"utterances partitioned, {world} GPU(s), no collective",
+                   "l2": "weights 650 MB, larger than L2"},
+        "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck}), flush=True)
+
+
 WHISPER_METRIC = "Whisper tokens/s (greedy decode tokens per second, whole job)"
 
 
@@ -756,7 +912,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="grx", choices=["grx", "reference"])
-    ap.add_argument("--workload", default="flowlm", choices=["flowlm", "tdt", "whisper", "mimi", "whisper_encoder"])
+    ap.add_argument("--workload", default="flowlm",
+                    choices=["flowlm", "tdt", "whisper", "mimi", "whisper_encoder", "fconf"])
     ap.add_argument("--batch", type=int, default=None, help="streams per GPU (flowlm 256, tdt 128)")
     ap.add_argument("--frames", type=int, default=None, help="frames per stream (flowlm 512, tdt 750)")
     ap.add_argument("--e2e-steps", type=int, default=1)
@@ -767,9 +924,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     args.batch = args.batch or {"flowlm": 256, "tdt": 128, "whisper": 32, "mimi": 256,
-                                "whisper_encoder": 8}[args.workload]
+                                "whisper_encoder": 8, "fconf": 4}[args.workload]
     args.frames = args.frames or {"flowlm": 512, "tdt": 750, "whisper": 224, "mimi": 32,
-                                  "whisper_encoder": 1}[args.workload]
+                                  "whisper_encoder": 1, "fconf": 3000}[args.workload]
     if args.impl == "reference":
         return run_reference(args, rank, world)
     if args.workload == "tdt":
@@ -780,6 +937,8 @@ def main():
         return run_mimi(args, rank, world, local)
     if args.workload == "whisper_encoder":
         return run_whisper_encoder(args, rank, world, local)
+    if args.workload == "fconf":
+        return run_fconf(args, rank, world, local)
 
     import torch
 

@@ -188,7 +188,14 @@ __device__ __forceinline__ float mm_dot(const float* x, const float* y, int k, b
     for (int k0 = 0; k0 < k; k0 += 256) {
       const int k1 = min(k, k0 + 256);
       float acc = 0.f;
-      for (int kk = k0; kk < k1; kk++) acc = __fmaf_rn(x[kk], y[kk], acc);
+      for (int kb = k0; kb < k1; kb += 16) {  // sixteen loads ahead of the chain
+        float yv[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) yv[u] = kb + u < k1 ? y[kb + u] : 0.f;
+#pragma unroll
+        for (int u = 0; u < 16; u++)
+          if (kb + u < k1) acc = __fmaf_rn(x[kb + u], yv[u], acc);
+      }
       c = __fadd_rn(c, acc);
     }
     return c;
@@ -209,7 +216,10 @@ __device__ __forceinline__ float mm_dot(const float* x, const float* y, int k, b
 // (nk = L for a block with a valid query, else the rows are zero); scores
 // (qu·k + qv·pp[jlo + nq − 1 − i + kk])·scale, masked keys −inf, expSub over
 // the row, × 1/Σ; then the values, MatMulF32 of the weights against the
-// head's value columns (K = nk). smem: qu, qv [hd], the row [nk].
+// head's value columns (K = nk). smem: qu, qv [hd], the row [nk], a key
+// tile and a position tile [kTile][hd + 1].
+constexpr int kTile = 64;  // keys per staged tile of k_fc_attn
+
 __global__ void __launch_bounds__(128) k_fc_attn(const float* qu, const float* qv, const float* k, const float* v,
                                                  const float* pp, float* out, int T, int D, int H, int L, float scale) {
   extern __shared__ float fsm[];
@@ -234,19 +244,40 @@ __global__ void __launch_bounds__(128) k_fc_attn(const float* qu, const float* q
   const int np = nq + nk - 1, jlo = T - 1 - (q1 - 1) + k0;
   const int lo = 0, hi = q < L ? L : 0;
   const bool packed = nq > 16 && i < nq / 6 * 6;
+  // keys in tiles of kTile: their key rows and position rows come into
+  // shared memory with coalesced loads (rows padded to an odd stride so that
+  // a warp's threads, one row each, read different banks), then thread j
+  // computes key t0 + j's two dots from there
+  float* kt = row + nk;
+  float* pt = kt + kTile * (hd + 1);
+  const int hs = hd + 1, h4 = hd >> 2;
   float mx = -__int_as_float(0x7f800000);
-  for (int kk = tid; kk < nk; kk += blockDim.x) {
-    const int kq = k0 + kk;
-    if (kq < lo || kq >= hi) {
-      row[kk] = -__int_as_float(0x7f800000);
-      continue;
+  for (int t0 = 0; t0 < nk; t0 += kTile) {
+    const int nt = min(kTile, nk - t0);
+    __syncthreads();  // the last tile's readers are done
+    for (int e = tid; e < nt * h4; e += blockDim.x) {
+      const int r = e / h4, c = (e - r * h4) * 4;
+      const float4 a = *reinterpret_cast<const float4*>(k + long(k0 + t0 + r) * D + h * hd + c);
+      const float4 b = *reinterpret_cast<const float4*>(pp + long(jlo + nq - 1 - i + t0 + r) * D + h * hd + c);
+      float* kr = kt + r * hs + c;
+      float* pr = pt + r * hs + c;
+      kr[0] = a.x, kr[1] = a.y, kr[2] = a.z, kr[3] = a.w;
+      pr[0] = b.x, pr[1] = b.y, pr[2] = b.z, pr[3] = b.w;
     }
-    const float sc = mm_dot(xu, k + long(kq) * D + h * hd, hd, packed, kk, nk);
-    const int jj = nq - 1 - i + kk;
-    const float bd = mm_dot(xv, pp + long(jlo + jj) * D + h * hd, hd, packed, jj, np);
-    const float val = __fmul_rn(__fadd_rn(sc, bd), scale);
-    row[kk] = val;
-    mx = fmaxf(mx, val);
+    __syncthreads();
+    if (tid < nt) {
+      const int kk = t0 + tid, kq = k0 + kk;
+      if (kq < lo || kq >= hi) {
+        row[kk] = -__int_as_float(0x7f800000);
+      } else {
+        const float sc = mm_dot(xu, kt + tid * hs, hd, packed, kk, nk);
+        const int jj = nq - 1 - i + kk;
+        const float bd = mm_dot(xv, pt + tid * hs, hd, packed, jj, np);
+        const float val = __fmul_rn(__fadd_rn(sc, bd), scale);
+        row[kk] = val;
+        mx = fmaxf(mx, val);
+      }
+    }
   }
 #pragma unroll
   for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, s));
@@ -293,7 +324,14 @@ __global__ void __launch_bounds__(128) k_fc_attn(const float* qu, const float* q
       for (int c0 = 0; c0 < nk; c0 += 256) {
         const int c1 = min(nk, c0 + 256);
         float acc = 0.f;
-        for (int kk = c0; kk < c1; kk++) acc = __fmaf_rn(row[kk], vd[long(kk) * D], acc);
+        for (int kb = c0; kb < c1; kb += 16) {  // sixteen loads ahead of the chain
+          float vv[16];
+#pragma unroll
+          for (int u = 0; u < 16; u++) vv[u] = kb + u < c1 ? vd[long(kb + u) * D] : 0.f;
+#pragma unroll
+          for (int u = 0; u < 16; u++)
+            if (kb + u < c1) acc = __fmaf_rn(row[kb + u], vv[u], acc);
+        }
         r = __fadd_rn(r, acc);
       }
     } else if (d < (hd & ~3)) {
@@ -380,7 +418,7 @@ void launch_fc_dwconv(const float* g, const float* w, const float* dwb, const fl
 }
 void launch_fc_attn(const float* qu, const float* qv, const float* k, const float* v, const float* pp, float* out,
                     int T, int D, int H, int L, float scale, cudaStream_t st) {
-  const size_t sm = (size_t(2) * (D / H) + size_t(T)) * sizeof(float);
+  const size_t sm = (size_t(2) * (D / H) + size_t(T) + size_t(2) * kTile * (D / H + 1)) * sizeof(float);
   k_fc_attn<<<dim3(H, T), 128, sm, st>>>(qu, qv, k, v, pp, out, T, D, H, L, scale);
 }
 void fconf_kernels_init() { cudaFuncSetAttribute(k_fc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); }
