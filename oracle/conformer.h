@@ -2,7 +2,11 @@
 // (conformer/encoder.go:41-480, model.go:350-410) for the offline case —
 // "regular" attention over all frames, centred depthwise convolution,
 // non-causal subsampling — restated operation by operation on kern.h and
-// flowlm.h. Only tests/ and the benchmark's CPU baseline use it.
+// flowlm.h. Only tests/ and the benchmark's CPU baseline use it. Checked
+// against a float64 encoder; parity against reference outputs unpinned (the
+// reference's encoder tests need model dumps that are not in the tree).
+// The position table's sin/cos are glibc's where the reference calls Go's
+// math package: the same to the last float64 ulp or nearly, not pinned.
 #pragma once
 #include <cmath>
 #include <limits>

@@ -1,6 +1,9 @@
 // TEST INFRASTRUCTURE ONLY: the CPU oracle of Mimi's decoder as Pocket TTS
 // runs it (pockettts/mimi.go:24-150, nn.go:52-64 and 258-327,
 // speak.go:177-190), restated on kern.h and flowlm.h. Only tests/ use it.
+// Checked by the reference's model-free streaming tests (pockettts/
+// nn_test.go:37-153, restated in tests/) and a float64 decoder; parity
+// against reference outputs unpinned (the tree has none for Mimi).
 #pragma once
 #include <algorithm>
 #include <cstring>

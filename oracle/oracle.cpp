@@ -851,6 +851,32 @@ void orc_mimi_decode(void* h, void* s, const float* lat, float* pcm) {
 int orc_mimi_frame(void* h) { return ((OMimi*)h)->m.frame; }
 void orc_elu(float* x, long n) { elu_vec(x, n); }
 
+// The streaming pieces alone, for the reference's model-free checks
+// (pockettts/nn_test.go:37-153): conv.run, convtr.run and attend with a
+// context window, float32 weights.
+void orc_mimi_conv_run(const float* w, const float* b, int cin, int cout, int k, int stride, int dil, float* prev,
+                       const float* x, int T, float* y) {
+  MConv c;
+  c.w.type = F32, c.w.rows = cout, c.w.cols = k * cin, c.w.f = w;
+  c.b = b, c.cin = cin, c.cout = cout, c.k = k, c.stride = stride, c.dil = dil;
+  std::vector<float> pv(prev, prev + size_t(c.past()) * cin);
+  conv_run(c, pv, x, T, y);
+  std::copy(pv.begin(), pv.end(), prev);
+}
+void orc_mimi_convtr_run(const float* w, const float* b, int cin, int cout, int k, int S, float* partial,
+                         const float* x, int T, float* y) {
+  MConvTr c;
+  c.w.type = F32, c.w.rows = k * cout, c.w.cols = cin, c.w.f = w;
+  c.b = b, c.cin = cin, c.cout = cout, c.k = k, c.stride = S;
+  std::vector<float> pt(partial, partial + size_t(k - S) * cout);
+  convtr_run(c, pt, x, T, y);
+  std::copy(pt.begin(), pt.end(), partial);
+}
+void orc_attend_window(float* out, const float* qkv, int T, const float* kc, const float* vc, int pos0, int d,
+                       int heads, int context) {
+  attend_window(out, qkv, T, kc, vc, pos0, d, heads, context);
+}
+
 // ---- the FastConformer encoder (conformer.h) ----
 
 struct OConf {

@@ -85,6 +85,9 @@ def lib():
             "orc_whisper_suppress": (I, [P, P, I]),
             "orc_whisper_ready": (I, [P]),
             "orc_whisper_encoder": (None, [P, I, I, I]),
+            "orc_mimi_conv_run": (None, [P, P, I, I, I, I, I, P, P, I, P]),
+            "orc_mimi_convtr_run": (None, [P, P, I, I, I, I, P, P, I, P]),
+            "orc_attend_window": (None, [P, P, I, P, P, I, I, I, I]),
             "orc_fconf_new": (P, [I, I, I, I, I, I, I, I, I]),
             "orc_fconf_free": (None, [P]),
             "orc_fconf_error": (C.c_char_p, [P]),

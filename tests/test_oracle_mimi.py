@@ -155,3 +155,85 @@ def test_mimi_decode_against_numpy_model(seed):
         assert got.shape == want.shape == (mc.frame,)
         err = np.sqrt(((got - want) ** 2).sum() / (want ** 2).sum())
         assert err < 0.02, f"frame {f}: {err:.4f}"
+
+
+# The reference's model-free checks of the streaming pieces
+# (pockettts/nn_test.go:37-153), restated on the oracle: a causal conv run
+# in pieces equals the whole input convolved after zero padding of
+# (k−1)·dil+1−stride; a transposed conv in pieces equals the whole output;
+# windowed attention fed in pieces equals softmax attention over each
+# query's window. Inputs are N(0,1) (the properties hold for any).
+
+
+def _near(got, want, tol=1e-5):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    assert got.shape == want.shape
+    assert np.all(np.abs(got - want) <= tol * (1 + np.abs(want)))
+
+
+@pytest.mark.parametrize("cin,cout,k,stride,dil", [(3, 5, 3, 1, 1), (4, 2, 8, 4, 1), (2, 3, 3, 1, 2), (6, 4, 1, 1, 1)])
+def test_conv_streaming(cin, cout, k, stride, dil):
+    rng = np.random.default_rng(1)
+    w = rng.normal(0, 1, (cout, k * cin)).astype(np.float32)  # [co][j][ci]
+    b = rng.normal(0, 1, cout).astype(np.float32)
+    T = 12 * stride
+    x = rng.normal(0, 1, (T, cin)).astype(np.float32)
+    P = (k - 1) * dil + 1 - stride
+    pad = np.vstack([np.zeros((P, cin)), x.astype(np.float64)])
+    want = np.array([[b[co] + sum(w[co, j * cin:(j + 1) * cin].astype(np.float64) @ pad[to * stride + j * dil]
+                                  for j in range(k)) for co in range(cout)] for to in range(T // stride)])
+    prev = np.zeros(max(P, 1) * cin, np.float32)
+    got, a = [], 0
+    for n in (2, 1, 5, 4):  # pieces, in strides
+        piece = np.ascontiguousarray(x[a * stride:(a + n) * stride])
+        y = np.empty((n, cout), np.float32)
+        orc.lib().orc_mimi_conv_run(orc.p(w), orc.p(b), cin, cout, k, stride, dil, orc.p(prev), orc.p(piece),
+                                    n * stride, orc.p(y))
+        got.append(y)
+        a += n
+    _near(np.vstack(got), want)
+
+
+def test_convtr_streaming():
+    rng = np.random.default_rng(3)
+    cin, cout, k, S, T = 3, 2, 8, 4, 9
+    w = rng.normal(0, 1, (k * cout, cin)).astype(np.float32)  # [j][co][ci]
+    b = rng.normal(0, 1, cout).astype(np.float32)
+    x = rng.normal(0, 1, (T, cin)).astype(np.float32)
+    full = np.tile(b.astype(np.float64), ((T - 1) * S + k, 1))
+    for ti in range(T):
+        full[ti * S:ti * S + k] += (w.astype(np.float64) @ x[ti]).reshape(k, cout)
+    part = np.zeros((k - S) * cout, np.float32)
+    got, start = [], 0
+    for n in (4, 1, 4):
+        piece = np.ascontiguousarray(x[start:start + n])
+        y = np.empty((n * S, cout), np.float32)
+        orc.lib().orc_mimi_convtr_run(orc.p(w), orc.p(b), cin, cout, k, S, orc.p(part), orc.p(piece), n, orc.p(y))
+        got.append(y)
+        start += n
+    _near(np.vstack(got), full[:T * S])
+
+
+def test_attend_window():
+    rng = np.random.default_rng(5)
+    d, heads, ctx, T = 8, 2, 5, 13
+    hd = d // heads
+    qkv = rng.normal(0, 1, (T, 3 * d)).astype(np.float32)
+    want = np.zeros((T, d))
+    for p_ in range(T):
+        lo = max(0, p_ - ctx + 1)
+        for h in range(heads):
+            s = slice(h * hd, (h + 1) * hd)
+            sc = np.array([qkv[p_, s].astype(np.float64) @ qkv[j, d:2 * d][s] for j in range(lo, p_ + 1)])
+            e = np.exp(sc / np.sqrt(hd))
+            want[p_, s] = (e / e.sum()) @ qkv[lo:p_ + 1, 2 * d:][:, s]
+    kc = np.ascontiguousarray(qkv[:, d:2 * d])
+    vc = np.ascontiguousarray(qkv[:, 2 * d:])
+    got, pos = [], 0
+    for n in (1, 6, 1, 5):
+        out = np.empty((n, d), np.float32)
+        part = np.ascontiguousarray(qkv[pos:pos + n])
+        orc.lib().orc_attend_window(orc.p(out), orc.p(part), n, orc.p(kc), orc.p(vc), pos, d, heads, ctx)
+        got.append(out)
+        pos += n
+    _near(np.vstack(got), want)
