@@ -221,11 +221,13 @@ __device__ __forceinline__ float mm_dot(const float* x, const float* y, int k, b
 constexpr int kTile = 64;  // keys per staged tile of k_fc_attn
 
 __global__ void __launch_bounds__(128) k_fc_attn(const float* qu, const float* qv, const float* k, const float* v,
-                                                 const float* pp, float* out, int T, int D, int H, int L, float scale) {
+                                                 const float* pp, float* out, int T, int D, int H, int L, float scale,
+                                                 int gemv_only) {
   extern __shared__ float fsm[];
   const int h = blockIdx.x, q = blockIdx.y, tid = threadIdx.x;
   const int hd = D / H, bl = 32;
   const int q0 = q / bl * bl, q1 = min(T, q0 + bl), nq = q1 - q0, i = q - q0;
+  if (gemv_only && nq > 16 && i < nq / 6 * 6) return;  // k_fc_attn_blk's row
   const int k0 = 0, nk = q0 < L ? L : 0;
   float* o = out + long(q) * D + h * hd;
   if (nk <= 0) {
@@ -381,6 +383,166 @@ __global__ void __launch_bounds__(128) k_fc_attn(const float* qu, const float* q
   }
 }
 
+// The packed-order rows of attention (those k_fc_attn returns on with
+// gemv_only), a block per (head, query block of 32): rows i < nq/6·6 of a
+// block with nq > 16. All its rows' scores against every key are computed
+// from shared-memory tiles of 32 key rows and of the position rows they
+// need (each score two fused chains over hd, 0 + the chain, as the packed
+// kernel does for K ≤ 256), kept in shared memory for the softmax (a warp
+// per row: EXP8 lanes, eight running sums, HSUM, Go's expf for the tail,
+// × 1/Σ), then each output runs the packed order over the keys (the chain
+// folded into C at every 256-deep boundary) from shared tiles of value rows.
+// Padded queries (q ≥ L) get zero rows, as the reference clears them.
+constexpr int kBQ = 32, kKT = 32, kBlkRows = 16;  // queries per block, keys per tile, rows per thread (values)
+
+size_t fc_blk_smem(int hd, int nk) {
+  const int hs = hd + 1;
+  return (size_t(2) * kBQ * hs + size_t(kKT) * hs + size_t(kKT + kBQ - 1) * hs + size_t(kBQ) * nk) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(256) k_fc_attn_blk(const float* qu, const float* qv, const float* k, const float* v,
+                                                     const float* pp, float* out, int T, int D, int H, int L,
+                                                     float scale) {
+  extern __shared__ float bsm[];
+  const int h = blockIdx.x, blk = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hd = D / H, hs = hd + 1;
+  const int q0 = blk * kBQ, q1 = min(T, q0 + kBQ), nq = q1 - q0;
+  if (nq <= 16) return;  // gemvRows throughout: k_fc_attn's
+  const int nr = nq / 6 * 6;  // the packed rows of this block
+  const int nk = q0 < L ? L : 0;
+  if (nk <= 0) {
+    for (int e = tid; e < nr * hd; e += blockDim.x) out[long(q0 + e / hd) * D + h * hd + e % hd] = 0.f;
+    return;
+  }
+  const int jlo = T - q1;  // T − 1 − (q1 − 1) + k0, k0 = 0
+  float* xu = bsm;
+  float* xv = xu + kBQ * hs;
+  float* kt = xv + kBQ * hs;           // key rows, later value rows [kKT][hs]
+  float* pt = kt + kKT * hs;           // position rows [kKT + kBQ − 1][hs]
+  float* S = pt + (kKT + kBQ - 1) * hs;  // [nr][nk]
+  const float NEG = -__int_as_float(0x7f800000);
+  for (int e = tid; e < nr * hd; e += blockDim.x) {
+    const int i = e / hd, d = e - i * hd;
+    xu[i * hs + d] = qu[long(q0 + i) * D + h * hd + d];
+    xv[i * hs + d] = qv[long(q0 + i) * D + h * hd + d];
+  }
+  // scores: warp w has rows w, w + 8, w + 16, w + 24; lane the tile's key
+  for (int t0 = 0; t0 < nk; t0 += kKT) {
+    const int nt = min(kKT, nk - t0);
+    // the tile's position rows: pair (i, t0 + j) reads row jlo + nq − 1 − i + t0 + j,
+    // i.e. staged row (nr − 1 − i) + j from pbase
+    const int pbase = jlo + nq - nr + t0, np_t = nr - 1 + nt;
+    __syncthreads();
+    for (int e = tid; e < nt * hd; e += blockDim.x) {
+      const int r = e / hd, d = e - r * hd;
+      kt[r * hs + d] = k[long(t0 + r) * D + h * hd + d];
+    }
+    for (int e = tid; e < np_t * hd; e += blockDim.x) {
+      const int r = e / hd, d = e - r * hd;
+      pt[r * hs + d] = pp[long(pbase + r) * D + h * hd + d];
+    }
+    __syncthreads();
+    if (lane < nt) {
+      float as[4], ab[4];
+      bool live[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        as[u] = ab[u] = 0.f;
+        const int i = warp + 8 * u;
+        live[u] = i < nr && q0 + i < L;
+      }
+      const float* kr = kt + lane * hs;
+      for (int d = 0; d < hd; d++) {
+        const float kv = kr[d];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int i = warp + 8 * u;
+          if (live[u]) {
+            as[u] = __fmaf_rn(xu[i * hs + d], kv, as[u]);
+            ab[u] = __fmaf_rn(xv[i * hs + d], pt[(nr - 1 - i + lane) * hs + d], ab[u]);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int i = warp + 8 * u;
+        if (i >= nr) continue;
+        S[i * nk + t0 + lane] =
+            live[u] ? __fmul_rn(__fadd_rn(__fadd_rn(0.f, as[u]), __fadd_rn(0.f, ab[u])), scale) : NEG;
+      }
+    }
+  }
+  __syncthreads();
+  // softmax of each row, a warp per row
+  for (int i = warp; i < nr; i += 8) {
+    float* r = S + i * nk;
+    float mx = NEG;
+    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, r[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    if (mx == NEG) {
+      for (int j = lane; j < nk; j += 32) r[j] = 0.f;
+      continue;
+    }
+    const int n8 = nk & ~7;
+    for (int j = lane; j < nk; j += 32) {
+      const float e = __fsub_rn(r[j], mx);
+      r[j] = j < n8 ? exp_avx(e) : expf_go(e);
+    }
+    __syncwarp();
+    float part = 0.f;
+    if (lane < 8)
+      for (int c = lane; c < n8; c += 8) part = __fadd_rn(part, r[c]);
+    float sum = hsum8_lanes(part);
+    if (lane == 0) {
+      float tail = 0.f;
+      for (int j = n8; j < nk; j++) tail = __fadd_rn(tail, r[j]);
+      sum = __fdiv_rn(1.f, __fadd_rn(sum, tail));
+    }
+    const float inv = __shfl_sync(FULL, sum, 0);
+    __syncwarp();
+    for (int j = lane; j < nk; j += 32) r[j] = __fmul_rn(r[j], inv);
+  }
+  // values: thread (g, d) has output column d of rows g, g + G, ... (G = 256 / hd)
+  const int G = blockDim.x / hd, g = tid / hd, d = tid - g * hd;
+  float acc[kBlkRows], c[kBlkRows];
+#pragma unroll
+  for (int j = 0; j < kBlkRows; j++) acc[j] = c[j] = 0.f;
+  for (int t0 = 0; t0 < nk; t0 += kKT) {
+    const int nt = min(kKT, nk - t0);
+    __syncthreads();  // score/softmax readers or the last value tile's are done
+    for (int e = tid; e < nt * hd; e += blockDim.x) {
+      const int r = e / hd, dd = e - r * hd;
+      kt[r * hs + dd] = v[long(t0 + r) * D + h * hd + dd];
+    }
+    __syncthreads();
+    if (g < G) {
+      if ((t0 & 255) == 0) {
+#pragma unroll
+        for (int j = 0; j < kBlkRows; j++) acc[j] = 0.f;
+      }
+      for (int kk = 0; kk < nt; kk++) {
+        const float vv = kt[kk * hs + d];
+#pragma unroll
+        for (int j = 0; j < kBlkRows; j++) {
+          const int i = g + j * G;
+          if (i < nr) acc[j] = __fmaf_rn(S[i * nk + t0 + kk], vv, acc[j]);
+        }
+      }
+      if (((t0 + kKT) & 255) == 0 || t0 + nt == nk) {
+#pragma unroll
+        for (int j = 0; j < kBlkRows; j++) c[j] = __fadd_rn(c[j], acc[j]);
+      }
+    }
+  }
+  if (g < G)
+#pragma unroll
+    for (int j = 0; j < kBlkRows; j++) {
+      const int i = g + j * G;
+      if (i < nr) out[long(q0 + i) * D + h * hd + d] = c[j];
+    }
+}
+
 }  // namespace
 
 void launch_fc_mel_in(const float* mel, float* in, int frames, int nm, int valid, cudaStream_t st) {
@@ -418,9 +580,18 @@ void launch_fc_dwconv(const float* g, const float* w, const float* dwb, const fl
 }
 void launch_fc_attn(const float* qu, const float* qv, const float* k, const float* v, const float* pp, float* out,
                     int T, int D, int H, int L, float scale, cudaStream_t st) {
-  const size_t sm = (size_t(2) * (D / H) + size_t(T) + size_t(2) * kTile * (D / H + 1)) * sizeof(float);
-  k_fc_attn<<<dim3(H, T), 128, sm, st>>>(qu, qv, k, v, pp, out, T, D, H, L, scale);
+  const int hd = D / H, nk = L;
+  // the block kernel takes the packed rows when their scores fit in shared
+  // memory (and a thread's rows in registers); the per-query kernel the rest
+  const size_t bsm = fc_blk_smem(hd, nk);
+  const bool blk = nk > 0 && bsm <= size_t(200) * 1024 && hd <= 256 && (kBQ + 256 / hd - 1) / (256 / hd) <= kBlkRows;
+  if (blk) k_fc_attn_blk<<<dim3(H, (T + kBQ - 1) / kBQ), 256, bsm, st>>>(qu, qv, k, v, pp, out, T, D, H, L, scale);
+  const size_t sm = (size_t(2) * hd + size_t(T) + size_t(2) * kTile * (hd + 1)) * sizeof(float);
+  k_fc_attn<<<dim3(H, T), 128, sm, st>>>(qu, qv, k, v, pp, out, T, D, H, L, scale, blk ? 1 : 0);
 }
-void fconf_kernels_init() { cudaFuncSetAttribute(k_fc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); }
+void fconf_kernels_init() {
+  cudaFuncSetAttribute(k_fc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaFuncSetAttribute(k_fc_attn_blk, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
 
 }  // namespace grx
