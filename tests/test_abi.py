@@ -50,3 +50,19 @@ def test_oracle_library_builds():
     orc.build()
     assert orc.LIB.exists()
     assert orc.lib().orc_expf_go(0.0) == 1.0
+
+
+def test_next_rows_fail_cleanly_without_device():
+    """The Mimi decoder, Whisper encoder and FastConformer handles refuse to
+    load without a device (an error code, no crash); the subsampling's row
+    count is plain host arithmetic (three stride-2 steps, encoder.go:32-39)."""
+    lib = g.lib()
+    for n, want in ((1, 1), (2, 1), (8, 1), (9, 2), (70, 9), (200, 25), (203, 26), (3000, 375)):
+        assert lib.grx_fconf_out_rows(n) == want
+    assert lib.grx_fconf_out_rows(0) == 0
+    if g.device_count() > 0:
+        pytest.skip("a device is present")
+    for cls in (g.Mimi, g.FConf):
+        with pytest.raises(g.GrxError) as e:
+            cls(b"GGUF" + b"\0" * 64)
+        assert e.value.code in (-2, -6)
