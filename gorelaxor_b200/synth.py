@@ -291,8 +291,10 @@ def _mat(rng, rows, cols):
     return _n(rng, (rows, cols), sd)
 
 
-def mimi_tensors(mc: MimiConfig, ldim: int, seed: int = 0) -> dict:
-    """Mimi decoder tensors in the converter's names (model.go:102-200)."""
+def mimi_tensors(mc: MimiConfig, ldim: int, seed: int = 0, encoder: bool = False) -> dict:
+    """Mimi decoder tensors in the converter's names (model.go:102-200); with
+    encoder, also the encoder's (SEANet encoder, mimi.enc_tf, mimi.down,
+    model.go:181-200, 308-313)."""
     rng = np.random.default_rng(seed + 31337)
     d = mc.d
     t: dict = {"mimi.quant": _n(rng, (d, ldim), 1.0 / np.sqrt(ldim)),
@@ -330,6 +332,40 @@ def mimi_tensors(mc: MimiConfig, ldim: int, seed: int = 0) -> dict:
         mult //= 2
     idx += 1
     conv(f"mimi.dec.{idx}", mc.nf, 1, mc.lastk)
+    if encoder:
+        rng2 = np.random.default_rng(seed + 65537)
+        for i in range(mc.layers):
+            p = f"mimi.enc_tf.{i}."
+            t[p + "norm1.weight"] = 1.0 + _n(rng2, d, 0.1)
+            t[p + "norm1.bias"] = _n(rng2, d, 0.1)
+            t[p + "norm2.weight"] = 1.0 + _n(rng2, d, 0.1)
+            t[p + "norm2.bias"] = _n(rng2, d, 0.1)
+            t[p + "attn_qkv.weight"] = _mat(rng2, 3 * d, d)
+            t[p + "attn_out.weight"] = _mat(rng2, d, d)
+            t[p + "ff1.weight"] = _mat(rng2, mc.ff, d)
+            t[p + "ff2.weight"] = _mat(rng2, d, mc.ff)
+            t[p + "ls1"] = np.abs(_n(rng2, d, 0.2))
+            t[p + "ls2"] = np.abs(_n(rng2, d, 0.2))
+
+        def econv(name, cin, cout, k):
+            t[name + ".weight"] = _mat(rng2, cout, k * cin)
+            t[name + ".bias"] = _n(rng2, cout, 0.05)
+
+        econv("mimi.enc.0", 1, mc.nf, mc.k)
+        idx, mult = 1, 1
+        for r in reversed(mc.ratios):
+            dim = mult * mc.nf
+            for _ in range(mc.nres):
+                econv(f"mimi.enc.{idx}.1", dim, dim // mc.comp, mc.resk)
+                econv(f"mimi.enc.{idx}.3", dim // mc.comp, dim, 1)
+                idx += 1
+            idx += 1
+            econv(f"mimi.enc.{idx}", dim, 2 * dim, 2 * r)
+            idx += 1
+            mult *= 2
+        idx += 1
+        econv(f"mimi.enc.{idx}", mult * mc.nf, d, mc.lastk)
+        t["mimi.down"] = _mat(rng2, ldim, 2 * mc.upsample * d)
     return t
 
 

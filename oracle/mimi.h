@@ -1,6 +1,7 @@
 // TEST INFRASTRUCTURE ONLY: the CPU oracle of Mimi's decoder as Pocket TTS
 // runs it (pockettts/mimi.go:24-150, nn.go:52-64 and 258-327,
-// speak.go:177-190), restated on kern.h and flowlm.h. Only tests/ use it.
+// speak.go:177-190) and of its encoder as CloneVoice runs it (mimi.go:152-
+// 179, voice.go:113-124), restated on kern.h and flowlm.h. Only tests/ use it.
 // Checked by the reference's model-free streaming tests (pockettts/
 // nn_test.go:37-153, restated in tests/) and a float64 decoder; parity
 // against reference outputs unpinned (the tree has none for Mimi).
@@ -226,20 +227,59 @@ struct MimiState {
   bool started = false;
 };
 
+// newSeaState (mimi.go:34-52): each step's carried rows (a residual block
+// has two slots).
+inline std::vector<std::vector<float>> sea_state(const std::vector<MStep>& steps) {
+  std::vector<std::vector<float>> prev;
+  for (const MStep& st : steps) {
+    if (st.kind == 0) prev.emplace_back(size_t(st.c.past()) * st.c.cin, 0.f);
+    if (st.kind == 1) prev.emplace_back(size_t(st.t.k - st.t.stride) * st.t.cout, 0.f);
+    if (st.kind == 2) {
+      prev.emplace_back(size_t(st.ra.past()) * st.ra.cin, 0.f);
+      prev.emplace_back(size_t(st.rb.past()) * st.rb.cin, 0.f);
+    }
+  }
+  return prev;
+}
+
 inline MimiState mimi_state(const MimiDecoder& m) {
   MimiState s;
   s.tf.k.assign(m.tf.layers.size(), {});
   s.tf.v.assign(m.tf.layers.size(), {});
   s.up_part.assign(size_t(m.upS) * m.tf.d, 0.f);
-  for (const MStep& st : m.steps) {
-    if (st.kind == 0) s.prev.emplace_back(size_t(st.c.past()) * st.c.cin, 0.f);
-    if (st.kind == 1) s.prev.emplace_back(size_t(st.t.k - st.t.stride) * st.t.cout, 0.f);
-    if (st.kind == 2) {
-      s.prev.emplace_back(size_t(st.ra.past()) * st.ra.cin, 0.f);
-      s.prev.emplace_back(size_t(st.rb.past()) * st.rb.cin, 0.f);
+  s.prev = sea_state(m.steps);
+  return s;
+}
+
+// runSea (mimi.go:61-106): T rows of Cc values through the steps, the
+// carried rows in prev; x, T and Cc become the output's.
+inline void run_sea(const std::vector<MStep>& steps, std::vector<std::vector<float>>& prev, std::vector<float>& x,
+                    int& T, int& Cc) {
+  size_t pi = 0;
+  for (const MStep& st : steps) {
+    if (st.elu) elu_vec(x.data(), long(T) * Cc);
+    if (st.kind == 0) {
+      std::vector<float> y(size_t(T / st.c.stride) * st.c.cout);
+      conv_run(st.c, prev[pi++], x.data(), T, y.data());
+      T /= st.c.stride;
+      Cc = st.c.cout;
+      x.swap(y);
+    } else if (st.kind == 1) {
+      std::vector<float> y(size_t(T) * st.t.stride * st.t.cout);
+      convtr_run(st.t, prev[pi++], x.data(), T, y.data());
+      T *= st.t.stride;
+      Cc = st.t.cout;
+      x.swap(y);
+    } else {
+      std::vector<float> v(x), h(size_t(T) * st.ra.cout), o(size_t(T) * Cc);
+      elu_vec(v.data(), long(T) * Cc);
+      conv_run(st.ra, prev[pi], v.data(), T, h.data());
+      elu_vec(h.data(), long(T) * st.ra.cout);
+      conv_run(st.rb, prev[pi + 1], h.data(), T, o.data());
+      for (size_t i = 0; i < x.size(); i++) x[i] = x[i] + o[i];
+      pi += 2;
     }
   }
-  return s;
 }
 
 // mimiDecoder.decode for one latent (mimi.go:126-150, runSea :45-98), then
@@ -256,37 +296,73 @@ inline void mimi_decode(const MimiDecoder& m, MimiState& s, const float* lat, fl
   int T = S, Cc = C;
   std::vector<float> x(full.begin(), full.begin() + long(S) * C);
   mtransformer_rows(m.tf, x.data(), T, s.tf);
-  size_t pi = 0;
-  for (const MStep& st : m.steps) {
-    if (st.elu) elu_vec(x.data(), long(T) * Cc);
-    if (st.kind == 0) {
-      std::vector<float> y(size_t(T / st.c.stride) * st.c.cout);
-      conv_run(st.c, s.prev[pi++], x.data(), T, y.data());
-      T /= st.c.stride;
-      Cc = st.c.cout;
-      x.swap(y);
-    } else if (st.kind == 1) {
-      std::vector<float> y(size_t(T) * st.t.stride * st.t.cout);
-      convtr_run(st.t, s.prev[pi++], x.data(), T, y.data());
-      T *= st.t.stride;
-      Cc = st.t.cout;
-      x.swap(y);
-    } else {
-      std::vector<float> v(x), h(size_t(T) * st.ra.cout), o(size_t(T) * Cc);
-      elu_vec(v.data(), long(T) * Cc);
-      conv_run(st.ra, s.prev[pi], v.data(), T, h.data());
-      elu_vec(h.data(), long(T) * st.ra.cout);
-      conv_run(st.rb, s.prev[pi + 1], h.data(), T, o.data());
-      for (size_t i = 0; i < x.size(); i++) x[i] = x[i] + o[i];
-      pi += 2;
-    }
-  }
+  run_sea(m.steps, s.prev, x, T, Cc);
   std::copy(x.begin(), x.begin() + long(T) * Cc, pcm);
   if (!s.started) {
     const int fade = m.sample_rate / 200, n = std::min(fade, T * Cc);
     for (int i = 0; i < n; i++) pcm[i] *= float(i) / float(fade - 1);
     s.started = true;
   }
+}
+
+// mimiEncoder (mimi.go:30-34, model.go:181-200, 308-313): the SEANet
+// encoder's steps, the transformer and the downsampling conv to 12.5 Hz
+// (weight [ldim][2·up·d], no bias, its first call padded with copies of
+// the first row: "replicate").
+struct MimiEncoder {
+  std::vector<MStep> steps;
+  MTransformer tf;
+  MConv down;
+  std::vector<float> down_b;
+};
+
+// encState (mimi.go:152-162).
+struct MimiEncState {
+  std::vector<std::vector<float>> sea;
+  Stream tf;
+  std::vector<float> down;
+  bool first = true;
+};
+
+inline MimiEncState mimi_enc_state(const MimiEncoder& e) {
+  MimiEncState s;
+  s.sea = sea_state(e.steps);
+  s.tf.k.assign(e.tf.layers.size(), {});
+  s.tf.v.assign(e.tf.layers.size(), {});
+  s.down.assign(size_t(e.down.past()) * e.down.cin, 0.f);
+  return s;
+}
+
+// encode (mimi.go:164-179): n samples (a multiple of the hop) → latents.
+inline std::vector<float> mimi_encode(const MimiEncoder& e, MimiEncState& st, const float* pcm, int n) {
+  std::vector<float> x(pcm, pcm + n);
+  int T = n, C = 1;
+  run_sea(e.steps, st.sea, x, T, C);
+  mtransformer_rows(e.tf, x.data(), T, st.tf);
+  if (st.first) {
+    for (int i = 0; i < e.down.past(); i++) std::copy(x.begin(), x.begin() + C, st.down.begin() + long(i) * C);
+    st.first = false;
+  }
+  std::vector<float> out(size_t(T / e.down.stride) * e.down.cout);
+  conv_run(e.down, st.down, x.data(), T, out.data());
+  return out;
+}
+
+// cloneCond's encoding (voice.go:113-124): x (24 kHz, after end_on_pause)
+// padded with zeros to whole frames, encoded twelve frames at a time with
+// one state. Returns the latents [frames][ldim].
+inline std::vector<float> mimi_clone_latents(const MimiEncoder& e, const float* x, int n, int frame) {
+  std::vector<float> buf(x, x + n);
+  buf.resize(size_t(n + (frame - n % frame) % frame), 0.f);
+  MimiEncState st = mimi_enc_state(e);
+  std::vector<float> lat;
+  const int piece = 12 * frame;
+  for (size_t i = 0; i < buf.size(); i += size_t(piece)) {
+    const int len = int(std::min(buf.size() - i, size_t(piece)));
+    std::vector<float> y = mimi_encode(e, st, buf.data() + i, len);
+    lat.insert(lat.end(), y.begin(), y.end());
+  }
+  return lat;
 }
 
 }  // namespace orc

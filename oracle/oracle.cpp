@@ -717,6 +717,9 @@ void orc_whisper_run(void* h, int n, const float* enc, const int* prompt, int np
 
 struct OMimi {
   MimiDecoder m;
+  MimiEncoder enc;
+  bool has_enc = false;
+  std::vector<float> zeros;
   std::map<std::string, Weight> w;
   std::map<std::string, const float*> v;
   std::string err;
@@ -839,7 +842,73 @@ int orc_mimi_ready(void* h) {
   last.elu = true;
   last.c = conv("mimi.dec." + std::to_string(idx), o->nf, 1, o->lastk, 1, 1);
   m.steps.push_back(last);
+  // the encoder (model.go:181-200, 308-313), when the tensors are there
+  if (o->w.count("mimi.enc.0.weight")) {
+    o->has_enc = true;
+    MimiEncoder& e = o->enc;
+    e.tf.d = m.tf.d, e.tf.heads = m.tf.heads, e.tf.ff = m.tf.ff, e.tf.context = m.tf.context;
+    e.tf.freqs = m.tf.freqs;
+    for (int i = 0;; i++) {
+      const std::string p = "mimi.enc_tf." + std::to_string(i) + ".";
+      if (!o->w.count(p + "attn_qkv.weight")) break;
+      MLayer l;
+      l.norm1w = V(p + "norm1.weight");
+      l.norm1b = V(p + "norm1.bias");
+      l.norm2w = V(p + "norm2.weight");
+      l.norm2b = V(p + "norm2.bias");
+      l.ls1 = V(p + "ls1");
+      l.ls2 = V(p + "ls2");
+      l.qkv = W(p + "attn_qkv.weight");
+      l.out = W(p + "attn_out.weight");
+      l.ff1 = W(p + "ff1.weight");
+      l.ff2 = W(p + "ff2.weight");
+      e.tf.layers.push_back(l);
+    }
+    MStep first;
+    first.c = conv("mimi.enc.0", 1, o->nf, o->kk, 1, 1);
+    e.steps.push_back(first);
+    int eidx = 1, emult = 1;
+    for (int ri = int(o->ratios.size()) - 1; ri >= 0; ri--) {
+      const int r = o->ratios[size_t(ri)], dim = emult * o->nf;
+      for (int j = 0, dl = 1; j < o->nres; j++, dl *= o->dil) {
+        const std::string p = "mimi.enc." + std::to_string(eidx) + ".";
+        MStep rb;
+        rb.kind = 2;
+        rb.ra = conv(p + "1", dim, dim / o->comp, o->resk, 1, dl);
+        rb.rb = conv(p + "3", dim / o->comp, dim, 1, 1, 1);
+        e.steps.push_back(rb);
+        eidx++;
+      }
+      eidx++;  // ELU
+      MStep cv;
+      cv.elu = true;
+      cv.c = conv("mimi.enc." + std::to_string(eidx), dim, 2 * dim, 2 * r, r, 1);
+      e.steps.push_back(cv);
+      eidx++;
+      emult *= 2;
+    }
+    eidx++;
+    MStep elast;
+    elast.elu = true;
+    elast.c = conv("mimi.enc." + std::to_string(eidx), emult * o->nf, m.tf.d, o->lastk, 1, 1);
+    e.steps.push_back(elast);
+    o->zeros.assign(size_t(m.ldim), 0.f);
+    e.down.w = W("mimi.down");
+    e.down.b = o->zeros.data();
+    e.down.cin = m.tf.d, e.down.cout = m.ldim, e.down.k = 2 * m.upS, e.down.stride = m.upS, e.down.dil = 1;
+  }
   return o->err.empty() ? 0 : -1;
+}
+
+// cloneCond's Mimi encoding of n samples (24 kHz): the latents [frames][ldim]
+// into out (room for (n + frame − 1)/frame rows); returns the row count, or
+// −1 without an encoder.
+int orc_mimi_clone_latents(void* h, const float* x, int n, float* out) {
+  auto* o = (OMimi*)h;
+  if (!o->has_enc) return -1;
+  const std::vector<float> lat = mimi_clone_latents(o->enc, x, n, o->m.frame);
+  std::copy(lat.begin(), lat.end(), out);
+  return int(lat.size() / size_t(o->m.ldim));
 }
 
 void* orc_mimi_state(void* h) { return new MimiState(mimi_state(((OMimi*)h)->m)); }

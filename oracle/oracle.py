@@ -86,6 +86,7 @@ def lib():
             "orc_whisper_ready": (I, [P]),
             "orc_whisper_encoder": (None, [P, I, I, I]),
             "orc_mimi_conv_run": (None, [P, P, I, I, I, I, I, P, P, I, P]),
+            "orc_mimi_clone_latents": (I, [P, P, I, P]),
             "orc_mimi_convtr_run": (None, [P, P, I, I, I, I, P, P, I, P]),
             "orc_attend_window": (None, [P, P, I, P, P, I, I, I, I]),
             "orc_fconf_new": (P, [I, I, I, I, I, I, I, I, I]),
@@ -496,6 +497,16 @@ class Mimi:
 
     def state(self):
         return MimiState(lib().orc_mimi_state(self.h))
+
+    def clone_latents(self, x: np.ndarray) -> np.ndarray:
+        """cloneCond's Mimi encoding (voice.go:113-124) of 24 kHz samples x:
+        latents [frames][ldim]."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(((x.size + self.frame - 1) // self.frame, self.ldim), np.float32)
+        n = lib().orc_mimi_clone_latents(self.h, p(x), x.size, p(out))
+        if n < 0:
+            raise RuntimeError("the Mimi tensors have no encoder")
+        return out[:n]
 
     def decode(self, st: "MimiState", latent) -> np.ndarray:
         """One latent (already scaled) → one frame of samples, with

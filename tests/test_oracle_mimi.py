@@ -237,3 +237,101 @@ def test_attend_window():
         got.append(out)
         pos += n
     _near(np.vstack(got), want)
+
+
+def _np_clone_latents(mc, t, x, ldim):
+    """A float64 Mimi encoder (SEANet encoder, windowed layer-scaled
+    transformer, the downsampling conv with its first row replicated) over
+    the whole clip at once — what the streaming encoder computes piece by
+    piece — with the int8 path's activation rounding where a weight is Q8_0."""
+    D = lambda a: np.asarray(a, np.float64)
+    isq = lambda name: isinstance(t[name], synth.Q8)
+    W = lambda name: D(synth.q8_dequant(t[name])) if isq(name) else D(t[name])
+
+    def q8round(v):
+        out = np.empty_like(v)
+        for b in range(0, v.size, 32):
+            blk = v[b:b + 32]
+            amax = np.abs(blk).max()
+            out[b:b + 32] = np.rint(blk * 127 / amax) * amax / 127 if amax else 0
+        return out
+
+    def lin(name, v, bias=None):
+        if isq(name):
+            v = np.stack([q8round(r) for r in v])
+        y = v @ W(name).T
+        return y + D(bias) if bias is not None else y
+
+    elu = lambda v: np.where(v > 0, v, np.expm1(np.minimum(v, 0)))
+
+    def conv(name, v, k, stride=1, dil=1, pad_rows=None, wname=None):
+        P = (k - 1) * dil + 1 - stride
+        pre = np.zeros((P, v.shape[1])) if pad_rows is None else pad_rows
+        buf = np.vstack([pre, v])
+        To = v.shape[0] // stride
+        col = np.stack([np.concatenate([buf[tt * stride + j * dil] for j in range(k)]) for tt in range(To)])
+        b = t.get(name + ".bias")
+        return lin(wname or name + ".weight", col, b)
+
+    frame = mc.frame
+    x = np.concatenate([D(x), np.zeros((frame - len(x) % frame) % frame)])[:, None]
+    x = conv("mimi.enc.0", x, mc.k)
+    idx, mult = 1, 1
+    for r in reversed(mc.ratios):
+        for j in range(mc.nres):
+            h = conv(f"mimi.enc.{idx}.1", elu(x), mc.resk, 1, mc.dil ** j)
+            x = x + conv(f"mimi.enc.{idx}.3", elu(h), 1)
+            idx += 1
+        idx += 1
+        x = conv(f"mimi.enc.{idx}", elu(x), 2 * r, r)
+        idx += 1
+        mult *= 2
+    idx += 1
+    x = conv(f"mimi.enc.{idx}", elu(x), mc.lastk)
+    d, hd = mc.d, mc.d // mc.heads
+    f = np.exp(-np.log(mc.max_period) * 2 / hd * np.arange(hd // 2))
+
+    def rope(v, pos):
+        v = v.reshape(mc.heads, hd // 2, 2).copy()
+        r_, i_ = v[..., 0].copy(), v[..., 1].copy()
+        v[..., 0], v[..., 1] = r_ * np.cos(f * pos) - i_ * np.sin(f * pos), r_ * np.sin(f * pos) + i_ * np.cos(f * pos)
+        return v.reshape(-1)
+
+    ln = lambda v, w, b: (v - v.mean(-1, keepdims=True)) / np.sqrt(v.var(-1, keepdims=True) + 1e-5) * D(w) + D(b)
+    gelu = lambda v: 0.5 * v * (1 + np.tanh(np.sqrt(2 / np.pi) * v * (1 + 0.044715 * v * v)))
+    T = x.shape[0]
+    for l in range(mc.layers):
+        p = f"mimi.enc_tf.{l}."
+        qkv = lin(p + "attn_qkv.weight", ln(x, t[p + "norm1.weight"], t[p + "norm1.bias"]))
+        q = np.stack([rope(qkv[r, :d], r) for r in range(T)])
+        k = np.stack([rope(qkv[r, d:2 * d], r) for r in range(T)])
+        v = qkv[:, 2 * d:]
+        att = np.zeros((T, d))
+        for r in range(T):
+            lo = max(0, r - mc.context + 1)
+            for h in range(mc.heads):
+                s = slice(h * hd, (h + 1) * hd)
+                sc = k[lo:r + 1, s] @ q[r, s] / np.sqrt(hd)
+                e = np.exp(sc - sc.max())
+                att[r, s] = (e / e.sum()) @ v[lo:r + 1, s]
+        x = x + D(t[p + "ls1"]) * lin(p + "attn_out.weight", att)
+        hh = ln(x, t[p + "norm2.weight"], t[p + "norm2.bias"])
+        x = x + D(t[p + "ls2"]) * lin(p + "ff2.weight", gelu(lin(p + "ff1.weight", hh)))
+    up = mc.upsample
+    return conv("mimi.down", x, 2 * up, up, 1, pad_rows=np.repeat(x[:1], up, axis=0), wname="mimi.down")
+
+
+@pytest.mark.parametrize("n", [1000, 1234])
+def test_mimi_clone_latents_against_numpy_model(n):
+    """cloneCond's Mimi encoding (voice.go:113-124, mimi.go:164-179) of a
+    clip padded to whole frames and encoded twelve frames at a time, against
+    the float64 encoder over the whole clip: within 2% relative RMS."""
+    mc = synth.MimiConfig()
+    t = synth.mimi_tensors(mc, LDIM, 2, encoder=True)
+    om = orc.Mimi(mc, t, LDIM)
+    x = np.random.default_rng(n).normal(0, 0.3, n).astype(np.float32)
+    got = om.clone_latents(x)
+    want = _np_clone_latents(mc, t, x, LDIM)
+    assert got.shape == want.shape == (-(-n // mc.frame), LDIM)
+    err = np.sqrt(((got - want) ** 2).sum() / (want ** 2).sum())
+    assert err < 0.02, err
