@@ -44,6 +44,7 @@ PEAKS = ROOT / "MEASURED_PEAKS.json"
 METRIC = "FlowLM frames/s (stream-frames per second, whole job)"
 UNIT = "frames/s"
 TRAFFIC_PER_ALGO = 143.51e6 / 139.79e6  # k_attn DRAM bytes / algorithmic bytes, measured (ncu)
+C0_FRAMES = 256  # one stream, 256 frames from a 64-position prefill
 
 
 def peaks():
@@ -116,20 +117,56 @@ def make_workload(n, seed0=1, prefill=64, layers=6, d=1024):
     return cfg, vs
 
 
-def cpu_sample(cfg, tensors, streams, frames, threads):
-    """The oracle (reference algorithm restated) on `threads` host threads:
-    `streams` independent streams × `frames` frames. Returns frames/s."""
-    from gorelaxor_b200 import synth
-    from oracle import oracle as orc
+def sample_prefill(run_frames, frames, prefill=64):
+    """The prefill length at which `frames` sampled frames attend, on
+    average, as many keys as the `run_frames` frames of a run from `prefill`
+    positions do (frame f attends prefill + f + 1 keys)."""
+    return max(1, prefill + run_frames // 2 - frames // 2)
 
-    om = orc.FlowLM(cfg, tensors)
-    _, vs = make_workload(streams)
-    sts = [om.stream(kv) for kv in vs]
-    noise = np.stack([synth.noise_frames(1 + i, frames, cfg.ldim, cfg.temperature) for i in range(streams)], axis=1)
-    t0 = time.perf_counter()
-    om.run(sts, noise, threads=threads)
-    dt = time.perf_counter() - t0
-    return streams * frames / dt, dt
+
+class CpuFlowLM:
+    """The reference's algorithm on the host: the oracle's fast mode (the
+    reference's SIMD kernels restated in their lane order, bit-identical to
+    the exact restatement; AVX-512 VNNI int8 tiles where the processor has
+    them), built once and warmed up before anything is timed."""
+
+    def __init__(self, cfg, tensors):
+        from oracle import oracle as orc
+
+        self.cfg, self.orc = cfg, orc
+        self.om = orc.FlowLM(cfg, tensors)
+        with orc.fast_mode() as fm:
+            self.kind = {2: "AVX-512 VNNI", 1: "AVX2", 0: "scalar"}[fm.kind]
+        self.sample(1, 2, 8, 1)  # packs the weight panels
+
+    def sample(self, streams, frames, prefill, threads):
+        """`streams` independent streams × `frames` frames from `prefill`
+        positions on `threads` threads (one stream per thread; a single
+        stream splits its products over them). Returns frames/s and the
+        wall time of the timed frames."""
+        from gorelaxor_b200 import synth
+
+        cfg = self.cfg
+        _, vs = make_workload(streams, prefill=prefill)
+        sts = [self.om.stream(kv) for kv in vs]
+        del vs
+        noise = np.stack([synth.noise_frames(1 + i, frames, cfg.ldim, cfg.temperature) for i in range(streams)], axis=1)
+        with self.orc.fast_mode():
+            t0 = time.perf_counter()
+            self.om.run(sts, noise, threads=threads)
+            dt = time.perf_counter() - t0
+        return streams * frames / dt, dt
+
+
+def cpu_sample(cfg, tensors, streams, frames, threads, run_frames=512, cpu=None):
+    """C1's CPU baseline: `streams` streams × `frames` frames at the run's
+    mean key count, one stream per thread. Returns frames/s, the wall time
+    and the prefill used."""
+    cpu = cpu or CpuFlowLM(cfg, tensors)
+    pre = sample_prefill(run_frames, frames)
+    cpu.sample(min(streams, threads), 2, pre, threads)  # warm-up at the same shape
+    v, dt = cpu.sample(streams, frames, pre, threads)
+    return v, dt, pre
 
 
 def run_reference(args, rank, world):
@@ -259,16 +296,19 @@ def run_reference(args, rank, world):
         return
     cfg = synth.FlowLMConfig()
     tensors = synth.flowlm_tensors(cfg, 0)
+    cpu = CpuFlowLM(cfg, tensors)
     streams, frames = min(args.batch, cores), 8
+    pre = sample_prefill(args.frames, frames)
     for _ in range(args.warmup):
-        cpu_sample(cfg, tensors, streams, 2, cores)
+        cpu.sample(streams, 2, pre, cores)
     vals, times = [], []
     for _ in range(args.steps):
-        v, dt = cpu_sample(cfg, tensors, streams, frames, cores)
+        v, dt = cpu.sample(streams, frames, pre, cores)
         vals.append(v)
         times.append(dt)
     value = float(np.mean(vals))
-    sample = f"{streams} streams x {frames} frames from the 64-position prefill per step, {cores} threads"
+    sample = (f"{streams} streams x {frames} frames per step from {pre}-position prefills (the run's mean of "
+              f"{64 + (args.frames + 1) / 2:.1f} keys), one stream per thread, {cores} threads, {cpu.kind} kernels")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
@@ -277,6 +317,13 @@ def run_reference(args, rank, world):
                        "frames": args.frames, "parallelism": "host threads"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    # C0 (one stream, batch 1): the stream's products split over every thread.
+    c0_frames = 32
+    c0_pre = sample_prefill(C0_FRAMES, c0_frames)
+    cpu.sample(1, 4, c0_pre, cores)
+    c0v, c0dt = cpu.sample(1, c0_frames, c0_pre, cores)
+    line["c0"] = {"value": c0v, "unit": UNIT, "us_per_frame": 1e6 / c0v, "cores": cores,
+                  "sample": f"1 stream x {c0_frames} frames from a {c0_pre}-position prefill, {cores} threads"}
     print(json.dumps(line), flush=True)
 
 
@@ -291,9 +338,10 @@ def tdt_cpu_sample(cfg, tensors, streams, frames, threads):
 
     om = orc.TDT(cfg, tensors)
     enc = np.stack([synth.encoder_frames(1 + i, frames, cfg.D) for i in range(streams)])
-    t0 = time.perf_counter()
-    om.run(enc, 16 * frames + 1024, threads)
-    dt = time.perf_counter() - t0
+    with orc.fast_mode():
+        t0 = time.perf_counter()
+        om.run(enc, 16 * frames + 1024, threads)
+        dt = time.perf_counter() - t0
     return streams * frames / dt, dt
 
 
@@ -430,10 +478,11 @@ def mimi_cpu_sample(mc, tensors, streams, frames, threads):
         for f in range(frames):
             om.decode(sts[i], lat[f, i])
 
-    t0 = time.perf_counter()
-    with ThreadPoolExecutor(max_workers=min(threads, streams)) as ex:
-        list(ex.map(one, range(streams)))
-    dt = time.perf_counter() - t0
+    with orc.fast_mode():
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=min(threads, streams)) as ex:
+            list(ex.map(one, range(streams)))
+        dt = time.perf_counter() - t0
     return streams * frames / dt, dt
 
 
@@ -550,10 +599,11 @@ def wenc_cpu_sample(cfg, tensors, words, windows, threads):
     mels = [synth.whisper_mel(1 + i, cfg) for i in range(windows)]
 
     def timed(blocks):
-        t0 = time.perf_counter()
-        with ThreadPoolExecutor(max_workers=min(threads, windows)) as ex:
-            list(ex.map(lambda m: om.encode(m, blocks), mels))
-        return time.perf_counter() - t0
+        with orc.fast_mode():
+            t0 = time.perf_counter()
+            with ThreadPoolExecutor(max_workers=min(threads, windows)) as ex:
+                list(ex.map(lambda m: om.encode(m, blocks), mels))
+            return time.perf_counter() - t0
 
     t_front, t_one = timed(0), timed(1)
     per_window = t_front + cfg.n_audio_layer * (t_one - t_front)
@@ -676,10 +726,11 @@ def fconf_cpu_sample(fc, tensors, utts, frames, threads):
     mels = [synth.fconf_mel(1 + i, fc.n_mels, frames) for i in range(utts)]
 
     def timed(blocks):
-        t0 = time.perf_counter()
-        with ThreadPoolExecutor(max_workers=min(threads, utts)) as ex:
-            rows = list(ex.map(lambda m: oc.encode(m, None, blocks).shape[0], mels))
-        return time.perf_counter() - t0, rows[0]
+        with orc.fast_mode():
+            t0 = time.perf_counter()
+            with ThreadPoolExecutor(max_workers=min(threads, utts)) as ex:
+                rows = list(ex.map(lambda m: oc.encode(m, None, blocks).shape[0], mels))
+            return time.perf_counter() - t0, rows[0]
 
     (t0, T), (t1, _) = timed(0), timed(1)
     per_utt = t0 + fc.layers * (t1 - t0)
@@ -796,9 +847,10 @@ def whisper_cpu_sample(cfg, tensors, words, streams, steps, threads):
     om = orc.Whisper(cfg, tensors, words)
     enc = np.stack([synth.whisper_encoder_out(1 + i, cfg) for i in range(streams)])
     prompt = [50360, 100, 200, 50257]
-    t0 = time.perf_counter()
-    om.run(enc, prompt, 3, steps, threads)
-    dt = time.perf_counter() - t0
+    with orc.fast_mode():
+        t0 = time.perf_counter()
+        om.run(enc, prompt, 3, steps, threads)
+        dt = time.perf_counter() - t0
     return streams * steps / dt, dt
 
 
@@ -1057,13 +1109,26 @@ def main():
                "d2h_bytes_per_step": F * B * (2 * cfg.ldim + 1) * 4,
                "note": "grx_streams_step per frame: noise H2D, latent+scaled+eos D2H, host-synchronous"}
 
+    # ---- C0: one stream, on this rank's GPU ----
+    c0 = run_c0(g, model, cfg, local, args.warmup, max(3, args.steps // 4)) if world == 1 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cores = os.cpu_count() or 1
         streams, frames = min(64, cores), 8
-        v, dt = cpu_sample(cfg, tensors, streams, frames, cores)
+        cpu_h = CpuFlowLM(cfg, tensors)
+        v, dt, pre = cpu_sample(cfg, tensors, streams, frames, cores, run_frames=F, cpu=cpu_h)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{streams} streams x {frames} frames from the 64-position prefill ({dt:.1f} s wall)"}
+               "sample": f"{streams} streams x {frames} frames from {pre}-position prefills (the run's mean key "
+                         f"count), one stream per thread, {cpu_h.kind} kernels ({dt:.1f} s wall, after a warm-up)"}
+        if c0 is not None:
+            c0_frames = 32
+            pre0 = sample_prefill(C0_FRAMES, c0_frames)
+            cpu_h.sample(1, 4, pre0, cores)
+            v0, _ = cpu_h.sample(1, c0_frames, pre0, cores)
+            c0["cpu_baseline"] = {"value": v0, "unit": UNIT, "cores": cores, "kind": "port",
+                                  "sample": f"1 stream x {c0_frames} frames from a {pre0}-position prefill, its "
+                                            f"products split over {cores} threads, {cpu_h.kind} kernels"}
 
     if dist:
         dist.barrier()
@@ -1089,8 +1154,89 @@ def main():
         "cpu_baseline": cpu,
         "gpu_launches": int(launches),
         "clocks": ck,
+        "c0": c0,
     }
     print(json.dumps(line), flush=True)
+
+
+def c0_bytes_per_frame(cfg, nk):
+    """SURVEY-style algorithmic bytes of one batch-1 frame attending nk keys:
+    the transformer's and flow head's weights once (Q8_0 at 34/32 bytes per
+    value, float32 at 4), lm.input and the EOS row, and the K/V rows read."""
+    d, ff, L, fd, ld = cfg.d, cfg.ff, cfg.layers, cfg.flow_dim, cfg.ldim
+    q8 = L * (3 * d * d + d * d + ff * d + d * ff)
+    q8 += fd * d + cfg.flow_depth * (3 * fd * fd + 2 * fd * fd) + 2 * fd * fd
+    f32 = fd * ld + ld * fd + d * ld + d
+    return q8 * 34 // 32 + f32 * 4 + L * 2 * d * 4 * nk
+
+
+def run_c0(g, model, cfg, local, warmup, steps):
+    """one stream from a 64-position prefill, 256 frames
+    per step, the latent fed back on the device. `value` is device-timed with
+    the noise resident in HBM (L2 flushed before each step); `e2e` is the
+    public per-frame call with pinned host buffers."""
+    import torch
+
+    F = C0_FRAMES
+    _, kvs = make_workload(1, seed0=1)
+    st = g.Streams(model, [model.voice(kvs[0])], F)
+    from gorelaxor_b200 import synth
+
+    noise = synth.noise_frames(1, F, cfg.ldim, cfg.temperature)[:, None, :].copy()
+    d_noise = torch.from_numpy(noise).cuda()
+    d_lat = torch.empty_like(d_noise)
+    d_eos = torch.empty((F, 1), device="cuda")
+    ext = torch.cuda.ExternalStream(st.cuda_stream())
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB, twice the L2
+    for _ in range(warmup):
+        st.reset()
+        st.run_device(F, d_noise.data_ptr(), d_lat.data_ptr(), d_eos.data_ptr())
+    st.sync()
+    clocks = Clocks(local)
+    clocks.start()
+    l0 = st.launches()
+    ms = []
+    for _ in range(steps):
+        st.reset()
+        flush.fill_(1.0)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        st.run_device(F, d_noise.data_ptr(), d_lat.data_ptr(), d_eos.data_ptr())
+        e1.record(ext)
+        st.sync()
+        ms.append(e0.elapsed_time(e1))
+    ck = clocks.stop()
+    launches = st.launches() - l0
+    t = float(np.mean(ms))
+    nk = 64 + np.arange(F) + 1
+    per_step = float(sum(c0_bytes_per_frame(cfg, int(k)) for k in nk))
+    hbm, peak_kind = peaks()
+    achieved = per_step / (t / 1000) / 1e9
+    # e2e: grx_streams_step per frame, pinned host noise in, latent/scaled/eos out
+    pin_noise = torch.from_numpy(noise).pin_memory().numpy()
+    outs = [torch.empty((1, cfg.ldim), pin_memory=True).numpy() for _ in range(2)]
+    pe = torch.empty(1, pin_memory=True).numpy()
+    st.reset()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for f in range(F):
+        st_step(st, pin_noise[f], outs[0], pe, outs[1])
+    e2e_s = time.perf_counter() - t0
+    return {
+        "workload": f"C0 FlowLM batch 1: 1 stream x {F} frames from a 64-position prefill",
+        "value": F / (t / 1000), "unit": UNIT, "us_per_frame": 1000 * t / F, "steps": steps, "warmup": warmup,
+        "e2e": {"value": F / e2e_s, "unit": UNIT, "h2d_bytes_per_step": F * cfg.ldim * 4,
+                "d2h_bytes_per_step": F * (2 * cfg.ldim + 1) * 4,
+                "note": "grx_streams_step per frame, host-synchronous"},
+        "roofline": {"bound": "hbm", "kernel": "whole frame", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_kind": peak_kind, "bytes_per_frame_mean": per_step / F,
+                     "note": "algorithmic bytes per frame (Q8_0 weights of the transformer and flow head, float32 "
+                             "rows, K/V rows 0..pos) over the frame's device time; the 82.9 MB of weights fit in "
+                             "the 126 MB L2, which is flushed before each step but not between the frames of a "
+                             "step, so later frames read weights largely from L2"},
+        "gpu_launches": int(launches), "clocks": ck,
+    }
 
 
 def st_step(st, noise_row, lat_out, eos_out, sc_out):

@@ -50,6 +50,18 @@ int scratch_on(int dev, uint8_t** out) {
   return GRX_OK;
 }
 
+// Puts the caller's current device back on every return path: the hosts this
+// entry point serves own their device state.
+struct DeviceGuard {
+  int prev = -1;
+  DeviceGuard() {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
 }  // namespace
 
 extern "C" int grx_linear_q8_static(const grx_weight* w, const float* d_x, int m, const float* d_bias,
@@ -74,6 +86,7 @@ extern "C" int grx_linear_q8_static(const grx_weight* w, const float* d_x, int m
                                   " values; split the rows or use grx_linear")
                                      .c_str());
   const int dev = weight_device(w);
+  const DeviceGuard keep;
   cudaError_t e = cudaSetDevice(dev);
   if (e != cudaSuccess)
     return set_error(GRX_ECUDA, (std::string("grx_linear_q8_static: cudaSetDevice: ") + cudaGetErrorString(e)).c_str());

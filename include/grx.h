@@ -89,7 +89,8 @@ int grx_linear(const grx_weight* w, const float* x, int m, const float* bias, fl
  * [m][cols], d_bias [rows] (may be NULL) and d_dst [m][rows] are DEVICE
  * pointers on the weight's device, owned by the caller; work is queued on
  * `stream` (a cudaStream_t, NULL for the default stream) and not waited
- * for. The call allocates nothing: the activations rounded to Q8_0 go to one
+ * for; the caller's current device is the same after the call as before
+ * it. The call allocates nothing: the activations rounded to Q8_0 go to one
  * fixed array in the library's device memory, GRX_STATIC_MAX_ELEMS int8
  * values plus their block scales (1.25 MiB), which every GPU that loads the
  * library holds until the process exits. m*cols above GRX_STATIC_MAX_ELEMS

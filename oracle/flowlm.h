@@ -138,7 +138,10 @@ inline std::vector<std::vector<float>> time_conds(const FlowLM& m, int steps) {
 // pockettts/nn.go:200-243: scores by gemvRows (dotF32x4 per group of four
 // keys, dotF32Go for the last nk%4), scaled, max, expSub, scaled by 1/Σ,
 // then the values added with AddScaled (axpy, one fused step per key).
+inline bool attend_one_fast(float* out, const float* q, const float* kc, const float* vc, int nk, int d, int heads);
+
 inline void attend_one(float* out, const float* q, const float* kc, const float* vc, int nk, int d, int heads) {
+  if (fast_on() && attend_one_fast(out, q, kc, vc, nk, d, heads)) return;
   int hd = d / heads;
   float scale = float(1 / std::sqrt(double(hd)));
   std::vector<float> sc((size_t)(nk));

@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <vector>
 
 namespace orc {
@@ -183,8 +184,13 @@ inline float gelu_avx(float v) {
   return e * 0.5f;
 }
 
+inline bool fast_on();
+inline bool gelu_vec_fast(float* x, int len);
+inline bool silu_vec_fast(float* x, int len);
+
 // geluVec, internal/kern/kernels_amd64.go:119-129.
 inline void gelu_vec(float* x, int len) {
+  if (fast_on() && gelu_vec_fast(x, len)) return;
   int n = len & ~7;
   for (int i = 0; i < n; i++) x[i] = gelu_avx(x[i]);
   for (int i = n; i < len; i++) x[i] = gelu_go(x[i]);
@@ -201,6 +207,7 @@ inline float silu_avx(float v) {
 
 // siluVec, internal/kern/kernels_amd64.go:241-250.
 inline void silu_vec(float* x, int len) {
+  if (fast_on() && silu_vec_fast(x, len)) return;
   int n = len & ~7;
   for (int i = 0; i < n; i++) x[i] = silu_avx(x[i]);
   for (int i = n; i < len; i++) x[i] = silu_go(x[i]);
@@ -354,8 +361,12 @@ inline void dot_q8x4(const float* x, const uint8_t* q, long ld, int k, float out
 
 enum WType { F32 = 0, F16 = 1, Q8_0 = 2 };
 
+struct PanelSlot;  // fast.h: a Q8_0 weight's panels for the fast mode
+
 // Weight, internal/kern/kern.go:41-50. `dropped` is DropRows (kern.go:99):
-// a packed Q8_0 weight whose products all take the int8 kernel.
+// a packed Q8_0 weight whose products all take the int8 kernel. `slot`
+// (shared by every copy of a model's weight) keeps the fast mode's panels,
+// packed on first use, as Weight.panels does (kern.go:48-49).
 struct Weight {
   int rows = 0, cols = 0;
   WType type = F32;
@@ -363,6 +374,7 @@ struct Weight {
   const uint16_t* h = nullptr;
   const uint8_t* q = nullptr;
   bool dropped = false;
+  std::shared_ptr<PanelSlot> slot;
 };
 
 // gemvRows for one row of A, internal/kern/gemm.go:195-259 (m=1, so no
@@ -472,9 +484,15 @@ inline void to_q8(uint8_t* out, const float* v, int rows, int cols) {
     }
 }
 
+// The fast mode (fast.h): the same values from SIMD kernels; false when
+// this processor lacks them.
+inline bool fast_on();
+inline bool linear_fast(float* dst, const float* x, int m, const Weight& w, const float* bias);
+
 // MatMul / Linear dispatch, internal/kern/kern.go:185-201 (the useInt
 // case, intMinM = 2, q8int.go:137; m ≤ smallM always on the token loop).
 inline void linear(float* dst, const float* x, int m, const Weight& w, const float* bias) {
+  if (fast_on() && linear_fast(dst, x, m, w, bias)) return;
   if (m == 0 || w.rows == 0) return;
   if (w.type == Q8_0 && (w.dropped || m >= 2)) {
     matmul_q8_int(dst, w.rows, x, w.cols, m, w, bias);

@@ -13,6 +13,7 @@
 #include <thread>
 
 #include "conformer.h"
+#include "fast.h"
 #include "flowlm.h"
 #include "mimi.h"
 #include "tdt.h"
@@ -55,6 +56,14 @@ extern "C" {
 
 // ---- kernel layer -------------------------------------------------------
 
+// The fast mode (fast.h) on or off for every later call; returns which
+// kernels it runs on this processor: 2 AVX-512 VNNI, 1 AVX2, 0 none (the
+// exact mode then runs).
+int orc_set_fast(int on) {
+  fast_flag().store(on ? 1 : 0);
+  return cpu_vnni512() ? 2 : cpu_avx2() ? 1 : 0;
+}
+
 float orc_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
 uint16_t orc_f32_to_f16(float f) { return f32_to_f16(f); }
 float orc_expf_go(float x) { return expf_go(x); }
@@ -77,6 +86,7 @@ void orc_linear(float* dst, const float* x, int m, int type, const void* w, int 
   wt.rows = rows;
   wt.cols = cols;
   wt.type = WType(type);
+  if (wt.type == Q8_0) wt.slot = std::make_shared<PanelSlot>();
   wt.f = (const float*)w;
   wt.h = (const uint16_t*)w;
   wt.q = (const uint8_t*)w;
@@ -124,6 +134,7 @@ void orc_flowlm_tensor(void* h, const char* name, int type, int rows, int cols, 
   w.rows = rows;
   w.cols = cols;
   w.type = WType(type);
+  if (w.type == Q8_0) w.slot = std::make_shared<PanelSlot>();
   w.f = (const float*)p;
   w.q = (const uint8_t*)p;
   o->w[name] = w;
@@ -313,6 +324,15 @@ void orc_flowlm_run(void* h, int n, void** streams, int frames, const float* noi
       }
     }
   };
+  if (fast_on() && n == 1 && threads > 1) {
+    // One stream: its products and attention heads split over the threads,
+    // as the reference's Speak runs with Options.Threads (speak.go:100-102).
+    Pool pool(threads);
+    tl_pool() = &pool;
+    work();
+    tl_pool() = nullptr;
+    return;
+  }
   threads = std::max(1, std::min(threads, n));
   std::vector<std::thread> ts;
   for (int t = 1; t < threads; t++) ts.emplace_back(work);
@@ -355,6 +375,7 @@ void orc_tdt_tensor(void* h, const char* name, int type, int rows, int cols, con
   w.rows = rows;
   w.cols = cols;
   w.type = WType(type);
+  if (w.type == Q8_0) w.slot = std::make_shared<PanelSlot>();
   w.f = (const float*)p;
   w.q = (const uint8_t*)p;
   o->w[name] = w;
@@ -488,6 +509,7 @@ void orc_whisper_tensor(void* h, const char* name, int type, int rows, int cols,
   w.rows = rows;
   w.cols = cols;
   w.type = WType(type);
+  if (w.type == Q8_0) w.slot = std::make_shared<PanelSlot>();
   w.f = (const float*)p;
   w.h = (const uint16_t*)p;
   o->w[name] = w;
@@ -657,6 +679,7 @@ void orc_whisper_matmul(float* c, const float* a, int m, int n, int k, int type,
   w.rows = n;
   w.cols = k;
   w.type = WType(type);
+  if (w.type == Q8_0) w.slot = std::make_shared<PanelSlot>();
   w.f = (const float*)b;
   w.h = (const uint16_t*)b;
   matmul_whisper(c, n, a, k, m, n, k, w, bias);
@@ -705,6 +728,15 @@ void orc_whisper_run(void* h, int n, const float* enc, const int* prompt, int np
       for (size_t k = 0; k < out.size(); k++) tokens[(size_t(i) * steps + k)] = out[k].id;
     }
   };
+  if (fast_on() && n == 1 && threads > 1) {
+    // One stream: its products and attention heads split over the threads,
+    // as the reference's Speak runs with Options.Threads (speak.go:100-102).
+    Pool pool(threads);
+    tl_pool() = &pool;
+    work();
+    tl_pool() = nullptr;
+    return;
+  }
   threads = std::max(1, std::min(threads, n));
   std::vector<std::thread> ts;
   for (int t = 1; t < threads; t++) ts.emplace_back(work);
@@ -755,6 +787,7 @@ void orc_mimi_tensor(void* h, const char* name, int type, int rows, int cols, co
   w.rows = rows;
   w.cols = cols;
   w.type = WType(type);
+  if (w.type == Q8_0) w.slot = std::make_shared<PanelSlot>();
   w.f = (const float*)p;
   w.q = (const uint8_t*)p;
   o->w[name] = w;
@@ -1013,6 +1046,7 @@ int orc_fconf_ready(void* h) {
       to_q8(o->own.back().data(), f.data(), w.rows, w.cols);
       w.type = Q8_0;
       w.q = o->own.back().data();
+      w.slot = std::make_shared<PanelSlot>();
     }
     return w;
   };

@@ -107,11 +107,26 @@ def lib():
             "orc_whisper_greedy": (I, [P, P, P, I, I, I, P, P]),
             "orc_whisper_run": (None, [P, I, P, P, I, I, I, P, I]),
         }
+        sig["orc_set_fast"] = (I, [I])
         for k, (r, a) in sig.items():
             f = getattr(L, k)
             f.restype, f.argtypes = r, a
         _lib = L
     return _lib
+
+
+class fast_mode:
+    """The oracle's fast mode (fast.h: the same values from SIMD kernels in
+    the reference's lane order) for the calls inside a with-block; `kind` is
+    2 on AVX-512 VNNI, 1 on AVX2, 0 where neither exists (exact mode then)."""
+
+    def __enter__(self):
+        self.kind = lib().orc_set_fast(1)
+        return self
+
+    def __exit__(self, *exc):
+        lib().orc_set_fast(0)
+        return False
 
 
 def p(a):

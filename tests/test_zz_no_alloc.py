@@ -31,26 +31,30 @@ def _case(seed, m, n, k, bias, dropped):
     return gw, x, b
 
 
-def _static(gw, x, b):
+def _static(gw, x, b, side_stream=False):
     m = x.shape[0]
     dx = torch.from_numpy(x).to("cuda:0")
     db = torch.from_numpy(b).to("cuda:0") if b is not None else None
     dy = torch.full((m, gw.rows), float("nan"), device="cuda:0")
-    stream = torch.cuda.current_stream(0).cuda_stream
-    g.linear_q8_static(gw, dx.data_ptr(), m, db.data_ptr() if db is not None else None, dy.data_ptr(), stream)
+    s = torch.cuda.Stream(0) if side_stream else torch.cuda.current_stream(0)
+    s.wait_stream(torch.cuda.current_stream(0))  # the inputs are written on the current stream
+    before = torch.cuda.current_device()
+    g.linear_q8_static(gw, dx.data_ptr(), m, db.data_ptr() if db is not None else None, dy.data_ptr(), s.cuda_stream)
+    assert torch.cuda.current_device() == before, "the call changed the caller's current device"
     torch.cuda.synchronize(0)
     return dy.cpu().numpy()
 
 
 def test_static_scratch_matches_linear_on_consecutive_calls(have_gpu):
-    # a large call (tensor-core product, bias), then a smaller one (M <= 8
-    # kernel, rows dropped, no bias) over the first one's leftovers, then the
-    # first again over the second's.
+    # a large call (the batched int8 product of more than 8 rows, with bias),
+    # then a smaller one (the product of up to 8 rows, rows dropped, no bias)
+    # over the first one's leftovers, then the first again over the second's,
+    # this time on a stream of its own instead of the default one.
     cases = [_case(1, 256, 1024, 4096, True, False),  # m*cols = 2^20, the whole array
              _case(2, 5, 256, 512, False, True)]
-    for gw, x, b in cases + cases[:1]:
+    for i, (gw, x, b) in enumerate(cases + cases[:1]):
         want = g.linear(gw, x, b)
-        got = _static(gw, x, b)
+        got = _static(gw, x, b, side_stream=i == 2)
         ne, rel = mismatch(got, want)
         assert bits_equal(got, want), f"{ne} of {got.size} differ (max rel {rel:.2e}, tolerance {TOL})"
 
