@@ -27,7 +27,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libgrx.so"
 
-GRX_ERRORS = {-1: "EINVAL", -2: "EFORMAT", -3: "ENOMEM", -4: "ECUDA", -5: "ERANGE", -6: "ENODEV"}
+GRX_ERRORS = {-1: "EINVAL", -2: "EFORMAT", -3: "ENOMEM", -4: "ECUDA", -5: "ERANGE", -6: "ENODEV", -7: "ETIMEDOUT"}
 
 _lib = None
 
@@ -77,6 +77,8 @@ def _sig(lib):
         "grx_streams_launches": (L, [P]),
         "grx_streams_cuda_stream": (P, [P]),
         "grx_streams_parts": (I, [P]),
+        "grx_streams_persistent": (I, [P]),
+        "grx_streams_watchdog_test": (I, [P]),
         "grx_mimi_load": (I, [P, S, I, PP]),
         "grx_mimi_free": (None, [P]),
         "grx_mimi_dims": (I, [P] + [C.POINTER(C.c_int)] * 8),
@@ -116,6 +118,7 @@ def _sig(lib):
         "grx_whisper_dims": (I, [P] + [C.POINTER(C.c_int)] * 6),
         "grx_whisper_tokens": (I, [P] + [C.POINTER(C.c_int)] * 6),
         "grx_whisper_suppressed": (I, [P, P, I]),
+        "grx_whisper_exact_rows": (L, [P]),
         "grx_whisper_batch_create": (I, [P, I, PP]),
         "grx_whisper_batch_free": (None, [P]),
         "grx_whisper_set_audio": (I, [P, P]),
@@ -158,11 +161,16 @@ def lib():
     return _lib
 
 
+def last_error() -> str:
+    """The calling thread's last error message (grx_last_error)."""
+    buf = C.create_string_buffer(4096)
+    lib().grx_last_error(buf, 4096)
+    return buf.value.decode(errors="replace")
+
+
 def _check(rc: int):
     if rc < 0:
-        buf = C.create_string_buffer(4096)
-        lib().grx_last_error(buf, 4096)
-        raise GrxError(rc, buf.value.decode(errors="replace"))
+        raise GrxError(rc, last_error())
     return rc
 
 
@@ -395,6 +403,15 @@ class Streams:
         """1, or 2 when the set runs as two concurrent parts."""
         return _check(lib().grx_streams_parts(self._h))
 
+    def persistent(self) -> bool:
+        """Whether the set runs its frames in the persistent one-stream kernel."""
+        return bool(_check(lib().grx_streams_persistent(self._h)))
+
+    def watchdog_test(self) -> int:
+        """Runs the persistent kernel with a grid barrier nothing completes;
+        returns the status code its bounded waits give (GRX_ETIMEDOUT, -7)."""
+        return lib().grx_streams_watchdog_test(self._h)
+
     def __del__(self, _free=_FREE):
         h, self._h = getattr(self, "_h", None), None
         if h:
@@ -623,6 +640,11 @@ class Whisper:
         out = np.zeros(512, np.int32)
         n = _check(lib().grx_whisper_suppressed(self._h, _ptr(out), 512))
         return out[:n].tolist()
+
+    def exact_rows(self) -> int:
+        """Rows process/sample decided in the reference's sequential order
+        (a parallel decision fell within its margin), since the model loaded."""
+        return int(lib().grx_whisper_exact_rows(self._h))
 
     def __del__(self, _free=_FREE):
         h, self._h = getattr(self, "_h", None), None

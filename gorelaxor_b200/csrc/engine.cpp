@@ -109,6 +109,16 @@ struct grx_streams {
   std::vector<std::unique_ptr<grx_streams>> parts;
   int row0 = 0;  // a part's first stream within its parent
   cudaEvent_t ev = nullptr;
+  // One stream runs its frames in the persistent kernel (k_frame1.cu) when
+  // the model and the device suit it: its arguments in device memory, the
+  // launch shape, the grid barrier counter and the watchdog's error word.
+  bool b1 = false;
+  Frame1Args* f1 = nullptr;
+  size_t f1_smem = 0;
+  uint32_t f1_slot = 0;
+  int f1_grid = 0;
+  unsigned* f1_bar = nullptr;
+  int* f1_err = nullptr;
   ~grx_streams() {
     parts.clear();
     cudaSetDevice(ar.dev);
@@ -365,6 +375,127 @@ int enqueue_frame(grx_streams* s) {
   launch_tick(s->io, st);
   k++;
   return k;
+}
+
+// Sets up the persistent one-stream kernel for a set of one stream whose
+// model has one decode step (GRX_FRAME1=0 keeps the per-kernel graph path).
+// Leaves b1 false when the model or the device does not suit it.
+int frame1_setup(grx_streams* s) {
+  const char* env = getenv("GRX_FRAME1");
+  grx_flowlm* m = s->m;
+  if ((env && env[0] == '0') || s->n != 1 || m->steps != 1 || m->L > F1_MAX_LAYERS || m->depth > F1_MAX_DEPTH ||
+      m->depth < 1)
+    return GRX_OK;
+  int G = 0, coop = 0;
+  CK(cudaDeviceGetAttribute(&G, cudaDevAttrMultiProcessorCount, s->ar.dev));
+  CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, s->ar.dev));
+  if (!coop) return GRX_OK;
+  Frame1Args A;
+  A.d = m->d;
+  A.heads = m->heads;
+  A.ff = m->ff;
+  A.L = m->L;
+  A.ldim = m->ldim;
+  A.fd = m->fd;
+  A.depth = m->depth;
+  A.cap = s->cap;
+  for (int l = 0; l < m->L; l++) {
+    const Layer& ly = m->layers[size_t(l)];
+    A.layers[l].n1w = ly.n1w;
+    A.layers[l].n1b = ly.n1b;
+    A.layers[l].n2w = ly.n2w;
+    A.layers[l].n2b = ly.n2b;
+    A.layers[l].qkv = ly.qkv;
+    A.layers[l].out = ly.out;
+    A.layers[l].ff1 = ly.ff1;
+    A.layers[l].ff2 = ly.ff2;
+  }
+  for (int k = 0; k < m->depth; k++) {
+    const Res& r = m->res[size_t(k)];
+    A.res[k].nw = r.nw;
+    A.res[k].nb = r.nb;
+    A.res[k].b1 = r.b1;
+    A.res[k].b2 = r.b2;
+    A.res[k].adab = r.adab;
+    A.res[k].fc1 = r.fc1;
+    A.res[k].fc2 = r.fc2;
+    A.res[k].ada = r.ada;
+  }
+  A.win = m->win;
+  A.outw = m->outw;
+  A.outb = m->outb;
+  A.eosw = m->eosw;
+  A.eosb = m->eosb;
+  A.mean = m->mean;
+  A.stdv = m->stdv;
+  A.cond = m->cond;
+  A.fada = m->fada;
+  A.condb = m->condb;
+  A.fin = m->fin;
+  A.finb = m->finb;
+  A.fadab = m->fadab;
+  A.fout = m->fout;
+  A.foutb = m->foutb;
+  A.tc = m->tc;
+  A.kv = s->kv;
+  A.pos = s->pos;
+  A.rope = s->rope;
+  A.x = s->x;
+  A.q = s->q;
+  A.lm_out = s->lm_out;
+  A.eos = s->eos;
+  A.lat = s->lat;
+  A.sy = s->sy;
+  A.h = s->h;
+  A.mod2 = s->mod2;
+  A.mm = s->mm;
+  A.io = s->io;
+  size_t smem = 0;
+  uint32_t slot = 0;
+  if (!frame1_suits(A, &smem, &slot, G) || frame1_max_active(smem) < 1) {
+    cudaGetLastError();
+    return GRX_OK;
+  }
+  int rc = 0;
+  A.att = s->ar.alloc<float>(size_t(m->d), &rc);
+  A.ffq = s->ar.alloc<int8_t>(size_t(m->ff), &rc);
+  A.ffs = s->ar.alloc<float>(size_t(m->ff / 32), &rc);
+  A.mod = s->ar.alloc<float>(size_t(m->depth) * 3 * m->fd, &rc);
+  A.bar = s->ar.alloc<unsigned>(1, &rc);
+  A.err = s->ar.alloc<int>(1, &rc);
+  if (rc) return rc;
+  CK(cudaMemset(A.err, 0, sizeof(int)));
+  s->f1 = s->ar.upload(&A, 1, &rc);
+  if (rc) return rc;
+  s->f1_smem = smem;
+  s->f1_slot = slot;
+  s->f1_grid = G;
+  s->f1_bar = A.bar;
+  s->f1_err = A.err;
+  s->b1 = true;
+  return GRX_OK;
+}
+
+// Queues `frames` frames of a persistent-kernel set.
+int frame1_run(grx_streams* s, int frames, int stall = 0) {
+  if (frames <= 0) return GRX_OK;
+  CK(cudaMemsetAsync(s->f1_bar, 0, sizeof(unsigned), s->st));
+  CK(launch_frame1(s->f1, s->f1_smem, s->f1_slot, s->f1_grid, frames, stall, s->st));
+  s->launches += 1;
+  return GRX_OK;
+}
+
+// After the set's stream is synchronised: GRX_ETIMEDOUT if a bounded wait of
+// the persistent kernel ran out (the set's state is then undefined until a
+// reset).
+int frame1_check(grx_streams* s) {
+  if (!s->b1) return GRX_OK;
+  int e = 0;
+  CK(cudaMemcpy(&e, s->f1_err, sizeof e, cudaMemcpyDeviceToHost));
+  if (e)
+    return fail(GRX_ETIMEDOUT, std::string("the persistent frame kernel gave up on a ") +
+                                   (e == 1 ? "grid barrier" : "weight copy") + " after its one-second limit");
+  return GRX_OK;
 }
 
 // A device-resident run replays kGraphFrames frames per graph launch (the
@@ -866,6 +997,7 @@ int grx_streams_reset(grx_streams* s) {
   grx_flowlm* m = s->m;
   CK(cudaSetDevice(s->ar.dev));
   CK(cudaMemcpyAsync(s->pos, s->pos0, sizeof(int) * size_t(s->n), cudaMemcpyDeviceToDevice, s->st));
+  if (s->b1) CK(cudaMemsetAsync(s->f1_err, 0, sizeof(int), s->st));
   for (int i = 0; i < s->n; i++)
     CK(cudaMemcpyAsync(s->lat + size_t(i) * m->ldim, m->bos, sizeof(float) * size_t(m->ldim), cudaMemcpyDeviceToDevice,
                        s->st));
@@ -1227,6 +1359,8 @@ static int streams_create_one(grx_flowlm* m, int n, const grx_voice* const* voic
       }
   }
   CK(cudaMemcpy(s->pos0, p0.data(), sizeof(int) * size_t(n), cudaMemcpyHostToDevice));
+  rc = frame1_setup(s.get());
+  if (rc) return rc;
   rc = grx_streams_reset(s.get());
   if (rc) return rc;
   rc = build_graph(s.get());
@@ -1294,15 +1428,28 @@ int grx_streams_step(grx_streams* s, const float* noise, float* lm_out, float* e
     const size_t r0 = size_t(q->row0), nl = size_t(q->n) * ld;
     FrameIO io{q->noise1, nullptr, nullptr, q->eos1, 0, nullptr, q->n, 0, 0, 1};
     CK(cudaMemcpyAsync(q->noise1, noise + r0 * ld, nl * 4, cudaMemcpyHostToDevice, q->st));
+    if (q->b1) {
+      io.latent = q->lat1;
+      io.scaled = q->scaled1;
+    }
     CK(cudaMemcpyAsync(q->io, &io, sizeof io, cudaMemcpyHostToDevice, q->st));
-    CK(cudaGraphLaunch(q->exec, q->st));
-    q->launches += q->per_frame;
+    if (q->b1) {
+      rc = frame1_run(q, 1);
+      if (rc) return rc;
+    } else {
+      CK(cudaGraphLaunch(q->exec, q->st));
+      q->launches += q->per_frame;
+    }
     if (lm_out) CK(cudaMemcpyAsync(lm_out + r0 * d, q->lm_out, size_t(q->n) * d * 4, cudaMemcpyDeviceToHost, q->st));
     if (eos) CK(cudaMemcpyAsync(eos + r0, q->eos1, size_t(q->n) * 4, cudaMemcpyDeviceToHost, q->st));
     if (latent) CK(cudaMemcpyAsync(latent + r0 * ld, q->lat1, nl * 4, cudaMemcpyDeviceToHost, q->st));
     if (scaled) CK(cudaMemcpyAsync(scaled + r0 * ld, q->scaled1, nl * 4, cudaMemcpyDeviceToHost, q->st));
   }
   for (grx_streams* q : sets) CK(cudaStreamSynchronize(q->st));
+  for (grx_streams* q : sets) {
+    rc = frame1_check(q);
+    if (rc) return rc;
+  }
   return GRX_OK;
 }
 
@@ -1319,6 +1466,7 @@ int grx_streams_run_device_timed(grx_streams* s, int frames, const float* d_nois
   if (s->parts.empty()) {
     FrameIO io{d_noise, d_latent, nullptr, d_eos, 0, d_attn_ts, s->n, 0, 0, 1};
     CK(cudaMemcpyAsync(s->io, &io, sizeof io, cudaMemcpyHostToDevice, s->st));
+    if (s->b1) return frame1_run(s, frames);
     int rc2 = replay_frames(s, frames);
     if (rc2) return rc2;
     s->launches += int64_t(frames) * s->per_frame;
@@ -1351,7 +1499,28 @@ int grx_streams_sync(grx_streams* s) {
   CK(cudaSetDevice(s->ar.dev));
   CK(cudaStreamSynchronize(s->st));
   CK(cudaGetLastError());
-  return GRX_OK;
+  return frame1_check(s);
+}
+
+int grx_streams_persistent(const grx_streams* s) {
+  if (!s) return fail(GRX_EINVAL, "null streams");
+  return s->b1 ? 1 : 0;
+}
+
+int grx_streams_watchdog_test(grx_streams* s) {
+  if (!s) return fail(GRX_EINVAL, "null streams");
+  if (!s->b1) return fail(GRX_EINVAL, "grx_streams_watchdog_test: the set does not run the persistent kernel");
+  CK(cudaSetDevice(s->ar.dev));
+  int rc = check_room(s, 1);
+  if (rc) return rc;
+  FrameIO io{s->noise1, s->lat1, s->scaled1, s->eos1, 0, nullptr, s->n, 0, 0, 1};
+  CK(cudaMemsetAsync(s->noise1, 0, sizeof(float) * size_t(s->m->ldim), s->st));
+  CK(cudaMemcpyAsync(s->io, &io, sizeof io, cudaMemcpyHostToDevice, s->st));
+  rc = frame1_run(s, 1, 1);
+  if (rc) return rc;
+  CK(cudaStreamSynchronize(s->st));
+  CK(cudaGetLastError());
+  return frame1_check(s);
 }
 
 }  // extern "C"

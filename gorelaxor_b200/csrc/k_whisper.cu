@@ -849,6 +849,7 @@ __global__ void __launch_bounds__(1024) k_wproc(WRows r, float* logits, float* s
     int o[4];
     if (amb) {
       proc_exact(lg, n, beg, o);
+      if (v.exact_rows) atomicAdd(v.exact_rows, 1ull);
     } else {
       const int id = best.i;
       const int tid = id >= beg ? id : bts.i;

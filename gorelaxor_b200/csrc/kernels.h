@@ -266,6 +266,51 @@ void launch_time_norm(const float* y0, const float* y1, const float* a0, const f
 void launch_cond_step(const float* y0, const float* tc, float* sy, int M, int N, cudaStream_t st);
 
 
+// ---- one stream's FlowLM frames in one persistent kernel (k_frame1.cu) ----
+constexpr int F1_THREADS = 512, F1_SLOTS = 5, F1_MAX_LAYERS = 12, F1_MAX_DEPTH = 4;
+
+struct F1Layer {
+  const float *n1w = nullptr, *n1b = nullptr, *n2w = nullptr, *n2b = nullptr;
+  DQ8 qkv, out, ff1, ff2;
+};
+struct F1Res {
+  const float *nw = nullptr, *nb = nullptr, *b1 = nullptr, *b2 = nullptr, *adab = nullptr;
+  DQ8 fc1, fc2, ada;
+};
+
+// Everything the kernel reads and writes, in device memory (one copy per
+// stream set); see engine.cpp for what each field is.
+struct Frame1Args {
+  int d = 0, heads = 0, ff = 0, L = 0, ldim = 0, fd = 0, depth = 0, cap = 0;
+  F1Layer layers[F1_MAX_LAYERS];
+  F1Res res[F1_MAX_DEPTH];
+  const float *win = nullptr, *outw = nullptr, *outb = nullptr, *eosw = nullptr;
+  float eosb = 0.f;
+  const float *mean = nullptr, *stdv = nullptr;
+  DQ8 cond, fada;
+  const float *condb = nullptr, *fin = nullptr, *finb = nullptr, *fadab = nullptr, *fout = nullptr, *foutb = nullptr;
+  const float* tc = nullptr;  // [fd]: the one decode step's time condition
+  float* kv = nullptr;        // the stream's cache [L][2][H][cap][64]
+  int* pos = nullptr;
+  const float* rope = nullptr;
+  float *x = nullptr, *q = nullptr, *att = nullptr, *lm_out = nullptr, *eos = nullptr, *lat = nullptr;
+  int8_t* ffq = nullptr;
+  float* ffs = nullptr;
+  float *sy = nullptr, *h = nullptr, *mod = nullptr, *mod2 = nullptr, *mm = nullptr;
+  FrameIO* io = nullptr;
+  unsigned* bar = nullptr;  // grid barrier arrivals, zeroed before each launch
+  int* err = nullptr;       // set when a bounded wait ran out
+};
+
+// Whether the model and set fit the kernel on a grid of G CTAs; its shared
+// memory and weight slot size.
+bool frame1_suits(const Frame1Args& A, size_t* smem, uint32_t* slot_bytes, int G);
+int frame1_max_active(size_t smem);
+// Queues `frames` frames (a cooperative launch of G CTAs); stall: the
+// watchdog check, a run whose first grid barrier never completes.
+cudaError_t launch_frame1(const Frame1Args* d_args, size_t smem, uint32_t slot_bytes, int G, int frames, int stall,
+                          cudaStream_t st);
+
 // ---- the FastConformer encoder (k_fconf.cu), one utterance, rows [time][channels] ----
 void launch_fc_mel_in(const float* mel, float* in, int frames, int nm, int valid, cudaStream_t st);
 void launch_fc_conv0(const float* in, int T, int F, const float* w, const float* b, int c, float* out, int T1, int F1,
@@ -349,6 +394,9 @@ struct WVocabDev {
       space = -1, n_suppress = 0;
   const int* suppress = nullptr;
   int audio_ctx = 1500;
+  // Rows k_wproc recomputed in the reference's sequential order because a
+  // parallel decision fell within its margin (device counter).
+  unsigned long long* exact_rows = nullptr;
 };
 
 void launch_wembed(const WRows& r, const WMat& tok_emb, const float* dec_pos, float* x, cudaStream_t st);

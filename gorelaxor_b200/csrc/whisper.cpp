@@ -527,12 +527,22 @@ int grx_whisper_load(const void* bytes, size_t len, int device, grx_whisper** ou
   v.n_suppress = int(m->suppress.size());
   v.suppress = m->suppress.empty() ? nullptr : m->ar.upload(m->suppress.data(), m->suppress.size(), &rc);
   v.audio_ctx = m->n_audio_ctx;
+  v.exact_rows = m->ar.alloc<unsigned long long>(1, &rc);
   if (rc) return rc;
+  CK(cudaMemset(v.exact_rows, 0, sizeof(unsigned long long)));
   *out = m.release();
   return GRX_OK;
 }
 
 void grx_whisper_free(grx_whisper* m) { delete m; }
+
+int64_t grx_whisper_exact_rows(const grx_whisper* m) {
+  if (!m) return fail(GRX_EINVAL, "null model");
+  unsigned long long v = 0;
+  CK(cudaSetDevice(m->dev));
+  CK(cudaMemcpy(&v, m->voc.exact_rows, sizeof v, cudaMemcpyDeviceToHost));
+  return int64_t(v);
+}
 
 int grx_whisper_dims(const grx_whisper* m, int* n_vocab, int* n_audio_ctx, int* n_state, int* n_head,
                      int* n_text_layer, int* n_text_ctx) {

@@ -27,6 +27,7 @@ extern "C" {
 #define GRX_ECUDA -4      /* a CUDA call failed */
 #define GRX_ERANGE -5     /* a stream ran past the positions its state was made for, or a size above a fixed limit */
 #define GRX_ENODEV -6     /* no such device */
+#define GRX_ETIMEDOUT -7  /* a bounded wait inside a kernel ran out (its watchdog); the state it was working on is undefined until reset */
 
 /* The calling thread's last error message (empty if none); returns the
  * message length. */
@@ -188,6 +189,21 @@ int grx_streams_parts(const grx_streams* s);
 int grx_streams_pos(const grx_streams* s, int i);
 /* Device kernel launches issued by this stream set since creation. */
 int64_t grx_streams_launches(const grx_streams* s);
+/* 1 when the set runs its frames in the persistent one-stream kernel: a set
+ * of one stream whose model has one decode step (a flow head of depth 1 to
+ * 4) runs every frame of a step or a device-resident run as one cooperative
+ * launch, one block per SM, with grid barriers between the frame's
+ * dependent steps (GRX_FRAME1=0, read when the set is created, keeps the
+ * per-kernel path). Same results bit for bit. Its waits are bounded (about
+ * a second each); one that runs out makes grx_streams_step /
+ * grx_streams_sync return GRX_ETIMEDOUT. 0 otherwise. */
+int grx_streams_persistent(const grx_streams* s);
+/* Checks the persistent kernel's watchdog: runs it once with a grid barrier
+ * that nothing completes and returns what its bounded waits report —
+ * GRX_ETIMEDOUT, after about a second, when they work. The set's positions
+ * are unchanged; reset it before the next frame. GRX_EINVAL for a set that
+ * does not run the persistent kernel. */
+int grx_streams_watchdog_test(grx_streams* s);
 
 /* ------------------------------------------- Pocket TTS Mimi decoder ----
  * mimiDecoder (pockettts/mimi.go:24-150): the latent projection, the
@@ -330,6 +346,12 @@ int grx_whisper_dims(const grx_whisper* m, int* n_vocab, int* n_audio_ctx, int* 
 int grx_whisper_tokens(const grx_whisper* m, int* eot, int* sot, int* prev, int* nosp, int* beg, int* n_lang);
 /* vocab.suppressed() (vocab.go:103-118) into out (up to cap); returns the count. */
 int grx_whisper_suppressed(const grx_whisper* m, int* out, int cap);
+/* How many sampled rows, over every batch of this model since it was
+ * loaded, were decided in the reference's sequential order: process/sample
+ * sums the vocabulary as trees and recomputes a row in sequence when a
+ * decision it feeds (the timestamp rule, the winner against an earlier
+ * index) falls within the margin those sums' roundings could move. */
+int64_t grx_whisper_exact_rows(const grx_whisper* m);
 /* n streams, each a decoding sequence (its self-attention cache, this
  * window's cross K/V, its sampling state). */
 int grx_whisper_batch_create(grx_whisper* m, int n, grx_whisper_batch** out);

@@ -421,6 +421,66 @@ inline void gemv_rows_fast(float* y, const float* x, const Weight& w, const floa
   }
 }
 
+inline bool gemv_rows_fast_ok(float* y, const float* x, const Weight& w, const float* bias) {
+  if (!cpu_avx2()) return false;
+  gemv_rows_fast(y, x, w, bias);
+  return true;
+}
+
+// whisper/gemm.go:124-209's packed product for rows below m/6·6 (same
+// values as matmul_whisper): per output c = bias (or 0), then for each
+// 256-deep pass c += the fused chain over that pass; lanes run 16 outputs'
+// chains side by side, the weight panel widened to float32 once per pass.
+__attribute__((target("avx2,fma,f16c"))) inline void mw_panel(float* c, int ldc, const float* a, int lda, int mfull,
+                                                               int n, int k, const Weight& b, int p, float* bt) {
+  constexpr int KC = 256;
+  const int col0 = p * 16, cols = std::min(16, n - col0);
+  for (int k0 = 0; k0 < k; k0 += KC) {
+    const int kn = std::min(KC, k - k0);
+    for (int kk = 0; kk < kn; kk++)
+      for (int j = 0; j < 16; j++) {
+        const int col = col0 + j;
+        bt[kk * 16 + j] = j < cols ? (b.type == F16 ? f16_to_f32(b.h[long(col) * k + k0 + kk]) : b.f[long(col) * k + k0 + kk])
+                                   : 0.f;
+      }
+    for (int i = 0; i < mfull; i++) {
+      const float* ai = a + long(i) * lda + k0;
+      __m256 lo = _mm256_setzero_ps(), hi = _mm256_setzero_ps();
+      for (int kk = 0; kk < kn; kk++) {
+        const __m256 av = _mm256_set1_ps(ai[kk]);
+        lo = _mm256_fmadd_ps(av, _mm256_loadu_ps(bt + kk * 16), lo);
+        hi = _mm256_fmadd_ps(av, _mm256_loadu_ps(bt + kk * 16 + 8), hi);
+      }
+      alignas(32) float acc[16];
+      _mm256_store_ps(acc, lo);
+      _mm256_store_ps(acc + 8, hi);
+      float* ci = c + long(i) * ldc + col0;
+      for (int j = 0; j < cols; j++) ci[j] = ci[j] + acc[j];
+    }
+  }
+}
+
+inline bool matmul_whisper_fast(float* c, int ldc, const float* a, int lda, int m, int n, int k, const Weight& b,
+                                const float* bias) {
+  if (!cpu_avx2() || m < 6 || !(b.type == F16 || b.type == F32)) return false;
+  const int mfull = m / 6 * 6, np = (n + 15) / 16;
+  for (int i = 0; i < mfull; i++)
+    for (int j = 0; j < n; j++) c[long(i) * ldc + j] = bias ? bias[j] : 0.f;
+  Pool* pool = tl_pool();
+  auto run = [&](int p0, int p1) {
+    std::vector<float> bt(256 * 16);
+    for (int p = p0; p < p1; p++) mw_panel(c, ldc, a, lda, mfull, n, k, b, p, bt.data());
+  };
+  if (pool && pool->size() > 1 && np > 1) {
+    const int items = std::min(np, 4 * pool->size());
+    pool->run(items, [&](int it) { run(np * it / items, np * (it + 1) / items); });
+  } else {
+    run(0, np);
+  }
+  for (int i = mfull; i < m; i++) gemv_rows_fast(c + long(i) * ldc, a + long(i) * lda, b, bias);
+  return true;
+}
+
 // kern.Linear with the fast kernels (the dispatch of kern.go:185-201).
 inline bool linear_fast(float* dst, const float* x, int m, const Weight& w, const float* bias) {
   if (!cpu_avx2()) return false;

@@ -377,9 +377,13 @@ struct Weight {
   std::shared_ptr<PanelSlot> slot;
 };
 
+inline bool fast_on();
+inline bool gemv_rows_fast_ok(float* y, const float* x, const Weight& w, const float* bias);
+
 // gemvRows for one row of A, internal/kern/gemm.go:195-259 (m=1, so no
 // Q8_0 widening; whisper/gemm.go:187-218 gemv is the same for F16/F32).
 inline void gemv_rows(float* y, const float* x, const Weight& w, const float* bias) {
+  if (fast_on() && gemv_rows_fast_ok(y, x, w, bias)) return;
   int n = w.rows, k = w.cols;
   for (int j = 0; j < n; j += 4) {
     if (j + 4 <= n) {

@@ -64,6 +64,19 @@ int orc_set_fast(int on) {
   return cpu_vnni512() ? 2 : cpu_avx2() ? 1 : 0;
 }
 
+// A pool of `threads` threads over which the calling thread's products and
+// attention heads split (a single stream's work, as the reference's
+// Options.Threads); threads <= 1 removes it.
+void orc_set_pool(int threads) {
+  static std::unique_ptr<Pool> pool;
+  tl_pool() = nullptr;
+  pool.reset();
+  if (threads > 1) {
+    pool = std::make_unique<Pool>(threads);
+    tl_pool() = pool.get();
+  }
+}
+
 float orc_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
 uint16_t orc_f32_to_f16(float f) { return f32_to_f16(f); }
 float orc_expf_go(float x) { return expf_go(x); }

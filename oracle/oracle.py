@@ -108,6 +108,7 @@ def lib():
             "orc_whisper_run": (None, [P, I, P, P, I, I, I, P, I]),
         }
         sig["orc_set_fast"] = (I, [I])
+        sig["orc_set_pool"] = (None, [I])
         for k, (r, a) in sig.items():
             f = getattr(L, k)
             f.restype, f.argtypes = r, a
@@ -118,13 +119,22 @@ def lib():
 class fast_mode:
     """The oracle's fast mode (fast.h: the same values from SIMD kernels in
     the reference's lane order) for the calls inside a with-block; `kind` is
-    2 on AVX-512 VNNI, 1 on AVX2, 0 where neither exists (exact mode then)."""
+    2 on AVX-512 VNNI, 1 on AVX2, 0 where neither exists (exact mode then).
+    With `threads`, a single call's products and heads split over that many
+    threads (calls made from this Python thread)."""
+
+    def __init__(self, threads: int = 0):
+        self.threads = threads
 
     def __enter__(self):
         self.kind = lib().orc_set_fast(1)
+        if self.threads > 1:
+            lib().orc_set_pool(self.threads)
         return self
 
     def __exit__(self, *exc):
+        if self.threads > 1:
+            lib().orc_set_pool(0)
         lib().orc_set_fast(0)
         return False
 

@@ -63,8 +63,12 @@ inline void softmax_whisper(float* x, int n) {
 }
 
 // matmul, whisper/gemm.go:124-209: C[m][n] = A[m][k]·Bᵀ + bias, B F16 or F32.
+inline bool matmul_whisper_fast(float* c, int ldc, const float* a, int lda, int m, int n, int k, const Weight& b,
+                                const float* bias);
+
 inline void matmul_whisper(float* c, int ldc, const float* a, int lda, int m, int n, int k, const Weight& b,
                            const float* bias) {
+  if (fast_on() && matmul_whisper_fast(c, ldc, a, lda, m, n, k, b, bias)) return;
   const int MR = 6, NR = 16, KC = 256;
   auto brow = [&](int col, int kk) { return b.type == F16 ? f16_to_f32(b.h[long(col) * k + kk]) : b.f[long(col) * k + kk]; };
   if (m < MR) {

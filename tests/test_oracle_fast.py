@@ -160,3 +160,39 @@ def test_fast_256bit_path_matches_exact():
     env = dict(os.environ, ORC_FAST_AVX2="1", PYTHONPATH=ROOT)
     r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("m,n,k,kind", [(6, 512, 512, 1), (7, 64, 300, 0), (13, 40, 96, 1), (1500, 64, 512, 1)])
+def test_fast_whisper_packed_product(m, n, k, kind):
+    """whisper/gemm.go:124-209 (bias, then += each 256-deep fused chain for
+    rows below m/6·6, gemv for the rest), F16 (kind 1) and F32 weights."""
+    _need_simd()
+    rng = np.random.default_rng(m + n + k)
+    a = rng.normal(0, 1, (m, k)).astype(np.float32)
+    wf = rng.normal(0, 0.1, (n, k)).astype(np.float32)
+    w = wf.astype(np.float16).view(np.uint16) if kind == 1 else wf
+    w = np.ascontiguousarray(w)
+    bias = rng.normal(0, 0.1, n).astype(np.float32)
+
+    def run():
+        c = np.empty((m, n), np.float32)
+        orc.lib().orc_whisper_matmul(orc.p(c), orc.p(a), m, n, k, kind, orc.p(w), orc.p(bias))
+        return c
+
+    e, f = _both(run)
+    assert bits_equal(e, f)
+
+
+def test_fast_whisper_greedy_small():
+    """A small Whisper decoder's cross K/V prep and 12 greedy steps, the
+    fast mode with a pool of 4 threads against the exact mode."""
+    _need_simd()
+    cfg = synth.WhisperConfig(n_state=128, n_head=2, n_text_layer=2, n_text_ctx=64)
+    t = synth.whisper_tensors(cfg, 0)
+    om = orc.Whisper(cfg, t, synth.whisper_words(cfg))
+    enc = synth.whisper_encoder_out(3, cfg)
+    prompt = [50360, 100, 200, 50257]
+    want, wns = om.greedy(om.seq(enc), prompt, 3, 12)
+    with orc.fast_mode(4):
+        got, ns = om.greedy(om.seq(enc), prompt, 3, 12)
+    assert np.array_equal(got, want) and np.float32(ns).view(np.uint32) == np.float32(wns).view(np.uint32)
