@@ -18,14 +18,15 @@ directly from the benchmark's distributions (f16 scale = f16(|N(0, 0.002)|),
 int8 uniform on [-127, 127]); everything else is float32.
 
 The GGUF layout (header, key/value section, tensor table, 32-byte aligned
-data) is the one tools/convert_nemo.py:71-147 writes and
-internal/gguf/gguf.go:292-354 reads.
+data) is the one internal/gguf/gguf.go:292-354 reads; tests/test_golden.py
+checks a file written by the reference's own converter against this
+library's reader.
 """
 
 from __future__ import annotations
 
 import struct
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 
@@ -57,81 +58,73 @@ class Q8:
         return (self.rows, self.cols)
 
 
-@dataclass
+def _le(v: int, width: int, signed: bool = False) -> bytes:
+    return int(v).to_bytes(width, "little", signed=signed)
+
+
 class GGUFWriter:
-    arch: str
-    kv: list = field(default_factory=list)
-    tensors: list = field(default_factory=list)
+    """A GGUF v3 file built in memory, in the layout internal/gguf/gguf.go:
+    292-354 parses: "GGUF", version 3, the tensor and key/value counts (u64);
+    each key/value as a string key, a u32 type code and the value; the
+    tensor table (name, dimension count, dims fastest-first as u64, the ggml
+    type, the offset into the data section); zero padding to a 32-byte
+    boundary, then each tensor's bytes, each starting on a 32-byte boundary
+    of the data section (general.alignment's default)."""
 
-    def __post_init__(self):
-        self.add("general.architecture", T_STR, self.arch)
+    def __init__(self, arch: str):
+        self._meta = bytearray()  # the encoded key/value pairs
+        self._count = 0
+        self._tensors: list[tuple[str, int, list[int], bytes]] = []
+        self.str("general.architecture", arch)
 
-    def add(self, key, vtype, value, etype=-1):
-        self.kv.append((key, vtype, value, etype))
+    def _begin(self, key: str, code: int) -> bytearray:
+        self._meta += _s(key) + _le(code, 4)
+        self._count += 1
+        return self._meta
 
-    def u32(self, k, v):
-        self.add(k, T_U32, int(v))
+    def u32(self, key, v):
+        self._begin(key, T_U32).extend(_le(v, 4))
 
-    def i32(self, k, v):
-        self.add(k, T_I32, int(v))
+    def i32(self, key, v):
+        self._begin(key, T_I32).extend(_le(v, 4, signed=True))
 
-    def f32(self, k, v):
-        self.add(k, T_F32, float(v))
+    def f32(self, key, v):
+        self._begin(key, T_F32).extend(np.float32(v).tobytes())
 
-    def str(self, k, v):
-        self.add(k, T_STR, str(v))
+    def bool(self, key, v):
+        self._begin(key, T_BOOL).append(1 if v else 0)
 
-    def bool(self, k, v):
-        self.add(k, T_BOOL, bool(v))
+    def str(self, key, v):
+        self._begin(key, T_STR).extend(_s(str(v)))
 
-    def i32s(self, k, v):
-        self.add(k, T_ARR, [int(x) for x in v], T_I32)
+    def i32s(self, key, v):
+        vals = np.asarray([int(x) for x in v], dtype="<i4")
+        self._begin(key, T_ARR).extend(_le(T_I32, 4) + _le(len(vals), 8) + vals.tobytes())
 
-    def tensor(self, name, arr):
-        self.tensors.append((name, arr))
-
-    @staticmethod
-    def _value(vtype, v, etype):
-        if vtype == T_STR:
-            return _s(v)
-        if vtype == T_ARR:
-            out = struct.pack("<IQ", etype, len(v))
-            if etype == T_STR:
-                return out + b"".join(_s(x) for x in v)
-            fmt = {T_I32: "<i", T_U32: "<I", T_F32: "<f", T_F64: "<d"}[etype]
-            return out + b"".join(struct.pack(fmt, x) for x in v)
-        fmt = {T_U32: "<I", T_I32: "<i", T_F32: "<f", T_BOOL: "<?", T_U64: "<Q", T_F64: "<d"}[vtype]
-        return struct.pack(fmt, v)
+    def tensor(self, name: str, arr) -> None:
+        """A Q8 matrix keeps its blocks; float16 and float32 arrays their
+        values (dims listed fastest first, as ggml does)."""
+        if isinstance(arr, Q8):
+            self._tensors.append((name, GGML_Q8_0, [arr.cols, arr.rows], arr.blocks.tobytes()))
+            return
+        kind, dt = (GGML_F16, "<f2") if np.asarray(arr).dtype == np.float16 else (GGML_F32, "<f4")
+        a = np.ascontiguousarray(arr, dtype=dt)
+        self._tensors.append((name, kind, [int(d) for d in a.shape[::-1]] or [1], a.tobytes()))
 
     def to_bytes(self) -> bytes:
-        infos, datas = [], []
-        off = 0
-        for name, arr in self.tensors:
-            if isinstance(arr, Q8):
-                dims, gtype, data = [arr.cols, arr.rows], GGML_Q8_0, arr.blocks.tobytes()
-            elif arr.dtype == np.float16:
-                a = np.ascontiguousarray(arr, dtype="<f2")
-                dims, gtype, data = (list(reversed(a.shape)) or [1]), GGML_F16, a.tobytes()
-            else:
-                a = np.ascontiguousarray(arr, dtype="<f4")
-                dims, gtype, data = (list(reversed(a.shape)) or [1]), GGML_F32, a.tobytes()
-            info = _s(name) + struct.pack("<I", len(dims))
-            info += b"".join(struct.pack("<Q", d) for d in dims)
-            info += struct.pack("<IQ", gtype, off)
-            infos.append(info)
-            datas.append(data)
-            off += len(data)
-            off += (-off) % ALIGN
-        head = b"GGUF" + struct.pack("<IQQ", 3, len(self.tensors), len(self.kv))
-        for k, vtype, v, etype in self.kv:
-            head += _s(k) + struct.pack("<I", vtype) + self._value(vtype, v, etype)
-        head += b"".join(infos)
-        head += b"\0" * ((-len(head)) % ALIGN)
-        parts = [head]
-        for d in datas:
-            parts.append(d)
-            parts.append(b"\0" * ((-len(d)) % ALIGN))
-        return b"".join(parts)
+        def pad(n):
+            return bytes((-n) % ALIGN)
+
+        out = bytearray(b"GGUF" + _le(3, 4) + _le(len(self._tensors), 8) + _le(self._count, 8))
+        out += self._meta
+        at = 0  # where each tensor's bytes start in the data section
+        for name, kind, dims, data in self._tensors:
+            out += _s(name) + _le(len(dims), 4) + b"".join(_le(d, 8) for d in dims) + _le(kind, 4) + _le(at, 8)
+            at += len(data) + len(pad(len(data)))
+        out += pad(len(out))
+        for _, _, _, data in self._tensors:
+            out += data + pad(len(data))
+        return bytes(out)
 
 
 # ------------------------------------------------------- value distributions
