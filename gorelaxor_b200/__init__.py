@@ -113,6 +113,7 @@ def _sig(lib):
         "grx_tdt_batch_cuda_stream": (P, [P]),
         "grx_tdt_batch_launches": (L, [P]),
         "grx_tdt_batch_iterations": (L, [P]),
+        "grx_tdt_batch_stream_iterations": (L, [P]),
         "grx_whisper_load": (I, [P, S, I, PP]),
         "grx_whisper_free": (None, [P]),
         "grx_whisper_dims": (I, [P] + [C.POINTER(C.c_int)] * 6),
@@ -608,6 +609,10 @@ class TDTBatch:
 
     def launches(self) -> int:
         return lib().grx_tdt_batch_launches(self._h)
+
+    def stream_iterations(self) -> int:
+        """The last decode's loop iterations summed over its streams."""
+        return int(_check(lib().grx_tdt_batch_stream_iterations(self._h)))
 
     def iterations(self) -> int:
         return lib().grx_tdt_batch_iterations(self._h)

@@ -439,4 +439,15 @@ int64_t grx_tdt_batch_launches(const grx_tdt_batch* b) { return b ? b->launches 
 
 int64_t grx_tdt_batch_iterations(const grx_tdt_batch* b) { return b ? b->iterations : -1; }
 
+int64_t grx_tdt_batch_stream_iterations(grx_tdt_batch* b) {
+  if (!b) return fail(GRX_EINVAL, "null batch");
+  CK(cudaSetDevice(b->ar.dev));
+  std::vector<int> it(size_t(b->n));
+  CK(cudaMemcpyAsync(it.data(), b->a.iter, sizeof(int) * size_t(b->n), cudaMemcpyDeviceToHost, b->st));
+  CK(cudaStreamSynchronize(b->st));
+  int64_t t = 0;
+  for (int v : it) t += v;
+  return t;
+}
+
 }  // extern "C"

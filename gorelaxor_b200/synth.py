@@ -665,6 +665,15 @@ def whisper_words(cfg: WhisperConfig) -> list[bytes]:
     return words
 
 
+def whisper_q8_bytes(cfg: "WhisperConfig") -> int:
+    """Q8_0 bytes a decode step reads once per token row: the token
+    embedding (the logits product), and per layer the self-attention's q, k,
+    v, o, the cross-attention's q and o (its k and v act on the encoder
+    output once per window) and the two MLP matrices."""
+    st = cfg.n_state
+    return (cfg.n_vocab * st + cfg.n_text_layer * (6 * st * st + 8 * st * st)) * Q8_BYTES // QK
+
+
 def whisper_tensors(cfg: WhisperConfig, seed: int = 0) -> dict:
     """The text decoder's tensors in whisper.cpp's names (model.go:464-484):
     matrices as Q8_0 (ftype 8), vectors and positions float32. The encoder's

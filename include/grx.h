@@ -327,6 +327,10 @@ void* grx_tdt_batch_cuda_stream(const grx_tdt_batch* b);
 /* Kernel launches and loop iterations (batch rounds) issued so far. */
 int64_t grx_tdt_batch_launches(const grx_tdt_batch* b);
 int64_t grx_tdt_batch_iterations(const grx_tdt_batch* b);
+/* Loop iterations of the last decode summed over its streams (each is one
+ * joint evaluation of one stream, the reference's unit of work in
+ * rnnt.go:138-171); waits for the batch's stream. */
+int64_t grx_tdt_batch_stream_iterations(grx_tdt_batch* b);
 
 /* ------------------------------------------- Whisper text decoder ---------
  * The token loop of whisper.Model (whisper/decoder.go:33-140,
