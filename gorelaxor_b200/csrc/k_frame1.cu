@@ -32,6 +32,13 @@
 #include "common.cuh"
 #include "kernels.h"
 
+// Phase marks for timing studies: a build may define F1_MARK(kind) to record
+// them (kind: 1 barrier passed, 2 prologue done, 3 weights ready, 4 phase
+// done, 6 barrier reached); the library defines it empty.
+#ifndef F1_MARK
+#define F1_MARK(kind)
+#endif
+
 namespace grx {
 
 namespace {
@@ -146,6 +153,7 @@ struct Ctl {
 // the launch); the k-th barrier waits for k·G arrivals. Bounded.
 __device__ bool grid_sync(const Frame1Args& A, Ctl& ctl) {
   __syncthreads();
+  F1_MARK(6);
   if (threadIdx.x == 0) {
     ctl.bar_k += 1;
     const unsigned target = ctl.stall ? 0xffffffffu : ctl.bar_k * gridDim.x;
@@ -171,6 +179,7 @@ __device__ bool grid_sync(const Frame1Args& A, Ctl& ctl) {
     asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
   }
   __syncthreads();
+  F1_MARK(1);
   return !ctl.fail;
 }
 
@@ -267,12 +276,14 @@ __device__ bool wait_task(const Frame1Args& A, const Smem& S, int g) {
   if (S.ctl->fail) return false;
   // every thread observes the completed phase itself (acquiring the copies)
   mbar_try(smem_addr(S.mbar + g % F1_SLOTS), uint32_t(g / F1_SLOTS) & 1u);
+  F1_MARK(3);
   return true;
 }
 
 // Frees task g's slot and starts the copies of task g + F1_SLOTS into it.
 __device__ void release_task(const Frame1Args& A, const Smem& S, int g, int ntasks) {
   __syncthreads();  // every thread is done reading the slot
+  F1_MARK(4);
   if (threadIdx.x == 0 && g + F1_SLOTS < ntasks) {
     issue_task(A, S, g + F1_SLOTS);
     S.ctl->issued = g + F1_SLOTS + 1;
@@ -686,6 +697,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
       if (!grid_sync(A, *S.ctl)) goto out;
       layer_norm(A.x, A.d, ly.n1w, ly.n1b, 1e-5, nullptr, nullptr, S.vf, S.red);
       quant_smem(S.vf, A.d, S.xq, S.xs);
+      F1_MARK(2);
       if (!wait_task(A, S, g)) goto out;
       phase_qkv(A, S, S.slot[g % F1_SLOTS], l, pos);
       release_task(A, S, g, ntasks);
@@ -693,6 +705,8 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
       // ---- attention ----
       if (!grid_sync(A, *S.ctl)) goto out;
       phase_attn(A, S, l, pos);
+      __syncthreads();
+      F1_MARK(4);
       // ---- out (+ residual) ----
       if (!grid_sync(A, *S.ctl)) goto out;
       for (int i = tid; i < A.d; i += NT) S.vf[i] = __ldcg(A.att + i);
