@@ -157,6 +157,7 @@ struct Ctl {
   unsigned bar_k;  // grid barriers passed
   int issued;      // tasks issued (their copies started)
   int stall;       // the watchdog check: no barrier completes
+  int pending;     // a task to issue once this CTA has arrived at the next barrier (−1: none)
   int ntab;        // regions in the task table
   uint16_t tstart[kMaxTasks + 1], tcount[kMaxTasks + 1];  // per task (index i + 1)
 };
@@ -165,13 +166,15 @@ struct Ctl {
 // the launch); the k-th barrier waits for k·G arrivals. The arrival is a
 // release (the CTA's writes, ordered before it by the block barrier, become
 // visible with it) and the polling load an acquire. Bounded.
-__device__ bool grid_sync(const Frame1Args& A, Ctl& ctl) {
+template <class Arrived>
+__device__ bool grid_sync(const Frame1Args& A, Ctl& ctl, Arrived arrived) {
   __syncthreads();
   F1_MARK(6);
   if (threadIdx.x == 0) {
     ctl.bar_k += 1;
     const unsigned target = ctl.stall ? 0xffffffffu : ctl.bar_k * gridDim.x;
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;\n" ::"l"(A.bar) : "memory");
+    arrived();  // work that overlaps the wait
     const unsigned long long t0 = gtime();
     for (int it = 0;; it++) {
       unsigned v;
@@ -287,14 +290,27 @@ __device__ bool wait_task(const Frame1Args& A, const Smem& S, int g) {
   return true;
 }
 
-// Frees task g's slot and starts the copies of task g + F1_SLOTS into it.
+// Frees task g's slot; the copies of task g + F1_SLOTS into it start once
+// this CTA has arrived at the next grid barrier (sync below), so that they
+// overlap the wait instead of delaying the arrival.
 __device__ void release_task(const Smem& S, int W, int g, int ntasks) {
   __syncthreads();  // every thread is done reading the slot
   F1_MARK(4);
-  if (threadIdx.x == 0 && g + F1_SLOTS < ntasks) {
-    issue_task(S, W, g + F1_SLOTS);
-    S.ctl->issued = g + F1_SLOTS + 1;
+  if (threadIdx.x == 0 && g + F1_SLOTS < ntasks) S.ctl->pending = g + F1_SLOTS;
+}
+
+__device__ void issue_pending(const Smem& S, int W) {
+  Ctl& ctl = *S.ctl;
+  if (ctl.pending >= 0) {
+    issue_task(S, W, ctl.pending);
+    ctl.issued = ctl.pending + 1;
+    ctl.pending = -1;
   }
+}
+
+// The grid barrier with the pending copies issued after this CTA's arrival.
+__device__ __forceinline__ bool sync(const Frame1Args& A, const Smem& S, int W) {
+  return grid_sync(A, *S.ctl, [&] { issue_pending(S, W); });
 }
 
 // Before leaving: every copy issued into this CTA's shared memory has landed
@@ -707,6 +723,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
     ctl.fail = 0;
     ctl.bar_k = 0;
     ctl.stall = stall;
+    ctl.pending = -1;
     int n = 0;
     for (int i = -1; i < W; i++) {  // this CTA's copies of every task, once per launch
       ctl.tstart[i + 1] = uint16_t(n);
@@ -738,7 +755,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
     for (int l = 0; l < A.L; l++) {
       const F1Layer& ly = A.layers[l];
       // ---- qkv (LayerNorm 1 → Q8_0 in every CTA) ----
-      if (!grid_sync(A, *S.ctl)) goto out;
+      if (!sync(A, S, W)) goto out;
       layer_norm(A.x, A.d, ly.n1w, ly.n1b, 1e-5, nullptr, nullptr, S.vf, S.xq, S.xs, S.red);
       F1_MARK(2);
       if (!wait_task(A, S, g)) goto out;
@@ -746,12 +763,12 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
       release_task(S, W, g, ntasks);
       g++;
       // ---- attention ----
-      if (!grid_sync(A, *S.ctl)) goto out;
+      if (!sync(A, S, W)) goto out;
       phase_attn(A, S, l, pos);
       __syncthreads();
       F1_MARK(4);
       // ---- out (+ residual) ----
-      if (!grid_sync(A, *S.ctl)) goto out;
+      if (!sync(A, S, W)) goto out;
       quant_global(A.att, A.d, S.xq, S.xs);
       if (!wait_task(A, S, g)) goto out;
       {
@@ -765,7 +782,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
       release_task(S, W, g, ntasks);
       g++;
       // ---- ff1 (LayerNorm 2 → Q8_0; GELU and the rounding of whole blocks here) ----
-      if (!grid_sync(A, *S.ctl)) goto out;
+      if (!sync(A, S, W)) goto out;
       layer_norm(A.x, A.d, ly.n2w, ly.n2b, 1e-5, nullptr, nullptr, S.vf, S.xq, S.xs, S.red);
       if (!wait_task(A, S, g)) goto out;
       {
@@ -784,7 +801,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
       release_task(S, W, g, ntasks);
       g++;
       // ---- ff2 (+ residual) ----
-      if (!grid_sync(A, *S.ctl)) goto out;
+      if (!sync(A, S, W)) goto out;
       for (int i = tid; i < A.ff / 16; i += NT)
         reinterpret_cast<int4*>(S.xq)[i] = __ldcg(reinterpret_cast<const int4*>(A.ffq) + i);
       for (int i = tid; i < A.ff / QK; i += NT) S.xs[i] = __ldcg(A.ffs + i);
@@ -802,7 +819,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
       g++;
     }
     // ---- out_norm → lm_out, EOS; cond (→ SiLU) and the flow input h ----
-    if (!grid_sync(A, *S.ctl)) goto out;
+    if (!sync(A, S, W)) goto out;
     layer_norm(A.x, A.d, A.outw, A.outb, 1e-5, nullptr, nullptr, S.vf, nullptr, nullptr, S.red);
     if (c == last) {
       for (int i = tid; i < A.d; i += NT) A.lm_out[i] = S.vf[i];
@@ -845,7 +862,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
     release_task(S, W, g, ntasks);
     g++;
     // ---- the adaLN projections of SiLU(y) ----
-    if (!grid_sync(A, *S.ctl)) goto out;
+    if (!sync(A, S, W)) goto out;
     for (int i = tid; i < A.fd; i += NT) S.vf[i] = __ldcg(A.sy + i);
     __syncthreads();
     if (!wait_task(A, S, g)) goto out;
@@ -867,7 +884,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
     for (int k = 0; k < A.depth; k++) {
       const F1Res& rb = A.res[k];
       const float* mod = A.mod + (size_t)k * 3 * A.fd;
-      if (!grid_sync(A, *S.ctl)) goto out;
+      if (!sync(A, S, W)) goto out;
       layer_norm(A.h, A.fd, rb.nw, rb.nb, 1e-6, mod, mod + A.fd, S.vf, nullptr, nullptr, S.red);
       if (!wait_task(A, S, g)) goto out;
       {
@@ -877,7 +894,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
       }
       release_task(S, W, g, ntasks);
       g++;
-      if (!grid_sync(A, *S.ctl)) goto out;
+      if (!sync(A, S, W)) goto out;
       for (int i = tid; i < A.fd; i += NT) S.vf[i] = __ldcg(A.mm + i);
       __syncthreads();
       if (!wait_task(A, S, g)) goto out;
@@ -894,7 +911,7 @@ __global__ void __launch_bounds__(NT, 1) k_frame1(const Frame1Args* __restrict__
       g++;
     }
     // ---- the final adaLN, the latent (every CTA), the next input rows ----
-    if (!grid_sync(A, *S.ctl)) goto out;
+    if (!sync(A, S, W)) goto out;
     layer_norm(A.h, A.fd, nullptr, nullptr, 1e-6, A.mod2, A.mod2 + A.fd, S.vf, nullptr, nullptr, S.red);
     {
       const int gi = tid >> 3;
