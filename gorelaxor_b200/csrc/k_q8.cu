@@ -220,6 +220,24 @@ __device__ __forceinline__ void q8_fold(f2& acc01, f2& acc23, f2 p01, f2 p23, f2
   acc23 = f2fma(f2fma(p23, dw, nm), da1, acc23);
 }
 
+// One finished output pair (row, col..col+1), every epilogue but the Q8_0
+// rounding: the RoPE'd K/V append, the residual add (with the layer scale),
+// or a plain store.
+__device__ __forceinline__ void epi_pair(const EpiArgs& e, int row, int col, float c0v, float c1v) {
+  if (e.epi == EPI_ROPE_KV) {
+    store_qkv_pair(e.kv, row, col, c0v, c1v);
+    return;
+  }
+  float2* yp = reinterpret_cast<float2*>(e.y + (size_t)row * e.ldy + col);
+  if (e.epi == EPI_RESID) {
+    const float2 o = *yp;
+    const float a0 = e.ls ? __fmul_rn(e.ls[col], c0v) : c0v, a1 = e.ls ? __fmul_rn(e.ls[col + 1], c1v) : c1v;
+    *yp = make_float2(__fadd_rn(o.x, a0), __fadd_rn(o.y, a1));
+  } else {
+    *yp = make_float2(c0v, c1v);
+  }
+}
+
 // The epilogue of both GEMM kernels: each thread's accumulators (rows g and
 // g+8 of its m-tiles, column pairs of its n-tiles) go where e says.
 template <int TM, int TN, int NWARPS>
@@ -260,20 +278,7 @@ __device__ __forceinline__ void gemm_epilogue(f2 (&acc)[TM][TN][2], const EpiArg
 #pragma unroll
       for (int h = 0; h < 2; h++) {
         const int row = m0 + arow + i * 16 + g + h * 8, col = n0 + brow + j * 8 + 2 * t4;
-        if (row >= M || col >= N) continue;
-        const float c0v = f2lo(acc[i][j][h]), c1v = f2hi(acc[i][j][h]);
-        if (e.epi == EPI_ROPE_KV) {
-          store_qkv_pair(e.kv, row, col, c0v, c1v);
-          continue;
-        }
-        float2* yp = reinterpret_cast<float2*>(e.y + (size_t)row * e.ldy + col);
-        if (e.epi == EPI_RESID) {
-          const float2 o = *yp;
-          const float a0 = e.ls ? __fmul_rn(e.ls[col], c0v) : c0v, a1 = e.ls ? __fmul_rn(e.ls[col + 1], c1v) : c1v;
-          *yp = make_float2(__fadd_rn(o.x, a0), __fadd_rn(o.y, a1));
-        } else {
-          *yp = make_float2(c0v, c1v);
-        }
+        if (row < M && col < N) epi_pair(e, row, col, f2lo(acc[i][j][h]), f2hi(acc[i][j][h]));
       }
 }
 
@@ -295,7 +300,7 @@ struct Cfg2 {
                        PD = (CD + NT - 1) / NT;
 };
 
-template <int TM, int TN, int WGM, int WGN, int STAGES>
+template <int TM, int TN, int WGM, int WGN, int STAGES, int PB = 1>
 __global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __restrict__ a,
                                                             const float2* __restrict__ as, int M,
                                                             const int8_t* __restrict__ wq,
@@ -420,29 +425,42 @@ __global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __res
     ws = ws + 1 == STAGES ? 0 : ws + 1;
     const uint32_t cur = sbase + rs * C::SST;
     rs = rs + 1 == STAGES ? 0 : rs + 1;
+    // PB blocks at a time: their MMAs are all issued before the first of
+    // their results is folded, so the MMA latencies overlap; the folds then
+    // run in block order, which is all the chain needs.
 #pragma unroll
-    for (int kk = 0; kk < 4; kk++) {
-      if (kt * 4 + kk >= nb) break;
-      const uint32_t kl = uint32_t(2 * kk) << 4;  // the block's first chunk (the swizzle keeps bit 0)
-      uint32_t af[TM][4], bf[TN][2];
+    for (int k0 = 0; k0 < 4; k0 += PB) {
+      if (kt * 4 + k0 >= nb) break;
+      f2 p[PB][TM][TN][2];
 #pragma unroll
-      for (int i = 0; i < TM; i++) ldsm_x4(af[i][0], af[i][1], af[i][2], af[i][3], (cur + aoff[i]) ^ kl);
+      for (int kb = 0; kb < PB; kb++) {
+        const int kk = k0 + kb;
+        if (kt * 4 + kk >= nb) break;
+        const uint32_t kl = uint32_t(2 * kk) << 4;  // the block's first chunk (the swizzle keeps bit 0)
+        uint32_t af[TM][4], bf[TN][2];
 #pragma unroll
-      for (int j = 0; j < TN / 2; j++)
-        ldsm_x4(bf[2 * j][0], bf[2 * j][1], bf[2 * j + 1][0], bf[2 * j + 1][1], (cur + boff[j]) ^ kl);
-      f2 p[TM][TN][2];
+        for (int i = 0; i < TM; i++) ldsm_x4(af[i][0], af[i][1], af[i][2], af[i][3], (cur + aoff[i]) ^ kl);
 #pragma unroll
-      for (int i = 0; i < TM; i++)
+        for (int j = 0; j < TN / 2; j++)
+          ldsm_x4(bf[2 * j][0], bf[2 * j][1], bf[2 * j + 1][0], bf[2 * j + 1][1], (cur + boff[j]) ^ kl);
 #pragma unroll
-        for (int j = 0; j < TN; j++) q8_mma(p[i][j][0], p[i][j][1], af[i], bf[j][0], bf[j][1]);
+        for (int i = 0; i < TM; i++)
 #pragma unroll
-      for (int j = 0; j < TN; j++) {
-        f2 dw, nm;
-        asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];\n" : "=l"(dw), "=l"(nm) : "r"(cur + doff[j] + kk * (BN / 2) * 16));
+          for (int j = 0; j < TN; j++) q8_mma(p[kb][i][j][0], p[kb][i][j][1], af[i], bf[j][0], bf[j][1]);
+      }
 #pragma unroll
-        for (int i = 0; i < TM; i++) {
-          const uint32_t sa = cur + soff[i] + kk * 8;
-          q8_fold(acc[i][j][0], acc[i][j][1], p[i][j][0], p[i][j][1], dw, nm, lds64(sa), lds64(sa + 8 * 32));
+      for (int kb = 0; kb < PB; kb++) {
+        const int kk = k0 + kb;
+        if (kt * 4 + kk >= nb) break;
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+          f2 dw, nm;
+          asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];\n" : "=l"(dw), "=l"(nm) : "r"(cur + doff[j] + kk * (BN / 2) * 16));
+#pragma unroll
+          for (int i = 0; i < TM; i++) {
+            const uint32_t sa = cur + soff[i] + kk * 8;
+            q8_fold(acc[i][j][0], acc[i][j][1], p[kb][i][j][0], p[kb][i][j][1], dw, nm, lds64(sa), lds64(sa + 8 * 32));
+          }
         }
       }
     }
@@ -451,7 +469,7 @@ __global__ void __launch_bounds__(32 * WGM * WGN) k_q8_gemm2(const int8_t* __res
   gemm_epilogue<TM, TN, WGM * WGN>(acc, e, smem_raw, m0, n0, arow, brow, g, t4, warp, lane, M, N, BM, BN);
 }
 
-template <int TM, int TN, int WGM, int WGN, int STAGES>
+template <int TM, int TN, int WGM, int WGN, int STAGES, int PB = 1>
 struct Gemm2 {
   using C = Cfg2<TM, TN, WGM, WGN>;
   static constexpr size_t smem() {
@@ -459,12 +477,12 @@ struct Gemm2 {
     return s > t ? s : t;
   }
   static void init() {
-    cudaFuncSetAttribute(k_q8_gemm2<TM, TN, WGM, WGN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_q8_gemm2<TM, TN, WGM, WGN, STAGES, PB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          int(smem()));
   }
   static void launch(const int8_t* a, const float2* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st) {
     dim3 grid((w.rows + C::BN - 1) / C::BN, (M + C::BM - 1) / C::BM);
-    k_q8_gemm2<TM, TN, WGM, WGN, STAGES><<<grid, C::NT, smem(), st>>>(a, as, M, w.q, w.dwnm, w.rows, w.cols, e);
+    k_q8_gemm2<TM, TN, WGM, WGN, STAGES, PB><<<grid, C::NT, smem(), st>>>(a, as, M, w.q, w.dwnm, w.rows, w.cols, e);
   }
 };
 
@@ -812,232 +830,6 @@ __global__ void __launch_bounds__(TcCfg<BN, EPW>::NT, 1)
   }
 }
 
-// ------------------------- GEMM on the 5th-gen tensor core, weight rows as M --
-//
-// k_q8_tcw: the same per-block chain with the operands swapped: the weight
-// rows are the MMA's M (128 per CTA) and BS activation rows (streams) its N,
-// so one tcgen05.mma.kind::i8 per Q8_0 block leaves the 128 × BS int32 block
-// dots in TMEM, lane = weight row. Each epilogue thread owns one weight row
-// (its TMEM lane): its dw and −1.5·2^23·dw are per-thread scalars, and only
-// the streams' activation scales differ across its columns (the epilogue
-// warps transpose a stage's scales once, so a pair of them is one 8-byte
-// read). Roles as k_q8_tc: warp 0 loads a 4-block stage by TMA (no
-// multicast), warp 1 issues one MMA per block into TMEM tiles holding the
-// magic bits and commits once per stage, EPW epilogue warps (two per TMEM
-// lane quarter with EPW = 8) fold each block into the chain with packed FMAs
-// and restore the magic bits. Every wait is bounded as in k_q8_tc.
-template <int BS, int EPW>
-struct TcwCfg {
-  static constexpr int NT = 64 + 32 * EPW;
-  static constexpr int CW = BS / (EPW / 4);  // streams per epilogue thread
-  static_assert(EPW % 4 == 0 && CW % 8 == 0, "epilogue warps cover the lane quarters; x8 TMEM loads");
-  static constexpr int TMEM_COLS = TC_GROUPS * TC_KB * BS;
-  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "allocation size");
-  static constexpr int W_BYTES = 128 * 128, A_BYTES = BS * 128, S_BYTES = BS * TC_KB * 8, D_BYTES = TC_KB * 64 * 16;
-  static constexpr int OFF_A = W_BYTES, OFF_S = OFF_A + A_BYTES, OFF_D = OFF_S + S_BYTES;
-  static constexpr int STAGE = (OFF_D + D_BYTES + 1023) / 1024 * 1024;
-  static constexpr int TX = W_BYTES + A_BYTES + S_BYTES + D_BYTES;
-  static constexpr int OFF_T = STAGE * TC_STAGES;  // per epilogue warp [block][CW] activation scales, transposed
-  static constexpr int OFF_BAR = OFF_T + EPW * TC_KB * CW * 4;
-  static constexpr int NBAR = 2 * TC_STAGES + 2 * TC_GROUPS + 1;
-  static constexpr int SMEM = 1024 + OFF_BAR + NBAR * 8 + 16;
-  static_assert((228 * 1024 / SMEM) * TMEM_COLS <= 512, "co-resident blocks must fit in TMEM");
-};
-
-__device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t* d) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
-               : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7])
-               : "r"(taddr)
-               : "memory");
-}
-__device__ __forceinline__ void tc_st8(uint32_t taddr, uint32_t v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};\n" ::"r"(taddr), "r"(v)
-               : "memory");
-}
-
-template <int BS, int EPW>
-__global__ void __launch_bounds__(TcwCfg<BS, EPW>::NT, 1)
-    k_q8_tcw(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap ma,
-             const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap md, int M, int N, int nb,
-             EpiArgs e) {
-  using C = TcwCfg<BS, EPW>;
-  constexpr int S = TC_STAGES, G = TC_GROUPS, CW = C::CW;
-  extern __shared__ uint8_t tcw_raw[];
-  const uint32_t raw = smem_u32(tcw_raw), base = (raw + 1023) & ~1023u;
-  uint8_t* gbase = tcw_raw + (base - raw);
-  const uint32_t bars = base + C::OFF_BAR;
-  auto full = [&](int s) { return bars + 8 * s; };
-  auto empty = [&](int s) { return bars + 8 * (S + s); };
-  auto tfull = [&](int g) { return bars + 8 * (2 * S + g); };
-  auto tempty = [&](int g) { return bars + 8 * (2 * S + G + g); };
-  const uint32_t done = bars + 8 * (2 * S + 2 * G);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::OFF_BAR + C::NBAR * 8);
-  __shared__ int dead_s;
-  volatile int* dead = &dead_s;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * 128, m0 = blockIdx.y * BS;
-  if (threadIdx.x == 0) {
-    dead_s = 0;
-    for (int s = 0; s < S; s++) {
-      mb_init(full(s), 1);
-      mb_init(empty(s), EPW);
-    }
-    for (int g = 0; g < G; g++) {
-      mb_init(tfull(g), 1);
-      mb_init(tempty(g), EPW);
-    }
-    mb_init(done, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-  }
-  if (warp == 1) {
-    asm volatile(
-        "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n"
-        "tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::"r"(smem_u32(tmem_slot)),
-        "r"(C::TMEM_COLS)
-        : "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const int nst = (nb + TC_KB - 1) / TC_KB;
-  const int q = warp & 3, hcol = (warp - 2) >> 2, c0 = hcol * CW;  // epilogue: lane quarter, first stream
-  if (warp >= 2) {  // every tile starts as the magic bits; the epilogue restores them after each read
-    const uint32_t t0 = tmem + (uint32_t(q * 32) << 16) + uint32_t(c0);
-    for (int b = 0; b < G * TC_KB; b++)
-#pragma unroll
-      for (int c = 0; c < CW / 8; c++) tc_st8(t0 + uint32_t(b * BS + 8 * c), uint32_t(MAGIC_BITS));
-    tc_wait_st();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-
-  if (warp == 0) {
-    int issued = 0;
-    for (int st = 0; st < nst; st++) {
-      const int s = st % S;
-      if (!__all_sync(FULL, mb_wait(empty(s), ((st / S) & 1) ^ 1, dead))) break;
-      const uint32_t sb = base + s * C::STAGE;
-      mb_expect_one(full(s), C::TX);
-      tma2d(sb, &mw, st * 128, n0, full(s));
-      tma2d(sb + C::OFF_A, &ma, st * 128, m0, full(s));
-      tma2d(sb + C::OFF_S, &ms, st * 8, m0, full(s));
-      tma2d(sb + C::OFF_D, &md, n0 * 2, st * TC_KB, full(s));
-      issued = st + 1;
-    }
-    if (*dead)  // let this block's copies land before it exits
-      for (int st = issued > S ? issued - S : 0; st < issued; st++) {
-        const long long t0 = clock64();
-        while (!mb_try(full(st % S), (st / S) & 1) && clock64() - t0 < (1LL << 30)) {
-        }
-      }
-  } else if (warp == 1) {
-    const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BS >> 3) << 17) | (uint32_t(128 >> 4) << 24);
-    for (int st = 0; st < nst; st++) {
-      const int s = st % S, g = st % G, nbl = min(TC_KB, nb - st * TC_KB);
-      if (!__all_sync(FULL, mb_wait(full(s), (st / S) & 1, dead))) break;
-      if (!__all_sync(FULL, mb_wait(tempty(g), ((st / G) & 1) ^ 1, dead))) break;
-      tc_fence_after();
-      const uint32_t sb = base + s * C::STAGE;
-      for (int kk = 0; kk < nbl; kk++)
-        tc_mma_i8(tmem + uint32_t((g * TC_KB + kk) * BS), tc_desc(sb + kk * 32), tc_desc(sb + C::OFF_A + kk * 32),
-                  idesc);
-      tc_commit(tfull(g));
-    }
-    tc_commit(done);  // every MMA issued has completed before the TMEM is released
-    const long long t0 = clock64();
-    while (!mb_try(done, 0) && clock64() - t0 < (1LL << 31)) {
-    }
-  } else {
-    const int nl = q * 32 + lane, n = n0 + nl;  // this thread's weight row
-    const uint32_t trow = tmem + (uint32_t(q * 32) << 16) + uint32_t(c0);
-    const float bv = e.bias && n < N ? e.bias[n] : 0.f;
-    f2 acc[CW / 2];
-#pragma unroll
-    for (int j = 0; j < CW / 2; j++) acc[j] = f2make(bv, bv);
-    float* tt = reinterpret_cast<float*>(gbase + C::OFF_T) + (warp - 2) * TC_KB * CW;
-    for (int st = 0; st < nst; st++) {
-      const int s = st % S, g = st % G, nbl = min(TC_KB, nb - st * TC_KB);
-      if (!__all_sync(FULL, mb_wait(full(s), (st / S) & 1, dead))) break;
-      // this warp's streams' activation scales for the stage as [block][stream]
-      // (the first of each (s, s) pair), in a buffer of its own
-      const float* sg = reinterpret_cast<const float*>(gbase + s * C::STAGE + C::OFF_S);
-      for (int i = lane; i < TC_KB * CW; i += 32) tt[i] = sg[(c0 + i % CW) * (2 * TC_KB) + 2 * (i / CW)];
-      __syncwarp();
-      if (!__all_sync(FULL, mb_wait(tfull(g), (st / G) & 1, dead))) break;
-      tc_fence_after();
-      const float4* dq = reinterpret_cast<const float4*>(gbase + s * C::STAGE + C::OFF_D);
-#pragma unroll
-      for (int kk = 0; kk < TC_KB; kk++) {
-        if (kk >= nbl) break;
-        const uint32_t tb = trow + uint32_t((g * TC_KB + kk) * BS);
-        uint32_t d[CW];
-#pragma unroll
-        for (int c = 0; c < CW / 8; c++) tc_ld8(tb + 8 * c, d + 8 * c);
-        tc_wait_ld();
-#pragma unroll
-        for (int c = 0; c < CW / 8; c++) tc_st8(tb + 8 * c, uint32_t(MAGIC_BITS));
-        const float4 qd = dq[kk * 64 + (nl >> 1)];  // {dw[2p], dw[2p+1], nm[2p], nm[2p+1]}
-        const float dw = (nl & 1) ? qd.y : qd.x, nm = (nl & 1) ? qd.w : qd.z;
-        const f2 dw2 = f2dup(dw), nm2 = f2dup(nm);
-        const f2* da = reinterpret_cast<const f2*>(tt + kk * CW);
-        f2 t[CW / 2];
-#pragma unroll
-        for (int j = 0; j < CW / 2; j++)
-          t[j] = f2fma(f2make(__uint_as_float(d[2 * j]), __uint_as_float(d[2 * j + 1])), dw2, nm2);
-#pragma unroll
-        for (int j = 0; j < CW / 2; j++) acc[j] = f2fma(t[j], da[j], acc[j]);
-      }
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();  // (also: every lane is done with tt before the next stage's scales)
-      if (lane == 0) {
-        mb_arrive(tempty(g));
-        mb_arrive(empty(s));
-      }
-    }
-    if (!*dead) {
-      if (e.epi == EPI_GELU_Q8) {  // the warp's 32 rows are one Q8_0 block of every stream
-#pragma unroll
-        for (int j = 0; j < CW; j++) {
-          const int m = m0 + c0 + j;
-          const float v = gelu_avx(j & 1 ? f2hi(acc[j / 2]) : f2lo(acc[j / 2]));
-          float sc;
-          const int8_t qv = quant_lane(v, &sc);
-          if (m < M && n < N) {
-            e.q8[(size_t)m * N + n] = qv;
-            if (lane == 0) e.q8s[(size_t)m * (N / QK) + n / QK] = make_float2(sc, sc);
-          }
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < CW; j++) {
-          const int m = m0 + c0 + j;
-          const float v = j & 1 ? f2hi(acc[j / 2]) : f2lo(acc[j / 2]);
-          if (e.epi == EPI_ROPE_KV) {
-            const float pv = __shfl_xor_sync(FULL, v, 1);
-            if (!(lane & 1) && m < M && n < N) store_qkv_pair(e.kv, m, n, v, pv);
-            continue;
-          }
-          if (m >= M || n >= N) continue;
-          float* yp = e.y + (size_t)m * e.ldy + n;
-          if (e.epi == EPI_RESID)
-            *yp = __fadd_rn(*yp, e.ls ? __fmul_rn(e.ls[n], v) : v);
-          else
-            *yp = v;
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
-  }
-}
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -1089,34 +881,6 @@ struct GemmTc {
   }
 };
 
-// The weights-as-M tensor-core product: its four tensor maps (weights and
-// activations 128-byte rows in the 128-byte swizzle, the activation scales,
-// the {dw, nm} quads of 128 rows), encoded per launch.
-template <int BS, int EPW>
-struct GemmTcw {
-  using C = TcwCfg<BS, EPW>;
-  static void init() {
-    cudaFuncSetAttribute(k_q8_tcw<BS, EPW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  }
-  static bool launch(const int8_t* a, const float2* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st) {
-    const int N = w.rows, K = w.cols, nb = K / QK, np2 = (N + 1) / 2;
-    if (!g_encode || nb % 2 || (e.epi == EPI_GELU_Q8 && N % 32) ||
-        ((uintptr_t(a) | uintptr_t(as) | uintptr_t(w.q) | uintptr_t(w.dwnm)) & 15))
-      return false;
-    CUtensorMap mw, ma, ms, md;
-    if (!tmap2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q, K, N, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !tmap2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, K, M, K, 128, BS, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !tmap2d(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, as, 2 * nb, M, 8 * nb, 2 * TC_KB, BS,
-                CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !tmap2d(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.dwnm, 4 * np2, nb, 16 * np2, 256, TC_KB,
-                CU_TENSOR_MAP_SWIZZLE_NONE))
-      return false;
-    dim3 grid((N + 127) / 128, (M + BS - 1) / BS);
-    k_q8_tcw<BS, EPW><<<grid, C::NT, C::SMEM, st>>>(mw, ma, ms, md, M, N, nb, e);
-    return true;
-  }
-};
-
 void tc_init_encode() {
   if (g_encode) return;
   void* fn = nullptr;
@@ -1133,17 +897,21 @@ void tc_init_encode() {
 // initialisation.
 bool g_q8_tc = false;
 
-// Tile shapes per product shape, the fastest of those timed at M = 256 on
-// B200, every one bit-identical to the others: 64×32 CTA tiles of four 32×16
-// warps for most (qkv 11.3 µs, attn_out 7.6, ff2 18.5 per product), 64×64
-// of four 32×32 warps for the widest (ff1 12.4).
-using GemmMid = Gemm2<2, 2, 2, 2, 4>;
-using GemmWide = Gemm2<2, 4, 2, 2, 4>;  // N > 3072
-// At M ≤ 128 (one part of a FlowLM set) more, smaller blocks win: 32×32 tiles
-// (qkv 7.78 µs, attn_out 5.53, ff2 17.0), and 64×64 tiles of eight 32×16
-// warps for the widest (ff1 8.09).
-using GemmSmall = Gemm2<1, 2, 2, 2, 4>;
+// Tile shapes per product shape, the fastest of those timed on B200, every
+// one bit-identical to the others. PB = 4: each warp issues the MMAs of four
+// Q8_0 blocks before folding them into its chains in block order, so the
+// tensor-pipe latency of one block overlaps the issue of the next three.
+// At M ≤ 128 (one part of a FlowLM set): 32×32 CTA tiles of four 16×16
+// warps (qkv 7.78 µs, attn_out 5.56, ff2 16.8 per product), and 64×64 tiles
+// of eight 32×16 warps for the widest (ff1 8.2).
+using GemmSmall = Gemm2<1, 2, 2, 2, 4, 4>;
 using GemmSmallWide = Gemm2<2, 2, 2, 4, 4>;  // N > 3072
+// At M > 128: 64×32 tiles of four 32×16 warps for qkv-wide products (qkv
+// 10.6 at M = 256), the 32×32 tiles above where N ≤ 2048 (attn_out 6.5,
+// ff2 19.5: twice the CTAs), 64×64 of four 32×32 warps for the widest
+// (ff1 11.7).
+using GemmMid = Gemm2<2, 2, 2, 2, 4, 4>;
+using GemmWide = Gemm2<2, 4, 2, 2, 4>;  // N > 3072
 
 }  // namespace
 
@@ -1177,8 +945,10 @@ void launch_q8_product(const int8_t* a, const float2* as, int M, const DQ8& w, c
       GemmSmall::launch(a, as, M, w, e, st);
   } else if (N > 3072) {
     GemmWide::launch(a, as, M, w, e, st);
-  } else {
+  } else if (N > 2048) {
     GemmMid::launch(a, as, M, w, e, st);
+  } else {
+    GemmSmall::launch(a, as, M, w, e, st);
   }
 }
 
