@@ -15,7 +15,7 @@
 // Weights stream independently of the barriers: each CTA's slice of every
 // product (its contiguous rows, int8 values and f16 scales, or float32 rows)
 // is a "task", and the CTA keeps F1_SLOTS tasks in flight with bulk async
-// copies (cp.async.bulk, no multicast) into a ring of shared-memory slots,
+// copies (plain cp.async.bulk, this CTA only) into a ring of shared-memory slots,
 // issued as soon as a slot frees up — several steps ahead of the barrier
 // chain. What a step needs beyond its own rows (the LayerNorm of the
 // residual, the rounding of the attention output) every CTA computes from
