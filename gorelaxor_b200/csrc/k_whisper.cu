@@ -12,11 +12,15 @@
 // process/sample; they reach a token only through comparisons, which are
 // checked against a safe margin and, when closer, recomputed in the
 // reference's sequential order.
+#include <algorithm>
 #include <cuda_fp16.h>
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace grx {
 
@@ -177,11 +181,202 @@ __global__ void __launch_bounds__(128) k_wself(WRows r, const float* q, const fl
   }
 }
 
+// ------------------------------------------------- bulk copies to shared --
+// A CTA stages rows it streams into shared memory with cp.async.bulk (this
+// CTA's own shared memory; no cluster-wide forms), completing on one
+// mbarrier. Every wait is bounded by about a second of %globaltimer; a CTA
+// whose copies do not arrive computes from global memory instead and waits
+// again (bounded) before leaving, so its shared memory is never released
+// under a copy in flight.
+constexpr unsigned long long kBulkWaitNs = 1000000000ull;
+
+__device__ __forceinline__ unsigned long long wtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool wbar_try(uint32_t bar) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar)
+      : "memory");
+  return ok != 0;
+}
+// Thread 0: arms the barrier for `bytes` and starts n copies of `each` bytes
+// (16-byte multiples, 16-byte aligned), source i at src + i·src_stride floats.
+__device__ void wbulk_start(uint64_t* mbar, float* dst, const float* src, size_t src_stride, int n, uint32_t each) {
+  const uint32_t bar = uint32_t(__cvta_generic_to_shared(mbar));
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bar) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(uint32_t(n) * each) : "memory");
+  for (int i = 0; i < n; i++)
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            uint32_t(__cvta_generic_to_shared(dst)) + uint32_t(i) * each),
+        "l"(src + i * src_stride), "r"(each), "r"(bar)
+        : "memory");
+}
+// Every thread: true once the copies have landed (thread 0 waits, bounded).
+__device__ bool wbulk_wait(uint64_t* mbar, int* ok) {
+  const uint32_t bar = uint32_t(__cvta_generic_to_shared(mbar));
+  if (threadIdx.x == 0) {
+    const unsigned long long t0 = wtime();
+    bool got = wbar_try(bar);
+    while (!got && wtime() - t0 < kBulkWaitNs) got = wbar_try(bar);
+    *ok = got;
+  }
+  __syncthreads();
+  if (!*ok) return false;
+  wbar_try(bar);  // every thread observes the completed phase itself
+  return true;
+}
+// Before leaving after a wait that gave up: wait once more, bounded.
+__device__ void wbulk_drain(uint64_t* mbar, int ok) {
+  if (threadIdx.x == 0 && !ok) {
+    const uint32_t bar = uint32_t(__cvta_generic_to_shared(mbar));
+    const unsigned long long t0 = wtime();
+    while (!wbar_try(bar) && wtime() - t0 < kBulkWaitNs) {
+    }
+  }
+  __syncthreads();
+}
+
 // ------------------------------------------------------- cross-attention
 // decoder.go:93-119 for (row, head): scores by dot4f32avx over the stream's
 // pre-scaled keys (16 lanes per key: lane l16 chains element 16c + l16,
 // then lanes l and l+8 add, HSUM), softmax, and o[d] = dot4f32avx(p, Vᵀ[d])
-// over ctx&~15 plus dotF32Go of the rest. 256 threads; hd = 64.
+// over ctx&~15 plus dotF32Go of the rest. hd = 64. Every key's score, and
+// every o[d], is a computation of its own; only the softmax's sum runs over
+// all keys. So the work splits two ways without changing a bit: k_wcross
+// does a (row, head) in one CTA; at few rows, k_wcross_sc spreads a head's
+// keys over KS CTAs (scores and a maximum per chunk into scratch) and
+// k_wcross_o spreads its 64 outputs over DS CTAs, each forming the softmax
+// from the stored scores.
+
+// Scores of keys [j0, j1) (j1 ≤ ctx&~3) into sc[j], groups of 16 lanes per
+// key, from kb (or, given, ks = those keys' rows staged in shared memory);
+// with `tail`, also the keys past the last group of four (dotF32Go, from
+// kb). Returns the thread's maximum.
+__device__ float wcross_scores(const float* qh, const float* kb, int j0, int j1, bool tail, int ctx, float* sc,
+                               const float* ks = nullptr) {
+  const int l16 = threadIdx.x & 15, grp = threadIdx.x >> 4, ng = blockDim.x >> 4;
+  float mx = NINF;
+  // UK keys' rows are loaded before the first of them is used (bytes in
+  // flight for the HBM stream); each key's dot is unchanged.
+  constexpr int UK = 8;
+  for (int jb = j0; jb < j1; jb += ng * UK) {
+    float kv[UK][4];
+#pragma unroll
+    for (int u = 0; u < UK; u++) {
+      const int j = jb + ng * u + grp;
+      if (j < j1) {
+        const float* kj = ks ? ks + (size_t)(j - j0) * 64 : kb + (size_t)j * 64;
+#pragma unroll
+        for (int c = 0; c < 4; c++) kv[u][c] = kj[16 * c + l16];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UK; u++) {
+      const int j = jb + ng * u + grp;
+      float a = 0.f;
+      if (j < j1) {
+#pragma unroll
+        for (int c = 0; c < 4; c++) a = __fmaf_rn(qh[16 * c + l16], kv[u][c], a);
+      }
+      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));  // lanes l < 8: acc0_l + acc1_l
+      float x = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
+      float y = __fadd_rn(x, __shfl_down_sync(0xffffffffu, x, 1));
+      const float z = __fadd_rn(y, __shfl_down_sync(0xffffffffu, y, 2));
+      if (l16 == 0 && j < j1) {
+        sc[j] = z;
+        mx = fmaxf(mx, z);
+      }
+    }
+  }
+  if (tail)
+    for (int j = (ctx & ~3) + threadIdx.x; j < ctx; j += blockDim.x) {  // keys past the last group of four: dotF32Go
+      const float* kj = kb + (size_t)j * 64;
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+      for (int i = 0; i < 64; i += 4) {
+        s0 = __fadd_rn(s0, __fmul_rn(qh[i], kj[i]));
+        s1 = __fadd_rn(s1, __fmul_rn(qh[i + 1], kj[i + 1]));
+        s2 = __fadd_rn(s2, __fmul_rn(qh[i + 2], kj[i + 2]));
+        s3 = __fadd_rn(s3, __fmul_rn(qh[i + 3], kj[i + 3]));
+      }
+      sc[j] = __fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3);
+      mx = fmaxf(mx, sc[j]);
+    }
+  return mx;
+}
+
+// Scores to probabilities in place: expSub against mx, then · (1/Σ).
+__device__ void wcross_softmax(float* sc, int ctx, float mx, float* sh) {
+  const float sum = exp_sub(sc, ctx, mx, sh);
+  const float inv = __fdiv_rn(1.f, sum);
+  for (int j = threadIdx.x; j < ctx; j += blockDim.x) sc[j] = __fmul_rn(sc[j], inv);
+  __syncthreads();
+}
+
+// o[d] for d = d0 + grp + ng·i, i < ND (ng groups of 16 lanes): the 16
+// lanes chain over ctx&~15 in steps of 16, then the HSUM and dotF32Go of
+// the rest; p = probabilities in shared memory, V row d at vb + (d − vd0)·ctx.
+template <int ND>
+__device__ void wcross_out(const float* p, const float* vb, int ctx, int d0, float* att, int vd0 = 0) {
+  const int l16 = threadIdx.x & 15, grp = threadIdx.x >> 4, ng = blockDim.x >> 4;
+  const int cf = ctx & ~15;
+  float acc[ND];
+#pragma unroll
+  for (int i = 0; i < ND; i++) acc[i] = 0.f;
+  constexpr int UV = 8;
+  for (int c0 = 0; c0 < cf; c0 += 16 * UV) {
+    float vv[UV][ND];
+#pragma unroll
+    for (int u = 0; u < UV; u++) {
+      const int c = c0 + 16 * u;
+      if (c < cf)
+#pragma unroll
+        for (int i = 0; i < ND; i++) vv[u][i] = vb[(size_t)(d0 - vd0 + grp + ng * i) * ctx + c + l16];
+    }
+#pragma unroll
+    for (int u = 0; u < UV; u++) {
+      const int c = c0 + 16 * u;
+      if (c < cf) {
+        const float pc = p[c + l16];
+#pragma unroll
+        for (int i = 0; i < ND; i++) acc[i] = __fmaf_rn(pc, vv[u][i], acc[i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < ND; i++) {
+    float a = __fadd_rn(acc[i], __shfl_down_sync(0xffffffffu, acc[i], 8));
+    float x = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
+    float y = __fadd_rn(x, __shfl_down_sync(0xffffffffu, x, 1));
+    float z = __fadd_rn(y, __shfl_down_sync(0xffffffffu, y, 2));
+    if (l16 == 0) {
+      const int d = d0 + grp + ng * i;
+      if (cf < ctx) {  // + dotF32Go of the tail (kernels_amd64.go dotF32x4)
+        const float* vd = vb + (size_t)(d - vd0) * ctx;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        int t = cf;
+        for (; t + 4 <= ctx; t += 4) {
+          s0 = __fadd_rn(s0, __fmul_rn(p[t], vd[t]));
+          s1 = __fadd_rn(s1, __fmul_rn(p[t + 1], vd[t + 1]));
+          s2 = __fadd_rn(s2, __fmul_rn(p[t + 2], vd[t + 2]));
+          s3 = __fadd_rn(s3, __fmul_rn(p[t + 3], vd[t + 3]));
+        }
+        for (; t < ctx; t++) s0 = __fadd_rn(s0, __fmul_rn(p[t], vd[t]));
+        z = __fadd_rn(z, __fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3));
+      }
+      att[d] = z;
+    }
+  }
+}
+
+// One CTA per (row, head), 256 threads.
 __global__ void __launch_bounds__(256) k_wcross(WRows r, const float* q, const float* ck, const float* cvt, float* att) {
   extern __shared__ float wsm[];  // [audio_ctx] scores, [64] q
   __shared__ float sh[40];
@@ -193,105 +388,69 @@ __global__ void __launch_bounds__(256) k_wcross(WRows r, const float* q, const f
   __syncthreads();
   const float* kb = ck + ((size_t)s * r.nh + h) * ctx * hd;
   const float* vb = cvt + ((size_t)s * r.nh + h) * hd * ctx;
-  const int lane = threadIdx.x & 31, l16 = threadIdx.x & 15, grp = threadIdx.x >> 4;
-  const int ctx4 = ctx & ~3;
-  float mx = NINF;
-  // UK keys' rows are loaded before the first of them is used (bytes in
-  // flight for the HBM stream); each key's dot is unchanged.
-  constexpr int UK = 8;
-  for (int j0 = 0; j0 < ctx4; j0 += 16 * UK) {
-    float kv[UK][4];
-#pragma unroll
-    for (int u = 0; u < UK; u++) {
-      const int j = j0 + 16 * u + grp;
-      if (j < ctx4) {
-        const float* kj = kb + (size_t)j * hd;
-#pragma unroll
-        for (int c = 0; c < 4; c++) kv[u][c] = kj[16 * c + l16];
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < UK; u++) {
-      const int j = j0 + 16 * u + grp;
-      float a = 0.f;
-      if (j < ctx4) {
-#pragma unroll
-        for (int c = 0; c < 4; c++) a = __fmaf_rn(qh[16 * c + l16], kv[u][c], a);
-      }
-      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));  // lanes l < 8: acc0_l + acc1_l
-      float x = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
-      float y = __fadd_rn(x, __shfl_down_sync(0xffffffffu, x, 1));
-      const float z = __fadd_rn(y, __shfl_down_sync(0xffffffffu, y, 2));
-      if (l16 == 0 && j < ctx4) {
-        sc[j] = z;
-        mx = fmaxf(mx, z);
-      }
-    }
-    (void)lane;
-  }
-  for (int j = ctx4 + threadIdx.x; j < ctx; j += blockDim.x) {  // keys past the last group of four: dotF32Go
-    const float* kj = kb + (size_t)j * hd;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    for (int i = 0; i < hd; i += 4) {
-      s0 = __fadd_rn(s0, __fmul_rn(qh[i], kj[i]));
-      s1 = __fadd_rn(s1, __fmul_rn(qh[i + 1], kj[i + 1]));
-      s2 = __fadd_rn(s2, __fmul_rn(qh[i + 2], kj[i + 2]));
-      s3 = __fadd_rn(s3, __fmul_rn(qh[i + 3], kj[i + 3]));
-    }
-    sc[j] = __fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3);
-    mx = fmaxf(mx, sc[j]);
-  }
+  float mx = wcross_scores(qh, kb, 0, ctx & ~3, true, ctx, sc);
   mx = block_max(mx, sh);
-  const float sum = exp_sub(sc, ctx, mx, sh);
-  const float inv = __fdiv_rn(1.f, sum);
-  for (int j = threadIdx.x; j < ctx; j += blockDim.x) sc[j] = __fmul_rn(sc[j], inv);
+  wcross_softmax(sc, ctx, mx, sh);
+  wcross_out<4>(sc, vb, ctx, 0, att + (size_t)row * st + h * hd);
+}
+
+// Scores of the keys of chunk blockIdx.z (ch keys, a multiple of 16; the
+// last chunk also takes the keys past ctx&~3) into sg[row][h][ctx], the
+// chunk's maximum into mg[row][h][chunk]. The chunk's key rows (contiguous)
+// are staged in shared memory by one bulk copy. 128 threads.
+__global__ void __launch_bounds__(128) k_wcross_sc(WRows r, const float* q, const float* ck, int ch, float* sg,
+                                                   float* mg) {
+  extern __shared__ __align__(128) float ksm[];  // [ch][64]
+  __shared__ float qh[64];
+  __shared__ float sh[40];
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int ok;
+  const int row = blockIdx.x, h = blockIdx.y, kc = blockIdx.z, nks = gridDim.z, hd = 64, ctx = r.audio_ctx;
+  const int s = r.row_stream[row], ctx4 = ctx & ~3;
+  const float* kb = ck + ((size_t)s * r.nh + h) * ctx * hd;
+  const int j0 = kc * ch, j1 = min(ctx4, j0 + ch);
+  if (threadIdx.x == 0) wbulk_start(&mbar, ksm, kb + (size_t)j0 * hd, 0, 1, uint32_t(j1 - j0) * hd * 4);
+  if (threadIdx.x < hd) qh[threadIdx.x] = q[(size_t)row * r.st + h * hd + threadIdx.x];
+  const bool staged = wbulk_wait(&mbar, &ok);
+  const size_t rh = (size_t)row * r.nh + h;
+  float mx = wcross_scores(qh, kb, j0, j1, kc == nks - 1, ctx, sg + rh * ctx, staged ? ksm : nullptr);
+  mx = block_max(mx, sh);
+  if (threadIdx.x == 0) mg[rh * nks + kc] = mx;
+  wbulk_drain(&mbar, ok);
+}
+
+// The softmax of (row, head) from the stored scores and maxima, then the
+// DW outputs of slice blockIdx.z: 16 lanes per output, 16·DW threads. With
+// STAGE the slice's V rows (DW rows of ctx floats) are staged in shared
+// memory by bulk copies started first, so they land while the softmax is
+// formed; without, they stream from global memory.
+template <int DW, bool STAGE>
+__global__ void __launch_bounds__(16 * DW) k_wcross_o(WRows r, const float* cvt, int nks, const float* sg,
+                                                     const float* mg, float* att) {
+  extern __shared__ __align__(128) float wsm[];  // [ctx] probabilities (16-byte padded), [DW][ctx] V rows
+  __shared__ float sh[40];
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int ok;
+  const int row = blockIdx.x, h = blockIdx.y, hd = 64, ctx = r.audio_ctx, d0 = blockIdx.z * DW;
+  const int s = r.row_stream[row];
+  const float* vb = cvt + ((size_t)s * r.nh + h) * hd * ctx;
+  float* vsm = wsm + ((ctx + 3) & ~3);
+  if (STAGE && threadIdx.x == 0) wbulk_start(&mbar, vsm, vb + (size_t)d0 * ctx, ctx, DW, uint32_t(ctx) * 4);
+  const size_t rh = (size_t)row * r.nh + h;
+  float mx = NINF;
+  for (int i = 0; i < nks; i++) mx = fmaxf(mx, mg[rh * nks + i]);
+  for (int j = threadIdx.x; j < ctx; j += blockDim.x) wsm[j] = sg[rh * ctx + j];
   __syncthreads();
-  // o[d] for d = grp + 16i: the 16 lanes chain over ctx&~15 in steps of 16
-  const int cf = ctx & ~15;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  constexpr int UV = 8;
-  for (int c0 = 0; c0 < cf; c0 += 16 * UV) {
-    float vv[UV][4];
-#pragma unroll
-    for (int u = 0; u < UV; u++) {
-      const int c = c0 + 16 * u;
-      if (c < cf)
-#pragma unroll
-        for (int i = 0; i < 4; i++) vv[u][i] = vb[(size_t)(grp + 16 * i) * ctx + c + l16];
-    }
-#pragma unroll
-    for (int u = 0; u < UV; u++) {
-      const int c = c0 + 16 * u;
-      if (c < cf) {
-        const float p = sc[c + l16];
-#pragma unroll
-        for (int i = 0; i < 4; i++) acc[i] = __fmaf_rn(p, vv[u][i], acc[i]);
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    float a = __fadd_rn(acc[i], __shfl_down_sync(0xffffffffu, acc[i], 8));
-    float x = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
-    float y = __fadd_rn(x, __shfl_down_sync(0xffffffffu, x, 1));
-    float z = __fadd_rn(y, __shfl_down_sync(0xffffffffu, y, 2));
-    if (l16 == 0) {
-      const int d = grp + 16 * i;
-      if (cf < ctx) {  // + dotF32Go of the tail (kernels_amd64.go dotF32x4)
-        const float* vd = vb + (size_t)d * ctx;
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-        int t = cf;
-        for (; t + 4 <= ctx; t += 4) {
-          s0 = __fadd_rn(s0, __fmul_rn(sc[t], vd[t]));
-          s1 = __fadd_rn(s1, __fmul_rn(sc[t + 1], vd[t + 1]));
-          s2 = __fadd_rn(s2, __fmul_rn(sc[t + 2], vd[t + 2]));
-          s3 = __fadd_rn(s3, __fmul_rn(sc[t + 3], vd[t + 3]));
-        }
-        for (; t < ctx; t++) s0 = __fadd_rn(s0, __fmul_rn(sc[t], vd[t]));
-        z = __fadd_rn(z, __fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3));
-      }
-      att[(size_t)row * st + h * hd + d] = z;
-    }
+  wcross_softmax(wsm, ctx, mx, sh);
+  float* out = att + (size_t)row * r.st + h * hd;
+  if constexpr (STAGE) {
+    if (wbulk_wait(&mbar, &ok))
+      wcross_out<1>(wsm, vsm, ctx, d0, out, d0);
+    else
+      wcross_out<1>(wsm, vb, ctx, d0, out);
+    wbulk_drain(&mbar, ok);
+  } else {
+    wcross_out<1>(wsm, vb, ctx, d0, out);
   }
 }
 
@@ -743,34 +902,91 @@ __device__ VI block_vi_max(VI x, VI* sh) {
 // One pass takes e_i = expf(lg_i − max) for the whole row into scratch;
 // without the timestamp rule's masking softmaxInf's terms are those same
 // e_i (and so is its sum), so only the timestamps are taken again.
-__global__ void __launch_bounds__(1024) k_wproc(WRows r, float* logits, float* scratch, WVocabDev v, WSample* state,
+// Reductions of a row spread over a cluster of CL CTAs: each CTA's block
+// result goes to its own slot, and after the cluster barrier every thread
+// combines the CL slots in rank order (so every CTA holds the same value).
+template <int CL>
+__device__ float cl_max(float v, float* sh, float* slot) {
+  v = block_max(v, sh);
+  if constexpr (CL == 1) {
+    return v;
+  } else {
+    cg::cluster_group c = cg::this_cluster();
+    if (threadIdx.x == 0) *slot = v;
+    c.sync();
+    float r = NINF;
+    for (int k = 0; k < CL; k++) r = fmaxf(r, *c.map_shared_rank(slot, k));
+    return r;
+  }
+}
+template <int CL>
+__device__ float cl_sum(float v, float* sh, float* slot) {
+  v = block_sum(v, sh);
+  if constexpr (CL == 1) {
+    return v;
+  } else {
+    cg::cluster_group c = cg::this_cluster();
+    if (threadIdx.x == 0) *slot = v;
+    c.sync();
+    float r = 0.f;
+    for (int k = 0; k < CL; k++) r = __fadd_rn(r, *c.map_shared_rank(slot, k));
+    return r;
+  }
+}
+template <int CL>
+__device__ VI cl_vi_max(VI v, VI* sh, VI* slot) {
+  v = block_vi_max(v, sh);
+  if constexpr (CL == 1) {
+    return v;
+  } else {
+    cg::cluster_group c = cg::this_cluster();
+    if (threadIdx.x == 0) *slot = v;
+    c.sync();
+    VI r = *c.map_shared_rank(slot, 0);
+    for (int k = 1; k < CL; k++) r = vi_max(r, *c.map_shared_rank(slot, k));
+    return r;
+  }
+}
+
+// Rows spread over clusters of CL CTAs (CL = 1: one CTA per row); CTA k of a
+// row's cluster takes vocabulary entries [n·k/CL, n·(k+1)/CL), applies the
+// rules that fall there and keeps its e_i; the sums combine partials in a
+// fixed order, which the margins above make safe.
+template <int CL>
+__global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float* scratch, WVocabDev v, WSample* state,
                                                 int* out, const int* step, int* next_tok) {
   __shared__ float shf[40];
   __shared__ VI shv[32];
+  __shared__ float clf[8];
+  __shared__ VI clv[2];
   __shared__ int amb;
-  const int row = blockIdx.x, s = r.row_stream[row], n = v.n, beg = v.beg;
+  const int row = blockIdx.x / CL, rank = blockIdx.x % CL, s = r.row_stream[row], n = v.n, beg = v.beg;
+  const int a0 = int((long long)n * rank / CL), a1 = int((long long)n * (rank + 1) / CL);
   float* lg = logits + (size_t)row * n;
   float* e = scratch + (size_t)row * n;
   const WSample q = state[s];
   const bool initial = q.nt == 0;
+  auto setinf = [&](int i) {
+    if (i >= a0 && i < a1) lg[i] = NINF;
+  };
   // ---- the rules
   if (threadIdx.x == 0) {
     amb = 0;
     if (initial) {
-      lg[v.eot] = NINF;
-      if (v.space >= 0) lg[v.space] = NINF;
+      setinf(v.eot);
+      if (v.space >= 0) setinf(v.space);
     }
-    lg[v.not_] = NINF;
-    lg[v.sot] = lg[v.nosp] = lg[v.solm] = NINF;
-    lg[v.translate] = lg[v.transcribe] = lg[v.prev] = NINF;
+    setinf(v.not_);
+    setinf(v.sot), setinf(v.nosp), setinf(v.solm);
+    setinf(v.translate), setinf(v.transcribe), setinf(v.prev);
   }
-  for (int i = threadIdx.x; i < v.n_lang; i += blockDim.x) lg[v.sot + 1 + i] = NINF;
-  for (int i = threadIdx.x; i < v.n_suppress; i += blockDim.x) lg[v.suppress[i]] = NINF;
+  for (int i = threadIdx.x; i < v.n_lang; i += blockDim.x) setinf(v.sot + 1 + i);
+  for (int i = threadIdx.x; i < v.n_suppress; i += blockDim.x) setinf(v.suppress[i]);
   __syncthreads();
   const bool last = q.nt > 0 && q.last >= beg, penult = q.nt < 2 || q.penult >= beg;
   const int tid0 = int(round(1.0 / (30.0 / double(v.audio_ctx))));
   float mx = NINF, mts = NINF, mtx = NINF;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = a0 + threadIdx.x; i < a1; i += blockDim.x) {
     bool m = false;
     if (last) m = penult ? i >= beg : i < v.eot;
     if (initial && i >= beg + tid0 + 1) m = true;
@@ -781,27 +997,27 @@ __global__ void __launch_bounds__(1024) k_wproc(WRows r, float* logits, float* s
     if (i >= beg) mts = fmaxf(mts, x);
     else mtx = fmaxf(mtx, x);
   }
-  mx = block_max(mx, shf);
-  mts = block_max(mts, shf);
-  mtx = block_max(mtx, shf);
+  mx = cl_max<CL>(mx, shf, &clf[0]);
+  mts = cl_max<CL>(mts, shf, &clf[1]);
+  mtx = cl_max<CL>(mtx, shf, &clf[2]);
   // ---- logSoftmax's sum, with e_i kept
   float s1 = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = a0 + threadIdx.x; i < a1; i += blockDim.x) {
     const float x = lg[i];
     const float ei = x > NINF ? expf_go(__fsub_rn(x, mx)) : 0.f;
     e[i] = ei;
     s1 = __fadd_rn(s1, ei);
   }
-  s1 = block_sum(s1, shf);
+  s1 = cl_sum<CL>(s1, shf, &clf[3]);
   const float ls = __fadd_rn(float(log(double(s1))), mx);
   // ---- the timestamp rule
   const float ts_max = mts > NINF ? __fsub_rn(mts, ls) : NINF;  // the largest of logprobs[beg:]
   bool mask_text = false;
   if (ts_max > NINF) {
     float sum = 0.f;
-    for (int i = beg + threadIdx.x; i < n; i += blockDim.x)
+    for (int i = max(beg, a0) + threadIdx.x; i < a1; i += blockDim.x)
       if (lg[i] > NINF) sum = __fadd_rn(sum, expf_go(__fsub_rn(__fsub_rn(lg[i], ls), ts_max)));
-    sum = block_sum(sum, shf);
+    sum = cl_sum<CL>(sum, shf, &clf[4]);
     const float ts_lp = __fadd_rn(float(log(double(sum))), ts_max);
     const float text_max = mtx > NINF ? __fsub_rn(mtx, ls) : NINF;
     mask_text = ts_lp > text_max;
@@ -813,39 +1029,39 @@ __global__ void __launch_bounds__(1024) k_wproc(WRows r, float* logits, float* s
   float s2 = s1;
   if (mask_text) {
     s2 = 0.f;
-    for (int i = beg + threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = max(beg, a0) + threadIdx.x; i < a1; i += blockDim.x) {
       const float x = lg[i];
       const float ei = x > NINF ? expf_go(__fsub_rn(x, mts)) : 0.f;
       e[i] = ei;
       s2 = __fadd_rn(s2, ei);
     }
-    s2 = block_sum(s2, shf);
+    s2 = cl_sum<CL>(s2, shf, &clf[5]);
   }
   __syncthreads();
   VI best{-1.f, n}, bts{-1.f, n};
-  for (int i = lo + threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = max(lo, a0) + threadIdx.x; i < a1; i += blockDim.x) {
     const float ei = e[i];
     best = vi_max(best, VI{ei, i});
     if (i >= beg) bts = vi_max(bts, VI{ei, i});
   }
+  best = cl_vi_max<CL>(best, shv, &clv[0]);
+  bts = cl_vi_max<CL>(bts, shv, &clv[1]);
   if (mask_text && lo > 0 && best.v < 0.f) best = VI{-1.f, n};
-  best = block_vi_max(best, shv);
-  bts = block_vi_max(bts, shv);
   // masked text has probability 0: it only wins if nothing else is positive
   if (mask_text && !(best.v > 0.f)) best = VI{0.f, 0};
   // the largest e before each winner that is smaller than it
   float near = 0.f, near_t = 0.f;
-  for (int i = lo + threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = max(lo, a0) + threadIdx.x; i < a1; i += blockDim.x) {
     const float ei = e[i];
     if (i < best.i && ei < best.v) near = fmaxf(near, ei);
     if (i >= beg && i < bts.i && ei < bts.v) near_t = fmaxf(near_t, ei);
   }
-  near = block_max(near, shf);
-  near_t = block_max(near_t, shf);
+  near = cl_max<CL>(near, shf, &clf[6]);
+  near_t = cl_max<CL>(near_t, shf, &clf[7]);
   const float margin = 1.f - 9.5367431640625e-07f;  // 1 − 2^-20
   if ((best.v > 0.f && near >= best.v * margin) || (bts.v > 0.f && near_t >= bts.v * margin)) amb = 1;
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && rank == 0) {
     int o[4];
     if (amb) {
       proc_exact(lg, n, beg, o);
@@ -872,6 +1088,7 @@ __global__ void __launch_bounds__(1024) k_wproc(WRows r, float* logits, float* s
     state[s] = ns;
     if (next_tok) next_tok[row] = o[0];
   }
+  if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while its slots may be read
 }
 
 // softmax(row)[nosp] (mathx.go:78-90): EXP8 lanes over n&~7 summed in order
@@ -915,8 +1132,31 @@ void launch_wself(const WRows& r, const float* q, const float* sk, const float* 
   k_wself<<<dim3(r.rows, r.nh), 128, (r.text_ctx + 64) * 4, st>>>(r, q, sk, sv, att);
 }
 
-void launch_wcross(const WRows& r, const float* q, const float* ck, const float* cvt, float* att, cudaStream_t st) {
-  k_wcross<<<dim3(r.rows, r.nh), 256, (r.audio_ctx + 64) * 4, st>>>(r, q, ck, cvt, att);
+void launch_wcross(const WRows& r, const float* q, const float* ck, const float* cvt, float* att, float* scratch,
+                   size_t scratch_floats, cudaStream_t st) {
+  // One CTA per (row, head) when those fill the GPU; otherwise a head's keys
+  // (chunks of at most 256) and its outputs are spread over more CTAs, their
+  // rows staged by bulk copies (same bits either way).
+  const int heads = r.rows * r.nh, ctx = r.audio_ctx, ctx4 = ctx & ~3;
+  const int target = 4 * 148;
+  int ks = std::min((target + heads - 1) / heads, std::max(1, ctx4 / 64));
+  const int ch = std::min(256, ((ctx4 + ks - 1) / ks + 15) / 16 * 16);
+  ks = std::max(1, (ctx4 + ch - 1) / ch);
+  const size_t need = size_t(heads) * ctx + size_t(heads) * ks;
+  if (heads >= 2 * 148 || r.nh * 64 != r.st || !scratch || need > scratch_floats || ctx4 == 0 || ctx % 4 ||
+      ctx > 1500) {
+    k_wcross<<<dim3(r.rows, r.nh), 256, (ctx + 64) * 4, st>>>(r, q, ck, cvt, att);
+    return;
+  }
+  float* sg = scratch;
+  float* mg = scratch + size_t(heads) * ctx;
+  k_wcross_sc<<<dim3(r.rows, r.nh, ks), 128, size_t(ch) * 64 * 4, st>>>(r, q, ck, ch, sg, mg);
+  if (heads * 16 <= target)
+    k_wcross_o<4, true><<<dim3(r.rows, r.nh, 16), 64, size_t(ctx) * 4 * 5, st>>>(r, cvt, ks, sg, mg, att);
+  else if (heads * 8 <= target)
+    k_wcross_o<8, true><<<dim3(r.rows, r.nh, 8), 128, size_t(ctx) * 4 * 9, st>>>(r, cvt, ks, sg, mg, att);
+  else  // 16 outputs a CTA: staging them would leave two CTAs an SM
+    k_wcross_o<16, false><<<dim3(r.rows, r.nh, 4), 256, size_t(ctx) * 4, st>>>(r, cvt, ks, sg, mg, att);
 }
 
 void launch_wmm(const WmmArgs& a, int groups, cudaStream_t st) {
@@ -941,9 +1181,68 @@ void launch_wmm(const WmmArgs& a, int groups, cudaStream_t st) {
   k_wmm<<<grid, 256, 0, st>>>(a);
 }
 
+// Whether a cluster of `cl` 1024-thread CTAs of k_wproc can be resident
+// (asked once per size and device).
+bool wproc_cluster_fits(int cl) {
+  static int known[64][4] = {};  // 0 unknown, 1 fits, 2 does not
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int slot = cl == 8 ? 0 : cl == 4 ? 1 : 2;
+  if (dev < 0 || dev >= 64) return false;
+  if (known[dev][slot] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl);
+    cfg.blockDim = dim3(1024);
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cl;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const cudaError_t e = cl == 8   ? cudaOccupancyMaxActiveClusters(&n, k_wproc<8>, &cfg)
+                          : cl == 4 ? cudaOccupancyMaxActiveClusters(&n, k_wproc<4>, &cfg)
+                                    : cudaOccupancyMaxActiveClusters(&n, k_wproc<2>, &cfg);
+    if (e != cudaSuccess) cudaGetLastError();
+    known[dev][slot] = e == cudaSuccess && n > 0 ? 1 : 2;
+  }
+  return known[dev][slot] == 1;
+}
+
+void wdecode_init() {
+  for (int cl : {8, 4, 2}) wproc_cluster_fits(cl);
+  cudaFuncSetAttribute(k_wcross_sc, cudaFuncAttributeMaxDynamicSharedMemorySize, 256 * 64 * 4);
+  cudaFuncSetAttribute(k_wcross_o<8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 9 * 1500 * 4);
+}
+
 void launch_wproc(const WRows& r, float* logits, float* scratch, const WVocabDev& v, WSample* state, int* out,
                   const int* step, int* next_tok, cudaStream_t st) {
-  k_wproc<<<r.rows, 1024, 0, st>>>(r, logits, scratch, v, state, out, step, next_tok);
+  // Each row on a cluster of 8, 4 or 2 CTAs (one CTA an SM) while the rows
+  // leave SMs idle, else one CTA per row.
+  int cl = r.rows * 8 <= 148 ? 8 : r.rows * 4 <= 148 ? 4 : r.rows * 2 <= 148 ? 2 : 1;
+  while (cl > 1 && !wproc_cluster_fits(cl)) cl /= 2;
+  if (cl == 1) {
+    k_wproc<1><<<r.rows, 1024, 0, st>>>(r, logits, scratch, v, state, out, step, next_tok);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(r.rows * cl);
+  cfg.blockDim = dim3(1024);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cl;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (cl == 8)
+    cudaLaunchKernelEx(&cfg, k_wproc<8>, r, logits, scratch, v, state, out, step, next_tok);
+  else if (cl == 4)
+    cudaLaunchKernelEx(&cfg, k_wproc<4>, r, logits, scratch, v, state, out, step, next_tok);
+  else
+    cudaLaunchKernelEx(&cfg, k_wproc<2>, r, logits, scratch, v, state, out, step, next_tok);
 }
 
 void launch_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int advance, int* step, cudaStream_t st) {

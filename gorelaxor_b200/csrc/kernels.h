@@ -405,7 +405,10 @@ void launch_wln(const float* x, float* y, const float* w, const float* b, int ro
 void launch_wself(const WRows& r, const float* q, const float* sk, const float* sv, float* att, cudaStream_t st);
 // Cross-attention over the stream's pre-scaled keys [nh][ctx][hd] and
 // transposed values [nh][hd][ctx].
-void launch_wcross(const WRows& r, const float* q, const float* ck, const float* cvt, float* att, cudaStream_t st);
+// Cross-attention of every row; `scratch` (scratch_floats floats) holds the
+// scores when the heads are spread over several CTAs.
+void launch_wcross(const WRows& r, const float* q, const float* ck, const float* cvt, float* att, float* scratch,
+                   size_t scratch_floats, cudaStream_t st);
 // The packed-order product (whisper/gemm.go:124-209, rows < m/6·6) for
 // `groups` independent matrices (grid z): C = A·Wᵀ + bias, row i of group z
 // at a + z·a_zs + i·lda. Epilogues (mode): WM_STORE / WM_RESID (+=) /
@@ -446,6 +449,10 @@ void launch_wenc_conv2(const float* h1, float* x2, int state, int ctx, int n, cu
 void launch_wenc_heads(const float* q, const float* k, const float* v, float* qh, float* kh, float* vt, int ctx,
                        int state, int nh, float sc, int n, cudaStream_t st);
 void launch_wenc_softmax(float* x, int len, long rows, cudaStream_t st);
+// Once per device, outside any graph capture: which cluster sizes the
+// process/sample kernel can use, and the shared memory limits of the
+// cross-attention kernels.
+void wdecode_init();
 // process + sample at temperature 0 for every row (transcribe.go:370-494):
 // logits [rows][vocab] are masked in place (scratch [rows][vocab]); writes
 // out[*step][rows][4] (id, tid, p, plog), the next token and the stream's

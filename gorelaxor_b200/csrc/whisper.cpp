@@ -248,7 +248,7 @@ int enqueue_decode(grx_whisper_batch* b) {
     flin_w(L.o, b->att, st, n, L.ob, FE_RESID, b->x, st, nullptr, s), k++;
     launch_wln(b->x, b->cur, L.x_ln_w, L.x_ln_b, n, st, s), k++;
     flin_w(L.xq, b->cur, st, n, L.xqb, FE_BIAS, b->q, st, nullptr, s), k++;
-    launch_wcross(b->rows, b->q, ckl, cvl, b->att, s), k++;
+    launch_wcross(b->rows, b->q, ckl, cvl, b->att, b->scratch, size_t(n) * m->n_vocab, s), k++;
     flin_w(L.xo, b->att, st, n, L.xob, FE_RESID, b->x, st, nullptr, s), k++;
     launch_wln(b->x, b->cur, L.mlp_ln_w, L.mlp_ln_b, n, st, s), k++;
     flin_w(L.fc1, b->cur, st, n, L.fc1b, FE_GELU, b->ff, 4 * st, nullptr, s), k++;
@@ -581,6 +581,7 @@ int grx_whisper_batch_create(grx_whisper* m, int n, grx_whisper_batch** out) {
   b->m = m;
   b->n = n;
   CK(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking));
+  wdecode_init();
   int rc = 0;
   const int st = m->n_state, L = m->n_text_layer;
   b->sk = b->ar.alloc<float>(size_t(L) * layer_stride_self(m, n), &rc);
@@ -760,7 +761,8 @@ int prefill(grx_whisper_batch* b, const int* prompt, int np, int sot_at) {
     prompt_product(b, np, L.o, b->patt, st, L.ob, FE_RESID, b->px, st);
     launch_wln(b->px, b->pcur, L.x_ln_w, L.x_ln_b, R, st, s);
     prompt_product(b, np, L.xq, b->pcur, st, L.xqb, FE_BIAS, b->pq, st);
-    launch_wcross(pr, b->pq, b->ck + l * layer_stride_cross(m, n), b->cvt + l * layer_stride_cross(m, n), b->patt, s);
+    launch_wcross(pr, b->pq, b->ck + l * layer_stride_cross(m, n), b->cvt + l * layer_stride_cross(m, n), b->patt,
+                  b->scratch, size_t(n) * m->n_vocab, s);
     prompt_product(b, np, L.xo, b->patt, st, L.xob, FE_RESID, b->px, st);
     launch_wln(b->px, b->pcur, L.mlp_ln_w, L.mlp_ln_b, R, st, s);
     prompt_product(b, np, L.fc1, b->pcur, st, L.fc1b, FE_GELU, b->pff, 4 * st);

@@ -154,3 +154,28 @@ def test_whisper_long_prompt_packed_rows(have_gpu, np_):
         _check_tokens(toks[:, i], want)
         assert abs(ns[i] - wns) <= TOL * abs(wns)
 
+
+
+@pytest.mark.parametrize("n", [1, 20, 40, 80, 160])
+def test_whisper_launch_shapes(have_gpu, n):
+    """Every launch shape of the token step on the small model: cross-
+    attention spread over key chunks and output slices (fewer than 296
+    (row, head) pairs) or one CTA per pair (the 160-stream decode and every
+    prompt pass from 80 streams up), process/sample on clusters of 8, 4 or 2
+    CTAs per row or one CTA per row. Ids identical for every stream, and
+    every output of the first and last stream."""
+    cfg = synth.WhisperConfig(**SMALL_W)
+    gm, om = _models(cfg, seed=7)
+    steps = 6
+    enc = _enc(cfg, n, seed0=31)
+    b = g.WhisperBatch(gm, n)
+    b.set_audio(enc)
+    prompt, sot_at = _prompt(gm)
+    b.prompt(prompt, sot_at)
+    toks = b.run(steps)
+    ids = om.run(enc, prompt, sot_at, steps, 8)
+    for i in range(n):
+        assert np.array_equal(toks[:, i, 0], ids[i]), f"stream {i}: ids differ"
+    for i in {0, n - 1}:
+        want, _ = om.greedy(om.seq(enc[i]), prompt, sot_at, steps)
+        _check_tokens(toks[:, i], want)
