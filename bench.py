@@ -45,6 +45,10 @@ METRIC = "FlowLM frames/s (stream-frames per second, whole job)"
 UNIT = "frames/s"
 TRAFFIC_PER_ALGO = 143.51e6 / 139.79e6  # k_attn DRAM bytes / algorithmic bytes, measured (ncu)
 C0_FRAMES = 256  # one stream, 256 frames from a 64-position prefill
+# DRAM bytes per frame of the persistent one-stream kernel, from one ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum = 774.2 MB for a
+# launch of 16 frames that starts from a cold L2).
+C0_TRAFFIC_PER_FRAME = 774.2e6 / 16
 
 
 def peaks():
@@ -1273,6 +1277,11 @@ def run_c0(g, model, cfg, local, warmup, steps):
                 "note": "grx_streams_step per frame, host-synchronous"},
         "roofline": {"bound": "hbm", "kernel": "whole frame", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_kind": peak_kind, "bytes_per_frame_mean": per_step / F,
+                     "traffic": C0_TRAFFIC_PER_FRAME,
+                     "traffic_unit": "bytes per frame (ncu dram read+write of one k_frame1 launch of 16 frames "
+                                     "from a cold L2, divided by 16)",
+                     "limiter": "latency of the frame's dependency chain: 35 grid barriers and the steps between "
+                                "them (ncu: warps stalled at barriers 13.2 per issued instruction, DRAM 2.6 % busy)",
                      "note": "algorithmic bytes per frame (Q8_0 weights of the transformer and flow head, float32 "
                              "rows, K/V rows 0..pos) over the frame's device time; the 82.9 MB of weights fit in "
                              "the 126 MB L2, which is flushed before each step but not between the frames of a "

@@ -36,11 +36,10 @@ __device__ __forceinline__ int tx_at(int k, int m) { return k * TM + 4 * ((m >> 
 
 __host__ __device__ constexpr int t_wstride(int K) { return K + 16; }
 
-// Shared memory: NIN inputs [K][TM] floats, NIN × 32 weight rows, their
-// f16 block scales, and a [32][TM] tile for the epilogue.
-__host__ __device__ constexpr size_t tdt_smem(int K, int nin) {
-  return size_t(nin) * TM * K * 4 + size_t(nin) * TROWS * t_wstride(K) + size_t(nin) * TROWS * (K / QK) * 2 +
-         size_t(TROWS) * TM * 4;
+// Shared memory: one input [K][TM] floats, 32 weight rows, their f16 block
+// scales, and a [32][TM] tile for the epilogue.
+__host__ __device__ constexpr size_t tdt_smem(int K) {
+  return size_t(TM) * K * 4 + size_t(TROWS) * t_wstride(K) + size_t(TROWS) * (K / QK) * 2 + size_t(TROWS) * TM * 4;
 }
 
 // dot4q8avx's lanes for one weight row against TM staged streams: lane l of
@@ -122,10 +121,12 @@ struct TLin {
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(256) k_tdt_lin(TdtArgs a, TLin t, int parity) {
+__global__ void __launch_bounds__(256, MODE == T_JOINT ? 2 : 3) k_tdt_lin(TdtArgs a, TLin t, int parity) {
   const int layer = t.layer;
   extern __shared__ __align__(16) uint8_t tsm[];
-  constexpr int NIN = MODE == T_LSTM ? 2 : 1;
+  // The LSTM's two products (Wx·x, Wh·h) pass through the same tiles one
+  // after the other, which keeps the shared memory of a CTA to one input.
+  constexpr int NPASS = MODE == T_LSTM ? 2 : 1;
   if (MODE == T_LSTM && layer == 0 && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
     // the next iteration's lists start empty (k_tdt_decide fills them)
     a.counts[2 * (parity ^ 1)] = 0;
@@ -142,26 +143,28 @@ __global__ void __launch_bounds__(256) k_tdt_lin(TdtArgs a, TLin t, int parity) 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, grp = lane >> 3, l = lane & 7;
   const int r = warp * 4 + grp;  // this group's row within the tile
   float* sx = reinterpret_cast<float*>(tsm);
-  int8_t* sw = reinterpret_cast<int8_t*>(tsm + size_t(NIN) * TM * K * 4);
-  uint16_t* sd = reinterpret_cast<uint16_t*>(tsm + size_t(NIN) * TM * K * 4 + size_t(NIN) * TROWS * ws);
-  float* tile = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sd) + size_t(NIN) * TROWS * nb * 2);
+  int8_t* sw = reinterpret_cast<int8_t*>(tsm + size_t(TM) * K * 4);
+  uint16_t* sd = reinterpret_cast<uint16_t*>(tsm + size_t(TM) * K * 4 + size_t(TROWS) * ws);
+  float* tile = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sd) + size_t(TROWS) * nb * 2);
   __shared__ int s_stream[TM];
   if (threadIdx.x < TM) s_stream[threadIdx.x] = threadIdx.x < mt ? list[g0 + threadIdx.x] : -1;
-
-  // ---- the tile's weight rows and scales, by async copies
   const int nrows = MODE == T_LSTM ? TROWS : min(TROWS, t.w0.rows - int(blockIdx.x) * TROWS);
-  {
-    // tile row tr holds global row (LSTM) gate tr/8, unit 8·blockIdx.x + tr%8,
-    // or (PROJ, JOINT) row 32·blockIdx.x + tr
-    auto grow = [&](int tr) {
-      return MODE == T_LSTM ? (tr >> 3) * a.H + int(blockIdx.x) * 8 + (tr & 7) : int(blockIdx.x) * TROWS + tr;
-    };
-    const int cpr = K / 16;
-    for (int in = 0; in < NIN; in++) {
+  float out[TM];
+
+  for (int in = 0; in < NPASS; in++) {
+    if (in > 0) __syncthreads();  // every group is done with the previous pass's tiles
+    // ---- the tile's weight rows and scales, by async copies
+    {
+      // tile row tr holds global row (LSTM) gate tr/8, unit 8·blockIdx.x + tr%8,
+      // or (PROJ, JOINT) row 32·blockIdx.x + tr
+      auto grow = [&](int tr) {
+        return MODE == T_LSTM ? (tr >> 3) * a.H + int(blockIdx.x) * 8 + (tr & 7) : int(blockIdx.x) * TROWS + tr;
+      };
+      const int cpr = K / 16;
       const DQ8& W = in == 0 ? t.w0 : t.w1;
       for (int i = threadIdx.x; i < nrows * cpr; i += blockDim.x) {
         const int tr = i / cpr, c = i - tr * cpr;
-        cp16t(sw + (size_t(in) * TROWS + tr) * ws + c * 16, W.q + size_t(grow(tr)) * K + c * 16);
+        cp16t(sw + size_t(tr) * ws + c * 16, W.q + size_t(grow(tr)) * K + c * 16);
       }
       // scales: every load of the tile issued before the first store
       constexpr int SI = (TROWS * (1024 / QK) + 255) / 256;
@@ -174,20 +177,17 @@ __global__ void __launch_bounds__(256) k_tdt_lin(TdtArgs a, TLin t, int parity) 
 #pragma unroll
       for (int u = 0; u < SI; u++) {
         const int i = threadIdx.x + u * 256, tr = i / nb, b = i - tr * nb;
-        if (i < nrows * nb) sd[(size_t(in) * TROWS + tr) * nb + b] = dv[u];
+        if (i < nrows * nb) sd[size_t(tr) * nb + b] = dv[u];
       }
+      asm volatile("cp.async.commit_group;\n" ::);
     }
-    asm volatile("cp.async.commit_group;\n" ::);
-  }
-  __syncthreads();  // s_stream
+    if (in == 0) __syncthreads();  // s_stream
 
-  // ---- the streams' inputs, stream-minor: an item is four consecutive k of
-  // one stream (16-byte loads along the stream's row); BATCH items' loads
-  // are in flight before the first is stored.
-  constexpr int BATCH = 8;
-  const int k4n = K / 4, items = TM * k4n;
-  for (int in = 0; in < NIN; in++) {
-    float* dst = sx + size_t(in) * TM * K;
+    // ---- the streams' inputs, stream-minor: an item is four consecutive k
+    // of one stream (16-byte loads along the stream's row); BATCH items'
+    // loads are in flight before the first is stored.
+    constexpr int BATCH = 8;
+    const int k4n = K / 4, items = TM * k4n;
     for (int i0 = 0; i0 < items; i0 += BATCH * 256) {
       float4 v[BATCH], e[BATCH];
 #pragma unroll
@@ -237,40 +237,36 @@ __global__ void __launch_bounds__(256) k_tdt_lin(TdtArgs a, TLin t, int parity) 
           }
         }
 #pragma unroll
-        for (int j = 0; j < 4; j++) dst[tx_at(k + j, m)] = x[j];
+        for (int j = 0; j < 4; j++) sx[tx_at(k + j, m)] = x[j];
       }
     }
-  }
-  asm volatile("cp.async.wait_all;\n" ::);
-  __syncthreads();
+    asm volatile("cp.async.wait_all;\n" ::);
+    __syncthreads();
 
-  // ---- the products: row r of the tile for all TM streams, per input
-  float out[TM];
-  {
+    // ---- the product: row r of the tile for all TM streams
     f2 acc[TM / 2];
 #pragma unroll
     for (int p = 0; p < TM / 2; p++) acc[p] = 0;
     if (r < nrows) row_lanes(sw + size_t(r) * ws, sd + size_t(r) * nb, sx, nb, l, acc);
+    if (in == 0) {
 #pragma unroll
-    for (int p = 0; p < TM / 2; p++) {
-      out[2 * p] = hsum8_lanes(f2lo(acc[p]));
-      out[2 * p + 1] = hsum8_lanes(f2hi(acc[p]));
+      for (int p = 0; p < TM / 2; p++) {
+        out[2 * p] = hsum8_lanes(f2lo(acc[p]));
+        out[2 * p + 1] = hsum8_lanes(f2hi(acc[p]));
+      }
+    } else {
+      // gates[j] = (Wx·x + b)[j], then kern.Add of Wh·h (rnnt.go:57-59)
+      const int gr = (r >> 3) * a.H + blockIdx.x * 8 + (r & 7);
+      const float b = t.bias[gr];
+#pragma unroll
+      for (int p = 0; p < TM / 2; p++) {
+        const float h0 = hsum8_lanes(f2lo(acc[p])), h1 = hsum8_lanes(f2hi(acc[p]));
+        out[2 * p] = __fadd_rn(__fadd_rn(out[2 * p], b), h0);
+        out[2 * p + 1] = __fadd_rn(__fadd_rn(out[2 * p + 1], b), h1);
+      }
     }
   }
   if (MODE == T_LSTM) {
-    // gates[j] = (Wx·x + b)[j], then kern.Add of Wh·h (rnnt.go:57-59)
-    f2 acc[TM / 2];
-#pragma unroll
-    for (int p = 0; p < TM / 2; p++) acc[p] = 0;
-    row_lanes(sw + size_t(TROWS + r) * ws, sd + size_t(TROWS + r) * nb, sx + size_t(TM) * K, nb, l, acc);
-    const int gr = (r >> 3) * a.H + blockIdx.x * 8 + (r & 7);
-    const float b = t.bias[gr];
-#pragma unroll
-    for (int p = 0; p < TM / 2; p++) {
-      const float h0 = hsum8_lanes(f2lo(acc[p])), h1 = hsum8_lanes(f2hi(acc[p]));
-      out[2 * p] = __fadd_rn(__fadd_rn(out[2 * p], b), h0);
-      out[2 * p + 1] = __fadd_rn(__fadd_rn(out[2 * p + 1], b), h1);
-    }
     if (l == 0)
 #pragma unroll
       for (int m = 0; m < TM; m++) tile[r * TM + m] = out[m];
@@ -410,13 +406,13 @@ __global__ void k_tdt_begin_lists(TdtArgs a) {
 
 }  // namespace
 
-size_t tdt_lin_smem(int K, bool lstm) { return tdt_smem(K, lstm ? 2 : 1); }
+size_t tdt_lin_smem(int K, bool lstm) { return (void)lstm, tdt_smem(K); }
 
 void tdt_kernels_init() {
-  const size_t a = tdt_smem(1024, 2);
+  const size_t a = tdt_smem(1024);
   cudaFuncSetAttribute(k_tdt_lin<T_LSTM>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(a));
-  cudaFuncSetAttribute(k_tdt_lin<T_PROJ>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tdt_smem(1024, 1)));
-  cudaFuncSetAttribute(k_tdt_lin<T_JOINT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tdt_smem(1024, 1)));
+  cudaFuncSetAttribute(k_tdt_lin<T_PROJ>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tdt_smem(1024)));
+  cudaFuncSetAttribute(k_tdt_lin<T_JOINT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tdt_smem(1024)));
 }
 
 void launch_tdt_begin(const TdtArgs& a, cudaStream_t st) {
@@ -432,16 +428,16 @@ void launch_tdt_iteration(const TdtArgs& a, int parity, cudaStream_t st) {
     t.w1 = a.lstm_wh[l];
     t.bias = a.lstm_b[l];
     t.layer = l;
-    k_tdt_lin<T_LSTM><<<dim3(a.H / 8, sg), 256, tdt_smem(a.H, 2), st>>>(a, t, parity);
+    k_tdt_lin<T_LSTM><<<dim3(a.H / 8, sg), 256, tdt_smem(a.H), st>>>(a, t, parity);
   }
   TLin p;
   p.w0 = p.w1 = a.jpred;
   p.bias = a.jpred_b;
-  k_tdt_lin<T_PROJ><<<dim3((a.J + TROWS - 1) / TROWS, sg), 256, tdt_smem(a.H, 1), st>>>(a, p, parity);
+  k_tdt_lin<T_PROJ><<<dim3((a.J + TROWS - 1) / TROWS, sg), 256, tdt_smem(a.H), st>>>(a, p, parity);
   TLin j;
   j.w0 = j.w1 = a.jout;
   j.bias = a.jout_b;
-  k_tdt_lin<T_JOINT><<<dim3((a.nout + TROWS - 1) / TROWS, sg), 256, tdt_smem(a.J, 1), st>>>(a, j, parity);
+  k_tdt_lin<T_JOINT><<<dim3((a.nout + TROWS - 1) / TROWS, sg), 256, tdt_smem(a.J), st>>>(a, j, parity);
   k_tdt_decide<<<(a.n + 3) / 4, 128, 0, st>>>(a, parity);
 }
 
