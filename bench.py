@@ -275,6 +275,28 @@ def run_reference(args, rank, world):
             "e2e": {"value": value, "unit": "windows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
             flush=True)
         return
+    if args.workload == "mimi_encoder":
+        mc = mimi_config()
+        tensors = synth.mimi_tensors(mc, 32, 0, encoder=True)
+        clips, frames = min(args.batch, cores), 12
+        vals, times = [], []
+        for _ in range(args.steps):
+            v, dt = menc_cpu_sample(mc, tensors, clips, frames, cores)
+            vals.append(v)
+            times.append(dt)
+        value = float(np.mean(vals))
+        print(json.dumps({
+            "impl": "reference", "metric": MENC_METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
+            "data": "synthetic (seeded; the reference ships no weights)",
+            "config": {"workload": f"Mimi encode, {args.batch} clips x {args.frames} frames (sampled)",
+                       "global_batch": args.batch, "frames": args.frames, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "frames/s", "cores": clips, "kind": "port",
+                             "sample": f"{clips} clips x {frames} frames (one piece) per step, one clip per thread"},
+            "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
     if args.workload == "mimi":
         mc = mimi_config()
         tensors = synth.mimi_tensors(mc, 32, 0)
@@ -611,6 +633,122 @@ def run_mimi(args, rank, world, local):
         "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck,
     }
     print(json.dumps(line), flush=True)
+
+
+MENC_METRIC = "Mimi encoder frames/s (1920-sample 24 kHz audio frames encoded to latents per second, whole job)"
+
+
+def menc_clips(clips, samples, seed0=1):
+    """[clips][samples] clip audio, N(0, 0.3), clip i seeded seed0 + i."""
+    return np.stack([np.random.default_rng(seed0 + i).normal(0, 0.3, samples).astype(np.float32)
+                     for i in range(clips)])
+
+
+def menc_cpu_sample(mc, tensors, clips, frames, threads):
+    """The oracle's cloneCond encoding on host threads, one clip of `frames`
+    frames per thread. Returns (frames/s, wall seconds)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+
+    om = orc.Mimi(mc, tensors, 32)
+    x = menc_clips(clips, frames * mc.frame)
+    with orc.fast_mode():
+        om.clone_latents(x[0][: mc.frame])  # warm-up
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=min(threads, clips)) as ex:
+            list(ex.map(om.clone_latents, list(x)))
+        dt = time.perf_counter() - t0
+    return clips * frames / dt, dt
+
+
+def run_mimi_encoder(args, rank, world, local):
+    """--workload mimi_encoder: Pocket TTS's Mimi encoder as voice cloning
+    runs it (cloneCond, voice.go:113-124): `batch` clips per GPU of `frames`
+    1920-sample frames each, encoded together, each from a fresh state; one
+    step = every clip."""
+    import torch
+
+    import gorelaxor_b200 as g
+    from gorelaxor_b200 import synth
+    from gorelaxor_b200.dist import max_over_ranks, partition
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    B, F = args.batch, args.frames
+    mc = mimi_config()
+    tensors = synth.mimi_tensors(mc, 32, 0, encoder=True)
+    gm = g.Mimi(synth.flowlm_gguf(synth.FlowLMConfig(), tensors, mimi=mc), device=local)
+    mine = partition(B * world, world, rank)
+    samples = F * gm.frame
+    x = menc_clips(len(mine), samples, seed0=1 + mine.start)
+    enc = g.MimiEncoder(gm, B, samples)
+    d_x = torch.from_numpy(x).cuda()
+    d_lat = torch.empty((B, F, gm.ldim), dtype=torch.float32, device="cuda")
+    ext = torch.cuda.ExternalStream(enc.cuda_stream())
+    for _ in range(args.warmup):
+        enc.encode_device(samples, d_x.data_ptr(), d_lat.data_ptr())
+        enc.sync()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    l0 = enc.launches()
+    if dist:
+        dist.barrier()
+    clocks.start()
+    ms = []
+    for _ in range(args.steps):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        enc.encode_device(samples, d_x.data_ptr(), d_lat.data_ptr())
+        e1.record(ext)
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    ck = clocks.stop()
+    launches = enc.launches() - l0
+    total_ms = max_over_ranks(float(np.sum(ms)), device="cuda")
+    value = args.steps * B * F * world / (total_ms / 1000)
+    e2e = None
+    if args.e2e_steps > 0:
+        pin = torch.from_numpy(x).pin_memory().numpy()
+        em = []
+        for _ in range(args.e2e_steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            enc.encode(pin)
+            em.append((time.perf_counter() - t0) * 1000)
+        emax = max_over_ranks(float(np.sum(em)), device="cuda")
+        e2e = {"value": args.e2e_steps * B * F * world / (emax / 1000), "unit": "frames/s",
+               "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(B * F * gm.ldim * 4),
+               "note": "grx_mimi_encode: clips H2D, latents D2H (device buffers allocated per call)"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        clips, frames = min(B, cores), 12
+        v, dt = menc_cpu_sample(mc, tensors, clips, frames, cores)
+        cpu = {"value": v, "unit": "frames/s", "cores": clips, "kind": "port",
+               "sample": f"{clips} clips x {frames} frames (one piece), one clip per thread ({dt:.1f} s wall)"}
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": MENC_METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8/f32",
+        "data": "synthetic (seeded Q8_0/f32 encoder in the converter's types, N(0, 0.3) audio)",
+        "config": {"workload": f"Mimi encode (voice cloning): {B} clips x {F} frames ({F * 0.08:.1f} s) per GPU",
+                   "global_batch": B * world, "frames": F,
+                   "parallelism": f"clips partitioned, {world} GPU(s), no collective",
+                   "l2": f"activations {B * 23} MB per GPU per piece at the sample rate, larger than L2"},
+        "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck}), flush=True)
 
 
 WENC_METRIC = "Whisper encoder windows/s (30 s log-mel windows encoded, cross K/V included, whole job)"
@@ -1011,7 +1149,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="grx", choices=["grx", "reference"])
     ap.add_argument("--workload", default="flowlm",
-                    choices=["flowlm", "tdt", "whisper", "mimi", "whisper_encoder", "fconf"])
+                    choices=["flowlm", "tdt", "whisper", "mimi", "mimi_encoder", "whisper_encoder", "fconf"])
     ap.add_argument("--batch", type=int, default=None, help="streams per GPU (flowlm 256, tdt 128)")
     ap.add_argument("--frames", type=int, default=None, help="frames per stream (flowlm 512, tdt 750)")
     ap.add_argument("--e2e-steps", type=int, default=1)
@@ -1021,9 +1159,9 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
-    args.batch = args.batch or {"flowlm": 256, "tdt": 128, "whisper": 32, "mimi": 256,
+    args.batch = args.batch or {"flowlm": 256, "tdt": 128, "whisper": 32, "mimi": 256, "mimi_encoder": 16,
                                 "whisper_encoder": 8, "fconf": 4}[args.workload]
-    args.frames = args.frames or {"flowlm": 512, "tdt": 750, "whisper": 224, "mimi": 32,
+    args.frames = args.frames or {"flowlm": 512, "tdt": 750, "whisper": 224, "mimi": 32, "mimi_encoder": 125,
                                   "whisper_encoder": 1, "fconf": 3000}[args.workload]
     if args.impl == "reference":
         return run_reference(args, rank, world)
@@ -1033,6 +1171,8 @@ def main():
         return run_whisper(args, rank, world, local)
     if args.workload == "mimi":
         return run_mimi(args, rank, world, local)
+    if args.workload == "mimi_encoder":
+        return run_mimi_encoder(args, rank, world, local)
     if args.workload == "whisper_encoder":
         return run_whisper_encoder(args, rank, world, local)
     if args.workload == "fconf":

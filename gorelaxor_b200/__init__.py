@@ -91,6 +91,11 @@ def _sig(lib):
         "grx_mimi_cuda_stream": (P, [P]),
         "grx_mimi_launches": (L, [P]),
         "grx_mimi_frames": (I, [P]),
+        "grx_mimi_encoder_create": (I, [P, I, I, PP]),
+        "grx_mimi_encode_device": (I, [P, I, P, P]),
+        "grx_mimi_encode": (I, [P, I, P, P]),
+        "grx_mimi_clone_latents": (I, [P, P, I, P, C.POINTER(C.c_int)]),
+        "grx_voice_clone": (I, [P, P, P, I, PP]),
         "grx_fconf_load": (I, [P, S, I, PP]),
         "grx_fconf_free": (None, [P]),
         "grx_fconf_dims": (I, [P] + [C.POINTER(C.c_int)] * 5),
@@ -301,6 +306,16 @@ class FlowLM:
         _check(lib().grx_voice_raw(self._h, a.shape[2], _ptr(a), C.byref(h)))
         return Voice(h)
 
+    def voice_clone(self, mimi: "Mimi", pcm: np.ndarray) -> "Voice":
+        """Model.CloneVoice after resampling and end_on_pause (voice.go:
+        94-106): Mimi's encoding of the 24 kHz clip, then the flow LM."""
+        x = np.ascontiguousarray(pcm, dtype=np.float32).ravel()
+        h = C.c_void_p()
+        _check(lib().grx_voice_clone(self._h, mimi._h, _ptr(x), x.size, C.byref(h)))
+        v = Voice(h)
+        v._model = self
+        return v
+
     def voice_from_latents(self, latents: np.ndarray) -> "Voice":
         """The voice a clip's Mimi latents [n][ldim] make (the flow-LM half
         of CloneVoice, voice.go:94-106)."""
@@ -436,10 +451,58 @@ class Mimi:
         (self.d, self.heads, self.layers, self.context, self.upsample, self.ldim, self.frame,
          self.sample_rate) = [x.value for x in v]
 
+    def clone_latents(self, pcm: np.ndarray) -> np.ndarray:
+        """cloneCond's Mimi encoding of one 24 kHz clip (voice.go:113-124):
+        latents [frames][ldim], frames = ceil(len / frame)."""
+        x = np.ascontiguousarray(pcm, dtype=np.float32).ravel()
+        frames = -(-x.size // self.frame)
+        out = np.empty((frames, self.ldim), np.float32)
+        _check(lib().grx_mimi_clone_latents(self._h, _ptr(x), x.size, _ptr(out), None))
+        return out
+
     def __del__(self, _free=_FREE):
         h, self._h = getattr(self, "_h", None), None
         if h:
             _free["grx_mimi_free"](h)
+
+
+class MimiEncoder:
+    """n clips through Mimi's encoder together (mimi.go:152-179), each from
+    a fresh state, as cloneCond encodes one (voice.go:113-124)."""
+
+    def __init__(self, model: Mimi, n: int, max_samples: int):
+        self.model, self.n, self.max_samples = model, n, max_samples
+        h = C.c_void_p()
+        _check(lib().grx_mimi_encoder_create(model._h, n, max_samples, C.byref(h)))
+        self._h = h
+
+    def encode(self, pcm: np.ndarray) -> np.ndarray:
+        """pcm [n][samples] → latents [n][frames][ldim]."""
+        m = self.model
+        x = np.ascontiguousarray(pcm, dtype=np.float32).reshape(self.n, -1)
+        frames = -(-x.shape[1] // m.frame)
+        out = np.empty((self.n, frames, m.ldim), np.float32)
+        _check(lib().grx_mimi_encode(self._h, x.shape[1], _ptr(x), _ptr(out)))
+        return out
+
+    def encode_device(self, samples: int, d_pcm: int, d_latents: int):
+        """Device pointers (ints): pcm [n][samples] in, latents
+        [n][frames][ldim] out. Asynchronous."""
+        _check(lib().grx_mimi_encode_device(self._h, samples, C.c_void_p(d_pcm), C.c_void_p(d_latents)))
+
+    def sync(self):
+        _check(lib().grx_mimi_sync(self._h))
+
+    def cuda_stream(self) -> int:
+        return lib().grx_mimi_cuda_stream(self._h) or 0
+
+    def launches(self) -> int:
+        return lib().grx_mimi_launches(self._h)
+
+    def __del__(self, _free=_FREE):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            _free["grx_mimi_streams_free"](h)
 
 
 class MimiStreams:

@@ -88,6 +88,78 @@ __global__ void k_mimi_stage(const float* x, const float* carry_in, float* carry
     st4(carry_out + (size_t(s) * P + r - T) * C + c, v);
 }
 
+// k_mimi_stage for a channel count that is not a multiple of four (the
+// encoder's first convolution reads one channel): one value per thread.
+__global__ void k_mimi_stage_s(const float* x, const float* carry_in, float* carry_out, float* stage, int T, int C,
+                               int P, int elu) {
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nst = (P + T) * C;
+  if (i >= nst + P * C) return;
+  const int q = i < nst ? i : i - nst;
+  const int rq = q / C, c = q - rq * C, r = rq + (i < nst ? 0 : T);
+  float v;
+  if (r < P) {
+    v = carry_in[(size_t(s) * P + r) * C + c];
+  } else {
+    v = x[(size_t(s) * T + r - P) * C + c];
+    if (elu) v = elu_at(v, (r - P) * C + c, T * C);
+  }
+  if (i < nst)
+    stage[(size_t(s) * (P + T) + r) * C + c] = v;
+  else
+    carry_out[(size_t(s) * P + r - T) * C + c] = v;
+}
+
+// gemvRows (gemm.go:195-259) of a float32 weight with K < 16 columns for
+// rows [off, T) of every stream: every dot is dotF32Go (four strided
+// unfused sums, gemm.go:294-308); an output in a group of four is
+// 0 + dot (dotF32x4's zeroed start, kernels_amd64.go:75-95), the last n % 4
+// the dot itself; then + bias, stored or (resid) added to y.
+__global__ void k_mimi_gemv_small(const float* x, int ldx, int sstride, int T, int off, const float* w, int N, int K,
+                                  const float* bias, float* y, int resid) {
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x, rows = T - off;
+  if (i >= rows * N) return;
+  const int t = off + i / N, j = i - (i / N) * N;
+  const float* xr = x + (size_t(s) * sstride + t) * ldx;
+  const float* wr = w + size_t(j) * K;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int k = 0;
+  for (; k + 4 <= K; k += 4) {
+    s0 = __fadd_rn(s0, __fmul_rn(xr[k], wr[k]));
+    s1 = __fadd_rn(s1, __fmul_rn(xr[k + 1], wr[k + 1]));
+    s2 = __fadd_rn(s2, __fmul_rn(xr[k + 2], wr[k + 2]));
+    s3 = __fadd_rn(s3, __fmul_rn(xr[k + 3], wr[k + 3]));
+  }
+  for (; k < K; k++) s0 = __fadd_rn(s0, __fmul_rn(xr[k], wr[k]));
+  float v = __fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3);
+  if (j < (N & ~3)) v = __fadd_rn(0.f, v);
+  if (bias) v = __fadd_rn(v, bias[j]);
+  float* yp = y + (size_t(s) * T + t) * N + j;
+  *yp = resid ? __fadd_rn(*yp, v) : v;
+}
+
+// The row tables of a call of T rows per stream (the encoder's last piece
+// can be shorter than the others): row r belongs to stream slot r / T,
+// call-stream i starts at row i·T, runs T rows and uses slot i.
+__global__ void k_mimi_rowtab(int T, int n, int* rowslot, int* crow0, int* cT, int* cslot) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n * T) rowslot[i] = i / T;
+  if (i < n) {
+    crow0[i] = i * T;
+    cT[i] = T;
+    cslot[i] = i;
+  }
+}
+
+// The encoder's downsampling convolution pads its first call with copies of
+// the first row ("replicate", model.go:308-313): carry[s][p] = x[s][0] for
+// p < P.
+__global__ void k_mimi_replicate(const float* x, int T, int C, float* carry, int P) {
+  const int s = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P * C) return;
+  carry[size_t(s) * P * C + i] = x[size_t(s) * T * C + i % C];
+}
+
 // conv.run's window (nn.go:275-300) for any stride and dilation: rows
 // [prev (P); x (T)] of cin values; output row t takes rows t·stride + j·dil
 // for j < k. The last P rows become the next call's prev.
@@ -344,7 +416,23 @@ void launch_mimi_elu(const float* in, float* out, int n, int len, cudaStream_t s
 
 void launch_mimi_stage(const float* x, const float* carry_in, float* carry_out, float* stage, int n, int T, int C,
                        int P, bool elu, cudaStream_t st) {
-  k_mimi_stage<<<grid2((2 * P + T) * (C / 4), n), 256, 0, st>>>(x, carry_in, carry_out, stage, T, C, P, elu ? 1 : 0);
+  if (C % 4)
+    k_mimi_stage_s<<<grid2((2 * P + T) * C, n), 256, 0, st>>>(x, carry_in, carry_out, stage, T, C, P, elu ? 1 : 0);
+  else
+    k_mimi_stage<<<grid2((2 * P + T) * (C / 4), n), 256, 0, st>>>(x, carry_in, carry_out, stage, T, C, P, elu ? 1 : 0);
+}
+
+void launch_mimi_gemv_small(const float* x, int ldx, int sstride, int T, int off, const float* w, int N, int K,
+                            const float* bias, float* y, bool resid, int n, cudaStream_t st) {
+  k_mimi_gemv_small<<<grid2((T - off) * N, n), 256, 0, st>>>(x, ldx, sstride, T, off, w, N, K, bias, y, resid ? 1 : 0);
+}
+
+void launch_mimi_rowtab(int T, int n, int* rowslot, int* crow0, int* cT, int* cslot, cudaStream_t st) {
+  k_mimi_rowtab<<<(n * T + 255) / 256, 256, 0, st>>>(T, n, rowslot, crow0, cT, cslot);
+}
+
+void launch_mimi_replicate(const float* x, int T, int C, float* carry, int P, int n, cudaStream_t st) {
+  k_mimi_replicate<<<grid2(P * C, n), 256, 0, st>>>(x, T, C, carry, P);
 }
 
 void launch_mimi_im2col(const float* x, const float* prev_in, float* prev_out, float* col, int n, int T, int cin, int k,

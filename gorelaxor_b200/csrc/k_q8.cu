@@ -962,7 +962,7 @@ void q8_kernels_init() {
   GemmWide::init();
   GemmSmall::init();
   GemmSmallWide::init();
-  const int gv = 8 * 4096 + 8 * 128 * 4 + 8 * 32 * 4;
+  const int gv = 8 * kQ8GemvMaxK + 8 * (kQ8GemvMaxK / QK) * 4 + 8 * 32 * 4;
   cudaFuncSetAttribute(k_q8_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gv);
   cudaFuncSetAttribute(k_q8_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, gv);
   cudaFuncSetAttribute(k_q8_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gv);

@@ -97,6 +97,10 @@ struct LnArgs {
 
 void launch_ln(const LnArgs& a, int M, int D, cudaStream_t st);
 
+// The widest Q8_0 row (values) the up-to-8-row product takes: its rows of
+// activations sit in shared memory.
+constexpr int kQ8GemvMaxK = 16384;
+
 // Activation blocks rounded to Q8_0 travel as int8 values [M][K] and block
 // scales [M][K/32], each scale stored twice as a float2 (s, s): the
 // tensor-core product consumes it as one packed operand.
@@ -155,6 +159,15 @@ void launch_mimi_elu(const float* in, float* out, int n, int len, cudaStream_t s
 // stage [n][P + T][C] = [carry_in; x or ELU(x)]; carry_out = its last P rows.
 void launch_mimi_stage(const float* x, const float* carry_in, float* carry_out, float* stage, int n, int T, int C,
                        int P, bool elu, cudaStream_t st);
+// gemvRows of a float32 weight of K < 16 columns for rows [off, T) of every
+// stream (x rows at (s·sstride + t)·ldx; y [n][T][N], stored or added).
+void launch_mimi_gemv_small(const float* x, int ldx, int sstride, int T, int off, const float* w, int N, int K,
+                            const float* bias, float* y, bool resid, int n, cudaStream_t st);
+// The row tables of a call of T rows per stream: rowslot[r] = r / T,
+// crow0[i] = i·T, cT[i] = T, cslot[i] = i.
+void launch_mimi_rowtab(int T, int n, int* rowslot, int* crow0, int* cT, int* cslot, cudaStream_t st);
+// carry [n][P][C] = P copies of each stream's row 0 of x [n][T][C].
+void launch_mimi_replicate(const float* x, int T, int C, float* carry, int P, int n, cudaStream_t st);
 void launch_mimi_im2col(const float* x, const float* prev_in, float* prev_out, float* col, int n, int T, int cin, int k,
                         int stride, int dil, int P, cudaStream_t st);
 // Q8_0 rounding of rows t < T of K values at x + (s·sstride + t)·ldx, ELU

@@ -76,11 +76,22 @@ struct grx_mimi {
   float* up = nullptr;  // [d][2S]
   std::vector<MLayer> layers;
   std::vector<MStep> steps;
+  // the encoder, when the file has one (model.go:181-200, 308-313)
+  bool has_enc = false;
+  int hop = 0;  // samples per encoder transformer row
+  std::vector<MLayer> enc_layers;
+  std::vector<MStep> enc_steps;
+  MConv down;  // to the latent rate, no bias (down.b zeros), first call padded by replication
 };
 
 struct grx_mimi_streams {
   Arena ar;
   grx_mimi* m = nullptr;
+  // the network a set runs: the decoder's (S = upsample rows per call) or
+  // the encoder's (S = transformer rows of a full piece)
+  const std::vector<MLayer>* layers = nullptr;
+  const std::vector<MStep>* steps = nullptr;
+  int S = 0;
   int n = 0, max_frames = 0, ring = 0, frames = 0;  // frames decoded since the last reset (all streams)
   cudaStream_t st = nullptr;
   float* kv = nullptr;  // [n][layers][2][heads][ring][64]
@@ -96,6 +107,10 @@ struct grx_mimi_streams {
   std::vector<size_t> carry_n;  // values per stream
   float *sa = nullptr, *sb = nullptr, *se = nullptr, *stage = nullptr, *col = nullptr, *zt = nullptr, *sh = nullptr;
   int par = 0;
+  // encoder sets: the padded clips [n][max_samples], the latents of a piece,
+  // the row count the row tables were last written for
+  float *clip = nullptr, *piece_lat = nullptr;
+  int max_samples = 0, rows_for = -1;
   int64_t launches = 0;
   ~grx_mimi_streams() {
     cudaSetDevice(ar.dev);
@@ -147,6 +162,38 @@ MimiSizes mimi_sizes(const grx_mimi* m) {
     }
     s.act = std::max(s.act, size_t(T) * C);
   }
+  return s;
+}
+
+// The same for an encoder set: pieces of T0 samples through the SEANet
+// encoder, the transformer's rows, the downsampling convolution.
+MimiSizes enc_sizes(const grx_mimi* m, int T0) {
+  MimiSizes s;
+  int T = T0, C = 1;
+  auto prod = [&](const MW& w, int rows) { s.qk = std::max(s.qk, size_t(rows) * w.cols); };
+  auto conv = [&](const MConv& c, int t) {
+    const int To = t / c.stride;
+    if (staged(c))
+      s.stage = std::max(s.stage, size_t(c.past() + t) * c.cin);
+    else if (!(c.k == 1 && c.stride == 1))
+      s.col = std::max(s.col, size_t(To) * c.k * c.cin);
+    prod(c.w, To);
+    return To;
+  };
+  for (const MStep& st : m->enc_steps) {
+    s.act = std::max(s.act, size_t(T) * C);
+    if (st.kind == 0) {
+      T = conv(st.c, T);
+      C = st.c.cout;
+    } else {
+      conv(st.ra, T);
+      s.h = std::max(s.h, size_t(T) * st.ra.cout);
+      conv(st.rb, T);
+    }
+    s.act = std::max(s.act, size_t(T) * C);
+  }
+  conv(m->down, T);
+  s.qk = std::max(s.qk, size_t(T) * std::max(m->d, m->ff));
   return s;
 }
 
@@ -221,7 +268,10 @@ void mimi_product(grx_mimi_streams* s, const MW& w, const MIn& in, int T, const 
     }
     s->launches++;
   }
-  if (mf < T) {
+  if (mf < T && K % 4) {  // K < 16: dotF32Go alone
+    launch_mimi_gemv_small(in.x, in.ldx, in.sstride, T, mf, w.f, N, K, bias, y, resid, n, st);
+    s->launches++;
+  } else if (mf < T) {
     FArgs a;
     a.epi = resid ? FE_RESID : FE_BIAS;
     a.x = in.x;
@@ -303,14 +353,14 @@ void mimi_conv(grx_mimi_streams* s, const MConv& c, int ci, const float* x, int 
 
 // transformer.forward (nn.go:142-182) with the window and layer scales for
 // the S rows of every stream in s->x.
-void mimi_transformer(grx_mimi_streams* s) {
+void mimi_transformer(grx_mimi_streams* s, int S) {
   grx_mimi* m = s->m;
-  const int n = s->n, S = m->S, R = n * S, d = m->d, L = int(m->layers.size());
+  const int n = s->n, R = n * S, d = m->d, L = int(s->layers->size());
   cudaStream_t st = s->st;
   launch_mimi_rows(s->pos, S, R, s->rowpos, st);
   s->launches++;
   for (int l = 0; l < L; l++) {
-    const MLayer& ly = m->layers[size_t(l)];
+    const MLayer& ly = (*s->layers)[size_t(l)];
     LnArgs ln;
     ln.x = s->x;
     ln.w = ly.n1w;
@@ -382,7 +432,7 @@ void mimi_enqueue(grx_mimi_streams* s, const float* d_lat, float* d_pcm) {
   mimi_product(s, m->quant, MIn{d_lat, m->ldim, 1, m->ldim, 0}, 1, nullptr, s->z, false);
   launch_mimi_up(s->z, m->up, s->up_part[s->par], s->x, s->up_part[s->par ^ 1], n, S, C, st);
   s->launches++;
-  mimi_transformer(s);
+  mimi_transformer(s, S);
   float* x = s->x;
   int T = S, Cc = C;
   size_t ci = 0;
@@ -435,7 +485,7 @@ int mimi_reset(grx_mimi_streams* s) {
   CK(cudaMemsetAsync(s->pos, 0, sizeof(int) * size_t(n), s->st));
   CK(cudaMemsetAsync(s->started, 0, sizeof(int) * size_t(n), s->st));
   for (int b = 0; b < 2; b++) {
-    CK(cudaMemsetAsync(s->up_part[b], 0, sizeof(float) * size_t(n) * m->S * m->d, s->st));
+    if (s->up_part[b]) CK(cudaMemsetAsync(s->up_part[b], 0, sizeof(float) * size_t(n) * m->S * m->d, s->st));
     for (size_t i = 0; i < s->carry_n.size(); i++)
       if (s->carry_n[i]) CK(cudaMemsetAsync(s->carry[b][i], 0, sizeof(float) * size_t(n) * s->carry_n[i], s->st));
   }
@@ -445,12 +495,141 @@ int mimi_reset(grx_mimi_streams* s) {
   return GRX_OK;
 }
 
+// What every set holds, for s->layers, s->steps and s->S rows per
+// transformer call: the transformer's caches (rings of s->ring positions)
+// and activations, the step buffers sized by z, the carried rows of every
+// step (and of `extra`, a last convolution), the row tables for S rows and
+// the RoPE table of `positions` positions.
+int set_init(grx_mimi_streams* s, const MimiSizes& z, size_t positions, const MConv* extra) {
+  grx_mimi* m = s->m;
+  const int S = s->S, d = m->d, L = int(s->layers->size()), H = m->heads, hd = 64;
+  const size_t N = size_t(s->n), R = N * S;
+  int rc = 0;
+  s->kv = s->ar.alloc<float>(N * L * 2 * H * s->ring * hd, &rc);
+  s->pos = s->ar.alloc<int>(N, &rc);
+  s->started = s->ar.alloc<int>(N, &rc);
+  s->rowpos = s->ar.alloc<int>(R, &rc);
+  int* stat = s->ar.alloc<int>(R + 3 * N, &rc);
+  s->x = s->ar.alloc<float>(R * d, &rc);
+  s->qb = s->ar.alloc<float>(R * d, &rc);
+  s->xq = s->ar.alloc<int8_t>(R * d, &rc);
+  s->xs = s->ar.alloc<float2>(R * d / 32, &rc);
+  s->fq = s->ar.alloc<int8_t>(R * m->ff, &rc);
+  s->fs = s->ar.alloc<float2>(R * m->ff / 32, &rc);
+  s->aq = s->ar.alloc<int8_t>(N * z.qk, &rc);
+  s->as = s->ar.alloc<float2>(N * z.qk / 32 + 1, &rc);
+  s->sa = s->ar.alloc<float>(N * z.act, &rc);
+  s->sb = s->ar.alloc<float>(N * z.act, &rc);
+  s->se = s->ar.alloc<float>(N * z.act, &rc);
+  s->stage = s->ar.alloc<float>(N * z.stage, &rc);
+  s->col = s->ar.alloc<float>(N * z.col, &rc);
+  s->zt = s->ar.alloc<float>(N * z.zt, &rc);
+  s->sh = s->ar.alloc<float>(N * z.h, &rc);
+  for (const MStep& st : *s->steps) {
+    if (st.kind == 0) s->carry_n.push_back(size_t(st.c.past()) * st.c.cin);
+    if (st.kind == 1) s->carry_n.push_back(size_t(st.c.k - st.c.stride) * st.c.cout);
+    if (st.kind == 2) {
+      s->carry_n.push_back(size_t(st.ra.past()) * st.ra.cin);
+      s->carry_n.push_back(size_t(st.rb.past()) * st.rb.cin);
+    }
+  }
+  if (extra) s->carry_n.push_back(size_t(extra->past()) * extra->cin);
+  for (int b = 0; b < 2; b++)
+    for (size_t c : s->carry_n) s->carry[b].push_back(s->ar.alloc<float>(N * std::max<size_t>(c, 1), &rc));
+  if (rc) return rc;
+  // static row tables: row r is stream r / S; call-stream i is rows i·S ..
+  {
+    std::vector<int> h(R + 3 * N);
+    for (size_t r = 0; r < R; r++) h[r] = int(r / S);
+    for (size_t i = 0; i < N; i++) {
+      h[R + i] = int(i) * S;
+      h[R + N + i] = S;
+      h[R + 2 * N + i] = int(i);
+    }
+    CK(cudaMemcpy(stat, h.data(), sizeof(int) * h.size(), cudaMemcpyHostToDevice));
+    s->rowslot = stat;
+    s->crow0 = stat + R;
+    s->cT = stat + R + N;
+    s->cslot = stat + R + 2 * N;
+    s->rows_for = S;
+  }
+  // RoPE cos/sin for every position the streams can reach (nn.go:84-85)
+  {
+    std::vector<float> t(positions * hd);
+    for (size_t p = 0; p < positions; p++)
+      for (int i = 0; i < hd / 2; i++) {
+        double a = double(m->freqs[size_t(i)] * float(p));
+        t[(p * (hd / 2) + i) * 2] = float(std::cos(a));
+        t[(p * (hd / 2) + i) * 2 + 1] = float(std::sin(a));
+      }
+    s->rope = s->ar.upload(t.data(), t.size(), &rc);
+  }
+  return rc;
+}
+
 int check_frames(grx_mimi_streams* s, int frames) {
   if (frames < 0) return fail(GRX_EINVAL, "grx_mimi: a negative frame count");
   if (s->frames + frames > s->max_frames)
     return fail(GRX_ERANGE, "grx_mimi: the streams hold " + std::to_string(s->frames) + " frames; " +
                                 std::to_string(frames) + " more pass the " + std::to_string(s->max_frames) +
                                 " they were made for");
+  return GRX_OK;
+}
+
+// encode (mimi.go:164-179) as cloneCond runs it (voice.go:113-124), for
+// every clip of the set: the clips (d_pcm [n][samples]) padded with zeros
+// to whole frames, then twelve frames at a time through the SEANet
+// encoder, the transformer and the downsampling convolution with one state
+// per clip; d_lat [n][frames][ldim]. Queued on the set's stream.
+int enc_run(grx_mimi_streams* s, int samples, const float* d_pcm, float* d_lat) {
+  grx_mimi* m = s->m;
+  const int n = s->n, frame = m->frame, d = m->d, ldim = m->ldim, S = m->S, piece = 12 * frame;
+  const int frames = (samples + frame - 1) / frame, padded = frames * frame;
+  cudaStream_t st = s->st;
+  int rc = mimi_reset(s);
+  if (rc) return rc;
+  CK(cudaMemsetAsync(s->clip, 0, sizeof(float) * size_t(n) * padded, st));
+  CK(cudaMemcpy2DAsync(s->clip, sizeof(float) * padded, d_pcm, sizeof(float) * samples, sizeof(float) * samples, n,
+                       cudaMemcpyDeviceToDevice, st));
+  const size_t down_ci = s->carry_n.size() - 1;
+  auto other = [&](const float* p) { return p == s->sa ? s->sb : s->sa; };
+  for (int p0 = 0; p0 < padded; p0 += piece) {
+    const int T0 = std::min(piece, padded - p0);
+    CK(cudaMemcpy2DAsync(s->sa, sizeof(float) * T0, s->clip + p0, sizeof(float) * padded, sizeof(float) * T0, n,
+                         cudaMemcpyDeviceToDevice, st));
+    float* x = s->sa;
+    int T = T0;
+    size_t ci = 0;
+    for (const MStep& stp : m->enc_steps) {
+      if (stp.kind == 0) {
+        float* y = other(x);
+        mimi_conv(s, stp.c, int(ci++), x, T, stp.elu, y, false);
+        T /= stp.c.stride;
+        x = y;
+      } else {
+        // x + conv1x1(ELU(conv(ELU(x)))), the sum added into x in place
+        mimi_conv(s, stp.ra, int(ci), x, T, true, s->sh, false);
+        mimi_conv(s, stp.rb, int(ci + 1), s->sh, T, true, x, true);
+        ci += 2;
+      }
+    }
+    CK(cudaMemcpyAsync(s->x, x, sizeof(float) * size_t(n) * T * d, cudaMemcpyDeviceToDevice, st));
+    if (T != s->rows_for) {
+      launch_mimi_rowtab(T, n, s->rowslot, s->crow0, s->cT, s->cslot, st);
+      s->launches++;
+      s->rows_for = T;
+    }
+    mimi_transformer(s, T);
+    if (p0 == 0) {  // the first call's padding: copies of the first row
+      launch_mimi_replicate(s->x, T, d, s->carry[s->par][down_ci], m->down.past(), n, st);
+      s->launches++;
+    }
+    mimi_conv(s, m->down, int(down_ci), s->x, T, false, s->piece_lat, false);
+    const int fr = T / S;
+    CK(cudaMemcpy2DAsync(d_lat + size_t(p0 / frame) * ldim, sizeof(float) * frames * ldim, s->piece_lat,
+                         sizeof(float) * fr * ldim, sizeof(float) * fr * ldim, n, cudaMemcpyDeviceToDevice, st));
+    s->par ^= 1;
+  }
   return GRX_OK;
 }
 
@@ -505,12 +684,14 @@ int grx_mimi_load(const void* bytes, size_t len, int device, grx_mimi** out) {
     w.rows = int(rows);
     w.cols = int(cols);
     if (t.type == G_Q8_0) {
-      if (rows % 32 || cols > 4096)
-        err = "pockettts: " + name + " is a Q8_0 matrix outside what the kernels take (rows % 32, cols <= 4096)";
+      if (rows % 32 || cols > kQ8GemvMaxK)
+        err = "pockettts: " + name + " is a Q8_0 matrix outside what the kernels take (rows % 32, cols <= " +
+              std::to_string(kQ8GemvMaxK) + ")";
       w.q8 = true;
       w.q = upload_q8(m->ar, t.data, w.rows, w.cols, &rc);
     } else if (t.type == G_F32) {
-      if (cols % 4) err = "pockettts: " + name + " is a float32 matrix outside what the kernels take (cols % 4)";
+      if (cols % 4 && cols >= 16)
+        err = "pockettts: " + name + " is a float32 matrix outside what the kernels take (cols % 4)";
       std::vector<float> v;
       f.float32(name, v);
       w.f = m->ar.upload(v.data(), v.size(), &rc);
@@ -625,6 +806,65 @@ int grx_mimi_load(const void* bytes, size_t len, int device, grx_mimi** out) {
     last.c = conv("mimi.dec." + std::to_string(idx), nf, 1, lastk, 1, 1);
     m->steps.push_back(last);
   }
+  // the encoder (loader.encoder and the mimi.enc_tf transformer, model.go:
+  // 181-200; mimi.down, 308-313), when the file has one
+  if (f.has("mimi.enc.0.weight")) {
+    m->has_enc = true;
+    m->hop = hop;
+    for (int i = 0;; i++) {
+      const std::string p = "mimi.enc_tf." + std::to_string(i) + ".";
+      if (!f.has(p + "norm1.weight")) break;
+      MLayer ly;
+      ly.n1w = vec(p + "norm1.weight", d);
+      ly.n1b = vec(p + "norm1.bias", d);
+      ly.n2w = vec(p + "norm2.weight", d);
+      ly.n2b = vec(p + "norm2.bias", d);
+      MW qkv = mat(p + "attn_qkv.weight", 3 * d, d), o = mat(p + "attn_out.weight", d, d);
+      MW f1 = mat(p + "ff1.weight", ff, d), f2 = mat(p + "ff2.weight", d, ff);
+      ly.ls1 = vec(p + "ls1", d);
+      ly.ls2 = vec(p + "ls2", d);
+      if (err.empty() && !(qkv.q8 && o.q8 && f1.q8 && f2.q8))
+        err = "pockettts: " + p + "* are not all Q8_0 (this build runs the transformer's products on the int8 path)";
+      ly.qkv = qkv.q;
+      ly.out = o.q;
+      ly.ff1 = f1.q;
+      ly.ff2 = f2.q;
+      m->enc_layers.push_back(ly);
+    }
+    if (err.empty() && m->enc_layers.empty()) err = "pockettts: no mimi.enc_tf layers";
+    MStep first;
+    first.c = conv("mimi.enc.0", 1, nf, k, 1, 1);
+    m->enc_steps.push_back(first);
+    int eidx = 1, emult = 1;
+    for (int ri = int(ratios.size()) - 1; ri >= 0; ri--) {
+      const int r = ratios[size_t(ri)], rdim = emult * nf;
+      for (int j = 0, dl = 1; j < nres; j++, dl *= dil) {
+        const std::string p = "mimi.enc." + std::to_string(eidx) + ".";
+        MStep rb;
+        rb.kind = 2;
+        rb.ra = conv(p + "1", rdim, rdim / comp, resk, 1, dl);
+        rb.rb = conv(p + "3", rdim / comp, rdim, 1, 1, 1);
+        m->enc_steps.push_back(rb);
+        eidx++;
+      }
+      eidx++;  // the ELU
+      MStep cv;
+      cv.elu = true;
+      cv.c = conv("mimi.enc." + std::to_string(eidx), rdim, 2 * rdim, 2 * r, r, 1);
+      m->enc_steps.push_back(cv);
+      eidx++;
+      emult *= 2;
+    }
+    eidx++;
+    MStep elast;
+    elast.elu = true;
+    elast.c = conv("mimi.enc." + std::to_string(eidx), emult * nf, d, lastk, 1, 1);
+    m->enc_steps.push_back(elast);
+    m->down.w = mat("mimi.down", m->ldim, int64_t(2) * m->S * d);
+    const std::vector<float> zeros(size_t(m->ldim), 0.f);  // no bias: gemvRows still adds one of zeros
+    m->down.b = m->ar.upload(zeros.data(), zeros.size(), &rc);
+    m->down.cin = d, m->down.cout = m->ldim, m->down.k = 2 * m->S, m->down.stride = m->S, m->down.dil = 1;
+  }
   if (!err.empty()) return fail(GRX_EFORMAT, err);
   if (rc) return rc;
   *out = m.release();
@@ -649,7 +889,7 @@ int grx_mimi_dims(const grx_mimi* m, int* d, int* heads, int* layers, int* conte
 
 int grx_mimi_streams_create(grx_mimi* m, int n, int max_frames, grx_mimi_streams** out) {
   if (!m || !out || n < 1 || n > 65535 || max_frames < 1) return fail(GRX_EINVAL, "grx_mimi_streams_create: bad argument");
-  const int S = m->S, d = m->d, L = int(m->layers.size()), H = m->heads, hd = 64;
+  const int S = m->S, d = m->d;
   if (int64_t(max_frames) * S > (int64_t(1) << 30)) return fail(GRX_ERANGE, "grx_mimi_streams_create: too many frames");
   int rc = device_init(m->dev);
   if (rc) return rc;
@@ -657,75 +897,20 @@ int grx_mimi_streams_create(grx_mimi* m, int n, int max_frames, grx_mimi_streams
   auto s = std::make_unique<grx_mimi_streams>();
   s->ar.dev = m->dev;
   s->m = m;
+  s->layers = &m->layers;
+  s->steps = &m->steps;
+  s->S = S;
   s->n = n;
   s->max_frames = max_frames;
   s->ring = std::min(m->context + S - 1, max_frames * S);
   CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
-  const MimiSizes z = mimi_sizes(m);
-  const size_t N = size_t(n), R = N * S;
-  s->kv = s->ar.alloc<float>(N * L * 2 * H * s->ring * hd, &rc);
-  s->pos = s->ar.alloc<int>(N, &rc);
-  s->started = s->ar.alloc<int>(N, &rc);
-  s->rowpos = s->ar.alloc<int>(R, &rc);
-  int* stat = s->ar.alloc<int>(R + 3 * N, &rc);
+  const size_t N = size_t(n);
+  rc = set_init(s.get(), mimi_sizes(m), size_t(max_frames) * S, nullptr);
   s->lat = s->ar.alloc<float>(N * m->ldim, &rc);
   s->z = s->ar.alloc<float>(N * d, &rc);
-  s->x = s->ar.alloc<float>(R * d, &rc);
-  s->qb = s->ar.alloc<float>(R * d, &rc);
-  s->xq = s->ar.alloc<int8_t>(R * d, &rc);
-  s->xs = s->ar.alloc<float2>(R * d / 32, &rc);
-  s->fq = s->ar.alloc<int8_t>(R * m->ff, &rc);
-  s->fs = s->ar.alloc<float2>(R * m->ff / 32, &rc);
-  s->aq = s->ar.alloc<int8_t>(N * z.qk, &rc);
-  s->as = s->ar.alloc<float2>(N * z.qk / 32 + 1, &rc);
-  s->sa = s->ar.alloc<float>(N * z.act, &rc);
-  s->sb = s->ar.alloc<float>(N * z.act, &rc);
-  s->se = s->ar.alloc<float>(N * z.act, &rc);
-  s->stage = s->ar.alloc<float>(N * z.stage, &rc);
-  s->col = s->ar.alloc<float>(N * z.col, &rc);
-  s->zt = s->ar.alloc<float>(N * z.zt, &rc);
-  s->sh = s->ar.alloc<float>(N * z.h, &rc);
   s->pcm = s->ar.alloc<float>(N * m->frame, &rc);
   for (int b = 0; b < 2; b++) s->up_part[b] = s->ar.alloc<float>(N * S * d, &rc);
-  for (const MStep& st : m->steps) {
-    if (st.kind == 0) s->carry_n.push_back(size_t(st.c.past()) * st.c.cin);
-    if (st.kind == 1) s->carry_n.push_back(size_t(st.c.k - st.c.stride) * st.c.cout);
-    if (st.kind == 2) {
-      s->carry_n.push_back(size_t(st.ra.past()) * st.ra.cin);
-      s->carry_n.push_back(size_t(st.rb.past()) * st.rb.cin);
-    }
-  }
-  for (int b = 0; b < 2; b++)
-    for (size_t c : s->carry_n) s->carry[b].push_back(s->ar.alloc<float>(N * std::max<size_t>(c, 1), &rc));
   if (rc) return rc;
-  // static row tables: row r is stream r / S; call-stream i is rows i·S ..
-  {
-    std::vector<int> h(R + 3 * N);
-    for (size_t r = 0; r < R; r++) h[r] = int(r / S);
-    for (size_t i = 0; i < N; i++) {
-      h[R + i] = int(i) * S;
-      h[R + N + i] = S;
-      h[R + 2 * N + i] = int(i);
-    }
-    CK(cudaMemcpy(stat, h.data(), sizeof(int) * h.size(), cudaMemcpyHostToDevice));
-    s->rowslot = stat;
-    s->crow0 = stat + R;
-    s->cT = stat + R + N;
-    s->cslot = stat + R + 2 * N;
-  }
-  // RoPE cos/sin for every position the streams can reach (nn.go:84-85)
-  {
-    const size_t P = size_t(max_frames) * S;
-    std::vector<float> t(P * hd);
-    for (size_t p = 0; p < P; p++)
-      for (int i = 0; i < hd / 2; i++) {
-        double a = double(m->freqs[size_t(i)] * float(p));
-        t[(p * (hd / 2) + i) * 2] = float(std::cos(a));
-        t[(p * (hd / 2) + i) * 2 + 1] = float(std::sin(a));
-      }
-    s->rope = s->ar.upload(t.data(), t.size(), &rc);
-    if (rc) return rc;
-  }
   rc = mimi_reset(s.get());
   if (rc) return rc;
   *out = s.release();
@@ -733,6 +918,97 @@ int grx_mimi_streams_create(grx_mimi* m, int n, int max_frames, grx_mimi_streams
 }
 
 void grx_mimi_streams_free(grx_mimi_streams* s) { delete s; }
+
+int grx_mimi_encoder_create(grx_mimi* m, int n, int max_samples, grx_mimi_streams** out) {
+  if (!m || !out || n < 1 || n > 65535 || max_samples < 1)
+    return fail(GRX_EINVAL, "grx_mimi_encoder_create: bad argument");
+  if (!m->has_enc) return fail(GRX_EINVAL, "pockettts: this model file has no voice cloning");
+  const int frame = m->frame, S = m->S;
+  const int64_t frames = (int64_t(max_samples) + frame - 1) / frame;
+  if (frames * frame * int64_t(n) > (int64_t(1) << 31)) return fail(GRX_ERANGE, "grx_mimi_encoder_create: too many samples");
+  int rc = device_init(m->dev);
+  if (rc) return rc;
+  CK(cudaSetDevice(m->dev));
+  auto s = std::make_unique<grx_mimi_streams>();
+  s->ar.dev = m->dev;
+  s->m = m;
+  s->layers = &m->enc_layers;
+  s->steps = &m->enc_steps;
+  const int T0 = int(std::min<int64_t>(12 * frame, frames * frame));
+  s->S = T0 / m->hop;  // transformer rows of the longest piece
+  s->n = n;
+  s->max_samples = max_samples;
+  s->max_frames = int(frames);
+  s->ring = int(std::min<int64_t>(m->context + s->S - 1, frames * S));
+  CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+  rc = set_init(s.get(), enc_sizes(m, T0), size_t(frames) * S, &m->down);
+  s->clip = s->ar.alloc<float>(size_t(n) * frames * frame, &rc);
+  s->piece_lat = s->ar.alloc<float>(size_t(n) * 12 * m->ldim, &rc);
+  if (rc) return rc;
+  rc = mimi_reset(s.get());
+  if (rc) return rc;
+  *out = s.release();
+  return GRX_OK;
+}
+
+int grx_mimi_encode_device(grx_mimi_streams* s, int samples, const float* d_pcm, float* d_latents) {
+  if (!s || !d_pcm || !d_latents) return fail(GRX_EINVAL, "grx_mimi_encode_device: null argument");
+  if (!s->clip) return fail(GRX_EINVAL, "grx_mimi_encode_device: not an encoder set");
+  if (samples < 1 || samples > s->max_samples)
+    return fail(GRX_ERANGE, "grx_mimi_encode: " + std::to_string(samples) + " samples for a set made for 1.." +
+                                std::to_string(s->max_samples));
+  CK(cudaSetDevice(s->ar.dev));
+  int rc = enc_run(s, samples, d_pcm, d_latents);
+  if (rc) return rc;
+  CK(cudaGetLastError());
+  return GRX_OK;
+}
+
+int grx_mimi_encode(grx_mimi_streams* s, int samples, const float* pcm, float* latents) {
+  if (!s || !pcm || !latents) return fail(GRX_EINVAL, "grx_mimi_encode: null argument");
+  if (!s->clip) return fail(GRX_EINVAL, "grx_mimi_encode: not an encoder set");
+  if (samples < 1 || samples > s->max_samples)
+    return fail(GRX_ERANGE, "grx_mimi_encode: " + std::to_string(samples) + " samples for a set made for 1.." +
+                                std::to_string(s->max_samples));
+  grx_mimi* m = s->m;
+  const int frames = (samples + m->frame - 1) / m->frame;
+  CK(cudaSetDevice(s->ar.dev));
+  Arena tmp;
+  tmp.dev = s->ar.dev;
+  int rc = 0;
+  float* d_pcm = tmp.alloc<float>(size_t(s->n) * samples, &rc);
+  float* d_lat = tmp.alloc<float>(size_t(s->n) * frames * m->ldim, &rc);
+  if (rc) return rc;
+  CK(cudaMemcpyAsync(d_pcm, pcm, sizeof(float) * size_t(s->n) * samples, cudaMemcpyHostToDevice, s->st));
+  rc = enc_run(s, samples, d_pcm, d_lat);
+  if (rc) return rc;
+  CK(cudaMemcpyAsync(latents, d_lat, sizeof(float) * size_t(s->n) * frames * m->ldim, cudaMemcpyDeviceToHost, s->st));
+  CK(cudaStreamSynchronize(s->st));
+  CK(cudaGetLastError());
+  return GRX_OK;
+}
+
+int grx_mimi_clone_latents(grx_mimi* m, const float* pcm, int samples, float* latents, int* frames) {
+  if (!m || !pcm || !latents || samples < 1) return fail(GRX_EINVAL, "grx_mimi_clone_latents: bad argument");
+  grx_mimi_streams* s = nullptr;
+  int rc = grx_mimi_encoder_create(m, 1, samples, &s);
+  if (rc) return rc;
+  rc = grx_mimi_encode(s, samples, pcm, latents);
+  grx_mimi_streams_free(s);
+  if (rc) return rc;
+  if (frames) *frames = (samples + m->frame - 1) / m->frame;
+  return GRX_OK;
+}
+
+int grx_voice_clone(grx_flowlm* lm, grx_mimi* m, const float* pcm, int samples, grx_voice** out) {
+  if (!lm || !m || !pcm || !out || samples < 1) return fail(GRX_EINVAL, "grx_voice_clone: bad argument");
+  const int frames = (samples + m->frame - 1) / m->frame;
+  std::vector<float> lat(size_t(frames) * m->ldim);
+  int rc = grx_mimi_clone_latents(m, pcm, samples, lat.data(), nullptr);
+  if (rc) return rc;
+  return grx_voice_from_latents(lm, lat.data(), frames, out);
+}
+
 
 int grx_mimi_streams_reset(grx_mimi_streams* s) {
   if (!s) return fail(GRX_EINVAL, "null stream set");

@@ -218,8 +218,10 @@ typedef struct grx_mimi_streams grx_mimi_streams;
  * the same shape checks. Q8_0 matrices take the int8 path (the reference
  * packs them and drops their rows), float32 ones MatMul's float path. This
  * build takes 64-value heads, Q8_0 transformer matrices, Q8_0 matrices
- * with rows % 32 == 0 and cols <= 4096 and float32 ones with cols % 4 == 0;
- * other files give GRX_EINVAL or GRX_EFORMAT. */
+ * with rows % 32 == 0 and cols <= 16384 and float32 ones with cols % 4 == 0
+ * or cols < 16; other files give GRX_EINVAL or GRX_EFORMAT. A file with
+ * Mimi's encoder (mimi.enc.*, mimi.enc_tf.*, mimi.down: model.go:181-200,
+ * 308-313) also loads it, for grx_mimi_encoder_create. */
 int grx_mimi_load(const void* gguf, size_t len, int device, grx_mimi** out);
 void grx_mimi_free(grx_mimi* m);
 /* d, heads, transformer layers, context, upsampling stride, latent dim,
@@ -249,6 +251,31 @@ void* grx_mimi_cuda_stream(const grx_mimi_streams* s);
 int64_t grx_mimi_launches(const grx_mimi_streams* s);
 /* Frames decoded since creation or the last reset. */
 int grx_mimi_frames(const grx_mimi_streams* s);
+
+/* ------------------------------------------- Pocket TTS Mimi encoder ----
+ * mimiEncoder.encode (pockettts/mimi.go:152-179) as cloneCond runs it
+ * (voice.go:113-124): the SEANet encoder, the windowed transformer and the
+ * downsampling convolution to the latent rate, streaming over pieces of
+ * twelve frames. The clip is 24 kHz audio after CloneVoice's resampling and
+ * end_on_pause (voice.go:85-93, host work). */
+/* A set of n clips of up to max_samples samples each; needs a model file
+ * with the encoder (GRX_EINVAL otherwise). grx_mimi_streams_free frees it. */
+int grx_mimi_encoder_create(grx_mimi* m, int n, int max_samples, grx_mimi_streams** out);
+/* Every clip (d_pcm [n][samples], device) padded with zeros to whole frames
+ * and encoded twelve frames at a time with one state per clip, from a fresh
+ * state: d_latents [n][frames][ldim], frames = ceil(samples / frame).
+ * Asynchronous on the set's stream; grx_mimi_sync waits. */
+int grx_mimi_encode_device(grx_mimi_streams* s, int samples, const float* d_pcm, float* d_latents);
+/* The same from and to host memory (pcm [n][samples], latents
+ * [n][frames][ldim]). Synchronous. */
+int grx_mimi_encode(grx_mimi_streams* s, int samples, const float* pcm, float* latents);
+/* cloneCond's encoding of one clip: latents [frames][ldim] (room for
+ * ceil(samples / frame) rows), *frames (may be NULL) the row count. */
+int grx_mimi_clone_latents(grx_mimi* m, const float* pcm, int samples, float* latents, int* frames);
+/* Model.CloneVoice after resampling and end_on_pause (voice.go:94-106):
+ * the Mimi encoding of the clip (grx_mimi_clone_latents), then the flow-LM
+ * half (grx_voice_from_latents). */
+int grx_voice_clone(grx_flowlm* lm, grx_mimi* mimi, const float* pcm, int samples, grx_voice** out);
 
 /* ----------------------------------------- FastConformer encoder --------
  * conformer.Model.encode (conformer/encoder.go:123-489): the 8x
