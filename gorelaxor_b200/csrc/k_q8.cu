@@ -18,6 +18,9 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <type_traits>
+#include <unordered_map>
+
 #include <cstddef>
 #include <cstdlib>
 #include <cstdint>
@@ -831,6 +834,202 @@ __global__ void __launch_bounds__(TcCfg<BN, EPW>::NT, 1)
 }
 
 
+// ------------------------------------- GEMM, mma.sync fed by TMA --
+//
+// k_q8_gemm4: k_q8_gemm2's tiles, fold order and epilogues, with the loads
+// taken off the computing warps. One producer warp issues each stage's four
+// TMA copies (activation and weight tiles in the 128-byte swizzle — the
+// XOR layout k_q8_gemm2's ldmatrix addressing already reads — the
+// activation scales and the {dw, dw', nm, nm'} quads) on a full barrier;
+// the consumer warps wait on it, run the stage's four blocks (their MMAs
+// issued before the first fold) and arrive on the stage's empty barrier.
+// A full stage runs without block-count checks; the activation scales of a
+// stage are read once. Waits are bounded as in k_q8_tc (its fault word).
+template <int TM, int TN, int WGM, int WGN, int STAGES>
+struct Cfg4 {
+  using B = Cfg2<TM, TN, WGM, WGN>;
+  static constexpr int NWC = WGM * WGN, NT = 32 * (NWC + 1);
+  static constexpr int TX = B::BM * 128 + B::BN * 128 + B::BM * B::KB * 8 + B::KB * B::BN * 8;
+  static constexpr int OFF_BAR = STAGES * B::SST;
+  static constexpr int SMEM = 1024 + OFF_BAR + 2 * STAGES * 8;  // + alignment slack
+  static_assert(B::BM % 8 == 0 && B::SST % 1024 == 0, "swizzled tiles start on 1024-byte boundaries");
+};
+
+template <int TM, int TN, int WGM, int WGN, int STAGES>
+__global__ void __launch_bounds__(Cfg4<TM, TN, WGM, WGN, STAGES>::NT)
+    k_q8_gemm4(const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mw,
+               const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap md, int M, int N, int nb,
+               EpiArgs e) {
+  using C4 = Cfg4<TM, TN, WGM, WGN, STAGES>;
+  using C = typename C4::B;
+  constexpr int BM = C::BM, BN = C::BN, NWC = C4::NWC, KB = C::KB;
+  static_assert(TN % 2 == 0, "B fragments two column tiles at a time");
+  extern __shared__ uint8_t g4_raw[];
+  const uint32_t raw = smem_u32(g4_raw), sbase = (raw + 1023) & ~1023u;
+  uint8_t* gbase = g4_raw + (sbase - raw);
+  const uint32_t bars = sbase + C4::OFF_BAR;
+  auto full = [&](int s) { return bars + 8 * s; };
+  auto empty = [&](int s) { return bars + 8 * (STAGES + s); };
+  __shared__ int dead_s;
+  volatile int* dead = &dead_s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int nkt = (nb + KB - 1) / KB;
+  if (tid == 0) {
+    dead_s = 0;
+    for (int s = 0; s < STAGES; s++) {
+      mb_init(full(s), 1);
+      mb_init(empty(s), NWC);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+
+  f2 acc[TM][TN][2];
+  const int wm = warp / WGN, wn = warp % WGN, arow = wm * 16 * TM, brow = wn * 8 * TN;
+  if (warp == NWC) {
+    // ---- the producer warp
+    int issued = 0;
+    for (int kt = 0; kt < nkt; kt++) {
+      const int s = kt % STAGES;
+      if (!__all_sync(FULL, mb_wait(empty(s), ((kt / STAGES) & 1) ^ 1, dead))) break;
+      const uint32_t sb = sbase + s * C::SST;
+      mb_expect_one(full(s), C4::TX);
+      tma2d(sb + C::OFF_A, &ma, kt * 128, m0, full(s));
+      tma2d(sb + C::OFF_W, &mw, kt * 128, n0, full(s));
+      tma2d(sb + C::OFF_SA, &ms, kt * 8, m0, full(s));
+      tma2d(sb + C::OFF_DN, &md, n0 * 2, kt * KB, full(s));
+      issued = kt + 1;
+    }
+    // After a failure, let this block's copies land before it goes on.
+    if (*dead)
+      for (int kt = issued > STAGES ? issued - STAGES : 0; kt < issued; kt++) {
+        const long long t0 = clock64();
+        while (!mb_try(full(kt % STAGES), (kt / STAGES) & 1) && clock64() - t0 < (1LL << 30)) {
+        }
+      }
+  } else {
+    // ---- the consumer warps: fragment offsets within a stage
+    const int mat = lane >> 3;
+    uint32_t aoff[TM], boff[TN / 2];
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+      const int ra = arow + i * 16 + (lane & 7) + (mat & 1) * 8;
+      aoff[i] = C::OFF_A + ra * 128 + (((mat >> 1) ^ (ra & 7)) << 4);
+    }
+#pragma unroll
+    for (int j = 0; j < TN / 2; j++) {
+      const int rb = brow + j * 16 + (lane & 7) + (mat >> 1) * 8;
+      boff[j] = C::OFF_W + rb * 128 + (((mat & 1) ^ (rb & 7)) << 4);
+    }
+    uint32_t soff[TM], doff[TN];
+#pragma unroll
+    for (int i = 0; i < TM; i++) soff[i] = C::OFF_SA + (arow + i * 16 + g) * 32;
+#pragma unroll
+    for (int j = 0; j < TN; j++) doff[j] = C::OFF_DN + ((brow + j * 8) / 2 + t4) * 16;
+    // Each output's chain starts at its bias, or 0 (q8int.go:175-182).
+#pragma unroll
+    for (int j = 0; j < TN; j++) {
+      const int c0 = n0 + brow + j * 8 + 2 * t4;
+      const f2 b = f2make(e.bias && c0 < N ? e.bias[c0] : 0.f, e.bias && c0 + 1 < N ? e.bias[c0 + 1] : 0.f);
+#pragma unroll
+      for (int i = 0; i < TM; i++) acc[i][j][0] = acc[i][j][1] = b;
+    }
+    // The MMAs of a stage's first nbl blocks, then their folds in block order.
+    auto stage = [&](uint32_t cur, int nbl, auto whole_c) {
+      constexpr bool whole = decltype(whole_c)::value;
+      f2 da[TM][2][KB];
+#pragma unroll
+      for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+          for (int kk = 0; kk < KB; kk += 2)
+            asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];\n"
+                         : "=l"(da[i][h][kk]), "=l"(da[i][h][kk + 1])
+                         : "r"(cur + soff[i] + h * 8 * 32 + kk * 8));
+      f2 p[KB][TM][TN][2];
+#pragma unroll
+      for (int kk = 0; kk < KB; kk++) {
+        if (!whole && kk >= nbl) break;
+        const uint32_t kl = uint32_t(2 * kk) << 4;  // the block's first chunk (the swizzle keeps bit 0)
+        uint32_t af[TM][4], bf[TN][2];
+#pragma unroll
+        for (int i = 0; i < TM; i++) ldsm_x4(af[i][0], af[i][1], af[i][2], af[i][3], (cur + aoff[i]) ^ kl);
+#pragma unroll
+        for (int j = 0; j < TN / 2; j++)
+          ldsm_x4(bf[2 * j][0], bf[2 * j][1], bf[2 * j + 1][0], bf[2 * j + 1][1], (cur + boff[j]) ^ kl);
+#pragma unroll
+        for (int i = 0; i < TM; i++)
+#pragma unroll
+          for (int j = 0; j < TN; j++) q8_mma(p[kk][i][j][0], p[kk][i][j][1], af[i], bf[j][0], bf[j][1]);
+      }
+#pragma unroll
+      for (int kk = 0; kk < KB; kk++) {
+        if (!whole && kk >= nbl) break;
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+          f2 dw, nm;
+          asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];\n" : "=l"(dw), "=l"(nm) : "r"(cur + doff[j] + kk * (BN / 2) * 16));
+#pragma unroll
+          for (int i = 0; i < TM; i++)
+            q8_fold(acc[i][j][0], acc[i][j][1], p[kk][i][j][0], p[kk][i][j][1], dw, nm, da[i][0][kk], da[i][1][kk]);
+        }
+      }
+    };
+    for (int kt = 0; kt < nkt; kt++) {
+      const int s = kt % STAGES;
+      if (!__all_sync(FULL, mb_wait(full(s), (kt / STAGES) & 1, dead))) break;
+      const uint32_t cur = sbase + s * C::SST;
+      const int nbl = nb - kt * KB;
+      if (nbl >= KB)
+        stage(cur, KB, std::true_type{});
+      else
+        stage(cur, nbl, std::false_type{});
+      __syncwarp();
+      if (lane == 0) mb_arrive(empty(s));
+    }
+  }
+  __syncthreads();  // every stage consumed (or abandoned), every copy landed
+  if (e.epi == EPI_GELU_Q8) {
+    // A row's 32-column blocks span several warps: gather the tile in shared
+    // memory, then one warp per (row, block) rounds its block to Q8_0.
+    float* tile = reinterpret_cast<float*>(gbase);  // [BM][BN + 1]
+    if (warp < NWC)
+#pragma unroll
+      for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++)
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            const int r = arow + i * 16 + g + h * 8, c = brow + j * 8 + 2 * t4;
+            tile[r * (BN + 1) + c] = gelu_avx(f2lo(acc[i][j][h]));
+            tile[r * (BN + 1) + c + 1] = gelu_avx(f2hi(acc[i][j][h]));
+          }
+    __syncthreads();
+    for (int rb = warp; rb < BM * (BN / 32); rb += NWC + 1) {
+      const int r = rb / (BN / 32), cb = rb % (BN / 32), row = m0 + r;
+      float sc;
+      const int8_t qv = quant_lane(tile[r * (BN + 1) + cb * 32 + lane], &sc);
+      if (row < M) {
+        e.q8[(size_t)row * N + n0 + cb * 32 + lane] = qv;
+        if (lane == 0) e.q8s[(size_t)row * (N / QK) + (n0 + cb * 32) / QK] = make_float2(sc, sc);
+      }
+    }
+    return;
+  }
+  if (warp == NWC) return;
+#pragma unroll
+  for (int i = 0; i < TM; i++)
+#pragma unroll
+    for (int j = 0; j < TN; j++)
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int row = m0 + arow + i * 16 + g + h * 8, col = n0 + brow + j * 8 + 2 * t4;
+        if (row < M && col < N) epi_pair(e, row, col, f2lo(acc[i][j][h]), f2hi(acc[i][j][h]));
+      }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 bool tmap2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner, uint64_t outer,
@@ -881,6 +1080,66 @@ struct GemmTc {
   }
 };
 
+// A product's four tensor maps, kept per host thread and keyed by the
+// buffers and the tile, so a product launched again with the same operands
+// (a decode loop's layers, call after call) is not re-encoded.
+struct G4Key {
+  const void *a, *as, *wq, *dwnm;
+  int M, N, K, bm, bn;
+  bool operator==(const G4Key& o) const {
+    return a == o.a && as == o.as && wq == o.wq && dwnm == o.dwnm && M == o.M && N == o.N && K == o.K &&
+           bm == o.bm && bn == o.bn;
+  }
+};
+struct G4KeyHash {
+  size_t operator()(const G4Key& k) const {
+    size_t h = std::hash<const void*>()(k.a) ^ (std::hash<const void*>()(k.wq) * 31u);
+    return h ^ (size_t(k.M) * 1000003u) ^ (size_t(k.bm * 131 + k.bn) << 20);
+  }
+};
+struct G4Maps {
+  CUtensorMap ma, mw, ms, md;
+};
+
+const G4Maps* g4_maps(const int8_t* a, const float2* as, int M, const DQ8& w, int bm, int bn) {
+  thread_local std::unordered_map<G4Key, G4Maps, G4KeyHash> cache;
+  const int N = w.rows, K = w.cols, nb = K / QK, np2 = (N + 1) / 2;
+  const G4Key key{a, as, w.q, w.dwnm, M, N, K, bm, bn};
+  auto it = cache.find(key);
+  if (it != cache.end()) return &it->second;
+  G4Maps m;
+  if (!tmap2d(&m.ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, K, M, K, 128, bm, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !tmap2d(&m.mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q, K, N, K, 128, bn, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !tmap2d(&m.ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, as, 2 * nb, M, 8 * nb, 8, bm, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !tmap2d(&m.md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.dwnm, 4 * np2, nb, 16 * np2, 2 * bn, 4,
+              CU_TENSOR_MAP_SWIZZLE_NONE))
+    return nullptr;
+  if (cache.size() >= 4096) cache.clear();
+  return &cache.emplace(key, m).first->second;
+}
+
+template <int TM, int TN, int WGM, int WGN, int STAGES>
+struct Gemm4 {
+  using C4 = Cfg4<TM, TN, WGM, WGN, STAGES>;
+  using C = typename C4::B;
+  static constexpr int kTile = C::BM * (C::BN + 1) * 4 + 1024;  // the GELU epilogue's tile
+  static constexpr int kSmem = C4::SMEM > kTile ? C4::SMEM : kTile;
+  static void init() {
+    cudaFuncSetAttribute(k_q8_gemm4<TM, TN, WGM, WGN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  }
+  // False when the shape or the buffers do not suit the tensor maps; the
+  // caller then takes k_q8_gemm2 (identical results).
+  static bool launch(const int8_t* a, const float2* as, int M, const DQ8& w, const EpiArgs& e, cudaStream_t st) {
+    const int N = w.rows, nb = w.cols / QK;
+    if (!g_encode || nb % 2 || ((uintptr_t(a) | uintptr_t(as) | uintptr_t(w.q) | uintptr_t(w.dwnm)) & 15)) return false;
+    const G4Maps* m = g4_maps(a, as, M, w, C::BM, C::BN);
+    if (!m) return false;
+    dim3 grid((N + C::BN - 1) / C::BN, (M + C::BM - 1) / C::BM);
+    k_q8_gemm4<TM, TN, WGM, WGN, STAGES><<<grid, C4::NT, kSmem, st>>>(m->ma, m->mw, m->ms, m->md, M, N, nb, e);
+    return true;
+  }
+};
+
 void tc_init_encode() {
   if (g_encode) return;
   void* fn = nullptr;
@@ -896,6 +1155,18 @@ void tc_init_encode() {
 // rules out split-K), so it runs only when GRX_Q8_TC=1 is set at
 // initialisation.
 bool g_q8_tc = false;
+
+// The TMA-fed kernel's shapes (bit-identical to the others; graph-timed on
+// B200 at M = 128): 16×32 tiles of two 16×16 warps, six stages, for the
+// narrow products (attn_out 4.80 µs against 5.73, ff2 13.1 against 16.8);
+// 32×32 for qkv (7.07 against 7.56); 64×32 for ff1 (7.22 against 8.21) and,
+// at 129–256 rows, for the narrow ones (attn_out 5.82 against 6.49, ff2 15.4
+// against 19.4). Above 256 rows k_q8_gemm2 stays: Mimi's decoder at 512
+// rows per product ran 8 % slower on this kernel.
+bool g_q8_g4 = true;  // GRX_Q8_G4=0 at initialisation keeps every product on k_q8_gemm2
+using G4Narrow = Gemm4<1, 2, 1, 2, 6>;
+using G4Mid = Gemm4<1, 2, 2, 2, 4>;
+using G4Wide = Gemm4<2, 2, 2, 2, 4>;
 
 // Tile shapes per product shape, the fastest of those timed on B200, every
 // one bit-identical to the others. PB = 4: each warp issues the MMAs of four
@@ -938,6 +1209,16 @@ void launch_q8_product(const int8_t* a, const float2* as, int M, const DQ8& w, c
     return;
   }
   if (g_q8_tc && GemmTc<32, 4>::launch(a, as, M, w, e, st)) return;
+  if (!g_q8_g4 || M > 256) {
+    // the larger products (Mimi's, the TDT encoder projection, prefills)
+    // measured as fast or faster on k_q8_gemm2
+  } else if (M <= 128) {
+    if (N <= 2048 ? G4Narrow::launch(a, as, M, w, e, st)
+                  : N <= 3072 ? G4Mid::launch(a, as, M, w, e, st) : G4Wide::launch(a, as, M, w, e, st))
+      return;
+  } else if (N <= 2048 && G4Wide::launch(a, as, M, w, e, st)) {
+    return;
+  }
   if (M <= 128) {
     if (N > 3072)
       GemmSmallWide::launch(a, as, M, w, e, st);
@@ -957,7 +1238,12 @@ void q8_kernels_init() {
   tc_init_encode();
   const char* tc = getenv("GRX_Q8_TC");
   g_q8_tc = tc && tc[0] == '1';
+  const char* g4 = getenv("GRX_Q8_G4");
+  g_q8_g4 = !(g4 && g4[0] == '0');
   GemmTc<32, 4>::init();
+  G4Narrow::init();
+  G4Mid::init();
+  G4Wide::init();
   GemmMid::init();
   GemmWide::init();
   GemmSmall::init();

@@ -22,7 +22,8 @@ def _q8(rng, n, k):
 
 @pytest.mark.parametrize("m,n,k", [(1, 3072, 1024), (1, 1024, 4096), (3, 64, 96), (8, 96, 128), (17, 64, 128),
                                    (64, 1024, 1024), (256, 4096, 1024), (130, 200, 256), (40, 96, 192),
-                                   (130, 1000, 64)])
+                                   (130, 1000, 64), (100, 3072, 1024), (33, 4096, 1024), (200, 1024, 4096),
+                                   (128, 1024, 192), (300, 512, 512)])
 def test_q8_int8_path_bit_exact(have_gpu, m, n, k):
     """kern.Linear on a packed Q8_0 weight (int8 path, q8int.go:148-223):
     per-block int32 dots and the FMA chain give identical float32."""

@@ -1,7 +1,9 @@
-"""The tensor-core (tcgen05) int8 product, switched on with GRX_Q8_TC=1 at
-initialisation, against the oracle: the int8-path product tests and the
-FlowLM frame tests of test_gpu_flowlm.py rerun in a fresh process with the
-switch set, so every int8 product of more than 8 rows goes through it."""
+"""The int8 product's other kernels against the oracle: the int8-path product
+tests and the FlowLM frame tests of test_gpu_flowlm.py rerun in a fresh
+process with a switch set at initialisation — GRX_Q8_TC=1 (the tensor-core
+tcgen05 kernel for every product of more than 8 rows) and GRX_Q8_G4=0 (the
+mma.sync kernel with per-thread async copies for the products of 9 to 256
+rows that the TMA-fed one takes by default)."""
 
 import os
 import subprocess
@@ -14,8 +16,9 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
 
 
-def test_tensor_core_int8_product_bit_exact(have_gpu):
-    env = dict(os.environ, GRX_Q8_TC="1")
+@pytest.mark.parametrize("switch", [("GRX_Q8_TC", "1"), ("GRX_Q8_G4", "0")])
+def test_switched_int8_product_bit_exact(have_gpu, switch):
+    env = dict(os.environ, **{switch[0]: switch[1]})
     r = subprocess.run(
         [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", "tests/test_gpu_flowlm.py", "-k",
          "int8_path or small_frames or parts"],
