@@ -136,6 +136,8 @@ def _sig(lib):
         "grx_whisper_run": (I, [P, I, P]),
         "grx_whisper_run_device": (I, [P, I, P]),
         "grx_whisper_sync": (I, [P]),
+        "grx_whisper_persistent": (I, [P]),
+        "grx_whisper_watchdog_test": (I, [P]),
         "grx_whisper_cross": (I, [P, I, I, P, P]),
         "grx_whisper_logits": (I, [P, P]),
         "grx_whisper_batch_cuda_stream": (P, [P]),
@@ -770,6 +772,15 @@ class WhisperBatch:
 
     def sync(self):
         _check(lib().grx_whisper_sync(self._h))
+
+    def persistent(self) -> bool:
+        """Whether the batch runs its token loop in the persistent kernel."""
+        return bool(_check(lib().grx_whisper_persistent(self._h)))
+
+    def watchdog_test(self) -> int:
+        """Runs one step with a grid barrier nothing completes; returns the
+        status its bounded waits report (GRX_ETIMEDOUT when they work)."""
+        return lib().grx_whisper_watchdog_test(self._h)
 
     def cross(self, i: int, layer: int):
         m = self.model

@@ -948,23 +948,57 @@ __device__ VI cl_vi_max(VI v, VI* sh, VI* slot) {
   }
 }
 
-// Rows spread over clusters of CL CTAs (CL = 1: one CTA per row); CTA k of a
-// row's cluster takes vocabulary entries [n·k/CL, n·(k+1)/CL), applies the
-// rules that fall there and keeps its e_i; the sums combine partials in a
-// fixed order, which the margins above make safe.
+// The reductions process/sample makes over a row spread over several CTAs,
+// through a cluster's distributed shared memory: each CTA's block result in
+// its own slot, combined in rank order after the cluster barrier. Slots 0-7
+// take floats, 0-1 the (value, index) pairs.
 template <int CL>
-__global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float* scratch, WVocabDev v, WSample* state,
-                                                int* out, const int* step, int* next_tok) {
-  __shared__ float shf[40];
-  __shared__ VI shv[32];
-  __shared__ float clf[8];
-  __shared__ VI clv[2];
+struct ClusterRed {
+  float* shf;
+  VI* shv;
+  float* clf;
+  VI* clv;
+  __device__ void max3(float& a, float& b, float& c) {
+    a = cl_max<CL>(a, shf, &clf[0]);
+    b = cl_max<CL>(b, shf, &clf[1]);
+    c = cl_max<CL>(c, shf, &clf[2]);
+  }
+  __device__ float sum(float v, int slot) { return cl_sum<CL>(v, shf, &clf[3 + slot]); }
+  __device__ void vimax2(VI& a, VI& b) {
+    a = cl_vi_max<CL>(a, shv, &clv[0]);
+    b = cl_vi_max<CL>(b, shv, &clv[1]);
+  }
+  __device__ void max2(float& a, float& b) {
+    a = cl_max<CL>(a, shf, &clf[6]);
+    b = cl_max<CL>(b, shf, &clf[7]);
+  }
+  __device__ void done() {
+    if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while its slots may be read
+  }
+};
+
+// process + sample of one row (transcribe.go:370-494) by the CTAs that share
+// it: this CTA takes vocabulary entries [a0, a1), applies the rules that
+// fall there and keeps its e_i; the sums combine partials in a fixed order,
+// which the margins below make safe. `writer` marks the one CTA that writes
+// the outputs: out[0..3] (id, tid, p, plog), the stream's sampling state
+// and the next token.
+//
+// The three float32 sums of logSoftmax, the timestamp rule and softmaxInf
+// are taken in parallel, and every decision they feed is checked: the
+// timestamp rule must clear a relative margin of 2e-4, and the winning
+// probability must beat every earlier index's by a factor 1 − 2^-20 (the
+// division by the sum can then not tie them). A row that misses a margin is
+// recomputed by one thread in the reference's order. One pass takes
+// e_i = expf(lg_i − max) for the whole row into scratch; without the
+// timestamp rule's masking softmaxInf's terms are those same e_i (and so is
+// its sum), so only the timestamps are taken again.
+template <class Red>
+__device__ void proc_row(Red& red, float* lg, float* e, const WVocabDev& v, WSample* sp, int* orow, int* next_tok,
+                         int a0, int a1, bool writer) {
   __shared__ int amb;
-  const int row = blockIdx.x / CL, rank = blockIdx.x % CL, s = r.row_stream[row], n = v.n, beg = v.beg;
-  const int a0 = int((long long)n * rank / CL), a1 = int((long long)n * (rank + 1) / CL);
-  float* lg = logits + (size_t)row * n;
-  float* e = scratch + (size_t)row * n;
-  const WSample q = state[s];
+  const int n = v.n, beg = v.beg;
+  const WSample q = *sp;
   const bool initial = q.nt == 0;
   auto setinf = [&](int i) {
     if (i >= a0 && i < a1) lg[i] = NINF;
@@ -997,9 +1031,7 @@ __global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float
     if (i >= beg) mts = fmaxf(mts, x);
     else mtx = fmaxf(mtx, x);
   }
-  mx = cl_max<CL>(mx, shf, &clf[0]);
-  mts = cl_max<CL>(mts, shf, &clf[1]);
-  mtx = cl_max<CL>(mtx, shf, &clf[2]);
+  red.max3(mx, mts, mtx);
   // ---- logSoftmax's sum, with e_i kept
   float s1 = 0.f;
   for (int i = a0 + threadIdx.x; i < a1; i += blockDim.x) {
@@ -1008,7 +1040,7 @@ __global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float
     e[i] = ei;
     s1 = __fadd_rn(s1, ei);
   }
-  s1 = cl_sum<CL>(s1, shf, &clf[3]);
+  s1 = red.sum(s1, 0);
   const float ls = __fadd_rn(float(log(double(s1))), mx);
   // ---- the timestamp rule
   const float ts_max = mts > NINF ? __fsub_rn(mts, ls) : NINF;  // the largest of logprobs[beg:]
@@ -1017,7 +1049,7 @@ __global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float
     float sum = 0.f;
     for (int i = max(beg, a0) + threadIdx.x; i < a1; i += blockDim.x)
       if (lg[i] > NINF) sum = __fadd_rn(sum, expf_go(__fsub_rn(__fsub_rn(lg[i], ls), ts_max)));
-    sum = cl_sum<CL>(sum, shf, &clf[4]);
+    sum = red.sum(sum, 1);
     const float ts_lp = __fadd_rn(float(log(double(sum))), ts_max);
     const float text_max = mtx > NINF ? __fsub_rn(mtx, ls) : NINF;
     mask_text = ts_lp > text_max;
@@ -1035,7 +1067,7 @@ __global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float
       e[i] = ei;
       s2 = __fadd_rn(s2, ei);
     }
-    s2 = cl_sum<CL>(s2, shf, &clf[5]);
+    s2 = red.sum(s2, 2);
   }
   __syncthreads();
   VI best{-1.f, n}, bts{-1.f, n};
@@ -1044,8 +1076,7 @@ __global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float
     best = vi_max(best, VI{ei, i});
     if (i >= beg) bts = vi_max(bts, VI{ei, i});
   }
-  best = cl_vi_max<CL>(best, shv, &clv[0]);
-  bts = cl_vi_max<CL>(bts, shv, &clv[1]);
+  red.vimax2(best, bts);
   if (mask_text && lo > 0 && best.v < 0.f) best = VI{-1.f, n};
   // masked text has probability 0: it only wins if nothing else is positive
   if (mask_text && !(best.v > 0.f)) best = VI{0.f, 0};
@@ -1056,12 +1087,11 @@ __global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float
     if (i < best.i && ei < best.v) near = fmaxf(near, ei);
     if (i >= beg && i < bts.i && ei < bts.v) near_t = fmaxf(near_t, ei);
   }
-  near = cl_max<CL>(near, shf, &clf[6]);
-  near_t = cl_max<CL>(near_t, shf, &clf[7]);
+  red.max2(near, near_t);
   const float margin = 1.f - 9.5367431640625e-07f;  // 1 − 2^-20
   if ((best.v > 0.f && near >= best.v * margin) || (bts.v > 0.f && near_t >= bts.v * margin)) amb = 1;
   __syncthreads();
-  if (threadIdx.x == 0 && rank == 0) {
+  if (threadIdx.x == 0 && writer) {
     int o[4];
     if (amb) {
       proc_exact(lg, n, beg, o);
@@ -1074,7 +1104,6 @@ __global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float
       o[2] = __float_as_int(__fdiv_rn(best.v, s2));
       o[3] = __float_as_int(mask_text && id < beg ? NINF : __fsub_rn(lg[id], ls));
     }
-    int* orow = out + ((size_t)(step ? *step : 0) * r.rows + row) * 4;
     for (int i = 0; i < 4; i++) orow[i] = o[i];
     // the window loop's bookkeeping that process depends on (transcribe.go:218-224)
     WSample ns = q;
@@ -1085,10 +1114,27 @@ __global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float
       ns.seek_delta = 2 * (o[0] - beg);
       ns.has_ts = 1;
     }
-    state[s] = ns;
-    if (next_tok) next_tok[row] = o[0];
+    *sp = ns;
+    if (next_tok) *next_tok = o[0];
   }
-  if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while its slots may be read
+  red.done();
+}
+
+// Rows spread over clusters of CL CTAs (CL = 1: one CTA per row); CTA k of a
+// row's cluster takes vocabulary entries [n·k/CL, n·(k+1)/CL).
+template <int CL>
+__global__ void __launch_bounds__(1024, 1) k_wproc(WRows r, float* logits, float* scratch, WVocabDev v, WSample* state,
+                                                int* out, const int* step, int* next_tok) {
+  __shared__ float shf[40];
+  __shared__ VI shv[32];
+  __shared__ float clf[8];
+  __shared__ VI clv[2];
+  const int row = blockIdx.x / CL, rank = blockIdx.x % CL, s = r.row_stream[row], n = v.n;
+  const int a0 = int((long long)n * rank / CL), a1 = int((long long)n * (rank + 1) / CL);
+  ClusterRed<CL> red{shf, shv, clf, clv};
+  proc_row(red, logits + (size_t)row * n, scratch + (size_t)row * n, v, state + s,
+           out + ((size_t)(step ? *step : 0) * r.rows + row) * 4, next_tok ? next_tok + row : nullptr, a0, a1,
+           rank == 0);
 }
 
 // softmax(row)[nosp] (mathx.go:78-90): EXP8 lanes over n&~7 summed in order
@@ -1116,6 +1162,314 @@ __global__ void k_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int 
   const int p = row_pos[r] + advance;
   row_pos[r] = p;
   dst_row[r] = r * text_ctx + p;
+}
+
+// -------------------------------------- one stream's token loop, persistent
+//
+// k_wstep1 runs `steps` rounds of grx_whisper_run's step for a batch of one
+// stream — process/sample of the last logits, then the decode of the sampled
+// token — in one cooperative launch of one 512-thread CTA per SM, with a
+// grid barrier where a step needs every CTA's results. Per layer: the q/k/v
+// rows, self-attention (a CTA per head), o with the residual, LayerNorm and
+// xq, the cross scores (key chunks over the CTAs), the softmax and values
+// (two CTAs a head), xo with the residual, LayerNorm and fc1, fc2 with the
+// residual; then the final LayerNorm and the logits rows. Every CTA keeps a
+// copy of the residual row and forms the LayerNorms itself. The arithmetic
+// is the per-kernel path's: the products in k_flin's float-path lane order
+// (one 8-lane group per output row, dot4f16avx with Q8_0 widened as
+// f16(q·d)), the attention and process/sample code shared with those
+// kernels; process/sample's sums combine the CTAs' partials in CTA order
+// (the margins make the order safe, as for the cluster form). Every wait is
+// bounded (about a second); one that runs out sets the error word and every
+// CTA leaves.
+constexpr int WS_NT = 512;
+constexpr unsigned long long kWsWaitNs = 1000000000ull;
+
+struct WsCtl {
+  unsigned bar_k;
+  int fail;
+};
+
+__device__ bool ws_sync(const WStep1Args& A, WsCtl& ctl) {
+  __syncthreads();
+  if (threadIdx.x == 0 && !ctl.fail) {
+    ctl.bar_k += 1;
+    const unsigned target = A.stall ? 0xffffffffu : ctl.bar_k * gridDim.x;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;\n" ::"l"(A.bar) : "memory");
+    const unsigned long long t0 = wtime();
+    for (int it = 0;; it++) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(A.bar) : "memory");
+      if (v >= target) break;
+      if ((it & 63) == 63) {
+        if (*(volatile int*)A.err) {
+          ctl.fail = 1;
+          break;
+        }
+        if (wtime() - t0 > kWsWaitNs) {
+          atomicCAS(A.err, 0, 1);
+          ctl.fail = 1;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return !ctl.fail;
+}
+
+// process/sample's reductions over the whole grid: each CTA's block result
+// to its column of the partials, the grid barrier, then every thread
+// combines the columns in CTA order. Float slots: 0-2 the maxima, 3-5 the
+// sums, 6-7 the "near" maxima; (value, index) slots 0-1.
+struct GridRed {
+  const WStep1Args& A;
+  WsCtl& ctl;
+  float* shf;
+  VI* shv;
+  __device__ float col(int slot, int k) const { return A.part[size_t(slot) * gridDim.x + k]; }
+  __device__ void put(int slot, float v) const {
+    if (threadIdx.x == 0) A.part[size_t(slot) * gridDim.x + blockIdx.x] = v;
+  }
+  __device__ void max3(float& a, float& b, float& c) {
+    a = block_max(a, shf);
+    b = block_max(b, shf);
+    c = block_max(c, shf);
+    put(0, a), put(1, b), put(2, c);
+    ws_sync(A, ctl);
+    a = b = c = NINF;
+    for (int k = 0; k < int(gridDim.x); k++) a = fmaxf(a, col(0, k)), b = fmaxf(b, col(1, k)), c = fmaxf(c, col(2, k));
+  }
+  __device__ float sum(float v, int slot) {
+    v = block_sum(v, shf);
+    put(3 + slot, v);
+    ws_sync(A, ctl);
+    float r = 0.f;
+    for (int k = 0; k < int(gridDim.x); k++) r = __fadd_rn(r, col(3 + slot, k));
+    return r;
+  }
+  __device__ void vimax2(VI& a, VI& b) {
+    a = block_vi_max(a, shv);
+    b = block_vi_max(b, shv);
+    VI* pv = reinterpret_cast<VI*>(A.partv);
+    if (threadIdx.x == 0) pv[blockIdx.x] = a, pv[gridDim.x + blockIdx.x] = b;
+    ws_sync(A, ctl);
+    a = pv[0];
+    b = pv[gridDim.x];
+    for (int k = 1; k < int(gridDim.x); k++) a = vi_max(a, pv[k]), b = vi_max(b, pv[gridDim.x + k]);
+  }
+  __device__ void max2(float& a, float& b) {
+    a = block_max(a, shf);
+    b = block_max(b, shf);
+    put(6, a), put(7, b);
+    ws_sync(A, ctl);
+    a = b = NINF;
+    for (int k = 0; k < int(gridDim.x); k++) a = fmaxf(a, col(6, k)), b = fmaxf(b, col(7, k));
+  }
+  __device__ void done() {}
+};
+
+__device__ __forceinline__ int ws_split(int n, int c, int G) { return int((long long)n * c / G); }
+
+// whisper/mathx.go:55-75 over a row in shared memory (as k_wln).
+__device__ void ws_ln(const float* x, float* y, const float* w, const float* b, int n, double* shd) {
+  double s = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += double(x[i]);
+  s = block_sum_d(s, shd);
+  const float mean = float(s / double(n));
+  double vs = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const double d = double(__fsub_rn(x[i], mean));
+    vs += d * d;
+  }
+  vs = block_sum_d(vs, shd);
+  const float inv = float(1.0 / sqrt(vs / double(n) + 1e-5));
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    y[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i], mean), inv), w[i]), b[i]);
+  __syncthreads();
+}
+
+// A weight value as the decoder's products read it: float16, or a Q8_0
+// value widened as f16(q·d) (whisper/model.go:486-490).
+__device__ __forceinline__ float ws_w(const WMat& w, int n, int k, int K) {
+  if (w.h) return __half2float(__ushort_as_half(w.h[(size_t)n * K + k]));
+  return q8h(w.q[(size_t)n * K + k], h2f(w.d[(size_t)n * (K / QK) + k / QK]));
+}
+
+enum { WS_STORE = 0, WS_RESID = 1, WS_GELU = 2 };
+
+// Rows [r0, r1) of y = W·x (+ bias) for one input row x (shared memory, K
+// values): one 8-lane group per output row, lane l accumulating elements
+// 16c + l and 16c + 8 + l over c in order, then the two added and the HSUM
+// ((a0+a4)+(a1+a5))+((a2+a6)+(a3+a7)) — k_flin's order (dot4f16avx). RESID
+// stores res[n] + (dot + bias), GELU geluAVX(dot + bias).
+template <int EPI>
+__device__ void ws_rows(const WMat& w, const float* x, int K, int r0, int r1, const float* bias, float* y,
+                        const float* res) {
+  const int g = threadIdx.x >> 3, l = threadIdx.x & 7, ng = blockDim.x >> 3;
+  const unsigned gm = 0xffu << (threadIdx.x & 24);
+  for (int n = r0 + g; n < r1; n += ng) {
+    float a = 0.f, a1 = 0.f;
+#pragma unroll 4
+    for (int c16 = 0; c16 < K; c16 += 16) {
+      a = __fmaf_rn(x[c16 + l], ws_w(w, n, c16 + l, K), a);
+      a1 = __fmaf_rn(x[c16 + 8 + l], ws_w(w, n, c16 + 8 + l, K), a1);
+    }
+    float v = __fadd_rn(a, a1);
+    v = __fadd_rn(v, __shfl_xor_sync(gm, v, 4));
+    v = __fadd_rn(v, __shfl_xor_sync(gm, v, 1));
+    v = __fadd_rn(v, __shfl_xor_sync(gm, v, 2));
+    if (l == 0) {
+      const float o = bias ? __fadd_rn(v, bias[n]) : v;
+      if (EPI == WS_RESID)
+        y[n] = __fadd_rn(res[n], o);
+      else if (EPI == WS_GELU)
+        y[n] = gelu_avx(o);
+      else
+        y[n] = o;
+    }
+  }
+}
+
+// Self-attention of head h over keys 0..n-1 (decoder.go:70-87, as k_wself).
+__device__ void ws_self(const float* q, const float* sk, const float* sv, int st, int n, int h, float* sc, float* qh,
+                        float* sh, float* att) {
+  if (threadIdx.x < 64) qh[threadIdx.x] = q[h * 64 + threadIdx.x];
+  __syncthreads();
+  const float scale = float(1.0 / sqrt(double(64)));
+  const float* kb = sk + h * 64;
+  float mx = NINF;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float* kj = kb + (size_t)j * st;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; i += 4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kj + i);
+      s0 = __fadd_rn(s0, __fmul_rn(qh[i], k4.x));
+      s1 = __fadd_rn(s1, __fmul_rn(qh[i + 1], k4.y));
+      s2 = __fadd_rn(s2, __fmul_rn(qh[i + 2], k4.z));
+      s3 = __fadd_rn(s3, __fmul_rn(qh[i + 3], k4.w));
+    }
+    const float v = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3), scale);
+    sc[j] = v;
+    mx = fmaxf(mx, v);
+  }
+  mx = block_max(mx, sh);
+  const float sum = exp_sub(sc, n, mx, sh);
+  const float inv = __fdiv_rn(1.f, sum);
+  for (int j = threadIdx.x; j < n; j += blockDim.x) sc[j] = __fmul_rn(sc[j], inv);
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    const float* vb = sv + h * 64 + threadIdx.x;
+    float o = 0.f;
+    for (int j = 0; j < n; j++) o = __fadd_rn(o, __fmul_rn(sc[j], vb[(size_t)j * st]));
+    att[h * 64 + threadIdx.x] = o;
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restrict__ Ap, int pos0, int steps) {
+  const WStep1Args& A = *Ap;
+  extern __shared__ __align__(16) float wsm[];
+  const int st = A.st, ff = A.ff, ctx = A.ctx, nh = A.nh, G = gridDim.x, cta = blockIdx.x;
+  float* xs = wsm;                   // [st] the residual row
+  float* cur = xs + st;              // [max(st, ff)] a product's input
+  float* sc = cur + max(st, ff);     // [max(ctx, text_ctx)] scores
+  float* qh = sc + max(ctx, A.text_ctx);  // [64]
+  __shared__ float shf[40];
+  __shared__ VI shv[32];
+  __shared__ double shd[32];
+  __shared__ WsCtl ctl;
+  if (threadIdx.x == 0) ctl.bar_k = 0, ctl.fail = 0;
+  __syncthreads();
+  GridRed red{A, ctl, shf, shv};
+  // the cross scores' key chunks: about G / nh per head, whole groups of 16
+  const int ctx4 = ctx & ~3;
+  int ks = max(1, G / nh);
+  const int ch = ((ctx4 + ks - 1) / ks + 15) / 16 * 16;
+  ks = (ctx4 + ch - 1) / ch;
+  auto rows = [&](int n, int& r0, int& r1) {
+    r0 = ws_split(n, cta, G);
+    r1 = ws_split(n, cta + 1, G);
+  };
+  auto load = [&](float* dst, const float* src, int n) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    __syncthreads();
+  };
+  int i = 0;
+  for (; i < steps; i++) {
+    // ---- process + sample of the last logits (transcribe.go:370-494)
+    proc_row(red, A.logits, A.scratch, A.voc, A.state, A.out + 4 * i, A.row_tok, ws_split(A.vocab, cta, G),
+             ws_split(A.vocab, cta + 1, G), cta == 0);
+    if (!ws_sync(A, ctl)) break;
+    const int pos = pos0 + i, tok = A.row_tok[0];
+    // ---- decode of the token at pos (decoder.go:33-140): the embedding
+    for (int j = threadIdx.x; j < st; j += blockDim.x)
+      xs[j] = __fadd_rn(wmat_at(A.emb, tok, j), A.dec_pos[(size_t)pos * st + j]);
+    __syncthreads();
+    int r0, r1;
+    for (int l = 0; l < A.L; l++) {
+      const WS1Layer& Y = A.layers[l];
+      ws_ln(xs, cur, Y.ln1w, Y.ln1b, st, shd);
+      rows(st, r0, r1);
+      ws_rows<WS_STORE>(Y.q, cur, st, r0, r1, Y.qb, A.q, nullptr);
+      ws_rows<WS_STORE>(Y.k, cur, st, r0, r1, nullptr, Y.sk + (size_t)pos * st, nullptr);
+      ws_rows<WS_STORE>(Y.v, cur, st, r0, r1, Y.vb, Y.sv + (size_t)pos * st, nullptr);
+      if (!ws_sync(A, ctl)) break;
+      if (cta < nh) ws_self(A.q, Y.sk, Y.sv, st, pos + 1, cta, sc, qh, shf, A.att);
+      if (!ws_sync(A, ctl)) break;
+      load(cur, A.att, st);
+      ws_rows<WS_RESID>(Y.o, cur, st, r0, r1, Y.ob, A.x, xs);
+      if (!ws_sync(A, ctl)) break;
+      load(xs, A.x, st);
+      ws_ln(xs, cur, Y.ln2w, Y.ln2b, st, shd);
+      ws_rows<WS_STORE>(Y.xq, cur, st, r0, r1, Y.xqb, A.q, nullptr);
+      if (!ws_sync(A, ctl)) break;
+      if (cta < nh * ks) {  // cross scores of key chunk cta % ks of head cta / ks
+        const int h = cta / ks, kc = cta % ks, j0 = kc * ch, j1 = min(ctx4, j0 + ch);
+        if (threadIdx.x < 64) qh[threadIdx.x] = A.q[h * 64 + threadIdx.x];
+        __syncthreads();
+        float mx = wcross_scores(qh, Y.ck + (size_t)h * ctx * 64, j0, j1, kc == ks - 1, ctx, A.sg + (size_t)h * ctx);
+        mx = block_max(mx, shf);
+        if (threadIdx.x == 0) A.mg[h * ks + kc] = mx;
+      }
+      if (!ws_sync(A, ctl)) break;
+      if (cta < nh * 2) {  // softmax and 32 of the 64 outputs of head cta / 2
+        const int h = cta / 2, d0 = (cta % 2) * 32;
+        float mx = NINF;
+        for (int k = 0; k < ks; k++) mx = fmaxf(mx, A.mg[h * ks + k]);
+        load(sc, A.sg + (size_t)h * ctx, ctx);
+        wcross_softmax(sc, ctx, mx, shf);
+        wcross_out<1>(sc, Y.cvt + (size_t)h * 64 * ctx, ctx, d0, A.att + h * 64);
+      }
+      if (!ws_sync(A, ctl)) break;
+      load(cur, A.att, st);
+      ws_rows<WS_RESID>(Y.xo, cur, st, r0, r1, Y.xob, A.x, xs);
+      if (!ws_sync(A, ctl)) break;
+      load(xs, A.x, st);
+      ws_ln(xs, cur, Y.ln3w, Y.ln3b, st, shd);
+      int f0, f1;
+      rows(ff, f0, f1);
+      ws_rows<WS_GELU>(Y.fc1, cur, st, f0, f1, Y.fc1b, A.ffb, nullptr);
+      if (!ws_sync(A, ctl)) break;
+      load(cur, A.ffb, ff);
+      ws_rows<WS_RESID>(Y.fc2, cur, ff, r0, r1, Y.fc2b, A.x, xs);
+      if (!ws_sync(A, ctl)) break;
+      load(xs, A.x, st);
+    }
+    if (ctl.fail) break;
+    // ---- the final LayerNorm and the logits (no bias)
+    ws_ln(xs, cur, A.lnw, A.lnb, st, shd);
+    rows(A.vocab, r0, r1);
+    ws_rows<WS_STORE>(A.emb, cur, st, r0, r1, nullptr, A.logits, nullptr);
+    if (!ws_sync(A, ctl)) break;
+  }
+  // the positions and the run's step counter, as the per-kernel path leaves them
+  if (cta == 0 && threadIdx.x == 0 && !ctl.fail) {
+    A.row_pos[0] = pos0 + steps;
+    A.dst_row[0] = pos0 + steps;
+    *A.step = steps;
+  }
 }
 
 }  // namespace
@@ -1274,5 +1628,21 @@ void launch_wenc_softmax(float* x, int len, long rows, cudaStream_t st) {
 }
 
 void whisper_kernels_init() {}
+
+size_t wstep1_smem(const WStep1Args& a) {
+  return sizeof(float) * (size_t(a.st) + size_t(std::max(a.st, a.ff)) + size_t(std::max(a.ctx, a.text_ctx)) + 64);
+}
+
+int wstep1_max_active(size_t smem) {
+  int n = 0;
+  cudaFuncSetAttribute(k_wstep1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_wstep1, WS_NT, smem) != cudaSuccess) return 0;
+  return n;
+}
+
+cudaError_t launch_wstep1(const WStep1Args* d_args, int grid, size_t smem, int pos0, int steps, cudaStream_t st) {
+  void* args[] = {(void*)&d_args, (void*)&pos0, (void*)&steps};
+  return cudaLaunchCooperativeKernel((const void*)k_wstep1, dim3(grid), dim3(WS_NT), args, smem, st);
+}
 
 }  // namespace grx

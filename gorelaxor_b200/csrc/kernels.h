@@ -412,6 +412,37 @@ struct WVocabDev {
   unsigned long long* exact_rows = nullptr;
 };
 
+// ---- the token loop of one Whisper stream in one cooperative launch
+constexpr int WS1_MAX_LAYERS = 12;
+struct WS1Layer {
+  WMat q, k, v, o, xq, xo, fc1, fc2;
+  const float *qb, *vb, *ob, *xqb, *xob, *fc1b, *fc2b;
+  const float *ln1w, *ln1b, *ln2w, *ln2b, *ln3w, *ln3b;
+  float *sk, *sv;           // the stream's self K / V caches [text_ctx][st]
+  const float *ck, *cvt;    // its cross K [nh][ctx][64] (scaled) and Vᵀ [nh][64][ctx]
+};
+struct WStep1Args {
+  int st = 0, nh = 0, ctx = 0, text_ctx = 0, ff = 0, L = 0, vocab = 0;
+  WS1Layer layers[WS1_MAX_LAYERS];
+  WMat emb;
+  const float *dec_pos = nullptr, *lnw = nullptr, *lnb = nullptr;
+  WVocabDev voc;
+  WSample* state = nullptr;
+  int *out = nullptr, *row_tok = nullptr, *row_pos = nullptr, *dst_row = nullptr, *step = nullptr;
+  float *logits = nullptr, *scratch = nullptr, *x = nullptr, *q = nullptr, *att = nullptr, *ffb = nullptr;
+  float *sg = nullptr, *mg = nullptr, *part = nullptr;
+  void* partv = nullptr;     // (value, index) partials [2][grid]
+  unsigned* bar = nullptr;   // grid barrier arrivals (zeroed before a launch)
+  int* err = nullptr;        // 1: a wait ran out
+  int stall = 0;             // test hook: the first barrier never completes
+};
+// Shared memory a CTA of the kernel needs; whether the device runs it (one
+// 512-thread CTA per SM, cooperative launch); the launch (steps rounds of
+// sample-then-decode from position pos0).
+size_t wstep1_smem(const WStep1Args& a);
+int wstep1_max_active(size_t smem);
+cudaError_t launch_wstep1(const WStep1Args* d_args, int grid, size_t smem, int pos0, int steps, cudaStream_t st);
+
 void launch_wembed(const WRows& r, const WMat& tok_emb, const float* dec_pos, float* x, cudaStream_t st);
 void launch_wln(const float* x, float* y, const float* w, const float* b, int rows, int n, cudaStream_t st);
 // Self-attention of every row over its stream's cache rows 0..pos.

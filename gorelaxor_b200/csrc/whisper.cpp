@@ -194,6 +194,15 @@ struct grx_whisper_batch {
   cudaGraphExec_t g_decode = nullptr, g_step = nullptr;
   int per_decode = 0;
   int64_t launches = 0;
+  // a batch of one stream runs its token loop in the persistent kernel
+  // (k_wstep1): its arguments on the device, grid, barrier and error word
+  bool ws1 = false;
+  WStep1Args* ws1_args = nullptr;
+  int ws1_grid = 0;
+  size_t ws1_smem = 0;
+  unsigned* ws1_bar = nullptr;
+  int* ws1_err = nullptr;
+  int* ws1_out = nullptr;  // the run_out the arguments hold
   ~grx_whisper_batch() {
     cudaSetDevice(ar.dev);
     if (g_decode) cudaGraphExecDestroy(g_decode);
@@ -276,6 +285,95 @@ int capture(grx_whisper_batch* b, bool with_sample, cudaGraphExec_t* out) {
   if (e != cudaSuccess) return fail(GRX_ECUDA, std::string("whisper graph: ") + cudaGetErrorString(e));
   b->per_decode = k;
   return GRX_OK;
+}
+
+// The persistent token loop for a batch of one stream when the model and the
+// device suit it (GRX_WSTEP1=0 keeps the per-kernel graph): 64-value heads,
+// K of every product a multiple of 16, Q8_0 or float16 matrices, a
+// cooperative launch of one CTA per SM.
+int ws1_setup(grx_whisper_batch* b) {
+  const char* env = getenv("GRX_WSTEP1");
+  const grx_whisper* m = b->m;
+  if ((env && env[0] == '0') || b->n != 1 || m->n_head * 64 != m->n_state || m->n_state % 16 ||
+      m->layers.empty() || m->layers.size() > size_t(WS1_MAX_LAYERS) || m->n_vocab % 4 || m->n_audio_ctx % 4)
+    return GRX_OK;
+  auto ok = [](const WMat& w) { return (w.q != nullptr || w.h != nullptr) && w.f == nullptr && w.cols % 16 == 0; };
+  const int ff = m->layers[0].fc1.rows;
+  if (!ok(m->tok_emb) || ff % 16) return GRX_OK;
+  for (const WLayerDev& L : m->layers)
+    if (!ok(L.q) || !ok(L.k) || !ok(L.v) || !ok(L.o) || !ok(L.xq) || !ok(L.xo) || !ok(L.fc1) || !ok(L.fc2) ||
+        L.fc1.rows != ff)
+      return GRX_OK;
+  int G = 0, coop = 0;
+  CK(cudaDeviceGetAttribute(&G, cudaDevAttrMultiProcessorCount, b->ar.dev));
+  CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, b->ar.dev));
+  if (!coop || G < 2 * m->n_head) return GRX_OK;
+  WStep1Args A;
+  A.st = m->n_state;
+  A.nh = m->n_head;
+  A.ctx = m->n_audio_ctx;
+  A.text_ctx = m->n_text_ctx;
+  A.ff = ff;
+  A.L = int(m->layers.size());
+  A.vocab = m->n_vocab;
+  for (int l = 0; l < A.L; l++) {
+    const WLayerDev& L = m->layers[size_t(l)];
+    WS1Layer& Y = A.layers[l];
+    Y.q = L.q, Y.k = L.k, Y.v = L.v, Y.o = L.o, Y.xq = L.xq, Y.xo = L.xo, Y.fc1 = L.fc1, Y.fc2 = L.fc2;
+    Y.qb = L.qb, Y.vb = L.vb, Y.ob = L.ob, Y.xqb = L.xqb, Y.xob = L.xob, Y.fc1b = L.fc1b, Y.fc2b = L.fc2b;
+    Y.ln1w = L.attn_ln_w, Y.ln1b = L.attn_ln_b, Y.ln2w = L.x_ln_w, Y.ln2b = L.x_ln_b, Y.ln3w = L.mlp_ln_w,
+    Y.ln3b = L.mlp_ln_b;
+    Y.sk = b->sk + size_t(l) * layer_stride_self(m, 1);
+    Y.sv = b->sv + size_t(l) * layer_stride_self(m, 1);
+    Y.ck = b->ck + size_t(l) * layer_stride_cross(m, 1);
+    Y.cvt = b->cvt + size_t(l) * layer_stride_cross(m, 1);
+  }
+  A.emb = m->tok_emb;
+  A.dec_pos = m->dec_pos;
+  A.lnw = m->ln_w;
+  A.lnb = m->ln_b;
+  A.voc = m->voc;
+  A.state = b->state;
+  A.row_tok = b->row_tok;
+  A.row_pos = b->row_pos;
+  A.dst_row = b->dst_row;
+  A.step = b->step;
+  A.logits = b->logits;
+  A.scratch = b->scratch;
+  const size_t smem = wstep1_smem(A);
+  if (smem > 200 * 1024 || wstep1_max_active(smem) < 1) return GRX_OK;
+  int rc = 0;
+  A.x = b->ar.alloc<float>(size_t(A.st), &rc);
+  A.q = b->ar.alloc<float>(size_t(A.st), &rc);
+  A.att = b->ar.alloc<float>(size_t(A.st), &rc);
+  A.ffb = b->ar.alloc<float>(size_t(ff), &rc);
+  A.sg = b->ar.alloc<float>(size_t(A.nh) * A.ctx, &rc);
+  A.mg = b->ar.alloc<float>(size_t(G), &rc);
+  A.part = b->ar.alloc<float>(size_t(8) * G, &rc);
+  A.partv = b->ar.alloc<int2>(size_t(2) * G, &rc);
+  A.bar = b->ar.alloc<unsigned>(1, &rc);
+  A.err = b->ar.alloc<int>(1, &rc);
+  b->ws1_args = b->ar.alloc<WStep1Args>(1, &rc);
+  if (rc) return rc;
+  CK(cudaMemset(A.err, 0, sizeof(int)));
+  CK(cudaMemcpy(b->ws1_args, &A, sizeof A, cudaMemcpyHostToDevice));
+  b->ws1_bar = A.bar;
+  b->ws1_err = A.err;
+  b->ws1_grid = G;
+  b->ws1_smem = smem;
+  b->ws1 = true;
+  return GRX_OK;
+}
+
+// GRX_ETIMEDOUT when the persistent kernel gave up on a wait (the word is
+// cleared for the next run).
+int ws1_check(grx_whisper_batch* b) {
+  if (!b->ws1) return GRX_OK;
+  int e = 0;
+  CK(cudaMemcpy(&e, b->ws1_err, sizeof e, cudaMemcpyDeviceToHost));
+  if (!e) return GRX_OK;
+  CK(cudaMemset(b->ws1_err, 0, sizeof(int)));
+  return fail(GRX_ETIMEDOUT, "the persistent Whisper step gave up on a grid barrier after its one-second limit");
 }
 
 }  // namespace
@@ -617,6 +715,8 @@ int grx_whisper_batch_create(grx_whisper* m, int n, grx_whisper_batch** out) {
   r.row_stream = b->row_stream;
   r.row_pos = b->row_pos;
   r.row_tok = b->row_tok;
+  rc = ws1_setup(b.get());
+  if (rc) return rc;
   *out = b.release();
   return GRX_OK;
 }
@@ -973,6 +1073,19 @@ static int run(grx_whisper_batch* b, int steps) {
                                 std::to_string(b->m->n_text_ctx));
   int rc = ensure_run_out(b, steps);
   if (rc) return rc;
+  if (b->ws1) {  // the whole run in one launch
+    if (b->ws1_out != b->run_out) {
+      CK(cudaStreamSynchronize(b->st));
+      CK(cudaMemcpy(&b->ws1_args->out, &b->run_out, sizeof(int*), cudaMemcpyHostToDevice));
+      b->ws1_out = b->run_out;
+    }
+    CK(cudaMemsetAsync(b->ws1_bar, 0, sizeof(unsigned), b->st));
+    CK(cudaMemsetAsync(b->step, 0, sizeof(int), b->st));
+    CK(launch_wstep1(b->ws1_args, b->ws1_grid, b->ws1_smem, b->pos, steps, b->st));
+    b->launches += 1;
+    b->pos += steps;
+    return GRX_OK;
+  }
   if (!b->g_step) {
     rc = capture(b, true, &b->g_step);
     if (rc) return rc;
@@ -994,7 +1107,7 @@ int grx_whisper_run(grx_whisper_batch* b, int steps, int* tokens) {
   if (rc) return rc;
   CK(cudaMemcpyAsync(tokens, b->run_out, sizeof(int) * 4 * size_t(steps) * b->n, cudaMemcpyDeviceToHost, b->st));
   CK(cudaStreamSynchronize(b->st));
-  return GRX_OK;
+  return ws1_check(b);
 }
 
 int grx_whisper_run_device(grx_whisper_batch* b, int steps, int* d_tokens) {
@@ -1011,7 +1124,33 @@ int grx_whisper_sync(grx_whisper_batch* b) {
   CK(cudaSetDevice(b->ar.dev));
   CK(cudaStreamSynchronize(b->st));
   CK(cudaGetLastError());
-  return GRX_OK;
+  return ws1_check(b);
+}
+
+int grx_whisper_persistent(const grx_whisper_batch* b) { return b && b->ws1 ? 1 : 0; }
+
+int grx_whisper_watchdog_test(grx_whisper_batch* b) {
+  if (!b) return fail(GRX_EINVAL, "null batch");
+  if (!b->ws1) return fail(GRX_EINVAL, "grx_whisper_watchdog_test: the batch does not run the persistent kernel");
+  if (b->pos == 0 || b->pos + 1 > b->m->n_text_ctx) return fail(GRX_EINVAL, "grx_whisper_watchdog_test: decode a prompt first");
+  CK(cudaSetDevice(b->ar.dev));
+  int rc = ensure_run_out(b, 1);
+  if (rc) return rc;
+  // one step whose first grid barrier nothing completes
+  const int one = 1, zero = 0;
+  CK(cudaStreamSynchronize(b->st));
+  if (b->ws1_out != b->run_out) {
+    CK(cudaMemcpy(&b->ws1_args->out, &b->run_out, sizeof(int*), cudaMemcpyHostToDevice));
+    b->ws1_out = b->run_out;
+  }
+  CK(cudaMemcpy(&b->ws1_args->stall, &one, sizeof one, cudaMemcpyHostToDevice));
+  CK(cudaMemset(b->ws1_bar, 0, sizeof(unsigned)));
+  const cudaError_t e = launch_wstep1(b->ws1_args, b->ws1_grid, b->ws1_smem, b->pos, 1, b->st);
+  const cudaError_t e2 = cudaStreamSynchronize(b->st);
+  CK(cudaMemcpy(&b->ws1_args->stall, &zero, sizeof zero, cudaMemcpyHostToDevice));
+  CK(e);
+  CK(e2);
+  return ws1_check(b);
 }
 
 // The stream's cross K ([heads][ctx][hd], scaled) and Vᵀ ([heads][hd][ctx]) of a layer.

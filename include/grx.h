@@ -417,6 +417,23 @@ int grx_whisper_prompt(grx_whisper_batch* b, const int* prompt, int np, int sot_
 int grx_whisper_run(grx_whisper_batch* b, int steps, int* tokens);
 int grx_whisper_run_device(grx_whisper_batch* b, int steps, int* d_tokens);
 int grx_whisper_sync(grx_whisper_batch* b);
+/* 1 when the batch runs its token loop in the persistent one-stream kernel:
+ * a batch of one stream whose model has 64-value heads, Q8_0 or float16
+ * matrices with whole groups of 16 columns and at most 12 layers runs every
+ * step of grx_whisper_run(_device) as one cooperative launch, one block per
+ * SM, with grid barriers between a step's dependent parts (GRX_WSTEP1=0,
+ * read when the batch is created, keeps the per-kernel path). Same tokens
+ * bit for bit. Its waits are bounded (about a second each); one that runs
+ * out makes grx_whisper_run / grx_whisper_sync return GRX_ETIMEDOUT. 0
+ * otherwise. */
+int grx_whisper_persistent(const grx_whisper_batch* b);
+/* Checks the persistent kernel's watchdog: runs one step with a grid barrier
+ * that nothing completes and returns what its bounded waits report —
+ * GRX_ETIMEDOUT, after about a second, when they work. The batch's decoding
+ * state is undefined afterwards; set the window and decode a prompt again.
+ * GRX_EINVAL for a batch that does not run the persistent kernel or has no
+ * prompt decoded. */
+int grx_whisper_watchdog_test(grx_whisper_batch* b);
 /* Stream i's cross K [heads][ctx][64] and Vᵀ [heads][64][ctx] of a layer. */
 int grx_whisper_cross(grx_whisper_batch* b, int i, int layer, float* k, float* vt);
 /* The logits of the last decode, [n][n_vocab]. */
