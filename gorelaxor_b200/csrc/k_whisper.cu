@@ -320,12 +320,14 @@ __device__ void wcross_softmax(float* sc, int ctx, float mx, float* sh) {
   __syncthreads();
 }
 
-// o[d] for d = d0 + grp + ng·i, i < ND (ng groups of 16 lanes): the 16
-// lanes chain over ctx&~15 in steps of 16, then the HSUM and dotF32Go of
-// the rest; p = probabilities in shared memory, V row d at vb + (d − vd0)·ctx.
+// o[d] for d = d0 + grp + ng·i, i < ND (ng groups of 16 lanes, or only the
+// first ngrp groups when given): the 16 lanes chain over ctx&~15 in steps of
+// 16, then the HSUM and dotF32Go of the rest; p = probabilities in shared
+// memory, V row d at vb + (d − vd0)·ctx.
 template <int ND>
-__device__ void wcross_out(const float* p, const float* vb, int ctx, int d0, float* att, int vd0 = 0) {
+__device__ void wcross_out(const float* p, const float* vb, int ctx, int d0, float* att, int vd0 = 0, int ngrp = 0) {
   const int l16 = threadIdx.x & 15, grp = threadIdx.x >> 4, ng = blockDim.x >> 4;
+  if (ngrp && grp >= ngrp) return;  // whole warps (ngrp even)
   const int cf = ctx & ~15;
   float acc[ND];
 #pragma unroll
@@ -1170,18 +1172,25 @@ __global__ void k_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int 
 // stream — process/sample of the last logits, then the decode of the sampled
 // token — in one cooperative launch of one 512-thread CTA per SM, with a
 // grid barrier where a step needs every CTA's results. Per layer: the q/k/v
-// rows, self-attention (a CTA per head), o with the residual, LayerNorm and
-// xq, the cross scores (key chunks over the CTAs), the softmax and values
-// (two CTAs a head), xo with the residual, LayerNorm and fc1, fc2 with the
-// residual; then the final LayerNorm and the logits rows. Every CTA keeps a
-// copy of the residual row and forms the LayerNorms itself. The arithmetic
-// is the per-kernel path's: the products in k_flin's float-path lane order
-// (one 8-lane group per output row, dot4f16avx with Q8_0 widened as
-// f16(q·d)), the attention and process/sample code shared with those
-// kernels; process/sample's sums combine the CTAs' partials in CTA order
-// (the margins make the order safe, as for the cluster form). Every wait is
-// bounded (about a second); one that runs out sets the error word and every
-// CTA leaves.
+// rows, self-attention (a few CTAs a head, each with some of its outputs),
+// o with the residual, LayerNorm and xq, the cross scores (key chunks over
+// the CTAs), the softmax and values (a slice of a head's outputs a CTA, its
+// Vᵀ rows staged by async copies), xo with the residual, LayerNorm and fc1,
+// fc2 with the residual; then the final LayerNorm and the logits rows. Every
+// CTA keeps a copy of the residual row and forms the LayerNorms itself.
+//
+// Each CTA's weight rows reach shared memory ahead of use: a ring of two
+// buffers, the next layer's rows of all eight matrices (or the next chunk of
+// logits rows) copied by cp.async while the current one is computed, so the
+// products run on staged rows and only the barriers wait on memory.
+//
+// The arithmetic is the per-kernel path's: the products in k_flin's
+// float-path lane order (one 8-lane group per output row, dot4f16avx with
+// Q8_0 widened as f16(q·d)), the attention and process/sample code shared
+// with those kernels; process/sample's sums combine the CTAs' partials in one
+// fixed order on every CTA (the margins make the order safe, as for the
+// cluster form). Every wait is bounded (about a second); one that runs out
+// sets the error word and every CTA leaves.
 constexpr int WS_NT = 512;
 constexpr unsigned long long kWsWaitNs = 1000000000ull;
 
@@ -1219,17 +1228,42 @@ __device__ bool ws_sync(const WStep1Args& A, WsCtl& ctl) {
 }
 
 // process/sample's reductions over the whole grid: each CTA's block result
-// to its column of the partials, the grid barrier, then every thread
-// combines the columns in CTA order. Float slots: 0-2 the maxima, 3-5 the
-// sums, 6-7 the "near" maxima; (value, index) slots 0-1.
+// to its column of the partials, the grid barrier, then every CTA loads the
+// columns into shared memory at once and combines them in one fixed order —
+// lane l of a warp takes CTAs l, l+32, ... in sequence, then an xor tree over
+// the lanes. Float slots: 0-2 the maxima, 3-5 the sums, 6-7 the "near"
+// maxima; (value, index) slots 0-1.
 struct GridRed {
   const WStep1Args& A;
   WsCtl& ctl;
   float* shf;
   VI* shv;
-  __device__ float col(int slot, int k) const { return A.part[size_t(slot) * gridDim.x + k]; }
+  float* gcol;  // [3][WS1_MAX_GRID] gathered columns
+  VI* gvi;      // [2][WS1_MAX_GRID]
+  float* res;   // [3] combined results
+  VI* resv;     // [2]
   __device__ void put(int slot, float v) const {
     if (threadIdx.x == 0) A.part[size_t(slot) * gridDim.x + blockIdx.x] = v;
+  }
+  __device__ void gather(int s0, int ns) const {
+    const int G = gridDim.x;
+    for (int t = threadIdx.x; t < ns * G; t += blockDim.x) gcol[t] = A.part[size_t(s0) * G + t];
+    __syncthreads();
+  }
+  // warp j < ns: slot j's maximum (sum = false) or sum into res[j]
+  __device__ void combine(int ns, bool sum) const {
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, G = gridDim.x;
+    if (w < ns) {
+      float a = sum ? 0.f : NINF;
+      for (int k = l; k < G; k += 32) a = sum ? __fadd_rn(a, gcol[w * G + k]) : fmaxf(a, gcol[w * G + k]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float b = __shfl_xor_sync(0xffffffffu, a, o);
+        a = sum ? __fadd_rn(a, b) : fmaxf(a, b);
+      }
+      if (l == 0) res[w] = a;
+    }
+    __syncthreads();
   }
   __device__ void max3(float& a, float& b, float& c) {
     a = block_max(a, shf);
@@ -1237,34 +1271,51 @@ struct GridRed {
     c = block_max(c, shf);
     put(0, a), put(1, b), put(2, c);
     ws_sync(A, ctl);
-    a = b = c = NINF;
-    for (int k = 0; k < int(gridDim.x); k++) a = fmaxf(a, col(0, k)), b = fmaxf(b, col(1, k)), c = fmaxf(c, col(2, k));
+    gather(0, 3);
+    combine(3, false);
+    a = res[0], b = res[1], c = res[2];
   }
   __device__ float sum(float v, int slot) {
     v = block_sum(v, shf);
     put(3 + slot, v);
     ws_sync(A, ctl);
-    float r = 0.f;
-    for (int k = 0; k < int(gridDim.x); k++) r = __fadd_rn(r, col(3 + slot, k));
-    return r;
+    gather(3 + slot, 1);
+    combine(1, true);
+    return res[0];
   }
   __device__ void vimax2(VI& a, VI& b) {
     a = block_vi_max(a, shv);
     b = block_vi_max(b, shv);
     VI* pv = reinterpret_cast<VI*>(A.partv);
-    if (threadIdx.x == 0) pv[blockIdx.x] = a, pv[gridDim.x + blockIdx.x] = b;
+    const int G = gridDim.x;
+    if (threadIdx.x == 0) pv[blockIdx.x] = a, pv[G + blockIdx.x] = b;
     ws_sync(A, ctl);
-    a = pv[0];
-    b = pv[gridDim.x];
-    for (int k = 1; k < int(gridDim.x); k++) a = vi_max(a, pv[k]), b = vi_max(b, pv[gridDim.x + k]);
+    for (int t = threadIdx.x; t < 2 * G; t += blockDim.x) gvi[t] = pv[t];
+    __syncthreads();
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (w < 2) {
+      VI x{-1.f, 0x7fffffff};
+      for (int k = l; k < G; k += 32) x = vi_max(x, gvi[w * G + k]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        VI y;
+        y.v = __shfl_xor_sync(0xffffffffu, x.v, o);
+        y.i = __shfl_xor_sync(0xffffffffu, x.i, o);
+        x = vi_max(x, y);
+      }
+      if (l == 0) resv[w] = x;
+    }
+    __syncthreads();
+    a = resv[0], b = resv[1];
   }
   __device__ void max2(float& a, float& b) {
     a = block_max(a, shf);
     b = block_max(b, shf);
     put(6, a), put(7, b);
     ws_sync(A, ctl);
-    a = b = NINF;
-    for (int k = 0; k < int(gridDim.x); k++) a = fmaxf(a, col(6, k)), b = fmaxf(b, col(7, k));
+    gather(6, 2);
+    combine(2, false);
+    a = res[0], b = res[1];
   }
   __device__ void done() {}
 };
@@ -1289,37 +1340,90 @@ __device__ void ws_ln(const float* x, float* y, const float* w, const float* b, 
   __syncthreads();
 }
 
-// A weight value as the decoder's products read it: float16, or a Q8_0
-// value widened as f16(q·d) (whisper/model.go:486-490).
-__device__ __forceinline__ float ws_w(const WMat& w, int n, int k, int K) {
-  if (w.h) return __half2float(__ushort_as_half(w.h[(size_t)n * K + k]));
-  return q8h(w.q[(size_t)n * K + k], h2f(w.d[(size_t)n * (K / QK) + k / QK]));
+// ---- async copies into shared memory (cp.async; completion per thread,
+// then a CTA barrier before other threads read)
+__device__ __forceinline__ void cpa16(void* s, const void* g) {
+  const unsigned sa = unsigned(__cvta_generic_to_shared(s));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cpa8(void* s, const void* g) {
+  const unsigned sa = unsigned(__cvta_generic_to_shared(s));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(sa), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cpa4(void* s, const void* g) {
+  const unsigned sa = unsigned(__cvta_generic_to_shared(s));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Rows [r0, r1) of w (K columns) staged in shared memory at s: float16 rows
+// of 2K + 16 bytes, or Q8_0 rows of K + 16 int8 values followed by the rows'
+// K/32 float16 scales (the padding keeps four rows read by one warp in
+// different banks).
+__device__ void ws_stage(const WMat& w, int K, int r0, int r1, unsigned char* s) {
+  const int R = r1 - r0;
+  if (w.h) {
+    const int cpr = K / 8;
+    const unsigned char* g = reinterpret_cast<const unsigned char*>(w.h + (size_t)r0 * K);
+    for (int t = threadIdx.x; t < R * cpr; t += blockDim.x) {
+      const int r = t / cpr, c = t - r * cpr;
+      cpa16(s + r * (2 * K + 16) + c * 16, g + (size_t)r * 2 * K + c * 16);
+    }
+  } else {
+    const int cpr = K / 16;
+    const unsigned char* g = reinterpret_cast<const unsigned char*>(w.q + (size_t)r0 * K);
+    for (int t = threadIdx.x; t < R * cpr; t += blockDim.x) {
+      const int r = t / cpr, c = t - r * cpr;
+      cpa16(s + r * (K + 16) + c * 16, g + (size_t)r * K + c * 16);
+    }
+    const unsigned char* gd = reinterpret_cast<const unsigned char*>(w.d + (size_t)r0 * (K / QK));
+    unsigned char* sd = s + R * (K + 16);
+    for (int t = threadIdx.x; t < R * K / 64; t += blockDim.x) cpa4(sd + 4 * t, gd + 4 * t);
+  }
 }
 
 enum { WS_STORE = 0, WS_RESID = 1, WS_GELU = 2 };
 
 // Rows [r0, r1) of y = W·x (+ bias) for one input row x (shared memory, K
-// values): one 8-lane group per output row, lane l accumulating elements
-// 16c + l and 16c + 8 + l over c in order, then the two added and the HSUM
-// ((a0+a4)+(a1+a5))+((a2+a6)+(a3+a7)) — k_flin's order (dot4f16avx). RESID
-// stores res[n] + (dot + bias), GELU geluAVX(dot + bias).
+// values) from the rows staged at s: one 8-lane group per output row, lane
+// l accumulating elements 16c + l and 16c + 8 + l over c in order, then the
+// two added and the HSUM ((a0+a4)+(a1+a5))+((a2+a6)+(a3+a7)) — k_flin's
+// order (dot4f16avx), Q8_0 values widened as f16(q·d) (whisper/model.go:
+// 486-490). RESID stores res[n] + (dot + bias), GELU geluAVX(dot + bias).
 template <int EPI>
-__device__ void ws_rows(const WMat& w, const float* x, int K, int r0, int r1, const float* bias, float* y,
-                        const float* res) {
-  const int g = threadIdx.x >> 3, l = threadIdx.x & 7, ng = blockDim.x >> 3;
+__device__ void ws_rows(bool f16, const unsigned char* s, const float* x, int K, int r0, int r1, const float* bias,
+                        float* y, const float* res) {
+  const int g = threadIdx.x >> 3, l = threadIdx.x & 7, ng = blockDim.x >> 3, R = r1 - r0;
   const unsigned gm = 0xffu << (threadIdx.x & 24);
-  for (int n = r0 + g; n < r1; n += ng) {
+  for (int r = g; r < R; r += ng) {
     float a = 0.f, a1 = 0.f;
-#pragma unroll 4
-    for (int c16 = 0; c16 < K; c16 += 16) {
-      a = __fmaf_rn(x[c16 + l], ws_w(w, n, c16 + l, K), a);
-      a1 = __fmaf_rn(x[c16 + 8 + l], ws_w(w, n, c16 + 8 + l, K), a1);
+    if (f16) {
+      const uint16_t* wr = reinterpret_cast<const uint16_t*>(s + r * (2 * K + 16));
+#pragma unroll 8
+      for (int c16 = 0; c16 < K; c16 += 16) {
+        a = __fmaf_rn(x[c16 + l], h2f(wr[c16 + l]), a);
+        a1 = __fmaf_rn(x[c16 + 8 + l], h2f(wr[c16 + 8 + l]), a1);
+      }
+    } else {
+      const int8_t* wr = reinterpret_cast<const int8_t*>(s + r * (K + 16));
+      const uint16_t* dr = reinterpret_cast<const uint16_t*>(s + R * (K + 16)) + r * (K / QK);
+#pragma unroll 8
+      for (int c16 = 0; c16 < K; c16 += 16) {
+        const float d = h2f(dr[c16 / QK]);
+        a = __fmaf_rn(x[c16 + l], q8h(wr[c16 + l], d), a);
+        a1 = __fmaf_rn(x[c16 + 8 + l], q8h(wr[c16 + 8 + l], d), a1);
+      }
     }
     float v = __fadd_rn(a, a1);
     v = __fadd_rn(v, __shfl_xor_sync(gm, v, 4));
     v = __fadd_rn(v, __shfl_xor_sync(gm, v, 1));
     v = __fadd_rn(v, __shfl_xor_sync(gm, v, 2));
     if (l == 0) {
+      const int n = r0 + r;
       const float o = bias ? __fadd_rn(v, bias[n]) : v;
       if (EPI == WS_RESID)
         y[n] = __fadd_rn(res[n], o);
@@ -1331,9 +1435,31 @@ __device__ void ws_rows(const WMat& w, const float* x, int K, int r0, int r1, co
   }
 }
 
-// Self-attention of head h over keys 0..n-1 (decoder.go:70-87, as k_wself).
-__device__ void ws_self(const float* q, const float* sk, const float* sv, int st, int n, int h, float* sc, float* qh,
-                        float* sh, float* att) {
+// This CTA's rows of a layer's eight matrices in the order q, k, v, o, xq,
+// xo, fc1, fc2: their offsets in a weight buffer.
+struct WsPlan {
+  int off[9];
+};
+
+__device__ WsPlan ws_plan(const WS1Layer& Y, int st, int ff, int R, int Rf) {
+  WsPlan p;
+  const WMat* m[8] = {&Y.q, &Y.k, &Y.v, &Y.o, &Y.xq, &Y.xo, &Y.fc1, &Y.fc2};
+  p.off[0] = 0;
+  for (int i = 0; i < 8; i++)
+    p.off[i + 1] = p.off[i] + ws_slice_bytes(m[i]->h != nullptr, i == 6 ? Rf : R, i == 7 ? ff : st);
+  return p;
+}
+
+// Self-attention of head h over keys 0..n-1 (decoder.go:70-87, as k_wself),
+// outputs d0..d0+nd-1 of the head: every CTA of the head takes the scores
+// and softmax, its nd columns of V staged by async copies meanwhile.
+__device__ void ws_self(const float* q, const float* sk, const float* sv, int st, int n, int h, int d0, int nd,
+                        float* sc, float* qh, float* vs, float* sh, float* att) {
+  for (int t = threadIdx.x; t < n * (nd / 2); t += blockDim.x) {
+    const int j = t / (nd / 2), c = t - j * (nd / 2);
+    cpa8(vs + j * nd + 2 * c, sv + (size_t)j * st + h * 64 + d0 + 2 * c);
+  }
+  cpa_commit();
   if (threadIdx.x < 64) qh[threadIdx.x] = q[h * 64 + threadIdx.x];
   __syncthreads();
   const float scale = float(1.0 / sqrt(double(64)));
@@ -1358,40 +1484,77 @@ __device__ void ws_self(const float* q, const float* sk, const float* sv, int st
   const float sum = exp_sub(sc, n, mx, sh);
   const float inv = __fdiv_rn(1.f, sum);
   for (int j = threadIdx.x; j < n; j += blockDim.x) sc[j] = __fmul_rn(sc[j], inv);
+  cpa_wait<0>();
   __syncthreads();
-  if (threadIdx.x < 64) {
-    const float* vb = sv + h * 64 + threadIdx.x;
+  if (threadIdx.x < nd) {
     float o = 0.f;
-    for (int j = 0; j < n; j++) o = __fadd_rn(o, __fmul_rn(sc[j], vb[(size_t)j * st]));
-    att[h * 64 + threadIdx.x] = o;
+#pragma unroll 8
+    for (int j = 0; j < n; j++) o = __fadd_rn(o, __fmul_rn(sc[j], vs[j * nd + threadIdx.x]));
+    att[h * 64 + d0 + threadIdx.x] = o;
   }
   __syncthreads();
 }
 
 __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restrict__ Ap, int pos0, int steps) {
   const WStep1Args& A = *Ap;
-  extern __shared__ __align__(16) float wsm[];
-  const int st = A.st, ff = A.ff, ctx = A.ctx, nh = A.nh, G = gridDim.x, cta = blockIdx.x;
-  float* xs = wsm;                   // [st] the residual row
-  float* cur = xs + st;              // [max(st, ff)] a product's input
-  float* sc = cur + max(st, ff);     // [max(ctx, text_ctx)] scores
+  extern __shared__ __align__(128) float ws1m[];
+  const int st = A.st, ff = A.ff, ctx = A.ctx, nh = A.nh, G = gridDim.x, cta = blockIdx.x, L = A.L;
+  float* xs = ws1m;                       // [st] the residual row
+  float* cur = xs + st;                   // [max(st, ff)] a product's input
+  float* sc = cur + max(st, ff);          // [max(ctx, text_ctx)] scores
   float* qh = sc + max(ctx, A.text_ctx);  // [64]
+  float* xv = qh + 64;                    // [xv_floats] staged V columns
+  unsigned char* wbuf = reinterpret_cast<unsigned char*>(xv + A.xv_floats);  // [2][wb] weight rows
   __shared__ float shf[40];
   __shared__ VI shv[32];
   __shared__ double shd[32];
+  __shared__ float gcol[3 * WS1_MAX_GRID];
+  __shared__ VI gvi[2 * WS1_MAX_GRID];
+  __shared__ float gres[3];
+  __shared__ VI gresv[2];
   __shared__ WsCtl ctl;
   if (threadIdx.x == 0) ctl.bar_k = 0, ctl.fail = 0;
   __syncthreads();
-  GridRed red{A, ctl, shf, shv};
+  GridRed red{A, ctl, shf, shv, gcol, gvi, gres, gresv};
+  // this CTA's rows: [r0, r1) of the state-sized products, [f0, f1) of fc1,
+  // [v0, v1) of the logits in chunks of A.lrows
+  const int r0 = ws_split(st, cta, G), r1 = ws_split(st, cta + 1, G);
+  const int f0 = ws_split(ff, cta, G), f1 = ws_split(ff, cta + 1, G);
+  const int v0 = ws_split(A.vocab, cta, G), v1 = ws_split(A.vocab, cta + 1, G);
+  const int nchunk = max(1, (v1 - v0 + A.lrows - 1) / A.lrows);
+  const int items = L + nchunk;  // staged items a step: the layers, then the logits chunks
+  const bool emb16 = A.emb.h != nullptr;
+  auto stage = [&](int t, unsigned char* buf) {
+    if (t < L) {
+      const WS1Layer& Y = A.layers[t];
+      const WsPlan p = ws_plan(Y, st, ff, r1 - r0, f1 - f0);
+      const WMat* m[8] = {&Y.q, &Y.k, &Y.v, &Y.o, &Y.xq, &Y.xo, &Y.fc1, &Y.fc2};
+      for (int i = 0; i < 8; i++)
+        ws_stage(*m[i], i == 7 ? ff : st, i == 6 ? f0 : r0, i == 6 ? f1 : r1, buf + p.off[i]);
+    } else {
+      const int a = min(v1, v0 + (t - L) * A.lrows), b = min(v1, a + A.lrows);
+      ws_stage(A.emb, st, a, b, buf);
+    }
+  };
+  // item t of the step is consumed from buffer qi & 1; on entry the next
+  // item goes to the other buffer (whose last reader finished behind a CTA
+  // barrier), then this one's copies are waited for
+  int qi = 0;
+  auto consume = [&](int t) -> unsigned char* {
+    stage((t + 1) % items, wbuf + size_t((qi + 1) & 1) * A.wb);
+    cpa_commit();
+    cpa_wait<1>();
+    __syncthreads();
+    return wbuf + size_t((qi++) & 1) * A.wb;
+  };
+  stage(0, wbuf);
+  cpa_commit();
   // the cross scores' key chunks: about G / nh per head, whole groups of 16
   const int ctx4 = ctx & ~3;
   int ks = max(1, G / nh);
   const int ch = ((ctx4 + ks - 1) / ks + 15) / 16 * 16;
   ks = (ctx4 + ch - 1) / ch;
-  auto rows = [&](int n, int& r0, int& r1) {
-    r0 = ws_split(n, cta, G);
-    r1 = ws_split(n, cta + 1, G);
-  };
+  const int so_s = 64 / A.so_nd, xo_s = 64 / A.xo_nd;  // CTAs a head for self-attention and the values
   auto load = [&](float* dst, const float* src, int n) {
     for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
     __syncthreads();
@@ -1399,31 +1562,31 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
   int i = 0;
   for (; i < steps; i++) {
     // ---- process + sample of the last logits (transcribe.go:370-494)
-    proc_row(red, A.logits, A.scratch, A.voc, A.state, A.out + 4 * i, A.row_tok, ws_split(A.vocab, cta, G),
-             ws_split(A.vocab, cta + 1, G), cta == 0);
+    proc_row(red, A.logits, A.scratch, A.voc, A.state, A.out + 4 * i, A.row_tok, v0, v1, cta == 0);
     if (!ws_sync(A, ctl)) break;
     const int pos = pos0 + i, tok = A.row_tok[0];
     // ---- decode of the token at pos (decoder.go:33-140): the embedding
     for (int j = threadIdx.x; j < st; j += blockDim.x)
       xs[j] = __fadd_rn(wmat_at(A.emb, tok, j), A.dec_pos[(size_t)pos * st + j]);
     __syncthreads();
-    int r0, r1;
-    for (int l = 0; l < A.L; l++) {
+    for (int l = 0; l < L; l++) {
       const WS1Layer& Y = A.layers[l];
+      const unsigned char* wl = consume(l);
+      const WsPlan p = ws_plan(Y, st, ff, r1 - r0, f1 - f0);
       ws_ln(xs, cur, Y.ln1w, Y.ln1b, st, shd);
-      rows(st, r0, r1);
-      ws_rows<WS_STORE>(Y.q, cur, st, r0, r1, Y.qb, A.q, nullptr);
-      ws_rows<WS_STORE>(Y.k, cur, st, r0, r1, nullptr, Y.sk + (size_t)pos * st, nullptr);
-      ws_rows<WS_STORE>(Y.v, cur, st, r0, r1, Y.vb, Y.sv + (size_t)pos * st, nullptr);
+      ws_rows<WS_STORE>(Y.q.h != nullptr, wl + p.off[0], cur, st, r0, r1, Y.qb, A.q, nullptr);
+      ws_rows<WS_STORE>(Y.k.h != nullptr, wl + p.off[1], cur, st, r0, r1, nullptr, Y.sk + (size_t)pos * st, nullptr);
+      ws_rows<WS_STORE>(Y.v.h != nullptr, wl + p.off[2], cur, st, r0, r1, Y.vb, Y.sv + (size_t)pos * st, nullptr);
       if (!ws_sync(A, ctl)) break;
-      if (cta < nh) ws_self(A.q, Y.sk, Y.sv, st, pos + 1, cta, sc, qh, shf, A.att);
+      if (cta < nh * so_s)
+        ws_self(A.q, Y.sk, Y.sv, st, pos + 1, cta / so_s, (cta % so_s) * A.so_nd, A.so_nd, sc, qh, xv, shf, A.att);
       if (!ws_sync(A, ctl)) break;
       load(cur, A.att, st);
-      ws_rows<WS_RESID>(Y.o, cur, st, r0, r1, Y.ob, A.x, xs);
+      ws_rows<WS_RESID>(Y.o.h != nullptr, wl + p.off[3], cur, st, r0, r1, Y.ob, A.x, xs);
       if (!ws_sync(A, ctl)) break;
       load(xs, A.x, st);
       ws_ln(xs, cur, Y.ln2w, Y.ln2b, st, shd);
-      ws_rows<WS_STORE>(Y.xq, cur, st, r0, r1, Y.xqb, A.q, nullptr);
+      ws_rows<WS_STORE>(Y.xq.h != nullptr, wl + p.off[4], cur, st, r0, r1, Y.xqb, A.q, nullptr);
       if (!ws_sync(A, ctl)) break;
       if (cta < nh * ks) {  // cross scores of key chunk cta % ks of head cta / ks
         const int h = cta / ks, kc = cta % ks, j0 = kc * ch, j1 = min(ctx4, j0 + ch);
@@ -1434,36 +1597,44 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
         if (threadIdx.x == 0) A.mg[h * ks + kc] = mx;
       }
       if (!ws_sync(A, ctl)) break;
-      if (cta < nh * 2) {  // softmax and 32 of the 64 outputs of head cta / 2
-        const int h = cta / 2, d0 = (cta % 2) * 32;
-        float mx = NINF;
-        for (int k = 0; k < ks; k++) mx = fmaxf(mx, A.mg[h * ks + k]);
+      if (cta < nh * xo_s) {  // softmax and outputs d0..d0+xo_nd-1 of head h
+        const int h = cta / xo_s, d0 = (cta % xo_s) * A.xo_nd;
+        const float* vrow = Y.cvt + ((size_t)h * 64 + d0) * ctx;
+        for (int t = threadIdx.x; t < A.xo_nd * ctx / 4; t += blockDim.x) cpa16(xv + 4 * t, vrow + 4 * t);
+        cpa_commit();
+        float mx = threadIdx.x < ks ? A.mg[h * ks + threadIdx.x] : NINF;
+        mx = block_max(mx, shf);
         load(sc, A.sg + (size_t)h * ctx, ctx);
         wcross_softmax(sc, ctx, mx, shf);
-        wcross_out<1>(sc, Y.cvt + (size_t)h * 64 * ctx, ctx, d0, A.att + h * 64);
+        cpa_wait<0>();
+        __syncthreads();
+        wcross_out<1>(sc, xv, ctx, d0, A.att + h * 64, d0, A.xo_nd);
       }
       if (!ws_sync(A, ctl)) break;
       load(cur, A.att, st);
-      ws_rows<WS_RESID>(Y.xo, cur, st, r0, r1, Y.xob, A.x, xs);
+      ws_rows<WS_RESID>(Y.xo.h != nullptr, wl + p.off[5], cur, st, r0, r1, Y.xob, A.x, xs);
       if (!ws_sync(A, ctl)) break;
       load(xs, A.x, st);
       ws_ln(xs, cur, Y.ln3w, Y.ln3b, st, shd);
-      int f0, f1;
-      rows(ff, f0, f1);
-      ws_rows<WS_GELU>(Y.fc1, cur, st, f0, f1, Y.fc1b, A.ffb, nullptr);
+      ws_rows<WS_GELU>(Y.fc1.h != nullptr, wl + p.off[6], cur, st, f0, f1, Y.fc1b, A.ffb, nullptr);
       if (!ws_sync(A, ctl)) break;
       load(cur, A.ffb, ff);
-      ws_rows<WS_RESID>(Y.fc2, cur, ff, r0, r1, Y.fc2b, A.x, xs);
+      ws_rows<WS_RESID>(Y.fc2.h != nullptr, wl + p.off[7], cur, ff, r0, r1, Y.fc2b, A.x, xs);
       if (!ws_sync(A, ctl)) break;
       load(xs, A.x, st);
     }
     if (ctl.fail) break;
-    // ---- the final LayerNorm and the logits (no bias)
+    // ---- the final LayerNorm and the logits (no bias), chunk by chunk
     ws_ln(xs, cur, A.lnw, A.lnb, st, shd);
-    rows(A.vocab, r0, r1);
-    ws_rows<WS_STORE>(A.emb, cur, st, r0, r1, nullptr, A.logits, nullptr);
+    for (int c = 0; c < nchunk; c++) {
+      const unsigned char* wl = consume(L + c);
+      const int a = min(v1, v0 + c * A.lrows), b = min(v1, a + A.lrows);
+      ws_rows<WS_STORE>(emb16, wl, cur, st, a, b, nullptr, A.logits, nullptr);
+      __syncthreads();
+    }
     if (!ws_sync(A, ctl)) break;
   }
+  cpa_wait<0>();  // the prefetch for a next step
   // the positions and the run's step counter, as the per-kernel path leaves them
   if (cta == 0 && threadIdx.x == 0 && !ctl.fail) {
     A.row_pos[0] = pos0 + steps;
@@ -1630,13 +1801,21 @@ void launch_wenc_softmax(float* x, int len, long rows, cudaStream_t st) {
 void whisper_kernels_init() {}
 
 size_t wstep1_smem(const WStep1Args& a) {
-  return sizeof(float) * (size_t(a.st) + size_t(std::max(a.st, a.ff)) + size_t(std::max(a.ctx, a.text_ctx)) + 64);
+  const size_t floats = size_t(a.st) + size_t(std::max(a.st, a.ff)) + size_t(std::max(a.ctx, a.text_ctx)) + 64 +
+                        size_t(a.xv_floats);
+  return sizeof(float) * floats + 2 * size_t(a.wb);
 }
 
 int wstep1_max_active(size_t smem) {
   int n = 0;
-  cudaFuncSetAttribute(k_wstep1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_wstep1, WS_NT, smem) != cudaSuccess) return 0;
+  if (cudaFuncSetAttribute(k_wstep1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_wstep1, WS_NT, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
   return n;
 }
 

@@ -414,6 +414,7 @@ struct WVocabDev {
 
 // ---- the token loop of one Whisper stream in one cooperative launch
 constexpr int WS1_MAX_LAYERS = 12;
+constexpr int WS1_MAX_GRID = 160;  // CTAs of the persistent Whisper kernel at most
 struct WS1Layer {
   WMat q, k, v, o, xq, xo, fc1, fc2;
   const float *qb, *vb, *ob, *xqb, *xob, *fc1b, *fc2b;
@@ -435,7 +436,18 @@ struct WStep1Args {
   unsigned* bar = nullptr;   // grid barrier arrivals (zeroed before a launch)
   int* err = nullptr;        // 1: a wait ran out
   int stall = 0;             // test hook: the first barrier never completes
+  // shared-memory plan: two weight buffers of wb bytes, logits rows staged
+  // lrows at a time, so_nd / xo_nd outputs of a head per CTA in the self-
+  // and cross-attention values, xv_floats floats of staged V columns
+  int wb = 0, lrows = 0, so_nd = 0, xo_nd = 0, xv_floats = 0;
 };
+
+// Bytes of R rows of K columns staged in shared memory by the persistent
+// Whisper kernel: float16 rows of 2K + 16 bytes, or Q8_0 rows of K + 16
+// int8 values and then the rows' float16 scales, rounded up to 16.
+__host__ __device__ inline int ws_slice_bytes(bool f16, int R, int K) {
+  return f16 ? R * (2 * K + 16) : (R * (K + 16) + R * (K / 16) + 15) / 16 * 16;
+}
 // Shared memory a CTA of the kernel needs; whether the device runs it (one
 // 512-thread CTA per SM, cooperative launch); the launch (steps rounds of
 // sample-then-decode from position pos0).

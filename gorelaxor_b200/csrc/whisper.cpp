@@ -289,17 +289,21 @@ int capture(grx_whisper_batch* b, bool with_sample, cudaGraphExec_t* out) {
 
 // The persistent token loop for a batch of one stream when the model and the
 // device suit it (GRX_WSTEP1=0 keeps the per-kernel graph): 64-value heads,
-// K of every product a multiple of 16, Q8_0 or float16 matrices, a
-// cooperative launch of one CTA per SM.
+// K of every product a multiple of 64, Q8_0 or float16 matrices whose rows
+// can be copied in 16-byte pieces, a cooperative launch of one CTA per SM
+// with the weight buffers in shared memory.
 int ws1_setup(grx_whisper_batch* b) {
   const char* env = getenv("GRX_WSTEP1");
   const grx_whisper* m = b->m;
-  if ((env && env[0] == '0') || b->n != 1 || m->n_head * 64 != m->n_state || m->n_state % 16 ||
-      m->layers.empty() || m->layers.size() > size_t(WS1_MAX_LAYERS) || m->n_vocab % 4 || m->n_audio_ctx % 4)
+  if ((env && env[0] == '0') || b->n != 1 || m->n_head * 64 != m->n_state || m->layers.empty() ||
+      m->layers.size() > size_t(WS1_MAX_LAYERS) || m->n_vocab % 4 || m->n_audio_ctx % 4 || m->n_text_ctx % 4)
     return GRX_OK;
-  auto ok = [](const WMat& w) { return (w.q != nullptr || w.h != nullptr) && w.f == nullptr && w.cols % 16 == 0; };
+  auto al = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
+  auto ok = [&](const WMat& w) {
+    return w.f == nullptr && w.cols % 64 == 0 && (w.h ? al(w.h, 16) : w.q != nullptr && al(w.q, 16) && al(w.d, 4));
+  };
   const int ff = m->layers[0].fc1.rows;
-  if (!ok(m->tok_emb) || ff % 16) return GRX_OK;
+  if (!ok(m->tok_emb) || ff % 64 || !al(b->sv, 16) || !al(b->cvt, 16)) return GRX_OK;
   for (const WLayerDev& L : m->layers)
     if (!ok(L.q) || !ok(L.k) || !ok(L.v) || !ok(L.o) || !ok(L.xq) || !ok(L.xo) || !ok(L.fc1) || !ok(L.fc2) ||
         L.fc1.rows != ff)
@@ -307,7 +311,7 @@ int ws1_setup(grx_whisper_batch* b) {
   int G = 0, coop = 0;
   CK(cudaDeviceGetAttribute(&G, cudaDevAttrMultiProcessorCount, b->ar.dev));
   CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, b->ar.dev));
-  if (!coop || G < 2 * m->n_head) return GRX_OK;
+  if (!coop || G < 2 * m->n_head || G > WS1_MAX_GRID) return GRX_OK;
   WStep1Args A;
   A.st = m->n_state;
   A.nh = m->n_head;
@@ -340,8 +344,28 @@ int ws1_setup(grx_whisper_batch* b) {
   A.step = b->step;
   A.logits = b->logits;
   A.scratch = b->scratch;
+  // shared-memory plan: a weight buffer holds one layer's rows of this CTA
+  // (at most ceil(n/G) rows of each product) or a chunk of logits rows
+  const int R = (A.st + G - 1) / G, Rf = (ff + G - 1) / G;
+  int wb = 0;
+  for (const WS1Layer& Y : A.layers) {
+    if (&Y - A.layers >= A.L) break;
+    const WMat* mm[8] = {&Y.q, &Y.k, &Y.v, &Y.o, &Y.xq, &Y.xo, &Y.fc1, &Y.fc2};
+    int lb = 0;
+    for (int i = 0; i < 8; i++) lb += ws_slice_bytes(mm[i]->h != nullptr, i == 6 ? Rf : R, i == 7 ? ff : A.st);
+    wb = std::max(wb, lb);
+  }
+  A.lrows = std::min(64, (A.vocab + G - 1) / G);
+  wb = std::max(wb, ws_slice_bytes(A.emb.h != nullptr, A.lrows, A.st));
+  A.wb = (wb + 15) / 16 * 16;
+  // CTAs a head in the self-attention and cross values: a power of two up
+  // to 32 that fits G / heads, each with 64 / that outputs
+  int per = 1;
+  while (per * 2 <= std::min(32, G / A.nh)) per *= 2;
+  A.so_nd = A.xo_nd = 64 / per;
+  A.xv_floats = std::max(A.xo_nd * A.ctx, A.so_nd * A.text_ctx);
   const size_t smem = wstep1_smem(A);
-  if (smem > 200 * 1024 || wstep1_max_active(smem) < 1) return GRX_OK;
+  if (wstep1_max_active(smem) < 1) return GRX_OK;
   int rc = 0;
   A.x = b->ar.alloc<float>(size_t(A.st), &rc);
   A.q = b->ar.alloc<float>(size_t(A.st), &rc);
