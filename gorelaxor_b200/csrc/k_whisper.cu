@@ -260,7 +260,7 @@ __device__ void wbulk_drain(uint64_t* mbar, int ok) {
 // key, from kb (or, given, ks = those keys' rows staged in shared memory);
 // with `tail`, also the keys past the last group of four (dotF32Go, from
 // kb). Returns the thread's maximum.
-__device__ float wcross_scores(const float* qh, const float* kb, int j0, int j1, bool tail, int ctx, float* sc,
+__device__ __forceinline__ float wcross_scores(const float* qh, const float* kb, int j0, int j1, bool tail, int ctx, float* sc,
                                const float* ks = nullptr) {
   const int l16 = threadIdx.x & 15, grp = threadIdx.x >> 4, ng = blockDim.x >> 4;
   float mx = NINF;
@@ -313,7 +313,7 @@ __device__ float wcross_scores(const float* qh, const float* kb, int j0, int j1,
 }
 
 // Scores to probabilities in place: expSub against mx, then · (1/Σ).
-__device__ void wcross_softmax(float* sc, int ctx, float mx, float* sh) {
+__device__ __forceinline__ void wcross_softmax(float* sc, int ctx, float mx, float* sh) {
   const float sum = exp_sub(sc, ctx, mx, sh);
   const float inv = __fdiv_rn(1.f, sum);
   for (int j = threadIdx.x; j < ctx; j += blockDim.x) sc[j] = __fmul_rn(sc[j], inv);
@@ -325,7 +325,7 @@ __device__ void wcross_softmax(float* sc, int ctx, float mx, float* sh) {
 // 16, then the HSUM and dotF32Go of the rest; p = probabilities in shared
 // memory, V row d at vb + (d − vd0)·ctx.
 template <int ND>
-__device__ void wcross_out(const float* p, const float* vb, int ctx, int d0, float* att, int vd0 = 0, int ngrp = 0) {
+__device__ __forceinline__ void wcross_out(const float* p, const float* vb, int ctx, int d0, float* att, int vd0 = 0, int ngrp = 0) {
   const int l16 = threadIdx.x & 15, grp = threadIdx.x >> 4, ng = blockDim.x >> 4;
   if (ngrp && grp >= ngrp) return;  // whole warps (ngrp even)
   const int cf = ctx & ~15;
@@ -1174,8 +1174,8 @@ __global__ void k_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int 
 // grid barrier where a step needs every CTA's results. Per layer: the q/k/v
 // rows, self-attention (a few CTAs a head, each with some of its outputs),
 // o with the residual, LayerNorm and xq, the cross scores (key chunks over
-// the CTAs), the softmax and values (a slice of a head's outputs a CTA, its
-// Vᵀ rows staged by async copies), xo with the residual, LayerNorm and fc1,
+// the CTAs, their K rows staged ahead), the softmax and values (a slice of a
+// head's outputs a CTA, its Vᵀ rows staged ahead), xo with the residual, LayerNorm and fc1,
 // fc2 with the residual; then the final LayerNorm and the logits rows. Every
 // CTA keeps a copy of the residual row and forms the LayerNorms itself.
 //
@@ -1191,7 +1191,7 @@ __global__ void k_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int 
 // fixed order on every CTA (the margins make the order safe, as for the
 // cluster form). Every wait is bounded (about a second); one that runs out
 // sets the error word and every CTA leaves.
-constexpr int WS_NT = 512;
+constexpr int WS_NT = 256;
 constexpr unsigned long long kWsWaitNs = 1000000000ull;
 
 struct WsCtl {
@@ -1322,18 +1322,37 @@ struct GridRed {
 
 __device__ __forceinline__ int ws_split(int n, int c, int G) { return int((long long)n * c / G); }
 
+// A block's float64 sum: warps by xor shuffles, then the first warp over the
+// warps' sums (the float64 order does not reach the float32 results of the
+// LayerNorm but in a last-ulp tie, as for k_wln).
+__device__ __forceinline__ double ws_sum_d(double v, double* sh) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    double r = threadIdx.x < nw ? sh[threadIdx.x] : 0.0;
+    for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    if (threadIdx.x == 0) sh[32] = r;
+  }
+  __syncthreads();
+  const double r = sh[32];
+  __syncthreads();  // sh is reused by the next sum
+  return r;
+}
+
 // whisper/mathx.go:55-75 over a row in shared memory (as k_wln).
-__device__ void ws_ln(const float* x, float* y, const float* w, const float* b, int n, double* shd) {
+__device__ __noinline__ void ws_ln(const float* x, float* y, const float* w, const float* b, int n, double* shd) {
   double s = 0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) s += double(x[i]);
-  s = block_sum_d(s, shd);
+  s = ws_sum_d(s, shd);
   const float mean = float(s / double(n));
   double vs = 0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const double d = double(__fsub_rn(x[i], mean));
     vs += d * d;
   }
-  vs = block_sum_d(vs, shd);
+  vs = ws_sum_d(vs, shd);
   const float inv = float(1.0 / sqrt(vs / double(n) + 1e-5));
   for (int i = threadIdx.x; i < n; i += blockDim.x)
     y[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i], mean), inv), w[i]), b[i]);
@@ -1360,79 +1379,135 @@ __device__ __forceinline__ void cpa_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-// Rows [r0, r1) of w (K columns) staged in shared memory at s: float16 rows
-// of 2K + 16 bytes, or Q8_0 rows of K + 16 int8 values followed by the rows'
-// K/32 float16 scales (the padding keeps four rows read by one warp in
-// different banks).
-__device__ void ws_stage(const WMat& w, int K, int r0, int r1, unsigned char* s) {
-  const int R = r1 - r0;
-  if (w.h) {
-    const int cpr = K / 8;
-    const unsigned char* g = reinterpret_cast<const unsigned char*>(w.h + (size_t)r0 * K);
-    for (int t = threadIdx.x; t < R * cpr; t += blockDim.x) {
-      const int r = t / cpr, c = t - r * cpr;
-      cpa16(s + r * (2 * K + 16) + c * 16, g + (size_t)r * 2 * K + c * 16);
-    }
-  } else {
-    const int cpr = K / 16;
-    const unsigned char* g = reinterpret_cast<const unsigned char*>(w.q + (size_t)r0 * K);
-    for (int t = threadIdx.x; t < R * cpr; t += blockDim.x) {
-      const int r = t / cpr, c = t - r * cpr;
-      cpa16(s + r * (K + 16) + c * 16, g + (size_t)r * K + c * 16);
-    }
-    const unsigned char* gd = reinterpret_cast<const unsigned char*>(w.d + (size_t)r0 * (K / QK));
-    unsigned char* sd = s + R * (K + 16);
-    for (int t = threadIdx.x; t < R * K / 64; t += blockDim.x) cpa4(sd + 4 * t, gd + 4 * t);
-  }
+// Rows [r0, r1) of a float16 matrix (K columns) staged in shared memory at
+// s, rows of 2K + 16 bytes (the padding keeps the rows one warp reads in
+// different banks): a warp a row, its lanes along it.
+__device__ __forceinline__ void ws_stage(const WMat& w, int K, int r0, int r1, unsigned char* s) {
+  const int R = r1 - r0, wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5, cpr = K / 8;
+  const unsigned char* g = reinterpret_cast<const unsigned char*>(w.h + (size_t)r0 * K);
+  for (int r = wid; r < R; r += nw)
+    for (int c = lane; c < cpr; c += 32) cpa16(s + r * (2 * K + 16) + c * 16, g + (size_t)r * 2 * K + c * 16);
 }
 
 enum { WS_STORE = 0, WS_RESID = 1, WS_GELU = 2 };
 
-// Rows [r0, r1) of y = W·x (+ bias) for one input row x (shared memory, K
-// values) from the rows staged at s: one 8-lane group per output row, lane
-// l accumulating elements 16c + l and 16c + 8 + l over c in order, then the
-// two added and the HSUM ((a0+a4)+(a1+a5))+((a2+a6)+(a3+a7)) — k_flin's
-// order (dot4f16avx), Q8_0 values widened as f16(q·d) (whisper/model.go:
-// 486-490). RESID stores res[n] + (dot + bias), GELU geluAVX(dot + bias).
-template <int EPI>
-__device__ void ws_rows(bool f16, const unsigned char* s, const float* x, int K, int r0, int r1, const float* bias,
-                        float* y, const float* res) {
-  const int g = threadIdx.x >> 3, l = threadIdx.x & 7, ng = blockDim.x >> 3, R = r1 - r0;
-  const unsigned gm = 0xffu << (threadIdx.x & 24);
-  for (int r = g; r < R; r += ng) {
-    float a = 0.f, a1 = 0.f;
-    if (f16) {
-      const uint16_t* wr = reinterpret_cast<const uint16_t*>(s + r * (2 * K + 16));
+// One product's rows for ws_rows: the rows [r0, r0 + R) of a float16
+// matrix staged at s (rows of 2K + 16 bytes), their outputs y[r0 + r] (bias
+// optional; RESID adds res[r0 + r]).
+struct WsOut {
+  const unsigned char* s;
+  int r0, R;
+  const float* bias;
+  float* y;
+  const float* res;
+};
+
+// Up to three products with the same K and input row, and their epilogue.
+struct WsProd {
+  WsOut o[3];
+  int np, epi;
+};
+
+// The rows of the products in P (y = W·x (+ bias), x a row of K values in
+// shared memory) in k_flin's order (dot4f16avx): eight lanes l each with two
+// chains, elements 16c + l and 16c + 8 + l over c in order, the two added,
+// then the HSUM ((a0+a4)+(a1+a5))+((a2+a6)+(a3+a7)). When the rows fit the
+// block at 16 threads a row each thread runs one chain (thread l + 8 the
+// second chain of l); otherwise 4 threads a row run four chains each (thread
+// t the elements 4t..4t+3 of every 16, read as vectors; threads 2 and 3 the
+// second chains of 0 and 1). A call of its own: its loops are scheduled
+// apart from the persistent kernel's other state (inlined they lost 3-4x).
+// The matrices are float16 (Q8_0 ones widened beforehand as f16(q·d), the
+// values whisper/model.go:486-490 gives every product). RESID stores
+// res + (dot + bias), GELU geluAVX(dot + bias).
+__device__ __noinline__ void ws_product(const WsProd& P, const float* x, int K) {
+  const int np = P.np, epi = P.epi, nc = K / 16;
+  int tot = 0;
+  for (int m = 0; m < np; m++) tot += P.o[m].R;
+  const int tpr = tot * 16 <= int(blockDim.x) ? 16 : 4;
+  const int g = threadIdx.x / tpr, t = threadIdx.x % tpr, ng = blockDim.x / tpr;
+  for (int rb = 0; rb < tot; rb += ng) {  // whole warps through every round
+    int r = min(rb + g, tot - 1), m = 0;
+    while (m + 1 < np && r >= P.o[m].R) r -= P.o[m].R, m++;
+    const WsOut& O = P.o[m];
+    const unsigned char* wrow = O.s + r * (2 * K + 16);
+    const int n = O.r0 + r;
+    const float bv = O.bias && t == 0 ? __ldg(O.bias + n) : 0.f;  // in flight during the chains
+    float v;
+    if (tpr == 16) {
+      const float* xr = x + t;
+      const uint16_t* wr = reinterpret_cast<const uint16_t*>(wrow) + t;
+      float a = 0.f;
 #pragma unroll 8
-      for (int c16 = 0; c16 < K; c16 += 16) {
-        a = __fmaf_rn(x[c16 + l], h2f(wr[c16 + l]), a);
-        a1 = __fmaf_rn(x[c16 + 8 + l], h2f(wr[c16 + 8 + l]), a1);
-      }
+      for (int c = 0; c < nc; c++) a = __fmaf_rn(xr[16 * c], h2f(wr[16 * c]), a);
+      v = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));  // threads l < 8: a_l + a1_l
+      v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+      v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+      v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
     } else {
-      const int8_t* wr = reinterpret_cast<const int8_t*>(s + r * (K + 16));
-      const uint16_t* dr = reinterpret_cast<const uint16_t*>(s + R * (K + 16)) + r * (K / QK);
-#pragma unroll 8
-      for (int c16 = 0; c16 < K; c16 += 16) {
-        const float d = h2f(dr[c16 / QK]);
-        a = __fmaf_rn(x[c16 + l], q8h(wr[c16 + l], d), a);
-        a1 = __fmaf_rn(x[c16 + 8 + l], q8h(wr[c16 + 8 + l], d), a1);
+      const float4* x4 = reinterpret_cast<const float4*>(x) + t;
+      const uint2* w2 = reinterpret_cast<const uint2*>(wrow) + t;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < nc; c++) {
+        const float4 xv = x4[4 * c];
+        const uint2 wv = w2[4 * c];
+        a0 = __fmaf_rn(xv.x, h2f(uint16_t(wv.x)), a0);
+        a1 = __fmaf_rn(xv.y, h2f(uint16_t(wv.x >> 16)), a1);
+        a2 = __fmaf_rn(xv.z, h2f(uint16_t(wv.y)), a2);
+        a3 = __fmaf_rn(xv.w, h2f(uint16_t(wv.y >> 16)), a3);
       }
+      // v_l = a_l + a1_l (threads 0 and 1 take the second chains from 2 and 3)
+      a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 2));
+      a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 2));
+      a2 = __fadd_rn(a2, __shfl_down_sync(0xffffffffu, a2, 2));
+      a3 = __fadd_rn(a3, __shfl_down_sync(0xffffffffu, a3, 2));
+      // thread 0: v_j + v_(j+4), then the pairs
+      a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 1));
+      a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 1));
+      a2 = __fadd_rn(a2, __shfl_down_sync(0xffffffffu, a2, 1));
+      a3 = __fadd_rn(a3, __shfl_down_sync(0xffffffffu, a3, 1));
+      v = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
     }
-    float v = __fadd_rn(a, a1);
-    v = __fadd_rn(v, __shfl_xor_sync(gm, v, 4));
-    v = __fadd_rn(v, __shfl_xor_sync(gm, v, 1));
-    v = __fadd_rn(v, __shfl_xor_sync(gm, v, 2));
-    if (l == 0) {
-      const int n = r0 + r;
-      const float o = bias ? __fadd_rn(v, bias[n]) : v;
-      if (EPI == WS_RESID)
-        y[n] = __fadd_rn(res[n], o);
-      else if (EPI == WS_GELU)
-        y[n] = gelu_avx(o);
+    if (t == 0 && rb + g < tot) {
+      const float ov = O.bias ? __fadd_rn(v, bv) : v;
+      if (epi == WS_RESID)
+        O.y[n] = __fadd_rn(O.res[n], ov);
+      else if (epi == WS_GELU)
+        O.y[n] = gelu_avx(ov);
       else
-        y[n] = o;
+        O.y[n] = ov;
     }
   }
+}
+
+__device__ __forceinline__ void ws_rows(int epi, const WsOut& a, const float* x, int K) {
+  WsProd P;
+  P.o[0] = a, P.np = 1, P.epi = epi;
+  ws_product(P, x, K);
+}
+
+// n floats from global memory (16-byte aligned, n a multiple of 4) into
+// shared memory, up to four vectors a thread in flight before their stores;
+// read through L2 (data other CTAs wrote before the last grid barrier).
+__device__ __forceinline__ void ws_load(float* dst, const float* src, int n) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  const int n4 = n >> 2, bd = blockDim.x;
+  for (int i0 = 0; i0 < n4; i0 += 4 * bd) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int i = i0 + u * bd + int(threadIdx.x);
+      if (i < n4) v[u] = __ldcg(s4 + i);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int i = i0 + u * bd + int(threadIdx.x);
+      if (i < n4) d4[i] = v[u];
+    }
+  }
+  __syncthreads();
 }
 
 // This CTA's rows of a layer's eight matrices in the order q, k, v, o, xq,
@@ -1446,14 +1521,14 @@ __device__ WsPlan ws_plan(const WS1Layer& Y, int st, int ff, int R, int Rf) {
   const WMat* m[8] = {&Y.q, &Y.k, &Y.v, &Y.o, &Y.xq, &Y.xo, &Y.fc1, &Y.fc2};
   p.off[0] = 0;
   for (int i = 0; i < 8; i++)
-    p.off[i + 1] = p.off[i] + ws_slice_bytes(m[i]->h != nullptr, i == 6 ? Rf : R, i == 7 ? ff : st);
+    p.off[i + 1] = p.off[i] + ws_slice_bytes(true, i == 6 ? Rf : R, i == 7 ? ff : st);
   return p;
 }
 
 // Self-attention of head h over keys 0..n-1 (decoder.go:70-87, as k_wself),
 // outputs d0..d0+nd-1 of the head: every CTA of the head takes the scores
 // and softmax, its nd columns of V staged by async copies meanwhile.
-__device__ void ws_self(const float* q, const float* sk, const float* sv, int st, int n, int h, int d0, int nd,
+__device__ __noinline__ void ws_self(const float* q, const float* sk, const float* sv, int st, int n, int h, int d0, int nd,
                         float* sc, float* qh, float* vs, float* sh, float* att) {
   for (int t = threadIdx.x; t < n * (nd / 2); t += blockDim.x) {
     const int j = t / (nd / 2), c = t - j * (nd / 2);
@@ -1495,6 +1570,29 @@ __device__ void ws_self(const float* q, const float* sk, const float* sv, int st
   __syncthreads();
 }
 
+// h[i] = f16(q[i]·d[i/32]): the float16 value every Whisper product widens
+// a Q8_0 value to (whisper/model.go:486-490).
+__global__ void k_wwiden(const int8_t* q, const uint16_t* d, uint16_t* h, size_t n) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) h[i] = __half_as_ushort(__float2half_rn(__fmul_rn(float(q[i]), h2f(d[i / QK]))));
+}
+
+// The cross scores of keys [j0, j1) from staged rows and the values of
+// outputs d0..d0+nd-1 from staged Vᵀ rows, as calls of their own (their
+// loops scheduled apart from the persistent kernel's other state).
+__device__ __noinline__ float ws_xscores(const float* qh, const float* kb, int j0, int j1, bool tail, int ctx, float* sc,
+                                         const float* ks) {
+  return wcross_scores(qh, kb, j0, j1, tail, ctx, sc, ks);
+}
+
+__device__ __noinline__ void ws_xout(const float* p, const float* vs, int ctx, int d0, int nd, float* att) {
+  wcross_out<1>(p, vs, ctx, d0, att, d0, nd);
+}
+
+__device__ __noinline__ void ws_proc(GridRed& red, const WStep1Args& A, int i, int v0, int v1, bool writer) {
+  proc_row(red, A.logits, A.scratch, A.voc, A.state, A.out + 4 * i, A.row_tok, v0, v1, writer);
+}
+
 __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restrict__ Ap, int pos0, int steps) {
   const WStep1Args& A = *Ap;
   extern __shared__ __align__(128) float ws1m[];
@@ -1504,7 +1602,8 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
   float* sc = cur + max(st, ff);          // [max(ctx, text_ctx)] scores
   float* qh = sc + max(ctx, A.text_ctx);  // [64]
   float* xv = qh + 64;                    // [xv_floats] staged V columns
-  unsigned char* wbuf = reinterpret_cast<unsigned char*>(xv + A.xv_floats);  // [2][wb] weight rows
+  float* xk = xv + A.xv_floats;           // [xk_floats] staged cross K rows
+  unsigned char* wbuf = reinterpret_cast<unsigned char*>(xk + A.xk_floats);  // [2][wb] weight rows
   __shared__ float shf[40];
   __shared__ VI shv[32];
   __shared__ double shd[32];
@@ -1523,7 +1622,6 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
   const int v0 = ws_split(A.vocab, cta, G), v1 = ws_split(A.vocab, cta + 1, G);
   const int nchunk = max(1, (v1 - v0 + A.lrows - 1) / A.lrows);
   const int items = L + nchunk;  // staged items a step: the layers, then the logits chunks
-  const bool emb16 = A.emb.h != nullptr;
   auto stage = [&](int t, unsigned char* buf) {
     if (t < L) {
       const WS1Layer& Y = A.layers[t];
@@ -1555,14 +1653,10 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
   const int ch = ((ctx4 + ks - 1) / ks + 15) / 16 * 16;
   ks = (ctx4 + ch - 1) / ch;
   const int so_s = 64 / A.so_nd, xo_s = 64 / A.xo_nd;  // CTAs a head for self-attention and the values
-  auto load = [&](float* dst, const float* src, int n) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
-    __syncthreads();
-  };
   int i = 0;
   for (; i < steps; i++) {
     // ---- process + sample of the last logits (transcribe.go:370-494)
-    proc_row(red, A.logits, A.scratch, A.voc, A.state, A.out + 4 * i, A.row_tok, v0, v1, cta == 0);
+    ws_proc(red, A, i, v0, v1, cta == 0);
     if (!ws_sync(A, ctl)) break;
     const int pos = pos0 + i, tok = A.row_tok[0];
     // ---- decode of the token at pos (decoder.go:33-140): the embedding
@@ -1573,55 +1667,70 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
       const WS1Layer& Y = A.layers[l];
       const unsigned char* wl = consume(l);
       const WsPlan p = ws_plan(Y, st, ff, r1 - r0, f1 - f0);
+      if (cta < nh * ks) {  // this CTA's cross K rows, for the scores four phases on
+        const int h = cta / ks, j0 = (cta % ks) * ch, j1 = min(ctx4, j0 + ch);
+        const float* kr = Y.ck + ((size_t)h * ctx + j0) * 64;
+        for (int t = threadIdx.x; t < (j1 - j0) * 16; t += blockDim.x) cpa16(xk + 4 * t, kr + 4 * t);
+        cpa_commit();
+      }
       ws_ln(xs, cur, Y.ln1w, Y.ln1b, st, shd);
-      ws_rows<WS_STORE>(Y.q.h != nullptr, wl + p.off[0], cur, st, r0, r1, Y.qb, A.q, nullptr);
-      ws_rows<WS_STORE>(Y.k.h != nullptr, wl + p.off[1], cur, st, r0, r1, nullptr, Y.sk + (size_t)pos * st, nullptr);
-      ws_rows<WS_STORE>(Y.v.h != nullptr, wl + p.off[2], cur, st, r0, r1, Y.vb, Y.sv + (size_t)pos * st, nullptr);
+      {
+        const WsProd P = {{{wl + p.off[0], r0, r1 - r0, Y.qb, A.q, nullptr},
+                           {wl + p.off[1], r0, r1 - r0, nullptr, Y.sk + (size_t)pos * st, nullptr},
+                           {wl + p.off[2], r0, r1 - r0, Y.vb, Y.sv + (size_t)pos * st, nullptr}},
+                          3,
+                          WS_STORE};
+        ws_product(P, cur, st);
+      }
       if (!ws_sync(A, ctl)) break;
       if (cta < nh * so_s)
         ws_self(A.q, Y.sk, Y.sv, st, pos + 1, cta / so_s, (cta % so_s) * A.so_nd, A.so_nd, sc, qh, xv, shf, A.att);
       if (!ws_sync(A, ctl)) break;
-      load(cur, A.att, st);
-      ws_rows<WS_RESID>(Y.o.h != nullptr, wl + p.off[3], cur, st, r0, r1, Y.ob, A.x, xs);
+      if (cta < nh * xo_s) {  // the Vᵀ rows of this CTA's cross outputs, for three phases on
+        const int h = cta / xo_s, d0 = (cta % xo_s) * A.xo_nd;
+        const float* vrow = Y.cvt + ((size_t)h * 64 + d0) * ctx;
+        for (int t = threadIdx.x; t < A.xo_nd * ctx / 4; t += blockDim.x) cpa16(xv + 4 * t, vrow + 4 * t);
+        cpa_commit();
+      }
+      ws_load(cur, A.att, st);
+      ws_rows(WS_RESID, WsOut{wl + p.off[3], r0, r1 - r0, Y.ob, A.x, xs}, cur, st);
       if (!ws_sync(A, ctl)) break;
-      load(xs, A.x, st);
+      ws_load(xs, A.x, st);
       ws_ln(xs, cur, Y.ln2w, Y.ln2b, st, shd);
-      ws_rows<WS_STORE>(Y.xq.h != nullptr, wl + p.off[4], cur, st, r0, r1, Y.xqb, A.q, nullptr);
+      ws_rows(WS_STORE, WsOut{wl + p.off[4], r0, r1 - r0, Y.xqb, A.q, nullptr}, cur, st);
       if (!ws_sync(A, ctl)) break;
       if (cta < nh * ks) {  // cross scores of key chunk cta % ks of head cta / ks
         const int h = cta / ks, kc = cta % ks, j0 = kc * ch, j1 = min(ctx4, j0 + ch);
         if (threadIdx.x < 64) qh[threadIdx.x] = A.q[h * 64 + threadIdx.x];
+        cpa_wait<0>();
         __syncthreads();
-        float mx = wcross_scores(qh, Y.ck + (size_t)h * ctx * 64, j0, j1, kc == ks - 1, ctx, A.sg + (size_t)h * ctx);
+        float mx = ws_xscores(qh, Y.ck + (size_t)h * ctx * 64, j0, j1, kc == ks - 1, ctx, A.sg + (size_t)h * ctx, xk);
         mx = block_max(mx, shf);
         if (threadIdx.x == 0) A.mg[h * ks + kc] = mx;
       }
       if (!ws_sync(A, ctl)) break;
       if (cta < nh * xo_s) {  // softmax and outputs d0..d0+xo_nd-1 of head h
         const int h = cta / xo_s, d0 = (cta % xo_s) * A.xo_nd;
-        const float* vrow = Y.cvt + ((size_t)h * 64 + d0) * ctx;
-        for (int t = threadIdx.x; t < A.xo_nd * ctx / 4; t += blockDim.x) cpa16(xv + 4 * t, vrow + 4 * t);
-        cpa_commit();
         float mx = threadIdx.x < ks ? A.mg[h * ks + threadIdx.x] : NINF;
         mx = block_max(mx, shf);
-        load(sc, A.sg + (size_t)h * ctx, ctx);
+        ws_load(sc, A.sg + (size_t)h * ctx, ctx);
         wcross_softmax(sc, ctx, mx, shf);
         cpa_wait<0>();
         __syncthreads();
-        wcross_out<1>(sc, xv, ctx, d0, A.att + h * 64, d0, A.xo_nd);
+        ws_xout(sc, xv, ctx, d0, A.xo_nd, A.att + h * 64);
       }
       if (!ws_sync(A, ctl)) break;
-      load(cur, A.att, st);
-      ws_rows<WS_RESID>(Y.xo.h != nullptr, wl + p.off[5], cur, st, r0, r1, Y.xob, A.x, xs);
+      ws_load(cur, A.att, st);
+      ws_rows(WS_RESID, WsOut{wl + p.off[5], r0, r1 - r0, Y.xob, A.x, xs}, cur, st);
       if (!ws_sync(A, ctl)) break;
-      load(xs, A.x, st);
+      ws_load(xs, A.x, st);
       ws_ln(xs, cur, Y.ln3w, Y.ln3b, st, shd);
-      ws_rows<WS_GELU>(Y.fc1.h != nullptr, wl + p.off[6], cur, st, f0, f1, Y.fc1b, A.ffb, nullptr);
+      ws_rows(WS_GELU, WsOut{wl + p.off[6], f0, f1 - f0, Y.fc1b, A.ffb, nullptr}, cur, st);
       if (!ws_sync(A, ctl)) break;
-      load(cur, A.ffb, ff);
-      ws_rows<WS_RESID>(Y.fc2.h != nullptr, wl + p.off[7], cur, ff, r0, r1, Y.fc2b, A.x, xs);
+      ws_load(cur, A.ffb, ff);
+      ws_rows(WS_RESID, WsOut{wl + p.off[7], r0, r1 - r0, Y.fc2b, A.x, xs}, cur, ff);
       if (!ws_sync(A, ctl)) break;
-      load(xs, A.x, st);
+      ws_load(xs, A.x, st);
     }
     if (ctl.fail) break;
     // ---- the final LayerNorm and the logits (no bias), chunk by chunk
@@ -1629,7 +1738,7 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
     for (int c = 0; c < nchunk; c++) {
       const unsigned char* wl = consume(L + c);
       const int a = min(v1, v0 + c * A.lrows), b = min(v1, a + A.lrows);
-      ws_rows<WS_STORE>(emb16, wl, cur, st, a, b, nullptr, A.logits, nullptr);
+      ws_rows(WS_STORE, WsOut{wl, a, b - a, nullptr, A.logits, nullptr}, cur, st);
       __syncthreads();
     }
     if (!ws_sync(A, ctl)) break;
@@ -1800,9 +1909,14 @@ void launch_wenc_softmax(float* x, int len, long rows, cudaStream_t st) {
 
 void whisper_kernels_init() {}
 
+void launch_wwiden(const WMat& w, uint16_t* h, cudaStream_t st) {
+  const size_t n = size_t(w.rows) * w.cols;
+  k_wwiden<<<unsigned((n + 255) / 256), 256, 0, st>>>(w.q, w.d, h, n);
+}
+
 size_t wstep1_smem(const WStep1Args& a) {
   const size_t floats = size_t(a.st) + size_t(std::max(a.st, a.ff)) + size_t(std::max(a.ctx, a.text_ctx)) + 64 +
-                        size_t(a.xv_floats);
+                        size_t(a.xv_floats) + size_t(a.xk_floats);
   return sizeof(float) * floats + 2 * size_t(a.wb);
 }
 

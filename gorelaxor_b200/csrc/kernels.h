@@ -438,8 +438,9 @@ struct WStep1Args {
   int stall = 0;             // test hook: the first barrier never completes
   // shared-memory plan: two weight buffers of wb bytes, logits rows staged
   // lrows at a time, so_nd / xo_nd outputs of a head per CTA in the self-
-  // and cross-attention values, xv_floats floats of staged V columns
-  int wb = 0, lrows = 0, so_nd = 0, xo_nd = 0, xv_floats = 0;
+  // and cross-attention values, xv_floats floats of staged V columns,
+  // xk_floats of staged cross K rows
+  int wb = 0, lrows = 0, so_nd = 0, xo_nd = 0, xv_floats = 0, xk_floats = 0;
 };
 
 // Bytes of R rows of K columns staged in shared memory by the persistent
@@ -451,6 +452,8 @@ __host__ __device__ inline int ws_slice_bytes(bool f16, int R, int K) {
 // Shared memory a CTA of the kernel needs; whether the device runs it (one
 // 512-thread CTA per SM, cooperative launch); the launch (steps rounds of
 // sample-then-decode from position pos0).
+// h[i] = f16(q[i]·d[i/32]) for a Q8_0 matrix (the products' widening).
+void launch_wwiden(const WMat& w, uint16_t* h, cudaStream_t st);
 size_t wstep1_smem(const WStep1Args& a);
 int wstep1_max_active(size_t smem);
 cudaError_t launch_wstep1(const WStep1Args* d_args, int grid, size_t smem, int pos0, int steps, cudaStream_t st);

@@ -164,6 +164,9 @@ struct grx_whisper {
   float *dec_pos = nullptr, *ln_w = nullptr, *ln_b = nullptr;
   WVocabDev voc;
   std::vector<int> suppress;
+  // float16 copies of the decoder's Q8_0 matrices, each value f16(q·d) as
+  // the products widen it, made for the persistent one-stream kernel
+  std::map<const int8_t*, uint16_t*> wide;
 };
 
 struct grx_whisper_batch {
@@ -308,6 +311,22 @@ int ws1_setup(grx_whisper_batch* b) {
     if (!ok(L.q) || !ok(L.k) || !ok(L.v) || !ok(L.o) || !ok(L.xq) || !ok(L.xo) || !ok(L.fc1) || !ok(L.fc2) ||
         L.fc1.rows != ff)
       return GRX_OK;
+  // the matrices as the kernel reads them: Q8_0 ones widened once into
+  // float16 (the same values; its products then convert one value a term)
+  grx_whisper* mw = b->m;
+  int wrc = 0;
+  auto wide = [&](WMat w) {
+    if (w.h || !w.q) return w;
+    uint16_t*& h = mw->wide[w.q];
+    if (!h) {
+      h = mw->ar.alloc<uint16_t>(size_t(w.rows) * w.cols, &wrc);
+      if (!h) return w;
+      launch_wwiden(w, h, nullptr);
+    }
+    WMat o = w;
+    o.q = nullptr, o.d = nullptr, o.h = h;
+    return o;
+  };
   int G = 0, coop = 0;
   CK(cudaDeviceGetAttribute(&G, cudaDevAttrMultiProcessorCount, b->ar.dev));
   CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, b->ar.dev));
@@ -323,7 +342,8 @@ int ws1_setup(grx_whisper_batch* b) {
   for (int l = 0; l < A.L; l++) {
     const WLayerDev& L = m->layers[size_t(l)];
     WS1Layer& Y = A.layers[l];
-    Y.q = L.q, Y.k = L.k, Y.v = L.v, Y.o = L.o, Y.xq = L.xq, Y.xo = L.xo, Y.fc1 = L.fc1, Y.fc2 = L.fc2;
+    Y.q = wide(L.q), Y.k = wide(L.k), Y.v = wide(L.v), Y.o = wide(L.o), Y.xq = wide(L.xq), Y.xo = wide(L.xo);
+    Y.fc1 = wide(L.fc1), Y.fc2 = wide(L.fc2);
     Y.qb = L.qb, Y.vb = L.vb, Y.ob = L.ob, Y.xqb = L.xqb, Y.xob = L.xob, Y.fc1b = L.fc1b, Y.fc2b = L.fc2b;
     Y.ln1w = L.attn_ln_w, Y.ln1b = L.attn_ln_b, Y.ln2w = L.x_ln_w, Y.ln2b = L.x_ln_b, Y.ln3w = L.mlp_ln_w,
     Y.ln3b = L.mlp_ln_b;
@@ -332,7 +352,12 @@ int ws1_setup(grx_whisper_batch* b) {
     Y.ck = b->ck + size_t(l) * layer_stride_cross(m, 1);
     Y.cvt = b->cvt + size_t(l) * layer_stride_cross(m, 1);
   }
-  A.emb = m->tok_emb;
+  A.emb = wide(m->tok_emb);
+  if (wrc) {  // no room for the float16 copies: the per-kernel path
+    cudaGetLastError();
+    return GRX_OK;
+  }
+  CK(cudaDeviceSynchronize());
   A.dec_pos = m->dec_pos;
   A.lnw = m->ln_w;
   A.lnb = m->ln_b;
@@ -352,11 +377,11 @@ int ws1_setup(grx_whisper_batch* b) {
     if (&Y - A.layers >= A.L) break;
     const WMat* mm[8] = {&Y.q, &Y.k, &Y.v, &Y.o, &Y.xq, &Y.xo, &Y.fc1, &Y.fc2};
     int lb = 0;
-    for (int i = 0; i < 8; i++) lb += ws_slice_bytes(mm[i]->h != nullptr, i == 6 ? Rf : R, i == 7 ? ff : A.st);
+    for (int i = 0; i < 8; i++) lb += ws_slice_bytes(true, i == 6 ? Rf : R, i == 7 ? ff : A.st);
     wb = std::max(wb, lb);
   }
   A.lrows = std::min(64, (A.vocab + G - 1) / G);
-  wb = std::max(wb, ws_slice_bytes(A.emb.h != nullptr, A.lrows, A.st));
+  wb = std::max(wb, ws_slice_bytes(true, A.lrows, A.st));
   A.wb = (wb + 15) / 16 * 16;
   // CTAs a head in the self-attention and cross values: a power of two up
   // to 32 that fits G / heads, each with 64 / that outputs
@@ -364,6 +389,10 @@ int ws1_setup(grx_whisper_batch* b) {
   while (per * 2 <= std::min(32, G / A.nh)) per *= 2;
   A.so_nd = A.xo_nd = 64 / per;
   A.xv_floats = std::max(A.xo_nd * A.ctx, A.so_nd * A.text_ctx);
+  {  // a CTA's key chunk of the cross scores, as k_wstep1 splits them
+    const int ctx4 = A.ctx & ~3, ks = std::max(1, G / A.nh);
+    A.xk_floats = ((ctx4 + ks - 1) / ks + 15) / 16 * 16 * 64;
+  }
   const size_t smem = wstep1_smem(A);
   if (wstep1_max_active(smem) < 1) return GRX_OK;
   int rc = 0;
