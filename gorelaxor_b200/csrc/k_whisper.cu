@@ -1181,8 +1181,10 @@ __global__ void k_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int 
 //
 // Each CTA's weight rows reach shared memory ahead of use: a ring of two
 // buffers, the next layer's rows of all eight matrices (or the next chunk of
-// logits rows) copied by cp.async while the current one is computed, so the
-// products run on staged rows and only the barriers wait on memory.
+// logits rows) brought by bulk copies (a row each, on the buffer's mbarrier)
+// while the current one is computed, so the products run on staged rows and
+// only the barriers wait on memory. The cross K and V rows a CTA needs come
+// the same way a few phases ahead.
 //
 // The arithmetic is the per-kernel path's: the products in k_flin's
 // float-path lane order (one 8-lane group per output row, dot4f16avx with
@@ -1359,34 +1361,17 @@ __device__ __noinline__ void ws_ln(const float* x, float* y, const float* w, con
   __syncthreads();
 }
 
-// ---- async copies into shared memory (cp.async; completion per thread,
-// then a CTA barrier before other threads read)
-__device__ __forceinline__ void cpa16(void* s, const void* g) {
-  const unsigned sa = unsigned(__cvta_generic_to_shared(s));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(g) : "memory");
-}
+// ---- async copies into shared memory (cp.async, for the strided V columns
+// of self-attention; completion per thread, then a CTA barrier before other
+// threads read)
 __device__ __forceinline__ void cpa8(void* s, const void* g) {
   const unsigned sa = unsigned(__cvta_generic_to_shared(s));
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(sa), "l"(g) : "memory");
-}
-__device__ __forceinline__ void cpa4(void* s, const void* g) {
-  const unsigned sa = unsigned(__cvta_generic_to_shared(s));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(g) : "memory");
 }
 __device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cpa_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
-// Rows [r0, r1) of a float16 matrix (K columns) staged in shared memory at
-// s, rows of 2K + 16 bytes (the padding keeps the rows one warp reads in
-// different banks): a warp a row, its lanes along it.
-__device__ __forceinline__ void ws_stage(const WMat& w, int K, int r0, int r1, unsigned char* s) {
-  const int R = r1 - r0, wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5, cpr = K / 8;
-  const unsigned char* g = reinterpret_cast<const unsigned char*>(w.h + (size_t)r0 * K);
-  for (int r = wid; r < R; r += nw)
-    for (int c = lane; c < cpr; c += 32) cpa16(s + r * (2 * K + 16) + c * 16, g + (size_t)r * 2 * K + c * 16);
 }
 
 enum { WS_STORE = 0, WS_RESID = 1, WS_GELU = 2 };
@@ -1570,6 +1555,57 @@ __device__ __noinline__ void ws_self(const float* q, const float* sk, const floa
   __syncthreads();
 }
 
+// ---- bulk copies into this CTA's own shared memory, completing on an
+// mbarrier (no cluster-wide forms); thread 0 waits, bounded like the grid
+// barrier, and a wait that runs out sets the error word.
+__device__ __forceinline__ bool ws_bar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void ws_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+// One contiguous copy (16-byte aligned ends, a multiple of 16 bytes). The
+// proxy fence orders the CTA's earlier reads of the destination (behind a
+// CTA barrier) before the copy's writes.
+__device__ __forceinline__ void ws_bulk(void* dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   unsigned(__cvta_generic_to_shared(dst))),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ bool ws_bar_wait(const WStep1Args& A, WsCtl& ctl, uint32_t bar, uint32_t parity) {
+  if (threadIdx.x == 0 && !ctl.fail) {
+    const unsigned long long t0 = wtime();
+    bool got = ws_bar_try(bar, parity);
+    while (!got && wtime() - t0 < kWsWaitNs) got = ws_bar_try(bar, parity);
+    if (!got) {
+      atomicCAS(A.err, 0, 1);
+      ctl.fail = 1;
+    }
+  }
+  __syncthreads();
+  if (ctl.fail) return false;
+  ws_bar_try(bar, parity);  // every thread observes the completed phase itself
+  return true;
+}
+// Before leaving: the last fill of a barrier landed (bounded), so no copy
+// is in flight into shared memory the CTA releases.
+__device__ void ws_bar_drain(uint32_t bar, unsigned fills) {
+  if (threadIdx.x == 0 && fills > 0) {
+    const unsigned long long t0 = wtime();
+    while (!ws_bar_try(bar, (fills - 1) & 1) && wtime() - t0 < kWsWaitNs) {
+    }
+  }
+}
+
 // h[i] = f16(q[i]·d[i/32]): the float16 value every Whisper product widens
 // a Q8_0 value to (whisper/model.go:486-490).
 __global__ void k_wwiden(const int8_t* q, const uint16_t* d, uint16_t* h, size_t n) {
@@ -1612,8 +1648,14 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
   __shared__ float gres[3];
   __shared__ VI gresv[2];
   __shared__ WsCtl ctl;
-  if (threadIdx.x == 0) ctl.bar_k = 0, ctl.fail = 0;
+  __shared__ __align__(8) uint64_t mbar[4];  // weight buffers 0 and 1, cross K rows, cross V rows
+  if (threadIdx.x == 0) {
+    ctl.bar_k = 0, ctl.fail = 0;
+    for (int b = 0; b < 4; b++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_addr(&mbar[b])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
   __syncthreads();
+  unsigned fills[4] = {0, 0, 0, 0};
   GridRed red{A, ctl, shf, shv, gcol, gvi, gres, gresv};
   // this CTA's rows: [r0, r1) of the state-sized products, [f0, f1) of fc1,
   // [v0, v1) of the logits in chunks of A.lrows
@@ -1622,31 +1664,44 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
   const int v0 = ws_split(A.vocab, cta, G), v1 = ws_split(A.vocab, cta + 1, G);
   const int nchunk = max(1, (v1 - v0 + A.lrows - 1) / A.lrows);
   const int items = L + nchunk;  // staged items a step: the layers, then the logits chunks
-  auto stage = [&](int t, unsigned char* buf) {
+  // item t of a step into weight buffer b: a bulk copy a row (thread c the
+  // c-th row of the layer's eight slices, or of the logits chunk)
+  auto stage = [&](int t, int b) {
+    unsigned char* buf = wbuf + size_t(b) * A.wb;
+    const uint32_t bar = smem_addr(&mbar[b]);
+    fills[b]++;
     if (t < L) {
       const WS1Layer& Y = A.layers[t];
       const WsPlan p = ws_plan(Y, st, ff, r1 - r0, f1 - f0);
+      const int R = r1 - r0, Rf = f1 - f0;
+      if (threadIdx.x == 0) ws_expect(bar, uint32_t(2 * (6 * R * st + Rf * st + R * ff)));
       const WMat* m[8] = {&Y.q, &Y.k, &Y.v, &Y.o, &Y.xq, &Y.xo, &Y.fc1, &Y.fc2};
-      for (int i = 0; i < 8; i++)
-        ws_stage(*m[i], i == 7 ? ff : st, i == 6 ? f0 : r0, i == 6 ? f1 : r1, buf + p.off[i]);
+      for (int c = threadIdx.x; c < 7 * R + Rf; c += blockDim.x) {
+        int k = c, i = 0;
+        while (k >= (i == 6 ? Rf : R)) k -= (i == 6 ? Rf : R), i++;
+        const int K = i == 7 ? ff : st, row = (i == 6 ? f0 : r0) + k;
+        ws_bulk(buf + p.off[i] + k * (2 * K + 16), m[i]->h + (size_t)row * K, uint32_t(2 * K), bar);
+      }
     } else {
-      const int a = min(v1, v0 + (t - L) * A.lrows), b = min(v1, a + A.lrows);
-      ws_stage(A.emb, st, a, b, buf);
+      const int a = min(v1, v0 + (t - L) * A.lrows), e = min(v1, a + A.lrows);
+      if (threadIdx.x == 0) ws_expect(bar, uint32_t(2 * (e - a) * st));
+      for (int c = threadIdx.x; c < e - a; c += blockDim.x)
+        ws_bulk(buf + c * (2 * st + 16), A.emb.h + (size_t)(a + c) * st, uint32_t(2 * st), bar);
     }
   };
-  // item t of the step is consumed from buffer qi & 1; on entry the next
-  // item goes to the other buffer (whose last reader finished behind a CTA
-  // barrier), then this one's copies are waited for
+  // item t of the step is consumed from buffer qi & 1 (that buffer's fill
+  // qi / 2); on entry the next item goes to the other buffer (whose last
+  // reader finished behind a CTA barrier), then this one's copies are waited
+  // for. nullptr when the wait ran out.
   int qi = 0;
-  auto consume = [&](int t) -> unsigned char* {
-    stage((t + 1) % items, wbuf + size_t((qi + 1) & 1) * A.wb);
-    cpa_commit();
-    cpa_wait<1>();
-    __syncthreads();
-    return wbuf + size_t((qi++) & 1) * A.wb;
+  auto consume = [&](int t) -> const unsigned char* {
+    stage((t + 1) % items, (qi + 1) & 1);
+    const int b = qi & 1;
+    if (!ws_bar_wait(A, ctl, smem_addr(&mbar[b]), (qi >> 1) & 1)) return nullptr;
+    qi++;
+    return wbuf + size_t(b) * A.wb;
   };
-  stage(0, wbuf);
-  cpa_commit();
+  stage(0, 0);
   // the cross scores' key chunks: about G / nh per head, whole groups of 16
   const int ctx4 = ctx & ~3;
   int ks = max(1, G / nh);
@@ -1666,13 +1721,14 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
     for (int l = 0; l < L; l++) {
       const WS1Layer& Y = A.layers[l];
       const unsigned char* wl = consume(l);
+      if (!wl) break;
       const WsPlan p = ws_plan(Y, st, ff, r1 - r0, f1 - f0);
-      if (cta < nh * ks) {  // this CTA's cross K rows, for the scores four phases on
+      if (cta < nh * ks && threadIdx.x == 0) {  // this CTA's cross K rows, for the scores four phases on
         const int h = cta / ks, j0 = (cta % ks) * ch, j1 = min(ctx4, j0 + ch);
-        const float* kr = Y.ck + ((size_t)h * ctx + j0) * 64;
-        for (int t = threadIdx.x; t < (j1 - j0) * 16; t += blockDim.x) cpa16(xk + 4 * t, kr + 4 * t);
-        cpa_commit();
+        ws_expect(smem_addr(&mbar[2]), uint32_t((j1 - j0) * 256));
+        ws_bulk(xk, Y.ck + ((size_t)h * ctx + j0) * 64, uint32_t((j1 - j0) * 256), smem_addr(&mbar[2]));
       }
+      if (cta < nh * ks) fills[2]++;
       ws_ln(xs, cur, Y.ln1w, Y.ln1b, st, shd);
       {
         const WsProd P = {{{wl + p.off[0], r0, r1 - r0, Y.qb, A.q, nullptr},
@@ -1688,9 +1744,11 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
       if (!ws_sync(A, ctl)) break;
       if (cta < nh * xo_s) {  // the Vᵀ rows of this CTA's cross outputs, for three phases on
         const int h = cta / xo_s, d0 = (cta % xo_s) * A.xo_nd;
-        const float* vrow = Y.cvt + ((size_t)h * 64 + d0) * ctx;
-        for (int t = threadIdx.x; t < A.xo_nd * ctx / 4; t += blockDim.x) cpa16(xv + 4 * t, vrow + 4 * t);
-        cpa_commit();
+        if (threadIdx.x == 0) {
+          ws_expect(smem_addr(&mbar[3]), uint32_t(A.xo_nd * ctx * 4));
+          ws_bulk(xv, Y.cvt + ((size_t)h * 64 + d0) * ctx, uint32_t(A.xo_nd * ctx * 4), smem_addr(&mbar[3]));
+        }
+        fills[3]++;
       }
       ws_load(cur, A.att, st);
       ws_rows(WS_RESID, WsOut{wl + p.off[3], r0, r1 - r0, Y.ob, A.x, xs}, cur, st);
@@ -1702,8 +1760,7 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
       if (cta < nh * ks) {  // cross scores of key chunk cta % ks of head cta / ks
         const int h = cta / ks, kc = cta % ks, j0 = kc * ch, j1 = min(ctx4, j0 + ch);
         if (threadIdx.x < 64) qh[threadIdx.x] = A.q[h * 64 + threadIdx.x];
-        cpa_wait<0>();
-        __syncthreads();
+        if (!ws_bar_wait(A, ctl, smem_addr(&mbar[2]), (fills[2] - 1) & 1)) break;
         float mx = ws_xscores(qh, Y.ck + (size_t)h * ctx * 64, j0, j1, kc == ks - 1, ctx, A.sg + (size_t)h * ctx, xk);
         mx = block_max(mx, shf);
         if (threadIdx.x == 0) A.mg[h * ks + kc] = mx;
@@ -1715,8 +1772,7 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
         mx = block_max(mx, shf);
         ws_load(sc, A.sg + (size_t)h * ctx, ctx);
         wcross_softmax(sc, ctx, mx, shf);
-        cpa_wait<0>();
-        __syncthreads();
+        if (!ws_bar_wait(A, ctl, smem_addr(&mbar[3]), (fills[3] - 1) & 1)) break;
         ws_xout(sc, xv, ctx, d0, A.xo_nd, A.att + h * 64);
       }
       if (!ws_sync(A, ctl)) break;
@@ -1737,13 +1793,17 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
     ws_ln(xs, cur, A.lnw, A.lnb, st, shd);
     for (int c = 0; c < nchunk; c++) {
       const unsigned char* wl = consume(L + c);
+      if (!wl) break;
       const int a = min(v1, v0 + c * A.lrows), b = min(v1, a + A.lrows);
       ws_rows(WS_STORE, WsOut{wl, a, b - a, nullptr, A.logits, nullptr}, cur, st);
       __syncthreads();
     }
     if (!ws_sync(A, ctl)) break;
   }
-  cpa_wait<0>();  // the prefetch for a next step
+  // no copy in flight into the shared memory the CTA releases: the prefetch
+  // for a next step, and any a failed wait left
+  for (int b = 0; b < 4; b++) ws_bar_drain(smem_addr(&mbar[b]), fills[b]);
+  cpa_wait<0>();
   // the positions and the run's step counter, as the per-kernel path leaves them
   if (cta == 0 && threadIdx.x == 0 && !ctl.fail) {
     A.row_pos[0] = pos0 + steps;
