@@ -120,6 +120,7 @@ __device__ float exp_sub(float* e, int n, float mx, float* sh) {
   __syncthreads();
   if (threadIdx.x < 8) {
     float a = 0.f;
+#pragma unroll 8
     for (int c = threadIdx.x; c < n8; c += 8) a = __fadd_rn(a, e[c]);
     sh[threadIdx.x] = a;
   }
@@ -966,6 +967,10 @@ struct ClusterRed {
     c = cl_max<CL>(c, shf, &clf[2]);
   }
   __device__ float sum(float v, int slot) { return cl_sum<CL>(v, shf, &clf[3 + slot]); }
+  __device__ void sum2(float& a, float& b) {
+    a = cl_sum<CL>(a, shf, &clf[3]);
+    b = cl_sum<CL>(b, shf, &clf[4]);
+  }
   __device__ void vimax2(VI& a, VI& b) {
     a = cl_vi_max<CL>(a, shv, &clv[0]);
     b = cl_vi_max<CL>(b, shv, &clv[1]);
@@ -986,28 +991,31 @@ struct ClusterRed {
 // the outputs: out[0..3] (id, tid, p, plog), the stream's sampling state
 // and the next token.
 //
-// The three float32 sums of logSoftmax, the timestamp rule and softmaxInf
-// are taken in parallel, and every decision they feed is checked: the
-// timestamp rule must clear a relative margin of 2e-4, and the winning
-// probability must beat every earlier index's by a factor 1 − 2^-20 (the
-// division by the sum can then not tie them). A row that misses a margin is
-// recomputed by one thread in the reference's order. One pass takes
-// e_i = expf(lg_i − max) for the whole row into scratch; without the
-// timestamp rule's masking softmaxInf's terms are those same e_i (and so is
-// its sum), so only the timestamps are taken again.
-template <class Red>
-__device__ void proc_row(Red& red, float* lg, float* e, const WVocabDev& v, WSample* sp, int* orow, int* next_tok,
-                         int a0, int a1, bool writer) {
-  __shared__ int amb;
-  const int n = v.n, beg = v.beg;
-  const WSample q = *sp;
+// The float32 sums of logSoftmax, the timestamp rule and softmaxInf are taken
+// in parallel, and every decision they feed is checked: the timestamp rule
+// must clear a relative margin of 2e-4, and the winning probability must
+// beat every earlier index's by a factor 1 − 2^-20 (the division by the sum
+// can then not tie them). A row that misses a margin is recomputed by one
+// thread in the reference's order. One pass takes e_i = expf(lg_i − max)
+// for the whole row into scratch and, in the same reduction, the
+// timestamps' Σ expf(lg_i − max_ts): the timestamp rule's logsumexp of
+// logprobs[beg:] is log of that plus (max_ts − ls) (the reference sums
+// expf((lg_i − ls) − (max_ts − ls)); the two differ by a few ulps of the
+// exponents, far inside the margin), and with text masked it is softmaxInf's
+// sum too, whose terms are then taken again into scratch.
+//
+// proc_prep is the first part: the rules on this CTA's entries and their
+// maxima (all, timestamps, text), per thread; proc_finish the rest from the
+// row's maxima.
+__device__ __forceinline__ void proc_prep(float* lg, const WVocabDev& v, const WSample& q, int a0, int a1, int* amb,
+                                          float& mx, float& mts, float& mtx) {
+  const int beg = v.beg;
   const bool initial = q.nt == 0;
   auto setinf = [&](int i) {
     if (i >= a0 && i < a1) lg[i] = NINF;
   };
-  // ---- the rules
   if (threadIdx.x == 0) {
-    amb = 0;
+    *amb = 0;
     if (initial) {
       setinf(v.eot);
       if (v.space >= 0) setinf(v.space);
@@ -1021,7 +1029,7 @@ __device__ void proc_row(Red& red, float* lg, float* e, const WVocabDev& v, WSam
   __syncthreads();
   const bool last = q.nt > 0 && q.last >= beg, penult = q.nt < 2 || q.penult >= beg;
   const int tid0 = int(round(1.0 / (30.0 / double(v.audio_ctx))));
-  float mx = NINF, mts = NINF, mtx = NINF;
+  mx = NINF, mts = NINF, mtx = NINF;
   for (int i = a0 + threadIdx.x; i < a1; i += blockDim.x) {
     bool m = false;
     if (last) m = penult ? i >= beg : i < v.eot;
@@ -1033,43 +1041,43 @@ __device__ void proc_row(Red& red, float* lg, float* e, const WVocabDev& v, WSam
     if (i >= beg) mts = fmaxf(mts, x);
     else mtx = fmaxf(mtx, x);
   }
-  red.max3(mx, mts, mtx);
-  // ---- logSoftmax's sum, with e_i kept
-  float s1 = 0.f;
+}
+
+template <class Red>
+__device__ __forceinline__ void proc_finish(Red& red, float* lg, float* e, const WVocabDev& v, WSample* sp,
+                                            const WSample& q, int* orow, int* next_tok, int a0, int a1, bool writer,
+                                            int* amb, float mx, float mts, float mtx) {
+  const int n = v.n, beg = v.beg;
+  // ---- logSoftmax's sum with e_i kept, and the timestamps' sum
+  float s1 = 0.f, sts = 0.f;
   for (int i = a0 + threadIdx.x; i < a1; i += blockDim.x) {
     const float x = lg[i];
     const float ei = x > NINF ? expf_go(__fsub_rn(x, mx)) : 0.f;
     e[i] = ei;
     s1 = __fadd_rn(s1, ei);
+    if (i >= beg && x > NINF) sts = __fadd_rn(sts, expf_go(__fsub_rn(x, mts)));
   }
-  s1 = red.sum(s1, 0);
+  red.sum2(s1, sts);
   const float ls = __fadd_rn(float(log(double(s1))), mx);
   // ---- the timestamp rule
   const float ts_max = mts > NINF ? __fsub_rn(mts, ls) : NINF;  // the largest of logprobs[beg:]
   bool mask_text = false;
   if (ts_max > NINF) {
-    float sum = 0.f;
-    for (int i = max(beg, a0) + threadIdx.x; i < a1; i += blockDim.x)
-      if (lg[i] > NINF) sum = __fadd_rn(sum, expf_go(__fsub_rn(__fsub_rn(lg[i], ls), ts_max)));
-    sum = red.sum(sum, 1);
-    const float ts_lp = __fadd_rn(float(log(double(sum))), ts_max);
+    const float ts_lp = __fadd_rn(float(log(double(sts))), ts_max);
     const float text_max = mtx > NINF ? __fsub_rn(mtx, ls) : NINF;
     mask_text = ts_lp > text_max;
-    if (text_max > NINF && fabsf(ts_lp - text_max) <= 2e-4f * (1.f + fabsf(text_max))) amb = 1;
+    if (text_max > NINF && fabsf(ts_lp - text_max) <= 2e-4f * (1.f + fabsf(text_max))) *amb = 1;
   }
   // ---- softmaxInf's terms: the same e_i, or, with text masked, the
-  // timestamps' again against their own maximum
+  // timestamps' against their own maximum (their sum is sts)
   const int lo = mask_text ? beg : 0;
   float s2 = s1;
   if (mask_text) {
-    s2 = 0.f;
+    s2 = sts;
     for (int i = max(beg, a0) + threadIdx.x; i < a1; i += blockDim.x) {
       const float x = lg[i];
-      const float ei = x > NINF ? expf_go(__fsub_rn(x, mts)) : 0.f;
-      e[i] = ei;
-      s2 = __fadd_rn(s2, ei);
+      e[i] = x > NINF ? expf_go(__fsub_rn(x, mts)) : 0.f;
     }
-    s2 = red.sum(s2, 2);
   }
   __syncthreads();
   VI best{-1.f, n}, bts{-1.f, n};
@@ -1091,11 +1099,11 @@ __device__ void proc_row(Red& red, float* lg, float* e, const WVocabDev& v, WSam
   }
   red.max2(near, near_t);
   const float margin = 1.f - 9.5367431640625e-07f;  // 1 − 2^-20
-  if ((best.v > 0.f && near >= best.v * margin) || (bts.v > 0.f && near_t >= bts.v * margin)) amb = 1;
+  if ((best.v > 0.f && near >= best.v * margin) || (bts.v > 0.f && near_t >= bts.v * margin)) *amb = 1;
   __syncthreads();
   if (threadIdx.x == 0 && writer) {
     int o[4];
-    if (amb) {
+    if (*amb) {
       proc_exact(lg, n, beg, o);
       if (v.exact_rows) atomicAdd(v.exact_rows, 1ull);
     } else {
@@ -1120,6 +1128,17 @@ __device__ void proc_row(Red& red, float* lg, float* e, const WVocabDev& v, WSam
     if (next_tok) *next_tok = o[0];
   }
   red.done();
+}
+
+template <class Red>
+__device__ void proc_row(Red& red, float* lg, float* e, const WVocabDev& v, WSample* sp, int* orow, int* next_tok,
+                         int a0, int a1, bool writer) {
+  __shared__ int amb;
+  const WSample q = *sp;
+  float mx, mts, mtx;
+  proc_prep(lg, v, q, a0, a1, &amb, mx, mts, mtx);
+  red.max3(mx, mts, mtx);
+  proc_finish(red, lg, e, v, sp, q, orow, next_tok, a0, a1, writer, &amb, mx, mts, mtx);
 }
 
 // Rows spread over clusters of CL CTAs (CL = 1: one CTA per row); CTA k of a
@@ -1277,13 +1296,20 @@ struct GridRed {
     combine(3, false);
     a = res[0], b = res[1], c = res[2];
   }
-  __device__ float sum(float v, int slot) {
-    v = block_sum(v, shf);
-    put(3 + slot, v);
+  __device__ void sum2(float& a, float& b) {
+    a = block_sum(a, shf);
+    b = block_sum(b, shf);
+    put(3, a), put(4, b);
     ws_sync(A, ctl);
-    gather(3 + slot, 1);
-    combine(1, true);
-    return res[0];
+    gather(3, 2);
+    combine(2, true);
+    a = res[0], b = res[1];
+  }
+  // the row's maxima whose partials the logits phase left in slots 0-2
+  __device__ void maxima(float& a, float& b, float& c) {
+    gather(0, 3);
+    combine(3, false);
+    a = res[0], b = res[1], c = res[2];
   }
   __device__ void vimax2(VI& a, VI& b) {
     a = block_vi_max(a, shv);
@@ -1625,8 +1651,33 @@ __device__ __noinline__ void ws_xout(const float* p, const float* vs, int ctx, i
   wcross_out<1>(p, vs, ctx, d0, att, d0, nd);
 }
 
-__device__ __noinline__ void ws_proc(GridRed& red, const WStep1Args& A, int i, int v0, int v1, bool writer) {
-  proc_row(red, A.logits, A.scratch, A.voc, A.state, A.out + 4 * i, A.row_tok, v0, v1, writer);
+// process + sample of step i: the rules and maxima first unless the
+// previous step's logits phase took them (`prepped`: their partials in the
+// reduction slots 0-2).
+__device__ __noinline__ void ws_proc(GridRed& red, const WStep1Args& A, int i, int v0, int v1, bool writer,
+                                     bool prepped, int* amb) {
+  const WSample q = *A.state;
+  float mx, mts, mtx;
+  if (prepped) {
+    red.maxima(mx, mts, mtx);
+  } else {
+    proc_prep(A.logits, A.voc, q, v0, v1, amb, mx, mts, mtx);
+    red.max3(mx, mts, mtx);
+  }
+  proc_finish(red, A.logits, A.scratch, A.voc, A.state, q, A.out + 4 * i, A.row_tok, v0, v1, writer, amb, mx, mts,
+              mtx);
+}
+
+// The rules and this CTA's maxima of the logits just made, for the next
+// step's process (its state is the one the current step's sample left).
+__device__ __noinline__ void ws_prep(GridRed& red, const WStep1Args& A, int v0, int v1, int* amb) {
+  const WSample q = *A.state;
+  float mx, mts, mtx;
+  proc_prep(A.logits, A.voc, q, v0, v1, amb, mx, mts, mtx);
+  mx = block_max(mx, red.shf);
+  mts = block_max(mts, red.shf);
+  mtx = block_max(mtx, red.shf);
+  red.put(0, mx), red.put(1, mts), red.put(2, mtx);
 }
 
 __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restrict__ Ap, int pos0, int steps) {
@@ -1648,6 +1699,7 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
   __shared__ float gres[3];
   __shared__ VI gresv[2];
   __shared__ WsCtl ctl;
+  __shared__ int amb;  // process/sample's "recompute in order" flag
   __shared__ __align__(8) uint64_t mbar[4];  // weight buffers 0 and 1, cross K rows, cross V rows
   if (threadIdx.x == 0) {
     ctl.bar_k = 0, ctl.fail = 0;
@@ -1711,7 +1763,7 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
   int i = 0;
   for (; i < steps; i++) {
     // ---- process + sample of the last logits (transcribe.go:370-494)
-    ws_proc(red, A, i, v0, v1, cta == 0);
+    ws_proc(red, A, i, v0, v1, cta == 0, i > 0, &amb);
     if (!ws_sync(A, ctl)) break;
     const int pos = pos0 + i, tok = A.row_tok[0];
     // ---- decode of the token at pos (decoder.go:33-140): the embedding
@@ -1798,6 +1850,8 @@ __global__ void __launch_bounds__(WS_NT, 1) k_wstep1(const WStep1Args* __restric
       ws_rows(WS_STORE, WsOut{wl, a, b - a, nullptr, A.logits, nullptr}, cur, st);
       __syncthreads();
     }
+    if (ctl.fail) break;
+    if (i + 1 < steps) ws_prep(red, A, v0, v1, &amb);  // the last step's logits stay as made
     if (!ws_sync(A, ctl)) break;
   }
   // no copy in flight into the shared memory the CTA releases: the prefetch
