@@ -1189,7 +1189,7 @@ __global__ void k_wtick(int rows, int* row_pos, int* dst_row, int text_ctx, int 
 //
 // k_wstep1 runs `steps` rounds of grx_whisper_run's step for a batch of one
 // stream — process/sample of the last logits, then the decode of the sampled
-// token — in one cooperative launch of one 512-thread CTA per SM, with a
+// token — in one cooperative launch of one 256-thread CTA per SM, with a
 // grid barrier where a step needs every CTA's results. Per layer: the q/k/v
 // rows, self-attention (a few CTAs a head, each with some of its outputs),
 // o with the residual, LayerNorm and xq, the cross scores (key chunks over
@@ -1529,7 +1529,6 @@ struct WsPlan {
 
 __device__ WsPlan ws_plan(const WS1Layer& Y, int st, int ff, int R, int Rf) {
   WsPlan p;
-  const WMat* m[8] = {&Y.q, &Y.k, &Y.v, &Y.o, &Y.xq, &Y.xo, &Y.fc1, &Y.fc2};
   p.off[0] = 0;
   for (int i = 0; i < 8; i++)
     p.off[i + 1] = p.off[i] + ws_slice_bytes(true, i == 6 ? Rf : R, i == 7 ? ff : st);

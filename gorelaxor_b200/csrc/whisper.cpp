@@ -375,7 +375,6 @@ int ws1_setup(grx_whisper_batch* b) {
   int wb = 0;
   for (const WS1Layer& Y : A.layers) {
     if (&Y - A.layers >= A.L) break;
-    const WMat* mm[8] = {&Y.q, &Y.k, &Y.v, &Y.o, &Y.xq, &Y.xo, &Y.fc1, &Y.fc2};
     int lb = 0;
     for (int i = 0; i < 8; i++) lb += ws_slice_bytes(true, i == 6 ? Rf : R, i == 7 ? ff : A.st);
     wb = std::max(wb, lb);
