@@ -1440,6 +1440,12 @@ int grx_streams_step(grx_streams* s, const float* noise, float* lm_out, float* e
       CK(cudaGraphLaunch(q->exec, q->st));
       q->launches += q->per_frame;
     }
+  }
+  // the copies out after every part's frame is queued: a copy to pageable
+  // host memory returns only when it is done, and would otherwise hold back
+  // the next part's launch
+  for (grx_streams* q : sets) {
+    const size_t r0 = size_t(q->row0), nl = size_t(q->n) * ld;
     if (lm_out) CK(cudaMemcpyAsync(lm_out + r0 * d, q->lm_out, size_t(q->n) * d * 4, cudaMemcpyDeviceToHost, q->st));
     if (eos) CK(cudaMemcpyAsync(eos + r0, q->eos1, size_t(q->n) * 4, cudaMemcpyDeviceToHost, q->st));
     if (latent) CK(cudaMemcpyAsync(latent + r0 * ld, q->lat1, nl * 4, cudaMemcpyDeviceToHost, q->st));
