@@ -119,9 +119,15 @@ struct grx_streams {
   int f1_grid = 0;
   unsigned* f1_bar = nullptr;
   int* f1_err = nullptr;
+  // the error word as a launch left it, copied on the stream into pinned
+  // memory, so a check after the stream's synchronisation needs no copy of
+  // its own (f1_err_copied: such a copy was queued since the last check)
+  int* f1_err_h = nullptr;
+  bool f1_err_copied = false;
   ~grx_streams() {
     parts.clear();
     cudaSetDevice(ar.dev);
+    if (f1_err_h) cudaFreeHost(f1_err_h);
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
     if (exec_n) cudaGraphExecDestroy(exec_n);
@@ -465,6 +471,7 @@ int frame1_setup(grx_streams* s) {
   A.err = s->ar.alloc<int>(1, &rc);
   if (rc) return rc;
   CK(cudaMemset(A.err, 0, sizeof(int)));
+  CK(cudaHostAlloc(&s->f1_err_h, sizeof(int), cudaHostAllocDefault));
   s->f1 = s->ar.upload(&A, 1, &rc);
   if (rc) return rc;
   s->f1_smem = smem;
@@ -481,6 +488,8 @@ int frame1_run(grx_streams* s, int frames, int stall = 0) {
   if (frames <= 0) return GRX_OK;
   CK(cudaMemsetAsync(s->f1_bar, 0, sizeof(unsigned), s->st));
   CK(launch_frame1(s->f1, s->f1_smem, s->f1_slot, s->f1_grid, frames, stall, s->st));
+  CK(cudaMemcpyAsync(s->f1_err_h, s->f1_err, sizeof(int), cudaMemcpyDeviceToHost, s->st));
+  s->f1_err_copied = true;
   s->launches += 1;
   return GRX_OK;
 }
@@ -491,7 +500,12 @@ int frame1_run(grx_streams* s, int frames, int stall = 0) {
 int frame1_check(grx_streams* s) {
   if (!s->b1) return GRX_OK;
   int e = 0;
-  CK(cudaMemcpy(&e, s->f1_err, sizeof e, cudaMemcpyDeviceToHost));
+  if (s->f1_err_copied) {
+    e = *s->f1_err_h;
+    s->f1_err_copied = false;
+  } else {
+    CK(cudaMemcpy(&e, s->f1_err, sizeof e, cudaMemcpyDeviceToHost));
+  }
   if (e)
     return fail(GRX_ETIMEDOUT, std::string("the persistent frame kernel gave up on a ") +
                                    (e == 1 ? "grid barrier" : "weight copy") + " after its one-second limit");
@@ -1002,6 +1016,7 @@ int grx_streams_reset(grx_streams* s) {
     CK(cudaMemcpyAsync(s->lat + size_t(i) * m->ldim, m->bos, sizeof(float) * size_t(m->ldim), cudaMemcpyDeviceToDevice,
                        s->st));
   CK(cudaStreamSynchronize(s->st));
+  s->f1_err_copied = false;  // the reset cleared the word; a copy queued before it is stale
   return GRX_OK;
 }
 
