@@ -151,6 +151,16 @@ __device__ __forceinline__ void fl_out(const FArgs& a, int m, int n, float r) {
     case FE_ROWPOS:
       a.y[(size_t)a.dst_row[m] * a.ldy + n] = v;
       break;
+    case FE_QKV: {
+      const int sg = n / a.seg, c = n - sg * a.seg;
+      const float* b = a.qkv_bias[sg];
+      const float w = b ? __fadd_rn(r, b[c]) : r;
+      if (sg == 0)
+        a.y[(size_t)m * a.ldy + c] = w;
+      else
+        a.qkv_y[sg - 1][(size_t)a.dst_row[m] * a.ldy + c] = w;
+      break;
+    }
     default:
       *yp = v;
   }

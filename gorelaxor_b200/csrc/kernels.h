@@ -220,6 +220,7 @@ enum FEpi {
   FE_RESID = 5,   // y += dot + bias                  (whisper/decoder.go:89,121,129: matmul then addTo)
   FE_GELU = 6,    // y = geluAVX(dot + bias)          (whisper/decoder.go:127)
   FE_ROWPOS = 7,  // y[dst_row[m]·ldy + n] = dot + bias  (a cache row per input row)
+  FE_QKV = 8,     // whisper's q, k, v stacked: q to y, k and v to their cache rows (decoder.go:62-68)
 };
 
 struct FArgs {
@@ -255,6 +256,13 @@ struct FArgs {
   // (m / rg_len)·rg_stride + rg_off + m % rg_len of x and row
   // (m / rg_len)·ry_stride + ry_off + m % rg_len of y (rg_len 0: row m).
   int rg_len = 0, rg_stride = 0, rg_off = 0, ry_stride = 0, ry_off = 0;
+  // FE_QKV: the weight is three matrices of `seg` rows stacked (q, k, v).
+  // Column c of the first goes to y[m·ldy + c] (+ qkv_bias[0][c]); of the
+  // second and third to qkv_y[0] and qkv_y[1] at row dst_row[m] (stride
+  // ldy), + qkv_bias[1] / [2] where given. `bias` stays null.
+  int seg = 0;
+  const float* qkv_bias[3] = {nullptr, nullptr, nullptr};
+  float* qkv_y[2] = {nullptr, nullptr};
 };
 
 void launch_flin(const FArgs& a, int M, cudaStream_t st);

@@ -25,6 +25,9 @@ struct WLayerDev {
   float *attn_ln_w, *attn_ln_b, *x_ln_w, *x_ln_b, *mlp_ln_w, *mlp_ln_b;
   WMat q, k, v, o, xq, xk, xv, xo, fc1, fc2;
   float *qb, *vb, *ob, *xqb, *xvb, *xob, *fc1b, *fc2b;
+  // q, k and v stacked into one matrix of 3·n_state rows, for one product
+  // launch a decode step (rows 0 when their types differ)
+  WMat qkv;
 };
 
 // A ggml tensor of the file: type, dims (fastest first), its bytes.
@@ -253,9 +256,32 @@ int enqueue_decode(grx_whisper_batch* b) {
     const float* ckl = b->ck + l * layer_stride_cross(m, n);
     const float* cvl = b->cvt + l * layer_stride_cross(m, n);
     launch_wln(b->x, b->cur, L.attn_ln_w, L.attn_ln_b, n, st, s), k++;
-    flin_w(L.q, b->cur, st, n, L.qb, FE_BIAS, b->q, st, nullptr, s), k++;
-    flin_w(L.k, b->cur, st, n, nullptr, FE_ROWPOS, skl, st, b->dst_row, s), k++;
-    flin_w(L.v, b->cur, st, n, L.vb, FE_ROWPOS, svl, st, b->dst_row, s), k++;
+    if (L.qkv.rows == 3 * st) {
+      // q, k and v in one launch: the same products, three times the rows
+      FArgs a;
+      a.epi = FE_QKV;
+      a.x = b->cur;
+      a.ldx = st;
+      a.wq = L.qkv.q;
+      a.wd = L.qkv.d;
+      a.wh = L.qkv.h;
+      a.q8_as_f16 = L.qkv.q != nullptr;
+      a.N = L.qkv.rows;
+      a.K = L.qkv.cols;
+      a.y = b->q;
+      a.ldy = st;
+      a.dst_row = b->dst_row;
+      a.seg = st;
+      a.qkv_bias[0] = L.qb;
+      a.qkv_bias[2] = L.vb;
+      a.qkv_y[0] = skl;
+      a.qkv_y[1] = svl;
+      launch_flin(a, n, s), k++;
+    } else {
+      flin_w(L.q, b->cur, st, n, L.qb, FE_BIAS, b->q, st, nullptr, s), k++;
+      flin_w(L.k, b->cur, st, n, nullptr, FE_ROWPOS, skl, st, b->dst_row, s), k++;
+      flin_w(L.v, b->cur, st, n, L.vb, FE_ROWPOS, svl, st, b->dst_row, s), k++;
+    }
     launch_wself(b->rows, b->q, skl, svl, b->att, s), k++;
     flin_w(L.o, b->att, st, n, L.ob, FE_RESID, b->x, st, nullptr, s), k++;
     launch_wln(b->x, b->cur, L.x_ln_w, L.x_ln_b, n, st, s), k++;
@@ -582,6 +608,37 @@ int grx_whisper_load(const void* bytes, size_t len, int device, grx_whisper** ou
     }
     return w;
   };
+  // three matrices of one type and width stacked by rows on the device
+  auto stack3 = [&](const WMat& a, const WMat& b, const WMat& c) -> WMat {
+    WMat w;
+    const WMat* ms[3] = {&a, &b, &c};
+    const bool q8 = a.q && b.q && c.q, h16 = a.h && b.h && c.h;
+    if (rc || !(q8 || h16) || b.cols != a.cols || c.cols != a.cols) return w;
+    w.rows = a.rows + b.rows + c.rows;
+    w.cols = a.cols;
+    if (q8) {
+      int8_t* q = m->ar.alloc<int8_t>(size_t(w.rows) * w.cols, &rc);
+      uint16_t* d = m->ar.alloc<uint16_t>(size_t(w.rows) * w.cols / 32, &rc);
+      if (rc) return WMat{};
+      for (int i = 0, r = 0; i < 3; r += ms[i]->rows, i++) {
+        const size_t n = size_t(ms[i]->rows) * w.cols;
+        if (cudaMemcpy(q + size_t(r) * w.cols, ms[i]->q, n, cudaMemcpyDeviceToDevice) != cudaSuccess ||
+            cudaMemcpy(d + size_t(r) * w.cols / 32, ms[i]->d, n / 32 * 2, cudaMemcpyDeviceToDevice) != cudaSuccess)
+          rc = fail(GRX_ECUDA, "stacking q, k and v failed");
+      }
+      w.q = q;
+      w.d = d;
+    } else {
+      uint16_t* h = m->ar.alloc<uint16_t>(size_t(w.rows) * w.cols, &rc);
+      if (rc) return WMat{};
+      for (int i = 0, r = 0; i < 3; r += ms[i]->rows, i++)
+        if (cudaMemcpy(h + size_t(r) * w.cols, ms[i]->h, size_t(ms[i]->rows) * w.cols * 2, cudaMemcpyDeviceToDevice) !=
+            cudaSuccess)
+          rc = fail(GRX_ECUDA, "stacking q, k and v failed");
+      w.h = h;
+    }
+    return w;
+  };
   m->dec_pos = vec2("decoder.positional_embedding", m->n_text_ctx, st);
   m->tok_emb = mat("decoder.token_embedding.weight", m->n_vocab, st);
   m->ln_w = vec("decoder.ln.weight", st);
@@ -613,6 +670,7 @@ int grx_whisper_load(const void* bytes, size_t len, int device, grx_whisper** ou
     L.fc1b = vec(lp + "mlp.0.bias", 4 * st);
     L.fc2 = mat(lp + "mlp.2.weight", st, 4 * st);
     L.fc2b = vec(lp + "mlp.2.bias", st);
+    L.qkv = stack3(L.q, L.k, L.v);
     m->layers.push_back(L);
   }
   // the audio encoder (model.go:352-372), bound when the file has it
