@@ -83,6 +83,9 @@ struct grx_voice {
   std::string model;
 };
 
+// Bytes of a set's FrameIO before its noise rows in their shared device block.
+constexpr size_t kIoPad = 256;
+
 struct grx_streams {
   Arena ar;
   grx_flowlm* m = nullptr;
@@ -124,10 +127,20 @@ struct grx_streams {
   // its own (f1_err_copied: such a copy was queued since the last check)
   int* f1_err_h = nullptr;
   bool f1_err_copied = false;
+  // grx_streams_step's traffic, one copy each way: the frame's FrameIO and
+  // noise rows are one device block (io, then noise1 kIoPad bytes in),
+  // filled from in1_h; the latent, scaled and eos rows and then the
+  // persistent kernel's error word are another (out1), read into out1_h
+  uint8_t* in1_h = nullptr;
+  size_t in1_bytes = 0;
+  float *out1 = nullptr, *out1_h = nullptr;
+  size_t out1_floats = 0;
   ~grx_streams() {
     parts.clear();
     cudaSetDevice(ar.dev);
     if (f1_err_h) cudaFreeHost(f1_err_h);
+    if (in1_h) cudaFreeHost(in1_h);
+    if (out1_h) cudaFreeHost(out1_h);
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
     if (exec_n) cudaGraphExecDestroy(exec_n);
@@ -468,7 +481,7 @@ int frame1_setup(grx_streams* s) {
   A.ffs = s->ar.alloc<float>(size_t(m->ff / 32), &rc);
   A.mod = s->ar.alloc<float>(size_t(m->depth) * 3 * m->fd, &rc);
   A.bar = s->ar.alloc<unsigned>(1, &rc);
-  A.err = s->ar.alloc<int>(1, &rc);
+  A.err = reinterpret_cast<int*>(s->out1 + s->out1_floats - 1);  // read back with the step's outputs
   if (rc) return rc;
   CK(cudaMemset(A.err, 0, sizeof(int)));
   CK(cudaHostAlloc(&s->f1_err_h, sizeof(int), cudaHostAllocDefault));
@@ -483,14 +496,23 @@ int frame1_setup(grx_streams* s) {
   return GRX_OK;
 }
 
-// Queues `frames` frames of a persistent-kernel set.
-int frame1_run(grx_streams* s, int frames, int stall = 0) {
+// Queues `frames` frames of a persistent-kernel set, then (copy_err) the
+// copy of its error word that frame1_check reads.
+int frame1_run(grx_streams* s, int frames, int stall = 0, bool copy_err = true) {
   if (frames <= 0) return GRX_OK;
   CK(cudaMemsetAsync(s->f1_bar, 0, sizeof(unsigned), s->st));
   CK(launch_frame1(s->f1, s->f1_smem, s->f1_slot, s->f1_grid, frames, stall, s->st));
-  CK(cudaMemcpyAsync(s->f1_err_h, s->f1_err, sizeof(int), cudaMemcpyDeviceToHost, s->st));
-  s->f1_err_copied = true;
+  if (copy_err) CK(cudaMemcpyAsync(s->f1_err_h, s->f1_err, sizeof(int), cudaMemcpyDeviceToHost, s->st));
+  s->f1_err_copied = copy_err;
   s->launches += 1;
+  return GRX_OK;
+}
+
+// The persistent kernel's error word as the host read it.
+int frame1_error(int e) {
+  if (e)
+    return fail(GRX_ETIMEDOUT, std::string("the persistent frame kernel gave up on a ") +
+                                   (e == 1 ? "grid barrier" : "weight copy") + " after its one-second limit");
   return GRX_OK;
 }
 
@@ -506,10 +528,7 @@ int frame1_check(grx_streams* s) {
   } else {
     CK(cudaMemcpy(&e, s->f1_err, sizeof e, cudaMemcpyDeviceToHost));
   }
-  if (e)
-    return fail(GRX_ETIMEDOUT, std::string("the persistent frame kernel gave up on a ") +
-                                   (e == 1 ? "grid barrier" : "weight copy") + " after its one-second limit");
-  return GRX_OK;
+  return frame1_error(e);
 }
 
 // A device-resident run replays kGraphFrames frames per graph launch (the
@@ -1324,12 +1343,21 @@ static int streams_create_one(grx_flowlm* m, int n, const grx_voice* const* voic
   s->nrm = s->ar.alloc<float>(size_t(n) * fd, &rc);
   s->mm = s->ar.alloc<float>(size_t(n) * fd, &rc);
   s->cur = s->ar.alloc<float>(size_t(n) * ld, &rc);
-  s->noise1 = s->ar.alloc<float>(size_t(n) * ld, &rc);
-  s->lat1 = s->ar.alloc<float>(size_t(n) * ld, &rc);
-  s->scaled1 = s->ar.alloc<float>(size_t(n) * ld, &rc);
-  s->eos1 = s->ar.alloc<float>(size_t(n), &rc);
-  s->io = s->ar.alloc<FrameIO>(1, &rc);
+  {
+    static_assert(sizeof(FrameIO) <= kIoPad, "the noise rows follow the FrameIO");
+    s->in1_bytes = kIoPad + size_t(n) * ld * 4;
+    uint8_t* in1 = s->ar.alloc<uint8_t>(s->in1_bytes, &rc);
+    s->io = reinterpret_cast<FrameIO*>(in1);
+    s->noise1 = reinterpret_cast<float*>(in1 + kIoPad);
+    s->out1_floats = 2 * size_t(n) * ld + size_t(n) + 1;
+    s->out1 = s->ar.alloc<float>(s->out1_floats, &rc);
+    s->lat1 = s->out1;
+    s->scaled1 = s->out1 + size_t(n) * ld;
+    s->eos1 = s->out1 + 2 * size_t(n) * ld;
+  }
   if (rc) return rc;
+  CK(cudaHostAlloc(&s->in1_h, s->in1_bytes, cudaHostAllocDefault));
+  CK(cudaHostAlloc(&s->out1_h, s->out1_floats * 4, cudaHostAllocDefault));
   // RoPE cos/sin for every position the streams can reach (nn.go:84-85).
   {
     std::vector<float> t(size_t(s->cap) * hd);
@@ -1442,14 +1470,16 @@ int grx_streams_step(grx_streams* s, const float* noise, float* lm_out, float* e
   for (grx_streams* q : sets) {
     const size_t r0 = size_t(q->row0), nl = size_t(q->n) * ld;
     FrameIO io{q->noise1, nullptr, nullptr, q->eos1, 0, nullptr, q->n, 0, 0, 1};
-    CK(cudaMemcpyAsync(q->noise1, noise + r0 * ld, nl * 4, cudaMemcpyHostToDevice, q->st));
     if (q->b1) {
       io.latent = q->lat1;
       io.scaled = q->scaled1;
     }
-    CK(cudaMemcpyAsync(q->io, &io, sizeof io, cudaMemcpyHostToDevice, q->st));
+    // the FrameIO and the noise rows in one copy
+    std::memcpy(q->in1_h, &io, sizeof io);
+    std::memcpy(q->in1_h + kIoPad, noise + r0 * ld, nl * 4);
+    CK(cudaMemcpyAsync(q->io, q->in1_h, q->in1_bytes, cudaMemcpyHostToDevice, q->st));
     if (q->b1) {
-      rc = frame1_run(q, 1);
+      rc = frame1_run(q, 1, 0, false);  // its error word comes back with the outputs
       if (rc) return rc;
     } else {
       CK(cudaGraphLaunch(q->exec, q->st));
@@ -1460,16 +1490,24 @@ int grx_streams_step(grx_streams* s, const float* noise, float* lm_out, float* e
   // host memory returns only when it is done, and would otherwise hold back
   // the next part's launch
   for (grx_streams* q : sets) {
-    const size_t r0 = size_t(q->row0), nl = size_t(q->n) * ld;
+    const size_t r0 = size_t(q->row0);
     if (lm_out) CK(cudaMemcpyAsync(lm_out + r0 * d, q->lm_out, size_t(q->n) * d * 4, cudaMemcpyDeviceToHost, q->st));
-    if (eos) CK(cudaMemcpyAsync(eos + r0, q->eos1, size_t(q->n) * 4, cudaMemcpyDeviceToHost, q->st));
-    if (latent) CK(cudaMemcpyAsync(latent + r0 * ld, q->lat1, nl * 4, cudaMemcpyDeviceToHost, q->st));
-    if (scaled) CK(cudaMemcpyAsync(scaled + r0 * ld, q->scaled1, nl * 4, cudaMemcpyDeviceToHost, q->st));
+    // latent, scaled, eos and the error word in one copy
+    CK(cudaMemcpyAsync(q->out1_h, q->out1, q->out1_floats * 4, cudaMemcpyDeviceToHost, q->st));
   }
   for (grx_streams* q : sets) CK(cudaStreamSynchronize(q->st));
   for (grx_streams* q : sets) {
-    rc = frame1_check(q);
-    if (rc) return rc;
+    const size_t r0 = size_t(q->row0), nl = size_t(q->n) * ld;
+    const float* o = q->out1_h;
+    if (latent) std::memcpy(latent + r0 * ld, o, nl * 4);
+    if (scaled) std::memcpy(scaled + r0 * ld, o + nl, nl * 4);
+    if (eos) std::memcpy(eos + r0, o + 2 * nl, size_t(q->n) * 4);
+    if (q->b1) {
+      int e = 0;
+      std::memcpy(&e, o + q->out1_floats - 1, sizeof e);
+      rc = frame1_error(e);
+      if (rc) return rc;
+    }
   }
   return GRX_OK;
 }
