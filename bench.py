@@ -1187,7 +1187,9 @@ def main():
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        # each rank builds its 256 voices (3.2 GB of caches) before the first
+        # barrier; with eight ranks on one host that can take minutes
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
 
     import gorelaxor_b200 as g
     from gorelaxor_b200 import synth
