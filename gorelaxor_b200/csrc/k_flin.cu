@@ -490,8 +490,12 @@ void fl_dispatch(const FArgs& a, cudaStream_t st) {
       fl_launch<WM, 1, 8, 8, 64>(a, st);
   } else if (fl_ctas<WM, 2, 16, 16, 256>(a) >= 2 * kFillCtas) {
     fl_launch<WM, 2, 16, 16, 256>(a, st);  // 32 rows × 32 streams
-  } else if (a.K <= 64) {
-    fl_launch<WM, 2, 8, 8, 128>(a, st);  // 16 rows × 16 streams
+  } else if (a.K <= 64 || (a.M <= 32 && fl_ctas<WM, 2, 8, 8, 128>(a) >= kFillCtas)) {
+    // 16 rows × 16 streams; at up to 32 streams also for deep products that
+    // still fill the SMs (Whisper's stacked q/k/v and fc1 at 32 streams:
+    // 30.1 k tokens/s against 29.3 k), which at 128 streams (the FlowLM flow
+    // head) measured slower than 64 × 4
+    fl_launch<WM, 2, 8, 8, 128>(a, st);
   } else if (fl_ctas<WM, 2, 4, 32, 256>(a) >= kFillCtas) {
     fl_launch<WM, 2, 4, 32, 256>(a, st);  // 64 rows × 4 streams
   } else {
