@@ -112,8 +112,16 @@ struct grx_mimi_streams {
   float *clip = nullptr, *piece_lat = nullptr;
   int max_samples = 0, rows_for = -1;
   int64_t launches = 0;
+  // A decoder set's call as CUDA graphs, one per carried-buffer parity,
+  // captured on first use with the set's own latent and sample buffers
+  // (graph_tried: capture was attempted; graph_launches: kernels per call).
+  cudaGraphExec_t graph[2] = {nullptr, nullptr};
+  bool graph_tried = false;
+  int64_t graph_launches = 0;
   ~grx_mimi_streams() {
     cudaSetDevice(ar.dev);
+    for (cudaGraphExec_t g : graph)
+      if (g) cudaGraphExecDestroy(g);
     if (st) cudaStreamDestroy(st);
   }
 };
@@ -476,6 +484,48 @@ void mimi_enqueue(grx_mimi_streams* s, const float* d_lat, float* d_pcm) {
   launch_mimi_fade(d_pcm, s->started, n, m->frame, m->sample_rate / 200, st);
   s->launches++;
   s->par ^= 1;
+}
+
+// One decode call of every stream (latents d_lat in, samples d_pcm out):
+// the captured graph of the call's parity when there is one (the latents
+// and samples pass through the set's own buffers), else the launches.
+void mimi_decode_frame(grx_mimi_streams* s, const float* d_lat, float* d_pcm) {
+  grx_mimi* m = s->m;
+  cudaStream_t st = s->st;
+  if (!s->graph_tried) {
+    s->graph_tried = true;
+    const int par0 = s->par;
+    const int64_t l0 = s->launches;
+    bool ok = true;
+    for (int p = 0; p < 2 && ok; p++) {
+      s->par = p;
+      cudaGraph_t g = nullptr;
+      ok = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+      if (ok) mimi_enqueue(s, s->lat, s->pcm);
+      ok = cudaStreamEndCapture(st, &g) == cudaSuccess && ok && g;
+      if (ok) ok = cudaGraphInstantiate(&s->graph[p], g, 0) == cudaSuccess;
+      if (g) cudaGraphDestroy(g);
+    }
+    s->graph_launches = (s->launches - l0) / 2;
+    s->launches = l0;
+    s->par = par0;
+    if (!ok) {
+      cudaGetLastError();
+      for (cudaGraphExec_t& g : s->graph)
+        if (g) cudaGraphExecDestroy(g), g = nullptr;
+    }
+  }
+  if (!s->graph[0] || !s->graph[1]) {
+    mimi_enqueue(s, d_lat, d_pcm);
+    return;
+  }
+  if (d_lat != s->lat)
+    cudaMemcpyAsync(s->lat, d_lat, sizeof(float) * size_t(s->n) * m->ldim, cudaMemcpyDeviceToDevice, st);
+  cudaGraphLaunch(s->graph[s->par], st);
+  s->par ^= 1;
+  s->launches += s->graph_launches;
+  if (d_pcm != s->pcm)
+    cudaMemcpyAsync(d_pcm, s->pcm, sizeof(float) * size_t(s->n) * m->frame, cudaMemcpyDeviceToDevice, st);
 }
 
 int mimi_reset(grx_mimi_streams* s) {
@@ -1022,7 +1072,7 @@ int grx_mimi_decode(grx_mimi_streams* s, const float* latents, float* pcm) {
   grx_mimi* m = s->m;
   CK(cudaSetDevice(s->ar.dev));
   CK(cudaMemcpyAsync(s->lat, latents, sizeof(float) * size_t(s->n) * m->ldim, cudaMemcpyHostToDevice, s->st));
-  mimi_enqueue(s, s->lat, s->pcm);
+  mimi_decode_frame(s, s->lat, s->pcm);
   s->frames++;
   if (pcm)
     CK(cudaMemcpyAsync(pcm, s->pcm, sizeof(float) * size_t(s->n) * m->frame, cudaMemcpyDeviceToHost, s->st));
@@ -1038,7 +1088,7 @@ int grx_mimi_decode_device(grx_mimi_streams* s, int frames, const float* d_laten
   grx_mimi* m = s->m;
   CK(cudaSetDevice(s->ar.dev));
   for (int f = 0; f < frames; f++) {
-    mimi_enqueue(s, d_latents + size_t(f) * s->n * m->ldim, d_pcm + size_t(f) * s->n * m->frame);
+    mimi_decode_frame(s, d_latents + size_t(f) * s->n * m->ldim, d_pcm + size_t(f) * s->n * m->frame);
     s->frames++;
   }
   CK(cudaGetLastError());
