@@ -90,6 +90,30 @@ def test_whisper_cross_kv_and_greedy(have_gpu, f16):
         assert abs(ns[i] - wns) <= TOL * abs(wns)
 
 
+def test_whisper_mixed_qkv_types(have_gpu):
+    """A file whose first layer stores attn.key as float16 and attn.query and
+    attn.value as Q8_0: that layer keeps three product launches (its matrices
+    are not stacked) while the second takes the stacked q/k/v launch. Greedy
+    tokens as the oracle's over three streams (the per-kernel decode step)."""
+    cfg = synth.WhisperConfig(**SMALL_W)
+    t = synth.whisper_tensors(cfg, 5)
+    words = synth.whisper_words(cfg)
+    name = "decoder.blocks.0.attn.key.weight"
+    gm = g.Whisper(synth.whisper_ggml(cfg, t, words, f16_bits={name: orc.q8_to_f16(t[name])}))
+    om = orc.Whisper(cfg, t, words)
+    n, steps = 3, 16
+    enc = _enc(cfg, n, seed0=21)
+    b = g.WhisperBatch(gm, n)
+    assert not b.persistent()
+    b.set_audio(enc)
+    prompt, sot_at = _prompt(gm)
+    b.prompt(prompt, sot_at)
+    toks = b.run(steps)
+    for i in range(n):
+        want, _ = om.greedy(om.seq(enc[i]), prompt, sot_at, steps)
+        _check_tokens(toks[:, i], want)
+
+
 def test_whisper_base_shape(have_gpu):
     """The base.en decoder shape (state 512, 8 heads, 6 layers, vocab 51864,
     text context 448) on one stream: prompt and 6 greedy steps."""
