@@ -118,10 +118,22 @@ struct grx_mimi_streams {
   cudaGraphExec_t graph[2] = {nullptr, nullptr};
   bool graph_tried = false;
   int64_t graph_launches = 0;
+  // An encoder set's pieces as CUDA graphs, by piece length, carried-buffer
+  // parity and whether the piece is the clip's first (null exec: capture
+  // failed, the piece is launched directly).
+  struct PieceGraph {
+    int T0, par;
+    bool first;
+    cudaGraphExec_t exec;
+    int64_t launches;
+  };
+  std::vector<PieceGraph> piece_graphs;
   ~grx_mimi_streams() {
     cudaSetDevice(ar.dev);
     for (cudaGraphExec_t g : graph)
       if (g) cudaGraphExecDestroy(g);
+    for (const PieceGraph& pg : piece_graphs)
+      if (pg.exec) cudaGraphExecDestroy(pg.exec);
     if (st) cudaStreamDestroy(st);
   }
 };
@@ -643,10 +655,9 @@ int enc_run(grx_mimi_streams* s, int samples, const float* d_pcm, float* d_lat) 
                        cudaMemcpyDeviceToDevice, st));
   const size_t down_ci = s->carry_n.size() - 1;
   auto other = [&](const float* p) { return p == s->sa ? s->sb : s->sa; };
-  for (int p0 = 0; p0 < padded; p0 += piece) {
-    const int T0 = std::min(piece, padded - p0);
-    CK(cudaMemcpy2DAsync(s->sa, sizeof(float) * T0, s->clip + p0, sizeof(float) * padded, sizeof(float) * T0, n,
-                         cudaMemcpyDeviceToDevice, st));
+  // a piece from its samples in sa to its latents in piece_lat: SEANet's
+  // encoder, the transformer on its T rows, the downsampling
+  auto piece_kernels = [&](int T0, bool first) {
     float* x = s->sa;
     int T = T0;
     size_t ci = 0;
@@ -663,18 +674,56 @@ int enc_run(grx_mimi_streams* s, int samples, const float* d_pcm, float* d_lat) 
         ci += 2;
       }
     }
-    CK(cudaMemcpyAsync(s->x, x, sizeof(float) * size_t(n) * T * d, cudaMemcpyDeviceToDevice, st));
+    cudaMemcpyAsync(s->x, x, sizeof(float) * size_t(n) * T * d, cudaMemcpyDeviceToDevice, st);
+    mimi_transformer(s, T);
+    if (first) {  // the first call's padding: copies of the first row
+      launch_mimi_replicate(s->x, T, d, s->carry[s->par][down_ci], m->down.past(), n, st);
+      s->launches++;
+    }
+    mimi_conv(s, m->down, int(down_ci), s->x, T, false, s->piece_lat, false);
+  };
+  for (int p0 = 0; p0 < padded; p0 += piece) {
+    const int T0 = std::min(piece, padded - p0);
+    const bool first = p0 == 0;
+    CK(cudaMemcpy2DAsync(s->sa, sizeof(float) * T0, s->clip + p0, sizeof(float) * padded, sizeof(float) * T0, n,
+                         cudaMemcpyDeviceToDevice, st));
+    int T = T0;  // the transformer's rows: the encoder's strides applied
+    for (const MStep& stp : m->enc_steps)
+      if (stp.kind == 0) T /= stp.c.stride;
     if (T != s->rows_for) {
       launch_mimi_rowtab(T, n, s->rowslot, s->crow0, s->cT, s->cslot, st);
       s->launches++;
       s->rows_for = T;
     }
-    mimi_transformer(s, T);
-    if (p0 == 0) {  // the first call's padding: copies of the first row
-      launch_mimi_replicate(s->x, T, d, s->carry[s->par][down_ci], m->down.past(), n, st);
-      s->launches++;
+    // the piece's kernels from a graph captured the first time its shape
+    // comes (same launches, same bits)
+    grx_mimi_streams::PieceGraph* pg = nullptr;
+    for (auto& e : s->piece_graphs)
+      if (e.T0 == T0 && e.par == s->par && e.first == first) pg = &e;
+    if (!pg) {
+      grx_mimi_streams::PieceGraph e{T0, s->par, first, nullptr, 0};
+      const int64_t l0 = s->launches;
+      cudaGraph_t g = nullptr;
+      bool ok = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+      if (ok) piece_kernels(T0, first);
+      ok = cudaStreamEndCapture(st, &g) == cudaSuccess && ok && g;
+      if (ok) ok = cudaGraphInstantiate(&e.exec, g, 0) == cudaSuccess;
+      if (g) cudaGraphDestroy(g);
+      if (!ok) {
+        cudaGetLastError();
+        e.exec = nullptr;
+      }
+      e.launches = s->launches - l0;
+      s->launches = l0;
+      s->piece_graphs.push_back(e);
+      pg = &s->piece_graphs.back();
     }
-    mimi_conv(s, m->down, int(down_ci), s->x, T, false, s->piece_lat, false);
+    if (pg->exec) {
+      CK(cudaGraphLaunch(pg->exec, st));
+      s->launches += pg->launches;
+    } else {
+      piece_kernels(T0, first);
+    }
     const int fr = T / S;
     CK(cudaMemcpy2DAsync(d_lat + size_t(p0 / frame) * ldim, sizeof(float) * frames * ldim, s->piece_lat,
                          sizeof(float) * fr * ldim, sizeof(float) * fr * ldim, n, cudaMemcpyDeviceToDevice, st));
