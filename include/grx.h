@@ -242,7 +242,9 @@ int grx_mimi_decode(grx_mimi_streams* s, const float* latents, float* pcm);
 /* `frames` calls of grx_mimi_decode, device-resident: d_latents
  * [frames][n][ldim] in, d_pcm [frames][n][frame] out (device pointers on
  * the set's device). Asynchronous on the library's stream; grx_mimi_sync
- * waits. */
+ * waits. A set's first decode call (either form) captures the call's
+ * kernels into CUDA graphs on the set's stream, which later calls replay;
+ * an encoder set does the same per piece shape. */
 int grx_mimi_decode_device(grx_mimi_streams* s, int frames, const float* d_latents, float* d_pcm);
 int grx_mimi_sync(grx_mimi_streams* s);
 /* The cudaStream_t the set's kernels run on. */
